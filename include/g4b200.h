@@ -1,0 +1,115 @@
+/* g4b200: B200 (sm_100a) kernels for the Gemma-4-12B single-token decoder-layer ops.
+ *
+ * C ABI of libg4b200.so. Each op entry point replaces one `#[device(chip = 1)] pub fn` of the
+ * reference crate `furiosa-opt-gemma4-12B/src/ops.rs`, with the same name (prefixed `g4_`),
+ * the same parameters in the same order and the same meaning; `&HbmTensor` becomes a const
+ * device pointer, `&mut HbmTensor` a mutable one. Shapes are the reference's fixed axes
+ * (src/axes.rs:1-28): H = 3840, L = 15360, Ns = 8, Gs = 2, Ds = 256, Qs = 4096,
+ * Ps = 2048, ring slots Ts (1024 by default), RoPE rows E (32768 by default).
+ *
+ * Element encodings (all little-endian, row-major, no padding):
+ *   bf16     uint16_t bit pattern
+ *   f8e4m3   uint8_t code (e4m3fn)
+ *   f4e2m1   two codes per byte, element 2i in the low nibble (the reference's packing)
+ *   f32/i32  native
+ *
+ * Conventions:
+ *   - Every call validates its arguments on the host and returns a g4_status; it never
+ *     aborts. Calls are asynchronous and ordered on the caller's CUDA stream (`stream` is a
+ *     cudaStream_t; NULL means the legacy default stream).
+ *   - Every pointer must be device memory of the context's device, 16-byte aligned.
+ *   - Offsets that live in device memory (kv_offset, rope_offset) are checked on the
+ *     device: an out-of-range value skips the writes that depend on it and raises a bit
+ *     that g4_ctx_check() reports as G4_ERR_DEVICE.
+ *   - A context owns scratch memory (split-K partials, tickets, the GeGLU activation).
+ *     Calls on one context must not overlap on the GPU (use one stream per context).
+ *     A context is thread-compatible, not thread-safe, like the reference's single
+ *     device-owning thread (src/api/worker.rs:45-72).
+ */
+#ifndef G4B200_H
+#define G4B200_H
+
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+typedef int32_t g4_status;
+#define G4_OK 0
+#define G4_ERR_INVALID_ARGUMENT (-1) /* null pointer, bad size */
+#define G4_ERR_MISALIGNED (-2)       /* pointer not 16-byte aligned */
+#define G4_ERR_CUDA (-3)             /* a CUDA runtime call failed (see g4_last_error) */
+#define G4_ERR_DEVICE (-4)           /* a kernel raised a device-side error bit */
+#define G4_ERR_UNSUPPORTED (-5)      /* a size this build does not handle */
+
+/* device-side error bits reported by g4_ctx_check() */
+#define G4_DEVERR_KV_OFFSET 1u    /* kv_offset outside the ring or not slot-aligned */
+#define G4_DEVERR_ROPE_OFFSET 2u  /* rope_offset outside the table or not row-aligned */
+#define G4_DEVERR_WAIT_TIMEOUT 4u /* a bounded in-kernel wait gave up */
+
+typedef struct g4_ctx g4_ctx;
+
+/* Create a context on `device` (allocates scratch, prepares kernels). No reference
+ * counterpart: the reference's `Device::new` (src/bin/test_kernels.rs:781) plays this role. */
+g4_status g4_ctx_create(int device, g4_ctx** out);
+g4_status g4_ctx_destroy(g4_ctx* ctx);
+
+/* Synchronise `stream`, then read and clear the device-side error word. Returns G4_OK or
+ * G4_ERR_DEVICE with the bits in *flags (may be NULL). */
+g4_status g4_ctx_check(g4_ctx* ctx, void* stream, uint32_t* flags);
+
+/* Allow an op to start its weight prefetch while the previous kernel on the stream is still
+ * running (programmatic dependent launch). Off by default. */
+g4_status g4_ctx_set_overlap(g4_ctx* ctx, int enable);
+
+const char* g4_status_string(g4_status status);
+const char* g4_last_error(const g4_ctx* ctx);
+
+/* Replaces ops::sliding_project_qkv (src/ops.rs:37-76).
+ * x[H], q_weight[Qs,H], k_weight[Ps,H], v_weight[Ps,H] (f8e4m3), *_weight_scale bf16 per row,
+ * input_rms_weight[H], q_rms_weight[Ds], k_rms_weight[Ds], kv_offset/rope_offset: one device
+ * i32 each, BYTE offsets ((pos % ring_len)*Ns*Ds*2 and pos*Ds*2); cos/sin [rope_rows, Ds] bf16
+ * with the low half of sin pre-negated; k_cache/v_cache [ring_len, Ns, Ds] bf16 (only the
+ * addressed slot is written); q_out [Ns, Gs, Ds]. ring_len = Ts = 1024 and rope_rows = E =
+ * 32768 reproduce the reference shapes. */
+g4_status g4_sliding_project_qkv(g4_ctx* ctx, const uint16_t* x, const uint8_t* q_weight, const uint8_t* k_weight,
+                                 const uint8_t* v_weight, const uint16_t* q_weight_scale,
+                                 const uint16_t* k_weight_scale, const uint16_t* v_weight_scale,
+                                 const uint16_t* input_rms_weight, const uint16_t* q_rms_weight,
+                                 const uint16_t* k_rms_weight, const int32_t* kv_offset, const int32_t* rope_offset,
+                                 const uint16_t* cos, const uint16_t* sin, uint16_t* k_cache, uint16_t* v_cache,
+                                 uint16_t* q_out, int32_t ring_len, int32_t rope_rows, void* stream);
+
+/* Replaces ops::sliding_attention (src/ops.rs:118-128).
+ * q [Ns, Gs, Ds], k/v [ring_len, Ns, Ds] bf16, mask [ring_len] f32 (the reference passes a
+ * 0/1 row), out_hbm [Ns, Gs, Ds]. `scale` multiplies q.k before the bf16 score rounding; the
+ * reference model uses 1.0. ring_len must be a multiple of 256, at most 8192. */
+g4_status g4_sliding_attention(g4_ctx* ctx, const uint16_t* q, const uint16_t* k, const uint16_t* v,
+                               const float* mask, uint16_t* out_hbm, int32_t ring_len, float scale, void* stream);
+
+/* Replaces ops::sliding_attention_output (src/ops.rs:130-146).
+ * x [Ns, Gs, Ds] (= [Qs]) bf16, post_attn_rms_weight [H], o_weight [H, Qs] f8e4m3,
+ * o_weight_scale [H] bf16, residual_hbm [H] bf16 read and overwritten in place. */
+g4_status g4_sliding_attention_output(g4_ctx* ctx, const uint16_t* x, const uint16_t* post_attn_rms_weight,
+                                      const uint8_t* o_weight, const uint16_t* o_weight_scale,
+                                      uint16_t* residual_hbm, void* stream);
+
+/* Replaces ops::decoder_feedforward (src/ops.rs:201-239).
+ * residual_hbm [H] bf16 in place; up/gate packed [L, H/2] and down packed [H, L/2] f4e2m1;
+ * up/gate scales [L, H/16] and down scale [H, L/16] f8e4m3; *_global_scale one f32 each,
+ * already the RECIPROCAL of the checkpoint's global scale; layer_scalar bf16 (element 0 is
+ * used; the reference stores 8 copies). */
+g4_status g4_decoder_feedforward(g4_ctx* ctx, uint16_t* residual_hbm, const uint16_t* pre_ff_rms_weight,
+                                 const uint8_t* up_weight_packed, const uint8_t* gate_weight_packed,
+                                 const uint8_t* down_weight_packed, const uint8_t* up_weight_scale,
+                                 const uint8_t* gate_weight_scale, const uint8_t* down_weight_scale,
+                                 const float* up_global_scale, const float* gate_global_scale,
+                                 const float* down_global_scale, const uint16_t* post_ff_rms_weight,
+                                 const uint16_t* layer_scalar, void* stream);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* G4B200_H */

@@ -1,0 +1,267 @@
+// C ABI of libg4b200.so (declared in include/g4b200.h): contexts, argument validation and
+// the op entry points. No computation happens here; every op launches the sm_100a kernels
+// of g4_proj.cu / g4_attention.cu and there is no host or CPU fallback.
+#include <cstdio>
+#include <cstring>
+
+#include "../../include/g4b200.h"
+#include "g4_ops.cuh"
+
+namespace g4 {
+int attention_slot_multiple();
+int attention_max_ring();
+}  // namespace g4
+
+struct g4_ctx {
+  int device = 0;
+  int sm_count = 0;
+  bool overlap = false;
+  void* scratch = nullptr;
+  size_t scratch_bytes = 0;
+  g4::Scratch sc{};
+  char last_error[256] = {0};
+};
+
+namespace {
+
+// Restores the caller's current device when the call returns.
+struct DeviceGuard {
+  int prev = -1;
+  explicit DeviceGuard(int dev) {
+    if (cudaGetDevice(&prev) != cudaSuccess) prev = -1;
+    if (prev != dev) cudaSetDevice(dev);
+  }
+  ~DeviceGuard() {
+    int cur = -1;
+    if (prev >= 0 && cudaGetDevice(&cur) == cudaSuccess && cur != prev) cudaSetDevice(prev);
+  }
+};
+
+g4_status fail(g4_ctx* ctx, g4_status st, const char* fmt, const char* what) {
+  if (ctx) snprintf(ctx->last_error, sizeof ctx->last_error, fmt, what);
+  return st;
+}
+
+g4_status cuda_status(g4_ctx* ctx, cudaError_t e, const char* where) {
+  if (e == cudaSuccess) return G4_OK;
+  if (ctx) snprintf(ctx->last_error, sizeof ctx->last_error, "%s: %s", where, cudaGetErrorString(e));
+  return G4_ERR_CUDA;
+}
+
+bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
+
+// Every pointer non-null and 16-byte aligned.
+g4_status check_ptrs(g4_ctx* ctx, std::initializer_list<std::pair<const void*, const char*>> ptrs) {
+  for (const auto& p : ptrs) {
+    if (!p.first) return fail(ctx, G4_ERR_INVALID_ARGUMENT, "null pointer: %s", p.second);
+    if (!aligned16(p.first)) return fail(ctx, G4_ERR_MISALIGNED, "pointer not 16-byte aligned: %s", p.second);
+  }
+  return G4_OK;
+}
+
+g4::LaunchEnv env_of(const g4_ctx* ctx, void* stream) {
+  g4::LaunchEnv env;
+  env.device = ctx->device;
+  env.sm_count = ctx->sm_count;
+  env.stream = static_cast<cudaStream_t>(stream);
+  env.pdl = ctx->overlap;
+  env.sc = ctx->sc;
+  return env;
+}
+
+}  // namespace
+
+extern "C" {
+
+const char* g4_status_string(g4_status s) {
+  switch (s) {
+    case G4_OK: return "ok";
+    case G4_ERR_INVALID_ARGUMENT: return "invalid argument";
+    case G4_ERR_MISALIGNED: return "misaligned pointer";
+    case G4_ERR_CUDA: return "CUDA error";
+    case G4_ERR_DEVICE: return "device-side error";
+    case G4_ERR_UNSUPPORTED: return "unsupported size";
+    default: return "unknown status";
+  }
+}
+
+const char* g4_last_error(const g4_ctx* ctx) { return ctx ? ctx->last_error : "no context"; }
+
+g4_status g4_ctx_create(int device, g4_ctx** out) {
+  if (!out) return G4_ERR_INVALID_ARGUMENT;
+  *out = nullptr;
+  int count = 0;
+  if (cudaGetDeviceCount(&count) != cudaSuccess || device < 0 || device >= count) return G4_ERR_INVALID_ARGUMENT;
+  g4_ctx* ctx = new g4_ctx();
+  ctx->device = device;
+  DeviceGuard guard(device);
+  cudaError_t e = cudaDeviceGetAttribute(&ctx->sm_count, cudaDevAttrMultiProcessorCount, device);
+  int major = 0, minor = 0;
+  if (e == cudaSuccess) e = cudaDeviceGetAttribute(&major, cudaDevAttrComputeCapabilityMajor, device);
+  if (e == cudaSuccess) e = cudaDeviceGetAttribute(&minor, cudaDevAttrComputeCapabilityMinor, device);
+  if (e != cudaSuccess) {
+    delete ctx;
+    return G4_ERR_CUDA;
+  }
+  if (major != 10 || minor != 0) {  // the kernels are built for sm_100a only
+    delete ctx;
+    return G4_ERR_UNSUPPORTED;
+  }
+  // scratch: error word + counters | partials | y | act
+  const size_t off_counters = 256;
+  const size_t off_partials = off_counters + g4::kCounterCount * sizeof(uint32_t);
+  const size_t off_y = off_partials + g4::kPartialFloats * sizeof(float);
+  const size_t off_act = off_y + g4::kYElems * sizeof(uint16_t);
+  const size_t total = off_act + size_t(64) * g4::kL * sizeof(uint16_t);
+  e = cudaMalloc(&ctx->scratch, total);
+  if (e == cudaSuccess) e = cudaMemset(ctx->scratch, 0, total);
+  if (e == cudaSuccess) e = g4::prepare_proj_kernels();
+  if (e == cudaSuccess) e = g4::prepare_attention_kernels();
+  if (e == cudaSuccess) e = cudaDeviceSynchronize();
+  if (e != cudaSuccess) {
+    if (ctx->scratch) cudaFree(ctx->scratch);
+    delete ctx;
+    return G4_ERR_CUDA;
+  }
+  uint8_t* base = static_cast<uint8_t*>(ctx->scratch);
+  ctx->scratch_bytes = total;
+  ctx->sc.err = reinterpret_cast<uint32_t*>(base);
+  ctx->sc.counters = reinterpret_cast<uint32_t*>(base + off_counters);
+  ctx->sc.partials = reinterpret_cast<float*>(base + off_partials);
+  ctx->sc.y = reinterpret_cast<uint16_t*>(base + off_y);
+  ctx->sc.act = reinterpret_cast<uint16_t*>(base + off_act);
+  *out = ctx;
+  return G4_OK;
+}
+
+g4_status g4_ctx_destroy(g4_ctx* ctx) {
+  if (!ctx) return G4_ERR_INVALID_ARGUMENT;
+  DeviceGuard guard(ctx->device);
+  cudaError_t e = cudaSuccess;
+  if (ctx->scratch) e = cudaFree(ctx->scratch);
+  delete ctx;
+  return e == cudaSuccess ? G4_OK : G4_ERR_CUDA;
+}
+
+g4_status g4_ctx_set_overlap(g4_ctx* ctx, int enable) {
+  if (!ctx) return G4_ERR_INVALID_ARGUMENT;
+  ctx->overlap = enable != 0;
+  return G4_OK;
+}
+
+g4_status g4_ctx_check(g4_ctx* ctx, void* stream, uint32_t* flags) {
+  if (!ctx) return G4_ERR_INVALID_ARGUMENT;
+  DeviceGuard guard(ctx->device);
+  uint32_t word = 0;
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  cudaError_t e = cudaStreamSynchronize(s);
+  if (e == cudaSuccess) e = cudaMemcpy(&word, ctx->sc.err, sizeof word, cudaMemcpyDeviceToHost);
+  if (e == cudaSuccess && word) e = cudaMemset(ctx->sc.err, 0, sizeof word);
+  if (e == cudaSuccess && (word & G4_DEVERR_WAIT_TIMEOUT)) {
+    // an abandoned launch can leave tickets half counted: start the next call clean
+    e = cudaMemset(ctx->sc.counters, 0, g4::kCounterCount * sizeof(uint32_t));
+  }
+  if (flags) *flags = word;
+  if (e != cudaSuccess) return cuda_status(ctx, e, "g4_ctx_check");
+  if (word) {
+    snprintf(ctx->last_error, sizeof ctx->last_error, "device error bits 0x%x", word);
+    return G4_ERR_DEVICE;
+  }
+  return G4_OK;
+}
+
+g4_status g4_sliding_project_qkv(g4_ctx* ctx, const uint16_t* x, const uint8_t* q_weight, const uint8_t* k_weight,
+                                 const uint8_t* v_weight, const uint16_t* q_weight_scale,
+                                 const uint16_t* k_weight_scale, const uint16_t* v_weight_scale,
+                                 const uint16_t* input_rms_weight, const uint16_t* q_rms_weight,
+                                 const uint16_t* k_rms_weight, const int32_t* kv_offset, const int32_t* rope_offset,
+                                 const uint16_t* cos, const uint16_t* sin, uint16_t* k_cache, uint16_t* v_cache,
+                                 uint16_t* q_out, int32_t ring_len, int32_t rope_rows, void* stream) {
+  if (!ctx) return G4_ERR_INVALID_ARGUMENT;
+  g4_status st = check_ptrs(ctx, {{x, "x"},
+                                  {q_weight, "q_weight"},
+                                  {k_weight, "k_weight"},
+                                  {v_weight, "v_weight"},
+                                  {q_weight_scale, "q_weight_scale"},
+                                  {k_weight_scale, "k_weight_scale"},
+                                  {v_weight_scale, "v_weight_scale"},
+                                  {input_rms_weight, "input_rms_weight"},
+                                  {q_rms_weight, "q_rms_weight"},
+                                  {k_rms_weight, "k_rms_weight"},
+                                  {kv_offset, "kv_offset"},
+                                  {rope_offset, "rope_offset"},
+                                  {cos, "cos"},
+                                  {sin, "sin"},
+                                  {k_cache, "k_cache"},
+                                  {v_cache, "v_cache"},
+                                  {q_out, "q_out"}});
+  if (st != G4_OK) return st;
+  if (ring_len <= 0 || rope_rows <= 0)
+    return fail(ctx, G4_ERR_INVALID_ARGUMENT, "%s must be positive", ring_len <= 0 ? "ring_len" : "rope_rows");
+  if (int64_t(rope_rows) * g4::kDs * 2 > INT32_MAX || int64_t(ring_len) * g4::kPs * 2 > INT32_MAX)
+    return fail(ctx, G4_ERR_UNSUPPORTED, "%s: byte offsets would overflow i32", "ring_len/rope_rows");
+  DeviceGuard guard(ctx->device);
+  g4::QkvArgs a{x,        q_weight,      k_weight,  v_weight, q_weight_scale, k_weight_scale, v_weight_scale,
+                input_rms_weight, q_rms_weight, k_rms_weight, kv_offset, rope_offset, cos, sin,
+                k_cache,  v_cache,       q_out,     ring_len, rope_rows};
+  return cuda_status(ctx, g4::launch_qkv(a, env_of(ctx, stream)), "sliding_project_qkv launch");
+}
+
+g4_status g4_sliding_attention(g4_ctx* ctx, const uint16_t* q, const uint16_t* k, const uint16_t* v,
+                               const float* mask, uint16_t* out_hbm, int32_t ring_len, float scale, void* stream) {
+  if (!ctx) return G4_ERR_INVALID_ARGUMENT;
+  g4_status st = check_ptrs(ctx, {{q, "q"}, {k, "k"}, {v, "v"}, {mask, "mask"}, {out_hbm, "out_hbm"}});
+  if (st != G4_OK) return st;
+  if (ring_len <= 0 || ring_len % g4::attention_slot_multiple() != 0 || ring_len > g4::attention_max_ring())
+    return fail(ctx, G4_ERR_UNSUPPORTED, "%s must be a positive multiple of 256, at most 8192", "ring_len");
+  if (!(scale == scale)) return fail(ctx, G4_ERR_INVALID_ARGUMENT, "%s is NaN", "scale");
+  DeviceGuard guard(ctx->device);
+  g4::AttnArgs a{q, k, v, mask, out_hbm, ring_len, scale};
+  return cuda_status(ctx, g4::launch_attention(a, env_of(ctx, stream)), "sliding_attention launch");
+}
+
+g4_status g4_sliding_attention_output(g4_ctx* ctx, const uint16_t* x, const uint16_t* post_attn_rms_weight,
+                                      const uint8_t* o_weight, const uint16_t* o_weight_scale,
+                                      uint16_t* residual_hbm, void* stream) {
+  if (!ctx) return G4_ERR_INVALID_ARGUMENT;
+  g4_status st = check_ptrs(ctx, {{x, "x"},
+                                  {post_attn_rms_weight, "post_attn_rms_weight"},
+                                  {o_weight, "o_weight"},
+                                  {o_weight_scale, "o_weight_scale"},
+                                  {residual_hbm, "residual_hbm"}});
+  if (st != G4_OK) return st;
+  DeviceGuard guard(ctx->device);
+  g4::OArgs a{x, post_attn_rms_weight, o_weight, o_weight_scale, residual_hbm};
+  return cuda_status(ctx, g4::launch_o(a, env_of(ctx, stream)), "sliding_attention_output launch");
+}
+
+g4_status g4_decoder_feedforward(g4_ctx* ctx, uint16_t* residual_hbm, const uint16_t* pre_ff_rms_weight,
+                                 const uint8_t* up_weight_packed, const uint8_t* gate_weight_packed,
+                                 const uint8_t* down_weight_packed, const uint8_t* up_weight_scale,
+                                 const uint8_t* gate_weight_scale, const uint8_t* down_weight_scale,
+                                 const float* up_global_scale, const float* gate_global_scale,
+                                 const float* down_global_scale, const uint16_t* post_ff_rms_weight,
+                                 const uint16_t* layer_scalar, void* stream) {
+  if (!ctx) return G4_ERR_INVALID_ARGUMENT;
+  g4_status st = check_ptrs(ctx, {{residual_hbm, "residual_hbm"},
+                                  {pre_ff_rms_weight, "pre_ff_rms_weight"},
+                                  {up_weight_packed, "up_weight_packed"},
+                                  {gate_weight_packed, "gate_weight_packed"},
+                                  {down_weight_packed, "down_weight_packed"},
+                                  {up_weight_scale, "up_weight_scale"},
+                                  {gate_weight_scale, "gate_weight_scale"},
+                                  {down_weight_scale, "down_weight_scale"},
+                                  {up_global_scale, "up_global_scale"},
+                                  {gate_global_scale, "gate_global_scale"},
+                                  {down_global_scale, "down_global_scale"},
+                                  {post_ff_rms_weight, "post_ff_rms_weight"},
+                                  {layer_scalar, "layer_scalar"}});
+  if (st != G4_OK) return st;
+  DeviceGuard guard(ctx->device);
+  g4::FfnArgs a{residual_hbm,      pre_ff_rms_weight, up_weight_packed, gate_weight_packed, down_weight_packed,
+                up_weight_scale,   gate_weight_scale, down_weight_scale, up_global_scale,   gate_global_scale,
+                down_global_scale, post_ff_rms_weight, layer_scalar};
+  return cuda_status(ctx, g4::launch_ffn_nvfp4(a, env_of(ctx, stream)), "decoder_feedforward launch");
+}
+
+}  // extern "C"

@@ -1,0 +1,227 @@
+// Shared device helpers for the Gemma-4 decode-layer kernels (sm_100a).
+//
+// Shapes follow the reference's axes (furiosa-opt-gemma4-12B/src/axes.rs:1-28):
+// H = 3840 hidden, L = 15360 FFN, Ns = 8 KV heads, Gs = 2 query heads per KV head,
+// Ds = 256 head dim, Qs = 4096, Ps = 2048, Ts = 1024 ring slots, E = 32768 RoPE rows.
+#pragma once
+
+#include <cuda_bf16.h>
+#include <cuda_fp16.h>
+#include <cuda_runtime.h>
+#include <stdint.h>
+
+namespace g4 {
+
+constexpr int kH = 3840;
+constexpr int kL = 15360;
+constexpr int kNs = 8;
+constexpr int kGs = 2;
+constexpr int kDs = 256;
+constexpr int kQs = kNs * kGs * kDs;  // 4096
+constexpr int kPs = kNs * kDs;        // 2048
+constexpr int kTs = 1024;
+constexpr int kE = 32768;
+constexpr float kEps = 1e-6f;
+
+// Bits of the device-resident error word (`Scratch::err`). Kernels never trap: a bad
+// device-side operand (an out-of-ring cache offset, a timed-out wait) sets a bit and the
+// affected writes are skipped; the host reads the word back with g4_ctx_check().
+enum : uint32_t {
+  kErrKvOffset = 1u << 0,
+  kErrRopeOffset = 1u << 1,
+  kErrWaitTimeout = 1u << 2,
+};
+
+// Global scratch owned by a context. Counters are zero between launches: every kernel that
+// bumps one resets it before it exits.
+struct Scratch {
+  uint32_t* err;       // error word
+  uint32_t* counters;  // ticket counters (kCounterCount)
+  float* partials;     // split-K partial row sums
+  uint16_t* y;         // bf16 projected rows awaiting a grid-level epilogue
+  uint16_t* act;       // bf16 GeGLU activation [M][L]
+};
+constexpr int kCounterCount = 4096;
+constexpr int kCtaCounter = 4000;       // last-CTA ticket for whole-vector epilogues
+constexpr int kHeadCounterBase = 3968;  // 32 per-head tickets of the QKV op
+constexpr size_t kPartialFloats = size_t(1) << 21;  // 8 MiB of split-K partials
+constexpr size_t kYElems = 65536;
+
+// ---------------------------------------------------------------------------------------
+// bf16 / f16 / fp8 / fp4 conversions
+
+__device__ __forceinline__ float bf16_to_f32(uint16_t b) { return __uint_as_float(uint32_t(b) << 16); }
+
+// Round-to-nearest-even f32 -> bf16 bits (inputs here are finite; NaN is kept quiet).
+__device__ __forceinline__ uint16_t f32_to_bf16(float f) {
+  return __bfloat16_as_ushort(__float2bfloat16_rn(f));
+}
+__device__ __forceinline__ float bf16_round(float f) { return bf16_to_f32(f32_to_bf16(f)); }
+
+// Two e4m3 codes (low byte -> low half) to an exact f16x2.
+__device__ __forceinline__ uint32_t cvt_e4m3x2_f16x2(uint16_t two) {
+  uint32_t r;
+  asm("cvt.rn.f16x2.e4m3x2 %0, %1;" : "=r"(r) : "h"(two));
+  return r;
+}
+
+// Each byte of `w` holds two e2m1 codes (low nibble first); returns four exact f16x2.
+__device__ __forceinline__ void cvt_e2m1x8_f16x2(uint32_t w, uint32_t& r0, uint32_t& r1, uint32_t& r2, uint32_t& r3) {
+  asm("{\n .reg .b8 b0, b1, b2, b3;\n mov.b32 {b0, b1, b2, b3}, %4;\n"
+      " cvt.rn.f16x2.e2m1x2 %0, b0;\n cvt.rn.f16x2.e2m1x2 %1, b1;\n"
+      " cvt.rn.f16x2.e2m1x2 %2, b2;\n cvt.rn.f16x2.e2m1x2 %3, b3;\n}"
+      : "=r"(r0), "=r"(r1), "=r"(r2), "=r"(r3)
+      : "r"(w));
+}
+
+__device__ __forceinline__ uint32_t hmul2_u32(uint32_t a, uint32_t b) {
+  __half2 r = __hmul2(*reinterpret_cast<__half2*>(&a), *reinterpret_cast<__half2*>(&b));
+  return *reinterpret_cast<uint32_t*>(&r);
+}
+
+// f32 with the given unbiased exponent (exact power of two, normal range only).
+__device__ __forceinline__ float pow2f(int e) { return __uint_as_float(uint32_t(e + 127) << 23); }
+
+// ---------------------------------------------------------------------------------------
+// Tensor-op dot product: D(16x8,f32) += A(16x16,f16) * B(16x8,f16)
+
+__device__ __forceinline__ void mma_16816(float (&d)[4], uint32_t a0, uint32_t a1, uint32_t a2, uint32_t a3,
+                                          uint32_t b0, uint32_t b1) {
+  asm volatile(
+      "mma.sync.aligned.m16n8k16.row.col.f32.f16.f16.f32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, {%0,%1,%2,%3};"
+      : "+f"(d[0]), "+f"(d[1]), "+f"(d[2]), "+f"(d[3])
+      : "r"(a0), "r"(a1), "r"(a2), "r"(a3), "r"(b0), "r"(b1));
+}
+
+// ---------------------------------------------------------------------------------------
+// mbarrier + TMA bulk copy (global -> shared), no multicast.
+
+__device__ __forceinline__ uint32_t smem_u32(const void* p) {
+  return static_cast<uint32_t>(__cvta_generic_to_shared(p));
+}
+
+__device__ __forceinline__ void mbar_init(uint64_t* bar, uint32_t count) {
+  asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(smem_u32(bar)), "r"(count) : "memory");
+}
+
+__device__ __forceinline__ void fence_mbar_init() {
+  asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+}
+
+__device__ __forceinline__ void mbar_arrive_expect_tx(uint64_t* bar, uint32_t bytes) {
+  asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(smem_u32(bar)), "r"(bytes)
+               : "memory");
+}
+
+__device__ __forceinline__ bool mbar_try_wait(uint64_t* bar, uint32_t parity) {
+  uint32_t ok;
+  asm volatile(
+      "{\n .reg .pred p;\n mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n selp.u32 %0, 1, 0, p;\n}"
+      : "=r"(ok)
+      : "r"(smem_u32(bar)), "r"(parity)
+      : "memory");
+  return ok != 0;
+}
+
+__device__ __forceinline__ uint64_t globaltimer_ns() {
+  uint64_t t;
+  asm volatile("mov.u64 %0, %globaltimer;" : "=l"(t));
+  return t;
+}
+
+// Wait for a barrier phase with a time limit. A copy that never lands (it cannot, for a
+// valid address) would otherwise hang the SM; after the limit the wait gives up, raises
+// kErrWaitTimeout and the caller abandons its remaining work.
+constexpr uint64_t kWaitLimitNs = 2000000000ull;  // 2 s
+__device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, uint32_t* err) {
+  if (mbar_try_wait(bar, parity)) return true;
+  const uint64_t t0 = globaltimer_ns();
+  while (!mbar_try_wait(bar, parity)) {
+    if (globaltimer_ns() - t0 > kWaitLimitNs) {
+      atomicOr(err, kErrWaitTimeout);
+      return false;
+    }
+  }
+  return true;
+}
+
+// L2 policy for weights that are read exactly once per call.
+__device__ __forceinline__ uint64_t l2_evict_first_policy() {
+  uint64_t p;
+  asm volatile("createpolicy.fractional.L2::evict_first.b64 %0, 1.0;" : "=l"(p));
+  return p;
+}
+
+// 1-D bulk copy: `bytes` (multiple of 16, both addresses 16-byte aligned) land in shared
+// memory and complete `bytes` of transaction count on `bar`.
+__device__ __forceinline__ void bulk_g2s(void* dst, const void* src, uint32_t bytes, uint64_t* bar, uint64_t policy) {
+  asm volatile(
+      "cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes.L2::cache_hint [%0], [%1], %2, [%3], %4;" ::"r"(
+          smem_u32(dst)),
+      "l"(src), "r"(bytes), "r"(smem_u32(bar)), "l"(policy)
+      : "memory");
+}
+
+// Programmatic dependent launch: let the next kernel in the stream start its prologue, and
+// wait for the previous kernel's results before reading them.
+__device__ __forceinline__ void pdl_launch_dependents() { asm volatile("griddepcontrol.launch_dependents;" ::: "memory"); }
+__device__ __forceinline__ void pdl_wait_primary() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+
+// L2-coherent loads for data other CTAs of the same launch wrote.
+__device__ __forceinline__ float ld_cg_f32(const float* p) { return __ldcg(p); }
+__device__ __forceinline__ uint4 ld_cg_u4(const void* p) { return __ldcg(reinterpret_cast<const uint4*>(p)); }
+
+// ---------------------------------------------------------------------------------------
+// Reductions
+
+__device__ __forceinline__ float warp_max(float v) {
+#pragma unroll
+  for (int o = 16; o; o >>= 1) v = fmaxf(v, __shfl_xor_sync(0xffffffffu, v, o));
+  return v;
+}
+__device__ __forceinline__ double warp_sum_d(double v) {
+#pragma unroll
+  for (int o = 16; o; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+  return v;
+}
+
+// Block-wide reductions; `red` needs blockDim.x / 32 doubles of shared memory.
+__device__ __forceinline__ double block_sum_d(double v, double* red) {
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5, nw = blockDim.x >> 5;
+  v = warp_sum_d(v);
+  __syncthreads();
+  if (lane == 0) red[warp] = v;
+  __syncthreads();
+  double t = 0.0;
+  for (int i = 0; i < nw; ++i) t += red[i];  // fixed order: identical in every CTA
+  return t;
+}
+__device__ __forceinline__ float block_max(float v, float* red) {
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5, nw = blockDim.x >> 5;
+  v = warp_max(v);
+  __syncthreads();
+  if (lane == 0) red[warp] = v;
+  __syncthreads();
+  float t = 0.f;
+  for (int i = 0; i < nw; ++i) t = fmaxf(t, red[i]);
+  return t;
+}
+
+// RMSNorm statistics exactly as the reference computes them (gemma4.py:83-89): the mean of
+// squares of bf16 values, accumulated without loss in f64 and narrowed to f32, then
+// 1/sqrt(ms + eps) with IEEE-rounded sqrt and divide.
+__device__ __forceinline__ float rms_inverse(double sumsq, int n) {
+  const float ms = static_cast<float>(sumsq / static_cast<double>(n));
+  return 1.0f / sqrtf(ms + kEps);
+}
+
+// Split-K ranges: warp `w` of `nw` owns chunks [begin, end) of `total`.
+__device__ __forceinline__ int64_t split_begin(int64_t w, int64_t nw, int64_t total) { return (w * total) / nw; }
+
+// True when a warp's chunk range starts at global chunk `q` (so a partial for `q` exists).
+__device__ __forceinline__ bool is_range_start(int64_t q, int64_t nw, int64_t total) {
+  const int64_t w = (q * nw + total - 1) / total;  // smallest w with w*total/nw >= q
+  return w < nw && split_begin(w, nw, total) == q;
+}
+
+}  // namespace g4

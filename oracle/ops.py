@@ -1,0 +1,280 @@
+"""CPU restatement of the reference's decode-layer ops (TEST INFRASTRUCTURE, not product code).
+
+Only `tests/`, `__graft_entry__.smoke()` and bench.py's CPU legs may import this module,
+and only as the checker. The product path (the CUDA library) never calls it.
+
+Every function restates the reference's PyTorch oracle with numpy, keeping each bf16
+rounding point the oracle has (each torch op on bf16 tensors computes in f32 and rounds
+its result to bf16 once). Values travel as raw bf16 bit patterns (`uint16`) so that the
+rounding is explicit. Citations use `FOG` = `furiosa-opt-gemma4-12B/` of the reference:
+
+- RMSNorm                     FOG/scripts/reference/gemma4.py:75-89
+- scaled_projection           FOG/scripts/generate_references.py:265-274
+- RoPE (rotate_half form)     FOG/scripts/generate_references.py:213-220, gemma4.py:120-122
+- sliding_project_qkv         FOG/scripts/generate_references.py:291-334 (op: FOG/src/ops.rs:37-76)
+- sliding_attention_output    FOG/scripts/generate_references.py:337-355 (op: FOG/src/ops.rs:130-146)
+- decoder_feedforward         FOG/scripts/generate_references.py:358-414 (op: FOG/src/ops.rs:201-239)
+- MLP / GeGLU (gelu tanh)     FOG/scripts/reference/gemma4.py:189-197
+- sliding_attention           FOG/src/device/sliding/attention.rs:7-199 (op: FOG/src/ops.rs:118-128);
+                              the reference's tests never pin this op, so its restatement follows
+                              the device semantics and is validated against a float64 softmax.
+
+Dot products accumulate in f32 (numpy sgemv); the reference's torch CPU kernels also
+accumulate in f32 but in their own order, so results agree to within the reference
+harness tolerances (FOG/src/bin/test_kernels.rs:447-465), not bit for bit.
+"""
+
+from __future__ import annotations
+
+import numpy as np
+
+EPS = np.float32(1e-6)
+F4_MAGNITUDES = np.array([0.0, 0.5, 1.0, 1.5, 2.0, 3.0, 4.0, 6.0], dtype=np.float32)
+
+
+# --- bf16 / f8 / f4 value helpers -------------------------------------------------------
+
+def bf16_to_f32(bits) -> np.ndarray:
+    return (np.asarray(bits, dtype=np.uint16).astype(np.uint32) << np.uint32(16)).view(np.float32)
+
+
+def f32_to_bf16(values) -> np.ndarray:
+    """Round-half-to-even to bf16 bits; NaN stays NaN (quiet), inf stays inf."""
+    v = np.ascontiguousarray(values, dtype=np.float32)
+    bits = v.view(np.uint32)
+    rounding = np.uint32(0x7FFF) + ((bits >> np.uint32(16)) & np.uint32(1))
+    out = ((bits + rounding) >> np.uint32(16)).astype(np.uint16)
+    nan = np.isnan(v)
+    if nan.any():
+        out[nan] = ((bits[nan] >> np.uint32(16)) | np.uint32(0x40)).astype(np.uint16)
+    return out
+
+
+def bf16_round(values) -> np.ndarray:
+    """f32 -> nearest bf16 value, returned as f32."""
+    return bf16_to_f32(f32_to_bf16(values))
+
+
+def e4m3_to_f32(codes) -> np.ndarray:
+    """Decode float8_e4m3fn codes exactly (bias 7, subnormals, 0x7F/0xFF = NaN)."""
+    c = np.asarray(codes, dtype=np.uint8)
+    sign = np.where(c & 0x80, -1.0, 1.0).astype(np.float32)
+    e = ((c >> 3) & 0xF).astype(np.int32)
+    m = (c & 0x7).astype(np.float32)
+    normal = np.ldexp(1.0 + m / 8.0, e - 7).astype(np.float32)
+    sub = np.ldexp(m / 8.0, -6).astype(np.float32)
+    out = sign * np.where(e == 0, sub, normal)
+    out = np.where((c & 0x7F) == 0x7F, np.float32(np.nan), out)
+    return out.astype(np.float32)
+
+
+def f4_unpack(packed, rows: int, cols: int) -> np.ndarray:
+    """Packed e2m1 (low nibble = even element) -> f32 values [rows, cols]."""
+    p = np.asarray(packed, dtype=np.uint8).reshape(rows, cols // 2)
+    codes = np.empty((rows, cols), dtype=np.uint8)
+    codes[:, 0::2] = p & 0x0F
+    codes[:, 1::2] = p >> 4
+    mag = F4_MAGNITUDES[codes & 0x7]
+    return np.where(codes & 0x8, -mag, mag).astype(np.float32)
+
+
+def nvfp4_dequant(packed, block_scale_codes, rows: int, cols: int) -> np.ndarray:
+    """codes * e4m3 local scale repeated over 16 elements (generate_references.py:396-398).
+
+    Every product is exact in f32 and in bf16 (2-bit x 4-bit significands), so the
+    reference's `.to(torch.bfloat16)` of the folded weight (generate_references.py:407)
+    changes nothing.
+    """
+    values = f4_unpack(packed, rows, cols)
+    scale = e4m3_to_f32(block_scale_codes).reshape(rows, cols // 16)
+    return values * np.repeat(scale, 16, axis=1)
+
+
+# --- building blocks -------------------------------------------------------------------
+
+def rms_norm(x_bits, weight_bits=None, eps=EPS) -> np.ndarray:
+    """gemma4.RMSNorm on bf16 input over the last axis (gemma4.py:83-89).
+
+    x.float(); x * rsqrt(mean(x^2) + eps); optionally * weight.float(); to bf16.
+    """
+    x = bf16_to_f32(x_bits)
+    ms = np.mean(x.astype(np.float64) ** 2, axis=-1, keepdims=True).astype(np.float32)
+    inv = (np.float32(1.0) / np.sqrt(ms + np.float32(eps))).astype(np.float32)
+    y = (x * inv).astype(np.float32)
+    if weight_bits is not None:
+        y = (y * bf16_to_f32(weight_bits)).astype(np.float32)
+    return f32_to_bf16(y)
+
+
+def scaled_projection(x_bits, weight_f32, scale_f32) -> np.ndarray:
+    """bf16((x.float() @ codes.T) * scale) with an f32 contraction (generate_references.py:265-274)."""
+    x = bf16_to_f32(x_bits)
+    acc = (weight_f32 @ x).astype(np.float32)
+    return f32_to_bf16(acc * np.asarray(scale_f32, dtype=np.float32))
+
+
+def linear_bf16(x_bits, weight_f32) -> np.ndarray:
+    """bf16 nn.Linear (no bias): f32 contraction of bf16 operands, one rounding to bf16."""
+    x = bf16_to_f32(x_bits)
+    return f32_to_bf16((weight_f32 @ x).astype(np.float32))
+
+
+def gelu_tanh(x_bits) -> np.ndarray:
+    """F.gelu(approximate='tanh') on bf16: f32 math, bf16 result (gemma4.py:197)."""
+    x = bf16_to_f32(x_bits)
+    k = np.float32(0.7978845608028654)  # sqrt(2/pi)
+    cube = (x * x * x).astype(np.float32)
+    inner = k * (x + np.float32(0.044715) * cube)
+    y = np.float32(0.5) * x * (np.float32(1.0) + np.tanh(inner.astype(np.float32)))
+    return f32_to_bf16(y.astype(np.float32))
+
+
+def mul_bf16(a_bits, b_bits) -> np.ndarray:
+    return f32_to_bf16(bf16_to_f32(a_bits) * bf16_to_f32(b_bits))
+
+
+def add_bf16(a_bits, b_bits) -> np.ndarray:
+    return f32_to_bf16(bf16_to_f32(a_bits) + bf16_to_f32(b_bits))
+
+
+def rope(x_bits, cos_bits, sin_bits) -> np.ndarray:
+    """(x*cos) + (rotate_half(x)*sin), each product and the sum rounded to bf16.
+
+    `sin_bits` is the UNMODIFIED sin row; generate_references.py:213-220 with
+    gemma4.rotate_half (gemma4.py:120-122).
+    """
+    x = bf16_to_f32(x_bits)
+    half = x.shape[-1] // 2
+    rot = np.concatenate([-x[..., half:], x[..., :half]], axis=-1)
+    a = bf16_round(x * bf16_to_f32(cos_bits))
+    b = bf16_round(rot * bf16_to_f32(sin_bits))
+    return f32_to_bf16(a + b)
+
+
+def rope_tables(head_dim: int, theta: float, partial_rotary_factor: float, pos: int):
+    """cos/sin rows in f64, narrowed to f32 (generate_references.py:184-197)."""
+    angles = int(partial_rotary_factor * head_dim // 2)
+    inv_freq = 1.0 / (np.float64(theta) ** (np.arange(0, 2 * angles, 2, dtype=np.float64) / head_dim))
+    inv_freq = np.concatenate([inv_freq, np.zeros(head_dim // 2 - angles, dtype=np.float64)])
+    emb = np.concatenate([pos * inv_freq, pos * inv_freq])
+    return np.cos(emb).astype(np.float32), np.sin(emb).astype(np.float32)
+
+
+def negate_low_half(sin: np.ndarray) -> np.ndarray:
+    """The kernel-side sin operand: low half pre-negated (generate_references.py:200-210)."""
+    out = np.array(sin, dtype=np.float32, copy=True)
+    out[: len(out) // 2] *= -1.0
+    return out
+
+
+# --- the ops -----------------------------------------------------------------------------
+
+def sliding_project_qkv(x, q_weight, k_weight, v_weight, q_scale, k_scale, v_scale,
+                        input_rms_weight, q_rms_weight, k_rms_weight, cos_row, sin_row_kernel,
+                        n_kv=8, group=2, head_dim=256):
+    """Fused QKV op (generate_references.py:321-334).
+
+    Weights are e4m3 code arrays [rows, H]; scales/gammas are bf16 bits; `cos_row` and
+    `sin_row_kernel` are the bf16 rows at the position, `sin_row_kernel` with its low half
+    pre-negated exactly as the kernel receives it. Returns (q [n_kv, group, D], k [n_kv, D],
+    v [n_kv, D]) as bf16 bits.
+    """
+    h = rms_norm(x, input_rms_weight)
+    sin_true = np.array(sin_row_kernel, dtype=np.uint16, copy=True)
+    sin_true[: head_dim // 2] ^= np.uint16(0x8000)
+    q = scaled_projection(h, e4m3_to_f32(q_weight), bf16_to_f32(q_scale)).reshape(n_kv * group, head_dim)
+    q = rope(rms_norm(q, q_rms_weight), cos_row, sin_true)
+    k = scaled_projection(h, e4m3_to_f32(k_weight), bf16_to_f32(k_scale)).reshape(n_kv, head_dim)
+    k = rope(rms_norm(k, k_rms_weight), cos_row, sin_true)
+    v = scaled_projection(h, e4m3_to_f32(v_weight), bf16_to_f32(v_scale)).reshape(n_kv, head_dim)
+    v = rms_norm(v, None)
+    return q.reshape(n_kv, group, head_dim), k, v
+
+
+def sliding_attention_output(x, post_rms_weight, o_weight, o_scale, residual):
+    """O projection -> post-attention RMSNorm -> residual add (generate_references.py:353-355)."""
+    projected = scaled_projection(np.asarray(x).reshape(-1), e4m3_to_f32(o_weight), bf16_to_f32(o_scale))
+    normalized = rms_norm(projected, post_rms_weight)
+    return add_bf16(residual, normalized)
+
+
+def feedforward_dense(residual, pre_rms_weight, post_rms_weight, w_up, w_gate, w_down,
+                      g_up, g_gate, g_down, layer_scalar_bits):
+    """decoder_feedforward on already-dequantised f32 weights (generate_references.py:404-413).
+
+    `g_*` are the f32 reciprocal global scales (1.0 for a per-channel FP8 variant whose
+    channel scale has been folded in by `feedforward_fp8`). Returns the new residual bits.
+    """
+    h = rms_norm(residual, pre_rms_weight)
+    up = f32_to_bf16(bf16_to_f32(linear_bf16(h, w_up)) * np.float32(g_up))
+    gate = f32_to_bf16(bf16_to_f32(linear_bf16(h, w_gate)) * np.float32(g_gate))
+    act = mul_bf16(gelu_tanh(gate), up)
+    down = f32_to_bf16(bf16_to_f32(linear_bf16(act, w_down)) * np.float32(g_down))
+    normalized = rms_norm(down, post_rms_weight)
+    summed = add_bf16(residual, normalized)
+    return mul_bf16(summed, np.full(summed.shape, np.asarray(layer_scalar_bits).reshape(-1)[0], dtype=np.uint16))
+
+
+def decoder_feedforward(residual, pre_rms_weight, up_packed, gate_packed, down_packed,
+                        up_scale, gate_scale, down_scale, up_global, gate_global, down_global,
+                        post_rms_weight, layer_scalar, hidden=3840, inter=15360):
+    """NVFP4 GeGLU FFN with the reference epilogue (FOG/src/ops.rs:201-239)."""
+    w_up = nvfp4_dequant(up_packed, up_scale, inter, hidden)
+    w_gate = nvfp4_dequant(gate_packed, gate_scale, inter, hidden)
+    w_down = nvfp4_dequant(down_packed, down_scale, hidden, inter)
+    return feedforward_dense(residual, pre_rms_weight, post_rms_weight, w_up, w_gate, w_down,
+                             np.float32(up_global), np.float32(gate_global), np.float32(down_global),
+                             layer_scalar)
+
+
+def feedforward_fp8(residual, pre_rms_weight, up_w, gate_w, down_w, up_s, gate_s, down_s,
+                    post_rms_weight, layer_scalar, hidden=3840, inter=15360):
+    """FP8-per-channel FFN variant (no counterpart op in the reference).
+
+    Each projection is the reference's `scaled_projection` (generate_references.py:265-274):
+    bf16((x @ codes.T) * channel_scale) with an f32 per-output-channel scale, wrapped in the
+    same pre-RMS / GeGLU / post-RMS / residual / layer-scalar epilogue as
+    `decoder_feedforward`.
+    """
+    h = rms_norm(residual, pre_rms_weight)
+    up = scaled_projection(h, e4m3_to_f32(up_w).reshape(inter, hidden), up_s)
+    gate = scaled_projection(h, e4m3_to_f32(gate_w).reshape(inter, hidden), gate_s)
+    act = mul_bf16(gelu_tanh(gate), up)
+    down = scaled_projection(act, e4m3_to_f32(down_w).reshape(hidden, inter), down_s)
+    normalized = rms_norm(down, post_rms_weight)
+    summed = add_bf16(residual, normalized)
+    return mul_bf16(summed, np.full(summed.shape, np.asarray(layer_scalar).reshape(-1)[0], dtype=np.uint16))
+
+
+def sliding_attention(q, k_cache, v_cache, mask, scale=1.0):
+    """Restatement of the device attention (FOG/src/device/sliding/attention.rs:27-196).
+
+    q: bf16 bits [Ns, G, D]; caches: bf16 bits [T, Ns, D]; mask: f32 [T] (0/1 row).
+    s = bf16(scale * q.k) in f32; m = max over ALL slots; p = min(exp(s - m), mask);
+    sum = sum(p) + 1e-6; o = bf16(sum_t bf16(p_t) * v_t); out = bf16(o / sum).
+    """
+    qf = bf16_to_f32(q)
+    kf = bf16_to_f32(k_cache)
+    vf = bf16_to_f32(v_cache)
+    mk = np.asarray(mask, dtype=np.float32)
+    scores = np.einsum("ngd,tnd->ngt", qf, kf, dtype=np.float32, optimize=True).astype(np.float32)
+    s = bf16_round(scores * np.float32(scale))
+    m = s.max(axis=-1, keepdims=True)
+    p = np.minimum(np.exp((s - m).astype(np.float32)).astype(np.float32), mk[None, None, :])
+    total = (p.sum(axis=-1, dtype=np.float32) + EPS).astype(np.float32)
+    w = bf16_round(p)
+    o = bf16_round(np.einsum("ngt,tnd->ngd", w, vf, dtype=np.float32, optimize=True).astype(np.float32))
+    return f32_to_bf16((o / total[..., None]).astype(np.float32))
+
+
+def attention_float64(q, k_cache, v_cache, mask, scale=1.0):
+    """Masked softmax attention in float64 (the mathematical op, for validating the above)."""
+    qf = bf16_to_f32(q).astype(np.float64)
+    kf = bf16_to_f32(k_cache).astype(np.float64)
+    vf = bf16_to_f32(v_cache).astype(np.float64)
+    s = np.einsum("ngd,tnd->ngt", qf, kf) * scale
+    s = np.where(np.asarray(mask)[None, None, :] > 0, s, -np.inf)
+    s = s - s.max(axis=-1, keepdims=True)
+    p = np.exp(s)
+    p /= p.sum(axis=-1, keepdims=True)
+    return np.einsum("ngt,tnd->ngd", p, vf)

@@ -1,0 +1,115 @@
+#!/usr/bin/env python3
+"""Regenerate the golden fixtures in this directory from the reference's own CPU oracle.
+
+Run from the repository root in a container that has the reference workspace mounted:
+
+    python tests/golden/make_golden.py --reference /path/to/moa-workspace
+
+It imports (never copies) the reference's `furiosa-opt-gemma4-12B/scripts/generate_references.py`
+and `scripts/reference/gemma4.py` and records, per seeded run:
+
+- `reference_runs.npz`  expected outputs of `gen_sliding_project_qkv`, `gen_sliding_attention_output`
+                        and `gen_decoder_feedforward` for runs 0..8 (runs 0-2 are the official
+                        fixture, 3-8 the extra seeds of moa-dev/extra_seeds.py:103-111), stored as
+                        bf16 bit patterns, plus every input checksum the generator records.
+- `qkv_boundary.npz`    the two QKV cancellation cases from the reference's committed
+                        boundary suite (expected q/k/v and input checksums).
+- `ffn_stress.npz`      the committed FFN-stress expectation (3840 x bf16 0x3ecf).
+- `attention_sdpa.npz`  outputs of gemma4.py's own sliding attention call
+                        (`F.scaled_dot_product_attention(..., scale=1.0)`, gemma4.py:179-181) on
+                        seeded decode-step inputs: the only pin the reference offers for the
+                        attention op, which its grader never tests.
+
+Nothing at test time reads the reference; the GPU box only sees these fixtures.
+"""
+
+from __future__ import annotations
+
+import argparse
+import sys
+import time
+from pathlib import Path
+
+import numpy as np
+
+HERE = Path(__file__).resolve().parent
+RUNS = range(9)
+
+
+def bits(t) -> np.ndarray:
+    import torch
+    return t.detach().to(torch.bfloat16).contiguous().view(torch.int16).numpy().view(np.uint16).reshape(-1).copy()
+
+
+def main() -> None:
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--reference", type=Path, default=Path("/root/reference"))
+    ap.add_argument("--runs", type=int, default=len(RUNS))
+    args = ap.parse_args()
+
+    fog = args.reference / "furiosa-opt-gemma4-12B"
+    sys.path.insert(0, str(fog / "scripts"))
+    sys.path.insert(0, str(fog / "scripts" / "reference"))
+    import torch
+    import generate_references as ref  # the reference oracle, imported in place
+
+    torch.set_grad_enabled(False)
+    ref.verify_rope_matches_upstream()
+
+    out: dict[str, np.ndarray] = {}
+    for run in range(args.runs):
+        for name, build in ref.TESTS.items():
+            t0 = time.time()
+            outputs, checks = build(run)
+            for label, tensor in outputs.items():
+                out[f"run{run}.{name}.{label}"] = bits(tensor)
+            for label, value in checks.items():
+                out[f"run{run}.{name}.check.{label}"] = np.array([value], dtype=np.int64)
+            print(f"run {run} {name:28s} {time.time() - t0:6.1f}s", flush=True)
+    if out:
+        np.savez_compressed(HERE / "reference_runs.npz", **out)
+
+    from safetensors.numpy import load_file
+    cand = args.reference / "moa-dev" / "experiments" / "candidates"
+    boundary = load_file(str(cand / "qkv-scalar-sub-vrf" / "boundary-suite" / "fixtures" / "boundary.safetensors"))
+    keep = {}
+    for key, value in boundary.items():
+        if ".expected." in key:
+            keep[key] = bits(torch.from_numpy(value))
+        elif ".checksum." in key:
+            keep[key] = value.astype(np.int64)
+    np.savez_compressed(HERE / "qkv_boundary.npz", **keep)
+
+    stress = (cand / "ffn-native-down-weighted-residual" / "full-ffn-stress" / "expected-bf16.bin").read_bytes()
+    np.savez_compressed(HERE / "ffn_stress.npz", expected=np.frombuffer(stress, dtype="<u2").copy())
+
+    # gemma4.py's own attention math for one decode step: q [1,16,1,256] against K/V of T slots
+    # (each KV head repeated for its 2 query heads), 0/1 mask row -> boolean attn_mask.
+    import fixture_prng as fp
+    import torch.nn.functional as F
+    att = {}
+    for case, (t_len, valid, qscale) in enumerate([(1024, 1024, 1.0 / 16), (1024, 300, 1.0 / 16),
+                                                   (1024, 1, 1.0 / 16), (1024, 1024, 1.0)]):
+        seed = f"golden.attention.case{case}"
+        q = fp.bf16_signs(f"{seed}.q", 16 * 256, qscale)
+        k = fp.bf16_uniform(f"{seed}.k", t_len * 8 * 256, -1.0, 1.0)
+        v = fp.bf16_uniform(f"{seed}.v", t_len * 8 * 256, -1.0, 1.0)
+        mask = (np.arange(t_len) < valid).astype(np.float32)
+        qt = torch.from_numpy(q.view(np.int16)).view(torch.bfloat16).reshape(1, 16, 1, 256)
+        kt = torch.from_numpy(k.view(np.int16)).view(torch.bfloat16).reshape(t_len, 8, 256).permute(1, 0, 2)
+        vt = torch.from_numpy(v.view(np.int16)).view(torch.bfloat16).reshape(t_len, 8, 256).permute(1, 0, 2)
+        kt = kt.repeat_interleave(2, dim=0).unsqueeze(0)
+        vt = vt.repeat_interleave(2, dim=0).unsqueeze(0)
+        o = F.scaled_dot_product_attention(qt, kt, vt, attn_mask=torch.from_numpy(mask > 0).view(1, 1, 1, t_len),
+                                           scale=1.0)
+        # q/k/v are re-synthesised at test time from the same seeds (oracle/prng.py is pinned
+        # byte-for-byte by the run checksums), so only the shape parameters are stored.
+        att[f"case{case}.params"] = np.array([t_len, valid], dtype=np.int64)
+        att[f"case{case}.qscale"] = np.array([qscale], dtype=np.float64)
+        att[f"case{case}.expected"] = bits(o.reshape(-1))
+    np.savez_compressed(HERE / "attention_sdpa.npz", **att)
+    print("wrote", sorted(p.name for p in HERE.glob("*.npz")))
+
+
+if __name__ == "__main__":
+    main()

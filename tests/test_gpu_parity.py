@@ -1,0 +1,237 @@
+"""GPU parity: the CUDA ops (called through the C ABI) against the reference's golden outputs
+and the CPU oracle, on the reference's own seeded inputs (runs 0-8), its cancellation and
+stress cases, plus cache-integrity, determinism and error-path checks."""
+
+import numpy as np
+import pytest
+
+from oracle import ops as oracle
+from oracle import synth
+from helpers import ATOL, within
+
+pytestmark = pytest.mark.gpu
+RUNS = range(9)
+SENTINEL_K, SENTINEL_V, SENTINEL_Q = 0x3E80, 0xBF00, 0x3FC0
+
+
+def dev_tensor(arr, dtype=None):
+    import torch
+
+    a = np.ascontiguousarray(arr)
+    if a.dtype == np.uint16:
+        t = torch.from_numpy(a.view(np.int16)).view(torch.bfloat16)
+    else:
+        t = torch.from_numpy(a)
+    t = t.cuda()
+    return t.to(dtype) if dtype is not None else t
+
+
+def host_bits(t):
+    import torch
+
+    t = t.detach().cpu().contiguous()
+    if t.dtype == torch.bfloat16:
+        return t.view(torch.int16).numpy().view(np.uint16)
+    return t.numpy()
+
+
+# --------------------------------------------------------------------------------- QKV
+
+def run_qkv(device, d, ring=1024, rows=32768, fill=(SENTINEL_K, SENTINEL_V, SENTINEL_Q)):
+    from g4b200 import ops
+
+    cos = np.zeros((rows, 256), np.uint16)
+    sin = np.zeros((rows, 256), np.uint16)
+    cos[d["pos"]] = d["cos_row"]
+    sin[d["pos"]] = d["sin_row"]
+    k_cache = dev_tensor(np.full((ring, 8, 256), fill[0], np.uint16))
+    v_cache = dev_tensor(np.full((ring, 8, 256), fill[1], np.uint16))
+    q_out = dev_tensor(np.full((8, 2, 256), fill[2], np.uint16))
+    ops.sliding_project_qkv(device, dev_tensor(d["x"]), dev_tensor(d["q_weight"]), dev_tensor(d["k_weight"]),
+                            dev_tensor(d["v_weight"]), dev_tensor(d["q_weight_scale"]),
+                            dev_tensor(d["k_weight_scale"]), dev_tensor(d["v_weight_scale"]),
+                            dev_tensor(d["input_rms_weight"]), dev_tensor(d["q_rms_weight"]),
+                            dev_tensor(d["k_rms_weight"]), dev_tensor(d["kv_offset"]), dev_tensor(d["rope_offset"]),
+                            dev_tensor(cos), dev_tensor(sin), k_cache, v_cache, q_out)
+    device.check()
+    return host_bits(q_out), host_bits(k_cache), host_bits(v_cache)
+
+
+def check_untouched(cache, slot, fill):
+    mask = np.ones(cache.shape[0], bool)
+    mask[slot] = False
+    assert np.all(cache[mask] == fill), "a KV-cache slot the op does not target changed"
+
+
+@pytest.mark.parametrize("run", RUNS)
+def test_qkv_matches_reference(device, run, golden_runs):
+    d = synth.sliding_project_qkv(run)
+    q, kc, vc = run_qkv(device, d)
+    slot = d["pos"] % 1024
+    for label, got in (("q", q.reshape(-1)), ("k", kc[slot].reshape(-1)), ("v", vc[slot].reshape(-1))):
+        ok, maxd, exact = within(golden_runs[f"run{run}.sliding_project_qkv.expected.{label}"], got,
+                                 ATOL["sliding_project_qkv"])
+        assert ok, (label, maxd)
+        assert exact > 0.99, (label, exact)
+    check_untouched(kc, slot, SENTINEL_K)
+    check_untouched(vc, slot, SENTINEL_V)
+
+
+@pytest.mark.parametrize("case", [0, 1])
+def test_qkv_cancellation_cases(device, case, golden_boundary):
+    """Tiny activations after pre-RMS must survive (the reference's E53 regression)."""
+    d = synth.qkv_boundary_inputs(case)
+    q, kc, vc = run_qkv(device, d)
+    slot = d["pos"] % 1024
+    for label, got in (("q", q.reshape(-1)), ("k", kc[slot].reshape(-1)), ("v", vc[slot].reshape(-1))):
+        ok, maxd, exact = within(golden_boundary[f"case{case}.expected.{label}"], got, ATOL["sliding_project_qkv"])
+        assert ok, (label, maxd)
+        # at least as close as the reference oracle itself, which is bit-exact here
+        assert exact > 0.99, (label, exact)
+    check_untouched(kc, slot, SENTINEL_K)
+    check_untouched(vc, slot, SENTINEL_V)
+
+
+def test_qkv_ring_2048_and_bad_offset(device):
+    """BASELINE's [8 heads, 2048 slots] ring; an out-of-ring offset writes nothing and is reported."""
+    from g4b200 import G4Error
+
+    d = synth.sliding_project_qkv(4)
+    d["kv_offset"] = np.array([(1500) * 8 * 256 * 2], np.int32)
+    q, kc, vc = run_qkv(device, d, ring=2048)
+    ref_q, ref_k, ref_v = oracle.sliding_project_qkv(d["x"], d["q_weight"], d["k_weight"], d["v_weight"],
+                                                     d["q_weight_scale"], d["k_weight_scale"], d["v_weight_scale"],
+                                                     d["input_rms_weight"], d["q_rms_weight"], d["k_rms_weight"],
+                                                     d["cos_row"], d["sin_row"])
+    assert within(ref_k, kc[1500], ATOL["sliding_project_qkv"])[0]
+    assert within(ref_v, vc[1500], ATOL["sliding_project_qkv"])[0]
+    check_untouched(kc, 1500, SENTINEL_K)
+
+    d["kv_offset"] = np.array([2048 * 8 * 256 * 2], np.int32)  # one slot past the ring
+    with pytest.raises(G4Error) as err:
+        run_qkv(device, d, ring=2048)
+    assert err.value.flags & 1
+
+
+# --------------------------------------------------------------------------------- O
+
+def run_o(device, x, gamma, w, s, residual):
+    from g4b200 import ops
+
+    res = dev_tensor(residual)
+    ops.sliding_attention_output(device, dev_tensor(x), dev_tensor(gamma), dev_tensor(w), dev_tensor(s), res)
+    device.check()
+    return host_bits(res)
+
+
+@pytest.mark.parametrize("run", RUNS)
+def test_o_matches_reference(device, run, golden_runs):
+    d = synth.sliding_attention_output(run)
+    got = run_o(device, d["x"], d["post_attn_rms_weight"], d["o_weight"], d["o_weight_scale"], d["residual"])
+    ok, maxd, exact = within(golden_runs[f"run{run}.sliding_attention_output.expected"], got,
+                             ATOL["sliding_attention_output"])
+    assert ok, maxd
+    assert exact > 0.99, exact
+
+
+# --------------------------------------------------------------------------------- FFN
+
+def run_ffn(device, d):
+    from g4b200 import ops
+
+    res = dev_tensor(d["residual"])
+    ops.decoder_feedforward(device, res, dev_tensor(d["pre_ff_rms_weight"]), dev_tensor(d["up_weight_packed"]),
+                            dev_tensor(d["gate_weight_packed"]), dev_tensor(d["down_weight_packed"]),
+                            dev_tensor(d["up_weight_scale"]), dev_tensor(d["gate_weight_scale"]),
+                            dev_tensor(d["down_weight_scale"]), dev_tensor(d["up_global_scale"]),
+                            dev_tensor(d["gate_global_scale"]), dev_tensor(d["down_global_scale"]),
+                            dev_tensor(d["post_ff_rms_weight"]), dev_tensor(d["layer_scalar"]))
+    device.check()
+    return host_bits(res)
+
+
+@pytest.mark.parametrize("run", RUNS)
+def test_ffn_matches_reference(device, run, golden_runs):
+    d = synth.decoder_feedforward(run)
+    got = run_ffn(device, d)
+    ok, maxd, exact = within(golden_runs[f"run{run}.decoder_feedforward.expected"], got, ATOL["decoder_feedforward"])
+    assert ok, maxd
+    assert exact > 0.95, exact
+
+
+def test_ffn_stress_exact(device, golden_stress):
+    """The correlated case whose every output is bf16 0x3ecf must come out bit-exact."""
+    got = run_ffn(device, synth.ffn_stress())
+    assert np.array_equal(got, golden_stress["expected"]), np.unique(got, return_counts=True)
+
+
+def test_ffn_deterministic(device):
+    d = synth.decoder_feedforward(5)
+    a = run_ffn(device, d)
+    b = run_ffn(device, d)
+    assert np.array_equal(a, b)
+
+
+# --------------------------------------------------------------------------------- attention
+
+def run_attention(device, q, k, v, mask, scale=1.0):
+    import torch
+    from g4b200 import ops
+
+    out = torch.zeros((8, 2, 256), dtype=torch.bfloat16, device="cuda")
+    ops.sliding_attention(device, dev_tensor(q), dev_tensor(k), dev_tensor(v), dev_tensor(mask), out, scale=scale)
+    device.check()
+    return host_bits(out)
+
+
+@pytest.mark.parametrize("case", range(4))
+def test_attention_matches_oracle_and_reference_sdpa(device, case, golden_attention):
+    from test_oracle import attention_inputs
+
+    q, k, v, mask, qs = attention_inputs(golden_attention, case)
+    got = run_attention(device, q, k, v, mask)
+    ref = oracle.sliding_attention(q, k, v, mask)
+    ok, maxd, exact = within(ref, got, 0.01)
+    assert ok, maxd
+    assert exact > 0.9, exact
+    atol = 0.01 if qs < 1.0 else ATOL["sliding_attention_output"]
+    assert within(golden_attention[f"case{case}.expected"], got, atol)[0]
+
+
+@pytest.mark.parametrize("ring,scale", [(1024, 1.0 / 16), (4096, 1.0 / 16), (2048, 1.0)])
+def test_attention_rings_and_scales(device, ring, scale):
+    """BASELINE config c2 (L in {1024, 4096}, scale 1/16) and a masked ring."""
+    from oracle import prng
+
+    q = prng.bf16_signs(f"attn.{ring}.q", 16 * 256, 1.0).reshape(8, 2, 256)
+    k = prng.bf16_uniform(f"attn.{ring}.k", ring * 8 * 256, -1.0, 1.0).reshape(ring, 8, 256)
+    v = prng.bf16_uniform(f"attn.{ring}.v", ring * 8 * 256, -1.0, 1.0).reshape(ring, 8, 256)
+    mask = (np.arange(ring) <= ring * 3 // 4).astype(np.float32)
+    got = run_attention(device, q, k, v, mask, scale)
+    ref = oracle.sliding_attention(q, k, v, mask, scale)
+    ok, maxd, _ = within(ref, got, 0.01)
+    assert ok, maxd
+
+
+# --------------------------------------------------------------------------------- host checks
+
+def test_host_rejects_bad_arguments(device):
+    import torch
+    from g4b200 import G4Error, _abi, ops
+
+    d = synth.sliding_attention_output(0)
+    x, g, w, s, r = (dev_tensor(d[k]) for k in ("x", "post_attn_rms_weight", "o_weight", "o_weight_scale",
+                                                  "residual"))
+    with pytest.raises(ValueError):
+        ops.sliding_attention_output(device, x.reshape(-1), g, w, s, r)
+    with pytest.raises(TypeError):
+        ops.sliding_attention_output(device, x.float(), g, w, s, r)
+    # a misaligned pointer is refused by the C ABI itself
+    buf = torch.zeros(3840 + 8, dtype=torch.bfloat16, device="cuda")
+    st = _abi.lib().g4_sliding_attention_output(device.handle, x.data_ptr(), g.data_ptr(), w.data_ptr(), s.data_ptr(),
+                                                 buf.data_ptr() + 2, None)
+    assert st == _abi.G4_ERR_MISALIGNED
+    st = _abi.lib().g4_sliding_attention(device.handle, x.data_ptr(), w.data_ptr(), w.data_ptr(), s.data_ptr(),
+                                         r.data_ptr(), 1000, 1.0, None)
+    assert st == _abi.G4_ERR_UNSUPPORTED
+    device.check()
