@@ -112,7 +112,12 @@ g4_status g4_ctx_create(int device, g4_ctx** out) {
   const size_t off_partials = off_counters + g4::kCounterCount * sizeof(uint32_t);
   const size_t off_y = off_partials + g4::kPartialFloats * sizeof(float);
   const size_t off_act = off_y + g4::kYElems * sizeof(uint16_t);
-  const size_t total = off_act + size_t(64) * g4::kL * sizeof(uint16_t);
+  const size_t off_trace = off_act + size_t(64) * g4::kL * sizeof(uint16_t);
+#ifdef G4_TRACE
+  const size_t total = off_trace + size_t(65536 + 4096 * 32 * 8) * sizeof(uint64_t);
+#else
+  const size_t total = off_trace;
+#endif
   e = cudaMalloc(&ctx->scratch, total);
   if (e == cudaSuccess) e = cudaMemset(ctx->scratch, 0, total);
   if (e == cudaSuccess) e = g4::prepare_proj_kernels();
@@ -130,6 +135,11 @@ g4_status g4_ctx_create(int device, g4_ctx** out) {
   ctx->sc.partials = reinterpret_cast<float*>(base + off_partials);
   ctx->sc.y = reinterpret_cast<uint16_t*>(base + off_y);
   ctx->sc.act = reinterpret_cast<uint16_t*>(base + off_act);
+#ifdef G4_TRACE
+  ctx->sc.trace = reinterpret_cast<uint64_t*>(base + off_trace);
+#else
+  ctx->sc.trace = nullptr;
+#endif
   *out = ctx;
   return G4_OK;
 }
@@ -263,5 +273,17 @@ g4_status g4_decoder_feedforward(g4_ctx* ctx, uint16_t* residual_hbm, const uint
                 down_global_scale, post_ff_rms_weight, layer_scalar};
   return cuda_status(ctx, g4::launch_ffn_nvfp4(a, env_of(ctx, stream)), "decoder_feedforward launch");
 }
+
+#ifdef G4_TRACE
+// Profiling builds only (not part of the public header): copy the phase timestamps out.
+g4_status g4_trace_read(g4_ctx* ctx, uint64_t* host, int n) {
+  if (!ctx || !host || n < 0 || n > 65536 + 4096 * 32 * 8) return G4_ERR_INVALID_ARGUMENT;
+  DeviceGuard guard(ctx->device);
+  cudaError_t e = cudaDeviceSynchronize();
+  if (e == cudaSuccess) e = cudaMemcpy(host, ctx->sc.trace, size_t(n) * sizeof(uint64_t), cudaMemcpyDeviceToHost);
+  if (e == cudaSuccess) e = cudaMemset(ctx->sc.trace, 0, size_t(65536 + 4096 * 32 * 8) * sizeof(uint64_t));
+  return e == cudaSuccess ? G4_OK : G4_ERR_CUDA;
+}
+#endif
 
 }  // extern "C"

@@ -7,11 +7,13 @@
 //   sum[g] = sum_t p[g,t] + 1e-6
 //   out    = bf16( bf16(sum_t bf16(p[g,t]) v[t]) / sum[g] )
 //
-// One thread-block cluster of kClusterCtas CTAs per KV head; each CTA owns a contiguous
-// run of ring slots, streams that run's K rows and then its V rows through a TMA bulk-copy
-// ring, and the CTAs exchange their score maxima and output partials through distributed
-// shared memory, so the result equals a single pass over the whole ring (partials are
-// combined in rank order: deterministic).
+// One thread-block cluster of CL CTAs per KV head (CL = 16 where the GPU schedules clusters
+// of 16, else 8); each CTA owns a contiguous run of ring slots. At entry every CTA starts
+// copying its V rows into shared memory (cp.async, no registers held) and loads its K rows
+// straight into registers, so the whole working set is requested in one round trip. The CTAs
+// exchange their score maxima and output partials through distributed shared memory; rank 0
+// adds the partials in rank order, so the result equals one pass over the ring and does not
+// depend on timing.
 #include <cooperative_groups.h>
 
 #include "g4_ops.cuh"
@@ -21,57 +23,56 @@ namespace cg = cooperative_groups;
 namespace g4 {
 namespace {
 
-constexpr int kClusterCtas = 8;
-constexpr int kTile = 32;            // ring slots per bulk-copy tile
-constexpr int kStages = 4;           // tiles in flight per CTA
-constexpr int kThreads = 256;
-constexpr int kRowBytes = kDs * 2;   // one head's row in one slot
-constexpr int kTileBytes = kTile * kRowBytes;
-constexpr int kMaxSlotsPerCta = 1024;
+constexpr int kThreads = 512;
+constexpr int kWarps = kThreads / 32;
+constexpr int kRowBytes = kDs * 2;      // one head's row in one slot
+constexpr int kVChunk = 256;            // V rows resident in shared memory at a time (128 KB)
+constexpr int kKBatch = 16;             // K rows per warp held in registers at a time
+constexpr int kMaxSlotsPerCta = 1024;   // scores kept for the whole run of a CTA
 
 struct AttnSmem {
-  uint8_t ring[kStages][kTileBytes];
-  float score[kGs][kMaxSlotsPerCta];  // scores, then bf16-rounded probabilities
-  float opart[kGs][kDs];
+  uint8_t v[kVChunk * kRowBytes];
+  float score[kMaxSlotsPerCta][kGs];  // scores, then bf16-rounded probabilities
+  float opart[4][kGs][kDs];           // four slot residues, reduced before publishing
   float pub_max[kGs];
   float pub_sum[kGs];
-  float red[kThreads / 32][kGs];
-  uint64_t bars[kStages];
+  float red[kWarps][kGs];
 };
 
+__device__ __forceinline__ void cp_async16(void* smem_dst, const void* src) {
+  asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(smem_u32(smem_dst)), "l"(src) : "memory");
+}
+__device__ __forceinline__ void cp_async_commit() { asm volatile("cp.async.commit_group;" ::: "memory"); }
+__device__ __forceinline__ void cp_async_wait_all() { asm volatile("cp.async.wait_group 0;" ::: "memory"); }
+
+template <int CL>
 __global__ void __launch_bounds__(kThreads, 1) attention_kernel(AttnArgs a, Scratch sc) {
   extern __shared__ __align__(1024) uint8_t smem_raw[];
   AttnSmem& sm = *reinterpret_cast<AttnSmem*>(smem_raw);
   cg::cluster_group cluster = cg::this_cluster();
   const int rank = int(cluster.block_rank());
-  const int head = blockIdx.x / kClusterCtas;
+  const int head = blockIdx.x / CL;
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
-  const int per_cta = a.ring_len / kClusterCtas;
-  const int n_tiles = per_cta / kTile;
+  const int per_cta = a.ring_len / CL;      // <= kMaxSlotsPerCta, a multiple of kWarps
+  const int per_warp = per_cta / kWarps;
   const int slot0 = rank * per_cta;
-
-  if (tid == 0) {
-    for (int i = 0; i < kStages; ++i) mbar_init(&sm.bars[i], 1);
-    fence_mbar_init();
-  }
-  __syncthreads();
+  G4_STAMP(sc, 0);
 
   pdl_wait_primary();  // q and the cache rows come from the preceding QKV op
   pdl_launch_dependents();
+  G4_STAMP(sc, 1);
 
-  const uint64_t policy = l2_evict_first_policy();
-  // tile i < n_tiles: K rows; n_tiles <= i < 2 n_tiles: V rows
-  auto issue = [&](int i) {
-    if (warp != 0) return;
-    const uint16_t* cache = i < n_tiles ? a.k_cache : a.v_cache;
-    const int first = slot0 + (i % n_tiles) * kTile;
-    uint64_t* bar = &sm.bars[i % kStages];
-    if (lane == 0) mbar_arrive_expect_tx(bar, kTileBytes);
-    __syncwarp();
-    const uint16_t* src = cache + (size_t(first + lane) * kNs + head) * kDs;
-    bulk_g2s(sm.ring[i % kStages] + lane * kRowBytes, src, kRowBytes, bar, policy);
+  // V rows [first, first + count) of this CTA -> shared memory, asynchronously (16 B per request)
+  auto fetch_v = [&](int first, int count) {
+    const int chunks = count * (kRowBytes / 16);
+    for (int c = tid; c < chunks; c += kThreads) {
+      const int r = c / (kRowBytes / 16), o = c % (kRowBytes / 16);
+      cp_async16(sm.v + r * kRowBytes + o * 16,
+                 reinterpret_cast<const uint8_t*>(a.v_cache + (size_t(slot0 + first + r) * kNs + head) * kDs) + o * 16);
+    }
+    cp_async_commit();
   };
-  for (int i = 0; i < kStages && i < 2 * n_tiles; ++i) issue(i);
+  fetch_v(0, per_cta < kVChunk ? per_cta : kVChunk);
 
   // q rows of the two query heads of this KV head: lane holds dims 8*lane .. 8*lane+7
   float qv[kGs][8];
@@ -83,17 +84,19 @@ __global__ void __launch_bounds__(kThreads, 1) attention_kernel(AttnArgs a, Scra
     for (int j = 0; j < 8; ++j) qv[g][j] = bf16_to_f32(b[j]);
   }
 
-  bool ok = true;
-  // phase 1: scores
-  for (int i = 0; i < n_tiles; ++i) {
-    ok = ok && mbar_wait(&sm.bars[i % kStages], uint32_t((i / kStages) & 1), sc.err);
-    if (ok) {
-      const uint8_t* tile = sm.ring[i % kStages];
+  // phase 1: this warp's K rows straight into registers (kKBatch at a time), then its scores
+  const int wslot0 = warp * per_warp;
+  for (int kb0 = 0; kb0 < per_warp; kb0 += kKBatch) {
+    uint4 kr[kKBatch];
 #pragma unroll
-      for (int r = 0; r < kTile / (kThreads / 32); ++r) {
-        const int row = warp * (kTile / (kThreads / 32)) + r;
-        const uint4 raw = *reinterpret_cast<const uint4*>(tile + row * kRowBytes + lane * 16);
-        const uint16_t* kb = reinterpret_cast<const uint16_t*>(&raw);
+    for (int r = 0; r < kKBatch; ++r)
+      if (kb0 + r < per_warp)
+        kr[r] = __ldcs(reinterpret_cast<const uint4*>(a.k_cache + (size_t(slot0 + wslot0 + kb0 + r) * kNs + head) * kDs) +
+                       lane);
+#pragma unroll
+    for (int r = 0; r < kKBatch; ++r) {
+      if (kb0 + r < per_warp) {
+        const uint16_t* kb = reinterpret_cast<const uint16_t*>(&kr[r]);
         float d0 = 0.f, d1 = 0.f;
 #pragma unroll
         for (int j = 0; j < 8; ++j) {
@@ -107,23 +110,20 @@ __global__ void __launch_bounds__(kThreads, 1) attention_kernel(AttnArgs a, Scra
           d1 += __shfl_xor_sync(0xffffffffu, d1, o);
         }
         if (lane == 0) {
-          sm.score[0][i * kTile + row] = bf16_round(a.scale * d0);
-          sm.score[1][i * kTile + row] = bf16_round(a.scale * d1);
+          sm.score[wslot0 + kb0 + r][0] = bf16_round(a.scale * d0);
+          sm.score[wslot0 + kb0 + r][1] = bf16_round(a.scale * d1);
         }
       }
     }
-    __syncthreads();
-    if (i + kStages < 2 * n_tiles) {
-      asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
-      issue(i + kStages);
-    }
   }
+  __syncthreads();
+  G4_STAMP(sc, 2);
 
   // global max over the whole ring (every CTA of the cluster)
   float m0 = -INFINITY, m1 = -INFINITY;
   for (int t = tid; t < per_cta; t += kThreads) {
-    m0 = fmaxf(m0, sm.score[0][t]);
-    m1 = fmaxf(m1, sm.score[1][t]);
+    m0 = fmaxf(m0, sm.score[t][0]);
+    m1 = fmaxf(m1, sm.score[t][1]);
   }
   m0 = warp_max(m0);
   m1 = warp_max(m1);
@@ -134,7 +134,7 @@ __global__ void __launch_bounds__(kThreads, 1) attention_kernel(AttnArgs a, Scra
   __syncthreads();
   if (tid == 0) {
     float a0 = -INFINITY, a1 = -INFINITY;
-    for (int w = 0; w < kThreads / 32; ++w) {
+    for (int w = 0; w < kWarps; ++w) {
       a0 = fmaxf(a0, sm.red[w][0]);
       a1 = fmaxf(a1, sm.red[w][1]);
     }
@@ -143,113 +143,153 @@ __global__ void __launch_bounds__(kThreads, 1) attention_kernel(AttnArgs a, Scra
   }
   cluster.sync();
   float gm0 = -INFINITY, gm1 = -INFINITY;
-  for (int r = 0; r < kClusterCtas; ++r) {
+  for (int r = 0; r < CL; ++r) {
     const float* pm = cluster.map_shared_rank(sm.pub_max, r);
     gm0 = fmaxf(gm0, pm[0]);
     gm1 = fmaxf(gm1, pm[1]);
   }
+  G4_STAMP(sc, 3);
 
-  // probabilities and the local denominator
+  // probabilities and the local denominator (fixed summation order)
   float s0 = 0.f, s1 = 0.f;
   for (int t = tid; t < per_cta; t += kThreads) {
     const float mk = a.mask[slot0 + t];
-    const float p0 = fminf(expf(sm.score[0][t] - gm0), mk);
-    const float p1 = fminf(expf(sm.score[1][t] - gm1), mk);
+    const float p0 = fminf(expf(sm.score[t][0] - gm0), mk);
+    const float p1 = fminf(expf(sm.score[t][1] - gm1), mk);
     s0 += p0;
     s1 += p1;
-    sm.score[0][t] = bf16_round(p0);
-    sm.score[1][t] = bf16_round(p1);
+    sm.score[t][0] = bf16_round(p0);
+    sm.score[t][1] = bf16_round(p1);
   }
 #pragma unroll
   for (int o = 16; o; o >>= 1) {
     s0 += __shfl_xor_sync(0xffffffffu, s0, o);
     s1 += __shfl_xor_sync(0xffffffffu, s1, o);
   }
-  __syncthreads();  // all reads of sm.red (max) are done
+  __syncthreads();  // every read of sm.red (the maxima) is done
   if (lane == 0) {
     sm.red[warp][0] = s0;
     sm.red[warp][1] = s1;
   }
+  cp_async_wait_all();
   __syncthreads();
   if (tid == 0) {
     float a0 = 0.f, a1 = 0.f;
-    for (int w = 0; w < kThreads / 32; ++w) {
+    for (int w = 0; w < kWarps; ++w) {
       a0 += sm.red[w][0];
       a1 += sm.red[w][1];
     }
     sm.pub_sum[0] = a0;
     sm.pub_sum[1] = a1;
   }
+  G4_STAMP(sc, 4);
 
-  // phase 2: o = sum_t bf16(p) v, one output dim per thread
-  float o0 = 0.f, o1 = 0.f;
-  for (int i = n_tiles; i < 2 * n_tiles; ++i) {
-    ok = ok && mbar_wait(&sm.bars[i % kStages], uint32_t((i / kStages) & 1), sc.err);
-    if (ok) {
-      const uint16_t* tile = reinterpret_cast<const uint16_t*>(sm.ring[i % kStages]);
-      const int base = (i - n_tiles) * kTile;
-#pragma unroll 8
-      for (int r = 0; r < kTile; ++r) {
-        const float vf = bf16_to_f32(tile[r * kDs + tid]);
-        o0 = fmaf(sm.score[0][base + r], vf, o0);
-        o1 = fmaf(sm.score[1][base + r], vf, o1);
+  // phase 2: o = sum_t bf16(p) v. Thread (res, pair) covers dims 2*pair, 2*pair+1 of both
+  // query heads over the slots t = res (mod 4), one resident chunk of V rows at a time.
+  {
+    const int res = tid >> 7, pair = tid & 127;
+    float o00 = 0.f, o01 = 0.f, o10 = 0.f, o11 = 0.f;
+    for (int c0 = 0; c0 < per_cta; c0 += kVChunk) {
+      const int rows = per_cta - c0 < kVChunk ? per_cta - c0 : kVChunk;
+      if (c0 > 0) {  // later chunks of a long ring: refill the buffer
+        __syncthreads();
+        fetch_v(c0, rows);
+        cp_async_wait_all();
+        __syncthreads();
+      }
+      for (int t = res; t < rows; t += 4) {
+        const uint32_t vv = *reinterpret_cast<const uint32_t*>(sm.v + t * kRowBytes + pair * 4);
+        const float v0 = bf16_to_f32(uint16_t(vv & 0xffff)), v1 = bf16_to_f32(uint16_t(vv >> 16));
+        const float w0 = sm.score[c0 + t][0], w1 = sm.score[c0 + t][1];
+        o00 = fmaf(w0, v0, o00);
+        o01 = fmaf(w0, v1, o01);
+        o10 = fmaf(w1, v0, o10);
+        o11 = fmaf(w1, v1, o11);
       }
     }
-    __syncthreads();
-    if (i + kStages < 2 * n_tiles) {
-      asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
-      issue(i + kStages);
-    }
+    sm.opart[res][0][2 * pair] = o00;
+    sm.opart[res][0][2 * pair + 1] = o01;
+    sm.opart[res][1][2 * pair] = o10;
+    sm.opart[res][1][2 * pair + 1] = o11;
   }
-  sm.opart[0][tid] = o0;
-  sm.opart[1][tid] = o1;
+  __syncthreads();
+  {
+    const int g = tid >> 8, d = tid & 255;
+    sm.opart[0][g][d] = ((sm.opart[0][g][d] + sm.opart[1][g][d]) + sm.opart[2][g][d]) + sm.opart[3][g][d];
+  }
   cluster.sync();
+  G4_STAMP(sc, 5);
 
   if (rank == 0) {
-    float t0 = 0.f, t1 = 0.f, z0 = 0.f, z1 = 0.f;
-    for (int r = 0; r < kClusterCtas; ++r) {
-      const float* op = cluster.map_shared_rank(&sm.opart[0][0], r);
+    const int g = tid >> 8, d = tid & 255;
+    float o = 0.f, z = 0.f;
+    for (int r = 0; r < CL; ++r) {
+      const float* op = cluster.map_shared_rank(&sm.opart[0][0][0], r);
       const float* ps = cluster.map_shared_rank(sm.pub_sum, r);
-      t0 += op[tid];
-      t1 += op[kDs + tid];
-      z0 += ps[0];
-      z1 += ps[1];
+      o += op[g * kDs + d];
+      z += ps[g];
     }
-    z0 += kEps;
-    z1 += kEps;
-    if (ok) {
-      a.out[(head * kGs + 0) * kDs + tid] = f32_to_bf16(bf16_round(t0) / z0);
-      a.out[(head * kGs + 1) * kDs + tid] = f32_to_bf16(bf16_round(t1) / z1);
-    }
+    z += kEps;
+    a.out[(head * kGs + g) * kDs + d] = f32_to_bf16(bf16_round(o) / z);
   }
   cluster.sync();  // keep every CTA's shared memory alive until rank 0 has read it
+  G4_STAMP(sc, 6);
 }
+
+int g_cluster = 0;  // 16 or 8, decided once per process
 
 }  // namespace
 
 cudaError_t prepare_attention_kernels() {
-  return cudaFuncSetAttribute(attention_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, int(sizeof(AttnSmem)));
+  cudaError_t e = cudaFuncSetAttribute(attention_kernel<16>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                       int(sizeof(AttnSmem)));
+  if (e == cudaSuccess)
+    e = cudaFuncSetAttribute(attention_kernel<16>, cudaFuncAttributeNonPortableClusterSizeAllowed, 1);
+  if (e == cudaSuccess)
+    e = cudaFuncSetAttribute(attention_kernel<8>, cudaFuncAttributeMaxDynamicSharedMemorySize, int(sizeof(AttnSmem)));
+  if (e != cudaSuccess) return e;
+  if (g_cluster == 0) {
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3(kNs * 16);
+    cfg.blockDim = dim3(kThreads);
+    cfg.dynamicSmemBytes = sizeof(AttnSmem);
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeClusterDimension;
+    attr[0].val.clusterDim.x = 16;
+    attr[0].val.clusterDim.y = 1;
+    attr[0].val.clusterDim.z = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    int clusters = 0;
+    const cudaError_t q = cudaOccupancyMaxActiveClusters(&clusters, attention_kernel<16>, &cfg);
+    // 16-CTA clusters only when all kNs of them fit on the GPU at once
+    g_cluster = (q == cudaSuccess && clusters >= kNs) ? 16 : 8;
+    if (q != cudaSuccess) (void)cudaGetLastError();
+  }
+  return cudaSuccess;
 }
 
-int attention_slot_multiple() { return kClusterCtas * kTile; }
-int attention_max_ring() { return kClusterCtas * kMaxSlotsPerCta; }
+int attention_slot_multiple() { return (g_cluster ? g_cluster : 8) * kWarps; }
+int attention_max_ring() { return 8 * kMaxSlotsPerCta; }
 
 cudaError_t launch_attention(const AttnArgs& a, const LaunchEnv& env) {
+  const int cl = g_cluster ? g_cluster : 8;
   cudaLaunchConfig_t cfg = {};
-  cfg.gridDim = dim3(kNs * kClusterCtas);
+  cfg.gridDim = dim3(kNs * cl);
   cfg.blockDim = dim3(kThreads);
   cfg.dynamicSmemBytes = sizeof(AttnSmem);
   cfg.stream = env.stream;
   cudaLaunchAttribute attr[2];
   attr[0].id = cudaLaunchAttributeClusterDimension;
-  attr[0].val.clusterDim.x = kClusterCtas;
+  attr[0].val.clusterDim.x = cl;
   attr[0].val.clusterDim.y = 1;
   attr[0].val.clusterDim.z = 1;
   attr[1].id = cudaLaunchAttributeProgrammaticStreamSerialization;
   attr[1].val.programmaticStreamSerializationAllowed = env.pdl ? 1 : 0;
   cfg.attrs = attr;
   cfg.numAttrs = 2;
-  return cudaLaunchKernelEx(&cfg, attention_kernel, a, env.sc);
+  return cl == 16 ? cudaLaunchKernelEx(&cfg, attention_kernel<16>, a, env.sc)
+                  : cudaLaunchKernelEx(&cfg, attention_kernel<8>, a, env.sc);
 }
 
 }  // namespace g4

@@ -30,6 +30,7 @@ enum : uint32_t {
   kErrKvOffset = 1u << 0,
   kErrRopeOffset = 1u << 1,
   kErrWaitTimeout = 1u << 2,
+  kErrInternal = 1u << 3,  // a launch-geometry invariant did not hold (work was skipped)
 };
 
 // Global scratch owned by a context. Counters are zero between launches: every kernel that
@@ -40,6 +41,7 @@ struct Scratch {
   float* partials;     // split-K partial row sums
   uint16_t* y;         // bf16 projected rows awaiting a grid-level epilogue
   uint16_t* act;       // bf16 GeGLU activation [M][L]
+  uint64_t* trace;     // per-CTA phase timestamps (profiling builds only; null otherwise)
 };
 constexpr int kCounterCount = 4096;
 constexpr int kCtaCounter = 4000;       // last-CTA ticket for whole-vector epilogues
@@ -72,6 +74,14 @@ __device__ __forceinline__ void cvt_e2m1x8_f16x2(uint32_t w, uint32_t& r0, uint3
       " cvt.rn.f16x2.e2m1x2 %2, b2;\n cvt.rn.f16x2.e2m1x2 %3, b3;\n}"
       : "=r"(r0), "=r"(r1), "=r"(r2), "=r"(r3)
       : "r"(w));
+}
+
+// Two bytes of e2m1 codes (four values, low nibble first) to two exact f16x2.
+__device__ __forceinline__ void cvt_e2m1x4_f16x2(uint32_t two_bytes, uint32_t& r0, uint32_t& r1) {
+  asm("{\n .reg .b8 b0, b1, b2, b3;\n mov.b32 {b0, b1, b2, b3}, %2;\n"
+      " cvt.rn.f16x2.e2m1x2 %0, b0;\n cvt.rn.f16x2.e2m1x2 %1, b1;\n}"
+      : "=r"(r0), "=r"(r1)
+      : "r"(two_bytes));
 }
 
 __device__ __forceinline__ uint32_t hmul2_u32(uint32_t a, uint32_t b) {
@@ -167,9 +177,41 @@ __device__ __forceinline__ void bulk_g2s(void* dst, const void* src, uint32_t by
 __device__ __forceinline__ void pdl_launch_dependents() { asm volatile("griddepcontrol.launch_dependents;" ::: "memory"); }
 __device__ __forceinline__ void pdl_wait_primary() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
 
+// Ticket atomics with release / acquire semantics (cheaper than a sequentially consistent
+// __threadfence). Writers of the published data are ordered before a release by a preceding
+// __syncwarp / __syncthreads; readers are ordered after an acquire by a following one.
+__device__ __forceinline__ uint32_t atomic_add_acq_rel_gpu(uint32_t* p, uint32_t v) {
+  uint32_t old;
+  asm volatile("atom.acq_rel.gpu.global.add.u32 %0, [%1], %2;" : "=r"(old) : "l"(p), "r"(v) : "memory");
+  return old;
+}
+__device__ __forceinline__ void fence_acq_rel_gpu() { asm volatile("fence.acq_rel.gpu;" ::: "memory"); }
+
 // L2-coherent loads for data other CTAs of the same launch wrote.
 __device__ __forceinline__ float ld_cg_f32(const float* p) { return __ldcg(p); }
 __device__ __forceinline__ uint4 ld_cg_u4(const void* p) { return __ldcg(reinterpret_cast<const uint4*>(p)); }
+
+// Phase timestamps for profiling builds (-DG4_TRACE): thread 0 of each CTA records
+// %globaltimer at numbered points of a kernel into trace[blockIdx.x * 16 + point].
+#ifdef G4_TRACE
+#define G4_STAMP(sc, point)                                                                     \
+  do {                                                                                          \
+    if ((sc).trace && threadIdx.x == 0) (sc).trace[blockIdx.x * 16 + (point)] = globaltimer_ns(); \
+  } while (0)
+// Per-warp stamps go to trace[65536 + (blockIdx.x * 32 + warp) * 8 + point] (lane 0).
+#define G4_STAMP_WARP(sc, point)                                                                         \
+  do {                                                                                                   \
+    if ((sc).trace && (threadIdx.x & 31) == 0)                                                           \
+      (sc).trace[65536 + (blockIdx.x * 32 + (threadIdx.x >> 5)) * 8 + (point)] = globaltimer_ns();       \
+  } while (0)
+#else
+#define G4_STAMP(sc, point) \
+  do {                      \
+  } while (0)
+#define G4_STAMP_WARP(sc, point) \
+  do {                           \
+  } while (0)
+#endif
 
 // ---------------------------------------------------------------------------------------
 // Reductions

@@ -13,42 +13,31 @@
 namespace g4 {
 namespace {
 
-// ---------------------------------------------------------------------------------------
-// Configuration (chunk K, warps per CTA, ring slots per warp)
+constexpr int kBatch = 256;  // K elements per unit
 
-constexpr int kQkvKc = 640, kQkvW = 8, kQkvS = 2;
-constexpr int kOKc = 512, kOW = 8, kOS = 2;
-constexpr int kUgKc = 256, kUgW = 8, kUgS = 4;
-constexpr int kDnKc = 1024, kDnW = 8, kDnS = 2;
+// (warps per CTA, units each warp keeps in flight) of each pass; one CTA per SM
+constexpr int kQkvW = 12, kQkvS = 2;
+constexpr int kOW = 12, kOS = 2;
+constexpr int kUgW = 12, kUgS = 2;
+constexpr int kDnW = 12, kDnS = 2;
 
-template <WFmt F, int NMAT, int KC, int W, int S>
-constexpr size_t smem_bytes(int k_total) {
-  return size_t(W) * S * SlotLayout<F, NMAT, KC>::kSlotBytes + 2 * size_t(act_col_stride(k_total)) +
-         size_t(W) * S * 8 + 64 * 8;
+template <WFmt F, int NMAT, int S, int W, int K>
+constexpr size_t smem_bytes() {
+  return engine_smem<NMAT>(W) + 2 * size_t(act_col_stride<kBatch>(K)) + 64 * 8;
 }
 
 struct SmemView {
-  uint8_t* slots;
+  uint8_t* engine;
   uint8_t* cols;
-  uint64_t* bars;
   double* red;
 };
-
-template <WFmt F, int NMAT, int KC, int W, int S>
-__device__ SmemView carve(uint8_t* smem, int k_total) {
+template <WFmt F, int NMAT, int S, int W, int K>
+__device__ SmemView carve(uint8_t* smem) {
   SmemView v;
-  v.slots = smem;
-  v.cols = smem + size_t(W) * S * SlotLayout<F, NMAT, KC>::kSlotBytes;
-  v.bars = reinterpret_cast<uint64_t*>(v.cols + 2 * size_t(act_col_stride(k_total)));
-  v.red = reinterpret_cast<double*>(v.bars + W * S);
+  v.engine = smem;
+  v.cols = smem + engine_smem<NMAT>(W);
+  v.red = reinterpret_cast<double*>(v.cols + 2 * size_t(act_col_stride<kBatch>(K)));
   return v;
-}
-
-__device__ __forceinline__ void init_warp_bars(uint64_t* bars, int s) {
-  if ((threadIdx.x & 31) == 0)
-    for (int i = 0; i < s; ++i) mbar_init(bars + i, 1);
-  fence_mbar_init();
-  __syncwarp();
 }
 
 __device__ __forceinline__ float gelu_tanh(float x) {
@@ -61,35 +50,65 @@ __device__ __forceinline__ float gelu_tanh(float x) {
 // Last-CTA ticket: returns true in every thread of the CTA that finished last.
 __device__ bool last_cta(uint32_t* counter) {
   __shared__ uint32_t is_last;
-  __threadfence();
-  __syncthreads();
+  __syncthreads();  // every thread's stores of this CTA precede the release below
   if (threadIdx.x == 0) {
-    const uint32_t before = atomicAdd(counter, 1u);
+    const uint32_t before = atomic_add_acq_rel_gpu(counter, 1u);
     is_last = (before == gridDim.x - 1) ? 1u : 0u;
   }
-  __syncthreads();
-  if (is_last) __threadfence();
+  __syncthreads();  // ... and the acquire precedes every thread's loads after it
   return is_last != 0;
 }
 
-// residual[i] <- bf16(residual[i] + RMSNorm(y)[i]) [ * layer_scalar ], over `n` elements, by
-// the whole CTA (y is bf16 scratch written by other CTAs of this launch).
-__device__ void residual_epilogue(const uint16_t* y, const uint16_t* gamma, uint16_t* residual, int n,
-                                  const uint16_t* layer_scalar, double* red) {
+// h = bf16((x * inv_rms(x)) * gamma) for a bf16 vector of K elements held as VPT vectors per
+// thread (gemma4.py:83-89). Returns the f32 values of h in `vals`.
+template <int K, int VPT>
+__device__ void rms_norm_vec(const uint16_t* x, const uint16_t* gamma, float (&vals)[VPT][8], double* red) {
+  float gv[VPT][8];
+  load_bf16_vec<VPT>(x, K, vals, true);
+  load_bf16_vec<VPT>(gamma, K, gv, false);
   double ss = 0.0;
-  for (int i = threadIdx.x; i < n; i += blockDim.x) {
-    const float v = bf16_to_f32(__ldcg(y + i));
-    ss += double(v) * double(v);
-  }
-  ss = block_sum_d(ss, red);
-  const float inv = rms_inverse(ss, n);
+#pragma unroll
+  for (int v = 0; v < VPT; ++v)
+#pragma unroll
+    for (int j = 0; j < 8; ++j) ss += double(vals[v][j]) * double(vals[v][j]);
+  const float inv = rms_inverse(block_sum_d(ss, red), K);
+#pragma unroll
+  for (int v = 0; v < VPT; ++v)
+#pragma unroll
+    for (int j = 0; j < 8; ++j) vals[v][j] = bf16_round((vals[v][j] * inv) * gv[v][j]);
+}
+
+// residual <- bf16(residual + RMSNorm_gamma(y)) [then bf16(. * layer_scalar)], H elements, whole
+// CTA, single pass (y is bf16 scratch written by other CTAs of this launch).
+template <int THREADS>
+__device__ void residual_epilogue(const uint16_t* y, const uint16_t* gamma, uint16_t* residual,
+                                  const uint16_t* layer_scalar, double* red) {
+  constexpr int VPT = (kH / 8 + THREADS - 1) / THREADS;
+  float yv[VPT][8], gv[VPT][8], rv[VPT][8];
+  load_bf16_vec<VPT>(y, kH, yv, true);
+  load_bf16_vec<VPT>(gamma, kH, gv, false);
+  load_bf16_vec<VPT>(residual, kH, rv, true);
+  double ss = 0.0;
+#pragma unroll
+  for (int v = 0; v < VPT; ++v)
+#pragma unroll
+    for (int j = 0; j < 8; ++j) ss += double(yv[v][j]) * double(yv[v][j]);
+  const float inv = rms_inverse(block_sum_d(ss, red), kH);
   const float lam = layer_scalar ? bf16_to_f32(layer_scalar[0]) : 1.0f;
-  for (int i = threadIdx.x; i < n; i += blockDim.x) {
-    const float v = bf16_to_f32(__ldcg(y + i));
-    const float nrm = bf16_round((v * inv) * bf16_to_f32(gamma[i]));
-    float r = bf16_round(bf16_to_f32(residual[i]) + nrm);
-    if (layer_scalar) r = bf16_round(r * lam);
-    residual[i] = f32_to_bf16(r);
+#pragma unroll
+  for (int v = 0; v < VPT; ++v) {
+    const int base = (threadIdx.x + v * blockDim.x) * 8;
+    if (base < kH) {
+      __align__(16) uint16_t out[8];
+#pragma unroll
+      for (int j = 0; j < 8; ++j) {
+        const float nrm = bf16_round((yv[v][j] * inv) * gv[v][j]);
+        float r = bf16_round(rv[v][j] + nrm);
+        if (layer_scalar) r = bf16_round(r * lam);
+        out[j] = f32_to_bf16(r);
+      }
+      *reinterpret_cast<uint4*>(residual + base) = *reinterpret_cast<const uint4*>(out);
+    }
   }
 }
 
@@ -101,6 +120,24 @@ __device__ void qkv_head_epilogue(const QkvArgs& a, const Scratch& sc, int head)
   const int base = head * kDs;
   const uint4 raw = ld_cg_u4(sc.y + base + lane * 8);
   const uint16_t* yb = reinterpret_cast<const uint16_t*>(&raw);
+  const bool is_q = head < kNs * kGs, is_k = !is_q && head < kNs * kGs + kNs;
+  const uint16_t* gamma = is_q ? a.q_rms : (is_k ? a.k_rms : nullptr);
+  uint4 graw = make_uint4(0, 0, 0, 0);
+  if (gamma) graw = *reinterpret_cast<const uint4*>(gamma + lane * 8);
+  const uint16_t* gb = reinterpret_cast<const uint16_t*>(&graw);
+  const int kv = *a.kv_offset, rope = *a.rope_offset;
+  const bool kv_ok = kv >= 0 && (kv % (kPs * 2)) == 0 && kv / (kPs * 2) < a.ring_len;
+  const bool rope_ok = rope >= 0 && (rope % (kDs * 2)) == 0 && rope / (kDs * 2) < a.rope_rows;
+  if (!kv_ok || !rope_ok) {
+    if (lane == 0) atomicOr(sc.err, (kv_ok ? 0u : kErrKvOffset) | (rope_ok ? 0u : kErrRopeOffset));
+    return;
+  }
+  const int slot = kv / (kPs * 2), row = rope / (kDs * 2);
+  uint4 craw = make_uint4(0, 0, 0, 0), sraw = make_uint4(0, 0, 0, 0);
+  if (is_q || is_k) {
+    craw = *reinterpret_cast<const uint4*>(a.cos + size_t(row) * kDs + lane * 8);
+    sraw = *reinterpret_cast<const uint4*>(a.sin + size_t(row) * kDs + lane * 8);
+  }
   float y[8];
   double ss = 0.0;
 #pragma unroll
@@ -110,34 +147,24 @@ __device__ void qkv_head_epilogue(const QkvArgs& a, const Scratch& sc, int head)
   }
   ss = warp_sum_d(ss);
   const float inv = rms_inverse(ss, kDs);
-  const bool is_q = head < kNs * kGs, is_k = !is_q && head < kNs * kGs + kNs;
-  const uint16_t* gamma = is_q ? a.q_rms : (is_k ? a.k_rms : nullptr);
   float nrm[8];
 #pragma unroll
   for (int j = 0; j < 8; ++j) {
     const float s = y[j] * inv;
-    nrm[j] = gamma ? bf16_round(s * bf16_to_f32(gamma[lane * 8 + j])) : bf16_round(s);
+    nrm[j] = gamma ? bf16_round(s * bf16_to_f32(gb[j])) : bf16_round(s);
   }
-  const int kv = *a.kv_offset, rope = *a.rope_offset;
-  const bool kv_ok = kv >= 0 && (kv % (kPs * 2)) == 0 && kv / (kPs * 2) < a.ring_len;
-  const bool rope_ok = rope >= 0 && (rope % (kDs * 2)) == 0 && rope / (kDs * 2) < a.rope_rows;
-  if (!kv_ok || !rope_ok) {
-    if (lane == 0) atomicOr(sc.err, (kv_ok ? 0u : kErrKvOffset) | (rope_ok ? 0u : kErrRopeOffset));
-    return;
-  }
-  const int slot = kv / (kPs * 2), row = rope / (kDs * 2);
-  uint16_t outb[8];
+  __align__(16) uint16_t outb[8];
   if (is_q || is_k) {
     // RoPE, half-swap form with the low half of `sin` pre-negated by the caller:
     // out[i] = bf16(bf16(n[i] cos[i]) + bf16(n[i ^ 128] sin'[i])). Element i ^ 128 lives in
     // lane ^ 16.
-    const uint16_t* crow = a.cos + size_t(row) * kDs + lane * 8;
-    const uint16_t* srow = a.sin + size_t(row) * kDs + lane * 8;
+    const uint16_t* cb = reinterpret_cast<const uint16_t*>(&craw);
+    const uint16_t* sb = reinterpret_cast<const uint16_t*>(&sraw);
 #pragma unroll
     for (int j = 0; j < 8; ++j) {
       const float partner = __shfl_xor_sync(0xffffffffu, nrm[j], 16);
-      const float c = bf16_round(nrm[j] * bf16_to_f32(crow[j]));
-      const float s = bf16_round(partner * bf16_to_f32(srow[j]));
+      const float c = bf16_round(nrm[j] * bf16_to_f32(cb[j]));
+      const float s = bf16_round(partner * bf16_to_f32(sb[j]));
       outb[j] = f32_to_bf16(c + s);
     }
   } else {
@@ -156,16 +183,23 @@ __device__ void qkv_head_epilogue(const QkvArgs& a, const Scratch& sc, int head)
 
 __global__ void __launch_bounds__(kQkvW * 32, 1) qkv_kernel(QkvArgs a, Scratch sc) {
   constexpr WFmt F = WFmt::kFp8;
+  constexpr int W = kQkvW, S = kQkvS;
   extern __shared__ __align__(1024) uint8_t smem[];
-  const SmemView sm = carve<F, 1, kQkvKc, kQkvW, kQkvS>(smem, kH);
-  const int warp = threadIdx.x >> 5;
-  uint8_t* my_slots = sm.slots + size_t(warp) * kQkvS * SlotLayout<F, 1, kQkvKc>::kSlotBytes;
-  uint64_t* my_bars = sm.bars + warp * kQkvS;
-  init_warp_bars(my_bars, kQkvS);
+  const SmemView sm = carve<F, 1, S, W, kH>(smem);
+  G4_STAMP(sc, 0);
+  pdl_wait_primary();
+  pdl_launch_dependents();
+  G4_STAMP(sc, 1);
+
+  // pre-attention RMSNorm -> exact f16 activation columns
+  constexpr int VPT = (kH / 8 + W * 32 - 1) / (W * 32);
+  float h[VPT][8];
+  rms_norm_vec<kH, VPT>(a.x, a.input_rms, h, sm.red);
+  const float unscale = build_act_columns<kBatch, VPT>(sm.cols, kH, h, reinterpret_cast<float*>(sm.red));
+  __syncthreads();
+  G4_STAMP(sc, 2);
 
   constexpr int kGroups = (kQs + 2 * kPs) / 16;
-  constexpr int kC = kH / kQkvKc;
-  const int64_t nw = int64_t(gridDim.x) * kQkvW, wid = int64_t(blockIdx.x) * kQkvW + warp;
   auto rows_of = [&](int grp, int) -> const uint8_t* {
     const int r = grp * 16;
     if (r < kQs) return a.q_weight + size_t(r) * kH;
@@ -173,52 +207,27 @@ __global__ void __launch_bounds__(kQkvW * 32, 1) qkv_kernel(QkvArgs a, Scratch s
     return a.v_weight + size_t(r - kQs - kPs) * kH;
   };
   auto no_scales = [](int, int) -> const uint8_t* { return nullptr; };
-  stream_prefill<F, 1, kQkvKc, kQkvS>(my_slots, my_bars, kH, wid, nw, kGroups, kH, 0, rows_of, no_scales);
-
-  pdl_wait_primary();
-  pdl_launch_dependents();
-
-  // pre-attention RMSNorm (gemma4.py:83-89) -> exact f16 activation columns
-  double ss = 0.0;
-  for (int i = threadIdx.x; i < kH; i += blockDim.x) {
-    const float v = bf16_to_f32(a.x[i]);
-    ss += double(v) * double(v);
-  }
-  ss = block_sum_d(ss, sm.red);
-  const float inv = rms_inverse(ss, kH);
-  auto h_of = [&](int i) { return bf16_round((bf16_to_f32(a.x[i]) * inv) * bf16_to_f32(a.input_rms[i])); };
-  const float unscale = build_act_columns(sm.cols, kH, h_of, reinterpret_cast<float*>(sm.red));
-  __syncthreads();
-
-  const int64_t total = int64_t(kGroups) * kC;
-  auto flush = [&](int grp, int cstart, int nch, const float (&v)[1][2]) {
-    if (!flush_piece<1>(sc.partials, sc.counters + grp, grp, kC, cstart, nch, v)) return;
+  auto finalize = [&](int grp, const float (&tot)[1]) {
     const int lane = threadIdx.x & 31;
-    const float tot = gather_group<1>(sc.partials, grp, kC, 0, nw, total);
     if (lane < 16) {
       const int r = grp * 16 + lane;
       const uint16_t sb = r < kQs ? a.q_scale[r] : (r < kQs + kPs ? a.k_scale[r - kQs] : a.v_scale[r - kQs - kPs]);
       // scaled_projection: bf16((x @ codes.T) * scale) (generate_references.py:265-274)
-      sc.y[r] = f32_to_bf16((tot * unscale) * bf16_to_f32(sb));
+      sc.y[r] = f32_to_bf16((tot[0] * unscale) * bf16_to_f32(sb));
     }
-    __threadfence();
     __syncwarp();
     uint32_t head_done = 0;
+    const int head = grp / (kDs / 16);
     if (lane == 0) {
-      sc.counters[grp] = 0;
-      const int head = grp / (kDs / 16);
-      const uint32_t before = atomicAdd(sc.counters + kHeadCounterBase + head, 1u);
+      const uint32_t before = atomic_add_acq_rel_gpu(sc.counters + kHeadCounterBase + head, 1u);
       head_done = before == uint32_t(kDs / 16 - 1);
       if (head_done) sc.counters[kHeadCounterBase + head] = 0;
     }
     head_done = __shfl_sync(0xffffffffu, head_done, 0);
-    if (head_done) {
-      __threadfence();
-      qkv_head_epilogue(a, sc, grp / (kDs / 16));
-    }
+    if (head_done) qkv_head_epilogue(a, sc, head);
   };
-  stream_gemv<F, 1, kQkvKc, kQkvS>(my_slots, my_bars, sm.cols, kH, wid, nw, kGroups, kH, 0, rows_of, no_scales,
-                                    flush, sc.err, true);
+  stream_gemv<F, 1, kBatch, S, W>(sm.engine, sm.cols, kH, kGroups, kH, 0, rows_of, no_scales, finalize, sc);
+  G4_STAMP(sc, 3);
 }
 
 // ---------------------------------------------------------------------------------------
@@ -226,46 +235,39 @@ __global__ void __launch_bounds__(kQkvW * 32, 1) qkv_kernel(QkvArgs a, Scratch s
 
 __global__ void __launch_bounds__(kOW * 32, 1) o_kernel(OArgs a, Scratch sc) {
   constexpr WFmt F = WFmt::kFp8;
+  constexpr int W = kOW, S = kOS;
   extern __shared__ __align__(1024) uint8_t smem[];
-  const SmemView sm = carve<F, 1, kOKc, kOW, kOS>(smem, kQs);
-  const int warp = threadIdx.x >> 5;
-  uint8_t* my_slots = sm.slots + size_t(warp) * kOS * SlotLayout<F, 1, kOKc>::kSlotBytes;
-  uint64_t* my_bars = sm.bars + warp * kOS;
-  init_warp_bars(my_bars, kOS);
-
-  constexpr int kGroups = kH / 16;
-  constexpr int kC = kQs / kOKc;
-  const int64_t nw = int64_t(gridDim.x) * kOW, wid = int64_t(blockIdx.x) * kOW + warp;
-  auto rows_of = [&](int grp, int) -> const uint8_t* { return a.o_weight + size_t(grp) * 16 * kQs; };
-  auto no_scales = [](int, int) -> const uint8_t* { return nullptr; };
-  stream_prefill<F, 1, kOKc, kOS>(my_slots, my_bars, kQs, wid, nw, kGroups, kQs, 0, rows_of, no_scales);
-
+  const SmemView sm = carve<F, 1, S, W, kQs>(smem);
+  G4_STAMP(sc, 0);
   pdl_wait_primary();
   pdl_launch_dependents();
+  G4_STAMP(sc, 1);
 
-  auto h_of = [&](int i) { return bf16_to_f32(a.x[i]); };
-  const float unscale = build_act_columns(sm.cols, kQs, h_of, reinterpret_cast<float*>(sm.red));
+  constexpr int VPT = (kQs / 8 + W * 32 - 1) / (W * 32);
+  float xv[VPT][8];
+  load_bf16_vec<VPT>(a.x, kQs, xv, true);
+  const float unscale = build_act_columns<kBatch, VPT>(sm.cols, kQs, xv, reinterpret_cast<float*>(sm.red));
   __syncthreads();
+  G4_STAMP(sc, 2);
 
-  const int64_t total = int64_t(kGroups) * kC;
-  auto flush = [&](int grp, int cstart, int nch, const float (&v)[1][2]) {
-    if (!flush_piece<1>(sc.partials, sc.counters + grp, grp, kC, cstart, nch, v)) return;
+  constexpr int kGroups = kH / 16;
+  auto rows_of = [&](int grp, int) -> const uint8_t* { return a.o_weight + size_t(grp) * 16 * kQs; };
+  auto no_scales = [](int, int) -> const uint8_t* { return nullptr; };
+  auto finalize = [&](int grp, const float (&tot)[1]) {
     const int lane = threadIdx.x & 31;
-    const float tot = gather_group<1>(sc.partials, grp, kC, 0, nw, total);
     if (lane < 16) {
       const int r = grp * 16 + lane;
-      sc.y[r] = f32_to_bf16((tot * unscale) * bf16_to_f32(a.o_scale[r]));
+      sc.y[r] = f32_to_bf16((tot[0] * unscale) * bf16_to_f32(a.o_scale[r]));
     }
-    __syncwarp();
-    if (lane == 0) sc.counters[grp] = 0;
   };
-  stream_gemv<F, 1, kOKc, kOS>(my_slots, my_bars, sm.cols, kQs, wid, nw, kGroups, kQs, 0, rows_of, no_scales, flush,
-                                sc.err, true);
+  stream_gemv<F, 1, kBatch, S, W>(sm.engine, sm.cols, kQs, kGroups, kQs, 0, rows_of, no_scales, finalize, sc);
+  G4_STAMP(sc, 3);
 
   if (last_cta(sc.counters + kCtaCounter)) {
-    residual_epilogue(sc.y, a.post_rms, a.residual, kH, nullptr, sm.red);
+    residual_epilogue<W * 32>(sc.y, a.post_rms, a.residual, nullptr, sm.red);
     if (threadIdx.x == 0) sc.counters[kCtaCounter] = 0;
   }
+  G4_STAMP(sc, 4);
 }
 
 // ---------------------------------------------------------------------------------------
@@ -273,100 +275,78 @@ __global__ void __launch_bounds__(kOW * 32, 1) o_kernel(OArgs a, Scratch sc) {
 
 __global__ void __launch_bounds__(kUgW * 32, 1) ffn_upgate_kernel(FfnArgs a, Scratch sc) {
   constexpr WFmt F = WFmt::kNvfp4;
+  constexpr int W = kUgW, S = kUgS;
   extern __shared__ __align__(1024) uint8_t smem[];
-  const SmemView sm = carve<F, 2, kUgKc, kUgW, kUgS>(smem, kH);
-  const int warp = threadIdx.x >> 5;
-  uint8_t* my_slots = sm.slots + size_t(warp) * kUgS * SlotLayout<F, 2, kUgKc>::kSlotBytes;
-  uint64_t* my_bars = sm.bars + warp * kUgS;
-  init_warp_bars(my_bars, kUgS);
+  const SmemView sm = carve<F, 2, S, W, kH>(smem);
+  G4_STAMP(sc, 0);
+  pdl_wait_primary();
+  pdl_launch_dependents();
+  G4_STAMP(sc, 1);
+
+  constexpr int VPT = (kH / 8 + W * 32 - 1) / (W * 32);
+  float h[VPT][8];
+  rms_norm_vec<kH, VPT>(a.residual, a.pre_rms, h, sm.red);
+  const float unscale = build_act_columns<kBatch, VPT>(sm.cols, kH, h, reinterpret_cast<float*>(sm.red));
+  __syncthreads();
+  G4_STAMP(sc, 2);
+  const float g_up = *a.up_global, g_gate = *a.gate_global;
 
   constexpr int kGroups = kL / 16;
-  constexpr int kC = kH / kUgKc;
-  const int64_t nw = int64_t(gridDim.x) * kUgW, wid = int64_t(blockIdx.x) * kUgW + warp;
   auto rows_of = [&](int grp, int m) -> const uint8_t* {
     return (m == 0 ? a.up_packed : a.gate_packed) + size_t(grp) * 16 * (kH / 2);
   };
   auto scales_of = [&](int grp, int m) -> const uint8_t* {
     return (m == 0 ? a.up_scale : a.gate_scale) + size_t(grp) * 16 * (kH / 16);
   };
-  stream_prefill<F, 2, kUgKc, kUgS>(my_slots, my_bars, kH, wid, nw, kGroups, kH / 2, kH / 16, rows_of, scales_of);
-
-  pdl_wait_primary();
-  pdl_launch_dependents();
-
-  // pre-feed-forward RMSNorm of the residual
-  double ss = 0.0;
-  for (int i = threadIdx.x; i < kH; i += blockDim.x) {
-    const float v = bf16_to_f32(a.residual[i]);
-    ss += double(v) * double(v);
-  }
-  ss = block_sum_d(ss, sm.red);
-  const float inv = rms_inverse(ss, kH);
-  auto h_of = [&](int i) { return bf16_round((bf16_to_f32(a.residual[i]) * inv) * bf16_to_f32(a.pre_rms[i])); };
-  const float unscale = build_act_columns(sm.cols, kH, h_of, reinterpret_cast<float*>(sm.red));
-  __syncthreads();
-  const float g_up = *a.up_global, g_gate = *a.gate_global;
-
-  const int64_t total = int64_t(kGroups) * kC;
-  auto flush = [&](int grp, int cstart, int nch, const float (&v)[2][2]) {
-    if (!flush_piece<2>(sc.partials, sc.counters + grp, grp, kC, cstart, nch, v)) return;
+  auto finalize = [&](int grp, const float (&tot)[2]) {
     const int lane = threadIdx.x & 31;
-    const float tu = gather_group<2>(sc.partials, grp, kC, 0, nw, total);
-    const float tg = gather_group<2>(sc.partials, grp, kC, 1, nw, total);
     if (lane < 16) {
       // GloballyScaled(nn.Linear): bf16(bf16(x @ W.T) * g)  (generate_references.py:358-372)
-      const float up = bf16_round(bf16_round(tu * unscale) * g_up);
-      const float gate = bf16_round(bf16_round(tg * unscale) * g_gate);
+      const float up = bf16_round(bf16_round(tot[0] * unscale) * g_up);
+      const float gate = bf16_round(bf16_round(tot[1] * unscale) * g_gate);
       // down_proj input: bf16(bf16(gelu_tanh(gate)) * up)  (gemma4.py:197)
       sc.act[grp * 16 + lane] = f32_to_bf16(bf16_round(gelu_tanh(gate)) * up);
     }
-    __syncwarp();
-    if (lane == 0) sc.counters[grp] = 0;
   };
-  stream_gemv<F, 2, kUgKc, kUgS>(my_slots, my_bars, sm.cols, kH, wid, nw, kGroups, kH / 2, kH / 16, rows_of,
-                                  scales_of, flush, sc.err, true);
+  stream_gemv<F, 2, kBatch, S, W>(sm.engine, sm.cols, kH, kGroups, kH / 2, kH / 16, rows_of, scales_of, finalize,
+                                  sc);
+  G4_STAMP(sc, 3);
 }
 
 __global__ void __launch_bounds__(kDnW * 32, 1) ffn_down_kernel(FfnArgs a, Scratch sc) {
   constexpr WFmt F = WFmt::kNvfp4;
+  constexpr int W = kDnW, S = kDnS;
   extern __shared__ __align__(1024) uint8_t smem[];
-  const SmemView sm = carve<F, 1, kDnKc, kDnW, kDnS>(smem, kL);
-  const int warp = threadIdx.x >> 5;
-  uint8_t* my_slots = sm.slots + size_t(warp) * kDnS * SlotLayout<F, 1, kDnKc>::kSlotBytes;
-  uint64_t* my_bars = sm.bars + warp * kDnS;
-  init_warp_bars(my_bars, kDnS);
-
-  constexpr int kGroups = kH / 16;
-  constexpr int kC = kL / kDnKc;
-  const int64_t nw = int64_t(gridDim.x) * kDnW, wid = int64_t(blockIdx.x) * kDnW + warp;
-  auto rows_of = [&](int grp, int) -> const uint8_t* { return a.down_packed + size_t(grp) * 16 * (kL / 2); };
-  auto scales_of = [&](int grp, int) -> const uint8_t* { return a.down_scale + size_t(grp) * 16 * (kL / 16); };
-  stream_prefill<F, 1, kDnKc, kDnS>(my_slots, my_bars, kL, wid, nw, kGroups, kL / 2, kL / 16, rows_of, scales_of);
-
+  const SmemView sm = carve<F, 1, S, W, kL>(smem);
+  G4_STAMP(sc, 8);
   pdl_wait_primary();
   pdl_launch_dependents();
+  G4_STAMP(sc, 9);
 
-  auto h_of = [&](int i) { return bf16_to_f32(__ldcg(sc.act + i)); };
-  const float unscale = build_act_columns(sm.cols, kL, h_of, reinterpret_cast<float*>(sm.red));
+  constexpr int VPT = (kL / 8 + W * 32 - 1) / (W * 32);
+  float av[VPT][8];
+  load_bf16_vec<VPT>(sc.act, kL, av, true);
+  const float unscale = build_act_columns<kBatch, VPT>(sm.cols, kL, av, reinterpret_cast<float*>(sm.red));
   __syncthreads();
+  G4_STAMP(sc, 10);
   const float g_down = *a.down_global;
 
-  const int64_t total = int64_t(kGroups) * kC;
-  auto flush = [&](int grp, int cstart, int nch, const float (&v)[1][2]) {
-    if (!flush_piece<1>(sc.partials, sc.counters + grp, grp, kC, cstart, nch, v)) return;
+  constexpr int kGroups = kH / 16;
+  auto rows_of = [&](int grp, int) -> const uint8_t* { return a.down_packed + size_t(grp) * 16 * (kL / 2); };
+  auto scales_of = [&](int grp, int) -> const uint8_t* { return a.down_scale + size_t(grp) * 16 * (kL / 16); };
+  auto finalize = [&](int grp, const float (&tot)[1]) {
     const int lane = threadIdx.x & 31;
-    const float tot = gather_group<1>(sc.partials, grp, kC, 0, nw, total);
-    if (lane < 16) sc.y[grp * 16 + lane] = f32_to_bf16(bf16_round(tot * unscale) * g_down);
-    __syncwarp();
-    if (lane == 0) sc.counters[grp] = 0;
+    if (lane < 16) sc.y[grp * 16 + lane] = f32_to_bf16(bf16_round(tot[0] * unscale) * g_down);
   };
-  stream_gemv<F, 1, kDnKc, kDnS>(my_slots, my_bars, sm.cols, kL, wid, nw, kGroups, kL / 2, kL / 16, rows_of,
-                                  scales_of, flush, sc.err, true);
+  stream_gemv<F, 1, kBatch, S, W>(sm.engine, sm.cols, kL, kGroups, kL / 2, kL / 16, rows_of, scales_of, finalize,
+                                  sc);
+  G4_STAMP(sc, 11);
 
   if (last_cta(sc.counters + kCtaCounter)) {
-    residual_epilogue(sc.y, a.post_rms, a.residual, kH, a.layer_scalar, sm.red);
+    residual_epilogue<W * 32>(sc.y, a.post_rms, a.residual, a.layer_scalar, sm.red);
     if (threadIdx.x == 0) sc.counters[kCtaCounter] = 0;
   }
+  G4_STAMP(sc, 12);
 }
 
 // ---------------------------------------------------------------------------------------
@@ -388,10 +368,10 @@ cudaError_t launch(void (*kernel)(Args...), int grid, int block, size_t smem, co
   return cudaLaunchKernelEx(&cfg, kernel, args...);
 }
 
-constexpr size_t kQkvSmem = smem_bytes<WFmt::kFp8, 1, kQkvKc, kQkvW, kQkvS>(kH);
-constexpr size_t kOSmem = smem_bytes<WFmt::kFp8, 1, kOKc, kOW, kOS>(kQs);
-constexpr size_t kUgSmem = smem_bytes<WFmt::kNvfp4, 2, kUgKc, kUgW, kUgS>(kH);
-constexpr size_t kDnSmem = smem_bytes<WFmt::kNvfp4, 1, kDnKc, kDnW, kDnS>(kL);
+constexpr size_t kQkvSmem = smem_bytes<WFmt::kFp8, 1, kQkvS, kQkvW, kH>();
+constexpr size_t kOSmem = smem_bytes<WFmt::kFp8, 1, kOS, kOW, kQs>();
+constexpr size_t kUgSmem = smem_bytes<WFmt::kNvfp4, 2, kUgS, kUgW, kH>();
+constexpr size_t kDnSmem = smem_bytes<WFmt::kNvfp4, 1, kDnS, kDnW, kL>();
 static_assert(kQkvSmem <= 227 * 1024 && kOSmem <= 227 * 1024 && kUgSmem <= 227 * 1024 && kDnSmem <= 227 * 1024,
               "shared memory budget");
 
@@ -420,7 +400,7 @@ cudaError_t launch_ffn_nvfp4(const FfnArgs& a, const LaunchEnv& env) {
   cudaError_t e = launch(ffn_upgate_kernel, env.sm_count, kUgW * 32, kUgSmem, env, a, env.sc);
   if (e != cudaSuccess) return e;
   LaunchEnv chained = env;
-  chained.pdl = true;  // the down pass overlaps its weight prefetch with the up/gate tail
+  chained.pdl = true;  // the down pass launches while the up/gate pass drains
   return launch(ffn_down_kernel, env.sm_count, kDnW * 32, kDnSmem, chained, a, env.sc);
 }
 
