@@ -3,6 +3,7 @@
 // of g4_proj.cu / g4_attention.cu and there is no host or CPU fallback.
 #include <cstdio>
 #include <cstring>
+#include <utility>
 
 #include "../../include/g4b200.h"
 #include "g4_ops.cuh"
@@ -19,6 +20,7 @@ struct g4_ctx {
   void* scratch = nullptr;
   size_t scratch_bytes = 0;
   g4::Scratch sc{};
+  g4::TmapCache maps;
   char last_error[256] = {0};
 };
 
@@ -49,6 +51,7 @@ g4_status cuda_status(g4_ctx* ctx, cudaError_t e, const char* where) {
 }
 
 bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
+bool aligned32(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 31u) == 0; }
 
 // Every pointer non-null and 16-byte aligned.
 g4_status check_ptrs(g4_ctx* ctx, std::initializer_list<std::pair<const void*, const char*>> ptrs) {
@@ -59,13 +62,14 @@ g4_status check_ptrs(g4_ctx* ctx, std::initializer_list<std::pair<const void*, c
   return G4_OK;
 }
 
-g4::LaunchEnv env_of(const g4_ctx* ctx, void* stream) {
+g4::LaunchEnv env_of(g4_ctx* ctx, void* stream) {
   g4::LaunchEnv env;
   env.device = ctx->device;
   env.sm_count = ctx->sm_count;
   env.stream = static_cast<cudaStream_t>(stream);
   env.pdl = ctx->overlap;
   env.sc = ctx->sc;
+  env.maps = &ctx->maps;
   return env;
 }
 
@@ -267,6 +271,11 @@ g4_status g4_decoder_feedforward(g4_ctx* ctx, uint16_t* residual_hbm, const uint
                                   {post_ff_rms_weight, "post_ff_rms_weight"},
                                   {layer_scalar, "layer_scalar"}});
   if (st != G4_OK) return st;
+  // packed e2m1 matrices are read by TMA as 16-code groups, which needs 32-byte alignment
+  for (const auto& p : {std::make_pair(static_cast<const void*>(up_weight_packed), "up_weight_packed"),
+                        std::make_pair(static_cast<const void*>(gate_weight_packed), "gate_weight_packed"),
+                        std::make_pair(static_cast<const void*>(down_weight_packed), "down_weight_packed")})
+    if (!aligned32(p.first)) return fail(ctx, G4_ERR_MISALIGNED, "pointer not 32-byte aligned: %s", p.second);
   DeviceGuard guard(ctx->device);
   g4::FfnArgs a{residual_hbm,      pre_ff_rms_weight, up_weight_packed, gate_weight_packed, down_weight_packed,
                 up_weight_scale,   gate_weight_scale, down_weight_scale, up_global_scale,   gate_global_scale,
@@ -275,6 +284,17 @@ g4_status g4_decoder_feedforward(g4_ctx* ctx, uint16_t* residual_hbm, const uint
 }
 
 #ifdef G4_TRACE
+// Profiling builds only (not part of the public header): copy scratch vectors out
+// (which = 0: y [65536] bf16, 1: act [15360] bf16).
+g4_status g4_debug_read(g4_ctx* ctx, int which, void* host, int bytes) {
+  if (!ctx || !host || bytes < 0 || bytes > 131072) return G4_ERR_INVALID_ARGUMENT;
+  DeviceGuard guard(ctx->device);
+  cudaError_t e = cudaDeviceSynchronize();
+  const void* src = which == 0 ? static_cast<const void*>(ctx->sc.y) : static_cast<const void*>(ctx->sc.act);
+  if (e == cudaSuccess) e = cudaMemcpy(host, src, size_t(bytes), cudaMemcpyDeviceToHost);
+  return e == cudaSuccess ? G4_OK : G4_ERR_CUDA;
+}
+
 // Profiling builds only (not part of the public header): copy the phase timestamps out.
 g4_status g4_trace_read(g4_ctx* ctx, uint64_t* host, int n) {
   if (!ctx || !host || n < 0 || n > 65536 + 4096 * 32 * 8) return G4_ERR_INVALID_ARGUMENT;

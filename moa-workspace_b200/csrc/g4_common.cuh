@@ -257,6 +257,30 @@ __device__ __forceinline__ float rms_inverse(double sumsq, int n) {
   return 1.0f / sqrtf(ms + kEps);
 }
 
+// Load a bf16 K-vector (16-byte aligned) as VPT 8-element vectors per thread, all loads in
+// flight at once. Elements past k read as zero. `coherent` loads go through L2 only (for data
+// another CTA or the preceding kernel wrote).
+template <int VPT>
+__device__ __forceinline__ void load_bf16_vec(const uint16_t* src, int k, float (&vals)[VPT][8], bool coherent) {
+  uint4 raw[VPT];
+#pragma unroll
+  for (int v = 0; v < VPT; ++v) {
+    const int base = (threadIdx.x + v * blockDim.x) * 8;
+    raw[v] = make_uint4(0, 0, 0, 0);
+    if (base < k)
+      raw[v] = coherent ? __ldcg(reinterpret_cast<const uint4*>(src + base)) : *reinterpret_cast<const uint4*>(src + base);
+  }
+#pragma unroll
+  for (int v = 0; v < VPT; ++v) {
+    const uint16_t* b = reinterpret_cast<const uint16_t*>(&raw[v]);
+#pragma unroll
+    for (int j = 0; j < 8; ++j) vals[v][j] = bf16_to_f32(b[j]);
+  }
+}
+
+// Global partial slots per split tile (a tile's K range spans at most this many CTAs).
+constexpr int kMaxCtasPerGroup = 8;
+
 // Split-K ranges: warp `w` of `nw` owns chunks [begin, end) of `total`.
 __device__ __forceinline__ int64_t split_begin(int64_t w, int64_t nw, int64_t total) { return (w * total) / nw; }
 

@@ -1,6 +1,7 @@
 // Host-side launch interface of the decode-layer kernels (internal to the library).
 #pragma once
 
+#include <cuda.h>
 #include <cuda_runtime.h>
 #include <stdint.h>
 
@@ -64,12 +65,37 @@ struct FfnArgs {
   const uint16_t* layer_scalar;
 };
 
+// TMA tensor maps of the weight matrices, encoded on the host once per (pointer, shape) and
+// kept by the context (encoding costs microseconds; a map is 128 bytes).
+class TmapCache {
+ public:
+  // Row-major uint8 matrix [rows, cols] (fp8 codes, e4m3 scales), box {box_cols, box_rows}.
+  cudaError_t u8(const void* base, uint64_t cols, uint64_t rows, uint32_t box_cols, uint32_t box_rows, bool swizzle128,
+                 CUtensorMap* out);
+  // Row-major packed e2m1 matrix [rows, cols/2 bytes], loaded as 128-element boxes unpacked to a
+  // byte per code in shared memory (the layout tcgen05 kind::f8f6f4 reads), 128-byte swizzle.
+  cudaError_t fp4(const void* base, uint64_t cols, uint64_t rows, uint32_t box_rows, CUtensorMap* out);
+
+ private:
+  struct Entry {
+    const void* base = nullptr;
+    uint64_t key = 0;
+    CUtensorMap map;
+  };
+  static constexpr int kEntries = 256;
+  Entry entries_[kEntries];
+  int next_ = 0;
+  const CUtensorMap* find(const void* base, uint64_t key) const;
+  void put(const void* base, uint64_t key, const CUtensorMap& map);
+};
+
 struct LaunchEnv {
   int device;
   int sm_count;
   cudaStream_t stream;
   bool pdl;  // launch with programmatic stream serialization
   Scratch sc;
+  TmapCache* maps;
 };
 
 cudaError_t prepare_proj_kernels();       // one-time attributes (dynamic shared memory)

@@ -2,43 +2,28 @@
 //   - fused QKV   (reference: furiosa-opt-gemma4-12B/src/ops.rs:37-76)
 //   - O + post-RMSNorm + residual (ops.rs:130-146)
 //   - NVFP4 GeGLU feed-forward with the weighted residual epilogue (ops.rs:201-239)
-// Each is one streaming pass over its weights (g4_stream.cuh) with the reference's
-// normalisation / RoPE / GeGLU / residual steps fused into the prologue and epilogues. The
+// Each is one tensor-core streaming pass over its weights (g4_gemv.cuh) with the reference's
+// normalisation / RoPE / GeGLU / residual steps fused into the prologue and the epilogues. The
 // rounding points are the reference oracle's (furiosa-opt-gemma4-12B/scripts/
 // generate_references.py:265-274, 291-414): every op that torch runs on bf16 tensors is
 // computed in f32 and rounded to bf16 once, at the same place.
+#include <cudaTypedefs.h>
+
+#include <utility>
+
+#include "g4_gemv.cuh"
 #include "g4_ops.cuh"
-#include "g4_stream.cuh"
 
 namespace g4 {
 namespace {
 
-constexpr int kBatch = 256;  // K elements per unit
-
-// (warps per CTA, units each warp keeps in flight) of each pass; one CTA per SM
-constexpr int kQkvW = 12, kQkvS = 2;
-constexpr int kOW = 12, kOS = 2;
-constexpr int kUgW = 12, kUgS = 2;
-constexpr int kDnW = 12, kDnS = 2;
-
-template <WFmt F, int NMAT, int S, int W, int K>
-constexpr size_t smem_bytes() {
-  return engine_smem<NMAT>(W) + 2 * size_t(act_col_stride<kBatch>(K)) + 64 * 8;
-}
-
-struct SmemView {
-  uint8_t* engine;
-  uint8_t* cols;
-  double* red;
-};
-template <WFmt F, int NMAT, int S, int W, int K>
-__device__ SmemView carve(uint8_t* smem) {
-  SmemView v;
-  v.engine = smem;
-  v.cols = smem + engine_smem<NMAT>(W);
-  v.red = reinterpret_cast<double*>(v.cols + 2 * size_t(act_col_stride<kBatch>(K)));
-  return v;
-}
+// Pipeline shapes: <nvfp4, stages, K units per tile, tiles, B slots>. Units per tile = K / 256;
+// B slots >= the largest number of distinct K units one CTA's run touches on a 148-SM grid
+// (launchers grow the grid if a smaller GPU would need more).
+using QkvShape = GemvShape<false, 6, kH / kUnitK, (kQs + 2 * kPs) / kTileRows, 8>;
+using OShape = GemvShape<false, 6, kQs / kUnitK, kH / kTileRows, 4>;
+using UpGateShape = GemvShape<true, 5, kH / kUnitK, kL / 64, 15>;  // tile = 64 up rows + 64 gate rows
+using DownShape = GemvShape<true, 5, kL / kUnitK, kH / kTileRows, 13>;
 
 __device__ __forceinline__ float gelu_tanh(float x) {
   // F.gelu(approximate="tanh"): 0.5 * x * (1 + tanh(sqrt(2/pi) * (x + 0.044715 * x^3)))
@@ -59,23 +44,51 @@ __device__ bool last_cta(uint32_t* counter) {
   return is_last != 0;
 }
 
-// h = bf16((x * inv_rms(x)) * gamma) for a bf16 vector of K elements held as VPT vectors per
-// thread (gemma4.py:83-89). Returns the f32 values of h in `vals`.
-template <int K, int VPT>
-__device__ void rms_norm_vec(const uint16_t* x, const uint16_t* gamma, float (&vals)[VPT][8], double* red) {
-  float gv[VPT][8];
-  load_bf16_vec<VPT>(x, K, vals, true);
-  load_bf16_vec<VPT>(gamma, K, gv, false);
+// 1 / sqrt(mean(x^2) + eps) of a bf16 vector of K elements written by the preceding kernel
+// (gemma4.py:83-89): squares summed exactly in f64, the mean narrowed to f32.
+template <int K>
+__device__ float rms_inverse_of(const uint16_t* x, double* red) {
   double ss = 0.0;
+  for (int k = threadIdx.x * 8; k < K; k += blockDim.x * 8) {
+    const uint4 raw = __ldcg(reinterpret_cast<const uint4*>(x + k));
+    const uint16_t* b = reinterpret_cast<const uint16_t*>(&raw);
 #pragma unroll
-  for (int v = 0; v < VPT; ++v)
+    for (int j = 0; j < 8; ++j) {
+      const double f = bf16_to_f32(b[j]);
+      ss += f * f;
+    }
+  }
+  return rms_inverse(block_sum_d(ss, red), K);
+}
+
+// 16 bf16 elements from a vector another kernel wrote (L2-coherent loads).
+__device__ __forceinline__ void load16_cg(const uint16_t* p, float (&v)[16]) {
+  const uint4 a = __ldcg(reinterpret_cast<const uint4*>(p));
+  const uint4 b = __ldcg(reinterpret_cast<const uint4*>(p + 8));
+  const uint16_t* ha = reinterpret_cast<const uint16_t*>(&a);
+  const uint16_t* hb = reinterpret_cast<const uint16_t*>(&b);
 #pragma unroll
-    for (int j = 0; j < 8; ++j) ss += double(vals[v][j]) * double(vals[v][j]);
-  const float inv = rms_inverse(block_sum_d(ss, red), K);
+  for (int j = 0; j < 8; ++j) {
+    v[j] = bf16_to_f32(ha[j]);
+    v[8 + j] = bf16_to_f32(hb[j]);
+  }
+}
+
+// h = bf16((x * inv) * gamma) for 16 elements (the pre-norm of the QKV and FFN ops).
+__device__ __forceinline__ void rms_scaled16(const uint16_t* x, const uint16_t* gamma, float inv, float (&v)[16]) {
+  float g[16];
+  load16_cg(x, v);
+  const uint4 ga = *reinterpret_cast<const uint4*>(gamma);
+  const uint4 gb = *reinterpret_cast<const uint4*>(gamma + 8);
+  const uint16_t* ha = reinterpret_cast<const uint16_t*>(&ga);
+  const uint16_t* hb = reinterpret_cast<const uint16_t*>(&gb);
 #pragma unroll
-  for (int v = 0; v < VPT; ++v)
+  for (int j = 0; j < 8; ++j) {
+    g[j] = bf16_to_f32(ha[j]);
+    g[8 + j] = bf16_to_f32(hb[j]);
+  }
 #pragma unroll
-    for (int j = 0; j < 8; ++j) vals[v][j] = bf16_round((vals[v][j] * inv) * gv[v][j]);
+  for (int j = 0; j < 16; ++j) v[j] = bf16_round((v[j] * inv) * g[j]);
 }
 
 // residual <- bf16(residual + RMSNorm_gamma(y)) [then bf16(. * layer_scalar)], H elements, whole
@@ -115,6 +128,8 @@ __device__ void residual_epilogue(const uint16_t* y, const uint16_t* gamma, uint
 // ---------------------------------------------------------------------------------------
 // QKV
 
+// Per-head RMSNorm (+ RoPE for q and k) of one projected head and its store: q_out, or the
+// addressed ring slot of the K / V cache. One warp, eight elements per lane.
 __device__ void qkv_head_epilogue(const QkvArgs& a, const Scratch& sc, int head) {
   const int lane = threadIdx.x & 31;
   const int base = head * kDs;
@@ -181,183 +196,179 @@ __device__ void qkv_head_epilogue(const QkvArgs& a, const Scratch& sc, int head)
   *reinterpret_cast<uint4*>(dst) = *reinterpret_cast<const uint4*>(outb);
 }
 
-__global__ void __launch_bounds__(kQkvW * 32, 1) qkv_kernel(QkvArgs a, Scratch sc) {
-  constexpr WFmt F = WFmt::kFp8;
-  constexpr int W = kQkvW, S = kQkvS;
-  extern __shared__ __align__(1024) uint8_t smem[];
-  const SmemView sm = carve<F, 1, S, W, kH>(smem);
-  G4_STAMP(sc, 0);
-  pdl_wait_primary();
-  pdl_launch_dependents();
-  G4_STAMP(sc, 1);
+struct QkvMaps {
+  CUtensorMap q, k, v;
+};
 
-  // pre-attention RMSNorm -> exact f16 activation columns
-  constexpr int VPT = (kH / 8 + W * 32 - 1) / (W * 32);
-  float h[VPT][8];
-  rms_norm_vec<kH, VPT>(a.x, a.input_rms, h, sm.red);
-  const float unscale = build_act_columns<kBatch, VPT>(sm.cols, kH, h, reinterpret_cast<float*>(sm.red));
-  __syncthreads();
-  G4_STAMP(sc, 2);
+struct QkvOp {
+  const QkvMaps* maps;
+  QkvArgs a;
+  Scratch sc;
+  float inv = 0.f;
+  uint32_t tx_bytes = QkvShape::kABytes;
 
-  constexpr int kGroups = (kQs + 2 * kPs) / 16;
-  auto rows_of = [&](int grp, int) -> const uint8_t* {
-    const int r = grp * 16;
-    if (r < kQs) return a.q_weight + size_t(r) * kH;
-    if (r < kQs + kPs) return a.k_weight + size_t(r - kQs) * kH;
-    return a.v_weight + size_t(r - kQs - kPs) * kH;
-  };
-  auto no_scales = [](int, int) -> const uint8_t* { return nullptr; };
-  auto finalize = [&](int grp, const float (&tot)[1]) {
-    const int lane = threadIdx.x & 31;
-    if (lane < 16) {
-      const int r = grp * 16 + lane;
-      const uint16_t sb = r < kQs ? a.q_scale[r] : (r < kQs + kPs ? a.k_scale[r - kQs] : a.v_scale[r - kQs - kPs]);
-      // scaled_projection: bf16((x @ codes.T) * scale) (generate_references.py:265-274)
-      sc.y[r] = f32_to_bf16((tot[0] * unscale) * bf16_to_f32(sb));
-    }
-    __syncwarp();
-    uint32_t head_done = 0;
-    const int head = grp / (kDs / 16);
-    if (lane == 0) {
+  __device__ void load_unit(uint8_t* stage, int tile, int kc, uint64_t* bar, uint64_t policy) const {
+    constexpr int kQTiles = kQs / kTileRows, kKTiles = kPs / kTileRows;
+    const CUtensorMap* m = tile < kQTiles ? &maps->q : (tile < kQTiles + kKTiles ? &maps->k : &maps->v);
+    const int row0 = (tile < kQTiles ? tile : (tile < kQTiles + kKTiles ? tile - kQTiles : tile - kQTiles - kKTiles)) *
+                     kTileRows;
+    tma_load_2d(stage, m, kc * kUnitK, row0, bar, policy);
+    tma_load_2d(stage + 16384, m, kc * kUnitK + 128, row0, bar, policy);
+  }
+  __device__ void prologue(GemvCtl& ctl) { inv = rms_inverse_of<kH>(a.x, ctl.red_d); }
+  __device__ void act16(int k0, float (&v)[16]) const { rms_scaled16(a.x + k0, a.input_rms + k0, inv, v); }
+  __device__ void finalize_tile(int tile, int row, float v, GemvCtl& ctl) const {
+    const int r = tile * kTileRows + row;
+    const uint16_t sb = r < kQs ? a.q_scale[r] : (r < kQs + kPs ? a.k_scale[r - kQs] : a.v_scale[r - kQs - kPs]);
+    // scaled_projection: bf16((x @ codes.T) * scale) (generate_references.py:265-274)
+    sc.y[r] = f32_to_bf16(v * bf16_to_f32(sb));
+    named_bar(kEpiBarrier, kEpiThreads);
+    const int head = r / kDs;  // two tiles per head
+    if (row == 0) {
       const uint32_t before = atomic_add_acq_rel_gpu(sc.counters + kHeadCounterBase + head, 1u);
-      head_done = before == uint32_t(kDs / 16 - 1);
-      if (head_done) sc.counters[kHeadCounterBase + head] = 0;
+      const bool done = before == uint32_t(kDs / kTileRows - 1);
+      if (done) sc.counters[kHeadCounterBase + head] = 0;
+      ctl.bcast2 = done ? 1u : 0u;
     }
-    head_done = __shfl_sync(0xffffffffu, head_done, 0);
-    if (head_done) qkv_head_epilogue(a, sc, head);
-  };
-  stream_gemv<F, 1, kBatch, S, W>(sm.engine, sm.cols, kH, kGroups, kH, 0, rows_of, no_scales, finalize, sc);
-  G4_STAMP(sc, 3);
+    named_bar(kEpiBarrier, kEpiThreads);
+    // the warp holding row 0 (it took the ticket) normalises, rotates and stores the head
+    if (ctl.bcast2 && (threadIdx.x >> 5) == 4) qkv_head_epilogue(a, sc, head);
+  }
+};
+
+__global__ void __launch_bounds__(kGemvThreads, 1) qkv_kernel(const __grid_constant__ QkvMaps maps, QkvArgs a,
+                                                              Scratch sc) {
+  extern __shared__ __align__(1024) uint8_t smem[];
+  QkvOp op{&maps, a, sc};
+  gemv_run<QkvShape>(op, smem, sc);
 }
 
 // ---------------------------------------------------------------------------------------
 // O projection + post-attention RMSNorm + residual
 
-__global__ void __launch_bounds__(kOW * 32, 1) o_kernel(OArgs a, Scratch sc) {
-  constexpr WFmt F = WFmt::kFp8;
-  constexpr int W = kOW, S = kOS;
+struct OOp {
+  const CUtensorMap* map;
+  OArgs a;
+  Scratch sc;
+  uint32_t tx_bytes = OShape::kABytes;
+
+  __device__ void load_unit(uint8_t* stage, int tile, int kc, uint64_t* bar, uint64_t policy) const {
+    tma_load_2d(stage, map, kc * kUnitK, tile * kTileRows, bar, policy);
+    tma_load_2d(stage + 16384, map, kc * kUnitK + 128, tile * kTileRows, bar, policy);
+  }
+  __device__ void prologue(GemvCtl&) {}
+  __device__ void act16(int k0, float (&v)[16]) const { load16_cg(a.x + k0, v); }
+  __device__ void finalize_tile(int tile, int row, float v, GemvCtl&) const {
+    const int r = tile * kTileRows + row;
+    sc.y[r] = f32_to_bf16(v * bf16_to_f32(a.o_scale[r]));
+  }
+};
+
+__global__ void __launch_bounds__(kGemvThreads, 1) o_kernel(const __grid_constant__ CUtensorMap map, OArgs a,
+                                                            Scratch sc) {
   extern __shared__ __align__(1024) uint8_t smem[];
-  const SmemView sm = carve<F, 1, S, W, kQs>(smem);
-  G4_STAMP(sc, 0);
-  pdl_wait_primary();
-  pdl_launch_dependents();
-  G4_STAMP(sc, 1);
-
-  constexpr int VPT = (kQs / 8 + W * 32 - 1) / (W * 32);
-  float xv[VPT][8];
-  load_bf16_vec<VPT>(a.x, kQs, xv, true);
-  const float unscale = build_act_columns<kBatch, VPT>(sm.cols, kQs, xv, reinterpret_cast<float*>(sm.red));
-  __syncthreads();
-  G4_STAMP(sc, 2);
-
-  constexpr int kGroups = kH / 16;
-  auto rows_of = [&](int grp, int) -> const uint8_t* { return a.o_weight + size_t(grp) * 16 * kQs; };
-  auto no_scales = [](int, int) -> const uint8_t* { return nullptr; };
-  auto finalize = [&](int grp, const float (&tot)[1]) {
-    const int lane = threadIdx.x & 31;
-    if (lane < 16) {
-      const int r = grp * 16 + lane;
-      sc.y[r] = f32_to_bf16((tot[0] * unscale) * bf16_to_f32(a.o_scale[r]));
-    }
-  };
-  stream_gemv<F, 1, kBatch, S, W>(sm.engine, sm.cols, kQs, kGroups, kQs, 0, rows_of, no_scales, finalize, sc);
-  G4_STAMP(sc, 3);
-
+  __shared__ double red[8];
+  OOp op{&map, a, sc};
+  gemv_run<OShape>(op, smem, sc);
   if (last_cta(sc.counters + kCtaCounter)) {
-    residual_epilogue<W * 32>(sc.y, a.post_rms, a.residual, nullptr, sm.red);
+    residual_epilogue<kGemvThreads>(sc.y, a.post_rms, a.residual, nullptr, red);
     if (threadIdx.x == 0) sc.counters[kCtaCounter] = 0;
   }
-  G4_STAMP(sc, 4);
 }
 
 // ---------------------------------------------------------------------------------------
 // NVFP4 feed-forward: up/gate + GeGLU, then down + post-RMSNorm + residual + layer scalar
 
-__global__ void __launch_bounds__(kUgW * 32, 1) ffn_upgate_kernel(FfnArgs a, Scratch sc) {
-  constexpr WFmt F = WFmt::kNvfp4;
-  constexpr int W = kUgW, S = kUgS;
+struct UpGateMaps {
+  CUtensorMap up, gate, up_s, gate_s;
+};
+
+struct UpGateOp {
+  const UpGateMaps* maps;
+  FfnArgs a;
+  Scratch sc;
+  float inv = 0.f, g_up = 0.f, g_gate = 0.f;
+  uint32_t tx_bytes = 4 * 64 * 64 + 2 * 64 * 16;  // four 64-row e2m1 boxes + two scale boxes
+
+  // stage: [K 0-127: up rows (8 KB) | gate rows (8 KB)] [K 128-255: same] [up scales | gate scales]
+  __device__ void load_unit(uint8_t* stage, int tile, int kc, uint64_t* bar, uint64_t policy) const {
+    const int row0 = tile * 64, x = kc * kUnitK;
+    tma_load_2d(stage, &maps->up, x, row0, bar, policy);
+    tma_load_2d(stage + 8192, &maps->gate, x, row0, bar, policy);
+    tma_load_2d(stage + 16384, &maps->up, x + 128, row0, bar, policy);
+    tma_load_2d(stage + 24576, &maps->gate, x + 128, row0, bar, policy);
+    tma_load_2d(stage + UpGateShape::kABytes, &maps->up_s, kc * (kUnitK / 16), row0, bar, policy);
+    tma_load_2d(stage + UpGateShape::kABytes + 1024, &maps->gate_s, kc * (kUnitK / 16), row0, bar, policy);
+  }
+  __device__ void prologue(GemvCtl& ctl) {
+    inv = rms_inverse_of<kH>(a.residual, ctl.red_d);
+    g_up = *a.up_global;
+    g_gate = *a.gate_global;
+  }
+  __device__ void act16(int k0, float (&v)[16]) const { rms_scaled16(a.residual + k0, a.pre_rms + k0, inv, v); }
+  __device__ void finalize_tile(int tile, int row, float v, GemvCtl& ctl) const {
+    // GloballyScaled(nn.Linear): bf16(bf16(x @ W.T) * g)  (generate_references.py:358-372)
+    const float val = bf16_round(bf16_round(v) * (row < 64 ? g_up : g_gate));
+    if (row >= 64) ctl.xchg[row - 64] = val;
+    named_bar(kEpiBarrier, kEpiThreads);
+    // down_proj input: bf16(bf16(gelu_tanh(gate)) * up)  (gemma4.py:197)
+    if (row < 64) sc.act[tile * 64 + row] = f32_to_bf16(bf16_round(gelu_tanh(ctl.xchg[row])) * val);
+    named_bar(kEpiBarrier, kEpiThreads);
+  }
+};
+
+__global__ void __launch_bounds__(kGemvThreads, 1) ffn_upgate_kernel(const __grid_constant__ UpGateMaps maps, FfnArgs a,
+                                                                     Scratch sc) {
   extern __shared__ __align__(1024) uint8_t smem[];
-  const SmemView sm = carve<F, 2, S, W, kH>(smem);
-  G4_STAMP(sc, 0);
-  pdl_wait_primary();
-  pdl_launch_dependents();
-  G4_STAMP(sc, 1);
-
-  constexpr int VPT = (kH / 8 + W * 32 - 1) / (W * 32);
-  float h[VPT][8];
-  rms_norm_vec<kH, VPT>(a.residual, a.pre_rms, h, sm.red);
-  const float unscale = build_act_columns<kBatch, VPT>(sm.cols, kH, h, reinterpret_cast<float*>(sm.red));
-  __syncthreads();
-  G4_STAMP(sc, 2);
-  const float g_up = *a.up_global, g_gate = *a.gate_global;
-
-  constexpr int kGroups = kL / 16;
-  auto rows_of = [&](int grp, int m) -> const uint8_t* {
-    return (m == 0 ? a.up_packed : a.gate_packed) + size_t(grp) * 16 * (kH / 2);
-  };
-  auto scales_of = [&](int grp, int m) -> const uint8_t* {
-    return (m == 0 ? a.up_scale : a.gate_scale) + size_t(grp) * 16 * (kH / 16);
-  };
-  auto finalize = [&](int grp, const float (&tot)[2]) {
-    const int lane = threadIdx.x & 31;
-    if (lane < 16) {
-      // GloballyScaled(nn.Linear): bf16(bf16(x @ W.T) * g)  (generate_references.py:358-372)
-      const float up = bf16_round(bf16_round(tot[0] * unscale) * g_up);
-      const float gate = bf16_round(bf16_round(tot[1] * unscale) * g_gate);
-      // down_proj input: bf16(bf16(gelu_tanh(gate)) * up)  (gemma4.py:197)
-      sc.act[grp * 16 + lane] = f32_to_bf16(bf16_round(gelu_tanh(gate)) * up);
-    }
-  };
-  stream_gemv<F, 2, kBatch, S, W>(sm.engine, sm.cols, kH, kGroups, kH / 2, kH / 16, rows_of, scales_of, finalize,
-                                  sc);
-  G4_STAMP(sc, 3);
+  UpGateOp op{&maps, a, sc};
+  gemv_run<UpGateShape>(op, smem, sc);
 }
 
-__global__ void __launch_bounds__(kDnW * 32, 1) ffn_down_kernel(FfnArgs a, Scratch sc) {
-  constexpr WFmt F = WFmt::kNvfp4;
-  constexpr int W = kDnW, S = kDnS;
+struct DownMaps {
+  CUtensorMap w, s;
+};
+
+struct DownOp {
+  const DownMaps* maps;
+  FfnArgs a;
+  Scratch sc;
+  float g_down = 0.f;
+  uint32_t tx_bytes = 2 * 128 * 64 + 128 * 16;
+
+  __device__ void load_unit(uint8_t* stage, int tile, int kc, uint64_t* bar, uint64_t policy) const {
+    const int row0 = tile * kTileRows, x = kc * kUnitK;
+    tma_load_2d(stage, &maps->w, x, row0, bar, policy);
+    tma_load_2d(stage + 16384, &maps->w, x + 128, row0, bar, policy);
+    tma_load_2d(stage + DownShape::kABytes, &maps->s, kc * (kUnitK / 16), row0, bar, policy);
+  }
+  __device__ void prologue(GemvCtl&) { g_down = *a.down_global; }
+  __device__ void act16(int k0, float (&v)[16]) const { load16_cg(sc.act + k0, v); }
+  __device__ void finalize_tile(int tile, int row, float v, GemvCtl&) const {
+    const int r = tile * kTileRows + row;
+    sc.y[r] = f32_to_bf16(bf16_round(v) * g_down);
+  }
+};
+
+__global__ void __launch_bounds__(kGemvThreads, 1) ffn_down_kernel(const __grid_constant__ DownMaps maps, FfnArgs a,
+                                                                   Scratch sc) {
   extern __shared__ __align__(1024) uint8_t smem[];
-  const SmemView sm = carve<F, 1, S, W, kL>(smem);
-  G4_STAMP(sc, 8);
-  pdl_wait_primary();
-  pdl_launch_dependents();
-  G4_STAMP(sc, 9);
-
-  constexpr int VPT = (kL / 8 + W * 32 - 1) / (W * 32);
-  float av[VPT][8];
-  load_bf16_vec<VPT>(sc.act, kL, av, true);
-  const float unscale = build_act_columns<kBatch, VPT>(sm.cols, kL, av, reinterpret_cast<float*>(sm.red));
-  __syncthreads();
-  G4_STAMP(sc, 10);
-  const float g_down = *a.down_global;
-
-  constexpr int kGroups = kH / 16;
-  auto rows_of = [&](int grp, int) -> const uint8_t* { return a.down_packed + size_t(grp) * 16 * (kL / 2); };
-  auto scales_of = [&](int grp, int) -> const uint8_t* { return a.down_scale + size_t(grp) * 16 * (kL / 16); };
-  auto finalize = [&](int grp, const float (&tot)[1]) {
-    const int lane = threadIdx.x & 31;
-    if (lane < 16) sc.y[grp * 16 + lane] = f32_to_bf16(bf16_round(tot[0] * unscale) * g_down);
-  };
-  stream_gemv<F, 1, kBatch, S, W>(sm.engine, sm.cols, kL, kGroups, kL / 2, kL / 16, rows_of, scales_of, finalize,
-                                  sc);
-  G4_STAMP(sc, 11);
-
+  __shared__ double red[8];
+  DownOp op{&maps, a, sc};
+  gemv_run<DownShape>(op, smem, sc);
   if (last_cta(sc.counters + kCtaCounter)) {
-    residual_epilogue<W * 32>(sc.y, a.post_rms, a.residual, a.layer_scalar, sm.red);
+    residual_epilogue<kGemvThreads>(sc.y, a.post_rms, a.residual, a.layer_scalar, red);
     if (threadIdx.x == 0) sc.counters[kCtaCounter] = 0;
   }
-  G4_STAMP(sc, 12);
 }
 
 // ---------------------------------------------------------------------------------------
 // launch helpers
 
-template <class... Args>
-cudaError_t launch(void (*kernel)(Args...), int grid, int block, size_t smem, const LaunchEnv& env,
-                   Args... args) {
+template <class... KArgs, class... Args>
+cudaError_t launch(void (*kernel)(KArgs...), int grid, size_t smem, const LaunchEnv& env, Args&&... args) {
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = dim3(grid);
-  cfg.blockDim = dim3(block);
+  cfg.blockDim = dim3(kGemvThreads);
   cfg.dynamicSmemBytes = smem;
   cfg.stream = env.stream;
   cudaLaunchAttribute attr[1];
@@ -365,43 +376,137 @@ cudaError_t launch(void (*kernel)(Args...), int grid, int block, size_t smem, co
   attr[0].val.programmaticStreamSerializationAllowed = env.pdl ? 1 : 0;
   cfg.attrs = attr;
   cfg.numAttrs = 1;
-  return cudaLaunchKernelEx(&cfg, kernel, args...);
+  return cudaLaunchKernelEx(&cfg, kernel, std::forward<Args>(args)...);
 }
 
-constexpr size_t kQkvSmem = smem_bytes<WFmt::kFp8, 1, kQkvS, kQkvW, kH>();
-constexpr size_t kOSmem = smem_bytes<WFmt::kFp8, 1, kOS, kOW, kQs>();
-constexpr size_t kUgSmem = smem_bytes<WFmt::kNvfp4, 2, kUgS, kUgW, kH>();
-constexpr size_t kDnSmem = smem_bytes<WFmt::kNvfp4, 1, kDnS, kDnW, kL>();
-static_assert(kQkvSmem <= 227 * 1024 && kOSmem <= 227 * 1024 && kUgSmem <= 227 * 1024 && kDnSmem <= 227 * 1024,
-              "shared memory budget");
+// One CTA per SM, unless a smaller GPU would give a CTA more K units than its B slots hold.
+template <class Shape>
+int grid_for(const LaunchEnv& env) {
+  const int need = (Shape::kTotalUnits + Shape::kBSlots - 1) / Shape::kBSlots;
+  return env.sm_count > need ? env.sm_count : need;
+}
 
 }  // namespace
 
 cudaError_t prepare_proj_kernels() {
   cudaError_t e;
-  if ((e = cudaFuncSetAttribute(qkv_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, int(kQkvSmem)))) return e;
-  if ((e = cudaFuncSetAttribute(o_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, int(kOSmem)))) return e;
-  if ((e = cudaFuncSetAttribute(ffn_upgate_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, int(kUgSmem))))
+  if ((e = cudaFuncSetAttribute(qkv_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, int(QkvShape::kSmemBytes))))
     return e;
-  if ((e = cudaFuncSetAttribute(ffn_down_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, int(kDnSmem))))
+  if ((e = cudaFuncSetAttribute(o_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, int(OShape::kSmemBytes))))
+    return e;
+  if ((e = cudaFuncSetAttribute(ffn_upgate_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                int(UpGateShape::kSmemBytes))))
+    return e;
+  if ((e = cudaFuncSetAttribute(ffn_down_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                int(DownShape::kSmemBytes))))
     return e;
   return cudaSuccess;
 }
 
 cudaError_t launch_qkv(const QkvArgs& a, const LaunchEnv& env) {
-  return launch(qkv_kernel, env.sm_count, kQkvW * 32, kQkvSmem, env, a, env.sc);
+  QkvMaps m;
+  cudaError_t e;
+  if ((e = env.maps->u8(a.q_weight, kH, kQs, 128, kTileRows, true, &m.q))) return e;
+  if ((e = env.maps->u8(a.k_weight, kH, kPs, 128, kTileRows, true, &m.k))) return e;
+  if ((e = env.maps->u8(a.v_weight, kH, kPs, 128, kTileRows, true, &m.v))) return e;
+  return launch(qkv_kernel, grid_for<QkvShape>(env), QkvShape::kSmemBytes, env, m, a, env.sc);
 }
 
 cudaError_t launch_o(const OArgs& a, const LaunchEnv& env) {
-  return launch(o_kernel, env.sm_count, kOW * 32, kOSmem, env, a, env.sc);
+  CUtensorMap m;
+  cudaError_t e;
+  if ((e = env.maps->u8(a.o_weight, kQs, kH, 128, kTileRows, true, &m))) return e;
+  return launch(o_kernel, grid_for<OShape>(env), OShape::kSmemBytes, env, m, a, env.sc);
 }
 
 cudaError_t launch_ffn_nvfp4(const FfnArgs& a, const LaunchEnv& env) {
-  cudaError_t e = launch(ffn_upgate_kernel, env.sm_count, kUgW * 32, kUgSmem, env, a, env.sc);
+  UpGateMaps ug;
+  DownMaps dn;
+  cudaError_t e;
+  if ((e = env.maps->fp4(a.up_packed, kH, kL, 64, &ug.up))) return e;
+  if ((e = env.maps->fp4(a.gate_packed, kH, kL, 64, &ug.gate))) return e;
+  if ((e = env.maps->u8(a.up_scale, kH / 16, kL, 16, 64, false, &ug.up_s))) return e;
+  if ((e = env.maps->u8(a.gate_scale, kH / 16, kL, 16, 64, false, &ug.gate_s))) return e;
+  if ((e = env.maps->fp4(a.down_packed, kL, kH, kTileRows, &dn.w))) return e;
+  if ((e = env.maps->u8(a.down_scale, kL / 16, kH, 16, kTileRows, false, &dn.s))) return e;
+  e = launch(ffn_upgate_kernel, grid_for<UpGateShape>(env), UpGateShape::kSmemBytes, env, ug, a, env.sc);
   if (e != cudaSuccess) return e;
   LaunchEnv chained = env;
-  chained.pdl = true;  // the down pass launches while the up/gate pass drains
-  return launch(ffn_down_kernel, env.sm_count, kDnW * 32, kDnSmem, chained, a, env.sc);
+  chained.pdl = true;  // the down pass prefetches its weights while the up/gate pass drains
+  return launch(ffn_down_kernel, grid_for<DownShape>(env), DownShape::kSmemBytes, chained, dn, a, env.sc);
+}
+
+// ---------------------------------------------------------------------------------------
+// tensor maps
+
+namespace {
+PFN_cuTensorMapEncodeTiled_v12000 encode_fn() {
+  static PFN_cuTensorMapEncodeTiled_v12000 fn = [] {
+    void* p = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q) != cudaSuccess ||
+        q != cudaDriverEntryPointSuccess)
+      p = nullptr;
+    return reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(p);
+  }();
+  return fn;
+}
+}  // namespace
+
+const CUtensorMap* TmapCache::find(const void* base, uint64_t key) const {
+  for (int i = 0; i < kEntries; ++i)
+    if (entries_[i].base == base && entries_[i].key == key) return &entries_[i].map;
+  return nullptr;
+}
+
+void TmapCache::put(const void* base, uint64_t key, const CUtensorMap& map) {
+  entries_[next_].base = base;
+  entries_[next_].key = key;
+  entries_[next_].map = map;
+  next_ = (next_ + 1) % kEntries;
+}
+
+cudaError_t TmapCache::u8(const void* base, uint64_t cols, uint64_t rows, uint32_t box_cols, uint32_t box_rows,
+                          bool swizzle128, CUtensorMap* out) {
+  const uint64_t key = (cols << 34) ^ (rows << 12) ^ (uint64_t(box_cols) << 4) ^ (uint64_t(box_rows) << 1) ^
+                       (swizzle128 ? 1u : 0u) ^ (uint64_t(1) << 63);
+  if (const CUtensorMap* m = find(base, key)) {
+    *out = *m;
+    return cudaSuccess;
+  }
+  auto enc = encode_fn();
+  if (!enc) return cudaErrorNotSupported;
+  const cuuint64_t gdim[2] = {cols, rows};
+  const cuuint64_t gstride[1] = {cols};
+  const cuuint32_t box[2] = {box_cols, box_rows};
+  const cuuint32_t estride[2] = {1, 1};
+  const CUresult r = enc(out, CU_TENSOR_MAP_DATA_TYPE_UINT8, 2, const_cast<void*>(base), gdim, gstride, box, estride,
+                         CU_TENSOR_MAP_INTERLEAVE_NONE,
+                         swizzle128 ? CU_TENSOR_MAP_SWIZZLE_128B : CU_TENSOR_MAP_SWIZZLE_NONE,
+                         CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  if (r != CUDA_SUCCESS) return cudaErrorInvalidValue;
+  put(base, key, *out);
+  return cudaSuccess;
+}
+
+cudaError_t TmapCache::fp4(const void* base, uint64_t cols, uint64_t rows, uint32_t box_rows, CUtensorMap* out) {
+  const uint64_t key = (cols << 34) ^ (rows << 12) ^ (uint64_t(box_rows) << 1);
+  if (const CUtensorMap* m = find(base, key)) {
+    *out = *m;
+    return cudaSuccess;
+  }
+  auto enc = encode_fn();
+  if (!enc) return cudaErrorNotSupported;
+  const cuuint64_t gdim[2] = {cols, rows};
+  const cuuint64_t gstride[1] = {cols / 2};
+  const cuuint32_t box[2] = {128, box_rows};
+  const cuuint32_t estride[2] = {1, 1};
+  const CUresult r = enc(out, CU_TENSOR_MAP_DATA_TYPE_16U4_ALIGN16B, 2, const_cast<void*>(base), gdim, gstride, box,
+                         estride, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+                         CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  if (r != CUDA_SUCCESS) return cudaErrorInvalidValue;
+  put(base, key, *out);
+  return cudaSuccess;
 }
 
 }  // namespace g4

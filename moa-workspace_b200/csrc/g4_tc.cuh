@@ -1,0 +1,203 @@
+// Blackwell (sm_100a) building blocks of the weight-streaming engine: TMA tensor-tile loads,
+// mbarriers with bounded waits, tcgen05 (TMEM allocation, kind::f8f6f4 MMA, commit, loads)
+// and the shared-memory matrix descriptors. No TMA multicast is used anywhere.
+#pragma once
+
+#include <cuda.h>
+
+#include "g4_common.cuh"
+
+namespace g4 {
+
+// ---------------------------------------------------------------------------------------
+// mbarriers shared by several roles of a CTA. A wait gives up after kWaitLimitNs or when
+// another role has already given up (`abort` in shared memory), so a stalled pipeline ends
+// the kernel instead of hanging the SM.
+
+__device__ __forceinline__ void mbar_arrive(uint64_t* bar) {
+  asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(smem_u32(bar)) : "memory");
+}
+
+__device__ __forceinline__ bool mbar_wait_or_abort(uint64_t* bar, uint32_t parity, volatile uint32_t* abort,
+                                                   uint32_t* err) {
+  if (mbar_try_wait(bar, parity)) return true;
+  const uint64_t t0 = globaltimer_ns();
+  while (!mbar_try_wait(bar, parity)) {
+    if (*abort) return false;
+    if (globaltimer_ns() - t0 > kWaitLimitNs) {
+      *abort = 1u;
+      atomicOr(err, kErrWaitTimeout);
+      return false;
+    }
+  }
+  return true;
+}
+
+// Named barrier among `count` threads (a multiple of 32) of the CTA.
+__device__ __forceinline__ void named_bar(int id, int count) {
+  asm volatile("bar.sync %0, %1;" ::"r"(id), "r"(count) : "memory");
+}
+
+// ---------------------------------------------------------------------------------------
+// TMA: 2-D tensor tile -> shared memory, completing its bytes on an mbarrier. The tensor map
+// is a __grid_constant__ kernel parameter. x (innermost, in elements) is always a multiple of
+// the 128-element box here, so it meets the 16-byte coordinate rule for every element type.
+
+__device__ __forceinline__ void tma_load_2d(void* dst, const CUtensorMap* map, int x, int y, uint64_t* bar,
+                                            uint64_t policy) {
+  asm volatile(
+      "cp.async.bulk.tensor.2d.shared::cluster.global.mbarrier::complete_tx::bytes.L2::cache_hint"
+      " [%0], [%1, {%2, %3}], [%4], %5;" ::"r"(smem_u32(dst)),
+      "l"(reinterpret_cast<uint64_t>(map)), "r"(x), "r"(y), "r"(smem_u32(bar)), "l"(policy)
+      : "memory");
+}
+
+__device__ __forceinline__ void tma_prefetch_map(const CUtensorMap* map) {
+  asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(map)) : "memory");
+}
+
+// ---------------------------------------------------------------------------------------
+// TMEM
+
+__device__ __forceinline__ void tmem_alloc(uint32_t* slot, uint32_t ncols) {  // whole warp
+  asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(slot)), "r"(ncols)
+               : "memory");
+  asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
+}
+__device__ __forceinline__ void tmem_dealloc(uint32_t taddr, uint32_t ncols) {  // whole warp
+  asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(taddr), "r"(ncols) : "memory");
+}
+__device__ __forceinline__ void tc_fence_before() { asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory"); }
+__device__ __forceinline__ void tc_fence_after() { asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory"); }
+
+// 32 lanes x 8 / 32 consecutive columns of f32 (this warp's lane quarter).
+__device__ __forceinline__ void tmem_ld8(uint32_t taddr, float (&v)[8]) {
+  uint32_t r[8];
+  asm volatile("tcgen05.ld.sync.aligned.32x32b.x8.b32 {%0,%1,%2,%3,%4,%5,%6,%7}, [%8];"
+               : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7])
+               : "r"(taddr));
+#pragma unroll
+  for (int i = 0; i < 8; ++i) v[i] = __uint_as_float(r[i]);
+}
+__device__ __forceinline__ void tmem_ld32(uint32_t taddr, float (&v)[32]) {
+  uint32_t r[32];
+  asm volatile(
+      "tcgen05.ld.sync.aligned.32x32b.x32.b32 {%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,"
+      "%16,%17,%18,%19,%20,%21,%22,%23,%24,%25,%26,%27,%28,%29,%30,%31}, [%32];"
+      : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7]), "=r"(r[8]),
+        "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]), "=r"(r[15]), "=r"(r[16]),
+        "=r"(r[17]), "=r"(r[18]), "=r"(r[19]), "=r"(r[20]), "=r"(r[21]), "=r"(r[22]), "=r"(r[23]), "=r"(r[24]),
+        "=r"(r[25]), "=r"(r[26]), "=r"(r[27]), "=r"(r[28]), "=r"(r[29]), "=r"(r[30]), "=r"(r[31])
+      : "r"(taddr));
+#pragma unroll
+  for (int i = 0; i < 32; ++i) v[i] = __uint_as_float(r[i]);
+}
+__device__ __forceinline__ void tmem_ld_wait() { asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory"); }
+
+// ---------------------------------------------------------------------------------------
+// UMMA descriptors
+
+// K-major operand in the 128-byte swizzle layout: rows of 128 bytes (128 one-byte elements, or
+// 128 e2m1 codes unpacked to a byte each by the 16U4_ALIGN16B tensor map), 8-row atoms of
+// 1024 bytes stacked densely (stride 1024). `saddr` is the row-0 address of the K slice: the
+// 1024-aligned atom base plus 32 bytes per 32-element K step.
+__device__ __forceinline__ uint64_t umma_desc_sw128(uint32_t saddr) {
+  uint64_t d = uint64_t((saddr & 0x3FFFFu) >> 4);  // start address
+  d |= uint64_t(1) << 16;                           // leading offset (unused for swizzled K-major)
+  d |= uint64_t(1024 >> 4) << 32;                   // stride between 8-row atoms
+  d |= uint64_t(1) << 46;                           // descriptor version (sm_100)
+  d |= uint64_t(2) << 61;                           // SWIZZLE_128B
+  return d;
+}
+
+// Byte offset of (row, byte k) inside a 1024-aligned SW128 K-major region.
+__device__ __forceinline__ uint32_t sw128_offset(uint32_t row, uint32_t kbyte) {
+  return row * 128u + ((((kbyte >> 4) ^ (row & 7u))) << 4) + (kbyte & 15u);
+}
+
+enum : uint32_t { kFmtE4M3 = 0, kFmtE2M1 = 5 };
+
+// Instruction descriptor of tcgen05.mma kind::f8f6f4: f32 accumulate, both operands K-major.
+__host__ __device__ constexpr uint32_t umma_idesc_f8f6f4(uint32_t afmt, uint32_t bfmt, int m, int n) {
+  return (1u << 4) | (afmt << 7) | (bfmt << 10) | (uint32_t(n >> 3) << 17) | (uint32_t(m >> 4) << 24);
+}
+
+// D[tmem] (+)= A[smem] * B[smem]^T, issued by one thread.
+__device__ __forceinline__ void umma_f8f6f4(uint32_t tmem_d, uint64_t adesc, uint64_t bdesc, uint32_t idesc,
+                                            uint32_t accumulate) {
+  asm volatile(
+      "{\n .reg .pred p;\n setp.ne.b32 p, %4, 0;\n"
+      " tcgen05.mma.cta_group::1.kind::f8f6f4 [%0], %1, %2, %3, p;\n}\n" ::"r"(tmem_d),
+      "l"(adesc), "l"(bdesc), "r"(idesc), "r"(accumulate)
+      : "memory");
+}
+
+// Arrive on `bar` once every MMA this thread issued so far has completed.
+__device__ __forceinline__ void umma_commit(uint64_t* bar) {
+  asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(smem_u32(bar))
+               : "memory");
+}
+
+// ---------------------------------------------------------------------------------------
+// Exact e4m3 terms of a bf16 activation.
+//
+// For v = x * 2^E with |v| < 256 the terms t_0 = e4m3(v), t_j = e4m3(r_j) with r_0 = v,
+// r_{j+1} = (r_j - t_j) * 16 (round to nearest even each time; every r_j is exact in f32 and
+// never exceeds 256) satisfy v = sum_j t_j 16^-j - r_NT 16^-NT. Each term carries 4 significant
+// bits, so a bf16 value (8 bits) is exact in two terms once it is in e4m3's normal range and
+// every further term extends the exact range 16x downwards: NT terms keep all of v for
+// |v| >= 2^(10 - 4 NT) and leave an absolute error below 2^(-10 - 4 (NT - 1)) otherwise. The
+// tensor cores contract each term exactly against the weight codes, so sum_k w_k v_k is
+// reproduced to f32 accuracy even when large values cancel and tiny ones decide the result.
+
+// Two f32 -> two e4m3 codes (round to nearest even, saturating) in the low 16 bits (lo in the
+// low byte). 16-bit values stay inside the asm blocks.
+__device__ __forceinline__ uint32_t f32x2_to_e4m3x2(float lo, float hi) {
+  uint32_t r;
+  asm("{\n .reg .b16 t;\n cvt.rn.satfinite.e4m3x2.f32 t, %1, %2;\n cvt.u32.u16 %0, t;\n}" : "=r"(r) : "f"(hi), "f"(lo));
+  return r;
+}
+// The two e4m3 codes in the low 16 bits of `two` (low byte first) as exact f32 values.
+__device__ __forceinline__ float2 e4m3x2_to_f32x2(uint32_t two) {
+  uint32_t h;
+  asm("{\n .reg .b16 lo, hi;\n mov.b32 {lo, hi}, %1;\n cvt.rn.f16x2.e4m3x2 %0, lo;\n}" : "=r"(h) : "r"(two));
+  const __half2 hv = __halves2half2(__ushort_as_half(uint16_t(h & 0xffffu)), __ushort_as_half(uint16_t(h >> 16)));
+  return __half22float2(hv);
+}
+
+// Split 16 values (already scaled by 2^E) into NT 16-byte rows of e4m3 terms (element j in
+// byte j of each row).
+template <int NT>
+__device__ __forceinline__ void split_terms16(const float (&v)[16], uint4 (&t)[NT]) {
+  uint32_t w[NT][4];
+#pragma unroll
+  for (int j = 0; j < NT; ++j) w[j][0] = w[j][1] = w[j][2] = w[j][3] = 0u;
+#pragma unroll
+  for (int i = 0; i < 8; ++i) {
+    float ra = v[2 * i], rb = v[2 * i + 1];
+    const int sh = 16 * (i % 2);
+#pragma unroll
+    for (int j = 0; j < NT; ++j) {
+      const uint32_t c = f32x2_to_e4m3x2(ra, rb);
+      w[j][i / 2] |= c << sh;
+      if (j + 1 < NT) {
+        const float2 d = e4m3x2_to_f32x2(c);
+        ra = (ra - d.x) * 16.0f;
+        rb = (rb - d.y) * 16.0f;
+      }
+    }
+  }
+#pragma unroll
+  for (int j = 0; j < NT; ++j) t[j] = make_uint4(w[j][0], w[j][1], w[j][2], w[j][3]);
+}
+
+// sum_j d[j] 16^-j, smallest term first.
+template <int NT>
+__device__ __forceinline__ float combine_terms(const float* d) {
+  float acc = d[NT - 1];
+#pragma unroll
+  for (int j = NT - 2; j >= 0; --j) acc = fmaf(acc, 0.0625f, d[j]);
+  return acc;
+}
+
+}  // namespace g4
