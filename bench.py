@@ -166,6 +166,18 @@ class Layer:
         self.gate_p, self.gate_s, self.gate_g = quant_nvfp4(normal(L, H, std=0.02))
         self.down_p, self.down_s, self.down_g = quant_nvfp4(normal(H, L, std=0.02))
         self.layer_scalar = bf(torch.full((8,), 0.375, device=dev))
+        self.tiled = False
+
+    def tile(self, ops, device):
+        """Repack the weight matrices into the GPU-native unit-tiled layout (once, at load)."""
+        for attr, name in (("q_w", "q_weight"), ("k_w", "k_weight"), ("v_w", "v_weight"), ("o_w", "o_weight"),
+                           ("down_p", "down_weight_packed"), ("down_s", "down_weight_scale")):
+            setattr(self, attr, ops.tile_weight(device, name, getattr(self, attr)))
+        self.upgate_p = ops.pack_upgate(device, self.up_p, self.gate_p, scales=False)
+        self.upgate_s = ops.pack_upgate(device, self.up_s, self.gate_s, scales=True)
+        self.up_p = self.gate_p = self.up_s = self.gate_s = None
+        self.tiled = True
+        return self
 
 
 class Workspace:
@@ -195,12 +207,16 @@ def layer_step(ops, device, w: Workspace, lay: Layer, which=("qkv", "attn", "o",
     if "qkv" in which:
         ops.sliding_project_qkv(device, w.residual, lay.q_w, lay.k_w, lay.v_w, lay.q_s, lay.k_s, lay.v_s,
                                 lay.input_rms, lay.q_rms, lay.k_rms, w.kv_offset, w.rope_offset, w.cos, w.sin,
-                                lay.k_cache, lay.v_cache, w.q)
+                                lay.k_cache, lay.v_cache, w.q, tiled=lay.tiled)
     if "attn" in which:
         ops.sliding_attention(device, w.q, lay.k_cache, lay.v_cache, w.mask, w.attn, scale=1.0)
     if "o" in which:
-        ops.sliding_attention_output(device, w.attn, lay.post_attn_rms, lay.o_w, lay.o_s, w.residual)
-    if "ffn" in which:
+        ops.sliding_attention_output(device, w.attn, lay.post_attn_rms, lay.o_w, lay.o_s, w.residual,
+                                     tiled=lay.tiled)
+    if "ffn" in which and lay.tiled:
+        ops.decoder_feedforward_tiled(device, w.residual, lay.pre_ff_rms, lay.upgate_p, lay.down_p, lay.upgate_s,
+                                      lay.down_s, lay.up_g, lay.gate_g, lay.down_g, lay.post_ff_rms, lay.layer_scalar)
+    elif "ffn" in which:
         ops.decoder_feedforward(device, w.residual, lay.pre_ff_rms, lay.up_p, lay.gate_p, lay.down_p, lay.up_s,
                                 lay.gate_s, lay.down_s, lay.up_g, lay.gate_g, lay.down_g, lay.post_ff_rms,
                                 lay.layer_scalar)
@@ -355,7 +371,7 @@ def run_ours(args):
     dev = torch.device("cuda", local)
     gen = torch.Generator(device=dev)
     gen.manual_seed(1000 + rank)
-    layers = [Layer(gen, dev) for _ in range(N_LAYERS)]
+    layers = [Layer(gen, dev).tile(ops, device) for _ in range(N_LAYERS)]
     ws = Workspace(gen, dev)
     torch.cuda.synchronize()
 
@@ -496,7 +512,7 @@ def run_only(args):
     dev = torch.device("cuda", 0)
     gen = torch.Generator(device=dev)
     gen.manual_seed(1000)
-    layers = [Layer(gen, dev) for _ in range(N_LAYERS)]
+    layers = [Layer(gen, dev).tile(ops, device) for _ in range(N_LAYERS)]
     ws = Workspace(gen, dev)
     for i in range(args.warmup):
         layer_step(ops, device, ws, layers[i % N_LAYERS], (args.only,))

@@ -17,7 +17,8 @@
  *   - Every call validates its arguments on the host and returns a g4_status; it never
  *     aborts. Calls are asynchronous and ordered on the caller's CUDA stream (`stream` is a
  *     cudaStream_t; NULL means the legacy default stream).
- *   - Every pointer must be device memory of the context's device, 16-byte aligned.
+ *   - Every pointer must be device memory of the context's device, 16-byte aligned; the packed
+ *     f4e2m1 weight matrices 32-byte aligned (they are read by the tensor-memory accelerator).
  *   - Offsets that live in device memory (kv_offset, rope_offset) are checked on the
  *     device: an out-of-range value skips the writes that depend on it and raises a bit
  *     that g4_ctx_check() reports as G4_ERR_DEVICE.
@@ -107,6 +108,46 @@ g4_status g4_decoder_feedforward(g4_ctx* ctx, uint16_t* residual_hbm, const uint
                                  const float* up_global_scale, const float* gate_global_scale,
                                  const float* down_global_scale, const uint16_t* post_ff_rms_weight,
                                  const uint16_t* layer_scalar, void* stream);
+
+/* GPU-native weight layout (no reference counterpart: the reference's loader,
+ * src/host/load.rs:142-325, writes row-major HBM tensors). The weights are static, so a caller
+ * packs them once at load time; the *_tiled entry points below then fetch every pipeline unit
+ * (the 256 K elements of a tile of rows) as one contiguous block with one TMA request.
+ * Copies the byte matrix src [rows, row_bytes] (and, if src2 is not NULL, the same-shaped src2)
+ * to dst (rows * row_bytes bytes per source, no overlap): with U = row_bytes / unit_bytes and n
+ * sources, block (t, u) = [unit u of src's tile-t rows][unit u of src2's tile-t rows]:
+ *   dst[(((t * U + u) * n + which) * tile_rows + r) * unit_bytes + b]
+ *     = src_which[(t * tile_rows + r) * row_bytes + u * unit_bytes + b]
+ * Parameters (unit_bytes, tile_rows) per matrix:
+ *   q, k, v, o weights (f8e4m3), one source each               128, 128
+ *   up + gate packed codes (src = up, src2 = gate)              64, 64
+ *   up + gate block scales (src = up, src2 = gate)              16, 64
+ *   down packed codes                                           64, 128
+ *   down block scales                                           16, 128 */
+g4_status g4_pack_tiles(g4_ctx* ctx, const uint8_t* src, const uint8_t* src2, uint8_t* dst, int32_t rows,
+                        int32_t row_bytes, int32_t unit_bytes, int32_t tile_rows, void* stream);
+
+/* The weight-streaming ops on weights packed by g4_pack_tiles; every other argument and every
+ * result is that of the entry point of the same name without the suffix. The FFN takes the
+ * up/gate codes and block scales as the interleaved buffers of one two-source g4_pack_tiles
+ * call each. */
+g4_status g4_sliding_project_qkv_tiled(g4_ctx* ctx, const uint16_t* x, const uint8_t* q_weight,
+                                       const uint8_t* k_weight, const uint8_t* v_weight,
+                                       const uint16_t* q_weight_scale, const uint16_t* k_weight_scale,
+                                       const uint16_t* v_weight_scale, const uint16_t* input_rms_weight,
+                                       const uint16_t* q_rms_weight, const uint16_t* k_rms_weight,
+                                       const int32_t* kv_offset, const int32_t* rope_offset, const uint16_t* cos,
+                                       const uint16_t* sin, uint16_t* k_cache, uint16_t* v_cache, uint16_t* q_out,
+                                       int32_t ring_len, int32_t rope_rows, void* stream);
+g4_status g4_sliding_attention_output_tiled(g4_ctx* ctx, const uint16_t* x, const uint16_t* post_attn_rms_weight,
+                                            const uint8_t* o_weight, const uint16_t* o_weight_scale,
+                                            uint16_t* residual_hbm, void* stream);
+g4_status g4_decoder_feedforward_tiled(g4_ctx* ctx, uint16_t* residual_hbm, const uint16_t* pre_ff_rms_weight,
+                                       const uint8_t* up_gate_weight_tiled, const uint8_t* down_weight_tiled,
+                                       const uint8_t* up_gate_scale_tiled, const uint8_t* down_scale_tiled,
+                                       const float* up_global_scale, const float* gate_global_scale,
+                                       const float* down_global_scale, const uint16_t* post_ff_rms_weight,
+                                       const uint16_t* layer_scalar, void* stream);
 
 #ifdef __cplusplus
 }

@@ -184,7 +184,7 @@ g4_status g4_ctx_check(g4_ctx* ctx, void* stream, uint32_t* flags) {
   return G4_OK;
 }
 
-g4_status g4_sliding_project_qkv(g4_ctx* ctx, const uint16_t* x, const uint8_t* q_weight, const uint8_t* k_weight,
+static g4_status project_qkv(bool tiled, g4_ctx* ctx, const uint16_t* x, const uint8_t* q_weight, const uint8_t* k_weight,
                                  const uint8_t* v_weight, const uint16_t* q_weight_scale,
                                  const uint16_t* k_weight_scale, const uint16_t* v_weight_scale,
                                  const uint16_t* input_rms_weight, const uint16_t* q_rms_weight,
@@ -217,7 +217,7 @@ g4_status g4_sliding_project_qkv(g4_ctx* ctx, const uint16_t* x, const uint8_t* 
   DeviceGuard guard(ctx->device);
   g4::QkvArgs a{x,        q_weight,      k_weight,  v_weight, q_weight_scale, k_weight_scale, v_weight_scale,
                 input_rms_weight, q_rms_weight, k_rms_weight, kv_offset, rope_offset, cos, sin,
-                k_cache,  v_cache,       q_out,     ring_len, rope_rows};
+                k_cache,  v_cache,       q_out,     ring_len, rope_rows, tiled};
   return cuda_status(ctx, g4::launch_qkv(a, env_of(ctx, stream)), "sliding_project_qkv launch");
 }
 
@@ -234,7 +234,7 @@ g4_status g4_sliding_attention(g4_ctx* ctx, const uint16_t* q, const uint16_t* k
   return cuda_status(ctx, g4::launch_attention(a, env_of(ctx, stream)), "sliding_attention launch");
 }
 
-g4_status g4_sliding_attention_output(g4_ctx* ctx, const uint16_t* x, const uint16_t* post_attn_rms_weight,
+static g4_status attention_output(bool tiled, g4_ctx* ctx, const uint16_t* x, const uint16_t* post_attn_rms_weight,
                                       const uint8_t* o_weight, const uint16_t* o_weight_scale,
                                       uint16_t* residual_hbm, void* stream) {
   if (!ctx) return G4_ERR_INVALID_ARGUMENT;
@@ -245,11 +245,11 @@ g4_status g4_sliding_attention_output(g4_ctx* ctx, const uint16_t* x, const uint
                                   {residual_hbm, "residual_hbm"}});
   if (st != G4_OK) return st;
   DeviceGuard guard(ctx->device);
-  g4::OArgs a{x, post_attn_rms_weight, o_weight, o_weight_scale, residual_hbm};
+  g4::OArgs a{x, post_attn_rms_weight, o_weight, o_weight_scale, residual_hbm, tiled};
   return cuda_status(ctx, g4::launch_o(a, env_of(ctx, stream)), "sliding_attention_output launch");
 }
 
-g4_status g4_decoder_feedforward(g4_ctx* ctx, uint16_t* residual_hbm, const uint16_t* pre_ff_rms_weight,
+static g4_status decoder_feedforward(bool tiled, g4_ctx* ctx, uint16_t* residual_hbm, const uint16_t* pre_ff_rms_weight,
                                  const uint8_t* up_weight_packed, const uint8_t* gate_weight_packed,
                                  const uint8_t* down_weight_packed, const uint8_t* up_weight_scale,
                                  const uint8_t* gate_weight_scale, const uint8_t* down_weight_scale,
@@ -279,8 +279,96 @@ g4_status g4_decoder_feedforward(g4_ctx* ctx, uint16_t* residual_hbm, const uint
   DeviceGuard guard(ctx->device);
   g4::FfnArgs a{residual_hbm,      pre_ff_rms_weight, up_weight_packed, gate_weight_packed, down_weight_packed,
                 up_weight_scale,   gate_weight_scale, down_weight_scale, up_global_scale,   gate_global_scale,
-                down_global_scale, post_ff_rms_weight, layer_scalar};
+                down_global_scale, post_ff_rms_weight, layer_scalar, tiled};
   return cuda_status(ctx, g4::launch_ffn_nvfp4(a, env_of(ctx, stream)), "decoder_feedforward launch");
+}
+
+
+g4_status g4_sliding_project_qkv(g4_ctx* ctx, const uint16_t* x, const uint8_t* q_weight, const uint8_t* k_weight,
+                                 const uint8_t* v_weight, const uint16_t* q_weight_scale,
+                                 const uint16_t* k_weight_scale, const uint16_t* v_weight_scale,
+                                 const uint16_t* input_rms_weight, const uint16_t* q_rms_weight,
+                                 const uint16_t* k_rms_weight, const int32_t* kv_offset, const int32_t* rope_offset,
+                                 const uint16_t* cos, const uint16_t* sin, uint16_t* k_cache, uint16_t* v_cache,
+                                 uint16_t* q_out, int32_t ring_len, int32_t rope_rows, void* stream) {
+  return project_qkv(false, ctx, x, q_weight, k_weight, v_weight, q_weight_scale, k_weight_scale, v_weight_scale,
+                     input_rms_weight, q_rms_weight, k_rms_weight, kv_offset, rope_offset, cos, sin, k_cache, v_cache,
+                     q_out, ring_len, rope_rows, stream);
+}
+
+g4_status g4_sliding_project_qkv_tiled(g4_ctx* ctx, const uint16_t* x, const uint8_t* q_weight,
+                                       const uint8_t* k_weight, const uint8_t* v_weight,
+                                       const uint16_t* q_weight_scale, const uint16_t* k_weight_scale,
+                                       const uint16_t* v_weight_scale, const uint16_t* input_rms_weight,
+                                       const uint16_t* q_rms_weight, const uint16_t* k_rms_weight,
+                                       const int32_t* kv_offset, const int32_t* rope_offset, const uint16_t* cos,
+                                       const uint16_t* sin, uint16_t* k_cache, uint16_t* v_cache, uint16_t* q_out,
+                                       int32_t ring_len, int32_t rope_rows, void* stream) {
+  return project_qkv(true, ctx, x, q_weight, k_weight, v_weight, q_weight_scale, k_weight_scale, v_weight_scale,
+                     input_rms_weight, q_rms_weight, k_rms_weight, kv_offset, rope_offset, cos, sin, k_cache, v_cache,
+                     q_out, ring_len, rope_rows, stream);
+}
+
+g4_status g4_sliding_attention_output(g4_ctx* ctx, const uint16_t* x, const uint16_t* post_attn_rms_weight,
+                                      const uint8_t* o_weight, const uint16_t* o_weight_scale,
+                                      uint16_t* residual_hbm, void* stream) {
+  return attention_output(false, ctx, x, post_attn_rms_weight, o_weight, o_weight_scale, residual_hbm, stream);
+}
+
+g4_status g4_sliding_attention_output_tiled(g4_ctx* ctx, const uint16_t* x, const uint16_t* post_attn_rms_weight,
+                                            const uint8_t* o_weight, const uint16_t* o_weight_scale,
+                                            uint16_t* residual_hbm, void* stream) {
+  return attention_output(true, ctx, x, post_attn_rms_weight, o_weight, o_weight_scale, residual_hbm, stream);
+}
+
+g4_status g4_decoder_feedforward(g4_ctx* ctx, uint16_t* residual_hbm, const uint16_t* pre_ff_rms_weight,
+                                 const uint8_t* up_weight_packed, const uint8_t* gate_weight_packed,
+                                 const uint8_t* down_weight_packed, const uint8_t* up_weight_scale,
+                                 const uint8_t* gate_weight_scale, const uint8_t* down_weight_scale,
+                                 const float* up_global_scale, const float* gate_global_scale,
+                                 const float* down_global_scale, const uint16_t* post_ff_rms_weight,
+                                 const uint16_t* layer_scalar, void* stream) {
+  return decoder_feedforward(false, ctx, residual_hbm, pre_ff_rms_weight, up_weight_packed, gate_weight_packed,
+                             down_weight_packed, up_weight_scale, gate_weight_scale, down_weight_scale,
+                             up_global_scale, gate_global_scale, down_global_scale, post_ff_rms_weight, layer_scalar,
+                             stream);
+}
+
+g4_status g4_decoder_feedforward_tiled(g4_ctx* ctx, uint16_t* residual_hbm, const uint16_t* pre_ff_rms_weight,
+                                       const uint8_t* up_gate_weight_tiled, const uint8_t* down_weight_tiled,
+                                       const uint8_t* up_gate_scale_tiled, const uint8_t* down_scale_tiled,
+                                       const float* up_global_scale, const float* gate_global_scale,
+                                       const float* down_global_scale, const uint16_t* post_ff_rms_weight,
+                                       const uint16_t* layer_scalar, void* stream) {
+  // the gate matrices are interleaved into the up buffers: pass them again where the row-major
+  // path takes the gate pointers (validated, not read)
+  return decoder_feedforward(true, ctx, residual_hbm, pre_ff_rms_weight, up_gate_weight_tiled, up_gate_weight_tiled,
+                             down_weight_tiled, up_gate_scale_tiled, up_gate_scale_tiled, down_scale_tiled,
+                             up_global_scale, gate_global_scale, down_global_scale, post_ff_rms_weight, layer_scalar,
+                             stream);
+}
+
+g4_status g4_pack_tiles(g4_ctx* ctx, const uint8_t* src, const uint8_t* src2, uint8_t* dst, int32_t rows,
+                        int32_t row_bytes, int32_t unit_bytes, int32_t tile_rows, void* stream) {
+  if (!ctx) return G4_ERR_INVALID_ARGUMENT;
+  g4_status st = check_ptrs(ctx, {{src, "src"}, {dst, "dst"}});
+  if (st != G4_OK) return st;
+  if (src2 && !aligned16(src2)) return fail(ctx, G4_ERR_MISALIGNED, "pointer not 16-byte aligned: %s", "src2");
+  if (rows <= 0 || row_bytes <= 0 || unit_bytes <= 0 || tile_rows <= 0 || unit_bytes % 16 != 0 ||
+      row_bytes % unit_bytes != 0 || rows % tile_rows != 0)
+    return fail(ctx, G4_ERR_INVALID_ARGUMENT, "%s: need rows %% tile_rows == 0, row_bytes %% unit_bytes == 0, "
+                "unit_bytes %% 16 == 0", "g4_pack_tiles");
+  const uintptr_t n = uintptr_t(rows) * uintptr_t(row_bytes);
+  const uintptr_t d0 = reinterpret_cast<uintptr_t>(dst), dn = n * (src2 ? 2 : 1);
+  for (const uint8_t* sp : {src, src2}) {
+    const uintptr_t s0 = reinterpret_cast<uintptr_t>(sp);
+    if (sp && s0 < d0 + dn && d0 < s0 + n)
+      return fail(ctx, G4_ERR_INVALID_ARGUMENT, "%s: a source overlaps dst", "g4_pack_tiles");
+  }
+  DeviceGuard guard(ctx->device);
+  return cuda_status(ctx, g4::launch_pack_tiles(src, src2, dst, rows, row_bytes, unit_bytes, tile_rows,
+                                                static_cast<cudaStream_t>(stream)),
+                     "g4_pack_tiles launch");
 }
 
 #ifdef G4_TRACE

@@ -113,6 +113,7 @@ __global__ void __launch_bounds__(kThreads, 1) attention_kernel(AttnArgs a, Scra
           sm.score[wslot0 + kb0 + r][0] = bf16_round(a.scale * d0);
           sm.score[wslot0 + kb0 + r][1] = bf16_round(a.scale * d1);
         }
+        __syncwarp();
       }
     }
   }
@@ -131,6 +132,7 @@ __global__ void __launch_bounds__(kThreads, 1) attention_kernel(AttnArgs a, Scra
     sm.red[warp][0] = m0;
     sm.red[warp][1] = m1;
   }
+  __syncwarp();
   __syncthreads();
   if (tid == 0) {
     float a0 = -INFINITY, a1 = -INFINITY;
@@ -141,6 +143,7 @@ __global__ void __launch_bounds__(kThreads, 1) attention_kernel(AttnArgs a, Scra
     sm.pub_max[0] = a0;
     sm.pub_max[1] = a1;
   }
+  __syncwarp();
   cluster.sync();
   float gm0 = -INFINITY, gm1 = -INFINITY;
   for (int r = 0; r < CL; ++r) {
@@ -171,6 +174,7 @@ __global__ void __launch_bounds__(kThreads, 1) attention_kernel(AttnArgs a, Scra
     sm.red[warp][0] = s0;
     sm.red[warp][1] = s1;
   }
+  __syncwarp();
   cp_async_wait_all();
   __syncthreads();
   if (tid == 0) {
@@ -182,6 +186,7 @@ __global__ void __launch_bounds__(kThreads, 1) attention_kernel(AttnArgs a, Scra
     sm.pub_sum[0] = a0;
     sm.pub_sum[1] = a1;
   }
+  __syncwarp();
   G4_STAMP(sc, 4);
 
   // phase 2: o = sum_t bf16(p) v. Thread (res, pair) covers dims 2*pair, 2*pair+1 of both
@@ -288,8 +293,12 @@ cudaError_t launch_attention(const AttnArgs& a, const LaunchEnv& env) {
   attr[1].val.programmaticStreamSerializationAllowed = env.pdl ? 1 : 0;
   cfg.attrs = attr;
   cfg.numAttrs = 2;
-  return cl == 16 ? cudaLaunchKernelEx(&cfg, attention_kernel<16>, a, env.sc)
-                  : cudaLaunchKernelEx(&cfg, attention_kernel<8>, a, env.sc);
+  Scratch sc = env.sc;
+#ifdef G4_TRACE
+  if (sc.trace) sc.trace += 4096;  // profiling builds: separate stamp rows per kernel
+#endif
+  return cl == 16 ? cudaLaunchKernelEx(&cfg, attention_kernel<16>, a, sc)
+                  : cudaLaunchKernelEx(&cfg, attention_kernel<8>, a, sc);
 }
 
 }  // namespace g4

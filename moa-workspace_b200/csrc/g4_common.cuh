@@ -133,6 +133,17 @@ __device__ __forceinline__ bool mbar_try_wait(uint64_t* bar, uint32_t parity) {
   return ok != 0;
 }
 
+// Non-blocking test of a barrier phase (never suspends the thread).
+__device__ __forceinline__ bool mbar_test(uint64_t* bar, uint32_t parity) {
+  uint32_t ok;
+  asm volatile(
+      "{\n .reg .pred p;\n mbarrier.test_wait.parity.shared::cta.b64 p, [%1], %2;\n selp.u32 %0, 1, 0, p;\n}"
+      : "=r"(ok)
+      : "r"(smem_u32(bar)), "r"(parity)
+      : "memory");
+  return ok != 0;
+}
+
 __device__ __forceinline__ uint64_t globaltimer_ns() {
   uint64_t t;
   asm volatile("mov.u64 %0, %globaltimer;" : "=l"(t));
@@ -198,6 +209,11 @@ __device__ __forceinline__ uint4 ld_cg_u4(const void* p) { return __ldcg(reinter
   do {                                                                                          \
     if ((sc).trace && threadIdx.x == 0) (sc).trace[blockIdx.x * 16 + (point)] = globaltimer_ns(); \
   } while (0)
+// G4_STAMP_T records from whichever single thread calls it.
+#define G4_STAMP_T(sc, point)                                                      \
+  do {                                                                            \
+    if ((sc).trace) (sc).trace[blockIdx.x * 16 + (point)] = globaltimer_ns();     \
+  } while (0)
 // Per-warp stamps go to trace[65536 + (blockIdx.x * 32 + warp) * 8 + point] (lane 0).
 #define G4_STAMP_WARP(sc, point)                                                                         \
   do {                                                                                                   \
@@ -207,6 +223,9 @@ __device__ __forceinline__ uint4 ld_cg_u4(const void* p) { return __ldcg(reinter
 #else
 #define G4_STAMP(sc, point) \
   do {                      \
+  } while (0)
+#define G4_STAMP_T(sc, point) \
+  do {                        \
   } while (0)
 #define G4_STAMP_WARP(sc, point) \
   do {                           \
@@ -233,6 +252,7 @@ __device__ __forceinline__ double block_sum_d(double v, double* red) {
   v = warp_sum_d(v);
   __syncthreads();
   if (lane == 0) red[warp] = v;
+  __syncwarp();
   __syncthreads();
   double t = 0.0;
   for (int i = 0; i < nw; ++i) t += red[i];  // fixed order: identical in every CTA
@@ -243,6 +263,7 @@ __device__ __forceinline__ float block_max(float v, float* red) {
   v = warp_max(v);
   __syncthreads();
   if (lane == 0) red[warp] = v;
+  __syncwarp();
   __syncthreads();
   float t = 0.f;
   for (int i = 0; i < nw; ++i) t = fmaxf(t, red[i]);

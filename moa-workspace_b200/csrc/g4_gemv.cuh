@@ -8,7 +8,8 @@
 //             into an S-stage shared-memory ring. The first S units are requested before the
 //             kernel waits on the preceding kernel (weights never depend on it).
 //   warp 1    MMA issuer: tcgen05.mma kind::f8f6f4 (A = weight codes, e4m3 or e2m1; B = the
-//             activation as exact e4m3 terms) into a ring of TMEM accumulator slots.
+//             activation as exact e4m3 terms) into a ring of TMEM accumulator slots; one
+//             tcgen05.commit per unit both frees the stage and hands the slot to the epilogue.
 //   warps 2-5 epilogue: one thread per tile row; reads its TMEM lane, combines the terms (and
 //             the NVFP4 block scales) in f32 and finalises or publishes the row.
 // The activation is scaled by a power of two before the split, chosen per 16-element group
@@ -36,26 +37,31 @@ constexpr int kTileRows = 128;
 constexpr int kUmmaN = 8;
 constexpr int kMmaPerUnit = kUnitK / 32;
 constexpr int kEpiBarrier = 1;  // named barrier id of the epilogue warps
+constexpr int kMmaLookahead = 4;  // units whose readiness the MMA thread tests in one go
 
-template <bool FP4, int STAGES, int UPT, int TILES, int BSLOTS>
+template <bool FP4, int STAGES, int UPT, int TILES, int BSLOTS, int L2AHEAD = 6>
 struct GemvShape {
   static constexpr bool kFp4 = FP4;
   static constexpr int kStages = STAGES;
+  static constexpr int kL2Ahead = L2AHEAD;  // units requested into L2 beyond the shared-memory ring
   static constexpr int kUnitsPerTile = UPT;
   static constexpr int kTiles = TILES;
   static constexpr int kBSlots = BSLOTS;  // distinct K units one CTA may touch
   static constexpr int kTotalUnits = UPT * TILES;
   static constexpr int kABytes = 2 * kTileRows * 128;                 // two 128-element K halves
   static constexpr int kScaleBytes = FP4 ? kTileRows * (kUnitK / 16) : 0;
-  static constexpr int kStageBytes = kABytes + (FP4 ? 2048 : 0);
+  static constexpr int kStageBytes = kABytes;
   static constexpr int kTmemSlots = FP4 ? 8 : 16;
-  static constexpr int kSlotCols = FP4 ? kMmaPerUnit * kUmmaN : kUmmaN;
   static constexpr uint32_t kTmemCols = FP4 ? 512u : 128u;
+  static constexpr int kSlotCols = FP4 ? kMmaPerUnit * kUmmaN : kUmmaN;
+  static_assert(STAGES <= kTmemSlots, "a stage is released through its unit's TMEM-slot barrier");
   static constexpr uint32_t kIdesc = umma_idesc_f8f6f4(FP4 ? kFmtE2M1 : kFmtE4M3, kFmtE4M3, kTileRows, kUmmaN);
   static constexpr int kTerms = FP4 ? kUmmaN / 2 : kUmmaN;  // e4m3 terms per activation element
-  // shared memory: stages | B slots | term scales (2^-E per 16-element group) | control block
+  // shared memory: stages | B slots | block-scale ring (nvfp4, one per TMEM slot) |
+  //                term scales (2^-E per 16-element group) | control block
   static constexpr size_t kOffB = size_t(STAGES) * kStageBytes;
-  static constexpr size_t kOffExp = kOffB + size_t(BSLOTS) * 2048;
+  static constexpr size_t kOffScl = kOffB + size_t(BSLOTS) * 2048;
+  static constexpr size_t kOffExp = kOffScl + (FP4 ? size_t(kTmemSlots) * kScaleBytes : 0);
   static constexpr size_t kOffCtl = kOffExp + size_t(BSLOTS) * 16 * sizeof(float);
   static constexpr size_t kSmemBytes = kOffCtl + 1024 + 1024;  // control block + alignment slack
   static_assert(kStageBytes % 1024 == 0, "stages must keep 1024-byte alignment");
@@ -63,7 +69,7 @@ struct GemvShape {
 };
 
 struct GemvCtl {
-  uint64_t full[8], empty[8], tfull[16], tempty[16], drain;
+  uint64_t full[8], sfull[16], done[16], tempty[16], drain;
   uint32_t tmem_base;
   uint32_t abort;
   uint32_t bcast;
@@ -97,12 +103,30 @@ struct GemvCta {
   __device__ int bslot(int kc) const { return (kc - c0 + Shape::kUnitsPerTile) % Shape::kUnitsPerTile; }
 };
 
+// Sum of squares of 16 bf16 values (two uint4), exact in f64.
+__device__ __forceinline__ double sum_squares_bf16x16(const uint4& a, const uint4& b) {
+  const uint32_t w[8] = {a.x, a.y, a.z, a.w, b.x, b.y, b.z, b.w};
+  double ss = 0.0;
+#pragma unroll
+  for (int i = 0; i < 8; ++i) {
+    const double lo = __uint_as_float(w[i] << 16), hi = __uint_as_float(w[i] & 0xffff0000u);
+    ss += lo * lo + hi * hi;
+  }
+  return ss;
+}
+
 // Engine driver. `op` supplies:
 //   void load_unit(uint8_t* stage, int tile, int kc, uint64_t* bar, uint64_t policy) const  (TMA)
-//   void prologue(GemvCtl&)          all threads, after the wait on the preceding kernel
-//   void act16(int k0, float (&v)[16]) const   activation elements k0..k0+15 (bf16 values)
+//   void load_scales(uint8_t* dst, int tile, int kc, uint64_t* bar, uint64_t policy) const (nvfp4)
+//   void prefetch_l2(int u0, int u1) const      units [u0, u1) into L2 (may do nothing)
+//   static bool kRms, int kRmsGroups   whether the activation is RMS-normalised over its
+//                                      kRmsGroups * 16 elements (every group is then loaded)
+//   void prologue(GemvCtl&)            scalar loads, after the wait on the preceding kernel
+//   void load_group(int g, uint4 (&raw)[4]) const   issue the loads of 16-element group g
+//                                      (bf16 input in raw[0..1], gamma in raw[2..3])
+//   void finish_group(const uint4 (&raw)[4], float inv, float (&v)[16]) const   the activation
 //   void finalize_tile(int tile, int row, float v, GemvCtl&) const   all 128 epilogue threads
-//   uint32_t tx_bytes                 bytes one unit's loads deliver
+//   uint32_t tx_bytes                  bytes one unit's weight tiles deliver (block scales: kScaleBytes)
 template <class Shape, class Op>
 __device__ void gemv_run(Op& op, uint8_t* smem_raw, const Scratch& sc) {
   constexpr int S = Shape::kStages, UPT = Shape::kUnitsPerTile, T = Shape::kTmemSlots;
@@ -121,20 +145,21 @@ __device__ void gemv_run(Op& op, uint8_t* smem_raw, const Scratch& sc) {
   c.c0 = c.u0 % UPT;
   const int nslots = c.n < UPT ? c.n : UPT;
   volatile uint32_t* abort = &ctl.abort;
+  G4_STAMP(sc, 0);
 
   if (c.tid == 0) {
-    for (int i = 0; i < S; ++i) {
-      mbar_init(&ctl.full[i], 1);
-      mbar_init(&ctl.empty[i], Shape::kFp4 ? 1 + 4 : 1);
-    }
+    for (int i = 0; i < S; ++i) mbar_init(&ctl.full[i], 1);
     for (int i = 0; i < T; ++i) {
-      mbar_init(&ctl.tfull[i], 1);
-      mbar_init(&ctl.tempty[i], 4);
+      mbar_init(&ctl.sfull[i], 1);  // nvfp4: the unit's block scales have landed in the ring
+      mbar_init(&ctl.done[i], 1);   // the unit's MMAs have completed (one commit per unit)
+      mbar_init(&ctl.tempty[i], 4); // the epilogue is done with the TMEM slot (and scale slot)
     }
     mbar_init(&ctl.drain, 1);
     ctl.abort = 0;
     fence_mbar_init();
   }
+  if (c.tid < 16) ctl.unit_max[c.tid] = 0u;
+  __syncwarp();
   if (c.warp == 1) tmem_alloc(&ctl.tmem_base, Shape::kTmemCols);
   tc_fence_before();
   __syncthreads();
@@ -145,20 +170,55 @@ __device__ void gemv_run(Op& op, uint8_t* smem_raw, const Scratch& sc) {
   const uint64_t policy = l2_evict_first_policy();
   const int prefetch = c.n < S ? c.n : S;
   if (c.tid == 0) {
-    for (int i = 0; i < prefetch; ++i) {
+    for (int i = 0; i < prefetch; ++i) {  // i < S <= T: every stage and scale slot is free
       const int u = c.u0 + i;
       mbar_arrive_expect_tx(&ctl.full[i], op.tx_bytes);
       op.load_unit(c.stage(i), u / UPT, u % UPT, &ctl.full[i], policy);
+      if constexpr (Shape::kFp4) {
+        mbar_arrive_expect_tx(&ctl.sfull[i], Shape::kScaleBytes);
+        op.load_scales(smem + Shape::kOffScl + size_t(i) * Shape::kScaleBytes, u / UPT, u % UPT, &ctl.sfull[i], policy);
+      }
     }
+    // the next units go to L2 only: the ring's loads then hit L2 instead of waiting on HBM
+    op.prefetch_l2(c.u0 + prefetch, c.u0 + (prefetch + Shape::kL2Ahead < c.n ? prefetch + Shape::kL2Ahead : c.n));
   }
+  __syncwarp();  // CTA barriers below need converged warps
   pdl_wait_primary();
   pdl_launch_dependents();
+  G4_STAMP(sc, 1);
 
-  // activation -> B operand (only the K units this CTA touches)
-  op.prologue(ctl);
+  // activation -> B operand (only the K units this CTA touches). Every global load of the
+  // prologue is issued before any is used: one round trip while the weight tiles stream in.
   float* gexp = reinterpret_cast<float*>(smem + Shape::kOffExp);  // [slot][group] 2^-E
   {
-    const int groups = nslots * (kUnitK / 16);
+    constexpr int MAXG = 2;  // 16-element groups per thread
+    static_assert(!Op::kRms || Op::kRmsGroups <= MAXG * kGemvThreads, "RMS statistic: too many groups");
+    static_assert(Shape::kBSlots * 16 <= MAXG * kGemvThreads, "B slots: too many groups");
+    op.prologue(ctl);  // scalar loads only
+    int grp[MAXG];
+    bool have[MAXG];
+    uint4 raw[MAXG][4];
+#pragma unroll
+    for (int q = 0; q < MAXG; ++q) {
+      const int j = c.tid + q * kGemvThreads;
+      if constexpr (Op::kRms) {  // the RMS statistic needs the whole vector
+        grp[q] = j;
+        have[q] = j < Op::kRmsGroups;
+      } else {  // only the groups of this CTA's K units
+        grp[q] = ((c.c0 + j / 16) % UPT) * 16 + j % 16;
+        have[q] = j < nslots * 16;
+      }
+      if (have[q]) op.load_group(grp[q], raw[q]);
+    }
+    float inv = 0.f;
+    G4_STAMP(sc, 9);
+    if constexpr (Op::kRms) {
+      double ss = 0.0;
+#pragma unroll
+      for (int q = 0; q < MAXG; ++q)
+        if (have[q]) ss += sum_squares_bf16x16(raw[q][0], raw[q][1]);
+      inv = rms_inverse(block_sum_d(ss, ctl.red_d), Op::kRmsGroups * 16);
+    }
     // exponent E of a max |v| so that max |v| 2^E lies in [128, 256)
     auto exponent_of = [](float amax) {
       int e = 0;
@@ -168,40 +228,41 @@ __device__ void gemv_run(Op& op, uint8_t* smem_raw, const Scratch& sc) {
       }
       return e;
     };
-    if constexpr (!Shape::kFp4) {
-      if (c.tid < 16) ctl.unit_max[c.tid] = 0u;
-      __syncthreads();
-      for (int g = c.tid; g < groups; g += kGemvThreads) {
-        float v[16];
-        op.act16(((c.c0 + g / 16) % UPT) * kUnitK + (g % 16) * 16, v);
-        float amax = 0.f;
+    float v[MAXG][16], amax[MAXG];
+    int slot[MAXG];
 #pragma unroll
-        for (int j = 0; j < 16; ++j) amax = fmaxf(amax, fabsf(v[j]));
-        atomicMax(&ctl.unit_max[g / 16], __float_as_uint(amax));  // non-negative floats order as ints
+    for (int q = 0; q < MAXG; ++q) {
+      slot[q] = c.bslot(grp[q] / 16);
+      have[q] = have[q] && slot[q] < nslots;
+      amax[q] = 0.f;
+      if (have[q]) {
+        op.finish_group(raw[q], inv, v[q]);
+#pragma unroll
+        for (int j = 0; j < 16; ++j) amax[q] = fmaxf(amax[q], fabsf(v[q][j]));
+        if constexpr (!Shape::kFp4)  // one exponent per 256-element unit
+          atomicMax(&ctl.unit_max[slot[q]], __float_as_uint(amax[q]));  // non-negative floats order as ints
       }
+    }
+    if constexpr (!Shape::kFp4) {
       __syncthreads();
+#pragma unroll
+      for (int q = 0; q < MAXG; ++q)
+        if (have[q]) amax[q] = __uint_as_float(ctl.unit_max[slot[q]]);
     }
     const uint4 zero = make_uint4(0, 0, 0, 0);
-    for (int g = c.tid; g < groups; g += kGemvThreads) {
-      const int slot = g / 16, e16 = (g % 16) * 16;
-      const int kc = (c.c0 + slot) % UPT;
-      float v[16];
-      op.act16(kc * kUnitK + e16, v);
-      float amax = 0.f;
-      if constexpr (Shape::kFp4) {
+    G4_STAMP(sc, 10);
 #pragma unroll
-        for (int j = 0; j < 16; ++j) amax = fmaxf(amax, fabsf(v[j]));
-      } else {
-        amax = __uint_as_float(ctl.unit_max[slot]);
-      }
-      const int e = exponent_of(amax);
+    for (int q = 0; q < MAXG; ++q) {
+      if (!have[q]) continue;
+      const int e16 = (grp[q] % 16) * 16;
+      const int e = exponent_of(amax[q]);
       const float up = pow2f(e);
-      gexp[g] = pow2f(-e);
+      gexp[slot[q] * 16 + grp[q] % 16] = pow2f(-e);
 #pragma unroll
-      for (int j = 0; j < 16; ++j) v[j] *= up;
+      for (int j = 0; j < 16; ++j) v[q][j] *= up;
       uint4 tm[Shape::kTerms];
-      split_terms16<Shape::kTerms>(v, tm);
-      uint8_t* atom = c.bsm + size_t(slot) * 2048 + (e16 / 128) * 1024;
+      split_terms16<Shape::kTerms>(v[q], tm);
+      uint8_t* atom = c.bsm + size_t(slot[q]) * 2048 + (e16 / 128) * 1024;
       const uint32_t kb = e16 % 128;
       uint4 rows[8];
       if constexpr (Shape::kFp4) {
@@ -221,6 +282,7 @@ __device__ void gemv_run(Op& op, uint8_t* smem_raw, const Scratch& sc) {
   }
   asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
   __syncthreads();
+  G4_STAMP(sc, 2);
 
   if (c.warp == 0) {
     // ---------------------------------------------------------------- producer
@@ -228,11 +290,23 @@ __device__ void gemv_run(Op& op, uint8_t* smem_raw, const Scratch& sc) {
       int issued = prefetch;
       for (int i = prefetch; i < c.n; ++i) {
         const int s = i % S;
-        if (!mbar_wait_or_abort(&ctl.empty[s], uint32_t(((i / S) - 1) & 1), abort, sc.err)) break;
+        // stage s is free once the MMAs of unit i - S have completed
+        if (!mbar_wait_or_abort(&ctl.done[(i - S) % T], uint32_t(((i - S) / T) & 1), abort, sc.err)) break;
         const int u = c.u0 + i;
         mbar_arrive_expect_tx(&ctl.full[s], op.tx_bytes);
         op.load_unit(c.stage(s), u / UPT, u % UPT, &ctl.full[s], policy);
+        if ((i - prefetch) % 2 == 0 && i + Shape::kL2Ahead < c.n)  // two units per bulk L2 prefetch
+          op.prefetch_l2(u + Shape::kL2Ahead, c.u0 + (i + Shape::kL2Ahead + 2 < c.n ? i + Shape::kL2Ahead + 2 : c.n));
+        if constexpr (Shape::kFp4) {  // scale slot t is free once the epilogue is done with unit i - T
+          const int t = i % T;
+          if (i >= T && !mbar_wait_or_abort(&ctl.tempty[t], uint32_t(((i / T) - 1) & 1), abort, sc.err)) break;
+          mbar_arrive_expect_tx(&ctl.sfull[t], Shape::kScaleBytes);
+          op.load_scales(smem + Shape::kOffScl + size_t(t) * Shape::kScaleBytes, u / UPT, u % UPT, &ctl.sfull[t], policy);
+        }
         issued = i + 1;
+#ifdef G4_TRACE
+        if (sc.trace && blockIdx.x == 0 && i < 64) sc.trace[3000 + i] = globaltimer_ns();
+#endif
       }
       // every requested tile has landed before the CTA may exit
       for (int i = issued - S > 0 ? issued - S : 0; i < issued; ++i) {
@@ -240,15 +314,41 @@ __device__ void gemv_run(Op& op, uint8_t* smem_raw, const Scratch& sc) {
         while (!mbar_try_wait(&ctl.full[i % S], uint32_t((i / S) & 1)))
           if (globaltimer_ns() - t0 > kWaitLimitNs) break;
       }
+      if constexpr (Shape::kFp4) {
+        for (int i = issued - T > 0 ? issued - T : 0; i < issued; ++i) {
+          const uint64_t t0 = globaltimer_ns();
+          while (!mbar_try_wait(&ctl.sfull[i % T], uint32_t((i / T) & 1)))
+            if (globaltimer_ns() - t0 > kWaitLimitNs) break;
+        }
+      }
     }
+    __syncwarp();  // lanes 1..31 wait here for lane 0: the teardown barrier needs whole warps
   } else if (c.warp == 1) {
     // ---------------------------------------------------------------- MMA issuer
+    // One commit per unit both frees the stage's weight tiles and hands the TMEM slot to the
+    // epilogue. Any shared-memory access of this thread (an mbarrier test included) waits for
+    // the MMAs it has queued, so readiness is checked for several units at a time: one blocking
+    // wait for the next unit, then non-blocking tests of the following ones.
     if (c.lane == 0) {
-      for (int i = 0; i < c.n; ++i) {
+      int ready = 0;  // units [i, ready) have landed and have a free TMEM slot
+      bool alive = true;
+      for (int i = 0; i < c.n && alive; ++i) {
         const int s = i % S, t = i % T;
-        if (!mbar_wait_or_abort(&ctl.full[s], uint32_t((i / S) & 1), abort, sc.err)) break;
-        if (i >= T && !mbar_wait_or_abort(&ctl.tempty[t], uint32_t(((i / T) - 1) & 1), abort, sc.err)) break;
-        tc_fence_after();
+        if (i >= ready) {
+          alive = mbar_wait_or_abort(&ctl.full[s], uint32_t((i / S) & 1), abort, sc.err) &&
+                  (i < T || mbar_wait_or_abort(&ctl.tempty[t], uint32_t(((i / T) - 1) & 1), abort, sc.err));
+          if (!alive) break;
+          ready = i + 1;
+          while (ready < c.n && ready < i + kMmaLookahead &&
+                 mbar_test(&ctl.full[ready % S], uint32_t((ready / S) & 1)) &&
+                 (ready < T || mbar_test(&ctl.tempty[ready % T], uint32_t(((ready / T) - 1) & 1))))
+            ++ready;
+          tc_fence_after();
+        }
+        if (i == 0) G4_STAMP_T(sc, 3);
+#ifdef G4_TRACE
+        if (sc.trace && blockIdx.x == 0 && i < 64) sc.trace[3064 + i] = globaltimer_ns();
+#endif
         const int kc = (c.u0 + i) % UPT;
         const uint32_t a_base = smem_u32(c.stage(s));
         const uint32_t b_base = smem_u32(c.bsm) + uint32_t(c.bslot(kc)) * 2048u;
@@ -260,8 +360,11 @@ __device__ void gemv_run(Op& op, uint8_t* smem_raw, const Scratch& sc) {
           const uint32_t col = Shape::kFp4 ? uint32_t(t * Shape::kSlotCols + j * kUmmaN) : uint32_t(t * kUmmaN);
           umma_f8f6f4(tbase + col, ad, bd, Shape::kIdesc, Shape::kFp4 ? 0u : uint32_t(j > 0));
         }
-        umma_commit(&ctl.empty[s]);
-        umma_commit(&ctl.tfull[t]);
+        umma_commit(&ctl.done[t]);
+        if (i == c.n - 1) G4_STAMP_T(sc, 4);
+#ifdef G4_TRACE
+        if (sc.trace && blockIdx.x == 0 && i < 64) sc.trace[3128 + i] = globaltimer_ns();
+#endif
       }
       // nothing of ours may still be running when TMEM is released
       umma_commit(&ctl.drain);
@@ -269,6 +372,7 @@ __device__ void gemv_run(Op& op, uint8_t* smem_raw, const Scratch& sc) {
       while (!mbar_try_wait(&ctl.drain, 0))
         if (globaltimer_ns() - t0 > kWaitLimitNs) break;
     }
+    __syncwarp();  // lanes 1..31 wait here for lane 0: the teardown barrier needs whole warps
   } else {
     // ---------------------------------------------------------------- epilogue
     const int quarter = c.warp & 3;
@@ -278,8 +382,9 @@ __device__ void gemv_run(Op& op, uint8_t* smem_raw, const Scratch& sc) {
     int in_piece = 0;
     bool ok = true;  // after a failed wait the loop keeps its shape (named barriers) but skips work
     for (int i = 0; i < c.n; ++i) {
-      const int u = c.u0 + i, tile = u / UPT, kc = u % UPT, t = i % T, s = i % S;
-      if (ok) ok = mbar_wait_or_abort(&ctl.tfull[t], uint32_t((i / T) & 1), abort, sc.err);
+      const int u = c.u0 + i, tile = u / UPT, kc = u % UPT, t = i % T;
+      if (ok) ok = mbar_wait_or_abort(&ctl.done[t], uint32_t((i / T) & 1), abort, sc.err);
+      if (row == 0 && i == 0) G4_STAMP_T(sc, 5);
       tc_fence_after();
       if (!ok) {
       } else if constexpr (!Shape::kFp4) {
@@ -294,14 +399,13 @@ __device__ void gemv_run(Op& op, uint8_t* smem_raw, const Scratch& sc) {
         float d0[32], d1[32];
         tmem_ld32(tbase + lane_addr + uint32_t(t * Shape::kSlotCols), d0);
         tmem_ld32(tbase + lane_addr + uint32_t(t * Shape::kSlotCols + 32), d1);
-        const uint4 sraw = *reinterpret_cast<const uint4*>(c.stage(s) + Shape::kABytes + row * 16);
+        ok = mbar_wait_or_abort(&ctl.sfull[t], uint32_t((i / T) & 1), abort, sc.err);
+        const uint4 sraw =
+            *reinterpret_cast<const uint4*>(smem + Shape::kOffScl + size_t(t) * Shape::kScaleBytes + row * 16);
         tmem_ld_wait();
         tc_fence_before();
         __syncwarp();
-        if (c.lane == 0) {
-          mbar_arrive(&ctl.tempty[t]);
-          mbar_arrive(&ctl.empty[s]);
-        }
+        if (c.lane == 0) mbar_arrive(&ctl.tempty[t]);
         // block b of the unit: MMA b / 2, columns 4 (b % 2) .. 4 (b % 2) + 3 of its 8
         const uint32_t sw[4] = {sraw.x, sraw.y, sraw.z, sraw.w};
         const float* ge = gexp + c.bslot(kc) * 16;
@@ -317,6 +421,9 @@ __device__ void gemv_run(Op& op, uint8_t* smem_raw, const Scratch& sc) {
         }
       }
       ++in_piece;
+#ifdef G4_TRACE
+      if (sc.trace && blockIdx.x == 0 && i < 64 && row == 0) sc.trace[3192 + i] = globaltimer_ns();
+#endif
       if (kc == UPT - 1 || i == c.n - 1) {
         const float v = acc;
         if (in_piece == UPT) {
@@ -337,6 +444,7 @@ __device__ void gemv_run(Op& op, uint8_t* smem_raw, const Scratch& sc) {
               if (done) sc.counters[tile] = 0;
               ctl.bcast = done ? 1u : 0u;
             }
+            __syncwarp();
             named_bar(kEpiBarrier, kEpiThreads);
             if (ctl.bcast) {
               float tot = 0.f;
@@ -349,15 +457,21 @@ __device__ void gemv_run(Op& op, uint8_t* smem_raw, const Scratch& sc) {
         in_piece = 0;
       }
     }
+    if (row == 0) G4_STAMP_T(sc, 6);
   }
 
   // teardown: every MMA has completed (drain) and every TMEM load has been waited for
+  G4_STAMP_WARP(sc, 0);
   tc_fence_before();
   __syncthreads();
+  G4_STAMP(sc, 7);
+  G4_STAMP_WARP(sc, 1);
   if (c.warp == 1) {
     tc_fence_after();
     tmem_dealloc(tbase, Shape::kTmemCols);
+    G4_STAMP_WARP(sc, 2);
   }
+  G4_STAMP_WARP(sc, 3);
 }
 
 }  // namespace g4

@@ -29,6 +29,7 @@ struct QkvArgs {
   uint16_t* q_out;
   int ring_len;
   int rope_rows;
+  bool tiled;  // weights in the unit-tiled layout of g4_pack_tiles (else the reference row-major)
 };
 
 struct AttnArgs {
@@ -47,6 +48,7 @@ struct OArgs {
   const uint8_t* o_weight;
   const uint16_t* o_scale;
   uint16_t* residual;
+  bool tiled;
 };
 
 struct FfnArgs {
@@ -63,6 +65,7 @@ struct FfnArgs {
   const float* down_global;
   const uint16_t* post_rms;
   const uint16_t* layer_scalar;
+  bool tiled;
 };
 
 // TMA tensor maps of the weight matrices, encoded on the host once per (pointer, shape) and
@@ -104,5 +107,13 @@ cudaError_t launch_qkv(const QkvArgs& a, const LaunchEnv& env);
 cudaError_t launch_attention(const AttnArgs& a, const LaunchEnv& env);
 cudaError_t launch_o(const OArgs& a, const LaunchEnv& env);
 cudaError_t launch_ffn_nvfp4(const FfnArgs& a, const LaunchEnv& env);
+
+// Unit-tiled weight layout: rows grouped into tiles of `tile_rows`, each row cut into units of
+// `unit_bytes`; block (t, u) holds the unit-u bytes of tile t's rows of src and then (when src2
+// is given) of src2, contiguously; blocks are tile-major. With n = 1 or 2 sources:
+// dst[(((t * units + u) * n + which) * tile_rows + r) * unit_bytes + b]
+//   = src_which[(t * tile_rows + r) * row_bytes + u * unit_bytes + b].
+cudaError_t launch_pack_tiles(const uint8_t* src, const uint8_t* src2, uint8_t* dst, int rows, int row_bytes,
+                              int unit_bytes, int tile_rows, cudaStream_t stream);
 
 }  // namespace g4

@@ -40,53 +40,50 @@ __device__ bool last_cta(uint32_t* counter) {
     const uint32_t before = atomic_add_acq_rel_gpu(counter, 1u);
     is_last = (before == gridDim.x - 1) ? 1u : 0u;
   }
+  __syncwarp();
   __syncthreads();  // ... and the acquire precedes every thread's loads after it
   return is_last != 0;
 }
 
-// 1 / sqrt(mean(x^2) + eps) of a bf16 vector of K elements written by the preceding kernel
-// (gemma4.py:83-89): squares summed exactly in f64, the mean narrowed to f32.
-template <int K>
-__device__ float rms_inverse_of(const uint16_t* x, double* red) {
-  double ss = 0.0;
-  for (int k = threadIdx.x * 8; k < K; k += blockDim.x * 8) {
-    const uint4 raw = __ldcg(reinterpret_cast<const uint4*>(x + k));
-    const uint16_t* b = reinterpret_cast<const uint16_t*>(&raw);
-#pragma unroll
-    for (int j = 0; j < 8; ++j) {
-      const double f = bf16_to_f32(b[j]);
-      ss += f * f;
-    }
-  }
-  return rms_inverse(block_sum_d(ss, red), K);
+// Unit-tiled weights (g4_pack_tiles): pipeline unit u of a matrix is one contiguous block of
+// kUnitBox rows of 128 elements (both 128-element halves of its 128 rows, or of 64 up and 64 gate
+// rows), fetched by one 256-row TMA box; its block scales are one 128-row x 16-byte box.
+constexpr int kUnitBox = 2 * kTileRows;
+
+// Bring units [u0, u1) of a unit-tiled matrix (unit_bytes each) into L2 with one bulk prefetch.
+__device__ __forceinline__ void prefetch_units(const uint8_t* base, int u0, int u1, uint32_t unit_bytes) {
+  if (u1 > u0)
+    asm volatile("cp.async.bulk.prefetch.L2.global [%0], %1;" ::"l"(base + size_t(u0) * unit_bytes),
+                 "r"(uint32_t(u1 - u0) * unit_bytes)
+                 : "memory");
 }
 
-// 16 bf16 elements from a vector another kernel wrote (L2-coherent loads).
-__device__ __forceinline__ void load16_cg(const uint16_t* p, float (&v)[16]) {
-  const uint4 a = __ldcg(reinterpret_cast<const uint4*>(p));
-  const uint4 b = __ldcg(reinterpret_cast<const uint4*>(p + 8));
-  const uint16_t* ha = reinterpret_cast<const uint16_t*>(&a);
-  const uint16_t* hb = reinterpret_cast<const uint16_t*>(&b);
+// Loads of one 16-element group: bf16 input written by the preceding kernel (L2-coherent) and,
+// for the normalised ops, its gamma.
+__device__ __forceinline__ void load_group_cg(const uint16_t* x, int g, uint4 (&raw)[4]) {
+  raw[0] = __ldcg(reinterpret_cast<const uint4*>(x + 16 * g));
+  raw[1] = __ldcg(reinterpret_cast<const uint4*>(x + 16 * g + 8));
+}
+__device__ __forceinline__ void load_group_gamma(const uint16_t* gamma, int g, uint4 (&raw)[4]) {
+  raw[2] = *reinterpret_cast<const uint4*>(gamma + 16 * g);
+  raw[3] = *reinterpret_cast<const uint4*>(gamma + 16 * g + 8);
+}
+
+// The 16 bf16 values of two uint4 (element j in half j % 2 of word j / 2).
+__device__ __forceinline__ void bf16x16_to_f32(const uint4& a, const uint4& b, float (&v)[16]) {
+  const uint32_t w[8] = {a.x, a.y, a.z, a.w, b.x, b.y, b.z, b.w};
 #pragma unroll
-  for (int j = 0; j < 8; ++j) {
-    v[j] = bf16_to_f32(ha[j]);
-    v[8 + j] = bf16_to_f32(hb[j]);
+  for (int i = 0; i < 8; ++i) {
+    v[2 * i] = __uint_as_float(w[i] << 16);
+    v[2 * i + 1] = __uint_as_float(w[i] & 0xffff0000u);
   }
 }
 
-// h = bf16((x * inv) * gamma) for 16 elements (the pre-norm of the QKV and FFN ops).
-__device__ __forceinline__ void rms_scaled16(const uint16_t* x, const uint16_t* gamma, float inv, float (&v)[16]) {
+// h = bf16((x * inv) * gamma) for one group (the RMSNorm of gemma4.py:83-89).
+__device__ __forceinline__ void rms_apply16(const uint4 (&raw)[4], float inv, float (&v)[16]) {
   float g[16];
-  load16_cg(x, v);
-  const uint4 ga = *reinterpret_cast<const uint4*>(gamma);
-  const uint4 gb = *reinterpret_cast<const uint4*>(gamma + 8);
-  const uint16_t* ha = reinterpret_cast<const uint16_t*>(&ga);
-  const uint16_t* hb = reinterpret_cast<const uint16_t*>(&gb);
-#pragma unroll
-  for (int j = 0; j < 8; ++j) {
-    g[j] = bf16_to_f32(ha[j]);
-    g[8 + j] = bf16_to_f32(hb[j]);
-  }
+  bf16x16_to_f32(raw[0], raw[1], v);
+  bf16x16_to_f32(raw[2], raw[3], g);
 #pragma unroll
   for (int j = 0; j < 16; ++j) v[j] = bf16_round((v[j] * inv) * g[j]);
 }
@@ -204,19 +201,36 @@ struct QkvOp {
   const QkvMaps* maps;
   QkvArgs a;
   Scratch sc;
-  float inv = 0.f;
   uint32_t tx_bytes = QkvShape::kABytes;
+  static constexpr bool kRms = true;
+  static constexpr int kRmsGroups = kH / 16;
 
   __device__ void load_unit(uint8_t* stage, int tile, int kc, uint64_t* bar, uint64_t policy) const {
     constexpr int kQTiles = kQs / kTileRows, kKTiles = kPs / kTileRows;
     const CUtensorMap* m = tile < kQTiles ? &maps->q : (tile < kQTiles + kKTiles ? &maps->k : &maps->v);
-    const int row0 = (tile < kQTiles ? tile : (tile < kQTiles + kKTiles ? tile - kQTiles : tile - kQTiles - kKTiles)) *
-                     kTileRows;
-    tma_load_2d(stage, m, kc * kUnitK, row0, bar, policy);
-    tma_load_2d(stage + 16384, m, kc * kUnitK + 128, row0, bar, policy);
+    const int t = tile < kQTiles ? tile : (tile < kQTiles + kKTiles ? tile - kQTiles : tile - kQTiles - kKTiles);
+    if (a.tiled) {
+      tma_load_2d(stage, m, 0, (t * QkvShape::kUnitsPerTile + kc) * kUnitBox, bar, policy);
+    } else {  // row-major: (x = K offset, y = first row) per 128-element half
+      tma_load_2d(stage, m, kc * kUnitK, t * kTileRows, bar, policy);
+      tma_load_2d(stage + 16384, m, kc * kUnitK + 128, t * kTileRows, bar, policy);
+    }
   }
-  __device__ void prologue(GemvCtl& ctl) { inv = rms_inverse_of<kH>(a.x, ctl.red_d); }
-  __device__ void act16(int k0, float (&v)[16]) const { rms_scaled16(a.x + k0, a.input_rms + k0, inv, v); }
+  // units [u0, u1) of the fused q|k|v order into L2 (unit-tiled weights only)
+  __device__ void prefetch_l2(int u0, int u1) const {
+    if (!a.tiled) return;
+    constexpr int kQU = kQs / kTileRows * QkvShape::kUnitsPerTile, kKU = kPs / kTileRows * QkvShape::kUnitsPerTile;
+    constexpr uint32_t kB = QkvShape::kABytes;
+    prefetch_units(a.q_weight, u0, u1 < kQU ? u1 : kQU, kB);
+    prefetch_units(a.k_weight, (u0 > kQU ? u0 : kQU) - kQU, (u1 < kQU + kKU ? u1 : kQU + kKU) - kQU, kB);
+    prefetch_units(a.v_weight, (u0 > kQU + kKU ? u0 : kQU + kKU) - kQU - kKU, u1 - kQU - kKU, kB);
+  }
+  __device__ void prologue(GemvCtl&) {}
+  __device__ void load_group(int g, uint4 (&raw)[4]) const {
+    load_group_cg(a.x, g, raw);
+    load_group_gamma(a.input_rms, g, raw);
+  }
+  __device__ void finish_group(const uint4 (&raw)[4], float inv, float (&v)[16]) const { rms_apply16(raw, inv, v); }
   __device__ void finalize_tile(int tile, int row, float v, GemvCtl& ctl) const {
     const int r = tile * kTileRows + row;
     const uint16_t sb = r < kQs ? a.q_scale[r] : (r < kQs + kPs ? a.k_scale[r - kQs] : a.v_scale[r - kQs - kPs]);
@@ -230,6 +244,7 @@ struct QkvOp {
       if (done) sc.counters[kHeadCounterBase + head] = 0;
       ctl.bcast2 = done ? 1u : 0u;
     }
+    __syncwarp();
     named_bar(kEpiBarrier, kEpiThreads);
     // the warp holding row 0 (it took the ticket) normalises, rotates and stores the head
     if (ctl.bcast2 && (threadIdx.x >> 5) == 4) qkv_head_epilogue(a, sc, head);
@@ -251,13 +266,25 @@ struct OOp {
   OArgs a;
   Scratch sc;
   uint32_t tx_bytes = OShape::kABytes;
+  static constexpr bool kRms = false;
+  static constexpr int kRmsGroups = 0;
 
   __device__ void load_unit(uint8_t* stage, int tile, int kc, uint64_t* bar, uint64_t policy) const {
-    tma_load_2d(stage, map, kc * kUnitK, tile * kTileRows, bar, policy);
-    tma_load_2d(stage + 16384, map, kc * kUnitK + 128, tile * kTileRows, bar, policy);
+    if (a.tiled) {
+      tma_load_2d(stage, map, 0, (tile * OShape::kUnitsPerTile + kc) * kUnitBox, bar, policy);
+    } else {
+      tma_load_2d(stage, map, kc * kUnitK, tile * kTileRows, bar, policy);
+      tma_load_2d(stage + 16384, map, kc * kUnitK + 128, tile * kTileRows, bar, policy);
+    }
+  }
+  __device__ void prefetch_l2(int u0, int u1) const {
+    if (a.tiled) prefetch_units(a.o_weight, u0, u1, OShape::kABytes);
   }
   __device__ void prologue(GemvCtl&) {}
-  __device__ void act16(int k0, float (&v)[16]) const { load16_cg(a.x + k0, v); }
+  __device__ void load_group(int g, uint4 (&raw)[4]) const { load_group_cg(a.x, g, raw); }
+  __device__ void finish_group(const uint4 (&raw)[4], float, float (&v)[16]) const {
+    bf16x16_to_f32(raw[0], raw[1], v);
+  }
   __device__ void finalize_tile(int tile, int row, float v, GemvCtl&) const {
     const int r = tile * kTileRows + row;
     sc.y[r] = f32_to_bf16(v * bf16_to_f32(a.o_scale[r]));
@@ -274,6 +301,7 @@ __global__ void __launch_bounds__(kGemvThreads, 1) o_kernel(const __grid_constan
     residual_epilogue<kGemvThreads>(sc.y, a.post_rms, a.residual, nullptr, red);
     if (threadIdx.x == 0) sc.counters[kCtaCounter] = 0;
   }
+  G4_STAMP(sc, 8);
 }
 
 // ---------------------------------------------------------------------------------------
@@ -287,25 +315,46 @@ struct UpGateOp {
   const UpGateMaps* maps;
   FfnArgs a;
   Scratch sc;
-  float inv = 0.f, g_up = 0.f, g_gate = 0.f;
-  uint32_t tx_bytes = 4 * 64 * 64 + 2 * 64 * 16;  // four 64-row e2m1 boxes + two scale boxes
+  float g_up = 0.f, g_gate = 0.f;
+  uint32_t tx_bytes = 4 * 64 * 64;  // 256 rows x 64 bytes of packed e2m1 (one tiled box or four row-major)
+  static constexpr bool kRms = true;
+  static constexpr int kRmsGroups = kH / 16;
 
-  // stage: [K 0-127: up rows (8 KB) | gate rows (8 KB)] [K 128-255: same] [up scales | gate scales]
+  // stage: [K 0-127: up rows (8 KB) | gate rows (8 KB)] [K 128-255: same]
   __device__ void load_unit(uint8_t* stage, int tile, int kc, uint64_t* bar, uint64_t policy) const {
-    const int row0 = tile * 64, x = kc * kUnitK;
-    tma_load_2d(stage, &maps->up, x, row0, bar, policy);
-    tma_load_2d(stage + 8192, &maps->gate, x, row0, bar, policy);
-    tma_load_2d(stage + 16384, &maps->up, x + 128, row0, bar, policy);
-    tma_load_2d(stage + 24576, &maps->gate, x + 128, row0, bar, policy);
-    tma_load_2d(stage + UpGateShape::kABytes, &maps->up_s, kc * (kUnitK / 16), row0, bar, policy);
-    tma_load_2d(stage + UpGateShape::kABytes + 1024, &maps->gate_s, kc * (kUnitK / 16), row0, bar, policy);
+    if (a.tiled) {  // up and gate rows interleaved in one buffer: one box per unit
+      tma_load_2d(stage, &maps->up, 0, (tile * UpGateShape::kUnitsPerTile + kc) * kUnitBox, bar, policy);
+    } else {
+      const int x = kc * kUnitK;
+      tma_load_2d(stage, &maps->up, x, tile * 64, bar, policy);
+      tma_load_2d(stage + 8192, &maps->gate, x, tile * 64, bar, policy);
+      tma_load_2d(stage + 16384, &maps->up, x + 128, tile * 64, bar, policy);
+      tma_load_2d(stage + 24576, &maps->gate, x + 128, tile * 64, bar, policy);
+    }
   }
-  __device__ void prologue(GemvCtl& ctl) {
-    inv = rms_inverse_of<kH>(a.residual, ctl.red_d);
+  // block scales: [up rows | gate rows] x 16 bytes
+  __device__ void load_scales(uint8_t* dst, int tile, int kc, uint64_t* bar, uint64_t policy) const {
+    if (a.tiled) {
+      tma_load_2d(dst, &maps->up_s, 0, (tile * UpGateShape::kUnitsPerTile + kc) * kTileRows, bar, policy);
+    } else {
+      tma_load_2d(dst, &maps->up_s, kc * 16, tile * 64, bar, policy);
+      tma_load_2d(dst + 1024, &maps->gate_s, kc * 16, tile * 64, bar, policy);
+    }
+  }
+  __device__ void prefetch_l2(int u0, int u1) const {
+    if (!a.tiled) return;
+    prefetch_units(a.up_packed, u0, u1, UpGateShape::kABytes / 2);
+    prefetch_units(a.up_scale, u0, u1, UpGateShape::kScaleBytes);
+  }
+  __device__ void prologue(GemvCtl&) {
     g_up = *a.up_global;
     g_gate = *a.gate_global;
   }
-  __device__ void act16(int k0, float (&v)[16]) const { rms_scaled16(a.residual + k0, a.pre_rms + k0, inv, v); }
+  __device__ void load_group(int g, uint4 (&raw)[4]) const {
+    load_group_cg(a.residual, g, raw);
+    load_group_gamma(a.pre_rms, g, raw);
+  }
+  __device__ void finish_group(const uint4 (&raw)[4], float inv, float (&v)[16]) const { rms_apply16(raw, inv, v); }
   __device__ void finalize_tile(int tile, int row, float v, GemvCtl& ctl) const {
     // GloballyScaled(nn.Linear): bf16(bf16(x @ W.T) * g)  (generate_references.py:358-372)
     const float val = bf16_round(bf16_round(v) * (row < 64 ? g_up : g_gate));
@@ -322,6 +371,7 @@ __global__ void __launch_bounds__(kGemvThreads, 1) ffn_upgate_kernel(const __gri
   extern __shared__ __align__(1024) uint8_t smem[];
   UpGateOp op{&maps, a, sc};
   gemv_run<UpGateShape>(op, smem, sc);
+  G4_STAMP(sc, 8);
 }
 
 struct DownMaps {
@@ -333,16 +383,32 @@ struct DownOp {
   FfnArgs a;
   Scratch sc;
   float g_down = 0.f;
-  uint32_t tx_bytes = 2 * 128 * 64 + 128 * 16;
+  uint32_t tx_bytes = 2 * 128 * 64;  // 256 rows x 64 bytes of packed e2m1
+  static constexpr bool kRms = false;
+  static constexpr int kRmsGroups = 0;
 
   __device__ void load_unit(uint8_t* stage, int tile, int kc, uint64_t* bar, uint64_t policy) const {
-    const int row0 = tile * kTileRows, x = kc * kUnitK;
-    tma_load_2d(stage, &maps->w, x, row0, bar, policy);
-    tma_load_2d(stage + 16384, &maps->w, x + 128, row0, bar, policy);
-    tma_load_2d(stage + DownShape::kABytes, &maps->s, kc * (kUnitK / 16), row0, bar, policy);
+    if (a.tiled) {
+      tma_load_2d(stage, &maps->w, 0, (tile * DownShape::kUnitsPerTile + kc) * kUnitBox, bar, policy);
+    } else {
+      tma_load_2d(stage, &maps->w, kc * kUnitK, tile * kTileRows, bar, policy);
+      tma_load_2d(stage + 16384, &maps->w, kc * kUnitK + 128, tile * kTileRows, bar, policy);
+    }
+  }
+  __device__ void load_scales(uint8_t* dst, int tile, int kc, uint64_t* bar, uint64_t policy) const {
+    const int y = a.tiled ? (tile * DownShape::kUnitsPerTile + kc) * kTileRows : tile * kTileRows;
+    tma_load_2d(dst, &maps->s, a.tiled ? 0 : kc * 16, y, bar, policy);
+  }
+  __device__ void prefetch_l2(int u0, int u1) const {
+    if (!a.tiled) return;
+    prefetch_units(a.down_packed, u0, u1, DownShape::kABytes / 2);
+    prefetch_units(a.down_scale, u0, u1, DownShape::kScaleBytes);
   }
   __device__ void prologue(GemvCtl&) { g_down = *a.down_global; }
-  __device__ void act16(int k0, float (&v)[16]) const { load16_cg(sc.act + k0, v); }
+  __device__ void load_group(int g, uint4 (&raw)[4]) const { load_group_cg(sc.act, g, raw); }
+  __device__ void finish_group(const uint4 (&raw)[4], float, float (&v)[16]) const {
+    bf16x16_to_f32(raw[0], raw[1], v);
+  }
   __device__ void finalize_tile(int tile, int row, float v, GemvCtl&) const {
     const int r = tile * kTileRows + row;
     sc.y[r] = f32_to_bf16(bf16_round(v) * g_down);
@@ -359,6 +425,7 @@ __global__ void __launch_bounds__(kGemvThreads, 1) ffn_down_kernel(const __grid_
     residual_epilogue<kGemvThreads>(sc.y, a.post_rms, a.residual, a.layer_scalar, red);
     if (threadIdx.x == 0) sc.counters[kCtaCounter] = 0;
   }
+  G4_STAMP(sc, 8);
 }
 
 // ---------------------------------------------------------------------------------------
@@ -379,9 +446,11 @@ cudaError_t launch(void (*kernel)(KArgs...), int grid, size_t smem, const Launch
   return cudaLaunchKernelEx(&cfg, kernel, std::forward<Args>(args)...);
 }
 
-// One CTA per SM, unless a smaller GPU would give a CTA more K units than its B slots hold.
+// One CTA per SM, unless a smaller GPU would give a CTA more distinct K units than its B slots
+// hold (a run of n units touches min(n, units per tile) of them).
 template <class Shape>
 int grid_for(const LaunchEnv& env) {
+  if (Shape::kBSlots >= Shape::kUnitsPerTile) return env.sm_count;
   const int need = (Shape::kTotalUnits + Shape::kBSlots - 1) / Shape::kBSlots;
   return env.sm_count > need ? env.sm_count : need;
 }
@@ -406,34 +475,98 @@ cudaError_t prepare_proj_kernels() {
 cudaError_t launch_qkv(const QkvArgs& a, const LaunchEnv& env) {
   QkvMaps m;
   cudaError_t e;
-  if ((e = env.maps->u8(a.q_weight, kH, kQs, 128, kTileRows, true, &m.q))) return e;
-  if ((e = env.maps->u8(a.k_weight, kH, kPs, 128, kTileRows, true, &m.k))) return e;
-  if ((e = env.maps->u8(a.v_weight, kH, kPs, 128, kTileRows, true, &m.v))) return e;
-  return launch(qkv_kernel, grid_for<QkvShape>(env), QkvShape::kSmemBytes, env, m, a, env.sc);
+  // unit-tiled: a matrix of R rows is [R * K / 128, 128] bytes, one 256-row box per unit
+  const uint64_t cols = a.tiled ? 128 : kH, fq = a.tiled ? kH / 128 : 1;
+  const uint32_t box = a.tiled ? kUnitBox : kTileRows;
+  if ((e = env.maps->u8(a.q_weight, cols, kQs * fq, 128, box, true, &m.q))) return e;
+  if ((e = env.maps->u8(a.k_weight, cols, kPs * fq, 128, box, true, &m.k))) return e;
+  if ((e = env.maps->u8(a.v_weight, cols, kPs * fq, 128, box, true, &m.v))) return e;
+  return launch(qkv_kernel, grid_for<QkvShape>(env), QkvShape::kSmemBytes, env, m, a, env.sc);  // stamps at 0
 }
 
 cudaError_t launch_o(const OArgs& a, const LaunchEnv& env) {
   CUtensorMap m;
   cudaError_t e;
-  if ((e = env.maps->u8(a.o_weight, kQs, kH, 128, kTileRows, true, &m))) return e;
-  return launch(o_kernel, grid_for<OShape>(env), OShape::kSmemBytes, env, m, a, env.sc);
+  if ((e = env.maps->u8(a.o_weight, a.tiled ? 128 : kQs, a.tiled ? uint64_t(kH) * (kQs / 128) : kH, 128,
+                        a.tiled ? kUnitBox : kTileRows, true, &m)))
+    return e;
+  Scratch sc = env.sc;
+#ifdef G4_TRACE
+  if (sc.trace) sc.trace += 2 * 4096;  // profiling builds: separate stamp rows per kernel
+#endif
+  return launch(o_kernel, grid_for<OShape>(env), OShape::kSmemBytes, env, m, a, sc);
 }
 
 cudaError_t launch_ffn_nvfp4(const FfnArgs& a, const LaunchEnv& env) {
   UpGateMaps ug;
   DownMaps dn;
   cudaError_t e;
-  if ((e = env.maps->fp4(a.up_packed, kH, kL, 64, &ug.up))) return e;
-  if ((e = env.maps->fp4(a.gate_packed, kH, kL, 64, &ug.gate))) return e;
-  if ((e = env.maps->u8(a.up_scale, kH / 16, kL, 16, 64, false, &ug.up_s))) return e;
-  if ((e = env.maps->u8(a.gate_scale, kH / 16, kL, 16, 64, false, &ug.gate_s))) return e;
-  if ((e = env.maps->fp4(a.down_packed, kL, kH, kTileRows, &dn.w))) return e;
-  if ((e = env.maps->u8(a.down_scale, kL / 16, kH, 16, kTileRows, false, &dn.s))) return e;
-  e = launch(ffn_upgate_kernel, grid_for<UpGateShape>(env), UpGateShape::kSmemBytes, env, ug, a, env.sc);
+  if (a.tiled) {
+    // unit-tiled: up|gate codes interleaved [2 L * H / 128, 128 elements] (one 256-row box per
+    // unit), their scales [2 L * H / 256, 16 bytes]; down codes [H * L / 128, 128], scales
+    // [H * L / 256, 16]. gate_packed / gate_scale are not used (they live in the up buffers).
+    ug.gate = ug.up;
+    ug.gate_s = ug.up_s;
+    if ((e = env.maps->fp4(a.up_packed, 128, uint64_t(2) * kL * (kH / 128), kUnitBox, &ug.up))) return e;
+    if ((e = env.maps->u8(a.up_scale, 16, uint64_t(2) * kL * (kH / kUnitK), 16, kTileRows, false, &ug.up_s))) return e;
+    if ((e = env.maps->fp4(a.down_packed, 128, uint64_t(kH) * (kL / 128), kUnitBox, &dn.w))) return e;
+    if ((e = env.maps->u8(a.down_scale, 16, uint64_t(kH) * (kL / kUnitK), 16, kTileRows, false, &dn.s))) return e;
+  } else {
+    if ((e = env.maps->fp4(a.up_packed, kH, kL, 64, &ug.up))) return e;
+    if ((e = env.maps->fp4(a.gate_packed, kH, kL, 64, &ug.gate))) return e;
+    if ((e = env.maps->u8(a.up_scale, kH / 16, kL, 16, 64, false, &ug.up_s))) return e;
+    if ((e = env.maps->u8(a.gate_scale, kH / 16, kL, 16, 64, false, &ug.gate_s))) return e;
+    if ((e = env.maps->fp4(a.down_packed, kL, kH, kTileRows, &dn.w))) return e;
+    if ((e = env.maps->u8(a.down_scale, kL / 16, kH, 16, kTileRows, false, &dn.s))) return e;
+  }
+  Scratch sc = env.sc;
+#ifdef G4_TRACE
+  static int calls = 0;  // profiling builds: separate stamp rows per kernel, alternating per call
+  const int row_base = 3 + 2 * (calls++ % 2);
+  if (sc.trace) sc.trace += row_base * 4096;
+#endif
+  e = launch(ffn_upgate_kernel, grid_for<UpGateShape>(env), UpGateShape::kSmemBytes, env, ug, a, sc);
   if (e != cudaSuccess) return e;
   LaunchEnv chained = env;
   chained.pdl = true;  // the down pass prefetches its weights while the up/gate pass drains
-  return launch(ffn_down_kernel, grid_for<DownShape>(env), DownShape::kSmemBytes, chained, dn, a, env.sc);
+#ifdef G4_TRACE
+  if (chained.sc.trace) chained.sc.trace += (row_base + 1) * 4096;  // profiling builds: separate stamp rows
+#endif
+  return launch(ffn_down_kernel, grid_for<DownShape>(env), DownShape::kSmemBytes, chained, dn, a, chained.sc);
+}
+
+// ---------------------------------------------------------------------------------------
+// unit-tiled weight layout
+
+namespace {
+// dst block (t, u) = [src rows of tile t, unit u] then, with src2, [src2 rows of tile t, unit u]
+__global__ void pack_tiles_kernel(const uint8_t* __restrict__ src, const uint8_t* __restrict__ src2,
+                                  uint8_t* __restrict__ dst, int rows, int row_bytes, int unit_bytes, int tile_rows) {
+  // one thread per 16-byte chunk of the destination
+  const int units = row_bytes / unit_bytes, chunks = unit_bytes / 16, nsrc = src2 ? 2 : 1;
+  const int64_t total = int64_t(rows) * row_bytes / 16 * nsrc;
+  for (int64_t q = int64_t(blockIdx.x) * blockDim.x + threadIdx.x; q < total; q += int64_t(gridDim.x) * blockDim.x) {
+    const int b = int(q % chunks) * 16;
+    const int64_t row_in = q / chunks;  // ((blk * nsrc + which) * tile_rows + r)
+    const int r = int(row_in % tile_rows);
+    const int64_t bw = row_in / tile_rows;
+    const int which = int(bw % nsrc);
+    const int64_t blk = bw / nsrc;
+    const int u = int(blk % units);
+    const int64_t t = blk / units;
+    const uint8_t* from = which ? src2 : src;
+    *reinterpret_cast<uint4*>(dst + q * 16) =
+        *reinterpret_cast<const uint4*>(from + (t * tile_rows + r) * int64_t(row_bytes) + int64_t(u) * unit_bytes + b);
+  }
+}
+}  // namespace
+
+cudaError_t launch_pack_tiles(const uint8_t* src, const uint8_t* src2, uint8_t* dst, int rows, int row_bytes,
+                              int unit_bytes, int tile_rows, cudaStream_t stream) {
+  const int64_t total = int64_t(rows) * row_bytes / 16 * (src2 ? 2 : 1);
+  const int blocks = int((total + 255) / 256 < 4096 ? (total + 255) / 256 : 4096);
+  pack_tiles_kernel<<<blocks, 256, 0, stream>>>(src, src2, dst, rows, row_bytes, unit_bytes, tile_rows);
+  return cudaGetLastError();
 }
 
 // ---------------------------------------------------------------------------------------

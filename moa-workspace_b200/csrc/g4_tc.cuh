@@ -52,6 +52,13 @@ __device__ __forceinline__ void tma_load_2d(void* dst, const CUtensorMap* map, i
       : "memory");
 }
 
+// TMA: bring a 2-D tensor tile into L2 only (no shared memory, no barrier).
+__device__ __forceinline__ void tma_prefetch_l2_2d(const CUtensorMap* map, int x, int y) {
+  asm volatile("cp.async.bulk.prefetch.tensor.2d.L2.global.tile [%0, {%1, %2}];" ::"l"(reinterpret_cast<uint64_t>(map)),
+               "r"(x), "r"(y)
+               : "memory");
+}
+
 __device__ __forceinline__ void tma_prefetch_map(const CUtensorMap* map) {
   asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(map)) : "memory");
 }
@@ -184,6 +191,7 @@ __device__ __forceinline__ void split_terms16(const float (&v)[16], uint4 (&t)[N
         const float2 d = e4m3x2_to_f32x2(c);
         ra = (ra - d.x) * 16.0f;
         rb = (rb - d.y) * 16.0f;
+        if (ra == 0.f && rb == 0.f) break;  // every further term is zero
       }
     }
   }

@@ -91,8 +91,10 @@ def _arg(t: torch.Tensor, name: str, dtypes, shape, device: Device) -> ctypes.c_
 
 def sliding_project_qkv(device: Device, x, q_weight, k_weight, v_weight, q_weight_scale, k_weight_scale,
                         v_weight_scale, input_rms_weight, q_rms_weight, k_rms_weight, kv_offset, rope_offset,
-                        cos, sin, k_cache, v_cache, q_out, *, stream=None) -> None:
-    """ops::sliding_project_qkv (src/ops.rs:37-76). k_cache/v_cache: [ring, Ns, Ds]; cos/sin: [rows, Ds]."""
+                        cos, sin, k_cache, v_cache, q_out, *, tiled=False, stream=None) -> None:
+    """ops::sliding_project_qkv (src/ops.rs:37-76). k_cache/v_cache: [ring, Ns, Ds]; cos/sin: [rows, Ds].
+
+    tiled=True: q/k/v weights are in the unit-tiled layout made by `pack_tiles` (TILING)."""
     bf = torch.bfloat16
     ring = k_cache.shape[0] if k_cache.dim() == 3 else -1
     rows = cos.shape[0] if cos.dim() == 2 else -1
@@ -115,7 +117,8 @@ def sliding_project_qkv(device: Device, x, q_weight, k_weight, v_weight, q_weigh
         _arg(v_cache, "v_cache", bf, (ring, NS, DS), device),
         _arg(q_out, "q_out", bf, (NS, GS, DS), device),
     ]
-    st = _abi.lib().g4_sliding_project_qkv(device.handle, *args, ring, rows, _stream_ptr(stream, device.index))
+    fn = _abi.lib().g4_sliding_project_qkv_tiled if tiled else _abi.lib().g4_sliding_project_qkv
+    st = fn(device.handle, *args, ring, rows, _stream_ptr(stream, device.index))
     _check(device, st, "sliding_project_qkv")
 
 
@@ -135,8 +138,10 @@ def sliding_attention(device: Device, q, k, v, mask, out_hbm, *, scale: float = 
 
 
 def sliding_attention_output(device: Device, x, post_attn_rms_weight, o_weight, o_weight_scale, residual_hbm, *,
-                             stream=None) -> None:
-    """ops::sliding_attention_output (src/ops.rs:130-146). residual_hbm is updated in place."""
+                             tiled=False, stream=None) -> None:
+    """ops::sliding_attention_output (src/ops.rs:130-146). residual_hbm is updated in place.
+
+    tiled=True: o_weight is in the unit-tiled layout made by `pack_tiles` (TILING)."""
     bf = torch.bfloat16
     args = [
         _arg(x, "x", bf, (NS, GS, DS), device),
@@ -145,7 +150,8 @@ def sliding_attention_output(device: Device, x, post_attn_rms_weight, o_weight, 
         _arg(o_weight_scale, "o_weight_scale", bf, (H,), device),
         _arg(residual_hbm, "residual_hbm", bf, (H,), device),
     ]
-    st = _abi.lib().g4_sliding_attention_output(device.handle, *args, _stream_ptr(stream, device.index))
+    fn = _abi.lib().g4_sliding_attention_output_tiled if tiled else _abi.lib().g4_sliding_attention_output
+    st = fn(device.handle, *args, _stream_ptr(stream, device.index))
     _check(device, st, "sliding_attention_output")
 
 
@@ -175,3 +181,69 @@ def decoder_feedforward(device: Device, residual_hbm, pre_ff_rms_weight, up_weig
     ]
     st = _abi.lib().g4_decoder_feedforward(device.handle, *args, _stream_ptr(stream, device.index))
     _check(device, st, "decoder_feedforward")
+
+
+def decoder_feedforward_tiled(device: Device, residual_hbm, pre_ff_rms_weight, up_gate_weight_tiled,
+                              down_weight_tiled, up_gate_scale_tiled, down_scale_tiled, up_global_scale,
+                              gate_global_scale, down_global_scale, post_ff_rms_weight, layer_scalar, *,
+                              stream=None) -> None:
+    """decoder_feedforward on weights packed by `pack_upgate` / `tile_weight` (the GPU-native layout)."""
+    bf = torch.bfloat16
+    args = [
+        _arg(residual_hbm, "residual_hbm", bf, (H,), device),
+        _arg(pre_ff_rms_weight, "pre_ff_rms_weight", bf, (H,), device),
+        _arg(up_gate_weight_tiled, "up_gate_weight_tiled", torch.uint8, (2 * L, H // 2), device),
+        _arg(down_weight_tiled, "down_weight_tiled", torch.uint8, (H, L // 2), device),
+        _arg(up_gate_scale_tiled, "up_gate_scale_tiled", _BYTE_DTYPES, (2 * L, H // 16), device),
+        _arg(down_scale_tiled, "down_scale_tiled", _BYTE_DTYPES, (H, L // 16), device),
+        _arg(up_global_scale, "up_global_scale", torch.float32, (1,), device),
+        _arg(gate_global_scale, "gate_global_scale", torch.float32, (1,), device),
+        _arg(down_global_scale, "down_global_scale", torch.float32, (1,), device),
+        _arg(post_ff_rms_weight, "post_ff_rms_weight", bf, (H,), device),
+        _arg(layer_scalar, "layer_scalar", bf, (8,), device),
+    ]
+    st = _abi.lib().g4_decoder_feedforward_tiled(device.handle, *args, _stream_ptr(stream, device.index))
+    _check(device, st, "decoder_feedforward_tiled")
+
+
+# GPU-native (unit-tiled) layout of each weight matrix: (unit_bytes, tile_rows). A unit is the
+# 128 K elements of one tensor-memory-accelerator box (block scales: the 256 elements of one
+# pipeline step); the units of a tile of rows are contiguous in memory. The up and gate matrices
+# (codes and scales) are interleaved into one buffer by `pack_upgate`.
+TILING = {
+    "q_weight": (128, 128), "k_weight": (128, 128), "v_weight": (128, 128), "o_weight": (128, 128),
+    "up_gate_weight": (64, 64), "up_gate_scale": (16, 64),
+    "down_weight_packed": (64, 128), "down_weight_scale": (16, 128),
+}
+
+
+def pack_tiles(device: Device, src: torch.Tensor, src2: torch.Tensor | None = None, *, unit_bytes: int,
+               tile_rows: int, stream=None) -> torch.Tensor:
+    """src (and src2, interleaved tile by tile) [rows, row_bytes] in the unit-tiled layout; the
+    result has shape [rows * n_sources, row_bytes]. The weights are static: pack them once at load."""
+    if src.dim() != 2 or src.element_size() != 1:
+        raise ValueError("pack_tiles: expects a 2-D byte matrix")
+    if src2 is not None and (src2.shape != src.shape or src2.dtype != src.dtype):
+        raise ValueError("pack_tiles: src2 must match src")
+    n = 1 if src2 is None else 2
+    dst = torch.empty((src.shape[0] * n, src.shape[1]), dtype=src.dtype, device=src.device)
+    st = _abi.lib().g4_pack_tiles(device.handle, _arg(src, "src", src.dtype, None, device),
+                                  None if src2 is None else _arg(src2, "src2", src2.dtype, None, device),
+                                  _arg(dst, "dst", dst.dtype, None, device), src.shape[0], src.shape[1], unit_bytes,
+                                  tile_rows, _stream_ptr(stream, device.index))
+    _check(device, st, "pack_tiles")
+    return dst
+
+
+def tile_weight(device: Device, name: str, src: torch.Tensor, *, stream=None) -> torch.Tensor:
+    """`src` (the reference layout of weight `name`: q/k/v/o_weight, down_weight_packed or
+    down_weight_scale) in the GPU-native layout."""
+    unit_bytes, tile_rows = TILING[name]
+    return pack_tiles(device, src, unit_bytes=unit_bytes, tile_rows=tile_rows, stream=stream)
+
+
+def pack_upgate(device: Device, up: torch.Tensor, gate: torch.Tensor, *, scales: bool, stream=None) -> torch.Tensor:
+    """The up and gate packed codes (scales=False) or block scales (scales=True), interleaved in
+    the GPU-native layout of decoder_feedforward_tiled."""
+    unit_bytes, tile_rows = TILING["up_gate_scale" if scales else "up_gate_weight"]
+    return pack_tiles(device, up, gate, unit_bytes=unit_bytes, tile_rows=tile_rows, stream=stream)

@@ -235,3 +235,83 @@ def test_host_rejects_bad_arguments(device):
                                          r.data_ptr(), 1000, 1.0, None)
     assert st == _abi.G4_ERR_UNSUPPORTED
     device.check()
+
+
+# --------------------------------------------------------------------------------- unit-tiled weights
+
+def _tiled(device, name, arr):
+    from g4b200 import ops
+
+    return host_bits(ops.tile_weight(device, name, dev_tensor(arr)))
+
+
+def test_pack_tiles_layout(device):
+    """g4_pack_tiles against the layout formula, single- and two-source."""
+    from g4b200 import ops
+
+    rng = np.random.default_rng(7)
+    for name, (rows, row_bytes) in (("q_weight", (4096, 3840)), ("down_weight_packed", (3840, 7680)),
+                                    ("down_weight_scale", (3840, 960))):
+        unit, tr = ops.TILING[name]
+        src = rng.integers(0, 256, size=(rows, row_bytes), dtype=np.uint8)
+        got = _tiled(device, name, src).reshape(-1)
+        want = src.reshape(rows // tr, tr, row_bytes // unit, unit).transpose(0, 2, 1, 3).reshape(-1)
+        assert np.array_equal(got, want), name
+    for scales, (rows, row_bytes) in ((False, (15360, 1920)), (True, (15360, 240))):
+        unit, tr = ops.TILING["up_gate_scale" if scales else "up_gate_weight"]
+        a = rng.integers(0, 256, size=(rows, row_bytes), dtype=np.uint8)
+        b = rng.integers(0, 256, size=(rows, row_bytes), dtype=np.uint8)
+        got = host_bits(ops.pack_upgate(device, dev_tensor(a), dev_tensor(b), scales=scales)).reshape(-1)
+        pa = a.reshape(rows // tr, tr, row_bytes // unit, unit).transpose(0, 2, 1, 3)
+        pb = b.reshape(rows // tr, tr, row_bytes // unit, unit).transpose(0, 2, 1, 3)
+        want = np.stack([pa, pb], axis=2).reshape(-1)
+        assert np.array_equal(got, want), scales
+
+
+@pytest.mark.parametrize("run", [0, 3])
+def test_tiled_ops_bit_identical(device, run):
+    """The *_tiled entry points on packed weights give exactly the row-major entry points' results."""
+    import torch
+    from g4b200 import ops
+
+    d = synth.sliding_project_qkv(run)
+    q0, k0, v0 = run_qkv(device, d)
+    cos = np.zeros((32768, 256), np.uint16)
+    sin = np.zeros((32768, 256), np.uint16)
+    cos[d["pos"]], sin[d["pos"]] = d["cos_row"], d["sin_row"]
+    kc = dev_tensor(np.full((1024, 8, 256), SENTINEL_K, np.uint16))
+    vc = dev_tensor(np.full((1024, 8, 256), SENTINEL_V, np.uint16))
+    qo = dev_tensor(np.full((8, 2, 256), SENTINEL_Q, np.uint16))
+    ops.sliding_project_qkv(device, dev_tensor(d["x"]), *(ops.tile_weight(device, n, dev_tensor(d[n]))
+                                                          for n in ("q_weight", "k_weight", "v_weight")),
+                            dev_tensor(d["q_weight_scale"]), dev_tensor(d["k_weight_scale"]),
+                            dev_tensor(d["v_weight_scale"]), dev_tensor(d["input_rms_weight"]),
+                            dev_tensor(d["q_rms_weight"]), dev_tensor(d["k_rms_weight"]), dev_tensor(d["kv_offset"]),
+                            dev_tensor(d["rope_offset"]), dev_tensor(cos), dev_tensor(sin), kc, vc, qo, tiled=True)
+    device.check()
+    assert np.array_equal(host_bits(qo), q0) and np.array_equal(host_bits(kc), k0) and np.array_equal(host_bits(vc), v0)
+
+    d = synth.sliding_attention_output(run)
+    want = run_o(device, d["x"], d["post_attn_rms_weight"], d["o_weight"], d["o_weight_scale"], d["residual"])
+    res = dev_tensor(d["residual"])
+    ops.sliding_attention_output(device, dev_tensor(d["x"]), dev_tensor(d["post_attn_rms_weight"]),
+                                 ops.tile_weight(device, "o_weight", dev_tensor(d["o_weight"])),
+                                 dev_tensor(d["o_weight_scale"]), res, tiled=True)
+    device.check()
+    assert np.array_equal(host_bits(res), want)
+
+    for d in (synth.decoder_feedforward(run), synth.ffn_stress()):
+        want = run_ffn(device, d)
+        res = dev_tensor(d["residual"])
+        ug = ops.pack_upgate(device, dev_tensor(d["up_weight_packed"]), dev_tensor(d["gate_weight_packed"]),
+                             scales=False)
+        ugs = ops.pack_upgate(device, dev_tensor(d["up_weight_scale"]), dev_tensor(d["gate_weight_scale"]),
+                              scales=True)
+        ops.decoder_feedforward_tiled(device, res, dev_tensor(d["pre_ff_rms_weight"]), ug,
+                                      ops.tile_weight(device, "down_weight_packed", dev_tensor(d["down_weight_packed"])),
+                                      ugs, ops.tile_weight(device, "down_weight_scale", dev_tensor(d["down_weight_scale"])),
+                                      dev_tensor(d["up_global_scale"]), dev_tensor(d["gate_global_scale"]),
+                                      dev_tensor(d["down_global_scale"]), dev_tensor(d["post_ff_rms_weight"]),
+                                      dev_tensor(d["layer_scalar"]))
+        device.check()
+        assert np.array_equal(host_bits(res), want)
