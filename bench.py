@@ -51,6 +51,9 @@ BYTES = {
     "sliding_attention_output": H * QS + H * 2 + QS * 2 + H * 2 * 3,
     "decoder_feedforward": 2 * (L * H // 2 + L * H // 16) + (H * L // 2 + H * L // 16) + H * 2 * 4 + 8 * 2 + 12,
 }
+# DRAM bytes read + written per decoder_feedforward call (ffn_upgate + ffn_down): ncu --set full
+# capture of `python bench.py --only ffn --steps 3 --warmup 3` (dram__bytes_read.sum + write.sum)
+FFN_TRAFFIC = 66.43e6 + 0.69e6 + 33.29e6
 METRIC = "decode tokens/s through one Gemma-4 sliding decoder layer (QKV + attention + O + FFN ops, M=1)"
 WORKLOAD = ("gemma4-12b sliding decoder layer, M=1: fused QKV fp8 [8192x3840] + sliding attention "
             "(ring 1024 x 8 heads x 256, scale 1.0) + O fp8 [3840x4096] + NVFP4 GeGLU FFN [2x15360x3840 + 3840x15360]")
@@ -475,8 +478,8 @@ def run_ours(args):
         "scaling": "weak",
         "vs_baseline": None,
         "dtype": "bf16",
-        "arithmetic": "fp8 e4m3 / nvfp4 e2m1 weights dequantised exactly to f16, bf16 activations as exact f16 "
-                      "hi/lo pairs, f32 accumulation",
+        "arithmetic": "tcgen05 kind::f8f6f4: fp8 e4m3 / nvfp4 e2m1 weights x the bf16 activation split exactly "
+                      "into e4m3 terms, f32 accumulation in TMEM",
         "data": "synthetic",
         "config": {"workload": WORKLOAD, "global_batch": 1, "seq_len": TS, "parallelism": f"replicas x{world}",
                    "l2": f"inputs larger than L2: {N_LAYERS} distinct layers ({N_LAYERS * layer_bytes / 1e6:.0f} MB) "
@@ -539,8 +542,8 @@ def main():
     ap.add_argument("--warmup", type=int, default=64)
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--no-cpu", action="store_true", help="skip the CPU baseline sample")
-    ap.add_argument("--traffic", type=float, default=None,
-                    help="ncu dram bytes per decoder_feedforward call, if measured (reported as-is)")
+    ap.add_argument("--traffic", type=float, default=FFN_TRAFFIC,
+                    help="ncu dram bytes (read + write) per decoder_feedforward call")
     args = ap.parse_args()
     if args.warmup < 3:
         args.warmup = 3
