@@ -149,6 +149,29 @@ g4_status g4_decoder_feedforward_tiled(g4_ctx* ctx, uint16_t* residual_hbm, cons
                                        const float* down_global_scale, const uint16_t* post_ff_rms_weight,
                                        const uint16_t* layer_scalar, void* stream);
 
+/* No counterpart in the reference: ops::sliding_attention_output (src/ops.rs:130-146) with no
+ * context and no allocation, for callers that cannot create a g4_ctx. g4_ctx_create allocates
+ * device scratch (cudaMalloc) and host state; some callers may not allocate at all: a host
+ * runtime that plans every HBM buffer itself and hands the op only its own tensors (the
+ * reference's model: the caller allocates every buffer, src/host/runtime.rs:214-228), a
+ * process under a fixed device-memory budget, or a latency-critical thread where an allocation
+ * (and the synchronisation cudaMalloc/cudaFree may imply) is not acceptable.
+ * Arguments and result are those of g4_sliding_attention_output on reference-layout weights,
+ * on the CURRENT device and `stream`. The op's scratch (error word, split-K tickets, partial
+ * sums, the projected vector: 147,200 bytes on a B200) lives in one file-scope 192 KiB block
+ * of static device memory in this library, one per device. Returns G4_ERR_UNSUPPORTED if a GPU
+ * would need more than that, or is not sm_100. The error word and tickets must be zero when
+ * the kernel starts: the call zeroes them with cudaMemsetAsync on `stream` before each launch.
+ * The first call on a device looks up the block's address (cudaGetSymbolAddress, which may load
+ * the module) and sets kernel attributes: make that first call before any stream capture that
+ * should contain this op. The block is shared by every call on the device, so two calls whose
+ * executions overlap on the GPU (two streams, two threads) race and corrupt each other's
+ * results: order them on one stream. Device-side error bits of this entry point are not
+ * reported (there is no context to read them from). */
+g4_status g4_sliding_attention_output_noalloc(const uint16_t* x, const uint16_t* post_attn_rms_weight,
+                                              const uint8_t* o_weight, const uint16_t* o_weight_scale,
+                                              uint16_t* residual_hbm, void* stream);
+
 #ifdef __cplusplus
 }
 #endif

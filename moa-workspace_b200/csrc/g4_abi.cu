@@ -1,6 +1,7 @@
 // C ABI of libg4b200.so (declared in include/g4b200.h): contexts, argument validation and
 // the op entry points. No computation happens here; every op launches the sm_100a kernels
 // of g4_proj.cu / g4_attention.cu and there is no host or CPU fallback.
+#include <atomic>
 #include <cstdio>
 #include <cstring>
 #include <utility>
@@ -369,6 +370,90 @@ g4_status g4_pack_tiles(g4_ctx* ctx, const uint8_t* src, const uint8_t* src2, ui
   return cuda_status(ctx, g4::launch_pack_tiles(src, src2, dst, rows, row_bytes, unit_bytes, tile_rows,
                                                 static_cast<cudaStream_t>(stream)),
                      "g4_pack_tiles launch");
+}
+
+}  // extern "C"
+
+// ---------------------------------------------------------------------------------------
+// g4_sliding_attention_output_noalloc: the O op on a fixed block of static device memory.
+
+namespace {
+
+// 192 KiB per device (the O op needs 147,200 bytes on a 148-SM B200). Zero when the module
+// loads; the entry point zeroes the error word and the tickets again before every launch.
+constexpr size_t kStaticScratchBytes = size_t(192) << 10;
+constexpr int kStaticMaxDevices = 64;
+static __device__ __align__(256) uint8_t g_static_scratch[kStaticScratchBytes];
+
+// Per device: the block's address (cudaGetSymbolAddress) and the SM count, filled by the first
+// call on that device. Concurrent first calls store identical values.
+std::atomic<uint8_t*> g_static_base[kStaticMaxDevices];
+std::atomic<int> g_static_sms[kStaticMaxDevices];
+
+g4_status static_setup(int dev, uint8_t** base, int* sms) {
+  uint8_t* b = g_static_base[dev].load(std::memory_order_acquire);
+  if (b) {
+    *base = b;
+    *sms = g_static_sms[dev].load(std::memory_order_relaxed);
+    return G4_OK;
+  }
+  int major = 0, minor = 0, count = 0;
+  if (cudaDeviceGetAttribute(&major, cudaDevAttrComputeCapabilityMajor, dev) != cudaSuccess ||
+      cudaDeviceGetAttribute(&minor, cudaDevAttrComputeCapabilityMinor, dev) != cudaSuccess ||
+      cudaDeviceGetAttribute(&count, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess)
+    return G4_ERR_CUDA;
+  if (major != 10 || minor != 0) return G4_ERR_UNSUPPORTED;  // built for sm_100a only
+  if (g4::prepare_proj_kernels() != cudaSuccess) return G4_ERR_CUDA;
+  void* p = nullptr;
+  if (cudaGetSymbolAddress(&p, g_static_scratch) != cudaSuccess || !p) return G4_ERR_CUDA;
+  g_static_sms[dev].store(count, std::memory_order_relaxed);
+  g_static_base[dev].store(static_cast<uint8_t*>(p), std::memory_order_release);
+  *base = static_cast<uint8_t*>(p);
+  *sms = count;
+  return G4_OK;
+}
+
+}  // namespace
+
+extern "C" {
+
+g4_status g4_sliding_attention_output_noalloc(const uint16_t* x, const uint16_t* post_attn_rms_weight,
+                                              const uint8_t* o_weight, const uint16_t* o_weight_scale,
+                                              uint16_t* residual_hbm, void* stream) {
+  g4_status st = check_ptrs(nullptr, {{x, "x"},
+                                      {post_attn_rms_weight, "post_attn_rms_weight"},
+                                      {o_weight, "o_weight"},
+                                      {o_weight_scale, "o_weight_scale"},
+                                      {residual_hbm, "residual_hbm"}});
+  if (st != G4_OK) return st;
+  const size_t need = g4::o_scratch_bytes();
+  if (need > kStaticScratchBytes) return G4_ERR_UNSUPPORTED;  // this GPU needs more than the static block
+  int dev = -1;
+  if (cudaGetDevice(&dev) != cudaSuccess) return G4_ERR_CUDA;
+  if (dev < 0 || dev >= kStaticMaxDevices) return G4_ERR_UNSUPPORTED;
+  uint8_t* base = nullptr;
+  int sms = 0;
+  if ((st = static_setup(dev, &base, &sms)) != G4_OK) return st;
+
+  const size_t off_counters = g4::kScratchHeadBytes;
+  const size_t off_partials = off_counters + size_t(g4::kCounterCount) * sizeof(uint32_t);
+  const size_t off_y = need - size_t(g4::kH) * sizeof(uint16_t);  // y is the last region
+  g4::LaunchEnv env;
+  env.device = dev;
+  env.sm_count = sms;
+  env.stream = static_cast<cudaStream_t>(stream);
+  env.pdl = false;
+  env.sc.err = reinterpret_cast<uint32_t*>(base);
+  env.sc.counters = reinterpret_cast<uint32_t*>(base + off_counters);
+  env.sc.partials = reinterpret_cast<float*>(base + off_partials);
+  env.sc.y = reinterpret_cast<uint16_t*>(base + off_y);
+  env.sc.act = nullptr;
+  env.sc.trace = nullptr;
+  env.maps = nullptr;
+  // the error word and every ticket must be zero when the kernel starts
+  if (cudaMemsetAsync(base, 0, off_partials, env.stream) != cudaSuccess) return G4_ERR_CUDA;
+  const g4::OArgs a{x, post_attn_rms_weight, o_weight, o_weight_scale, residual_hbm, false};
+  return g4::launch_o_uncached(a, env) == cudaSuccess ? G4_OK : G4_ERR_CUDA;
 }
 
 #ifdef G4_TRACE

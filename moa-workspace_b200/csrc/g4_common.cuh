@@ -43,6 +43,7 @@ struct Scratch {
   uint16_t* act;       // bf16 GeGLU activation [M][L]
   uint64_t* trace;     // per-CTA phase timestamps (profiling builds only; null otherwise)
 };
+constexpr size_t kScratchHeadBytes = 256;  // the error word, padded to the scratch alignment
 constexpr int kCounterCount = 4096;
 constexpr int kCtaCounter = 4000;       // last-CTA ticket for whole-vector epilogues
 constexpr int kHeadCounterBase = 3968;  // 32 per-head tickets of the QKV op

@@ -108,6 +108,12 @@ cudaError_t launch_attention(const AttnArgs& a, const LaunchEnv& env);
 cudaError_t launch_o(const OArgs& a, const LaunchEnv& env);
 cudaError_t launch_ffn_nvfp4(const FfnArgs& a, const LaunchEnv& env);
 
+// The O op without a context: scratch laid out as [error word | kScratchHeadBytes][tickets]
+// [split-K partials][y] at env.sc, o_scratch_bytes() in total; the tensor map is encoded on the
+// stack (env.maps is not used). Row-major weights only.
+size_t o_scratch_bytes();
+cudaError_t launch_o_uncached(const OArgs& a, const LaunchEnv& env);
+
 // Unit-tiled weight layout: rows grouped into tiles of `tile_rows`, each row cut into units of
 // `unit_bytes`; block (t, u) holds the unit-u bytes of tile t's rows of src and then (when src2
 // is given) of src2, contiguously; blocks are tile-major. With n = 1 or 2 sources:

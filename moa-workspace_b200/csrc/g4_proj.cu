@@ -642,4 +642,28 @@ cudaError_t TmapCache::fp4(const void* base, uint64_t cols, uint64_t rows, uint3
   return cudaSuccess;
 }
 
+// ---------------------------------------------------------------------------------------
+// O projection on scratch the caller provides, with nothing cached or allocated
+
+size_t o_scratch_bytes() {
+  return kScratchHeadBytes + size_t(kCounterCount) * sizeof(uint32_t) +
+         size_t(OShape::kTiles) * kMaxCtasPerGroup * kTileRows * sizeof(float) + size_t(kH) * sizeof(uint16_t);
+}
+
+cudaError_t launch_o_uncached(const OArgs& a, const LaunchEnv& env) {
+  if (a.tiled) return cudaErrorInvalidValue;  // the reference (row-major) layout only
+  auto enc = encode_fn();
+  if (!enc) return cudaErrorNotSupported;
+  CUtensorMap m;
+  const cuuint64_t gdim[2] = {uint64_t(kQs), uint64_t(kH)};
+  const cuuint64_t gstride[1] = {uint64_t(kQs)};
+  const cuuint32_t box[2] = {128, uint32_t(kTileRows)};
+  const cuuint32_t estride[2] = {1, 1};
+  const CUresult r = enc(&m, CU_TENSOR_MAP_DATA_TYPE_UINT8, 2, const_cast<uint8_t*>(a.o_weight), gdim, gstride, box,
+                         estride, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+                         CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  if (r != CUDA_SUCCESS) return cudaErrorInvalidValue;
+  return launch(o_kernel, grid_for<OShape>(env), OShape::kSmemBytes, env, m, a, env.sc);
+}
+
 }  // namespace g4

@@ -40,6 +40,7 @@ SIGNATURES = {
     "g4_sliding_attention_output_tiled": [_p] * 6 + [_p],
     "g4_decoder_feedforward_tiled": [_p] * 12 + [_p],
     "g4_pack_tiles": [_p, _p, _p, _p, _i32, _i32, _i32, _i32, _p],
+    "g4_sliding_attention_output_noalloc": [_p] * 5 + [_p],
 }
 STRING_FUNCS = {"g4_status_string": [ctypes.c_int32], "g4_last_error": [_p]}
 
