@@ -478,8 +478,9 @@ def run_ours(args):
         "scaling": "weak",
         "vs_baseline": None,
         "dtype": "bf16",
-        "arithmetic": "tcgen05 kind::f8f6f4: fp8 e4m3 / nvfp4 e2m1 weights x the bf16 activation split exactly "
-                      "into e4m3 terms, f32 accumulation in TMEM",
+        "arithmetic": "tcgen05: fp8 e4m3 weights (kind::f8f6f4) x the bf16 activation as exact e4m3 terms; nvfp4 "
+                      "e2m1 weights with e4m3 block scales (kind::mxf4nvf4) x the activation as exact e2m1 digits; "
+                      "f32 accumulation in TMEM",
         "data": "synthetic",
         "config": {"workload": WORKLOAD, "global_batch": 1, "seq_len": TS, "parallelism": f"replicas x{world}",
                    "l2": f"inputs larger than L2: {N_LAYERS} distinct layers ({N_LAYERS * layer_bytes / 1e6:.0f} MB) "

@@ -17,8 +17,7 @@
  *   - Every call validates its arguments on the host and returns a g4_status; it never
  *     aborts. Calls are asynchronous and ordered on the caller's CUDA stream (`stream` is a
  *     cudaStream_t; NULL means the legacy default stream).
- *   - Every pointer must be device memory of the context's device, 16-byte aligned; the packed
- *     f4e2m1 weight matrices 32-byte aligned (they are read by the tensor-memory accelerator).
+ *   - Every pointer must be device memory of the context's device, 16-byte aligned.
  *   - Offsets that live in device memory (kv_offset, rope_offset) are checked on the
  *     device: an out-of-range value skips the writes that depend on it and raises a bit
  *     that g4_ctx_check() reports as G4_ERR_DEVICE.
@@ -48,6 +47,8 @@ typedef int32_t g4_status;
 #define G4_DEVERR_KV_OFFSET 1u    /* kv_offset outside the ring or not slot-aligned */
 #define G4_DEVERR_ROPE_OFFSET 2u  /* rope_offset outside the table or not row-aligned */
 #define G4_DEVERR_WAIT_TIMEOUT 4u /* a bounded in-kernel wait gave up */
+#define G4_DEVERR_NEGATIVE_SCALE 16u /* an nvfp4 block scale is negative (the reference's loader
+                                       * and harness only produce non-negative ones) */
 
 typedef struct g4_ctx g4_ctx;
 
@@ -120,17 +121,16 @@ g4_status g4_decoder_feedforward(g4_ctx* ctx, uint16_t* residual_hbm, const uint
  *     = src_which[(t * tile_rows + r) * row_bytes + u * unit_bytes + b]
  * Parameters (unit_bytes, tile_rows) per matrix:
  *   q, k, v, o weights (f8e4m3), one source each               128, 128
- *   up + gate packed codes (src = up, src2 = gate)              64, 64
+ *   up + gate packed codes (src = up, src2 = gate)              128, 64
  *   up + gate block scales (src = up, src2 = gate)              16, 64
- *   down packed codes                                           64, 128
+ *   down packed codes                                           128, 128
  *   down block scales                                           16, 128 */
 g4_status g4_pack_tiles(g4_ctx* ctx, const uint8_t* src, const uint8_t* src2, uint8_t* dst, int32_t rows,
                         int32_t row_bytes, int32_t unit_bytes, int32_t tile_rows, void* stream);
 
 /* The weight-streaming ops on weights packed by g4_pack_tiles; every other argument and every
  * result is that of the entry point of the same name without the suffix. The FFN takes the
- * up/gate codes and block scales as the interleaved buffers of one two-source g4_pack_tiles
- * call each. */
+ * up/gate codes and block scales as the interleaved buffers of one two-source call each. */
 g4_status g4_sliding_project_qkv_tiled(g4_ctx* ctx, const uint16_t* x, const uint8_t* q_weight,
                                        const uint8_t* k_weight, const uint8_t* v_weight,
                                        const uint16_t* q_weight_scale, const uint16_t* k_weight_scale,

@@ -52,7 +52,6 @@ g4_status cuda_status(g4_ctx* ctx, cudaError_t e, const char* where) {
 }
 
 bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
-bool aligned32(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 31u) == 0; }
 
 // Every pointer non-null and 16-byte aligned.
 g4_status check_ptrs(g4_ctx* ctx, std::initializer_list<std::pair<const void*, const char*>> ptrs) {
@@ -272,11 +271,6 @@ static g4_status decoder_feedforward(bool tiled, g4_ctx* ctx, uint16_t* residual
                                   {post_ff_rms_weight, "post_ff_rms_weight"},
                                   {layer_scalar, "layer_scalar"}});
   if (st != G4_OK) return st;
-  // packed e2m1 matrices are read by TMA as 16-code groups, which needs 32-byte alignment
-  for (const auto& p : {std::make_pair(static_cast<const void*>(up_weight_packed), "up_weight_packed"),
-                        std::make_pair(static_cast<const void*>(gate_weight_packed), "gate_weight_packed"),
-                        std::make_pair(static_cast<const void*>(down_weight_packed), "down_weight_packed")})
-    if (!aligned32(p.first)) return fail(ctx, G4_ERR_MISALIGNED, "pointer not 32-byte aligned: %s", p.second);
   DeviceGuard guard(ctx->device);
   g4::FfnArgs a{residual_hbm,      pre_ff_rms_weight, up_weight_packed, gate_weight_packed, down_weight_packed,
                 up_weight_scale,   gate_weight_scale, down_weight_scale, up_global_scale,   gate_global_scale,

@@ -31,6 +31,7 @@ enum : uint32_t {
   kErrRopeOffset = 1u << 1,
   kErrWaitTimeout = 1u << 2,
   kErrInternal = 1u << 3,  // a launch-geometry invariant did not hold (work was skipped)
+  kErrNegativeScale = 1u << 4,  // an nvfp4 block scale has its sign bit set
 };
 
 // Global scratch owned by a context. Counters are zero between launches: every kernel that

@@ -3,25 +3,30 @@
 //
 // Unit of work: 128 weight rows x 256 K elements (one UMMA tile row-block). The flat list of
 // tiles x K-units is split into one contiguous run per CTA (one CTA per SM), so every SM
-// streams the same number of bytes. Roles inside a CTA (192 threads):
-//   warp 0    TMA producer: 2-D tensor-map loads of the weight tiles (and NVFP4 block scales)
-//             into an S-stage shared-memory ring. The first S units are requested before the
-//             kernel waits on the preceding kernel (weights never depend on it).
-//   warp 1    MMA issuer: tcgen05.mma kind::f8f6f4 (A = weight codes, e4m3 or e2m1; B = the
-//             activation as exact e4m3 terms) into a ring of TMEM accumulator slots; one
-//             tcgen05.commit per unit both frees the stage and hands the slot to the epilogue.
-//   warps 2-5 epilogue: one thread per tile row; reads its TMEM lane, combines the terms (and
-//             the NVFP4 block scales) in f32 and finalises or publishes the row.
-// The activation is scaled by a power of two before the split, chosen per 16-element group
-// for nvfp4 weights (one block) and per 256-element unit for fp8 weights, so a few huge
-// activations never push small ones below the terms' range; the epilogue multiplies the
-// group's / unit's partial dot by the inverse factor.
-// B operand (N = 8 rows, K-major, 128-byte swizzle), per 256-element K unit:
-//   fp8 weights   rows 0..7 = terms t_0..t_7 of every element; one accumulator per unit.
-//   nvfp4 weights block-diagonal: within each 32-element MMA step, rows 0..3 hold the terms
-//                 t_0..t_3 of the first 16-element block and rows 4..7 those of the second,
-//                 so every MMA writes the per-block partial dots to its own 8 TMEM columns and
-//                 the epilogue applies the e4m3 block scale per (row, block) in f32.
+// streams the same number of bytes. Roles inside a CTA (224 threads):
+//   warp 0    TMA producer: tensor-map loads of the weight tiles (and the nvfp4 block scales)
+//             into an S-stage shared-memory ring. The ring is filled before the kernel
+//             waits on the preceding kernel (weights never depend on it).
+//   warp 1    MMA issuer (one thread). It never touches shared memory inside its loop: any
+//             shared-memory access of the issuing thread waits for the MMAs it has queued.
+//             Warp 6 (relay) waits on the unit's mbarriers and releases the issuer through a
+//             named barrier that also carries an abort flag. One tcgen05.commit per unit
+//             frees the stage.
+//   warps 2-5 epilogue: one thread per tile row; reads its TMEM lane and finalises or
+//             publishes the row. For nvfp4 weights they also move each unit's block scales
+//             from shared memory into TMEM (tcgen05.st) ahead of the MMAs.
+//
+// fp8 weights: tcgen05.mma kind::f8f6f4 (A = e4m3 codes, K = 32 per instruction; B = the
+//   activation as exact e4m3 terms, N = 8 rows: t_0..t_7). The activation is scaled by a power
+//   of two per 256-element unit before the split, so each unit has its own TMEM accumulator;
+//   the epilogue multiplies the unit's dot by the inverse factor and sums the units.
+// nvfp4 weights: tcgen05.mma kind::mxf4nvf4 with 16-element ue4m3 block scales (A = packed e2m1
+//   codes, K = 64 per instruction, its e4m3 block scales in TMEM; B = the activation as exact
+//   e2m1 base-8 digits, N = 16 rows: two exponent classes x 8 digits, B block scale 1). All
+//   units of a tile accumulate into one TMEM slot; the epilogue recombines the digits once per
+//   tile. Block scales live in TMEM in the scale-factor layout of the MMA: the scales of MMA j
+//   (blocks 4j..4j+3 of a row, 4 bytes) of row m sit in column 4j + m / 32, lane m % 32 of every
+//   lane quarter; each MMA's 4 columns start on a multiple of 4.
 // Rows whose K range is split across CTAs are published to global memory and summed by the
 // last CTA to finish the tile, in CTA order: the result never depends on timing.
 #pragma once
@@ -30,51 +35,63 @@
 
 namespace g4 {
 
-constexpr int kGemvThreads = 192;
+constexpr int kGemvThreads = 224;
 constexpr int kEpiThreads = 128;
+constexpr int kRelayWarp = 6;
 constexpr int kUnitK = 256;
 constexpr int kTileRows = 128;
-constexpr int kUmmaN = 8;
-constexpr int kMmaPerUnit = kUnitK / 32;
-constexpr int kEpiBarrier = 1;  // named barrier id of the epilogue warps
-constexpr int kMmaLookahead = 4;  // units whose readiness the MMA thread tests in one go
+constexpr int kEpiBarrier = 1;    // named barrier of the epilogue warps
+constexpr int kIssueBarrier = 2;  // named barrier of the MMA warp and the relay warp
+constexpr int kIssueThreads = 64;
 
 template <bool FP4, int STAGES, int UPT, int TILES, int BSLOTS, int L2AHEAD = 6>
 struct GemvShape {
   static constexpr bool kFp4 = FP4;
   static constexpr int kStages = STAGES;
+  static constexpr int kPreWait = STAGES;  // units requested before the dependency wait
   static constexpr int kL2Ahead = L2AHEAD;  // units requested into L2 beyond the shared-memory ring
   static constexpr int kUnitsPerTile = UPT;
   static constexpr int kTiles = TILES;
   static constexpr int kBSlots = BSLOTS;  // distinct K units one CTA may touch
   static constexpr int kTotalUnits = UPT * TILES;
-  static constexpr int kABytes = 2 * kTileRows * 128;                 // two 128-element K halves
-  static constexpr int kScaleBytes = FP4 ? kTileRows * (kUnitK / 16) : 0;
-  static constexpr int kStageBytes = kABytes;
-  static constexpr int kTmemSlots = FP4 ? 8 : 16;
-  static constexpr uint32_t kTmemCols = FP4 ? 512u : 128u;
-  static constexpr int kSlotCols = FP4 ? kMmaPerUnit * kUmmaN : kUmmaN;
-  static_assert(STAGES <= kTmemSlots, "a stage is released through its unit's TMEM-slot barrier");
-  static constexpr uint32_t kIdesc = umma_idesc_f8f6f4(FP4 ? kFmtE2M1 : kFmtE4M3, kFmtE4M3, kTileRows, kUmmaN);
-  static constexpr int kTerms = FP4 ? kUmmaN / 2 : kUmmaN;  // e4m3 terms per activation element
-  // shared memory: stages | B slots | block-scale ring (nvfp4, one per TMEM slot) |
-  //                term scales (2^-E per 16-element group) | control block
+  static constexpr int kN = FP4 ? 16 : 8;  // B rows: digits / terms
+  static constexpr int kABytes = FP4 ? kTileRows * 128 : 2 * kTileRows * 128;
+  static constexpr int kScaleBytes = FP4 ? kTileRows * 16 : 0;  // [128 rows][16 blocks] e4m3
+  static constexpr int kStageBytes = kABytes + kScaleBytes;
+  static constexpr int kBSlotBytes = 2048;  // fp8: 8 rows x 256 B; nvfp4: 16 rows x 128 B
+  // TMEM: fp8 - 16 accumulator slots of 8 columns (one per unit in flight).
+  //       nvfp4 - 4 tile accumulators of 16 columns | B scales (4 columns) | A scales, 16
+  //               columns per stage.
+  static constexpr int kTmemSlots = FP4 ? STAGES : 16;
+  static constexpr int kDSlots = 4;
+  static constexpr uint32_t kColSfb = 64;
+  static constexpr uint32_t kColSfa = 68;
+  static constexpr uint32_t kTmemCols = FP4 ? 256u : 128u;
+  static_assert(!FP4 || kColSfa + 16 * STAGES <= kTmemCols, "TMEM budget");
+  static_assert(FP4 || STAGES <= kTmemSlots, "a stage is released through its unit's TMEM-slot barrier");
+  static_assert(STAGES <= 12, "barrier arrays");
+  static constexpr uint32_t kIdesc =
+      FP4 ? umma_idesc_nvf4(kTileRows, kN) : umma_idesc_f8f6f4(kFmtE4M3, kFmtE4M3, kTileRows, kN);
+  // shared memory: stages | B slots | nvfp4 activation (bf16, 256 per B slot) |
+  //                fp8 unit scales 2^-E | control block
   static constexpr size_t kOffB = size_t(STAGES) * kStageBytes;
-  static constexpr size_t kOffScl = kOffB + size_t(BSLOTS) * 2048;
-  static constexpr size_t kOffExp = kOffScl + (FP4 ? size_t(kTmemSlots) * kScaleBytes : 0);
-  static constexpr size_t kOffCtl = kOffExp + size_t(BSLOTS) * 16 * sizeof(float);
+  static constexpr size_t kOffH = kOffB + size_t(BSLOTS) * kBSlotBytes;
+  static constexpr size_t kOffExp = kOffH + (FP4 ? size_t(BSLOTS) * 512 : 0);
+  static constexpr size_t kOffCtl = kOffExp + (FP4 ? 0 : size_t(BSLOTS) * 16 * sizeof(float));
   static constexpr size_t kSmemBytes = kOffCtl + 1024 + 1024;  // control block + alignment slack
   static_assert(kStageBytes % 1024 == 0, "stages must keep 1024-byte alignment");
   static_assert(kSmemBytes <= 227 * 1024, "shared memory budget");
 };
 
 struct GemvCtl {
-  uint64_t full[8], sfull[16], done[16], tempty[16], drain;
+  uint64_t full[12], sready[12], done[16], tempty[16], dfull[4], dempty[4], drain;
   uint32_t tmem_base;
   uint32_t abort;
   uint32_t bcast;
   uint32_t bcast2;
   uint32_t unit_max[16];  // per B slot: max |activation| bits (fp8 weights)
+  int pmax;               // nvfp4: largest exponent of this CTA's activation
+  uint32_t nonfinite;     // nvfp4: an activation of this CTA is Inf or NaN
   float xchg[64];
   double red_d[8];
   float red_f[8];
@@ -115,6 +132,30 @@ __device__ __forceinline__ double sum_squares_bf16x16(const uint4& a, const uint
   return ss;
 }
 
+// nvfp4 B operand: the digits of 8 consecutive activation elements (bf16 bits in `raw`) as
+// 4-byte pieces of the 16 B rows. An element of exponent e >= pc - 14 is class 0 (rows 0-7,
+// X = RN(v 2^(21 - pc)), exact); a smaller one is class 1 (rows 8-15, X = RN(v 2^(36 - pc)),
+// exact for e >= pc - 29, else off by less than 2^(pc - 37)). |X| < 2^22 in both classes.
+__device__ __forceinline__ void nvf4_digit_rows8(const uint4& raw, int pc, uint32_t (&rows)[16]) {
+  const uint32_t h[4] = {raw.x, raw.y, raw.z, raw.w};
+  uint32_t w[8];
+  uint32_t m0 = 0u;
+#pragma unroll
+  for (int k = 0; k < 8; ++k) {
+    const float v = __uint_as_float(k % 2 ? (h[k / 2] & 0xffff0000u) : (h[k / 2] << 16));
+    const bool cls0 = block_exponent(fabsf(v)) >= pc - 14;
+    const int x = __float2int_rn(mul_pow2(v, cls0 ? 21 - pc : 36 - pc));
+    w[k] = digit_codes8(uint32_t(x) + kDigitBias);
+    m0 |= cls0 ? (0xFu << (4 * k)) : 0u;
+  }
+  transpose8_nibbles(w);  // w[i]: nibble k = code of digit i of element k
+#pragma unroll
+  for (int i = 0; i < 8; ++i) {
+    rows[i] = w[i] & m0;
+    rows[8 + i] = w[i] & ~m0;
+  }
+}
+
 // Engine driver. `op` supplies:
 //   void load_unit(uint8_t* stage, int tile, int kc, uint64_t* bar, uint64_t policy) const  (TMA)
 //   void load_scales(uint8_t* dst, int tile, int kc, uint64_t* bar, uint64_t policy) const (nvfp4)
@@ -125,8 +166,9 @@ __device__ __forceinline__ double sum_squares_bf16x16(const uint4& a, const uint
 //   void load_group(int g, uint4 (&raw)[4]) const   issue the loads of 16-element group g
 //                                      (bf16 input in raw[0..1], gamma in raw[2..3])
 //   void finish_group(const uint4 (&raw)[4], float inv, float (&v)[16]) const   the activation
+//                                      (bf16-exact values)
 //   void finalize_tile(int tile, int row, float v, GemvCtl&) const   all 128 epilogue threads
-//   uint32_t tx_bytes                  bytes one unit's weight tiles deliver (block scales: kScaleBytes)
+//   uint32_t tx_bytes                  bytes one unit delivers (codes and, nvfp4, block scales)
 template <class Shape, class Op>
 __device__ void gemv_run(Op& op, uint8_t* smem_raw, const Scratch& sc) {
   constexpr int S = Shape::kStages, UPT = Shape::kUnitsPerTile, T = Shape::kTmemSlots;
@@ -148,14 +190,22 @@ __device__ void gemv_run(Op& op, uint8_t* smem_raw, const Scratch& sc) {
   G4_STAMP(sc, 0);
 
   if (c.tid == 0) {
-    for (int i = 0; i < S; ++i) mbar_init(&ctl.full[i], 1);
-    for (int i = 0; i < T; ++i) {
-      mbar_init(&ctl.sfull[i], 1);  // nvfp4: the unit's block scales have landed in the ring
-      mbar_init(&ctl.done[i], 1);   // the unit's MMAs have completed (one commit per unit)
-      mbar_init(&ctl.tempty[i], 4); // the epilogue is done with the TMEM slot (and scale slot)
+    for (int i = 0; i < S; ++i) {
+      mbar_init(&ctl.full[i], 1);
+      mbar_init(&ctl.sready[i], 4);  // nvfp4: the four epilogue warps put the unit's scales in TMEM
+    }
+    for (int i = 0; i < 16; ++i) {
+      mbar_init(&ctl.done[i], 1);    // the unit's MMAs have completed (one commit per unit)
+      mbar_init(&ctl.tempty[i], 4);  // fp8: the epilogue is done with the TMEM slot
+    }
+    for (int i = 0; i < Shape::kDSlots; ++i) {
+      mbar_init(&ctl.dfull[i], 1);   // nvfp4: the tile accumulator is complete
+      mbar_init(&ctl.dempty[i], 4);  // nvfp4: the epilogue has read it
     }
     mbar_init(&ctl.drain, 1);
     ctl.abort = 0;
+    ctl.pmax = -1000;
+    ctl.nonfinite = 0;
     fence_mbar_init();
   }
   if (c.tid < 16) ctl.unit_max[c.tid] = 0u;
@@ -166,30 +216,38 @@ __device__ void gemv_run(Op& op, uint8_t* smem_raw, const Scratch& sc) {
   tc_fence_after();
   const uint32_t tbase = ctl.tmem_base;
 
-  // weights first: they do not depend on the preceding kernel
+  // Weights do not depend on the preceding kernel: the first kPreWait units (the whole ring:
+  // measured faster than holding part of it back) are requested before waiting on it; the L2
+  // prefetch beyond the ring follows this CTA's activation loads.
   const uint64_t policy = l2_evict_first_policy();
   const int prefetch = c.n < S ? c.n : S;
-  if (c.tid == 0) {
-    for (int i = 0; i < prefetch; ++i) {  // i < S <= T: every stage and scale slot is free
+  const int prewait = prefetch < Shape::kPreWait ? prefetch : Shape::kPreWait;
+  auto request = [&](int i0, int i1) {  // units [i0, i1) into their (free) stages
+    for (int i = i0; i < i1; ++i) {
       const int u = c.u0 + i;
       mbar_arrive_expect_tx(&ctl.full[i], op.tx_bytes);
       op.load_unit(c.stage(i), u / UPT, u % UPT, &ctl.full[i], policy);
-      if constexpr (Shape::kFp4) {
-        mbar_arrive_expect_tx(&ctl.sfull[i], Shape::kScaleBytes);
-        op.load_scales(smem + Shape::kOffScl + size_t(i) * Shape::kScaleBytes, u / UPT, u % UPT, &ctl.sfull[i], policy);
-      }
+      if constexpr (Shape::kFp4) op.load_scales(c.stage(i) + Shape::kABytes, u / UPT, u % UPT, &ctl.full[i], policy);
     }
-    // the next units go to L2 only: the ring's loads then hit L2 instead of waiting on HBM
-    op.prefetch_l2(c.u0 + prefetch, c.u0 + (prefetch + Shape::kL2Ahead < c.n ? prefetch + Shape::kL2Ahead : c.n));
-  }
+  };
+  if (c.tid == 0) request(0, prewait);
   __syncwarp();  // CTA barriers below need converged warps
+  if constexpr (Shape::kFp4) {
+    // B block scales (1.0 for every block) and the first units' A scales into TMEM meanwhile
+    if (c.warp >= 2 && c.warp < 6) {
+      const uint32_t one[4] = {0x38383838u, 0x38383838u, 0x38383838u, 0x38383838u};
+      tmem_st4(tbase + (uint32_t((c.warp & 3) * 32) << 16) + Shape::kColSfb, one);
+      tmem_st_wait();
+    }
+  }
   pdl_wait_primary();
   pdl_launch_dependents();
   G4_STAMP(sc, 1);
 
   // activation -> B operand (only the K units this CTA touches). Every global load of the
   // prologue is issued before any is used: one round trip while the weight tiles stream in.
-  float* gexp = reinterpret_cast<float*>(smem + Shape::kOffExp);  // [slot][group] 2^-E
+  float* gexp = reinterpret_cast<float*>(smem + Shape::kOffExp);  // fp8: [slot][group] 2^-E
+  uint16_t* hsm = reinterpret_cast<uint16_t*>(smem + Shape::kOffH);  // nvfp4: [slot][256] bf16
   {
     constexpr int MAXG = 2;  // 16-element groups per thread
     static_assert(!Op::kRms || Op::kRmsGroups <= MAXG * kGemvThreads, "RMS statistic: too many groups");
@@ -210,6 +268,11 @@ __device__ void gemv_run(Op& op, uint8_t* smem_raw, const Scratch& sc) {
       }
       if (have[q]) op.load_group(grp[q], raw[q]);
     }
+    if (c.tid == 0) {
+      request(prewait, prefetch);
+      // the next units go to L2 only: the ring's loads then hit L2 instead of waiting on HBM
+      op.prefetch_l2(c.u0 + prefetch, c.u0 + (prefetch + Shape::kL2Ahead < c.n ? prefetch + Shape::kL2Ahead : c.n));
+    }
     float inv = 0.f;
     G4_STAMP(sc, 9);
     if constexpr (Op::kRms) {
@@ -219,68 +282,81 @@ __device__ void gemv_run(Op& op, uint8_t* smem_raw, const Scratch& sc) {
         if (have[q]) ss += sum_squares_bf16x16(raw[q][0], raw[q][1]);
       inv = rms_inverse(block_sum_d(ss, ctl.red_d), Op::kRmsGroups * 16);
     }
-    // exponent E of a max |v| so that max |v| 2^E lies in [128, 256)
-    auto exponent_of = [](float amax) {
-      int e = 0;
-      if (amax > 0.f) {
-        e = 7 - (int((__float_as_uint(amax) >> 23) & 0xff) - 127);
-        e = e > 120 ? 120 : (e < -120 ? -120 : e);
-      }
-      return e;
-    };
-    float v[MAXG][16], amax[MAXG];
+    float v[MAXG][16];
     int slot[MAXG];
 #pragma unroll
     for (int q = 0; q < MAXG; ++q) {
       slot[q] = c.bslot(grp[q] / 16);
       have[q] = have[q] && slot[q] < nslots;
-      amax[q] = 0.f;
       if (have[q]) {
         op.finish_group(raw[q], inv, v[q]);
+        float amax = 0.f;
+        bool nan = false;
 #pragma unroll
-        for (int j = 0; j < 16; ++j) amax[q] = fmaxf(amax[q], fabsf(v[q][j]));
-        if constexpr (!Shape::kFp4)  // one exponent per 256-element unit
-          atomicMax(&ctl.unit_max[slot[q]], __float_as_uint(amax[q]));  // non-negative floats order as ints
-      }
-    }
-    if constexpr (!Shape::kFp4) {
-      __syncthreads();
-#pragma unroll
-      for (int q = 0; q < MAXG; ++q)
-        if (have[q]) amax[q] = __uint_as_float(ctl.unit_max[slot[q]]);
-    }
-    const uint4 zero = make_uint4(0, 0, 0, 0);
-    G4_STAMP(sc, 10);
-#pragma unroll
-    for (int q = 0; q < MAXG; ++q) {
-      if (!have[q]) continue;
-      const int e16 = (grp[q] % 16) * 16;
-      const int e = exponent_of(amax[q]);
-      const float up = pow2f(e);
-      gexp[slot[q] * 16 + grp[q] % 16] = pow2f(-e);
-#pragma unroll
-      for (int j = 0; j < 16; ++j) v[q][j] *= up;
-      uint4 tm[Shape::kTerms];
-      split_terms16<Shape::kTerms>(v[q], tm);
-      uint8_t* atom = c.bsm + size_t(slot[q]) * 2048 + (e16 / 128) * 1024;
-      const uint32_t kb = e16 % 128;
-      uint4 rows[8];
-      if constexpr (Shape::kFp4) {
-        const bool second = (e16 / 16) % 2;
-#pragma unroll
-        for (int j = 0; j < 4; ++j) {
-          rows[j] = second ? zero : tm[j];
-          rows[4 + j] = second ? tm[j] : zero;
+        for (int j = 0; j < 16; ++j) {
+          amax = fmaxf(amax, fabsf(v[q][j]));
+          nan = nan || v[q][j] != v[q][j];
         }
-      } else {
+        if constexpr (Shape::kFp4) {
+          const int P = block_exponent(amax);
+          if (P > 127 || nan) ctl.nonfinite = 1u;
+          atomicMax(&ctl.pmax, P);
+          uint32_t bits[8];  // the bf16 values (exact) for the digit pass
 #pragma unroll
-        for (int j = 0; j < 8; ++j) rows[j] = tm[j];
+          for (int j = 0; j < 8; ++j)
+            bits[j] = (__float_as_uint(v[q][2 * j]) >> 16) | (__float_as_uint(v[q][2 * j + 1]) & 0xffff0000u);
+          uint4* dst = reinterpret_cast<uint4*>(hsm + slot[q] * 256 + (grp[q] % 16) * 16);
+          dst[0] = make_uint4(bits[0], bits[1], bits[2], bits[3]);
+          dst[1] = make_uint4(bits[4], bits[5], bits[6], bits[7]);
+        } else {  // one exponent per 256-element unit; non-negative floats order as ints
+          atomicMax(&ctl.unit_max[slot[q]], __float_as_uint(amax));
+        }
       }
-#pragma unroll
-      for (int r = 0; r < 8; ++r) *reinterpret_cast<uint4*>(atom + sw128_offset(r, kb)) = rows[r];
     }
+    __syncthreads();
+    G4_STAMP(sc, 10);
+    if constexpr (Shape::kFp4) {
+      // digit rows, one thread per 8 elements
+      const int pc = ctl.pmax;
+      for (int hb = c.tid; hb < nslots * 32; hb += kGemvThreads) {
+        const int sl = hb / 32, e8 = hb % 32;  // elements 8 e8 .. 8 e8 + 7 of slot sl
+        uint32_t rows[16];
+        nvf4_digit_rows8(*reinterpret_cast<const uint4*>(hsm + sl * 256 + e8 * 8), pc, rows);
+        uint8_t* bs = c.bsm + size_t(sl) * Shape::kBSlotBytes;
+#pragma unroll
+        for (int r = 0; r < 16; ++r) *reinterpret_cast<uint32_t*>(bs + sw128_offset(r, e8 * 4)) = rows[r];
+      }
+    } else {
+      // exponent E of a max |v| so that max |v| 2^E lies in [128, 256)
+      auto exponent_of = [](float a) {
+        int e = 0;
+        if (a > 0.f) {
+          e = 7 - (int((__float_as_uint(a) >> 23) & 0xff) - 127);
+          e = e > 120 ? 120 : (e < -120 ? -120 : e);
+        }
+        return e;
+      };
+#pragma unroll
+      for (int q = 0; q < MAXG; ++q) {
+        if (!have[q]) continue;
+        const int e16 = (grp[q] % 16) * 16;
+        const int e = exponent_of(__uint_as_float(ctl.unit_max[slot[q]]));
+        const float up = pow2f(e);
+        gexp[slot[q] * 16 + grp[q] % 16] = pow2f(-e);
+#pragma unroll
+        for (int j = 0; j < 16; ++j) v[q][j] *= up;
+        uint4 tm[8];
+        split_terms16<8>(v[q], tm);
+        uint8_t* atom = c.bsm + size_t(slot[q]) * Shape::kBSlotBytes + (e16 / 128) * 1024;
+        const uint32_t kb = e16 % 128;
+#pragma unroll
+        for (int r = 0; r < 8; ++r) *reinterpret_cast<uint4*>(atom + sw128_offset(r, kb)) = tm[r];
+      }
+    }
+    G4_STAMP(sc, 11);
   }
   asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+  tc_fence_before();
   __syncthreads();
   G4_STAMP(sc, 2);
 
@@ -291,18 +367,16 @@ __device__ void gemv_run(Op& op, uint8_t* smem_raw, const Scratch& sc) {
       for (int i = prefetch; i < c.n; ++i) {
         const int s = i % S;
         // stage s is free once the MMAs of unit i - S have completed
-        if (!mbar_wait_or_abort(&ctl.done[(i - S) % T], uint32_t(((i - S) / T) & 1), abort, sc.err)) break;
+        const int r = i - S;
+        const bool free = Shape::kFp4 ? mbar_wait_or_abort(&ctl.done[s], uint32_t((r / S) & 1), abort, sc.err)
+                                      : mbar_wait_or_abort(&ctl.done[r % T], uint32_t((r / T) & 1), abort, sc.err);
+        if (!free) break;
         const int u = c.u0 + i;
         mbar_arrive_expect_tx(&ctl.full[s], op.tx_bytes);
         op.load_unit(c.stage(s), u / UPT, u % UPT, &ctl.full[s], policy);
+        if constexpr (Shape::kFp4) op.load_scales(c.stage(s) + Shape::kABytes, u / UPT, u % UPT, &ctl.full[s], policy);
         if ((i - prefetch) % 2 == 0 && i + Shape::kL2Ahead < c.n)  // two units per bulk L2 prefetch
           op.prefetch_l2(u + Shape::kL2Ahead, c.u0 + (i + Shape::kL2Ahead + 2 < c.n ? i + Shape::kL2Ahead + 2 : c.n));
-        if constexpr (Shape::kFp4) {  // scale slot t is free once the epilogue is done with unit i - T
-          const int t = i % T;
-          if (i >= T && !mbar_wait_or_abort(&ctl.tempty[t], uint32_t(((i / T) - 1) & 1), abort, sc.err)) break;
-          mbar_arrive_expect_tx(&ctl.sfull[t], Shape::kScaleBytes);
-          op.load_scales(smem + Shape::kOffScl + size_t(t) * Shape::kScaleBytes, u / UPT, u % UPT, &ctl.sfull[t], policy);
-        }
         issued = i + 1;
 #ifdef G4_TRACE
         if (sc.trace && blockIdx.x == 0 && i < 64) sc.trace[3000 + i] = globaltimer_ns();
@@ -314,149 +388,196 @@ __device__ void gemv_run(Op& op, uint8_t* smem_raw, const Scratch& sc) {
         while (!mbar_try_wait(&ctl.full[i % S], uint32_t((i / S) & 1)))
           if (globaltimer_ns() - t0 > kWaitLimitNs) break;
       }
-      if constexpr (Shape::kFp4) {
-        for (int i = issued - T > 0 ? issued - T : 0; i < issued; ++i) {
-          const uint64_t t0 = globaltimer_ns();
-          while (!mbar_try_wait(&ctl.sfull[i % T], uint32_t((i / T) & 1)))
-            if (globaltimer_ns() - t0 > kWaitLimitNs) break;
-        }
-      }
     }
     __syncwarp();  // lanes 1..31 wait here for lane 0: the teardown barrier needs whole warps
+  } else if (c.warp == kRelayWarp) {
+    // ---------------------------------------------------------------- relay
+    // Unit i may be issued once it landed (fp8: and its TMEM slot is free; nvfp4: once its
+    // scales are in TMEM and, for the first unit of a tile piece, its accumulator is free).
+    // Both warps pass the issue barrier once per unit; a failed wait aborts both.
+    int piece = -1;
+    for (int i = 0; i < c.n; ++i) {
+      bool bad = false;
+      if (c.lane == 0) {
+        const int s = i % S, kc = (c.u0 + i) % UPT;
+        if constexpr (Shape::kFp4) {
+          const bool first = i == 0 || kc == 0;
+          if (first) ++piece;
+          bad = !mbar_wait_or_abort(&ctl.sready[s], uint32_t((i / S) & 1), abort, sc.err);
+          if (!bad && first && piece >= Shape::kDSlots)
+            bad = !mbar_wait_or_abort(&ctl.dempty[piece % Shape::kDSlots], uint32_t(((piece / Shape::kDSlots) - 1) & 1),
+                                      abort, sc.err);
+        } else {
+          bad = !mbar_wait_or_abort(&ctl.full[s], uint32_t((i / S) & 1), abort, sc.err) ||
+                (i >= T && !mbar_wait_or_abort(&ctl.tempty[i % T], uint32_t(((i / T) - 1) & 1), abort, sc.err));
+        }
+      }
+      __syncwarp();
+      if (named_bar_or(kIssueBarrier, kIssueThreads, bad)) break;
+    }
   } else if (c.warp == 1) {
     // ---------------------------------------------------------------- MMA issuer
-    // One commit per unit both frees the stage's weight tiles and hands the TMEM slot to the
-    // epilogue. Any shared-memory access of this thread (an mbarrier test included) waits for
-    // the MMAs it has queued, so readiness is checked for several units at a time: one blocking
-    // wait for the next unit, then non-blocking tests of the following ones.
-    if (c.lane == 0) {
-      int ready = 0;  // units [i, ready) have landed and have a free TMEM slot
-      bool alive = true;
-      for (int i = 0; i < c.n && alive; ++i) {
-        const int s = i % S, t = i % T;
-        if (i >= ready) {
-          alive = mbar_wait_or_abort(&ctl.full[s], uint32_t((i / S) & 1), abort, sc.err) &&
-                  (i < T || mbar_wait_or_abort(&ctl.tempty[t], uint32_t(((i / T) - 1) & 1), abort, sc.err));
-          if (!alive) break;
-          ready = i + 1;
-          while (ready < c.n && ready < i + kMmaLookahead &&
-                 mbar_test(&ctl.full[ready % S], uint32_t((ready / S) & 1)) &&
-                 (ready < T || mbar_test(&ctl.tempty[ready % T], uint32_t(((ready / T) - 1) & 1))))
-            ++ready;
-          tc_fence_after();
-        }
-        if (i == 0) G4_STAMP_T(sc, 3);
+    int piece = -1;
+    for (int i = 0; i < c.n; ++i) {
+      if (named_bar_or(kIssueBarrier, kIssueThreads, false)) break;
+      tc_fence_after();
+      if (i == 0) G4_STAMP_T(sc, 3);
+      if (c.lane == 0) {
 #ifdef G4_TRACE
         if (sc.trace && blockIdx.x == 0 && i < 64) sc.trace[3064 + i] = globaltimer_ns();
 #endif
-        const int kc = (c.u0 + i) % UPT;
+        const int s = i % S, t = i % T, kc = (c.u0 + i) % UPT;
         const uint32_t a_base = smem_u32(c.stage(s));
-        const uint32_t b_base = smem_u32(c.bsm) + uint32_t(c.bslot(kc)) * 2048u;
+        const uint32_t b_base = smem_u32(c.bsm) + uint32_t(c.bslot(kc)) * Shape::kBSlotBytes;
+        if constexpr (Shape::kFp4) {
+          const bool first = i == 0 || kc == 0;
+          if (first) ++piece;
+          const uint32_t d = tbase + uint32_t(piece % Shape::kDSlots) * 16u;
+          const uint32_t sfa = tbase + Shape::kColSfa + uint32_t(s) * 16u;
 #pragma unroll
-        for (int j = 0; j < kMmaPerUnit; ++j) {
-          const uint32_t h = j / 4, kk = j % 4;
-          const uint64_t ad = umma_desc_sw128(a_base + h * 16384u + kk * 32u);
-          const uint64_t bd = umma_desc_sw128(b_base + h * 1024u + kk * 32u);
-          const uint32_t col = Shape::kFp4 ? uint32_t(t * Shape::kSlotCols + j * kUmmaN) : uint32_t(t * kUmmaN);
-          umma_f8f6f4(tbase + col, ad, bd, Shape::kIdesc, Shape::kFp4 ? 0u : uint32_t(j > 0));
+          for (int j = 0; j < 4; ++j)
+            umma_nvf4(d, umma_desc_sw128(a_base + 32u * j), umma_desc_sw128(b_base + 32u * j), Shape::kIdesc,
+                      sfa + 4 * j, tbase + Shape::kColSfb, uint32_t(!first || j > 0));
+          umma_commit(&ctl.done[s]);
+          if (i == c.n - 1 || kc == UPT - 1) umma_commit(&ctl.dfull[piece % Shape::kDSlots]);
+        } else {
+#pragma unroll
+          for (int j = 0; j < 8; ++j) {
+            const uint32_t h = j / 4, kk = j % 4;
+            const uint64_t ad = umma_desc_sw128(a_base + h * 16384u + kk * 32u);
+            const uint64_t bd = umma_desc_sw128(b_base + h * 1024u + kk * 32u);
+            umma_f8f6f4(tbase + uint32_t(t * 8), ad, bd, Shape::kIdesc, uint32_t(j > 0));
+          }
+          umma_commit(&ctl.done[t]);
         }
-        umma_commit(&ctl.done[t]);
-        if (i == c.n - 1) G4_STAMP_T(sc, 4);
 #ifdef G4_TRACE
         if (sc.trace && blockIdx.x == 0 && i < 64) sc.trace[3128 + i] = globaltimer_ns();
 #endif
       }
-      // nothing of ours may still be running when TMEM is released
+      if (i == c.n - 1) G4_STAMP_T(sc, 4);
+      __syncwarp();
+    }
+    // nothing of ours may still be running when TMEM is released
+    if (c.lane == 0) {
       umma_commit(&ctl.drain);
       const uint64_t t0 = globaltimer_ns();
       while (!mbar_try_wait(&ctl.drain, 0))
         if (globaltimer_ns() - t0 > kWaitLimitNs) break;
     }
-    __syncwarp();  // lanes 1..31 wait here for lane 0: the teardown barrier needs whole warps
+    __syncwarp();
   } else {
-    // ---------------------------------------------------------------- epilogue
+    // ---------------------------------------------------------------- epilogue (warps 2-5)
     const int quarter = c.warp & 3;
     const int row = quarter * 32 + c.lane;
     const uint32_t lane_addr = uint32_t(quarter * 32) << 16;
     float acc = 0.f;
-    int in_piece = 0;
+    int in_piece = 0, piece = -1;
     bool ok = true;  // after a failed wait the loop keeps its shape (named barriers) but skips work
+    // nvfp4: block scales of units [prep, lim) from the stage into TMEM, in unit order. Row m's
+    // 16 scale bytes hold MMA j's 4 scales at bytes 4j..4j+3; this lane writes rows
+    // lane + 32 g (g = 0..3) to columns 4j + g of its lane quarter.
+    int prep = 0;
+    auto prepare = [&](int lim) {
+      for (; prep < lim; ++prep) {
+        const int s = prep % S;
+        if (ok) ok = mbar_wait_or_abort(&ctl.full[s], uint32_t((prep / S) & 1), abort, sc.err);
+        if (ok) {
+          const uint8_t* scl = c.stage(s) + Shape::kABytes;
+          uint32_t w[16];
+          uint32_t sign = 0u;
+#pragma unroll
+          for (int g = 0; g < 4; ++g) {
+            const uint4 r = *reinterpret_cast<const uint4*>(scl + (c.lane + 32 * g) * 16);
+            w[g] = r.x;
+            w[4 + g] = r.y;
+            w[8 + g] = r.z;
+            w[12 + g] = r.w;
+            sign |= r.x | r.y | r.z | r.w;
+          }
+          if (sign & 0x80808080u) atomicOr(sc.err, kErrNegativeScale);
+          tmem_st16(tbase + lane_addr + Shape::kColSfa + uint32_t(s) * 16u, w);
+          tmem_st_wait();
+        }
+        tc_fence_before();
+        __syncwarp();
+        if (c.lane == 0) mbar_arrive(&ctl.sready[s]);
+      }
+    };
     for (int i = 0; i < c.n; ++i) {
       const int u = c.u0 + i, tile = u / UPT, kc = u % UPT, t = i % T;
-      if (ok) ok = mbar_wait_or_abort(&ctl.done[t], uint32_t((i / T) & 1), abort, sc.err);
-      if (row == 0 && i == 0) G4_STAMP_T(sc, 5);
-      tc_fence_after();
-      if (!ok) {
-      } else if constexpr (!Shape::kFp4) {
-        float d[8];
-        tmem_ld8(tbase + lane_addr + uint32_t(t * kUmmaN), d);
-        tmem_ld_wait();
-        tc_fence_before();
-        __syncwarp();
-        if (c.lane == 0) mbar_arrive(&ctl.tempty[t]);
-        acc = fmaf(combine_terms<8>(d), gexp[c.bslot(kc) * 16], acc);
-      } else {
-        float d0[32], d1[32];
-        tmem_ld32(tbase + lane_addr + uint32_t(t * Shape::kSlotCols), d0);
-        tmem_ld32(tbase + lane_addr + uint32_t(t * Shape::kSlotCols + 32), d1);
-        ok = mbar_wait_or_abort(&ctl.sfull[t], uint32_t((i / T) & 1), abort, sc.err);
-        const uint4 sraw =
-            *reinterpret_cast<const uint4*>(smem + Shape::kOffScl + size_t(t) * Shape::kScaleBytes + row * 16);
-        tmem_ld_wait();
-        tc_fence_before();
-        __syncwarp();
-        if (c.lane == 0) mbar_arrive(&ctl.tempty[t]);
-        // block b of the unit: MMA b / 2, columns 4 (b % 2) .. 4 (b % 2) + 3 of its 8
-        const uint32_t sw[4] = {sraw.x, sraw.y, sraw.z, sraw.w};
-        const float* ge = gexp + c.bslot(kc) * 16;
-#pragma unroll
-        for (int b = 0; b < 8; ++b) {
-          const float2 sp = e4m3x2_to_f32x2(sw[b / 4] >> (16 * ((b / 2) % 2)));
-          acc = fmaf((b % 2) ? sp.y : sp.x, combine_terms<4>(d0 + (b / 2) * 8 + (b % 2) * 4) * ge[b], acc);
-        }
-#pragma unroll
-        for (int b = 8; b < 16; ++b) {
-          const float2 sp = e4m3x2_to_f32x2(sw[b / 4] >> (16 * ((b / 2) % 2)));
-          acc = fmaf((b % 2) ? sp.y : sp.x, combine_terms<4>(d1 + (b / 2 - 4) * 8 + (b % 2) * 4) * ge[b], acc);
-        }
-      }
+      const bool last = kc == UPT - 1 || i == c.n - 1;
       ++in_piece;
+      if constexpr (Shape::kFp4) {
+        if (i == 0 || kc == 0) ++piece;
+        if (!last) continue;
+        prepare(i + S < c.n ? i + S : c.n);  // keep the MMAs fed while this piece is finished
+        const int ds = piece % Shape::kDSlots;
+        if (ok) ok = mbar_wait_or_abort(&ctl.dfull[ds], uint32_t((piece / Shape::kDSlots) & 1), abort, sc.err);
+        if (row == 0 && piece == 0) G4_STAMP_T(sc, 5);
+        tc_fence_after();
+        float d[16];
+        if (ok) {
+          tmem_ld16(tbase + lane_addr + uint32_t(ds * 16), d);
+          tmem_ld_wait();
+        }
+        tc_fence_before();
+        __syncwarp();
+        if (c.lane == 0) mbar_arrive(&ctl.dempty[ds]);
+        if (ok) {
+          const int pc = ctl.pmax;
+          acc = mul_pow2(combine_digits8(d), pc - 20) + mul_pow2(combine_digits8(d + 8), pc - 35);
+          if (ctl.nonfinite) acc = __uint_as_float(0x7fc00000u);
+        }
+      } else {
+        if (ok) ok = mbar_wait_or_abort(&ctl.done[t], uint32_t((i / T) & 1), abort, sc.err);
+        if (row == 0 && i == 0) G4_STAMP_T(sc, 5);
+        tc_fence_after();
+        if (ok) {
+          float d[8];
+          tmem_ld8(tbase + lane_addr + uint32_t(t * 8), d);
+          tmem_ld_wait();
+          acc = fmaf(combine_terms<8>(d), gexp[c.bslot(kc) * 16], acc);
+        }
+        tc_fence_before();
+        __syncwarp();
+        if (c.lane == 0) mbar_arrive(&ctl.tempty[t]);
+        if (!last) continue;
+      }
 #ifdef G4_TRACE
       if (sc.trace && blockIdx.x == 0 && i < 64 && row == 0) sc.trace[3192 + i] = globaltimer_ns();
 #endif
-      if (kc == UPT - 1 || i == c.n - 1) {
-        const float v = acc;
-        if (in_piece == UPT) {
-          op.finalize_tile(tile, row, v, ctl);
+      const float val = acc;
+      if (in_piece == UPT) {
+        op.finalize_tile(tile, row, val, ctl);
+      } else {
+        // the tile's K range is split across CTAs: publish, the last to arrive adds them up
+        const int first = cta_of_unit(int64_t(tile) * UPT, grid, total);
+        const int lastc = cta_of_unit(int64_t(tile) * UPT + UPT - 1, grid, total);
+        float* part = sc.partials + size_t(tile) * kMaxCtasPerGroup * kTileRows;
+        if (lastc - first >= kMaxCtasPerGroup) {  // cannot happen for the shapes launched here
+          if (row == 0) atomicOr(sc.err, kErrInternal);
         } else {
-          // the tile's K range is split across CTAs: publish, the last to arrive adds them up
-          const int first = cta_of_unit(int64_t(tile) * UPT, grid, total);
-          const int last = cta_of_unit(int64_t(tile) * UPT + UPT - 1, grid, total);
-          float* part = sc.partials + size_t(tile) * kMaxCtasPerGroup * kTileRows;
-          if (last - first >= kMaxCtasPerGroup) {  // cannot happen for the shapes launched here
-            if (row == 0) atomicOr(sc.err, kErrInternal);
-          } else {
-            part[(blockIdx.x - first) * kTileRows + row] = v;
-            named_bar(kEpiBarrier, kEpiThreads);
-            if (row == 0) {
-              const uint32_t before = atomic_add_acq_rel_gpu(sc.counters + tile, uint32_t(in_piece));
-              const bool done = before + uint32_t(in_piece) == uint32_t(UPT);
-              if (done) sc.counters[tile] = 0;
-              ctl.bcast = done ? 1u : 0u;
-            }
-            __syncwarp();
-            named_bar(kEpiBarrier, kEpiThreads);
-            if (ctl.bcast) {
-              float tot = 0.f;
-              for (int cc = first; cc <= last; ++cc) tot += ld_cg_f32(part + (cc - first) * kTileRows + row);
-              op.finalize_tile(tile, row, tot, ctl);
-            }
+          part[(blockIdx.x - first) * kTileRows + row] = val;
+          named_bar(kEpiBarrier, kEpiThreads);
+          if (row == 0) {
+            const uint32_t before = atomic_add_acq_rel_gpu(sc.counters + tile, uint32_t(in_piece));
+            const bool done = before + uint32_t(in_piece) == uint32_t(UPT);
+            if (done) sc.counters[tile] = 0;
+            ctl.bcast = done ? 1u : 0u;
+          }
+          __syncwarp();
+          named_bar(kEpiBarrier, kEpiThreads);
+          if (ctl.bcast) {
+            float tot = 0.f;
+            for (int cc = first; cc <= lastc; ++cc) tot += ld_cg_f32(part + (cc - first) * kTileRows + row);
+            op.finalize_tile(tile, row, tot, ctl);
           }
         }
-        acc = 0.f;
-        in_piece = 0;
       }
+      acc = 0.f;
+      in_piece = 0;
     }
+    if constexpr (Shape::kFp4) prepare(c.n);
     if (row == 0) G4_STAMP_T(sc, 6);
   }
 

@@ -75,9 +75,6 @@ class TmapCache {
   // Row-major uint8 matrix [rows, cols] (fp8 codes, e4m3 scales), box {box_cols, box_rows}.
   cudaError_t u8(const void* base, uint64_t cols, uint64_t rows, uint32_t box_cols, uint32_t box_rows, bool swizzle128,
                  CUtensorMap* out);
-  // Row-major packed e2m1 matrix [rows, cols/2 bytes], loaded as 128-element boxes unpacked to a
-  // byte per code in shared memory (the layout tcgen05 kind::f8f6f4 reads), 128-byte swizzle.
-  cudaError_t fp4(const void* base, uint64_t cols, uint64_t rows, uint32_t box_rows, CUtensorMap* out);
 
  private:
   struct Entry {

@@ -22,8 +22,8 @@ namespace {
 // (launchers grow the grid if a smaller GPU would need more).
 using QkvShape = GemvShape<false, 6, kH / kUnitK, (kQs + 2 * kPs) / kTileRows, 8>;
 using OShape = GemvShape<false, 6, kQs / kUnitK, kH / kTileRows, 4>;
-using UpGateShape = GemvShape<true, 5, kH / kUnitK, kL / 64, 15>;  // tile = 64 up rows + 64 gate rows
-using DownShape = GemvShape<true, 5, kL / kUnitK, kH / kTileRows, 13>;
+using UpGateShape = GemvShape<true, 10, kH / kUnitK, kL / 64, 15>;  // tile = 64 up rows + 64 gate rows
+using DownShape = GemvShape<true, 10, kL / kUnitK, kH / kTileRows, 13>;
 
 __device__ __forceinline__ float gelu_tanh(float x) {
   // F.gelu(approximate="tanh"): 0.5 * x * (1 + tanh(sqrt(2/pi) * (x + 0.044715 * x^3)))
@@ -45,9 +45,10 @@ __device__ bool last_cta(uint32_t* counter) {
   return is_last != 0;
 }
 
-// Unit-tiled weights (g4_pack_tiles): pipeline unit u of a matrix is one contiguous block of
-// kUnitBox rows of 128 elements (both 128-element halves of its 128 rows, or of 64 up and 64 gate
-// rows), fetched by one 256-row TMA box; its block scales are one 128-row x 16-byte box.
+// Unit-tiled weights (g4_pack_tiles): pipeline unit u of a matrix is one contiguous block,
+// fetched by one TMA box: fp8, kUnitBox rows of 128 codes (both 128-element halves of its 128
+// rows); nvfp4, 128 rows of 128 bytes (64 up + 64 gate rows, or 128 down rows, each the unit's
+// 256 packed codes), its block scales one 2 KB block of the same 128 rows x 16 bytes.
 constexpr int kUnitBox = 2 * kTileRows;
 
 // Bring units [u0, u1) of a unit-tiled matrix (unit_bytes each) into L2 with one bulk prefetch.
@@ -92,7 +93,7 @@ __device__ __forceinline__ void rms_apply16(const uint4 (&raw)[4], float inv, fl
 // CTA, single pass (y is bf16 scratch written by other CTAs of this launch).
 template <int THREADS>
 __device__ void residual_epilogue(const uint16_t* y, const uint16_t* gamma, uint16_t* residual,
-                                  const uint16_t* layer_scalar, double* red) {
+                                  const uint16_t* layer_scalar, double* red, const Scratch& sc) {
   constexpr int VPT = (kH / 8 + THREADS - 1) / THREADS;
   float yv[VPT][8], gv[VPT][8], rv[VPT][8];
   load_bf16_vec<VPT>(y, kH, yv, true);
@@ -103,7 +104,9 @@ __device__ void residual_epilogue(const uint16_t* y, const uint16_t* gamma, uint
   for (int v = 0; v < VPT; ++v)
 #pragma unroll
     for (int j = 0; j < 8; ++j) ss += double(yv[v][j]) * double(yv[v][j]);
+  G4_STAMP(sc, 13);
   const float inv = rms_inverse(block_sum_d(ss, red), kH);
+  G4_STAMP(sc, 14);
   const float lam = layer_scalar ? bf16_to_f32(layer_scalar[0]) : 1.0f;
 #pragma unroll
   for (int v = 0; v < VPT; ++v) {
@@ -298,7 +301,8 @@ __global__ void __launch_bounds__(kGemvThreads, 1) o_kernel(const __grid_constan
   OOp op{&map, a, sc};
   gemv_run<OShape>(op, smem, sc);
   if (last_cta(sc.counters + kCtaCounter)) {
-    residual_epilogue<kGemvThreads>(sc.y, a.post_rms, a.residual, nullptr, red);
+    G4_STAMP(sc, 12);
+    residual_epilogue<kGemvThreads>(sc.y, a.post_rms, a.residual, nullptr, red, sc);
     if (threadIdx.x == 0) sc.counters[kCtaCounter] = 0;
   }
   G4_STAMP(sc, 8);
@@ -316,26 +320,25 @@ struct UpGateOp {
   FfnArgs a;
   Scratch sc;
   float g_up = 0.f, g_gate = 0.f;
-  uint32_t tx_bytes = 4 * 64 * 64;  // 256 rows x 64 bytes of packed e2m1 (one tiled box or four row-major)
+  uint32_t tx_bytes = UpGateShape::kABytes + UpGateShape::kScaleBytes;  // packed codes + block scales
   static constexpr bool kRms = true;
   static constexpr int kRmsGroups = kH / 16;
 
-  // stage: [K 0-127: up rows (8 KB) | gate rows (8 KB)] [K 128-255: same]
+  // stage: [64 up rows | 64 gate rows] x 128 bytes (the unit's 256 packed e2m1 codes per row)
   __device__ void load_unit(uint8_t* stage, int tile, int kc, uint64_t* bar, uint64_t policy) const {
     if (a.tiled) {  // up and gate rows interleaved in one buffer: one box per unit
-      tma_load_2d(stage, &maps->up, 0, (tile * UpGateShape::kUnitsPerTile + kc) * kUnitBox, bar, policy);
+      tma_load_2d(stage, &maps->up, 0, (tile * UpGateShape::kUnitsPerTile + kc) * kTileRows, bar, policy);
     } else {
-      const int x = kc * kUnitK;
-      tma_load_2d(stage, &maps->up, x, tile * 64, bar, policy);
-      tma_load_2d(stage + 8192, &maps->gate, x, tile * 64, bar, policy);
-      tma_load_2d(stage + 16384, &maps->up, x + 128, tile * 64, bar, policy);
-      tma_load_2d(stage + 24576, &maps->gate, x + 128, tile * 64, bar, policy);
+      tma_load_2d(stage, &maps->up, kc * 128, tile * 64, bar, policy);
+      tma_load_2d(stage + 8192, &maps->gate, kc * 128, tile * 64, bar, policy);
     }
   }
-  // block scales: [up rows | gate rows] x 16 bytes
+  // block scales [64 up rows | 64 gate rows] x 16 bytes: unit-tiled - one 2 KB block, one bulk
+  // copy; row-major - two boxes
   __device__ void load_scales(uint8_t* dst, int tile, int kc, uint64_t* bar, uint64_t policy) const {
     if (a.tiled) {
-      tma_load_2d(dst, &maps->up_s, 0, (tile * UpGateShape::kUnitsPerTile + kc) * kTileRows, bar, policy);
+      bulk_g2s(dst, a.up_scale + size_t(tile * UpGateShape::kUnitsPerTile + kc) * UpGateShape::kScaleBytes,
+               UpGateShape::kScaleBytes, bar, policy);
     } else {
       tma_load_2d(dst, &maps->up_s, kc * 16, tile * 64, bar, policy);
       tma_load_2d(dst + 1024, &maps->gate_s, kc * 16, tile * 64, bar, policy);
@@ -343,7 +346,7 @@ struct UpGateOp {
   }
   __device__ void prefetch_l2(int u0, int u1) const {
     if (!a.tiled) return;
-    prefetch_units(a.up_packed, u0, u1, UpGateShape::kABytes / 2);
+    prefetch_units(a.up_packed, u0, u1, UpGateShape::kABytes);
     prefetch_units(a.up_scale, u0, u1, UpGateShape::kScaleBytes);
   }
   __device__ void prologue(GemvCtl&) {
@@ -383,25 +386,28 @@ struct DownOp {
   FfnArgs a;
   Scratch sc;
   float g_down = 0.f;
-  uint32_t tx_bytes = 2 * 128 * 64;  // 256 rows x 64 bytes of packed e2m1
+  uint32_t tx_bytes = DownShape::kABytes + DownShape::kScaleBytes;
   static constexpr bool kRms = false;
   static constexpr int kRmsGroups = 0;
 
   __device__ void load_unit(uint8_t* stage, int tile, int kc, uint64_t* bar, uint64_t policy) const {
     if (a.tiled) {
-      tma_load_2d(stage, &maps->w, 0, (tile * DownShape::kUnitsPerTile + kc) * kUnitBox, bar, policy);
+      tma_load_2d(stage, &maps->w, 0, (tile * DownShape::kUnitsPerTile + kc) * kTileRows, bar, policy);
     } else {
-      tma_load_2d(stage, &maps->w, kc * kUnitK, tile * kTileRows, bar, policy);
-      tma_load_2d(stage + 16384, &maps->w, kc * kUnitK + 128, tile * kTileRows, bar, policy);
+      tma_load_2d(stage, &maps->w, kc * 128, tile * kTileRows, bar, policy);
     }
   }
   __device__ void load_scales(uint8_t* dst, int tile, int kc, uint64_t* bar, uint64_t policy) const {
-    const int y = a.tiled ? (tile * DownShape::kUnitsPerTile + kc) * kTileRows : tile * kTileRows;
-    tma_load_2d(dst, &maps->s, a.tiled ? 0 : kc * 16, y, bar, policy);
+    if (a.tiled) {
+      bulk_g2s(dst, a.down_scale + size_t(tile * DownShape::kUnitsPerTile + kc) * DownShape::kScaleBytes,
+               DownShape::kScaleBytes, bar, policy);
+    } else {
+      tma_load_2d(dst, &maps->s, kc * 16, tile * kTileRows, bar, policy);
+    }
   }
   __device__ void prefetch_l2(int u0, int u1) const {
     if (!a.tiled) return;
-    prefetch_units(a.down_packed, u0, u1, DownShape::kABytes / 2);
+    prefetch_units(a.down_packed, u0, u1, DownShape::kABytes);
     prefetch_units(a.down_scale, u0, u1, DownShape::kScaleBytes);
   }
   __device__ void prologue(GemvCtl&) { g_down = *a.down_global; }
@@ -422,7 +428,8 @@ __global__ void __launch_bounds__(kGemvThreads, 1) ffn_down_kernel(const __grid_
   DownOp op{&maps, a, sc};
   gemv_run<DownShape>(op, smem, sc);
   if (last_cta(sc.counters + kCtaCounter)) {
-    residual_epilogue<kGemvThreads>(sc.y, a.post_rms, a.residual, a.layer_scalar, red);
+    G4_STAMP(sc, 12);
+    residual_epilogue<kGemvThreads>(sc.y, a.post_rms, a.residual, a.layer_scalar, red, sc);
     if (threadIdx.x == 0) sc.counters[kCtaCounter] = 0;
   }
   G4_STAMP(sc, 8);
@@ -502,21 +509,24 @@ cudaError_t launch_ffn_nvfp4(const FfnArgs& a, const LaunchEnv& env) {
   DownMaps dn;
   cudaError_t e;
   if (a.tiled) {
-    // unit-tiled: up|gate codes interleaved [2 L * H / 128, 128 elements] (one 256-row box per
-    // unit), their scales [2 L * H / 256, 16 bytes]; down codes [H * L / 128, 128], scales
-    // [H * L / 256, 16]. gate_packed / gate_scale are not used (they live in the up buffers).
+    // unit-tiled: up|gate codes interleaved, one 128-row x 128-byte box per unit; down codes
+    // likewise. The block scales are read with bulk copies (no map). gate_packed / gate_scale
+    // are not used (they live in the up buffers).
     ug.gate = ug.up;
-    ug.gate_s = ug.up_s;
-    if ((e = env.maps->fp4(a.up_packed, 128, uint64_t(2) * kL * (kH / 128), kUnitBox, &ug.up))) return e;
-    if ((e = env.maps->u8(a.up_scale, 16, uint64_t(2) * kL * (kH / kUnitK), 16, kTileRows, false, &ug.up_s))) return e;
-    if ((e = env.maps->fp4(a.down_packed, 128, uint64_t(kH) * (kL / 128), kUnitBox, &dn.w))) return e;
-    if ((e = env.maps->u8(a.down_scale, 16, uint64_t(kH) * (kL / kUnitK), 16, kTileRows, false, &dn.s))) return e;
+    ug.gate_s = ug.up_s = ug.up;
+    dn.s = dn.w;
+    if ((e = env.maps->u8(a.up_packed, 128, uint64_t(kL) / 64 * (kH / kUnitK) * kTileRows, 128, kTileRows, true,
+                          &ug.up)))
+      return e;
+    if ((e = env.maps->u8(a.down_packed, 128, uint64_t(kH) / kTileRows * (kL / kUnitK) * kTileRows, 128, kTileRows,
+                          true, &dn.w)))
+      return e;
   } else {
-    if ((e = env.maps->fp4(a.up_packed, kH, kL, 64, &ug.up))) return e;
-    if ((e = env.maps->fp4(a.gate_packed, kH, kL, 64, &ug.gate))) return e;
+    if ((e = env.maps->u8(a.up_packed, kH / 2, kL, 128, 64, true, &ug.up))) return e;
+    if ((e = env.maps->u8(a.gate_packed, kH / 2, kL, 128, 64, true, &ug.gate))) return e;
     if ((e = env.maps->u8(a.up_scale, kH / 16, kL, 16, 64, false, &ug.up_s))) return e;
     if ((e = env.maps->u8(a.gate_scale, kH / 16, kL, 16, 64, false, &ug.gate_s))) return e;
-    if ((e = env.maps->fp4(a.down_packed, kL, kH, kTileRows, &dn.w))) return e;
+    if ((e = env.maps->u8(a.down_packed, kL / 2, kH, 128, kTileRows, true, &dn.w))) return e;
     if ((e = env.maps->u8(a.down_scale, kL / 16, kH, 16, kTileRows, false, &dn.s))) return e;
   }
   Scratch sc = env.sc;
@@ -622,25 +632,6 @@ cudaError_t TmapCache::u8(const void* base, uint64_t cols, uint64_t rows, uint32
   return cudaSuccess;
 }
 
-cudaError_t TmapCache::fp4(const void* base, uint64_t cols, uint64_t rows, uint32_t box_rows, CUtensorMap* out) {
-  const uint64_t key = (cols << 34) ^ (rows << 12) ^ (uint64_t(box_rows) << 1);
-  if (const CUtensorMap* m = find(base, key)) {
-    *out = *m;
-    return cudaSuccess;
-  }
-  auto enc = encode_fn();
-  if (!enc) return cudaErrorNotSupported;
-  const cuuint64_t gdim[2] = {cols, rows};
-  const cuuint64_t gstride[1] = {cols / 2};
-  const cuuint32_t box[2] = {128, box_rows};
-  const cuuint32_t estride[2] = {1, 1};
-  const CUresult r = enc(out, CU_TENSOR_MAP_DATA_TYPE_16U4_ALIGN16B, 2, const_cast<void*>(base), gdim, gstride, box,
-                         estride, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
-                         CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
-  if (r != CUDA_SUCCESS) return cudaErrorInvalidValue;
-  put(base, key, *out);
-  return cudaSuccess;
-}
 
 // ---------------------------------------------------------------------------------------
 // O projection on scratch the caller provides, with nothing cached or allocated

@@ -1,6 +1,7 @@
 // Blackwell (sm_100a) building blocks of the weight-streaming engine: TMA tensor-tile loads,
-// mbarriers with bounded waits, tcgen05 (TMEM allocation, kind::f8f6f4 MMA, commit, loads)
-// and the shared-memory matrix descriptors. No TMA multicast is used anywhere.
+// mbarriers with bounded waits, tcgen05 (TMEM allocation, kind::f8f6f4 and block-scaled
+// kind::mxf4nvf4 MMA, commit, TMEM loads and stores) and the shared-memory matrix descriptors.
+// No TMA multicast is used anywhere.
 #pragma once
 
 #include <cuda.h>
@@ -36,6 +37,18 @@ __device__ __forceinline__ bool mbar_wait_or_abort(uint64_t* bar, uint32_t parit
 // Named barrier among `count` threads (a multiple of 32) of the CTA.
 __device__ __forceinline__ void named_bar(int id, int count) {
   asm volatile("bar.sync %0, %1;" ::"r"(id), "r"(count) : "memory");
+}
+
+// Named barrier among `count` threads that also ORs a predicate over them: true in every
+// participant if any passed true. Whole warps only.
+__device__ __forceinline__ bool named_bar_or(int id, int count, bool pred) {
+  uint32_t r;
+  asm volatile(
+      "{\n .reg .pred pi, po;\n setp.ne.u32 pi, %1, 0;\n bar.red.or.pred po, %2, %3, pi;\n selp.u32 %0, 1, 0, po;\n}"
+      : "=r"(r)
+      : "r"(uint32_t(pred)), "r"(id), "r"(count)
+      : "memory");
+  return r != 0u;
 }
 
 // ---------------------------------------------------------------------------------------
@@ -99,6 +112,31 @@ __device__ __forceinline__ void tmem_ld32(uint32_t taddr, float (&v)[32]) {
 #pragma unroll
   for (int i = 0; i < 32; ++i) v[i] = __uint_as_float(r[i]);
 }
+__device__ __forceinline__ void tmem_ld16(uint32_t taddr, float (&v)[16]) {
+  uint32_t r[16];
+  asm volatile(
+      "tcgen05.ld.sync.aligned.32x32b.x16.b32 {%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15}, [%16];"
+      : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7]), "=r"(r[8]),
+        "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]), "=r"(r[15])
+      : "r"(taddr));
+#pragma unroll
+  for (int i = 0; i < 16; ++i) v[i] = __uint_as_float(r[i]);
+}
+// 32 lanes (this warp's quarter) x 16 consecutive columns from registers.
+__device__ __forceinline__ void tmem_st16(uint32_t taddr, const uint32_t (&v)[16]) {
+  asm volatile(
+      "tcgen05.st.sync.aligned.32x32b.x16.b32 [%0], {%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,%16};" ::"r"(
+          taddr),
+      "r"(v[0]), "r"(v[1]), "r"(v[2]), "r"(v[3]), "r"(v[4]), "r"(v[5]), "r"(v[6]), "r"(v[7]), "r"(v[8]), "r"(v[9]),
+      "r"(v[10]), "r"(v[11]), "r"(v[12]), "r"(v[13]), "r"(v[14]), "r"(v[15])
+      : "memory");
+}
+__device__ __forceinline__ void tmem_st4(uint32_t taddr, const uint32_t (&v)[4]) {
+  asm volatile("tcgen05.st.sync.aligned.32x32b.x4.b32 [%0], {%1,%2,%3,%4};" ::"r"(taddr), "r"(v[0]), "r"(v[1]), "r"(v[2]),
+               "r"(v[3])
+               : "memory");
+}
+__device__ __forceinline__ void tmem_st_wait() { asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory"); }
 __device__ __forceinline__ void tmem_ld_wait() { asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory"); }
 
 // ---------------------------------------------------------------------------------------
@@ -136,6 +174,23 @@ __device__ __forceinline__ void umma_f8f6f4(uint32_t tmem_d, uint64_t adesc, uin
       "{\n .reg .pred p;\n setp.ne.b32 p, %4, 0;\n"
       " tcgen05.mma.cta_group::1.kind::f8f6f4 [%0], %1, %2, %3, p;\n}\n" ::"r"(tmem_d),
       "l"(adesc), "l"(bdesc), "r"(idesc), "r"(accumulate)
+      : "memory");
+}
+
+// Instruction descriptor of tcgen05.mma kind::mxf4nvf4 with 16-element block scales (ue4m3):
+// A and B packed e2m1, f32 accumulate, both K-major, K = 64 per instruction.
+__host__ __device__ constexpr uint32_t umma_idesc_nvf4(int m, int n) {
+  return (1u << 7) | (1u << 10) | (uint32_t(n >> 3) << 17) | (uint32_t(m >> 4) << 24);
+}
+
+// D[tmem] (+)= (A . SFA)[smem] * (B . SFB)[smem]^T: every 16 K elements of a row of A (B) are
+// multiplied by that row's ue4m3 scale, read from TMEM at tsfa (tsfb). Issued by one thread.
+__device__ __forceinline__ void umma_nvf4(uint32_t tmem_d, uint64_t adesc, uint64_t bdesc, uint32_t idesc,
+                                          uint32_t tsfa, uint32_t tsfb, uint32_t accumulate) {
+  asm volatile(
+      "{\n .reg .pred p;\n setp.ne.b32 p, %4, 0;\n"
+      " tcgen05.mma.cta_group::1.kind::mxf4nvf4.block_scale.block16 [%0], %1, %2, %3, [%5], [%6], p;\n}\n" ::"r"(tmem_d),
+      "l"(adesc), "l"(bdesc), "r"(idesc), "r"(accumulate), "r"(tsfa), "r"(tsfb)
       : "memory");
 }
 
@@ -197,6 +252,70 @@ __device__ __forceinline__ void split_terms16(const float (&v)[16], uint4 (&t)[N
   }
 #pragma unroll
   for (int j = 0; j < NT; ++j) t[j] = make_uint4(w[j][0], w[j][1], w[j][2], w[j][3]);
+}
+
+// ---------------------------------------------------------------------------------------
+// Exact e2m1 digits of a bf16 activation (nvfp4 weights, kind::mxf4nvf4).
+//
+// An integer |X| < 2^22 is written with eight balanced base-8 digits: Y = X + 4 (8^8 - 1) / 7
+// is non-negative with base-8 digits e_i, and X = sum_i (e_i - 4) 8^i. Each digit d = e - 4 in
+// [-4, 3] is the e2m1 value d / 2 exactly, and the e2m1 code of d / 2 is |d| with the sign in
+// bit 3. The activation element v becomes X = RN(v 2^s) for a power of two chosen per exponent
+// class (the engine's B operand); the digits of 8 elements are built as nibble vectors.
+
+constexpr uint32_t kDigitBias = 0x924924u;  // 4 (8^8 - 1) / 7
+
+// x * 2^e for e in [-252, 254], in two exact power-of-two steps.
+__device__ __forceinline__ float mul_pow2(float x, int e) {
+  const int e1 = e / 2;
+  return (x * pow2f(e1)) * pow2f(e - e1);
+}
+
+// Exponent P with |v| < 2^(P+1) for the magnitude `amax`: at least -127 (subnormals and zero),
+// 128 for Inf / NaN.
+__device__ __forceinline__ int block_exponent(float amax) {
+  const int f = int((__float_as_uint(amax) >> 23) & 0xffu);
+  return f == 0 ? -127 : f - 127;
+}
+
+// The eight digit codes of Y = X + kDigitBias (< 2^24): nibble i holds the code of digit i.
+__device__ __forceinline__ uint32_t digit_codes8(uint32_t y) {
+  uint32_t e = (y & 0x000FFFu) | ((y & 0xFFF000u) << 4);  // 12-bit halves at bits 0 and 16
+  e = (e & 0x003F003Fu) | ((e & 0x0FC00FC0u) << 2);       // 6-bit quarters at bits 0, 8, 16, 24
+  e = (e & 0x07070707u) | ((e & 0x38383838u) << 1);       // digit e_i in nibble i
+  const uint32_t m = ((e >> 2) & 0x11111111u) * 0xFu;     // nibbles with e >= 4 (d >= 0)
+  return ((e ^ 0x44444444u) & m) | (((e ^ 0xFFFFFFFFu) - 0x33333333u) & ~m);  // d, or 8 | -d
+}
+
+// 8 x 8 nibble transpose: afterwards nibble k of w[i] is what nibble i of w[k] was.
+__device__ __forceinline__ void transpose8_nibbles(uint32_t (&w)[8]) {
+#pragma unroll
+  for (int k = 0; k < 4; ++k) {
+    const uint32_t a = w[k], b = w[k + 4];
+    w[k] = (a & 0x0000FFFFu) | (b << 16);
+    w[k + 4] = (a >> 16) | (b & 0xFFFF0000u);
+  }
+#pragma unroll
+  for (int q = 0; q < 4; ++q) {
+    const int k = (q / 2) * 4 + q % 2;  // 0, 1, 4, 5
+    const uint32_t a = w[k], b = w[k + 2];
+    w[k] = (a & 0x00FF00FFu) | ((b << 8) & 0xFF00FF00u);
+    w[k + 2] = ((a >> 8) & 0x00FF00FFu) | (b & 0xFF00FF00u);
+  }
+#pragma unroll
+  for (int k = 0; k < 8; k += 2) {
+    const uint32_t a = w[k], b = w[k + 1];
+    w[k] = (a & 0x0F0F0F0Fu) | ((b << 4) & 0xF0F0F0F0u);
+    w[k + 1] = ((a >> 4) & 0x0F0F0F0Fu) | (b & 0xF0F0F0F0u);
+  }
+}
+
+// sum_i d[i] 8^i, most significant digit first.
+__device__ __forceinline__ float combine_digits8(const float* d) {
+  float acc = d[7];
+#pragma unroll
+  for (int i = 6; i >= 0; --i) acc = fmaf(acc, 8.0f, d[i]);
+  return acc;
 }
 
 // sum_j d[j] 16^-j, smallest term first.

@@ -21,6 +21,7 @@ G4_ERR_UNSUPPORTED = -5
 DEVERR_KV_OFFSET = 1
 DEVERR_ROPE_OFFSET = 2
 DEVERR_WAIT_TIMEOUT = 4
+DEVERR_NEGATIVE_SCALE = 16
 
 _p = ctypes.c_void_p
 _i32 = ctypes.c_int32

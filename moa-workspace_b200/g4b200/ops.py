@@ -207,13 +207,14 @@ def decoder_feedforward_tiled(device: Device, residual_hbm, pre_ff_rms_weight, u
 
 
 # GPU-native (unit-tiled) layout of each weight matrix: (unit_bytes, tile_rows). A unit is the
-# 128 K elements of one tensor-memory-accelerator box (block scales: the 256 elements of one
-# pipeline step); the units of a tile of rows are contiguous in memory. The up and gate matrices
-# (codes and scales) are interleaved into one buffer by `pack_upgate`.
+# 256 K elements of a tile of rows (fp8: one tensor-memory-accelerator box of two 128-element
+# halves; nvfp4: 128 bytes of packed codes, or 16 block-scale bytes, per row); the units of a
+# tile are contiguous in memory. The up and gate matrices (codes and scales) are interleaved
+# into one buffer each by `pack_upgate`.
 TILING = {
     "q_weight": (128, 128), "k_weight": (128, 128), "v_weight": (128, 128), "o_weight": (128, 128),
-    "up_gate_weight": (64, 64), "up_gate_scale": (16, 64),
-    "down_weight_packed": (64, 128), "down_weight_scale": (16, 128),
+    "up_gate_weight": (128, 64), "up_gate_scale": (16, 64),
+    "down_weight_packed": (128, 128), "down_weight_scale": (16, 128),
 }
 
 
