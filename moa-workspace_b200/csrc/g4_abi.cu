@@ -116,7 +116,8 @@ g4_status g4_ctx_create(int device, g4_ctx** out) {
   const size_t off_partials = off_counters + g4::kCounterCount * sizeof(uint32_t);
   const size_t off_y = off_partials + g4::kPartialFloats * sizeof(float);
   const size_t off_act = off_y + g4::kYElems * sizeof(uint16_t);
-  const size_t off_trace = off_act + size_t(64) * g4::kL * sizeof(uint16_t);
+  const size_t off_ss = off_act + size_t(64) * g4::kL * sizeof(uint16_t);
+  const size_t off_trace = off_ss + size_t(g4::kTileSsCount) * sizeof(double);
 #ifdef G4_TRACE
   const size_t total = off_trace + size_t(65536 + 4096 * 32 * 8) * sizeof(uint64_t);
 #else
@@ -139,6 +140,7 @@ g4_status g4_ctx_create(int device, g4_ctx** out) {
   ctx->sc.partials = reinterpret_cast<float*>(base + off_partials);
   ctx->sc.y = reinterpret_cast<uint16_t*>(base + off_y);
   ctx->sc.act = reinterpret_cast<uint16_t*>(base + off_act);
+  ctx->sc.tile_ss = reinterpret_cast<double*>(base + off_ss);
 #ifdef G4_TRACE
   ctx->sc.trace = reinterpret_cast<uint64_t*>(base + off_trace);
 #else
@@ -373,7 +375,7 @@ g4_status g4_pack_tiles(g4_ctx* ctx, const uint8_t* src, const uint8_t* src2, ui
 
 namespace {
 
-// 192 KiB per device (the O op needs 147,200 bytes on a 148-SM B200). Zero when the module
+// 192 KiB per device (the O op needs 140,032 bytes on a 148-SM B200). Zero when the module
 // loads; the entry point zeroes the error word and the tickets again before every launch.
 constexpr size_t kStaticScratchBytes = size_t(192) << 10;
 constexpr int kStaticMaxDevices = 64;
@@ -431,7 +433,7 @@ g4_status g4_sliding_attention_output_noalloc(const uint16_t* x, const uint16_t*
 
   const size_t off_counters = g4::kScratchHeadBytes;
   const size_t off_partials = off_counters + size_t(g4::kCounterCount) * sizeof(uint32_t);
-  const size_t off_y = need - size_t(g4::kH) * sizeof(uint16_t);  // y is the last region
+  const size_t off_ss = need - size_t(g4::kTileSsCount) * sizeof(double);  // the last region
   g4::LaunchEnv env;
   env.device = dev;
   env.sm_count = sms;
@@ -440,11 +442,13 @@ g4_status g4_sliding_attention_output_noalloc(const uint16_t* x, const uint16_t*
   env.sc.err = reinterpret_cast<uint32_t*>(base);
   env.sc.counters = reinterpret_cast<uint32_t*>(base + off_counters);
   env.sc.partials = reinterpret_cast<float*>(base + off_partials);
-  env.sc.y = reinterpret_cast<uint16_t*>(base + off_y);
+  env.sc.y = nullptr;
   env.sc.act = nullptr;
+  env.sc.tile_ss = reinterpret_cast<double*>(base + off_ss);
   env.sc.trace = nullptr;
   env.maps = nullptr;
-  // the error word and every ticket must be zero when the kernel starts
+  // the error word and every ticket (the grid-barrier counter included) must be zero when the
+  // kernel starts
   if (cudaMemsetAsync(base, 0, off_partials, env.stream) != cudaSuccess) return G4_ERR_CUDA;
   const g4::OArgs a{x, post_attn_rms_weight, o_weight, o_weight_scale, residual_hbm, false};
   return g4::launch_o_uncached(a, env) == cudaSuccess ? G4_OK : G4_ERR_CUDA;

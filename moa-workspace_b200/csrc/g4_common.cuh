@@ -42,11 +42,14 @@ struct Scratch {
   float* partials;     // split-K partial row sums
   uint16_t* y;         // bf16 projected rows awaiting a grid-level epilogue
   uint16_t* act;       // bf16 GeGLU activation [M][L]
+  double* tile_ss;     // per output tile: sum of squares of its bf16 rows (kTileSsCount)
   uint64_t* trace;     // per-CTA phase timestamps (profiling builds only; null otherwise)
 };
+constexpr int kTileSsCount = 64;
 constexpr size_t kScratchHeadBytes = 256;  // the error word, padded to the scratch alignment
 constexpr int kCounterCount = 4096;
-constexpr int kCtaCounter = 4000;       // last-CTA ticket for whole-vector epilogues
+constexpr int kBarrierO = 4000;          // grid-barrier generation counters (multiples of the grid)
+constexpr int kBarrierDown = 4001;
 constexpr int kHeadCounterBase = 3968;  // 32 per-head tickets of the QKV op
 constexpr size_t kPartialFloats = size_t(1) << 21;  // 8 MiB of split-K partials
 constexpr size_t kYElems = 65536;
@@ -199,9 +202,26 @@ __device__ __forceinline__ uint32_t atomic_add_acq_rel_gpu(uint32_t* p, uint32_t
   return old;
 }
 __device__ __forceinline__ void fence_acq_rel_gpu() { asm volatile("fence.acq_rel.gpu;" ::: "memory"); }
+__device__ __forceinline__ uint32_t atomic_add_release_gpu(uint32_t* p, uint32_t v) {
+  uint32_t old;
+  asm volatile("atom.release.gpu.global.add.u32 %0, [%1], %2;" : "=r"(old) : "l"(p), "r"(v) : "memory");
+  return old;
+}
+__device__ __forceinline__ uint32_t ld_acquire_gpu(const uint32_t* p) {
+  uint32_t v;
+  asm volatile("ld.acquire.gpu.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
+  return v;
+}
 
 // L2-coherent loads for data other CTAs of the same launch wrote.
 __device__ __forceinline__ float ld_cg_f32(const float* p) { return __ldcg(p); }
+// 16 bytes global (L2) -> shared memory without a register round trip; wait with cp_async_wait_all.
+__device__ __forceinline__ void cp_async_16(void* smem_dst, const void* src) {
+  asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(smem_u32(smem_dst)), "l"(src) : "memory");
+}
+__device__ __forceinline__ void cp_async_wait_all() {
+  asm volatile("cp.async.commit_group;\n cp.async.wait_group 0;" ::: "memory");
+}
 __device__ __forceinline__ uint4 ld_cg_u4(const void* p) { return __ldcg(reinterpret_cast<const uint4*>(p)); }
 
 // Phase timestamps for profiling builds (-DG4_TRACE): thread 0 of each CTA records

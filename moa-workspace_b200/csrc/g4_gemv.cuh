@@ -43,12 +43,15 @@ constexpr int kTileRows = 128;
 constexpr int kEpiBarrier = 1;    // named barrier of the epilogue warps
 constexpr int kIssueBarrier = 2;  // named barrier of the MMA warp and the relay warp
 constexpr int kIssueThreads = 64;
+#ifndef G4_PREWAIT_UNITS
+#define G4_PREWAIT_UNITS 12  // at most the ring
+#endif
 
 template <bool FP4, int STAGES, int UPT, int TILES, int BSLOTS, int L2AHEAD = 6>
 struct GemvShape {
   static constexpr bool kFp4 = FP4;
   static constexpr int kStages = STAGES;
-  static constexpr int kPreWait = STAGES;  // units requested before the dependency wait
+  static constexpr int kPreWait = G4_PREWAIT_UNITS < STAGES ? G4_PREWAIT_UNITS : STAGES;  // before the dependency wait
   static constexpr int kL2Ahead = L2AHEAD;  // units requested into L2 beyond the shared-memory ring
   static constexpr int kUnitsPerTile = UPT;
   static constexpr int kTiles = TILES;
@@ -93,6 +96,7 @@ struct GemvCtl {
   int pmax;               // nvfp4: largest exponent of this CTA's activation
   uint32_t nonfinite;     // nvfp4: an activation of this CTA is Inf or NaN
   float xchg[64];
+  __align__(16) uint16_t out16[kTileRows];  // a tile's bf16 results, stored to global 16 bytes at a time
   double red_d[8];
   float red_f[8];
 };
@@ -163,11 +167,15 @@ __device__ __forceinline__ void nvf4_digit_rows8(const uint4& raw, int pc, uint3
 //   static bool kRms, int kRmsGroups   whether the activation is RMS-normalised over its
 //                                      kRmsGroups * 16 elements (every group is then loaded)
 //   void prologue(GemvCtl&)            scalar loads, after the wait on the preceding kernel
-//   void load_group(int g, uint4 (&raw)[4]) const   issue the loads of 16-element group g
-//                                      (bf16 input in raw[0..1], gamma in raw[2..3])
+//   void load_static(int g, uint4 (&raw)[4]) const  before the wait on the preceding kernel:
+//                                      issue the loads of group g's static inputs (gamma in raw[2..3])
+//   void load_group(int g, uint4 (&raw)[4]) const   issue the loads of 16-element group g of
+//                                      the activation (bf16, raw[0..1])
 //   void finish_group(const uint4 (&raw)[4], float inv, float (&v)[16]) const   the activation
 //                                      (bf16-exact values)
 //   void finalize_tile(int tile, int row, float v, GemvCtl&) const   all 128 epilogue threads
+//   static bool kOwnPieces             the op finishes every tile piece itself:
+//   void finish_piece(int tile, int row, float v, int units, GemvCtl&) const
 //   uint32_t tx_bytes                  bytes one unit delivers (codes and, nvfp4, block scales)
 template <class Shape, class Op>
 __device__ void gemv_run(Op& op, uint8_t* smem_raw, const Scratch& sc) {
@@ -222,57 +230,104 @@ __device__ void gemv_run(Op& op, uint8_t* smem_raw, const Scratch& sc) {
   const uint64_t policy = l2_evict_first_policy();
   const int prefetch = c.n < S ? c.n : S;
   const int prewait = prefetch < Shape::kPreWait ? prefetch : Shape::kPreWait;
-  auto request = [&](int i0, int i1) {  // units [i0, i1) into their (free) stages
-    for (int i = i0; i < i1; ++i) {
+  // units [i0, i1) into their (free) stages, thread i0 + k of the CTA issuing unit i0 + k: each
+  // TMA issue costs its thread tens of nanoseconds, so a single thread would stall the prologue.
+  auto request = [&](int i0, int i1) {
+    const int i = i0 + c.tid;
+    if (i < i1) {
       const int u = c.u0 + i;
       mbar_arrive_expect_tx(&ctl.full[i], op.tx_bytes);
       op.load_unit(c.stage(i), u / UPT, u % UPT, &ctl.full[i], policy);
       if constexpr (Shape::kFp4) op.load_scales(c.stage(i) + Shape::kABytes, u / UPT, u % UPT, &ctl.full[i], policy);
     }
   };
-  if (c.tid == 0) request(0, prewait);
+  request(0, prewait);
   __syncwarp();  // CTA barriers below need converged warps
+
+  // Epilogue warps (2-5): their lane quarter of TMEM, a flag that turns their later work into
+  // no-ops after a failed wait (their loops keep their shape for the named barriers), and for
+  // nvfp4 weights the copy of block scales of units [prep, lim) from the stages into TMEM, in
+  // unit order. Row m's 16 scale bytes hold MMA j's 4 scales at bytes 4j..4j+3; this lane
+  // writes rows lane + 32 g (g = 0..3) to columns 4j + g of its lane quarter.
+  const uint32_t lane_addr = uint32_t((c.warp & 3) * 32) << 16;
+  bool ok = true;
+  int prep = 0;
+  auto prepare = [&](int lim) {
+    for (; prep < lim; ++prep) {
+      const int s = prep % S;
+      if (ok) ok = mbar_wait_or_abort(&ctl.full[s], uint32_t((prep / S) & 1), abort, sc.err);
+      if (ok) {
+        const uint8_t* scl = c.stage(s) + Shape::kABytes;
+        uint32_t w[16];
+        uint32_t sign = 0u;
+#pragma unroll
+        for (int g = 0; g < 4; ++g) {
+          const uint4 r = *reinterpret_cast<const uint4*>(scl + (c.lane + 32 * g) * 16);
+          w[g] = r.x;
+          w[4 + g] = r.y;
+          w[8 + g] = r.z;
+          w[12 + g] = r.w;
+          sign |= r.x | r.y | r.z | r.w;
+        }
+        if (sign & 0x80808080u) atomicOr(sc.err, kErrNegativeScale);
+        tmem_st16(tbase + lane_addr + Shape::kColSfa + uint32_t(s) * 16u, w);
+        tmem_st_wait();
+      }
+      tc_fence_before();
+      __syncwarp();
+      if (c.lane == 0) mbar_arrive(&ctl.sready[s]);
+    }
+  };
   if constexpr (Shape::kFp4) {
-    // B block scales (1.0 for every block) and the first units' A scales into TMEM meanwhile
+    // B block scales (1.0 for every block) and the first units' A scales into TMEM while the
+    // preceding kernel finishes
     if (c.warp >= 2 && c.warp < 6) {
       const uint32_t one[4] = {0x38383838u, 0x38383838u, 0x38383838u, 0x38383838u};
-      tmem_st4(tbase + (uint32_t((c.warp & 3) * 32) << 16) + Shape::kColSfb, one);
+      tmem_st4(tbase + lane_addr + Shape::kColSfb, one);
       tmem_st_wait();
+      prepare(prewait < 2 ? prewait : 2);
     }
+  }
+  // activation -> B operand (only the K units this CTA touches). Every global load of the
+  // prologue is issued before any is used; the normalisation weights (static) before the wait
+  // on the preceding kernel, its output right after it.
+  float* gexp = reinterpret_cast<float*>(smem + Shape::kOffExp);  // fp8: [slot][group] 2^-E
+  uint16_t* hsm = reinterpret_cast<uint16_t*>(smem + Shape::kOffH);  // nvfp4: [slot][256] bf16
+  constexpr int MAXG = 2;  // 16-element groups per thread
+  static_assert(!Op::kRms || Op::kRmsGroups <= MAXG * kGemvThreads, "RMS statistic: too many groups");
+  static_assert(Shape::kBSlots * 16 <= MAXG * kGemvThreads, "B slots: too many groups");
+  int grp[MAXG];
+  bool have[MAXG];
+  uint4 raw[MAXG][4];
+#pragma unroll
+  for (int q = 0; q < MAXG; ++q) {
+    const int j = c.tid + q * kGemvThreads;
+    if constexpr (Op::kRms) {  // the RMS statistic needs the whole vector
+      grp[q] = j;
+      have[q] = j < Op::kRmsGroups;
+    } else {  // only the groups of this CTA's K units
+      grp[q] = ((c.c0 + j / 16) % UPT) * 16 + j % 16;
+      have[q] = j < nslots * 16;
+    }
+    if (have[q]) op.load_static(grp[q], raw[q]);
   }
   pdl_wait_primary();
   pdl_launch_dependents();
   G4_STAMP(sc, 1);
-
-  // activation -> B operand (only the K units this CTA touches). Every global load of the
-  // prologue is issued before any is used: one round trip while the weight tiles stream in.
-  float* gexp = reinterpret_cast<float*>(smem + Shape::kOffExp);  // fp8: [slot][group] 2^-E
-  uint16_t* hsm = reinterpret_cast<uint16_t*>(smem + Shape::kOffH);  // nvfp4: [slot][256] bf16
   {
-    constexpr int MAXG = 2;  // 16-element groups per thread
-    static_assert(!Op::kRms || Op::kRmsGroups <= MAXG * kGemvThreads, "RMS statistic: too many groups");
-    static_assert(Shape::kBSlots * 16 <= MAXG * kGemvThreads, "B slots: too many groups");
     op.prologue(ctl);  // scalar loads only
-    int grp[MAXG];
-    bool have[MAXG];
-    uint4 raw[MAXG][4];
 #pragma unroll
-    for (int q = 0; q < MAXG; ++q) {
-      const int j = c.tid + q * kGemvThreads;
-      if constexpr (Op::kRms) {  // the RMS statistic needs the whole vector
-        grp[q] = j;
-        have[q] = j < Op::kRmsGroups;
-      } else {  // only the groups of this CTA's K units
-        grp[q] = ((c.c0 + j / 16) % UPT) * 16 + j % 16;
-        have[q] = j < nslots * 16;
-      }
+    for (int q = 0; q < MAXG; ++q)
       if (have[q]) op.load_group(grp[q], raw[q]);
-    }
-    if (c.tid == 0) {
+    // The rest of the ring (and the L2 prefetch beyond it) is requested once the issuing
+    // thread's activation loads have landed: issued earlier, the weight data queued for this SM
+    // delays the activation's return by microseconds.
+    auto request_rest = [&]() {
       request(prewait, prefetch);
       // the next units go to L2 only: the ring's loads then hit L2 instead of waiting on HBM
-      op.prefetch_l2(c.u0 + prefetch, c.u0 + (prefetch + Shape::kL2Ahead < c.n ? prefetch + Shape::kL2Ahead : c.n));
-    }
+      if (c.tid == kGemvThreads - 1)
+        op.prefetch_l2(c.u0 + prefetch, c.u0 + (prefetch + Shape::kL2Ahead < c.n ? prefetch + Shape::kL2Ahead : c.n));
+    };
     float inv = 0.f;
     G4_STAMP(sc, 9);
     if constexpr (Op::kRms) {
@@ -280,7 +335,10 @@ __device__ void gemv_run(Op& op, uint8_t* smem_raw, const Scratch& sc) {
 #pragma unroll
       for (int q = 0; q < MAXG; ++q)
         if (have[q]) ss += sum_squares_bf16x16(raw[q][0], raw[q][1]);
+      request_rest();
+      G4_STAMP(sc, 12);
       inv = rms_inverse(block_sum_d(ss, ctl.red_d), Op::kRmsGroups * 16);
+      G4_STAMP(sc, 13);
     }
     float v[MAXG][16];
     int slot[MAXG];
@@ -313,6 +371,7 @@ __device__ void gemv_run(Op& op, uint8_t* smem_raw, const Scratch& sc) {
         }
       }
     }
+    if constexpr (!Op::kRms) request_rest();
     __syncthreads();
     G4_STAMP(sc, 10);
     if constexpr (Shape::kFp4) {
@@ -469,40 +528,8 @@ __device__ void gemv_run(Op& op, uint8_t* smem_raw, const Scratch& sc) {
     // ---------------------------------------------------------------- epilogue (warps 2-5)
     const int quarter = c.warp & 3;
     const int row = quarter * 32 + c.lane;
-    const uint32_t lane_addr = uint32_t(quarter * 32) << 16;
     float acc = 0.f;
     int in_piece = 0, piece = -1;
-    bool ok = true;  // after a failed wait the loop keeps its shape (named barriers) but skips work
-    // nvfp4: block scales of units [prep, lim) from the stage into TMEM, in unit order. Row m's
-    // 16 scale bytes hold MMA j's 4 scales at bytes 4j..4j+3; this lane writes rows
-    // lane + 32 g (g = 0..3) to columns 4j + g of its lane quarter.
-    int prep = 0;
-    auto prepare = [&](int lim) {
-      for (; prep < lim; ++prep) {
-        const int s = prep % S;
-        if (ok) ok = mbar_wait_or_abort(&ctl.full[s], uint32_t((prep / S) & 1), abort, sc.err);
-        if (ok) {
-          const uint8_t* scl = c.stage(s) + Shape::kABytes;
-          uint32_t w[16];
-          uint32_t sign = 0u;
-#pragma unroll
-          for (int g = 0; g < 4; ++g) {
-            const uint4 r = *reinterpret_cast<const uint4*>(scl + (c.lane + 32 * g) * 16);
-            w[g] = r.x;
-            w[4 + g] = r.y;
-            w[8 + g] = r.z;
-            w[12 + g] = r.w;
-            sign |= r.x | r.y | r.z | r.w;
-          }
-          if (sign & 0x80808080u) atomicOr(sc.err, kErrNegativeScale);
-          tmem_st16(tbase + lane_addr + Shape::kColSfa + uint32_t(s) * 16u, w);
-          tmem_st_wait();
-        }
-        tc_fence_before();
-        __syncwarp();
-        if (c.lane == 0) mbar_arrive(&ctl.sready[s]);
-      }
-    };
     for (int i = 0; i < c.n; ++i) {
       const int u = c.u0 + i, tile = u / UPT, kc = u % UPT, t = i % T;
       const bool last = kc == UPT - 1 || i == c.n - 1;
@@ -547,7 +574,9 @@ __device__ void gemv_run(Op& op, uint8_t* smem_raw, const Scratch& sc) {
       if (sc.trace && blockIdx.x == 0 && i < 64 && row == 0) sc.trace[3192 + i] = globaltimer_ns();
 #endif
       const float val = acc;
-      if (in_piece == UPT) {
+      if constexpr (Op::kOwnPieces) {
+        op.finish_piece(tile, row, val, in_piece, ctl);
+      } else if (in_piece == UPT) {
         op.finalize_tile(tile, row, val, ctl);
       } else {
         // the tile's K range is split across CTAs: publish, the last to arrive adds them up

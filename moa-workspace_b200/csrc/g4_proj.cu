@@ -32,19 +32,6 @@ __device__ __forceinline__ float gelu_tanh(float x) {
   return 0.5f * x * (1.0f + tanhf(inner));
 }
 
-// Last-CTA ticket: returns true in every thread of the CTA that finished last.
-__device__ bool last_cta(uint32_t* counter) {
-  __shared__ uint32_t is_last;
-  __syncthreads();  // every thread's stores of this CTA precede the release below
-  if (threadIdx.x == 0) {
-    const uint32_t before = atomic_add_acq_rel_gpu(counter, 1u);
-    is_last = (before == gridDim.x - 1) ? 1u : 0u;
-  }
-  __syncwarp();
-  __syncthreads();  // ... and the acquire precedes every thread's loads after it
-  return is_last != 0;
-}
-
 // Unit-tiled weights (g4_pack_tiles): pipeline unit u of a matrix is one contiguous block,
 // fetched by one TMA box: fp8, kUnitBox rows of 128 codes (both 128-element halves of its 128
 // rows); nvfp4, 128 rows of 128 bytes (64 up + 64 gate rows, or 128 down rows, each the unit's
@@ -89,112 +76,110 @@ __device__ __forceinline__ void rms_apply16(const uint4 (&raw)[4], float inv, fl
   for (int j = 0; j < 16; ++j) v[j] = bf16_round((v[j] * inv) * g[j]);
 }
 
-// residual <- bf16(residual + RMSNorm_gamma(y)) [then bf16(. * layer_scalar)], H elements, whole
-// CTA, single pass (y is bf16 scratch written by other CTAs of this launch).
-template <int THREADS>
-__device__ void residual_epilogue(const uint16_t* y, const uint16_t* gamma, uint16_t* residual,
-                                  const uint16_t* layer_scalar, double* red, const Scratch& sc) {
-  constexpr int VPT = (kH / 8 + THREADS - 1) / THREADS;
-  float yv[VPT][8], gv[VPT][8], rv[VPT][8];
-  load_bf16_vec<VPT>(y, kH, yv, true);
-  load_bf16_vec<VPT>(gamma, kH, gv, false);
-  load_bf16_vec<VPT>(residual, kH, rv, true);
-  double ss = 0.0;
-#pragma unroll
-  for (int v = 0; v < VPT; ++v)
-#pragma unroll
-    for (int j = 0; j < 8; ++j) ss += double(yv[v][j]) * double(yv[v][j]);
-  G4_STAMP(sc, 13);
-  const float inv = rms_inverse(block_sum_d(ss, red), kH);
-  G4_STAMP(sc, 14);
+// ---------------------------------------------------------------------------------------
+// Post-RMSNorm + residual (O and FFN down): residual <- bf16(residual + RMSNorm_gamma(y)) [then
+// bf16(. * layer_scalar)] over the H outputs. The statistic needs every output, so each CTA that
+// finishes a tile keeps its 128 values of y in shared memory and publishes their sum of squares;
+// after a grid-wide barrier every CTA reads the 30 sums (fixed order) and updates its own rows.
+// The barrier is safe because the grid has one CTA per SM and all of them become resident
+// (the next kernel cannot take an SM before this one's CTAs have all started); its wait is
+// bounded.
+
+constexpr int kMaxFinTiles = 4;  // tiles one CTA can finish (it overlaps at most 3 here)
+
+struct ResidualTail {
+  float y[kMaxFinTiles][kTileRows];                     // the finished tiles' outputs (bf16 values)
+  __align__(16) uint16_t gamma[kMaxFinTiles][kTileRows];  // their post-RMSNorm weights
+  __align__(16) uint16_t res[kMaxFinTiles][kTileRows];    // and residual rows (copied asynchronously)
+  int tile[kMaxFinTiles];
+  int n;
+  double red[4];
+  double ss[kTileSsCount];
+};
+
+// Called by the 128 epilogue threads when a tile is final: record it and publish its sum of
+// squares (f64, rows in order over the four warps).
+__device__ void tail_record(ResidualTail& t, const uint16_t* gamma, const uint16_t* residual, const Scratch& sc,
+                            int tile, int row, float y) {
+  const int f = t.n;
+  t.y[f][row] = y;
+  if (row < 16) {  // 16 x 16 bytes each, in flight while the kernel goes on
+    cp_async_16(&t.gamma[f][row * 8], gamma + tile * kTileRows + row * 8);
+    cp_async_16(&t.res[f][row * 8], residual + tile * kTileRows + row * 8);
+  }
+  double ss = warp_sum_d(double(y) * double(y));
+  if ((threadIdx.x & 31) == 0) t.red[row / 32] = ss;
+  named_bar(kEpiBarrier, kEpiThreads);
+  if (row == 0) {
+    sc.tile_ss[tile] = ((t.red[0] + t.red[1]) + t.red[2]) + t.red[3];
+    t.tile[f] = tile;
+    t.n = f + 1;
+  }
+  named_bar(kEpiBarrier, kEpiThreads);
+}
+
+// Whole CTA, after gemv_run: the grid barrier, then the update of the recorded rows.
+__device__ void tail_update(ResidualTail& t, uint16_t* residual, const Scratch& sc, uint32_t* barrier, int tiles,
+                            const uint16_t* layer_scalar) {
   const float lam = layer_scalar ? bf16_to_f32(layer_scalar[0]) : 1.0f;
-#pragma unroll
-  for (int v = 0; v < VPT; ++v) {
-    const int base = (threadIdx.x + v * blockDim.x) * 8;
-    if (base < kH) {
-      __align__(16) uint16_t out[8];
-#pragma unroll
-      for (int j = 0; j < 8; ++j) {
-        const float nrm = bf16_round((yv[v][j] * inv) * gv[v][j]);
-        float r = bf16_round(rv[v][j] + nrm);
-        if (layer_scalar) r = bf16_round(r * lam);
-        out[j] = f32_to_bf16(r);
+  cp_async_wait_all();
+  __syncthreads();  // every record (and tile_ss store) of this CTA precedes the arrival
+  if (threadIdx.x == 0) {
+    const uint32_t old = atomic_add_release_gpu(barrier, 1u);
+    const uint32_t target = old - old % gridDim.x + gridDim.x;
+    const uint64_t t0 = globaltimer_ns();
+    while (int32_t(ld_acquire_gpu(barrier) - target) < 0) {
+      if (globaltimer_ns() - t0 > kWaitLimitNs) {
+        atomicOr(sc.err, kErrWaitTimeout);
+        break;
       }
-      *reinterpret_cast<uint4*>(residual + base) = *reinterpret_cast<const uint4*>(out);
+      __nanosleep(32);
     }
   }
+  __syncthreads();
+  G4_STAMP(sc, 12);
+  if (threadIdx.x < tiles) t.ss[threadIdx.x] = __ldcg(sc.tile_ss + threadIdx.x);
+  __syncthreads();
+  double sum = 0.0;
+  for (int i = 0; i < tiles; ++i) sum += t.ss[i];  // fixed order: identical in every CTA
+  const float inv = rms_inverse(sum, kH);
+  const int e = threadIdx.x - 64;  // the epilogue threads own the recorded rows
+  if (e >= 0 && e < kEpiThreads) {
+    for (int f = 0; f < t.n; ++f) {
+      const float nrm = bf16_round((t.y[f][e] * inv) * bf16_to_f32(t.gamma[f][e]));
+      float r = bf16_round(bf16_to_f32(t.res[f][e]) + nrm);
+      if (layer_scalar) r = bf16_round(r * lam);
+      t.res[f][e] = f32_to_bf16(r);  // in place, then whole 16-byte stores (the next kernel reads
+    }                                // sectors written in 2-byte pieces slowly)
+  }
+  __syncthreads();
+  if (threadIdx.x < 16 * t.n) {
+    const int f = threadIdx.x / 16, q = threadIdx.x % 16;
+    reinterpret_cast<uint4*>(residual + t.tile[f] * kTileRows)[q] = reinterpret_cast<const uint4*>(t.res[f])[q];
+  }
+  G4_STAMP(sc, 13);
 }
 
 // ---------------------------------------------------------------------------------------
 // QKV
 
-// Per-head RMSNorm (+ RoPE for q and k) of one projected head and its store: q_out, or the
-// addressed ring slot of the K / V cache. One warp, eight elements per lane.
-__device__ void qkv_head_epilogue(const QkvArgs& a, const Scratch& sc, int head) {
-  const int lane = threadIdx.x & 31;
-  const int base = head * kDs;
-  const uint4 raw = ld_cg_u4(sc.y + base + lane * 8);
-  const uint16_t* yb = reinterpret_cast<const uint16_t*>(&raw);
-  const bool is_q = head < kNs * kGs, is_k = !is_q && head < kNs * kGs + kNs;
-  const uint16_t* gamma = is_q ? a.q_rms : (is_k ? a.k_rms : nullptr);
-  uint4 graw = make_uint4(0, 0, 0, 0);
-  if (gamma) graw = *reinterpret_cast<const uint4*>(gamma + lane * 8);
-  const uint16_t* gb = reinterpret_cast<const uint16_t*>(&graw);
-  const int kv = *a.kv_offset, rope = *a.rope_offset;
-  const bool kv_ok = kv >= 0 && (kv % (kPs * 2)) == 0 && kv / (kPs * 2) < a.ring_len;
-  const bool rope_ok = rope >= 0 && (rope % (kDs * 2)) == 0 && rope / (kDs * 2) < a.rope_rows;
-  if (!kv_ok || !rope_ok) {
-    if (lane == 0) atomicOr(sc.err, (kv_ok ? 0u : kErrKvOffset) | (rope_ok ? 0u : kErrRopeOffset));
-    return;
-  }
-  const int slot = kv / (kPs * 2), row = rope / (kDs * 2);
-  uint4 craw = make_uint4(0, 0, 0, 0), sraw = make_uint4(0, 0, 0, 0);
-  if (is_q || is_k) {
-    craw = *reinterpret_cast<const uint4*>(a.cos + size_t(row) * kDs + lane * 8);
-    sraw = *reinterpret_cast<const uint4*>(a.sin + size_t(row) * kDs + lane * 8);
-  }
-  float y[8];
-  double ss = 0.0;
-#pragma unroll
-  for (int j = 0; j < 8; ++j) {
-    y[j] = bf16_to_f32(yb[j]);
-    ss += double(y[j]) * double(y[j]);
-  }
-  ss = warp_sum_d(ss);
-  const float inv = rms_inverse(ss, kDs);
-  float nrm[8];
-#pragma unroll
-  for (int j = 0; j < 8; ++j) {
-    const float s = y[j] * inv;
-    nrm[j] = gamma ? bf16_round(s * bf16_to_f32(gb[j])) : bf16_round(s);
-  }
-  __align__(16) uint16_t outb[8];
-  if (is_q || is_k) {
-    // RoPE, half-swap form with the low half of `sin` pre-negated by the caller:
-    // out[i] = bf16(bf16(n[i] cos[i]) + bf16(n[i ^ 128] sin'[i])). Element i ^ 128 lives in
-    // lane ^ 16.
-    const uint16_t* cb = reinterpret_cast<const uint16_t*>(&craw);
-    const uint16_t* sb = reinterpret_cast<const uint16_t*>(&sraw);
-#pragma unroll
-    for (int j = 0; j < 8; ++j) {
-      const float partner = __shfl_xor_sync(0xffffffffu, nrm[j], 16);
-      const float c = bf16_round(nrm[j] * bf16_to_f32(cb[j]));
-      const float s = bf16_round(partner * bf16_to_f32(sb[j]));
-      outb[j] = f32_to_bf16(c + s);
-    }
-  } else {
-#pragma unroll
-    for (int j = 0; j < 8; ++j) outb[j] = f32_to_bf16(nrm[j]);
-  }
-  uint16_t* dst;
-  if (is_q)
-    dst = a.q_out + base + lane * 8;
-  else if (is_k)
-    dst = a.k_cache + size_t(slot) * kPs + (head - kNs * kGs) * kDs + lane * 8;
-  else
-    dst = a.v_cache + size_t(slot) * kPs + (head - kNs * kGs - kNs) * kDs + lane * 8;
-  *reinterpret_cast<uint4*>(dst) = *reinterpret_cast<const uint4*>(outb);
-}
+// Per-head RMSNorm (+ RoPE for q and k) and the store of one head (q_out, or the addressed ring
+// slot of the K / V cache). A head is 256 projected rows = two tiles; every CTA that computes a
+// piece of either tile publishes its partial row sums and adds its unit count to the head's
+// ticket, and the CTA that completes the 30 units sums the pieces (in CTA order) and finishes
+// the head with its 128 epilogue threads: thread e owns head elements e and e + 128, which are
+// exactly the two elements RoPE's half swap pairs.
+
+struct QkvStatic {  // per CTA, loaded while the weights stream in
+  __align__(16) uint16_t cos[kDs];
+  __align__(16) uint16_t sin[kDs];
+  __align__(16) uint16_t qg[kDs];
+  __align__(16) uint16_t kg[kDs];
+  __align__(16) uint16_t out[kDs];
+  double red[4];
+  int slot, row;
+  bool kv_ok, rope_ok;
+};
 
 struct QkvMaps {
   CUtensorMap q, k, v;
@@ -228,37 +213,129 @@ struct QkvOp {
     prefetch_units(a.k_weight, (u0 > kQU ? u0 : kQU) - kQU, (u1 < kQU + kKU ? u1 : kQU + kKU) - kQU, kB);
     prefetch_units(a.v_weight, (u0 > kQU + kKU ? u0 : kQU + kKU) - kQU - kKU, u1 - kQU - kKU, kB);
   }
-  __device__ void prologue(GemvCtl&) {}
-  __device__ void load_group(int g, uint4 (&raw)[4]) const {
-    load_group_cg(a.x, g, raw);
-    load_group_gamma(a.input_rms, g, raw);
+  static constexpr bool kOwnPieces = true;
+  QkvStatic* st;
+
+  // the position offsets (device-resident, written before the call), then the RoPE row and the
+  // per-head norm weights into shared memory, asynchronously (the epilogue threads wait for them)
+  __device__ void prologue(GemvCtl&) {
+    const int kv = *a.kv_offset, rope = *a.rope_offset;
+    const bool kv_ok = kv >= 0 && (kv % (kPs * 2)) == 0 && kv / (kPs * 2) < a.ring_len;
+    const bool rope_ok = rope >= 0 && (rope % (kDs * 2)) == 0 && rope / (kDs * 2) < a.rope_rows;
+    const int e = threadIdx.x - 64;
+    if (e == 0) {
+      st->kv_ok = kv_ok;
+      st->rope_ok = rope_ok;
+      st->slot = kv / (kPs * 2);
+      st->row = rope / (kDs * 2);
+    }
+    if (e >= 0 && e < 32) {  // 32 x 16 bytes per 256-element row
+      const int q = e;
+      if (rope_ok) {
+        const size_t row = size_t(rope / (kDs * 2)) * kDs;
+        cp_async_16(st->cos + q * 8, a.cos + row + q * 8);
+        cp_async_16(st->sin + q * 8, a.sin + row + q * 8);
+      }
+      cp_async_16(st->qg + q * 8, a.q_rms + q * 8);
+      cp_async_16(st->kg + q * 8, a.k_rms + q * 8);
+    }
   }
-  __device__ void finish_group(const uint4 (&raw)[4], float inv, float (&v)[16]) const { rms_apply16(raw, inv, v); }
-  __device__ void finalize_tile(int tile, int row, float v, GemvCtl& ctl) const {
-    const int r = tile * kTileRows + row;
-    const uint16_t sb = r < kQs ? a.q_scale[r] : (r < kQs + kPs ? a.k_scale[r - kQs] : a.v_scale[r - kQs - kPs]);
-    // scaled_projection: bf16((x @ codes.T) * scale) (generate_references.py:265-274)
-    sc.y[r] = f32_to_bf16(v * bf16_to_f32(sb));
+
+  __device__ void finish_piece(int tile, int row, float v, int in_piece, GemvCtl& ctl) const {
+    constexpr int UPT = QkvShape::kUnitsPerTile;
+    const int64_t grid = gridDim.x, total = QkvShape::kTotalUnits;
+    const int first = cta_of_unit(int64_t(tile) * UPT, grid, total);
+    sc.partials[size_t(tile) * kMaxCtasPerGroup * kTileRows + (blockIdx.x - first) * kTileRows + row] = v;
     named_bar(kEpiBarrier, kEpiThreads);
-    const int head = r / kDs;  // two tiles per head
+    const int head = tile / 2;
     if (row == 0) {
-      const uint32_t before = atomic_add_acq_rel_gpu(sc.counters + kHeadCounterBase + head, 1u);
-      const bool done = before == uint32_t(kDs / kTileRows - 1);
+      const uint32_t before = atomic_add_acq_rel_gpu(sc.counters + kHeadCounterBase + head, uint32_t(in_piece));
+      const bool done = before + uint32_t(in_piece) == uint32_t(2 * UPT);
       if (done) sc.counters[kHeadCounterBase + head] = 0;
       ctl.bcast2 = done ? 1u : 0u;
     }
     __syncwarp();
     named_bar(kEpiBarrier, kEpiThreads);
-    // the warp holding row 0 (it took the ticket) normalises, rotates and stores the head
-    if (ctl.bcast2 && (threadIdx.x >> 5) == 4) qkv_head_epilogue(a, sc, head);
+    if (ctl.bcast2) finish_head(head, row);
   }
+
+  __device__ void finish_head(int head, int e) const {
+    constexpr int UPT = QkvShape::kUnitsPerTile;
+    const int64_t grid = gridDim.x, total = QkvShape::kTotalUnits;
+    float y[2];
+#pragma unroll
+    for (int t = 0; t < 2; ++t) {  // element e + 128 t of the head = row e of tile 2 head + t
+      const int tile = 2 * head + t;
+      const int first = cta_of_unit(int64_t(tile) * UPT, grid, total);
+      const int last = cta_of_unit(int64_t(tile) * UPT + UPT - 1, grid, total);
+      const float* part = sc.partials + size_t(tile) * kMaxCtasPerGroup * kTileRows + e;
+      float acc = 0.f;
+      for (int cc = first; cc <= last; ++cc) acc += ld_cg_f32(part + (cc - first) * kTileRows);
+      const int r = tile * kTileRows + e;
+      const uint16_t sb = r < kQs ? a.q_scale[r] : (r < kQs + kPs ? a.k_scale[r - kQs] : a.v_scale[r - kQs - kPs]);
+      // scaled_projection: bf16((x @ codes.T) * scale) (generate_references.py:265-274)
+      y[t] = bf16_round(acc * bf16_to_f32(sb));
+    }
+    // RMSNorm over the head's 256 values (gemma4.py:83-89), the sum in a fixed order
+    double ss = warp_sum_d(double(y[0]) * double(y[0]) + double(y[1]) * double(y[1]));
+    cp_async_wait_all();
+    if ((threadIdx.x & 31) == 0) st->red[e / 32] = ss;
+    named_bar(kEpiBarrier, kEpiThreads);
+    const float inv = rms_inverse(((st->red[0] + st->red[1]) + st->red[2]) + st->red[3], kDs);
+    const bool is_q = head < kNs * kGs, is_k = !is_q && head < kNs * kGs + kNs;
+    if (!st->kv_ok || !st->rope_ok) {
+      if (e == 0) atomicOr(sc.err, (st->kv_ok ? 0u : kErrKvOffset) | (st->rope_ok ? 0u : kErrRopeOffset));
+      named_bar(kEpiBarrier, kEpiThreads);
+      return;
+    }
+    const uint16_t* gamma = is_q ? st->qg : (is_k ? st->kg : nullptr);
+    float nrm[2];
+#pragma unroll
+    for (int t = 0; t < 2; ++t) {
+      const float sv = y[t] * inv;
+      nrm[t] = gamma ? bf16_round(sv * bf16_to_f32(gamma[e + 128 * t])) : bf16_round(sv);
+    }
+    if (is_q || is_k) {
+      // RoPE, half-swap form with the low half of `sin` pre-negated by the caller:
+      // out[i] = bf16(bf16(n[i] cos[i]) + bf16(n[i ^ 128] sin'[i]))
+#pragma unroll
+      for (int t = 0; t < 2; ++t) {
+        const int i = e + 128 * t;
+        const float c = bf16_round(nrm[t] * bf16_to_f32(st->cos[i]));
+        const float sn = bf16_round(nrm[1 - t] * bf16_to_f32(st->sin[i]));
+        st->out[i] = f32_to_bf16(c + sn);
+      }
+    } else {
+      st->out[e] = f32_to_bf16(nrm[0]);
+      st->out[e + 128] = f32_to_bf16(nrm[1]);
+    }
+    named_bar(kEpiBarrier, kEpiThreads);
+    if (e < 32) {  // 16-byte stores
+      uint16_t* dst;
+      if (is_q)
+        dst = a.q_out + head * kDs;
+      else if (is_k)
+        dst = a.k_cache + size_t(st->slot) * kPs + (head - kNs * kGs) * kDs;
+      else
+        dst = a.v_cache + size_t(st->slot) * kPs + (head - kNs * kGs - kNs) * kDs;
+      reinterpret_cast<uint4*>(dst)[e] = reinterpret_cast<const uint4*>(st->out)[e];
+    }
+    named_bar(kEpiBarrier, kEpiThreads);
+  }
+
+  __device__ void load_static(int g, uint4 (&raw)[4]) const { load_group_gamma(a.input_rms, g, raw); }
+  __device__ void load_group(int g, uint4 (&raw)[4]) const { load_group_cg(a.x, g, raw); }
+  __device__ void finish_group(const uint4 (&raw)[4], float inv, float (&v)[16]) const { rms_apply16(raw, inv, v); }
 };
 
 __global__ void __launch_bounds__(kGemvThreads, 1) qkv_kernel(const __grid_constant__ QkvMaps maps, QkvArgs a,
                                                               Scratch sc) {
   extern __shared__ __align__(1024) uint8_t smem[];
+  __shared__ QkvStatic st;
   QkvOp op{&maps, a, sc};
+  op.st = &st;
   gemv_run<QkvShape>(op, smem, sc);
+  cp_async_wait_all();  // a CTA that finished no head still has the prologue's copies in flight
 }
 
 // ---------------------------------------------------------------------------------------
@@ -269,6 +346,7 @@ struct OOp {
   OArgs a;
   Scratch sc;
   uint32_t tx_bytes = OShape::kABytes;
+  static constexpr bool kOwnPieces = false;
   static constexpr bool kRms = false;
   static constexpr int kRmsGroups = 0;
 
@@ -284,27 +362,27 @@ struct OOp {
     if (a.tiled) prefetch_units(a.o_weight, u0, u1, OShape::kABytes);
   }
   __device__ void prologue(GemvCtl&) {}
+  __device__ void load_static(int, uint4 (&)[4]) const {}
   __device__ void load_group(int g, uint4 (&raw)[4]) const { load_group_cg(a.x, g, raw); }
   __device__ void finish_group(const uint4 (&raw)[4], float, float (&v)[16]) const {
     bf16x16_to_f32(raw[0], raw[1], v);
   }
   __device__ void finalize_tile(int tile, int row, float v, GemvCtl&) const {
     const int r = tile * kTileRows + row;
-    sc.y[r] = f32_to_bf16(v * bf16_to_f32(a.o_scale[r]));
+    tail_record(*tail, a.post_rms, a.residual, sc, tile, row, bf16_round(v * bf16_to_f32(a.o_scale[r])));
   }
+  ResidualTail* tail;
 };
 
 __global__ void __launch_bounds__(kGemvThreads, 1) o_kernel(const __grid_constant__ CUtensorMap map, OArgs a,
                                                             Scratch sc) {
   extern __shared__ __align__(1024) uint8_t smem[];
-  __shared__ double red[8];
+  __shared__ ResidualTail tail;
+  if (threadIdx.x == 0) tail.n = 0;  // ordered by the engine's first barrier
   OOp op{&map, a, sc};
+  op.tail = &tail;
   gemv_run<OShape>(op, smem, sc);
-  if (last_cta(sc.counters + kCtaCounter)) {
-    G4_STAMP(sc, 12);
-    residual_epilogue<kGemvThreads>(sc.y, a.post_rms, a.residual, nullptr, red, sc);
-    if (threadIdx.x == 0) sc.counters[kCtaCounter] = 0;
-  }
+  tail_update(tail, a.residual, sc, sc.counters + kBarrierO, kH / kTileRows, nullptr);
   G4_STAMP(sc, 8);
 }
 
@@ -321,6 +399,7 @@ struct UpGateOp {
   Scratch sc;
   float g_up = 0.f, g_gate = 0.f;
   uint32_t tx_bytes = UpGateShape::kABytes + UpGateShape::kScaleBytes;  // packed codes + block scales
+  static constexpr bool kOwnPieces = false;
   static constexpr bool kRms = true;
   static constexpr int kRmsGroups = kH / 16;
 
@@ -353,19 +432,19 @@ struct UpGateOp {
     g_up = *a.up_global;
     g_gate = *a.gate_global;
   }
-  __device__ void load_group(int g, uint4 (&raw)[4]) const {
-    load_group_cg(a.residual, g, raw);
-    load_group_gamma(a.pre_rms, g, raw);
-  }
+  __device__ void load_static(int g, uint4 (&raw)[4]) const { load_group_gamma(a.pre_rms, g, raw); }
+  __device__ void load_group(int g, uint4 (&raw)[4]) const { load_group_cg(a.residual, g, raw); }
   __device__ void finish_group(const uint4 (&raw)[4], float inv, float (&v)[16]) const { rms_apply16(raw, inv, v); }
   __device__ void finalize_tile(int tile, int row, float v, GemvCtl& ctl) const {
     // GloballyScaled(nn.Linear): bf16(bf16(x @ W.T) * g)  (generate_references.py:358-372)
     const float val = bf16_round(bf16_round(v) * (row < 64 ? g_up : g_gate));
     if (row >= 64) ctl.xchg[row - 64] = val;
     named_bar(kEpiBarrier, kEpiThreads);
-    // down_proj input: bf16(bf16(gelu_tanh(gate)) * up)  (gemma4.py:197)
-    if (row < 64) sc.act[tile * 64 + row] = f32_to_bf16(bf16_round(gelu_tanh(ctl.xchg[row])) * val);
+    // down_proj input: bf16(bf16(gelu_tanh(gate)) * up)  (gemma4.py:197). Whole 16-byte
+    // stores: a sector written in 2-byte pieces is slow for the next kernel to read.
+    if (row < 64) ctl.out16[row] = f32_to_bf16(bf16_round(gelu_tanh(ctl.xchg[row])) * val);
     named_bar(kEpiBarrier, kEpiThreads);
+    if (row < 8) reinterpret_cast<uint4*>(sc.act + tile * 64)[row] = reinterpret_cast<const uint4*>(ctl.out16)[row];
   }
 };
 
@@ -387,6 +466,7 @@ struct DownOp {
   Scratch sc;
   float g_down = 0.f;
   uint32_t tx_bytes = DownShape::kABytes + DownShape::kScaleBytes;
+  static constexpr bool kOwnPieces = false;
   static constexpr bool kRms = false;
   static constexpr int kRmsGroups = 0;
 
@@ -411,27 +491,27 @@ struct DownOp {
     prefetch_units(a.down_scale, u0, u1, DownShape::kScaleBytes);
   }
   __device__ void prologue(GemvCtl&) { g_down = *a.down_global; }
+  __device__ void load_static(int, uint4 (&)[4]) const {}
   __device__ void load_group(int g, uint4 (&raw)[4]) const { load_group_cg(sc.act, g, raw); }
   __device__ void finish_group(const uint4 (&raw)[4], float, float (&v)[16]) const {
     bf16x16_to_f32(raw[0], raw[1], v);
   }
   __device__ void finalize_tile(int tile, int row, float v, GemvCtl&) const {
-    const int r = tile * kTileRows + row;
-    sc.y[r] = f32_to_bf16(bf16_round(v) * g_down);
+    // GloballyScaled(nn.Linear): bf16(bf16(x @ W.T) * g)  (generate_references.py:358-413)
+    tail_record(*tail, a.post_rms, a.residual, sc, tile, row, bf16_round(bf16_round(v) * g_down));
   }
+  ResidualTail* tail;
 };
 
 __global__ void __launch_bounds__(kGemvThreads, 1) ffn_down_kernel(const __grid_constant__ DownMaps maps, FfnArgs a,
                                                                    Scratch sc) {
   extern __shared__ __align__(1024) uint8_t smem[];
-  __shared__ double red[8];
+  __shared__ ResidualTail tail;
+  if (threadIdx.x == 0) tail.n = 0;  // ordered by the engine's first barrier
   DownOp op{&maps, a, sc};
+  op.tail = &tail;
   gemv_run<DownShape>(op, smem, sc);
-  if (last_cta(sc.counters + kCtaCounter)) {
-    G4_STAMP(sc, 12);
-    residual_epilogue<kGemvThreads>(sc.y, a.post_rms, a.residual, a.layer_scalar, red, sc);
-    if (threadIdx.x == 0) sc.counters[kCtaCounter] = 0;
-  }
+  tail_update(tail, a.residual, sc, sc.counters + kBarrierDown, kH / kTileRows, a.layer_scalar);
   G4_STAMP(sc, 8);
 }
 
@@ -638,7 +718,7 @@ cudaError_t TmapCache::u8(const void* base, uint64_t cols, uint64_t rows, uint32
 
 size_t o_scratch_bytes() {
   return kScratchHeadBytes + size_t(kCounterCount) * sizeof(uint32_t) +
-         size_t(OShape::kTiles) * kMaxCtasPerGroup * kTileRows * sizeof(float) + size_t(kH) * sizeof(uint16_t);
+         size_t(OShape::kTiles) * kMaxCtasPerGroup * kTileRows * sizeof(float) + size_t(kTileSsCount) * sizeof(double);
 }
 
 cudaError_t launch_o_uncached(const OArgs& a, const LaunchEnv& env) {
