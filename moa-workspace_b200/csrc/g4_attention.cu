@@ -7,122 +7,132 @@
 //   sum[g] = sum_t p[g,t] + 1e-6
 //   out    = bf16( bf16(sum_t bf16(p[g,t]) v[t]) / sum[g] )
 //
-// One thread-block cluster of CL CTAs per KV head (CL = 16 where the GPU schedules clusters
-// of 16, else 8); each CTA owns a contiguous run of ring slots. At entry every CTA starts
-// copying its V rows into shared memory (cp.async, no registers held) and loads its K rows
-// straight into registers, so the whole working set is requested in one round trip. The CTAs
-// exchange their score maxima and output partials through distributed shared memory; rank 0
-// adds the partials in rank order, so the result equals one pass over the ring and does not
-// depend on timing.
-#include <cooperative_groups.h>
-
+// kChunks CTAs per KV head (128 CTAs for the 8 heads), each owning a contiguous run of ring slots.
+// A CTA copies its K and V rows into shared memory with TMA boxes of up to 128 rows,
+// scores its slots for the head's two query heads, and publishes its score maximum. The rounding
+// of p to bf16 depends on the maximum over the WHOLE ring, so the head's CTAs exchange maxima
+// through global memory (a bounded wait on a per-head generation counter: the 128 CTAs are all
+// resident, one per SM) before computing p. Each CTA then publishes its partial sum_t p and
+// sum_t bf16(p) v; the last CTA of the head (ticket) adds the partials in chunk order, so the
+// result does not depend on timing.
 #include "g4_ops.cuh"
-
-namespace cg = cooperative_groups;
+#include "g4_tc.cuh"
 
 namespace g4 {
 namespace {
 
-constexpr int kThreads = 512;
+constexpr int kChunks = 16;                // CTAs per KV head
+constexpr int kThreads = 256;
 constexpr int kWarps = kThreads / 32;
-constexpr int kRowBytes = kDs * 2;      // one head's row in one slot
-constexpr int kVChunk = 256;            // V rows resident in shared memory at a time (128 KB)
-constexpr int kKBatch = 16;             // K rows per warp held in registers at a time
-constexpr int kMaxSlotsPerCta = 1024;   // scores kept for the whole run of a CTA
+constexpr int kRowBytes = kDs * 2;         // one head's row in one slot
+constexpr int kSub = 128;                  // slots resident in shared memory per pass
+constexpr int kMaxRing = 8192;
+constexpr int kMaxPer = kMaxRing / kChunks;
+constexpr int kAttnBarrier = 3900;         // counters: per-head max-exchange generations
+constexpr int kAttnTicket = 3908;          // counters: per-head output tickets
+constexpr size_t kAttnPartials = size_t(1) << 20;  // float offset into the partials scratch
+constexpr int kPartFloats = 2 * kDs + 4;   // per (head, chunk): o[2][256], max[2], sum[2]
 
 struct AttnSmem {
-  uint8_t v[kVChunk * kRowBytes];
-  float score[kMaxSlotsPerCta][kGs];  // scores, then bf16-rounded probabilities
-  float opart[4][kGs][kDs];           // four slot residues, reduced before publishing
-  float pub_max[kGs];
-  float pub_sum[kGs];
+  uint8_t k[kSub * kRowBytes];
+  uint8_t v[kSub * kRowBytes];
+  float score[kMaxPer][kGs];  // scores, then bf16-rounded probabilities
   float red[kWarps][kGs];
+  float gmax[kGs];
+  __align__(16) uint16_t out[kGs * kDs];
+  uint64_t kbar, vbar;
+  uint32_t last;
 };
 
-__device__ __forceinline__ void cp_async16(void* smem_dst, const void* src) {
-  asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(smem_u32(smem_dst)), "l"(src) : "memory");
-}
-__device__ __forceinline__ void cp_async_commit() { asm volatile("cp.async.commit_group;" ::: "memory"); }
-__device__ __forceinline__ void cp_async_wait_all() { asm volatile("cp.async.wait_group 0;" ::: "memory"); }
+struct KvMaps {
+  CUtensorMap k, v;  // [ring][heads][dim] as (dim, head, slot), box {dim, 1, box_slots}
+};
 
-template <int CL>
-__global__ void __launch_bounds__(kThreads, 1) attention_kernel(AttnArgs a, Scratch sc) {
+__global__ void __launch_bounds__(kThreads, 1) attention_kernel(const __grid_constant__ KvMaps maps, AttnArgs a,
+                                                                int box_slots, Scratch sc) {
   extern __shared__ __align__(1024) uint8_t smem_raw[];
   AttnSmem& sm = *reinterpret_cast<AttnSmem*>(smem_raw);
-  cg::cluster_group cluster = cg::this_cluster();
-  const int rank = int(cluster.block_rank());
-  const int head = blockIdx.x / CL;
+  const int head = blockIdx.x / kChunks, chunk = blockIdx.x % kChunks;
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
-  const int per_cta = a.ring_len / CL;      // <= kMaxSlotsPerCta, a multiple of kWarps
-  const int per_warp = per_cta / kWarps;
-  const int slot0 = rank * per_cta;
+  const int per = a.ring_len / kChunks;  // a multiple of 16, at most kMaxPer
+  const int slot0 = chunk * per;
+  const int passes = (per + kSub - 1) / kSub;
+  volatile uint32_t abort_flag = 0;  // this CTA's own waits only
   G4_STAMP(sc, 0);
+  if (tid == 0) {
+    mbar_init(&sm.kbar, 1);
+    mbar_init(&sm.vbar, 1);
+    fence_mbar_init();
+  }
+  // While the preceding QKV op finishes, bring this CTA's K and V rows into L2: it writes one
+  // slot of them, but L2 is coherent, so the copies below (after the wait) still read its rows.
+  for (int b = tid; b < 2 * (per / box_slots); b += kThreads) {
+    const int nb = per / box_slots;
+    tma_prefetch_l2_3d(b < nb ? &maps.k : &maps.v, 0, head, slot0 + (b < nb ? b : b - nb) * box_slots);
+  }
+  __syncthreads();
 
   pdl_wait_primary();  // q and the cache rows come from the preceding QKV op
   pdl_launch_dependents();
   G4_STAMP(sc, 1);
 
-  // V rows [first, first + count) of this CTA -> shared memory, asynchronously (16 B per request)
-  auto fetch_v = [&](int first, int count) {
-    const int chunks = count * (kRowBytes / 16);
-    for (int c = tid; c < chunks; c += kThreads) {
-      const int r = c / (kRowBytes / 16), o = c % (kRowBytes / 16);
-      cp_async16(sm.v + r * kRowBytes + o * 16,
-                 reinterpret_cast<const uint8_t*>(a.v_cache + (size_t(slot0 + first + r) * kNs + head) * kDs) + o * 16);
-    }
-    cp_async_commit();
+  // rows [first, first + count) of a cache into a shared-memory buffer, box_slots rows per TMA load
+  const uint64_t policy = l2_evict_first_policy();  // each row is read once per step
+  auto fetch = [&](const CUtensorMap* map, uint8_t* dst, uint64_t* bar, int first, int count) {
+    if (tid == 0) mbar_arrive_expect_tx(bar, uint32_t(count) * kRowBytes);
+    for (int b = tid; b < count / box_slots; b += kThreads)
+      tma_load_3d(dst + b * box_slots * kRowBytes, map, 0, head, slot0 + first + b * box_slots, bar, policy);
   };
-  fetch_v(0, per_cta < kVChunk ? per_cta : kVChunk);
+  fetch(&maps.k, sm.k, &sm.kbar, 0, per < kSub ? per : kSub);
+  if (passes == 1) fetch(&maps.v, sm.v, &sm.vbar, 0, per);
 
-  // q rows of the two query heads of this KV head: lane holds dims 8*lane .. 8*lane+7
+  // q rows of the two query heads: lane holds dims 8 lane .. 8 lane + 7
   float qv[kGs][8];
 #pragma unroll
   for (int g = 0; g < kGs; ++g) {
-    const uint4 raw = *reinterpret_cast<const uint4*>(a.q + (head * kGs + g) * kDs + lane * 8);
+    const uint4 raw = __ldcg(reinterpret_cast<const uint4*>(a.q + (head * kGs + g) * kDs + lane * 8));
     const uint16_t* b = reinterpret_cast<const uint16_t*>(&raw);
 #pragma unroll
     for (int j = 0; j < 8; ++j) qv[g][j] = bf16_to_f32(b[j]);
   }
 
-  // phase 1: this warp's K rows straight into registers (kKBatch at a time), then its scores
-  const int wslot0 = warp * per_warp;
-  for (int kb0 = 0; kb0 < per_warp; kb0 += kKBatch) {
-    uint4 kr[kKBatch];
+  // phase 1: scores of every slot of this CTA, kSub at a time; warp w scores slots w, w + 8, ...
+  bool ok = true;
+  for (int p = 0; p < passes; ++p) {
+    const int first = p * kSub, rows = per - first < kSub ? per - first : kSub;
+    if (p > 0) {
+      __syncthreads();  // the previous pass is done with the K buffer
+      fetch(&maps.k, sm.k, &sm.kbar, first, rows);
+    }
+    if (ok) ok = mbar_wait_or_abort(&sm.kbar, uint32_t(p & 1), &abort_flag, sc.err);
+#pragma unroll 4
+    for (int t = warp; t < rows; t += kWarps) {
+      const uint4 kr = *reinterpret_cast<const uint4*>(sm.k + t * kRowBytes + lane * 16);
+      const uint16_t* kb = reinterpret_cast<const uint16_t*>(&kr);
+      float d0 = 0.f, d1 = 0.f;
 #pragma unroll
-    for (int r = 0; r < kKBatch; ++r)
-      if (kb0 + r < per_warp)
-        kr[r] = __ldcs(reinterpret_cast<const uint4*>(a.k_cache + (size_t(slot0 + wslot0 + kb0 + r) * kNs + head) * kDs) +
-                       lane);
+      for (int j = 0; j < 8; ++j) {
+        const float kf = bf16_to_f32(kb[j]);
+        d0 = fmaf(qv[0][j], kf, d0);
+        d1 = fmaf(qv[1][j], kf, d1);
+      }
 #pragma unroll
-    for (int r = 0; r < kKBatch; ++r) {
-      if (kb0 + r < per_warp) {
-        const uint16_t* kb = reinterpret_cast<const uint16_t*>(&kr[r]);
-        float d0 = 0.f, d1 = 0.f;
-#pragma unroll
-        for (int j = 0; j < 8; ++j) {
-          const float kf = bf16_to_f32(kb[j]);
-          d0 = fmaf(qv[0][j], kf, d0);
-          d1 = fmaf(qv[1][j], kf, d1);
-        }
-#pragma unroll
-        for (int o = 16; o; o >>= 1) {
-          d0 += __shfl_xor_sync(0xffffffffu, d0, o);
-          d1 += __shfl_xor_sync(0xffffffffu, d1, o);
-        }
-        if (lane == 0) {
-          sm.score[wslot0 + kb0 + r][0] = bf16_round(a.scale * d0);
-          sm.score[wslot0 + kb0 + r][1] = bf16_round(a.scale * d1);
-        }
-        __syncwarp();
+      for (int o = 16; o; o >>= 1) {
+        d0 += __shfl_xor_sync(0xffffffffu, d0, o);
+        d1 += __shfl_xor_sync(0xffffffffu, d1, o);
+      }
+      if (lane == 0) {
+        sm.score[first + t][0] = bf16_round(a.scale * d0);
+        sm.score[first + t][1] = bf16_round(a.scale * d1);
       }
     }
   }
   __syncthreads();
   G4_STAMP(sc, 2);
 
-  // global max over the whole ring (every CTA of the cluster)
+  // this CTA's maximum, published; then the head's maximum over all kChunks CTAs
   float m0 = -INFINITY, m1 = -INFINITY;
-  for (int t = tid; t < per_cta; t += kThreads) {
+  for (int t = tid; t < per; t += kThreads) {
     m0 = fmaxf(m0, sm.score[t][0]);
     m1 = fmaxf(m1, sm.score[t][1]);
   }
@@ -132,30 +142,45 @@ __global__ void __launch_bounds__(kThreads, 1) attention_kernel(AttnArgs a, Scra
     sm.red[warp][0] = m0;
     sm.red[warp][1] = m1;
   }
-  __syncwarp();
   __syncthreads();
+  float* parts = sc.partials + kAttnPartials + size_t(head) * kChunks * kPartFloats;
   if (tid == 0) {
     float a0 = -INFINITY, a1 = -INFINITY;
     for (int w = 0; w < kWarps; ++w) {
       a0 = fmaxf(a0, sm.red[w][0]);
       a1 = fmaxf(a1, sm.red[w][1]);
     }
-    sm.pub_max[0] = a0;
-    sm.pub_max[1] = a1;
+    parts[chunk * kPartFloats + 2 * kDs] = a0;
+    parts[chunk * kPartFloats + 2 * kDs + 1] = a1;
+    // generation barrier of the head's CTAs (the counter grows by kChunks per call)
+    uint32_t* bar = sc.counters + kAttnBarrier + head;
+    const uint32_t old = atomic_add_release_gpu(bar, 1u);
+    const uint32_t target = old - old % kChunks + kChunks;
+    const uint64_t t0 = globaltimer_ns();
+    while (int32_t(ld_acquire_gpu(bar) - target) < 0) {
+      if (globaltimer_ns() - t0 > kWaitLimitNs) {
+        atomicOr(sc.err, kErrWaitTimeout);
+        break;
+      }
+    }
   }
-  __syncwarp();
-  cluster.sync();
-  float gm0 = -INFINITY, gm1 = -INFINITY;
-  for (int r = 0; r < CL; ++r) {
-    const float* pm = cluster.map_shared_rank(sm.pub_max, r);
-    gm0 = fmaxf(gm0, pm[0]);
-    gm1 = fmaxf(gm1, pm[1]);
+  __syncthreads();
+  if (tid < kGs) {
+    float m = -INFINITY;
+    float pm[kChunks];
+#pragma unroll
+    for (int c = 0; c < kChunks; ++c) pm[c] = __ldcg(parts + c * kPartFloats + 2 * kDs + tid);
+#pragma unroll
+    for (int c = 0; c < kChunks; ++c) m = fmaxf(m, pm[c]);
+    sm.gmax[tid] = m;
   }
+  __syncthreads();
   G4_STAMP(sc, 3);
 
-  // probabilities and the local denominator (fixed summation order)
+  // probabilities and this CTA's denominator (fixed summation order)
+  const float gm0 = sm.gmax[0], gm1 = sm.gmax[1];
   float s0 = 0.f, s1 = 0.f;
-  for (int t = tid; t < per_cta; t += kThreads) {
+  for (int t = tid; t < per; t += kThreads) {
     const float mk = a.mask[slot0 + t];
     const float p0 = fminf(expf(sm.score[t][0] - gm0), mk);
     const float p1 = fminf(expf(sm.score[t][1] - gm1), mk);
@@ -164,141 +189,108 @@ __global__ void __launch_bounds__(kThreads, 1) attention_kernel(AttnArgs a, Scra
     sm.score[t][0] = bf16_round(p0);
     sm.score[t][1] = bf16_round(p1);
   }
-#pragma unroll
-  for (int o = 16; o; o >>= 1) {
-    s0 += __shfl_xor_sync(0xffffffffu, s0, o);
-    s1 += __shfl_xor_sync(0xffffffffu, s1, o);
-  }
+  s0 = warp_sum(s0);
+  s1 = warp_sum(s1);
   __syncthreads();  // every read of sm.red (the maxima) is done
   if (lane == 0) {
     sm.red[warp][0] = s0;
     sm.red[warp][1] = s1;
   }
-  __syncwarp();
-  cp_async_wait_all();
   __syncthreads();
-  if (tid == 0) {
-    float a0 = 0.f, a1 = 0.f;
-    for (int w = 0; w < kWarps; ++w) {
-      a0 += sm.red[w][0];
-      a1 += sm.red[w][1];
-    }
-    sm.pub_sum[0] = a0;
-    sm.pub_sum[1] = a1;
-  }
-  __syncwarp();
   G4_STAMP(sc, 4);
 
-  // phase 2: o = sum_t bf16(p) v. Thread (res, pair) covers dims 2*pair, 2*pair+1 of both
-  // query heads over the slots t = res (mod 4), one resident chunk of V rows at a time.
-  {
-    const int res = tid >> 7, pair = tid & 127;
-    float o00 = 0.f, o01 = 0.f, o10 = 0.f, o11 = 0.f;
-    for (int c0 = 0; c0 < per_cta; c0 += kVChunk) {
-      const int rows = per_cta - c0 < kVChunk ? per_cta - c0 : kVChunk;
-      if (c0 > 0) {  // later chunks of a long ring: refill the buffer
-        __syncthreads();
-        fetch_v(c0, rows);
-        cp_async_wait_all();
-        __syncthreads();
-      }
-      for (int t = res; t < rows; t += 4) {
-        const uint32_t vv = *reinterpret_cast<const uint32_t*>(sm.v + t * kRowBytes + pair * 4);
-        const float v0 = bf16_to_f32(uint16_t(vv & 0xffff)), v1 = bf16_to_f32(uint16_t(vv >> 16));
-        const float w0 = sm.score[c0 + t][0], w1 = sm.score[c0 + t][1];
-        o00 = fmaf(w0, v0, o00);
-        o01 = fmaf(w0, v1, o01);
-        o10 = fmaf(w1, v0, o10);
-        o11 = fmaf(w1, v1, o11);
-      }
+  // phase 2: o[g][d] = sum_t bf16(p[g][t]) v[t][d]; thread d owns dimension d of both heads
+  float o0 = 0.f, o1 = 0.f;
+  for (int p = 0; p < passes; ++p) {
+    const int first = p * kSub, rows = per - first < kSub ? per - first : kSub;
+    if (passes > 1) {
+      __syncthreads();  // the previous pass is done with the V buffer
+      fetch(&maps.v, sm.v, &sm.vbar, first, rows);
     }
-    sm.opart[res][0][2 * pair] = o00;
-    sm.opart[res][0][2 * pair + 1] = o01;
-    sm.opart[res][1][2 * pair] = o10;
-    sm.opart[res][1][2 * pair + 1] = o11;
+    if (ok) ok = mbar_wait_or_abort(&sm.vbar, uint32_t(p & 1), &abort_flag, sc.err);
+    for (int t = 0; t < rows; ++t) {
+      const float vf = bf16_to_f32(reinterpret_cast<const uint16_t*>(sm.v + t * kRowBytes)[tid]);
+      o0 = fmaf(sm.score[first + t][0], vf, o0);
+      o1 = fmaf(sm.score[first + t][1], vf, o1);
+    }
+  }
+  parts[chunk * kPartFloats + tid] = o0;
+  parts[chunk * kPartFloats + kDs + tid] = o1;
+  if (tid < kGs) {
+    float z = 0.f;
+    for (int w = 0; w < kWarps; ++w) z += sm.red[w][tid];
+    parts[chunk * kPartFloats + 2 * kDs + 2 + tid] = z;
+  }
+  __syncthreads();  // every partial of this CTA precedes the release below
+  if (tid == 0) {
+    uint32_t* ticket = sc.counters + kAttnTicket + head;
+    const uint32_t before = atomic_add_acq_rel_gpu(ticket, 1u);
+    sm.last = before == kChunks - 1 ? 1u : 0u;
+    if (sm.last) *ticket = 0u;
   }
   __syncthreads();
-  {
-    const int g = tid >> 8, d = tid & 255;
-    sm.opart[0][g][d] = ((sm.opart[0][g][d] + sm.opart[1][g][d]) + sm.opart[2][g][d]) + sm.opart[3][g][d];
-  }
-  cluster.sync();
   G4_STAMP(sc, 5);
 
-  if (rank == 0) {
-    const int g = tid >> 8, d = tid & 255;
-    float o = 0.f, z = 0.f;
-    for (int r = 0; r < CL; ++r) {
-      const float* op = cluster.map_shared_rank(&sm.opart[0][0][0], r);
-      const float* ps = cluster.map_shared_rank(sm.pub_sum, r);
-      o += op[g * kDs + d];
-      z += ps[g];
+  if (sm.last) {  // the head's last CTA: partials in chunk order
+    float o[kGs] = {0.f, 0.f}, z[kGs] = {0.f, 0.f};
+    float po[kChunks][kGs], pz[kChunks][kGs];
+#pragma unroll
+    for (int c = 0; c < kChunks; ++c) {  // every load in flight at once
+      const float* pc = parts + c * kPartFloats;
+      po[c][0] = __ldcg(pc + tid);
+      po[c][1] = __ldcg(pc + kDs + tid);
+      pz[c][0] = __ldcg(pc + 2 * kDs + 2);
+      pz[c][1] = __ldcg(pc + 2 * kDs + 3);
     }
-    z += kEps;
-    a.out[(head * kGs + g) * kDs + d] = f32_to_bf16(bf16_round(o) / z);
+#pragma unroll
+    for (int c = 0; c < kChunks; ++c) {
+      o[0] += po[c][0];
+      o[1] += po[c][1];
+      z[0] += pz[c][0];
+      z[1] += pz[c][1];
+    }
+#pragma unroll
+    for (int g = 0; g < kGs; ++g) sm.out[g * kDs + tid] = f32_to_bf16(bf16_round(o[g]) / (z[g] + kEps));
+    __syncthreads();
+    if (tid < kGs * kDs * 2 / 16)  // 16-byte stores
+      reinterpret_cast<uint4*>(a.out + head * kGs * kDs)[tid] = reinterpret_cast<const uint4*>(sm.out)[tid];
   }
-  cluster.sync();  // keep every CTA's shared memory alive until rank 0 has read it
   G4_STAMP(sc, 6);
 }
-
-int g_cluster = 0;  // 16 or 8, decided once per process
 
 }  // namespace
 
 cudaError_t prepare_attention_kernels() {
-  cudaError_t e = cudaFuncSetAttribute(attention_kernel<16>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                       int(sizeof(AttnSmem)));
-  if (e == cudaSuccess)
-    e = cudaFuncSetAttribute(attention_kernel<16>, cudaFuncAttributeNonPortableClusterSizeAllowed, 1);
-  if (e == cudaSuccess)
-    e = cudaFuncSetAttribute(attention_kernel<8>, cudaFuncAttributeMaxDynamicSharedMemorySize, int(sizeof(AttnSmem)));
-  if (e != cudaSuccess) return e;
-  if (g_cluster == 0) {
-    cudaLaunchConfig_t cfg = {};
-    cfg.gridDim = dim3(kNs * 16);
-    cfg.blockDim = dim3(kThreads);
-    cfg.dynamicSmemBytes = sizeof(AttnSmem);
-    cudaLaunchAttribute attr[1];
-    attr[0].id = cudaLaunchAttributeClusterDimension;
-    attr[0].val.clusterDim.x = 16;
-    attr[0].val.clusterDim.y = 1;
-    attr[0].val.clusterDim.z = 1;
-    cfg.attrs = attr;
-    cfg.numAttrs = 1;
-    int clusters = 0;
-    const cudaError_t q = cudaOccupancyMaxActiveClusters(&clusters, attention_kernel<16>, &cfg);
-    // 16-CTA clusters only when all kNs of them fit on the GPU at once
-    g_cluster = (q == cudaSuccess && clusters >= kNs) ? 16 : 8;
-    if (q != cudaSuccess) (void)cudaGetLastError();
-  }
-  return cudaSuccess;
+  return cudaFuncSetAttribute(attention_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, int(sizeof(AttnSmem)));
 }
 
-int attention_slot_multiple() { return (g_cluster ? g_cluster : 8) * kWarps; }
-int attention_max_ring() { return 8 * kMaxSlotsPerCta; }
+int attention_slot_multiple() { return kChunks * 16; }
+int attention_max_ring() { return kMaxRing; }
 
 cudaError_t launch_attention(const AttnArgs& a, const LaunchEnv& env) {
-  const int cl = g_cluster ? g_cluster : 8;
+  // box: the largest of 128, 64, 32, 16 slots that divides a CTA's run (a multiple of 16)
+  const int per = a.ring_len / kChunks;
+  int box = kSub;
+  while (per % box != 0) box /= 2;
+  KvMaps maps;
+  cudaError_t e;
+  if ((e = env.maps->kv(a.k_cache, uint64_t(a.ring_len), kNs, kDs, uint32_t(box), &maps.k))) return e;
+  if ((e = env.maps->kv(a.v_cache, uint64_t(a.ring_len), kNs, kDs, uint32_t(box), &maps.v))) return e;
   cudaLaunchConfig_t cfg = {};
-  cfg.gridDim = dim3(kNs * cl);
+  cfg.gridDim = dim3(kNs * kChunks);
   cfg.blockDim = dim3(kThreads);
   cfg.dynamicSmemBytes = sizeof(AttnSmem);
   cfg.stream = env.stream;
-  cudaLaunchAttribute attr[2];
-  attr[0].id = cudaLaunchAttributeClusterDimension;
-  attr[0].val.clusterDim.x = cl;
-  attr[0].val.clusterDim.y = 1;
-  attr[0].val.clusterDim.z = 1;
-  attr[1].id = cudaLaunchAttributeProgrammaticStreamSerialization;
-  attr[1].val.programmaticStreamSerializationAllowed = env.pdl ? 1 : 0;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = env.pdl ? 1 : 0;
   cfg.attrs = attr;
-  cfg.numAttrs = 2;
+  cfg.numAttrs = 1;
   Scratch sc = env.sc;
 #ifdef G4_TRACE
   if (sc.trace) sc.trace += 4096;  // profiling builds: separate stamp rows per kernel
 #endif
-  return cl == 16 ? cudaLaunchKernelEx(&cfg, attention_kernel<16>, a, sc)
-                  : cudaLaunchKernelEx(&cfg, attention_kernel<8>, a, sc);
+  return cudaLaunchKernelEx(&cfg, attention_kernel, maps, a, box, sc);
 }
 
 }  // namespace g4

@@ -257,6 +257,11 @@ __device__ __forceinline__ uint4 ld_cg_u4(const void* p) { return __ldcg(reinter
 // ---------------------------------------------------------------------------------------
 // Reductions
 
+__device__ __forceinline__ float warp_sum(float v) {
+#pragma unroll
+  for (int o = 16; o; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+  return v;
+}
 __device__ __forceinline__ float warp_max(float v) {
 #pragma unroll
   for (int o = 16; o; o >>= 1) v = fmaxf(v, __shfl_xor_sync(0xffffffffu, v, o));

@@ -689,6 +689,27 @@ void TmapCache::put(const void* base, uint64_t key, const CUtensorMap& map) {
   next_ = (next_ + 1) % kEntries;
 }
 
+cudaError_t TmapCache::kv(const void* base, uint64_t ring, uint32_t heads, uint32_t dim, uint32_t box_slots,
+                          CUtensorMap* out) {
+  const uint64_t key = (ring << 32) ^ (uint64_t(heads) << 24) ^ (uint64_t(dim) << 12) ^ box_slots ^ (uint64_t(3) << 62);
+  if (const CUtensorMap* m = find(base, key)) {
+    *out = *m;
+    return cudaSuccess;
+  }
+  auto enc = encode_fn();
+  if (!enc) return cudaErrorNotSupported;
+  const cuuint64_t gdim[3] = {dim, heads, ring};
+  const cuuint64_t gstride[2] = {uint64_t(dim) * 2, uint64_t(dim) * heads * 2};
+  const cuuint32_t box[3] = {dim, 1, box_slots};
+  const cuuint32_t estride[3] = {1, 1, 1};
+  const CUresult r = enc(out, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 3, const_cast<void*>(base), gdim, gstride, box, estride,
+                         CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_NONE, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                         CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  if (r != CUDA_SUCCESS) return cudaErrorInvalidValue;
+  put(base, key, *out);
+  return cudaSuccess;
+}
+
 cudaError_t TmapCache::u8(const void* base, uint64_t cols, uint64_t rows, uint32_t box_cols, uint32_t box_rows,
                           bool swizzle128, CUtensorMap* out) {
   const uint64_t key = (cols << 34) ^ (rows << 12) ^ (uint64_t(box_cols) << 4) ^ (uint64_t(box_rows) << 1) ^
