@@ -597,8 +597,14 @@ __device__ void gemv_run(Op& op, uint8_t* smem_raw, const Scratch& sc) {
           __syncwarp();
           named_bar(kEpiBarrier, kEpiThreads);
           if (ctl.bcast) {
+            float pv[kMaxCtasPerGroup];  // every load in flight at once, then the sum in CTA order
+#pragma unroll
+            for (int k = 0; k < kMaxCtasPerGroup; ++k)
+              pv[k] = k <= lastc - first ? ld_cg_f32(part + k * kTileRows + row) : 0.f;
             float tot = 0.f;
-            for (int cc = first; cc <= lastc; ++cc) tot += ld_cg_f32(part + (cc - first) * kTileRows + row);
+#pragma unroll
+            for (int k = 0; k < kMaxCtasPerGroup; ++k)
+              if (k <= lastc - first) tot += pv[k];
             op.finalize_tile(tile, row, tot, ctl);
           }
         }

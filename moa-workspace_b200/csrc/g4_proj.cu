@@ -269,10 +269,15 @@ struct QkvOp {
       const int first = cta_of_unit(int64_t(tile) * UPT, grid, total);
       const int last = cta_of_unit(int64_t(tile) * UPT + UPT - 1, grid, total);
       const float* part = sc.partials + size_t(tile) * kMaxCtasPerGroup * kTileRows + e;
-      float acc = 0.f;
-      for (int cc = first; cc <= last; ++cc) acc += ld_cg_f32(part + (cc - first) * kTileRows);
       const int r = tile * kTileRows + e;
       const uint16_t sb = r < kQs ? a.q_scale[r] : (r < kQs + kPs ? a.k_scale[r - kQs] : a.v_scale[r - kQs - kPs]);
+      float pv[kMaxCtasPerGroup];  // every load in flight at once, then the sum in CTA order
+#pragma unroll
+      for (int k = 0; k < kMaxCtasPerGroup; ++k) pv[k] = k <= last - first ? ld_cg_f32(part + k * kTileRows) : 0.f;
+      float acc = 0.f;
+#pragma unroll
+      for (int k = 0; k < kMaxCtasPerGroup; ++k)
+        if (k <= last - first) acc += pv[k];
       // scaled_projection: bf16((x @ codes.T) * scale) (generate_references.py:265-274)
       y[t] = bf16_round(acc * bf16_to_f32(sb));
     }
