@@ -8,8 +8,10 @@ sliding_attention_output (FP8) -> decoder_feedforward (NVFP4), all through libg4
     python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
 
 - value: tokens/s through one layer, device-timed with CUDA events over K steps replayed from a
-  CUDA graph, with weights, caches and activations resident in HBM (max over ranks; N>1 runs
-  one independent replica per GPU: weak scaling).
+  CUDA graph, with weights, caches and activations resident in HBM (max over ranks). N>1 splits
+  the layer tensor-parallel over the N GPUs (KV heads and FFN rows per rank; the O and down
+  partial sums are added across the GPUs inside those kernels over NVLink): one token per step
+  for the whole job, strong scaling.
 - e2e: the same metric through the public C ABI from pinned host buffers: every step copies the
   token's hidden state and position offsets host->device, runs the four ops and reads the
   resulting hidden state back.
@@ -43,14 +45,24 @@ for p in (str(REPO), str(REPO / "moa-workspace_b200")):
 
 H, L, NS, GS, DS, QS, PS, TS, E = 3840, 15360, 8, 2, 256, 4096, 2048, 1024, 32768
 N_LAYERS = 4
-# algorithmic bytes per op call at M=1 (weights + scales + activations read and written)
-BYTES = {
-    "sliding_project_qkv": (QS + 2 * PS) * H + (QS + 2 * PS) * 2 + H * 2 * 2 + DS * 2 * 2 + 4 * DS * 2
-                           + 2 * NS * DS * 2 + QS * 2,
-    "sliding_attention": 2 * TS * NS * DS * 2 + QS * 2 * 2 + TS * 4,
-    "sliding_attention_output": H * QS + H * 2 + QS * 2 + H * 2 * 3,
-    "decoder_feedforward": 2 * (L * H // 2 + L * H // 16) + (H * L // 2 + H * L // 16) + H * 2 * 4 + 8 * 2 + 12,
-}
+
+
+def op_bytes(world=1):
+    """Algorithmic bytes one GPU moves per op call at M=1 (weights + scales + activations read
+    and written) when the layer is split over `world` tensor-parallel ranks (1: the whole layer)."""
+    w, fr = world, L // world
+    dk = -(-fr // 256) * 256  # a rank's down K slice, zero-padded to whole 256-element units
+    return {
+        "sliding_project_qkv": (QS + 2 * PS) // w * H + (QS + 2 * PS) // w * 2 + H * 2 * 2 + DS * 2 * 2
+                               + 4 * DS * 2 + 2 * NS // w * DS * 2 + QS // w * 2,
+        "sliding_attention": 2 * TS * NS // w * DS * 2 + QS // w * 2 * 2 + TS * 4,
+        "sliding_attention_output": H * QS // w + H * 2 + QS // w * 2 + H * 2 * 3,
+        "decoder_feedforward": 2 * (fr * H // 2 + fr * H // 16) + (H * dk // 2 + H * dk // 16) + H * 2 * 4 + 8 * 2
+                               + 12,
+    }
+
+
+BYTES = op_bytes(1)
 # DRAM bytes read + written per decoder_feedforward call (ffn_upgate + ffn_down): ncu --set full
 # capture of `python bench.py --only ffn --steps 3 --warmup 3` (dram__bytes_read.sum + write.sum)
 FFN_TRAFFIC = 66.43e6 + 0.63e6 + 33.28e6
@@ -144,6 +156,8 @@ def quant_nvfp4(w):
 
 
 class Layer:
+    """One decoder layer's weights and ring caches (whole; `shard` keeps one rank's slices)."""
+
     def __init__(self, gen, dev):
         import torch
 
@@ -171,6 +185,21 @@ class Layer:
         self.layer_scalar = bf(torch.full((8,), 0.375, device=dev))
         self.tiled = False
 
+    # attribute -> the reference op parameter it is passed as (g4b200.tp's slicing rules)
+    SHARDED = {"q_w": "q_weight", "k_w": "k_weight", "v_w": "v_weight", "q_s": "q_weight_scale",
+               "k_s": "k_weight_scale", "v_s": "v_weight_scale", "k_cache": "k_cache", "v_cache": "v_cache",
+               "o_w": "o_weight", "up_p": "up_weight_packed", "gate_p": "gate_weight_packed",
+               "up_s": "up_weight_scale", "gate_s": "gate_weight_scale", "down_p": "down_weight_packed",
+               "down_s": "down_weight_scale"}
+
+    def shard(self, rank, world):
+        """Keep tensor-parallel rank `rank`'s slices of the sliced tensors."""
+        from g4b200 import tp
+
+        for attr, name in self.SHARDED.items():
+            setattr(self, attr, tp.shard(name, getattr(self, attr), rank, world))
+        return self
+
     def tile(self, ops, device):
         """Repack the weight matrices into the GPU-native unit-tiled layout (once, at load)."""
         for attr, name in (("q_w", "q_weight"), ("k_w", "k_weight"), ("v_w", "v_weight"), ("o_w", "o_weight"),
@@ -186,7 +215,7 @@ class Layer:
 class Workspace:
     """Per-token buffers shared by the layers (the reference host's Workspace/Decode)."""
 
-    def __init__(self, gen, dev, pos=1763):
+    def __init__(self, gen, dev, pos=1763, world=1):
         import numpy as np
         import torch
 
@@ -202,8 +231,8 @@ class Workspace:
         self.kv_offset = torch.tensor([(pos % TS) * NS * DS * 2], dtype=torch.int32, device=dev)
         self.rope_offset = torch.tensor([pos * DS * 2], dtype=torch.int32, device=dev)
         self.mask = (torch.arange(TS, device=dev) <= pos).to(torch.float32)
-        self.q = torch.zeros((NS, GS, DS), dtype=torch.bfloat16, device=dev)
-        self.attn = torch.zeros((NS, GS, DS), dtype=torch.bfloat16, device=dev)
+        self.q = torch.zeros((NS // world, GS, DS), dtype=torch.bfloat16, device=dev)  # this rank's heads
+        self.attn = torch.zeros((NS // world, GS, DS), dtype=torch.bfloat16, device=dev)
 
 
 def layer_step(ops, device, w: Workspace, lay: Layer, which=("qkv", "attn", "o", "ffn")):
@@ -367,16 +396,20 @@ def run_ours(args):
 
         dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120), device_id=torch.device("cuda", local))
 
-    from g4b200 import ops
+    from g4b200 import ops, tp
 
     device = ops.Device(local)
     device.set_overlap(True)
+    if dist:
+        tp.connect(device)  # this GPU is tensor-parallel rank `rank` of `world`
     dev = torch.device("cuda", local)
     gen = torch.Generator(device=dev)
-    gen.manual_seed(1000 + rank)
-    layers = [Layer(gen, dev).tile(ops, device) for _ in range(N_LAYERS)]
-    ws = Workspace(gen, dev)
+    gen.manual_seed(1000)  # the same whole layers on every rank; each keeps its slices
+    layers = [Layer(gen, dev).shard(rank, world).tile(ops, device) for _ in range(N_LAYERS)]
+    ws = Workspace(gen, dev, world=world)
     torch.cuda.synchronize()
+    if dist:
+        dist.barrier()  # the ranks' kernels wait on each other (bounded): start them together
 
     # correctness gate before timing: one step, no device-side errors
     layer_step(ops, device, ws, layers[0])
@@ -402,11 +435,13 @@ def run_ours(args):
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
         elapsed = float(t.item())
     device.check()
-    value = steps * world / elapsed
+    value = steps / elapsed  # one token through the layer per step, for the whole job
 
     # --- per-op device time (each op alone, graph of many calls rotating the layers)
     op_us = {}
     reps = 64
+    if dist:
+        dist.barrier()
     for key, name in (("qkv", "sliding_project_qkv"), ("attn", "sliding_attention"),
                       ("o", "sliding_attention_output"), ("ffn", "decoder_feedforward")):
         g = capture(torch, lambda i, k=key: layer_step(ops, device, ws, layers[i % N_LAYERS], (k,)), reps)
@@ -449,7 +484,7 @@ def run_ours(args):
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
         e2e_elapsed = float(t.item())
     device.check()
-    e2e_value = e2e_steps * world / e2e_elapsed
+    e2e_value = e2e_steps / e2e_elapsed
 
     cpu = None
     if rank == 0 and world == 1 and not args.no_cpu:
@@ -463,9 +498,10 @@ def run_ours(args):
         return 0
 
     pk, pk_kind = peaks()
-    ffn_bytes = BYTES["decoder_feedforward"]
+    rank_bytes = op_bytes(world)
+    ffn_bytes = rank_bytes["decoder_feedforward"]
     achieved = ffn_bytes / (op_us["decoder_feedforward"] * 1e-6) / 1e9
-    layer_bytes = sum(BYTES.values())
+    layer_bytes = sum(rank_bytes.values())  # per GPU
     line = {
         "metric": METRIC,
         "value": value,
@@ -475,26 +511,29 @@ def run_ours(args):
         "warmup": warm_replays * per_graph,
         "ms_per_step": elapsed / steps * 1e3,
         "higher_is_better": True,
-        "scaling": "weak",
+        "scaling": "strong" if world > 1 else "weak",
         "vs_baseline": None,
         "dtype": "bf16",
         "arithmetic": "tcgen05: fp8 e4m3 weights (kind::f8f6f4) x the bf16 activation as exact e4m3 terms; nvfp4 "
                       "e2m1 weights with e4m3 block scales (kind::mxf4nvf4) x the activation as exact e2m1 digits; "
                       "f32 accumulation in TMEM",
         "data": "synthetic",
-        "config": {"workload": WORKLOAD, "global_batch": 1, "seq_len": TS, "parallelism": f"replicas x{world}",
-                   "l2": f"inputs larger than L2: {N_LAYERS} distinct layers ({N_LAYERS * layer_bytes / 1e6:.0f} MB) "
-                         "rotated step to step", "launch": "CUDA graph of C-ABI calls, programmatic dependent launch"},
+        "config": {"workload": WORKLOAD, "global_batch": 1, "seq_len": TS,
+                   "parallelism": f"tp{world}" if world > 1 else "single GPU",
+                   "l2": f"inputs larger than L2: {N_LAYERS} distinct layers ({N_LAYERS * layer_bytes / 1e6:.0f} MB "
+                         "per GPU) rotated step to step",
+                   "launch": "CUDA graph of C-ABI calls, programmatic dependent launch"},
         "ops_us": {k: round(v, 3) for k, v in op_us.items()},
-        "ops_gbs": {k: round(BYTES[k] / (op_us[k] * 1e-6) / 1e9, 1) for k in op_us},
-        "layer_bytes": layer_bytes,
-        "layer_gbs": round(layer_bytes * steps * world / elapsed / world / 1e9, 1),
-        "roofline": {"bound": "hbm", "kernel": "decoder_feedforward (ffn_upgate + ffn_down kernels)",
+        "ops_gbs": {k: round(rank_bytes[k] / (op_us[k] * 1e-6) / 1e9, 1) for k in op_us},
+        "layer_bytes_per_gpu": layer_bytes,
+        "layer_gbs_per_gpu": round(layer_bytes * steps / elapsed / 1e9, 1),
+        "roofline": {"bound": "hbm", "kernel": "decoder_feedforward (ffn_upgate + ffn_down kernels, one GPU's slice)",
                      "achieved": round(achieved, 1), "peak": pk["hbm_gbs"], "unit": "GB/s",
                      "frac": round(achieved / pk["hbm_gbs"], 4), "peak_source": pk_kind,
-                     "algorithmic_bytes_per_launch": ffn_bytes, "traffic": args.traffic},
-        "e2e": {"value": e2e_value, "unit": "tokens/s", "h2d_bytes_per_step": H * 2 + 8,
-                "d2h_bytes_per_step": H * 2, "steps": e2e_steps},
+                     "algorithmic_bytes_per_launch": ffn_bytes,
+                     "traffic": args.traffic if world == 1 else None},
+        "e2e": {"value": e2e_value, "unit": "tokens/s", "h2d_bytes_per_step": (H * 2 + 8) * world,
+                "d2h_bytes_per_step": H * 2 * world, "steps": e2e_steps},
         "gpu_launches": steps * sum(KERNELS_PER_OP.values()),
         "clocks": sampler.summary(),
         "cpu_baseline": cpu,

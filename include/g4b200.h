@@ -49,6 +49,7 @@ typedef int32_t g4_status;
 #define G4_DEVERR_WAIT_TIMEOUT 4u /* a bounded in-kernel wait gave up */
 #define G4_DEVERR_NEGATIVE_SCALE 16u /* an nvfp4 block scale is negative (the reference's loader
                                        * and harness only produce non-negative ones) */
+#define G4_DEVERR_PEER_TIMEOUT 32u   /* a tensor-parallel peer's partial sums did not arrive */
 
 typedef struct g4_ctx g4_ctx;
 
@@ -158,8 +159,8 @@ g4_status g4_decoder_feedforward_tiled(g4_ctx* ctx, uint16_t* residual_hbm, cons
  * (and the synchronisation cudaMalloc/cudaFree may imply) is not acceptable.
  * Arguments and result are those of g4_sliding_attention_output on reference-layout weights,
  * on the CURRENT device and `stream`. The op's scratch (error word, tickets and the grid-barrier
- * counter, split-K partial sums, per-tile sums of squares: 140,032 bytes on a B200) lives in one
- * file-scope 192 KiB block of static device memory in this library, one per device. Returns
+ * counter, split-K partial sums, per-tile sums of squares: 262,912 bytes on a B200) lives in one
+ * file-scope 288 KiB block of static device memory in this library, one per device. Returns
  * G4_ERR_UNSUPPORTED if a GPU
  * would need more than that, or is not sm_100. The error word and tickets must be zero when
  * the kernel starts: the call zeroes them with cudaMemsetAsync on `stream` before each launch.
@@ -172,6 +173,40 @@ g4_status g4_decoder_feedforward_tiled(g4_ctx* ctx, uint16_t* residual_hbm, cons
 g4_status g4_sliding_attention_output_noalloc(const uint16_t* x, const uint16_t* post_attn_rms_weight,
                                               const uint8_t* o_weight, const uint16_t* o_weight_scale,
                                               uint16_t* residual_hbm, void* stream);
+
+/* ---- Tensor parallelism over the GPUs of one node (no reference counterpart: the reference
+ * runs a layer on one chip). A Megatron split over `world` ranks (1, 2, 4 or 8), one process
+ * (or context) per GPU. Rank r holds:
+ *   sliding_project_qkv   q_weight rows [4096 r/w, 4096 (r+1)/w) with their q_weight_scale
+ *                         entries (its 16/w query heads), k_weight / v_weight rows and scales
+ *                         [2048 r/w, 2048 (r+1)/w) (its 8/w KV heads), k_cache / v_cache
+ *                         [ring][8/w][256] (those heads' slice of every slot), q_out [16/w][256].
+ *                         x, the norm weights, cos / sin and the offsets are whole and the same
+ *                         on every rank; kv_offset stays a byte offset into the WHOLE layer's
+ *                         cache row (slot * 8 * 256 * 2), as the reference computes it.
+ *   sliding_attention     q [16/w][256], the cache slices, mask whole, out [16/w][256].
+ *   sliding_attention_output  x = this rank's attention output [4096/w], o_weight columns
+ *                         [4096 r/w, 4096 (r+1)/w) as a row-major [3840][4096/w] matrix;
+ *                         o_weight_scale, post_attn_rms_weight and residual_hbm whole.
+ *   decoder_feedforward   up / gate rows [15360 r/w, 15360 (r+1)/w) (packed [15360/w][1920],
+ *                         scales [15360/w][240]); down columns of the same range as a row-major
+ *                         [3840][D/2] packed matrix and [3840][D/16] scales, where D is 15360/w
+ *                         rounded up to a multiple of 256 (2048 at w = 8: columns past 1920 are
+ *                         zero codes with zero scales); global scales and norm weights whole.
+ * The O and down projections add the ranks' partial sums inside the kernel (a one-shot
+ * all-reduce over NVLink peer memory, in rank order: every rank's residual_hbm gets the same
+ * bits), then apply the same epilogue on every rank. Every rank must issue the same sequence of
+ * op calls. The unit-tiled layout (g4_pack_tiles) applies to the slices as to whole matrices.
+ *
+ * Setup: every rank calls g4_tp_init, the callers exchange the G4_TP_BLOB_BYTES blobs (any
+ * transport: torch.distributed, MPI, a file), and every rank calls g4_tp_connect with all of
+ * them in rank order. The ranks must be on distinct GPUs of one node (checked: the in-kernel
+ * exchange waits on the peers' kernels, which two ranks sharing a GPU cannot guarantee). A
+ * peer that does not arrive within 2 s sets G4_DEVERR_PEER_TIMEOUT; the ranks' exchange
+ * counters are then out of step: call g4_tp_init and g4_tp_connect again on every rank. */
+#define G4_TP_BLOB_BYTES 128
+g4_status g4_tp_init(g4_ctx* ctx, int32_t rank, int32_t world, void* blob_out);
+g4_status g4_tp_connect(g4_ctx* ctx, const void* blobs);
 
 #ifdef __cplusplus
 }

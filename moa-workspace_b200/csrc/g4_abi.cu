@@ -21,7 +21,15 @@ struct g4_ctx {
   void* scratch = nullptr;
   size_t scratch_bytes = 0;
   g4::Scratch sc{};
+  size_t act_bytes = 0;
   g4::TmapCache maps;
+  // tensor parallelism (g4_tp_init / g4_tp_connect); world 1 until then
+  int tp_rank = 0, tp_world = 1;
+  bool tp_ready = true;                    // connected (a world of 1 needs no peers)
+  void* tp_buf = nullptr;                  // this rank's exchange buffer, then its epoch counters
+  void* tp_peer[g4::kMaxTp] = {};          // the peers' buffers, opened in this process
+  unsigned char tp_blob[G4_TP_BLOB_BYTES] = {0};
+  g4::TpLink tp{0, 1, {}, nullptr};
   char last_error[256] = {0};
 };
 
@@ -70,8 +78,49 @@ g4::LaunchEnv env_of(g4_ctx* ctx, void* stream) {
   env.pdl = ctx->overlap;
   env.sc = ctx->sc;
   env.maps = &ctx->maps;
+  env.tp = ctx->tp;
   return env;
 }
+
+// Ops of a tensor-parallel context run only once it is connected to its peers.
+g4_status check_tp(g4_ctx* ctx) {
+  if (ctx->tp_ready) return G4_OK;
+  return fail(ctx, G4_ERR_INVALID_ARGUMENT, "%s", "tensor-parallel context is not connected (g4_tp_connect)");
+}
+
+// Close the peers' mappings and free this rank's exchange buffer; back to a world of 1.
+cudaError_t tp_release(g4_ctx* ctx) {
+  cudaError_t first = cudaSuccess;
+  for (void*& p : ctx->tp_peer) {
+    if (p) {
+      const cudaError_t e = cudaIpcCloseMemHandle(p);
+      if (first == cudaSuccess) first = e;
+      p = nullptr;
+    }
+  }
+  if (ctx->tp_buf) {
+    const cudaError_t e = cudaFree(ctx->tp_buf);
+    if (first == cudaSuccess) first = e;
+    ctx->tp_buf = nullptr;
+  }
+  ctx->tp_rank = 0;
+  ctx->tp_world = 1;
+  ctx->tp_ready = true;
+  ctx->tp = g4::TpLink{0, 1, {}, nullptr};
+  return first;
+}
+
+// The setup blob one rank hands to the others.
+struct TpBlob {
+  uint32_t magic, version;
+  int32_t rank, world;
+  unsigned char uuid[16];      // the rank's GPU
+  cudaIpcMemHandle_t handle;   // its exchange buffer
+  uint64_t bytes;              // the buffer's size
+};
+static_assert(sizeof(TpBlob) <= G4_TP_BLOB_BYTES, "blob size");
+constexpr uint32_t kTpMagic = 0x50543447u;  // "G4TP"
+constexpr size_t kTpBufferBytes = g4::kTpExchangeWords * sizeof(unsigned long long) + 256;  // + epochs
 
 }  // namespace
 
@@ -140,6 +189,7 @@ g4_status g4_ctx_create(int device, g4_ctx** out) {
   ctx->sc.partials = reinterpret_cast<float*>(base + off_partials);
   ctx->sc.y = reinterpret_cast<uint16_t*>(base + off_y);
   ctx->sc.act = reinterpret_cast<uint16_t*>(base + off_act);
+  ctx->act_bytes = off_ss - off_act;
   ctx->sc.tile_ss = reinterpret_cast<double*>(base + off_ss);
 #ifdef G4_TRACE
   ctx->sc.trace = reinterpret_cast<uint64_t*>(base + off_trace);
@@ -153,8 +203,11 @@ g4_status g4_ctx_create(int device, g4_ctx** out) {
 g4_status g4_ctx_destroy(g4_ctx* ctx) {
   if (!ctx) return G4_ERR_INVALID_ARGUMENT;
   DeviceGuard guard(ctx->device);
-  cudaError_t e = cudaSuccess;
-  if (ctx->scratch) e = cudaFree(ctx->scratch);
+  cudaError_t e = tp_release(ctx);
+  if (ctx->scratch) {
+    const cudaError_t f = cudaFree(ctx->scratch);
+    if (e == cudaSuccess) e = f;
+  }
   delete ctx;
   return e == cudaSuccess ? G4_OK : G4_ERR_CUDA;
 }
@@ -173,10 +226,13 @@ g4_status g4_ctx_check(g4_ctx* ctx, void* stream, uint32_t* flags) {
   cudaError_t e = cudaStreamSynchronize(s);
   if (e == cudaSuccess) e = cudaMemcpy(&word, ctx->sc.err, sizeof word, cudaMemcpyDeviceToHost);
   if (e == cudaSuccess && word) e = cudaMemset(ctx->sc.err, 0, sizeof word);
-  if (e == cudaSuccess && (word & G4_DEVERR_WAIT_TIMEOUT)) {
+  if (e == cudaSuccess && (word & (G4_DEVERR_WAIT_TIMEOUT | G4_DEVERR_PEER_TIMEOUT))) {
     // an abandoned launch can leave tickets half counted: start the next call clean
     e = cudaMemset(ctx->sc.counters, 0, g4::kCounterCount * sizeof(uint32_t));
   }
+  // the ranks' exchange counters are out of step after a missed peer: refuse ops until the
+  // caller sets the group up again
+  if (word & G4_DEVERR_PEER_TIMEOUT) ctx->tp_ready = false;
   if (flags) *flags = word;
   if (e != cudaSuccess) return cuda_status(ctx, e, "g4_ctx_check");
   if (word) {
@@ -216,6 +272,7 @@ static g4_status project_qkv(bool tiled, g4_ctx* ctx, const uint16_t* x, const u
     return fail(ctx, G4_ERR_INVALID_ARGUMENT, "%s must be positive", ring_len <= 0 ? "ring_len" : "rope_rows");
   if (int64_t(rope_rows) * g4::kDs * 2 > INT32_MAX || int64_t(ring_len) * g4::kPs * 2 > INT32_MAX)
     return fail(ctx, G4_ERR_UNSUPPORTED, "%s: byte offsets would overflow i32", "ring_len/rope_rows");
+  if ((st = check_tp(ctx)) != G4_OK) return st;
   DeviceGuard guard(ctx->device);
   g4::QkvArgs a{x,        q_weight,      k_weight,  v_weight, q_weight_scale, k_weight_scale, v_weight_scale,
                 input_rms_weight, q_rms_weight, k_rms_weight, kv_offset, rope_offset, cos, sin,
@@ -231,8 +288,9 @@ g4_status g4_sliding_attention(g4_ctx* ctx, const uint16_t* q, const uint16_t* k
   if (ring_len <= 0 || ring_len % g4::attention_slot_multiple() != 0 || ring_len > g4::attention_max_ring())
     return fail(ctx, G4_ERR_UNSUPPORTED, "%s must be a positive multiple of 256, at most 8192", "ring_len");
   if (!(scale == scale)) return fail(ctx, G4_ERR_INVALID_ARGUMENT, "%s is NaN", "scale");
+  if ((st = check_tp(ctx)) != G4_OK) return st;
   DeviceGuard guard(ctx->device);
-  g4::AttnArgs a{q, k, v, mask, out_hbm, ring_len, scale};
+  g4::AttnArgs a{q, k, v, mask, out_hbm, ring_len, g4::kNs / ctx->tp_world, scale};
   return cuda_status(ctx, g4::launch_attention(a, env_of(ctx, stream)), "sliding_attention launch");
 }
 
@@ -246,6 +304,7 @@ static g4_status attention_output(bool tiled, g4_ctx* ctx, const uint16_t* x, co
                                   {o_weight_scale, "o_weight_scale"},
                                   {residual_hbm, "residual_hbm"}});
   if (st != G4_OK) return st;
+  if ((st = check_tp(ctx)) != G4_OK) return st;
   DeviceGuard guard(ctx->device);
   g4::OArgs a{x, post_attn_rms_weight, o_weight, o_weight_scale, residual_hbm, tiled};
   return cuda_status(ctx, g4::launch_o(a, env_of(ctx, stream)), "sliding_attention_output launch");
@@ -273,6 +332,7 @@ static g4_status decoder_feedforward(bool tiled, g4_ctx* ctx, uint16_t* residual
                                   {post_ff_rms_weight, "post_ff_rms_weight"},
                                   {layer_scalar, "layer_scalar"}});
   if (st != G4_OK) return st;
+  if ((st = check_tp(ctx)) != G4_OK) return st;
   DeviceGuard guard(ctx->device);
   g4::FfnArgs a{residual_hbm,      pre_ff_rms_weight, up_weight_packed, gate_weight_packed, down_weight_packed,
                 up_weight_scale,   gate_weight_scale, down_weight_scale, up_global_scale,   gate_global_scale,
@@ -345,6 +405,95 @@ g4_status g4_decoder_feedforward_tiled(g4_ctx* ctx, uint16_t* residual_hbm, cons
                              stream);
 }
 
+g4_status g4_tp_init(g4_ctx* ctx, int32_t rank, int32_t world, void* blob_out) {
+  if (!ctx) return G4_ERR_INVALID_ARGUMENT;
+  if (!blob_out) return fail(ctx, G4_ERR_INVALID_ARGUMENT, "null pointer: %s", "blob_out");
+  if (!(world == 1 || world == 2 || world == 4 || world == 8) || rank < 0 || rank >= world)
+    return fail(ctx, G4_ERR_INVALID_ARGUMENT, "%s: world must be 1, 2, 4 or 8 and 0 <= rank < world", "g4_tp_init");
+  DeviceGuard guard(ctx->device);
+  cudaError_t e = tp_release(ctx);
+  cudaDeviceProp prop;
+  if (e == cudaSuccess) e = cudaGetDeviceProperties(&prop, ctx->device);
+  if (e == cudaSuccess) e = cudaMalloc(&ctx->tp_buf, kTpBufferBytes);
+  if (e == cudaSuccess) e = cudaMemset(ctx->tp_buf, 0, kTpBufferBytes);
+  // a rank's down slice is zero-padded to whole units: the padded activation entries must read 0
+  if (e == cudaSuccess) e = cudaMemset(ctx->sc.act, 0, ctx->act_bytes);
+  TpBlob b;
+  std::memset(&b, 0, sizeof b);
+  if (e == cudaSuccess && world > 1) e = cudaIpcGetMemHandle(&b.handle, ctx->tp_buf);
+  if (e == cudaSuccess) e = cudaDeviceSynchronize();
+  if (e != cudaSuccess) {
+    tp_release(ctx);
+    return cuda_status(ctx, e, "g4_tp_init");
+  }
+  b.magic = kTpMagic;
+  b.version = 1;
+  b.rank = rank;
+  b.world = world;
+  std::memcpy(b.uuid, prop.uuid.bytes, sizeof b.uuid);
+  b.bytes = kTpBufferBytes;
+  std::memset(ctx->tp_blob, 0, sizeof ctx->tp_blob);
+  std::memcpy(ctx->tp_blob, &b, sizeof b);
+  std::memcpy(blob_out, ctx->tp_blob, G4_TP_BLOB_BYTES);
+  ctx->tp_rank = rank;
+  ctx->tp_world = world;
+  ctx->tp = g4::TpLink{0, 1, {}, nullptr};
+  ctx->tp_ready = world == 1;
+  return G4_OK;
+}
+
+g4_status g4_tp_connect(g4_ctx* ctx, const void* blobs) {
+  if (!ctx) return G4_ERR_INVALID_ARGUMENT;
+  if (!blobs) return fail(ctx, G4_ERR_INVALID_ARGUMENT, "null pointer: %s", "blobs");
+  if (!ctx->tp_buf) return fail(ctx, G4_ERR_INVALID_ARGUMENT, "%s: call g4_tp_init first", "g4_tp_connect");
+  const int world = ctx->tp_world, rank = ctx->tp_rank;
+  const unsigned char* raw = static_cast<const unsigned char*>(blobs);
+  TpBlob b[g4::kMaxTp];
+  for (int s = 0; s < world; ++s) {
+    std::memcpy(&b[s], raw + size_t(s) * G4_TP_BLOB_BYTES, sizeof(TpBlob));
+    if (b[s].magic != kTpMagic || b[s].version != 1 || b[s].rank != s || b[s].world != world ||
+        b[s].bytes != kTpBufferBytes)
+      return fail(ctx, G4_ERR_INVALID_ARGUMENT, "%s: blobs are not every rank's g4_tp_init output in rank order",
+                  "g4_tp_connect");
+  }
+  if (std::memcmp(raw + size_t(rank) * G4_TP_BLOB_BYTES, ctx->tp_blob, G4_TP_BLOB_BYTES) != 0)
+    return fail(ctx, G4_ERR_INVALID_ARGUMENT, "%s: this rank's blob is not the one g4_tp_init returned",
+                "g4_tp_connect");
+  for (int s = 0; s < world; ++s)
+    for (int t = s + 1; t < world; ++t)
+      if (std::memcmp(b[s].uuid, b[t].uuid, sizeof b[s].uuid) == 0)
+        return fail(ctx, G4_ERR_UNSUPPORTED, "%s: two ranks share one GPU (the exchange needs one GPU per rank)",
+                    "g4_tp_connect");
+  DeviceGuard guard(ctx->device);
+  for (void*& p : ctx->tp_peer) {  // a second connect replaces the first
+    if (p) cudaIpcCloseMemHandle(p);
+    p = nullptr;
+  }
+  g4::TpLink link{rank, world, {}, nullptr};
+  for (int s = 0; s < world; ++s) {
+    if (s == rank) {
+      link.slots[s] = static_cast<unsigned long long*>(ctx->tp_buf);
+      continue;
+    }
+    void* p = nullptr;
+    const cudaError_t e = cudaIpcOpenMemHandle(&p, b[s].handle, cudaIpcMemLazyEnablePeerAccess);
+    if (e != cudaSuccess) {
+      for (void*& q : ctx->tp_peer) {
+        if (q) cudaIpcCloseMemHandle(q);
+        q = nullptr;
+      }
+      return cuda_status(ctx, e, "g4_tp_connect: opening a peer's exchange buffer");
+    }
+    ctx->tp_peer[s] = p;
+    link.slots[s] = static_cast<unsigned long long*>(p);
+  }
+  link.epoch = reinterpret_cast<uint32_t*>(static_cast<unsigned char*>(ctx->tp_buf) +
+                                           g4::kTpExchangeWords * sizeof(unsigned long long));
+  ctx->tp = link;
+  ctx->tp_ready = true;
+  return G4_OK;
+}
+
 g4_status g4_pack_tiles(g4_ctx* ctx, const uint8_t* src, const uint8_t* src2, uint8_t* dst, int32_t rows,
                         int32_t row_bytes, int32_t unit_bytes, int32_t tile_rows, void* stream) {
   if (!ctx) return G4_ERR_INVALID_ARGUMENT;
@@ -375,9 +524,9 @@ g4_status g4_pack_tiles(g4_ctx* ctx, const uint8_t* src, const uint8_t* src2, ui
 
 namespace {
 
-// 192 KiB per device (the O op needs 140,032 bytes on a 148-SM B200). Zero when the module
+// 288 KiB per device (the O op needs 262,912 bytes on a 148-SM B200). Zero when the module
 // loads; the entry point zeroes the error word and the tickets again before every launch.
-constexpr size_t kStaticScratchBytes = size_t(192) << 10;
+constexpr size_t kStaticScratchBytes = size_t(288) << 10;
 constexpr int kStaticMaxDevices = 64;
 static __device__ __align__(256) uint8_t g_static_scratch[kStaticScratchBytes];
 

@@ -7,7 +7,8 @@
 //   sum[g] = sum_t p[g,t] + 1e-6
 //   out    = bf16( bf16(sum_t bf16(p[g,t]) v[t]) / sum[g] )
 //
-// kChunks CTAs per KV head (128 CTAs for the 8 heads), each owning a contiguous run of ring slots.
+// kChunks CTAs per KV head (128 CTAs for the 8 heads; a tensor-parallel rank holds 8 / n of
+// them in its cache slice), each owning a contiguous run of ring slots.
 // A CTA copies its K and V rows into shared memory with TMA boxes of up to 128 rows,
 // scores its slots for the head's two query heads, and publishes its score maximum. The rounding
 // of p to bf16 depends on the maximum over the WHOLE ring, so the head's CTAs exchange maxima
@@ -274,10 +275,11 @@ cudaError_t launch_attention(const AttnArgs& a, const LaunchEnv& env) {
   while (per % box != 0) box /= 2;
   KvMaps maps;
   cudaError_t e;
-  if ((e = env.maps->kv(a.k_cache, uint64_t(a.ring_len), kNs, kDs, uint32_t(box), &maps.k))) return e;
-  if ((e = env.maps->kv(a.v_cache, uint64_t(a.ring_len), kNs, kDs, uint32_t(box), &maps.v))) return e;
+  if (a.heads < 1 || a.heads > kNs) return cudaErrorInvalidValue;
+  if ((e = env.maps->kv(a.k_cache, uint64_t(a.ring_len), uint32_t(a.heads), kDs, uint32_t(box), &maps.k))) return e;
+  if ((e = env.maps->kv(a.v_cache, uint64_t(a.ring_len), uint32_t(a.heads), kDs, uint32_t(box), &maps.v))) return e;
   cudaLaunchConfig_t cfg = {};
-  cfg.gridDim = dim3(kNs * kChunks);
+  cfg.gridDim = dim3(a.heads * kChunks);
   cfg.blockDim = dim3(kThreads);
   cfg.dynamicSmemBytes = sizeof(AttnSmem);
   cfg.stream = env.stream;

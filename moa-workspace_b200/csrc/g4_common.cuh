@@ -23,6 +23,23 @@ constexpr int kTs = 1024;
 constexpr int kE = 32768;
 constexpr float kEps = 1e-6f;
 
+// Tensor-parallel geometry (Megatron split over NTP ranks of one node): rank r owns KV heads
+// [8r/NTP, 8(r+1)/NTP) with their query heads and ring-cache slice, the matching K columns of
+// O, FFN rows [L r/NTP, L (r+1)/NTP) of up and gate and those K columns of down. The O and
+// down outputs are the sum of the ranks' partials (one exchange per op). The down K slice is
+// zero-padded to whole 256-element units (1920 -> 2048 at NTP = 8).
+constexpr int kMaxTp = 8;
+template <int NTP>
+struct TpGeo {
+  static_assert(NTP == 1 || NTP == 2 || NTP == 4 || NTP == 8, "tensor-parallel degree");
+  static constexpr int kRanks = NTP;
+  static constexpr int kKvHeads = kNs / NTP;
+  static constexpr int kQRows = kQs / NTP;   // q projection rows (2 kKvHeads heads)
+  static constexpr int kKvRows = kPs / NTP;  // k (and v) projection rows
+  static constexpr int kFfnRows = kL / NTP;  // up / gate rows = down K
+  static constexpr int kDownK = (kFfnRows + 255) / 256 * 256;
+};
+
 // Bits of the device-resident error word (`Scratch::err`). Kernels never trap: a bad
 // device-side operand (an out-of-ring cache offset, a timed-out wait) sets a bit and the
 // affected writes are skipped; the host reads the word back with g4_ctx_check().
@@ -32,6 +49,7 @@ enum : uint32_t {
   kErrWaitTimeout = 1u << 2,
   kErrInternal = 1u << 3,  // a launch-geometry invariant did not hold (work was skipped)
   kErrNegativeScale = 1u << 4,  // an nvfp4 block scale has its sign bit set
+  kErrPeerTimeout = 1u << 5,    // a tensor-parallel peer's partial did not arrive in time
 };
 
 // Global scratch owned by a context. Counters are zero between launches: every kernel that
@@ -46,6 +64,23 @@ struct Scratch {
   uint64_t* trace;     // per-CTA phase timestamps (profiling builds only; null otherwise)
 };
 constexpr int kTileSsCount = 64;
+
+// Tensor-parallel exchange (one-shot all-reduce of the O / down partials over NVLink peer
+// memory). Every rank owns one exchange buffer, mapped into every peer's address space:
+//   words [op][parity][tile][source rank][row], 8 bytes = (epoch << 32) | f32 bits,
+// written by the source with one 64-bit store, so a reader that sees the call's epoch sees the
+// value too. Each rank counts its calls per (op, tile) in `epoch` (local, never shared): the
+// n-th call writes epoch n into parity n & 1. A source can be at most one call ahead of a
+// reader per (op, tile): its next call's exchange needs the reader's contribution of this
+// call, which the reader posts only after its previous kernels completed.
+constexpr int kTpOps = 2;      // 0: O projection, 1: FFN down
+constexpr int kTpTiles = 30;   // H / 128 output tiles
+constexpr size_t kTpExchangeWords = size_t(kTpOps) * 2 * kTpTiles * kMaxTp * 128;
+struct TpLink {
+  int rank, world;                                 // world 1: no exchange
+  unsigned long long* slots[kMaxTp];               // rank s's exchange buffer (this process's mapping)
+  uint32_t* epoch;                                 // [op][tile] calls so far (this rank's memory)
+};
 constexpr size_t kScratchHeadBytes = 256;  // the error word, padded to the scratch alignment
 constexpr int kCounterCount = 4096;
 constexpr int kBarrierO = 4000;          // grid-barrier generation counters (multiples of the grid)
@@ -65,48 +100,8 @@ __device__ __forceinline__ uint16_t f32_to_bf16(float f) {
 }
 __device__ __forceinline__ float bf16_round(float f) { return bf16_to_f32(f32_to_bf16(f)); }
 
-// Two e4m3 codes (low byte -> low half) to an exact f16x2.
-__device__ __forceinline__ uint32_t cvt_e4m3x2_f16x2(uint16_t two) {
-  uint32_t r;
-  asm("cvt.rn.f16x2.e4m3x2 %0, %1;" : "=r"(r) : "h"(two));
-  return r;
-}
-
-// Each byte of `w` holds two e2m1 codes (low nibble first); returns four exact f16x2.
-__device__ __forceinline__ void cvt_e2m1x8_f16x2(uint32_t w, uint32_t& r0, uint32_t& r1, uint32_t& r2, uint32_t& r3) {
-  asm("{\n .reg .b8 b0, b1, b2, b3;\n mov.b32 {b0, b1, b2, b3}, %4;\n"
-      " cvt.rn.f16x2.e2m1x2 %0, b0;\n cvt.rn.f16x2.e2m1x2 %1, b1;\n"
-      " cvt.rn.f16x2.e2m1x2 %2, b2;\n cvt.rn.f16x2.e2m1x2 %3, b3;\n}"
-      : "=r"(r0), "=r"(r1), "=r"(r2), "=r"(r3)
-      : "r"(w));
-}
-
-// Two bytes of e2m1 codes (four values, low nibble first) to two exact f16x2.
-__device__ __forceinline__ void cvt_e2m1x4_f16x2(uint32_t two_bytes, uint32_t& r0, uint32_t& r1) {
-  asm("{\n .reg .b8 b0, b1, b2, b3;\n mov.b32 {b0, b1, b2, b3}, %2;\n"
-      " cvt.rn.f16x2.e2m1x2 %0, b0;\n cvt.rn.f16x2.e2m1x2 %1, b1;\n}"
-      : "=r"(r0), "=r"(r1)
-      : "r"(two_bytes));
-}
-
-__device__ __forceinline__ uint32_t hmul2_u32(uint32_t a, uint32_t b) {
-  __half2 r = __hmul2(*reinterpret_cast<__half2*>(&a), *reinterpret_cast<__half2*>(&b));
-  return *reinterpret_cast<uint32_t*>(&r);
-}
-
 // f32 with the given unbiased exponent (exact power of two, normal range only).
 __device__ __forceinline__ float pow2f(int e) { return __uint_as_float(uint32_t(e + 127) << 23); }
-
-// ---------------------------------------------------------------------------------------
-// Tensor-op dot product: D(16x8,f32) += A(16x16,f16) * B(16x8,f16)
-
-__device__ __forceinline__ void mma_16816(float (&d)[4], uint32_t a0, uint32_t a1, uint32_t a2, uint32_t a3,
-                                          uint32_t b0, uint32_t b1) {
-  asm volatile(
-      "mma.sync.aligned.m16n8k16.row.col.f32.f16.f16.f32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, {%0,%1,%2,%3};"
-      : "+f"(d[0]), "+f"(d[1]), "+f"(d[2]), "+f"(d[3])
-      : "r"(a0), "r"(a1), "r"(a2), "r"(a3), "r"(b0), "r"(b1));
-}
 
 // ---------------------------------------------------------------------------------------
 // mbarrier + TMA bulk copy (global -> shared), no multicast.
@@ -210,6 +205,16 @@ __device__ __forceinline__ uint32_t atomic_add_release_gpu(uint32_t* p, uint32_t
 __device__ __forceinline__ uint32_t ld_acquire_gpu(const uint32_t* p) {
   uint32_t v;
   asm volatile("ld.acquire.gpu.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
+  return v;
+}
+
+// System-scope 64-bit accesses for the tensor-parallel exchange words (peer memory over NVLink).
+__device__ __forceinline__ void st_relaxed_sys_u64(unsigned long long* p, unsigned long long v) {
+  asm volatile("st.relaxed.sys.global.u64 [%0], %1;" ::"l"(p), "l"(v) : "memory");
+}
+__device__ __forceinline__ unsigned long long ld_relaxed_sys_u64(const unsigned long long* p) {
+  unsigned long long v;
+  asm volatile("ld.relaxed.sys.global.u64 %0, [%1];" : "=l"(v) : "l"(p) : "memory");
   return v;
 }
 
@@ -327,15 +332,6 @@ __device__ __forceinline__ void load_bf16_vec(const uint16_t* src, int k, float 
 }
 
 // Global partial slots per split tile (a tile's K range spans at most this many CTAs).
-constexpr int kMaxCtasPerGroup = 8;
-
-// Split-K ranges: warp `w` of `nw` owns chunks [begin, end) of `total`.
-__device__ __forceinline__ int64_t split_begin(int64_t w, int64_t nw, int64_t total) { return (w * total) / nw; }
-
-// True when a warp's chunk range starts at global chunk `q` (so a partial for `q` exists).
-__device__ __forceinline__ bool is_range_start(int64_t q, int64_t nw, int64_t total) {
-  const int64_t w = (q * nw + total - 1) / total;  // smallest w with w*total/nw >= q
-  return w < nw && split_begin(w, nw, total) == q;
-}
+constexpr int kMaxCtasPerGroup = 16;
 
 }  // namespace g4

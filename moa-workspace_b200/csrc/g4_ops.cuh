@@ -39,6 +39,7 @@ struct AttnArgs {
   const float* mask;
   uint16_t* out;
   int ring_len;
+  int heads;  // KV heads in the cache (8 / tensor-parallel degree)
   float scale;
 };
 
@@ -99,6 +100,7 @@ struct LaunchEnv {
   bool pdl;  // launch with programmatic stream serialization
   Scratch sc;
   TmapCache* maps;
+  TpLink tp{0, 1, {}, nullptr};  // tensor-parallel rank (world 1: the whole layer on this GPU)
 };
 
 cudaError_t prepare_proj_kernels();       // one-time attributes (dynamic shared memory)
@@ -110,7 +112,7 @@ cudaError_t launch_ffn_nvfp4(const FfnArgs& a, const LaunchEnv& env);
 
 // The O op without a context: scratch laid out as [error word | kScratchHeadBytes][tickets]
 // [split-K partials][y] at env.sc, o_scratch_bytes() in total; the tensor map is encoded on the
-// stack (env.maps is not used). Row-major weights only.
+// stack (env.maps is not used). Row-major weights, one rank (env.tp.world == 1) only.
 size_t o_scratch_bytes();
 cudaError_t launch_o_uncached(const OArgs& a, const LaunchEnv& env);
 

@@ -9,6 +9,7 @@
 // computed in f32 and rounded to bf16 once, at the same place.
 #include <cudaTypedefs.h>
 
+#include <type_traits>
 #include <utility>
 
 #include "g4_gemv.cuh"
@@ -17,13 +18,20 @@
 namespace g4 {
 namespace {
 
-// Pipeline shapes: <nvfp4, stages, K units per tile, tiles, B slots>. Units per tile = K / 256;
-// B slots >= the largest number of distinct K units one CTA's run touches on a 148-SM grid
-// (launchers grow the grid if a smaller GPU would need more).
-using QkvShape = GemvShape<false, 6, kH / kUnitK, (kQs + 2 * kPs) / kTileRows, 8>;
-using OShape = GemvShape<false, 6, kQs / kUnitK, kH / kTileRows, 4>;
-using UpGateShape = GemvShape<true, 10, kH / kUnitK, kL / 64, 15>;  // tile = 64 up rows + 64 gate rows
-using DownShape = GemvShape<true, 10, kL / kUnitK, kH / kTileRows, 13>;
+// Pipeline shapes of one tensor-parallel rank (NTP ranks; 1 = the whole layer): <nvfp4, stages,
+// K units per tile, tiles, B slots>. Units per tile = K / 256; B slots >= the largest number of
+// distinct K units one CTA's run touches on a 148-SM grid (launchers grow the grid if a smaller
+// GPU would need more).
+template <int NTP>
+struct Shapes {
+  using Geo = TpGeo<NTP>;
+  static constexpr int kOUnits = Geo::kQRows / kUnitK;
+  static constexpr int kDownUnits = Geo::kDownK / kUnitK;
+  using Qkv = GemvShape<false, 6, kH / kUnitK, (Geo::kQRows + 2 * Geo::kKvRows) / kTileRows, 8>;
+  using O = GemvShape<false, 6, kOUnits, kH / kTileRows, (kOUnits < 4 ? kOUnits : 4)>;
+  using UpGate = GemvShape<true, 10, kH / kUnitK, Geo::kFfnRows / 64, 15>;  // tile = 64 up rows + 64 gate rows
+  using Down = GemvShape<true, 10, kDownUnits, kH / kTileRows, (kDownUnits < 13 ? kDownUnits : 13)>;
+};
 
 __device__ __forceinline__ float gelu_tanh(float x) {
   // F.gelu(approximate="tanh"): 0.5 * x * (1 + tanh(sqrt(2/pi) * (x + 0.044715 * x^3)))
@@ -74,6 +82,58 @@ __device__ __forceinline__ void rms_apply16(const uint4 (&raw)[4], float inv, fl
   bf16x16_to_f32(raw[2], raw[3], g);
 #pragma unroll
   for (int j = 0; j < 16; ++j) v[j] = bf16_round((v[j] * inv) * g[j]);
+}
+
+// ---------------------------------------------------------------------------------------
+// Tensor parallelism: the one-shot all-reduce of a finished tile's partial rows (O and down).
+// Called by the 128 epilogue threads of the CTA that finishes the tile; thread `row` stores its
+// word (epoch, value) into every peer's exchange buffer with one 64-bit system-scope store,
+// waits (bounded) until every peer's word of this call is in its own buffer and adds the
+// world's partials in rank order: every rank computes the same sum, bit for bit.
+__device__ float tp_allreduce(const TpLink& tp, int op, int tile, int row, float v, uint32_t* err) {
+  if (tp.world <= 1) return v;
+  uint32_t* ep = tp.epoch + op * kTpTiles + tile;
+  const uint32_t e = __ldcg(ep) + 1u;
+  named_bar(kEpiBarrier, kEpiThreads);  // every thread has read the count before it moves on
+  if (row == 0) *ep = e;
+  const size_t base = ((size_t(op) * 2 + (e & 1u)) * kTpTiles + tile) * kMaxTp;
+  const unsigned long long word = (static_cast<unsigned long long>(e) << 32) | __float_as_uint(v);
+#pragma unroll
+  for (int s = 0; s < kMaxTp; ++s)
+    if (s < tp.world && s != tp.rank) st_relaxed_sys_u64(tp.slots[s] + (base + tp.rank) * kTileRows + row, word);
+  const unsigned long long* mine = tp.slots[tp.rank] + base * kTileRows + row;
+  float pv[kMaxTp];
+  uint32_t pending = 0u;
+#pragma unroll
+  for (int s = 0; s < kMaxTp; ++s) {
+    pv[s] = s == tp.rank ? v : 0.f;
+    if (s < tp.world && s != tp.rank) pending |= 1u << s;
+  }
+  const uint64_t t0 = globaltimer_ns();
+  while (pending) {
+#pragma unroll
+    for (int s = 0; s < kMaxTp; ++s) {
+      if (pending & (1u << s)) {
+        const unsigned long long w = ld_relaxed_sys_u64(mine + s * kTileRows);
+        if (uint32_t(w >> 32) == e) {
+          pv[s] = __uint_as_float(uint32_t(w));
+          pending &= ~(1u << s);
+        }
+      }
+    }
+    if (pending && globaltimer_ns() - t0 > kWaitLimitNs) {  // a peer never arrived: flag it, poison the row
+      atomicOr(err, kErrPeerTimeout);
+#pragma unroll
+      for (int s = 0; s < kMaxTp; ++s)
+        if (pending & (1u << s)) pv[s] = __uint_as_float(0x7fc00000u);
+      break;
+    }
+  }
+  float sum = 0.f;
+#pragma unroll
+  for (int s = 0; s < kMaxTp; ++s)
+    if (s < tp.world) sum += pv[s];
+  return sum;
 }
 
 // ---------------------------------------------------------------------------------------
@@ -185,7 +245,12 @@ struct QkvMaps {
   CUtensorMap q, k, v;
 };
 
+template <int NTP>
 struct QkvOp {
+  using QkvShape = typename Shapes<NTP>::Qkv;
+  using Geo = TpGeo<NTP>;
+  static constexpr int kQRows = Geo::kQRows, kKvRows = Geo::kKvRows;
+  static constexpr int kQHeads = kQRows / kDs, kKvHeads = Geo::kKvHeads;
   const QkvMaps* maps;
   QkvArgs a;
   Scratch sc;
@@ -194,7 +259,7 @@ struct QkvOp {
   static constexpr int kRmsGroups = kH / 16;
 
   __device__ void load_unit(uint8_t* stage, int tile, int kc, uint64_t* bar, uint64_t policy) const {
-    constexpr int kQTiles = kQs / kTileRows, kKTiles = kPs / kTileRows;
+    constexpr int kQTiles = kQRows / kTileRows, kKTiles = kKvRows / kTileRows;
     const CUtensorMap* m = tile < kQTiles ? &maps->q : (tile < kQTiles + kKTiles ? &maps->k : &maps->v);
     const int t = tile < kQTiles ? tile : (tile < kQTiles + kKTiles ? tile - kQTiles : tile - kQTiles - kKTiles);
     if (a.tiled) {
@@ -207,7 +272,8 @@ struct QkvOp {
   // units [u0, u1) of the fused q|k|v order into L2 (unit-tiled weights only)
   __device__ void prefetch_l2(int u0, int u1) const {
     if (!a.tiled) return;
-    constexpr int kQU = kQs / kTileRows * QkvShape::kUnitsPerTile, kKU = kPs / kTileRows * QkvShape::kUnitsPerTile;
+    constexpr int kQU = kQRows / kTileRows * QkvShape::kUnitsPerTile;
+    constexpr int kKU = kKvRows / kTileRows * QkvShape::kUnitsPerTile;
     constexpr uint32_t kB = QkvShape::kABytes;
     prefetch_units(a.q_weight, u0, u1 < kQU ? u1 : kQU, kB);
     prefetch_units(a.k_weight, (u0 > kQU ? u0 : kQU) - kQU, (u1 < kQU + kKU ? u1 : kQU + kKU) - kQU, kB);
@@ -216,7 +282,8 @@ struct QkvOp {
   static constexpr bool kOwnPieces = true;
   QkvStatic* st;
 
-  // the position offsets (device-resident, written before the call), then the RoPE row and the
+  // the position offsets (device-resident, written before the call; byte offsets into the whole
+  // layer's cache and table, the same on every tensor-parallel rank), then the RoPE row and the
   // per-head norm weights into shared memory, asynchronously (the epilogue threads wait for them)
   __device__ void prologue(GemvCtl&) {
     const int kv = *a.kv_offset, rope = *a.rope_offset;
@@ -270,7 +337,8 @@ struct QkvOp {
       const int last = cta_of_unit(int64_t(tile) * UPT + UPT - 1, grid, total);
       const float* part = sc.partials + size_t(tile) * kMaxCtasPerGroup * kTileRows + e;
       const int r = tile * kTileRows + e;
-      const uint16_t sb = r < kQs ? a.q_scale[r] : (r < kQs + kPs ? a.k_scale[r - kQs] : a.v_scale[r - kQs - kPs]);
+      const uint16_t sb =
+          r < kQRows ? a.q_scale[r] : (r < kQRows + kKvRows ? a.k_scale[r - kQRows] : a.v_scale[r - kQRows - kKvRows]);
       float pv[kMaxCtasPerGroup];  // every load in flight at once, then the sum in CTA order
 #pragma unroll
       for (int k = 0; k < kMaxCtasPerGroup; ++k) pv[k] = k <= last - first ? ld_cg_f32(part + k * kTileRows) : 0.f;
@@ -287,7 +355,7 @@ struct QkvOp {
     if ((threadIdx.x & 31) == 0) st->red[e / 32] = ss;
     named_bar(kEpiBarrier, kEpiThreads);
     const float inv = rms_inverse(((st->red[0] + st->red[1]) + st->red[2]) + st->red[3], kDs);
-    const bool is_q = head < kNs * kGs, is_k = !is_q && head < kNs * kGs + kNs;
+    const bool is_q = head < kQHeads, is_k = !is_q && head < kQHeads + kKvHeads;
     if (!st->kv_ok || !st->rope_ok) {
       if (e == 0) atomicOr(sc.err, (st->kv_ok ? 0u : kErrKvOffset) | (st->rope_ok ? 0u : kErrRopeOffset));
       named_bar(kEpiBarrier, kEpiThreads);
@@ -320,9 +388,9 @@ struct QkvOp {
       if (is_q)
         dst = a.q_out + head * kDs;
       else if (is_k)
-        dst = a.k_cache + size_t(st->slot) * kPs + (head - kNs * kGs) * kDs;
+        dst = a.k_cache + size_t(st->slot) * kKvRows + (head - kQHeads) * kDs;
       else
-        dst = a.v_cache + size_t(st->slot) * kPs + (head - kNs * kGs - kNs) * kDs;
+        dst = a.v_cache + size_t(st->slot) * kKvRows + (head - kQHeads - kKvHeads) * kDs;
       reinterpret_cast<uint4*>(dst)[e] = reinterpret_cast<const uint4*>(st->out)[e];
     }
     named_bar(kEpiBarrier, kEpiThreads);
@@ -333,20 +401,23 @@ struct QkvOp {
   __device__ void finish_group(const uint4 (&raw)[4], float inv, float (&v)[16]) const { rms_apply16(raw, inv, v); }
 };
 
+template <int NTP>
 __global__ void __launch_bounds__(kGemvThreads, 1) qkv_kernel(const __grid_constant__ QkvMaps maps, QkvArgs a,
                                                               Scratch sc) {
   extern __shared__ __align__(1024) uint8_t smem[];
   __shared__ QkvStatic st;
-  QkvOp op{&maps, a, sc};
+  QkvOp<NTP> op{&maps, a, sc};
   op.st = &st;
-  gemv_run<QkvShape>(op, smem, sc);
+  gemv_run<typename Shapes<NTP>::Qkv>(op, smem, sc);
   cp_async_wait_all();  // a CTA that finished no head still has the prologue's copies in flight
 }
 
 // ---------------------------------------------------------------------------------------
 // O projection + post-attention RMSNorm + residual
 
+template <int NTP>
 struct OOp {
+  using OShape = typename Shapes<NTP>::O;
   const CUtensorMap* map;
   OArgs a;
   Scratch sc;
@@ -374,19 +445,23 @@ struct OOp {
   }
   __device__ void finalize_tile(int tile, int row, float v, GemvCtl&) const {
     const int r = tile * kTileRows + row;
-    tail_record(*tail, a.post_rms, a.residual, sc, tile, row, bf16_round(v * bf16_to_f32(a.o_scale[r])));
+    const float sum = tp_allreduce(*tp, 0, tile, row, v, sc.err);  // the K slices of every rank
+    tail_record(*tail, a.post_rms, a.residual, sc, tile, row, bf16_round(sum * bf16_to_f32(a.o_scale[r])));
   }
   ResidualTail* tail;
+  const TpLink* tp;
 };
 
+template <int NTP>
 __global__ void __launch_bounds__(kGemvThreads, 1) o_kernel(const __grid_constant__ CUtensorMap map, OArgs a,
-                                                            Scratch sc) {
+                                                            Scratch sc, const __grid_constant__ TpLink tp) {
   extern __shared__ __align__(1024) uint8_t smem[];
   __shared__ ResidualTail tail;
   if (threadIdx.x == 0) tail.n = 0;  // ordered by the engine's first barrier
-  OOp op{&map, a, sc};
+  OOp<NTP> op{&map, a, sc};
   op.tail = &tail;
-  gemv_run<OShape>(op, smem, sc);
+  op.tp = &tp;
+  gemv_run<typename Shapes<NTP>::O>(op, smem, sc);
   tail_update(tail, a.residual, sc, sc.counters + kBarrierO, kH / kTileRows, nullptr);
   G4_STAMP(sc, 8);
 }
@@ -398,7 +473,9 @@ struct UpGateMaps {
   CUtensorMap up, gate, up_s, gate_s;
 };
 
+template <int NTP>
 struct UpGateOp {
+  using UpGateShape = typename Shapes<NTP>::UpGate;
   const UpGateMaps* maps;
   FfnArgs a;
   Scratch sc;
@@ -453,11 +530,12 @@ struct UpGateOp {
   }
 };
 
+template <int NTP>
 __global__ void __launch_bounds__(kGemvThreads, 1) ffn_upgate_kernel(const __grid_constant__ UpGateMaps maps, FfnArgs a,
                                                                      Scratch sc) {
   extern __shared__ __align__(1024) uint8_t smem[];
-  UpGateOp op{&maps, a, sc};
-  gemv_run<UpGateShape>(op, smem, sc);
+  UpGateOp<NTP> op{&maps, a, sc};
+  gemv_run<typename Shapes<NTP>::UpGate>(op, smem, sc);
   G4_STAMP(sc, 8);
 }
 
@@ -465,7 +543,9 @@ struct DownMaps {
   CUtensorMap w, s;
 };
 
+template <int NTP>
 struct DownOp {
+  using DownShape = typename Shapes<NTP>::Down;
   const DownMaps* maps;
   FfnArgs a;
   Scratch sc;
@@ -502,20 +582,24 @@ struct DownOp {
     bf16x16_to_f32(raw[0], raw[1], v);
   }
   __device__ void finalize_tile(int tile, int row, float v, GemvCtl&) const {
+    const float sum = tp_allreduce(*tp, 1, tile, row, v, sc.err);  // the K slices of every rank
     // GloballyScaled(nn.Linear): bf16(bf16(x @ W.T) * g)  (generate_references.py:358-413)
-    tail_record(*tail, a.post_rms, a.residual, sc, tile, row, bf16_round(bf16_round(v) * g_down));
+    tail_record(*tail, a.post_rms, a.residual, sc, tile, row, bf16_round(bf16_round(sum) * g_down));
   }
   ResidualTail* tail;
+  const TpLink* tp;
 };
 
+template <int NTP>
 __global__ void __launch_bounds__(kGemvThreads, 1) ffn_down_kernel(const __grid_constant__ DownMaps maps, FfnArgs a,
-                                                                   Scratch sc) {
+                                                                   Scratch sc, const __grid_constant__ TpLink tp) {
   extern __shared__ __align__(1024) uint8_t smem[];
   __shared__ ResidualTail tail;
   if (threadIdx.x == 0) tail.n = 0;  // ordered by the engine's first barrier
-  DownOp op{&maps, a, sc};
+  DownOp<NTP> op{&maps, a, sc};
   op.tail = &tail;
-  gemv_run<DownShape>(op, smem, sc);
+  op.tp = &tp;
+  gemv_run<typename Shapes<NTP>::Down>(op, smem, sc);
   tail_update(tail, a.residual, sc, sc.counters + kBarrierDown, kH / kTileRows, a.layer_scalar);
   G4_STAMP(sc, 8);
 }
@@ -538,58 +622,81 @@ cudaError_t launch(void (*kernel)(KArgs...), int grid, size_t smem, const Launch
   return cudaLaunchKernelEx(&cfg, kernel, std::forward<Args>(args)...);
 }
 
-// One CTA per SM, unless a smaller GPU would give a CTA more distinct K units than its B slots
-// hold (a run of n units touches min(n, units per tile) of them).
+// One CTA per SM (at most one per unit), unless a smaller GPU would give a CTA more distinct K
+// units than its B slots hold (a run of n units touches min(n, units per tile) of them).
 template <class Shape>
 int grid_for(const LaunchEnv& env) {
-  if (Shape::kBSlots >= Shape::kUnitsPerTile) return env.sm_count;
-  const int need = (Shape::kTotalUnits + Shape::kBSlots - 1) / Shape::kBSlots;
-  return env.sm_count > need ? env.sm_count : need;
+  int grid = env.sm_count < Shape::kTotalUnits ? env.sm_count : Shape::kTotalUnits;
+  if (Shape::kBSlots < Shape::kUnitsPerTile) {
+    const int need = (Shape::kTotalUnits + Shape::kBSlots - 1) / Shape::kBSlots;
+    grid = grid > need ? grid : need;
+  }
+  return grid;
 }
 
-}  // namespace
+// The kernels of one tensor-parallel degree, called as f(std::integral_constant<int, NTP>).
+template <class F>
+cudaError_t by_degree(int world, F&& f) {
+  switch (world) {
+    case 1: return f(std::integral_constant<int, 1>{});
+    case 2: return f(std::integral_constant<int, 2>{});
+    case 4: return f(std::integral_constant<int, 4>{});
+    case 8: return f(std::integral_constant<int, 8>{});
+    default: return cudaErrorInvalidValue;
+  }
+}
 
-cudaError_t prepare_proj_kernels() {
+template <int NTP>
+cudaError_t prepare_degree() {
+  using S = Shapes<NTP>;
   cudaError_t e;
-  if ((e = cudaFuncSetAttribute(qkv_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, int(QkvShape::kSmemBytes))))
+  if ((e = cudaFuncSetAttribute(qkv_kernel<NTP>, cudaFuncAttributeMaxDynamicSharedMemorySize, int(S::Qkv::kSmemBytes))))
     return e;
-  if ((e = cudaFuncSetAttribute(o_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, int(OShape::kSmemBytes))))
+  if ((e = cudaFuncSetAttribute(o_kernel<NTP>, cudaFuncAttributeMaxDynamicSharedMemorySize, int(S::O::kSmemBytes))))
     return e;
-  if ((e = cudaFuncSetAttribute(ffn_upgate_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                int(UpGateShape::kSmemBytes))))
+  if ((e = cudaFuncSetAttribute(ffn_upgate_kernel<NTP>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                int(S::UpGate::kSmemBytes))))
     return e;
-  if ((e = cudaFuncSetAttribute(ffn_down_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                int(DownShape::kSmemBytes))))
-    return e;
-  return cudaSuccess;
+  return cudaFuncSetAttribute(ffn_down_kernel<NTP>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                              int(S::Down::kSmemBytes));
 }
 
-cudaError_t launch_qkv(const QkvArgs& a, const LaunchEnv& env) {
+template <int NTP>
+cudaError_t launch_qkv_t(const QkvArgs& a, const LaunchEnv& env) {
+  using Geo = TpGeo<NTP>;
+  using Shape = typename Shapes<NTP>::Qkv;
   QkvMaps m;
   cudaError_t e;
   // unit-tiled: a matrix of R rows is [R * K / 128, 128] bytes, one 256-row box per unit
   const uint64_t cols = a.tiled ? 128 : kH, fq = a.tiled ? kH / 128 : 1;
   const uint32_t box = a.tiled ? kUnitBox : kTileRows;
-  if ((e = env.maps->u8(a.q_weight, cols, kQs * fq, 128, box, true, &m.q))) return e;
-  if ((e = env.maps->u8(a.k_weight, cols, kPs * fq, 128, box, true, &m.k))) return e;
-  if ((e = env.maps->u8(a.v_weight, cols, kPs * fq, 128, box, true, &m.v))) return e;
-  return launch(qkv_kernel, grid_for<QkvShape>(env), QkvShape::kSmemBytes, env, m, a, env.sc);  // stamps at 0
+  if ((e = env.maps->u8(a.q_weight, cols, Geo::kQRows * fq, 128, box, true, &m.q))) return e;
+  if ((e = env.maps->u8(a.k_weight, cols, Geo::kKvRows * fq, 128, box, true, &m.k))) return e;
+  if ((e = env.maps->u8(a.v_weight, cols, Geo::kKvRows * fq, 128, box, true, &m.v))) return e;
+  return launch(qkv_kernel<NTP>, grid_for<Shape>(env), Shape::kSmemBytes, env, m, a, env.sc);  // stamps at 0
 }
 
-cudaError_t launch_o(const OArgs& a, const LaunchEnv& env) {
+template <int NTP>
+cudaError_t launch_o_t(const OArgs& a, const LaunchEnv& env) {
+  constexpr int kK = TpGeo<NTP>::kQRows;  // this rank's K slice of O
+  using Shape = typename Shapes<NTP>::O;
   CUtensorMap m;
   cudaError_t e;
-  if ((e = env.maps->u8(a.o_weight, a.tiled ? 128 : kQs, a.tiled ? uint64_t(kH) * (kQs / 128) : kH, 128,
+  if ((e = env.maps->u8(a.o_weight, a.tiled ? 128 : kK, a.tiled ? uint64_t(kH) * (kK / 128) : kH, 128,
                         a.tiled ? kUnitBox : kTileRows, true, &m)))
     return e;
   Scratch sc = env.sc;
 #ifdef G4_TRACE
   if (sc.trace) sc.trace += 2 * 4096;  // profiling builds: separate stamp rows per kernel
 #endif
-  return launch(o_kernel, grid_for<OShape>(env), OShape::kSmemBytes, env, m, a, sc);
+  return launch(o_kernel<NTP>, grid_for<Shape>(env), Shape::kSmemBytes, env, m, a, sc, env.tp);
 }
 
-cudaError_t launch_ffn_nvfp4(const FfnArgs& a, const LaunchEnv& env) {
+template <int NTP>
+cudaError_t launch_ffn_t(const FfnArgs& a, const LaunchEnv& env) {
+  constexpr int kRows = TpGeo<NTP>::kFfnRows, kDownK = TpGeo<NTP>::kDownK;
+  using UG = typename Shapes<NTP>::UpGate;
+  using DN = typename Shapes<NTP>::Down;
   UpGateMaps ug;
   DownMaps dn;
   cudaError_t e;
@@ -600,19 +707,19 @@ cudaError_t launch_ffn_nvfp4(const FfnArgs& a, const LaunchEnv& env) {
     ug.gate = ug.up;
     ug.gate_s = ug.up_s = ug.up;
     dn.s = dn.w;
-    if ((e = env.maps->u8(a.up_packed, 128, uint64_t(kL) / 64 * (kH / kUnitK) * kTileRows, 128, kTileRows, true,
+    if ((e = env.maps->u8(a.up_packed, 128, uint64_t(kRows) / 64 * (kH / kUnitK) * kTileRows, 128, kTileRows, true,
                           &ug.up)))
       return e;
-    if ((e = env.maps->u8(a.down_packed, 128, uint64_t(kH) / kTileRows * (kL / kUnitK) * kTileRows, 128, kTileRows,
-                          true, &dn.w)))
+    if ((e = env.maps->u8(a.down_packed, 128, uint64_t(kH) / kTileRows * (kDownK / kUnitK) * kTileRows, 128,
+                          kTileRows, true, &dn.w)))
       return e;
   } else {
-    if ((e = env.maps->u8(a.up_packed, kH / 2, kL, 128, 64, true, &ug.up))) return e;
-    if ((e = env.maps->u8(a.gate_packed, kH / 2, kL, 128, 64, true, &ug.gate))) return e;
-    if ((e = env.maps->u8(a.up_scale, kH / 16, kL, 16, 64, false, &ug.up_s))) return e;
-    if ((e = env.maps->u8(a.gate_scale, kH / 16, kL, 16, 64, false, &ug.gate_s))) return e;
-    if ((e = env.maps->u8(a.down_packed, kL / 2, kH, 128, kTileRows, true, &dn.w))) return e;
-    if ((e = env.maps->u8(a.down_scale, kL / 16, kH, 16, kTileRows, false, &dn.s))) return e;
+    if ((e = env.maps->u8(a.up_packed, kH / 2, kRows, 128, 64, true, &ug.up))) return e;
+    if ((e = env.maps->u8(a.gate_packed, kH / 2, kRows, 128, 64, true, &ug.gate))) return e;
+    if ((e = env.maps->u8(a.up_scale, kH / 16, kRows, 16, 64, false, &ug.up_s))) return e;
+    if ((e = env.maps->u8(a.gate_scale, kH / 16, kRows, 16, 64, false, &ug.gate_s))) return e;
+    if ((e = env.maps->u8(a.down_packed, kDownK / 2, kH, 128, kTileRows, true, &dn.w))) return e;
+    if ((e = env.maps->u8(a.down_scale, kDownK / 16, kH, 16, kTileRows, false, &dn.s))) return e;
   }
   Scratch sc = env.sc;
 #ifdef G4_TRACE
@@ -620,14 +727,36 @@ cudaError_t launch_ffn_nvfp4(const FfnArgs& a, const LaunchEnv& env) {
   const int row_base = 3 + 2 * (calls++ % 2);
   if (sc.trace) sc.trace += row_base * 4096;
 #endif
-  e = launch(ffn_upgate_kernel, grid_for<UpGateShape>(env), UpGateShape::kSmemBytes, env, ug, a, sc);
+  e = launch(ffn_upgate_kernel<NTP>, grid_for<UG>(env), UG::kSmemBytes, env, ug, a, sc);
   if (e != cudaSuccess) return e;
   LaunchEnv chained = env;
   chained.pdl = true;  // the down pass prefetches its weights while the up/gate pass drains
 #ifdef G4_TRACE
   if (chained.sc.trace) chained.sc.trace += (row_base + 1) * 4096;  // profiling builds: separate stamp rows
 #endif
-  return launch(ffn_down_kernel, grid_for<DownShape>(env), DownShape::kSmemBytes, chained, dn, a, chained.sc);
+  return launch(ffn_down_kernel<NTP>, grid_for<DN>(env), DN::kSmemBytes, chained, dn, a, chained.sc, env.tp);
+}
+
+}  // namespace
+
+cudaError_t prepare_proj_kernels() {
+  cudaError_t e;
+  if ((e = prepare_degree<1>())) return e;
+  if ((e = prepare_degree<2>())) return e;
+  if ((e = prepare_degree<4>())) return e;
+  return prepare_degree<8>();
+}
+
+cudaError_t launch_qkv(const QkvArgs& a, const LaunchEnv& env) {
+  return by_degree(env.tp.world, [&](auto d) { return launch_qkv_t<decltype(d)::value>(a, env); });
+}
+
+cudaError_t launch_o(const OArgs& a, const LaunchEnv& env) {
+  return by_degree(env.tp.world, [&](auto d) { return launch_o_t<decltype(d)::value>(a, env); });
+}
+
+cudaError_t launch_ffn_nvfp4(const FfnArgs& a, const LaunchEnv& env) {
+  return by_degree(env.tp.world, [&](auto d) { return launch_ffn_t<decltype(d)::value>(a, env); });
 }
 
 // ---------------------------------------------------------------------------------------
@@ -744,11 +873,12 @@ cudaError_t TmapCache::u8(const void* base, uint64_t cols, uint64_t rows, uint32
 
 size_t o_scratch_bytes() {
   return kScratchHeadBytes + size_t(kCounterCount) * sizeof(uint32_t) +
-         size_t(OShape::kTiles) * kMaxCtasPerGroup * kTileRows * sizeof(float) + size_t(kTileSsCount) * sizeof(double);
+         size_t(Shapes<1>::O::kTiles) * kMaxCtasPerGroup * kTileRows * sizeof(float) +
+         size_t(kTileSsCount) * sizeof(double);
 }
 
 cudaError_t launch_o_uncached(const OArgs& a, const LaunchEnv& env) {
-  if (a.tiled) return cudaErrorInvalidValue;  // the reference (row-major) layout only
+  if (a.tiled || env.tp.world != 1) return cudaErrorInvalidValue;  // one rank, row-major layout only
   auto enc = encode_fn();
   if (!enc) return cudaErrorNotSupported;
   CUtensorMap m;
@@ -760,7 +890,8 @@ cudaError_t launch_o_uncached(const OArgs& a, const LaunchEnv& env) {
                          estride, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
                          CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
   if (r != CUDA_SUCCESS) return cudaErrorInvalidValue;
-  return launch(o_kernel, grid_for<OShape>(env), OShape::kSmemBytes, env, m, a, env.sc);
+  using Shape = Shapes<1>::O;
+  return launch(o_kernel<1>, grid_for<Shape>(env), Shape::kSmemBytes, env, m, a, env.sc, env.tp);
 }
 
 }  // namespace g4

@@ -22,6 +22,9 @@ DEVERR_KV_OFFSET = 1
 DEVERR_ROPE_OFFSET = 2
 DEVERR_WAIT_TIMEOUT = 4
 DEVERR_NEGATIVE_SCALE = 16
+DEVERR_PEER_TIMEOUT = 32
+
+TP_BLOB_BYTES = 128
 
 _p = ctypes.c_void_p
 _i32 = ctypes.c_int32
@@ -42,6 +45,8 @@ SIGNATURES = {
     "g4_decoder_feedforward_tiled": [_p] * 12 + [_p],
     "g4_pack_tiles": [_p, _p, _p, _p, _i32, _i32, _i32, _i32, _p],
     "g4_sliding_attention_output_noalloc": [_p] * 5 + [_p],
+    "g4_tp_init": [_p, _i32, _i32, _p],
+    "g4_tp_connect": [_p, _p],
 }
 STRING_FUNCS = {"g4_status_string": [ctypes.c_int32], "g4_last_error": [_p]}
 

@@ -21,11 +21,23 @@ from ._abi import G4Error
 H, L, NS, GS, DS, QS, PS, TS, E = 3840, 15360, 8, 2, 256, 4096, 2048, 1024, 32768
 
 
+def geometry(world: int = 1) -> dict:
+    """Per-rank sizes of a tensor-parallel split over `world` ranks (1 = the whole layer):
+    KV heads, q rows, k/v rows, FFN rows (up/gate rows = down K) and the down K slice padded to
+    whole 256-element units (include/g4b200.h, tensor parallelism)."""
+    if world not in (1, 2, 4, 8):
+        raise ValueError(f"tensor-parallel world must be 1, 2, 4 or 8, got {world}")
+    ffn = L // world
+    return {"kv_heads": NS // world, "q_rows": QS // world, "kv_rows": PS // world, "ffn_rows": ffn,
+            "down_k": -(-ffn // 256) * 256}
+
+
 class Device:
     """One GPU and its g4 context (the role of furiosa_opt_std's `Device`)."""
 
     def __init__(self, index: int = 0):
         self.index = index
+        self.rank, self.world = 0, 1
         self._ctx = ctypes.c_void_p()
         st = _abi.lib().g4_ctx_create(index, ctypes.byref(self._ctx))
         if st != _abi.G4_OK:
@@ -61,6 +73,21 @@ class Device:
     def last_error(self) -> str:
         return _abi.lib().g4_last_error(self.handle).decode()
 
+    def tp_init(self, rank: int, world: int) -> bytes:
+        """g4_tp_init: make this context rank `rank` of a tensor-parallel group of `world` GPUs;
+        returns the setup blob every other rank needs (see `g4b200.tp.connect`)."""
+        blob = ctypes.create_string_buffer(_abi.TP_BLOB_BYTES)
+        _check(self, _abi.lib().g4_tp_init(self.handle, rank, world, blob), "g4_tp_init")
+        self.rank, self.world = rank, world
+        return blob.raw
+
+    def tp_connect(self, blobs: bytes) -> None:
+        """g4_tp_connect with every rank's blob, concatenated in rank order."""
+        if len(blobs) != _abi.TP_BLOB_BYTES * self.world:
+            raise ValueError(f"tp_connect: expected {self.world} blobs of {_abi.TP_BLOB_BYTES} bytes")
+        buf = ctypes.create_string_buffer(blobs, len(blobs))
+        _check(self, _abi.lib().g4_tp_connect(self.handle, buf), "g4_tp_connect")
+
 
 def _stream_ptr(stream, device_index: int) -> ctypes.c_void_p:
     s = stream if stream is not None else torch.cuda.current_stream(device_index)
@@ -94,18 +121,21 @@ def sliding_project_qkv(device: Device, x, q_weight, k_weight, v_weight, q_weigh
                         cos, sin, k_cache, v_cache, q_out, *, tiled=False, stream=None) -> None:
     """ops::sliding_project_qkv (src/ops.rs:37-76). k_cache/v_cache: [ring, Ns, Ds]; cos/sin: [rows, Ds].
 
-    tiled=True: q/k/v weights are in the unit-tiled layout made by `pack_tiles` (TILING)."""
+    tiled=True: q/k/v weights are in the unit-tiled layout made by `pack_tiles` (TILING).
+    On a tensor-parallel device the weights, caches and q_out are this rank's slices (`geometry`)."""
     bf = torch.bfloat16
+    g = geometry(device.world)
+    qr, kr, nh = g["q_rows"], g["kv_rows"], g["kv_heads"]
     ring = k_cache.shape[0] if k_cache.dim() == 3 else -1
     rows = cos.shape[0] if cos.dim() == 2 else -1
     args = [
         _arg(x, "x", bf, (H,), device),
-        _arg(q_weight, "q_weight", _BYTE_DTYPES, (QS, H), device),
-        _arg(k_weight, "k_weight", _BYTE_DTYPES, (PS, H), device),
-        _arg(v_weight, "v_weight", _BYTE_DTYPES, (PS, H), device),
-        _arg(q_weight_scale, "q_weight_scale", bf, (QS,), device),
-        _arg(k_weight_scale, "k_weight_scale", bf, (PS,), device),
-        _arg(v_weight_scale, "v_weight_scale", bf, (PS,), device),
+        _arg(q_weight, "q_weight", _BYTE_DTYPES, (qr, H), device),
+        _arg(k_weight, "k_weight", _BYTE_DTYPES, (kr, H), device),
+        _arg(v_weight, "v_weight", _BYTE_DTYPES, (kr, H), device),
+        _arg(q_weight_scale, "q_weight_scale", bf, (qr,), device),
+        _arg(k_weight_scale, "k_weight_scale", bf, (kr,), device),
+        _arg(v_weight_scale, "v_weight_scale", bf, (kr,), device),
         _arg(input_rms_weight, "input_rms_weight", bf, (H,), device),
         _arg(q_rms_weight, "q_rms_weight", bf, (DS,), device),
         _arg(k_rms_weight, "k_rms_weight", bf, (DS,), device),
@@ -113,9 +143,9 @@ def sliding_project_qkv(device: Device, x, q_weight, k_weight, v_weight, q_weigh
         _arg(rope_offset, "rope_offset", torch.int32, (1,), device),
         _arg(cos, "cos", bf, (rows, DS), device),
         _arg(sin, "sin", bf, (rows, DS), device),
-        _arg(k_cache, "k_cache", bf, (ring, NS, DS), device),
-        _arg(v_cache, "v_cache", bf, (ring, NS, DS), device),
-        _arg(q_out, "q_out", bf, (NS, GS, DS), device),
+        _arg(k_cache, "k_cache", bf, (ring, nh, DS), device),
+        _arg(v_cache, "v_cache", bf, (ring, nh, DS), device),
+        _arg(q_out, "q_out", bf, (nh, GS, DS), device),
     ]
     fn = _abi.lib().g4_sliding_project_qkv_tiled if tiled else _abi.lib().g4_sliding_project_qkv
     st = fn(device.handle, *args, ring, rows, _stream_ptr(stream, device.index))
@@ -123,15 +153,18 @@ def sliding_project_qkv(device: Device, x, q_weight, k_weight, v_weight, q_weigh
 
 
 def sliding_attention(device: Device, q, k, v, mask, out_hbm, *, scale: float = 1.0, stream=None) -> None:
-    """ops::sliding_attention (src/ops.rs:118-128). k/v: [ring, Ns, Ds]; mask: [ring] f32."""
+    """ops::sliding_attention (src/ops.rs:118-128). k/v: [ring, Ns, Ds]; mask: [ring] f32.
+
+    On a tensor-parallel device q, k, v and out_hbm are this rank's heads (`geometry`)."""
     bf = torch.bfloat16
+    nh = geometry(device.world)["kv_heads"]
     ring = k.shape[0] if k.dim() == 3 else -1
     args = [
-        _arg(q, "q", bf, (NS, GS, DS), device),
-        _arg(k, "k", bf, (ring, NS, DS), device),
-        _arg(v, "v", bf, (ring, NS, DS), device),
+        _arg(q, "q", bf, (nh, GS, DS), device),
+        _arg(k, "k", bf, (ring, nh, DS), device),
+        _arg(v, "v", bf, (ring, nh, DS), device),
         _arg(mask, "mask", torch.float32, (ring,), device),
-        _arg(out_hbm, "out_hbm", bf, (NS, GS, DS), device),
+        _arg(out_hbm, "out_hbm", bf, (nh, GS, DS), device),
     ]
     st = _abi.lib().g4_sliding_attention(device.handle, *args, ring, float(scale), _stream_ptr(stream, device.index))
     _check(device, st, "sliding_attention")
@@ -141,12 +174,14 @@ def sliding_attention_output(device: Device, x, post_attn_rms_weight, o_weight, 
                              tiled=False, stream=None) -> None:
     """ops::sliding_attention_output (src/ops.rs:130-146). residual_hbm is updated in place.
 
-    tiled=True: o_weight is in the unit-tiled layout made by `pack_tiles` (TILING)."""
+    tiled=True: o_weight is in the unit-tiled layout made by `pack_tiles` (TILING).
+    On a tensor-parallel device x is this rank's attention output and o_weight its K columns."""
     bf = torch.bfloat16
+    g = geometry(device.world)
     args = [
-        _arg(x, "x", bf, (NS, GS, DS), device),
+        _arg(x, "x", bf, (g["kv_heads"], GS, DS), device),
         _arg(post_attn_rms_weight, "post_attn_rms_weight", bf, (H,), device),
-        _arg(o_weight, "o_weight", _BYTE_DTYPES, (H, QS), device),
+        _arg(o_weight, "o_weight", _BYTE_DTYPES, (H, g["q_rows"]), device),
         _arg(o_weight_scale, "o_weight_scale", bf, (H,), device),
         _arg(residual_hbm, "residual_hbm", bf, (H,), device),
     ]
@@ -162,17 +197,20 @@ def decoder_feedforward(device: Device, residual_hbm, pre_ff_rms_weight, up_weig
     """ops::decoder_feedforward (src/ops.rs:201-239). residual_hbm is updated in place.
 
     *_global_scale hold the reciprocal of the checkpoint's global scale (src/host/load.rs:170-190).
+    On a tensor-parallel device the up/gate rows and down columns are this rank's slices.
     """
     bf = torch.bfloat16
+    g = geometry(device.world)
+    fr, dk = g["ffn_rows"], g["down_k"]
     args = [
         _arg(residual_hbm, "residual_hbm", bf, (H,), device),
         _arg(pre_ff_rms_weight, "pre_ff_rms_weight", bf, (H,), device),
-        _arg(up_weight_packed, "up_weight_packed", torch.uint8, (L, H // 2), device),
-        _arg(gate_weight_packed, "gate_weight_packed", torch.uint8, (L, H // 2), device),
-        _arg(down_weight_packed, "down_weight_packed", torch.uint8, (H, L // 2), device),
-        _arg(up_weight_scale, "up_weight_scale", _BYTE_DTYPES, (L, H // 16), device),
-        _arg(gate_weight_scale, "gate_weight_scale", _BYTE_DTYPES, (L, H // 16), device),
-        _arg(down_weight_scale, "down_weight_scale", _BYTE_DTYPES, (H, L // 16), device),
+        _arg(up_weight_packed, "up_weight_packed", torch.uint8, (fr, H // 2), device),
+        _arg(gate_weight_packed, "gate_weight_packed", torch.uint8, (fr, H // 2), device),
+        _arg(down_weight_packed, "down_weight_packed", torch.uint8, (H, dk // 2), device),
+        _arg(up_weight_scale, "up_weight_scale", _BYTE_DTYPES, (fr, H // 16), device),
+        _arg(gate_weight_scale, "gate_weight_scale", _BYTE_DTYPES, (fr, H // 16), device),
+        _arg(down_weight_scale, "down_weight_scale", _BYTE_DTYPES, (H, dk // 16), device),
         _arg(up_global_scale, "up_global_scale", torch.float32, (1,), device),
         _arg(gate_global_scale, "gate_global_scale", torch.float32, (1,), device),
         _arg(down_global_scale, "down_global_scale", torch.float32, (1,), device),
@@ -189,13 +227,15 @@ def decoder_feedforward_tiled(device: Device, residual_hbm, pre_ff_rms_weight, u
                               stream=None) -> None:
     """decoder_feedforward on weights packed by `pack_upgate` / `tile_weight` (the GPU-native layout)."""
     bf = torch.bfloat16
+    g = geometry(device.world)
+    fr, dk = g["ffn_rows"], g["down_k"]
     args = [
         _arg(residual_hbm, "residual_hbm", bf, (H,), device),
         _arg(pre_ff_rms_weight, "pre_ff_rms_weight", bf, (H,), device),
-        _arg(up_gate_weight_tiled, "up_gate_weight_tiled", torch.uint8, (2 * L, H // 2), device),
-        _arg(down_weight_tiled, "down_weight_tiled", torch.uint8, (H, L // 2), device),
-        _arg(up_gate_scale_tiled, "up_gate_scale_tiled", _BYTE_DTYPES, (2 * L, H // 16), device),
-        _arg(down_scale_tiled, "down_scale_tiled", _BYTE_DTYPES, (H, L // 16), device),
+        _arg(up_gate_weight_tiled, "up_gate_weight_tiled", torch.uint8, (2 * fr, H // 2), device),
+        _arg(down_weight_tiled, "down_weight_tiled", torch.uint8, (H, dk // 2), device),
+        _arg(up_gate_scale_tiled, "up_gate_scale_tiled", _BYTE_DTYPES, (2 * fr, H // 16), device),
+        _arg(down_scale_tiled, "down_scale_tiled", _BYTE_DTYPES, (H, dk // 16), device),
         _arg(up_global_scale, "up_global_scale", torch.float32, (1,), device),
         _arg(gate_global_scale, "gate_global_scale", torch.float32, (1,), device),
         _arg(down_global_scale, "down_global_scale", torch.float32, (1,), device),

@@ -18,6 +18,7 @@ rounding is explicit. Citations use `FOG` = `furiosa-opt-gemma4-12B/` of the ref
 - sliding_attention           FOG/src/device/sliding/attention.rs:7-199 (op: FOG/src/ops.rs:118-128);
                               the reference's tests never pin this op, so its restatement follows
                               the device semantics and is validated against a float64 softmax.
+- *_tp                        tensor-parallel split of O and the FFN (no reference counterpart)
 
 Dot products accumulate in f32 (numpy sgemv); the reference's torch CPU kernels also
 accumulate in f32 but in their own order, so results agree to within the reference
@@ -243,6 +244,47 @@ def feedforward_fp8(residual, pre_rms_weight, up_w, gate_w, down_w, up_s, gate_s
     down = scaled_projection(act, e4m3_to_f32(down_w).reshape(hidden, inter), down_s)
     normalized = rms_norm(down, post_rms_weight)
     summed = add_bf16(residual, normalized)
+    return mul_bf16(summed, np.full(summed.shape, np.asarray(layer_scalar).reshape(-1)[0], dtype=np.uint16))
+
+
+# --- tensor parallelism (no reference counterpart: the reference runs a layer on one chip) ---
+# The O and down contractions are split over `world` K slices; each rank's f32 partial sums
+# are added in rank order and the one-chip epilogue follows. The other ops are per head or per
+# row and split without changing any result.
+
+def sliding_attention_output_tp(x_parts, post_rms_weight, o_weight_parts, o_scale, residual):
+    """sliding_attention_output with the K = 4096 contraction split over ranks: x_parts[r] is
+    rank r's attention output (bf16 bits), o_weight_parts[r] its e4m3 columns [3840, 4096/w]."""
+    acc = None
+    for x_r, w_r in zip(x_parts, o_weight_parts):
+        part = (e4m3_to_f32(w_r) @ bf16_to_f32(np.asarray(x_r).reshape(-1))).astype(np.float32)
+        acc = part if acc is None else (acc + part).astype(np.float32)
+    projected = f32_to_bf16(acc * bf16_to_f32(o_scale))
+    return add_bf16(residual, rms_norm(projected, post_rms_weight))
+
+
+def decoder_feedforward_tp(residual, pre_rms_weight, up_parts, gate_parts, down_parts, up_global, gate_global,
+                           down_global, post_rms_weight, layer_scalar, hidden=3840):
+    """decoder_feedforward with the FFN rows split over ranks. up_parts[r] / gate_parts[r] are
+    (packed [rows_r, H/2], block scales [rows_r, H/16]) and down_parts[r] (packed [H, k_r/2],
+    block scales [H, k_r/16]) with k_r >= rows_r (columns past rows_r are zero padding)."""
+    h = rms_norm(residual, pre_rms_weight)
+    acc = None
+    for (up_p, up_s), (gate_p, gate_s), (down_p, down_s) in zip(up_parts, gate_parts, down_parts):
+        rows = up_p.shape[0]
+        w_up = nvfp4_dequant(up_p, up_s, rows, hidden)
+        w_gate = nvfp4_dequant(gate_p, gate_s, rows, hidden)
+        up = f32_to_bf16(bf16_to_f32(linear_bf16(h, w_up)) * np.float32(up_global))
+        gate = f32_to_bf16(bf16_to_f32(linear_bf16(h, w_gate)) * np.float32(gate_global))
+        act = bf16_to_f32(mul_bf16(gelu_tanh(gate), up))
+        k = down_p.shape[1] * 2
+        w_down = nvfp4_dequant(down_p, down_s, hidden, k)
+        act_pad = np.zeros(k, np.float32)
+        act_pad[:rows] = act
+        part = (w_down @ act_pad).astype(np.float32)
+        acc = part if acc is None else (acc + part).astype(np.float32)
+    down = f32_to_bf16(bf16_to_f32(f32_to_bf16(acc)) * np.float32(down_global))
+    summed = add_bf16(residual, rms_norm(down, post_rms_weight))
     return mul_bf16(summed, np.full(summed.shape, np.asarray(layer_scalar).reshape(-1)[0], dtype=np.uint16))
 
 
