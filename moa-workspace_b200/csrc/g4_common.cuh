@@ -83,7 +83,7 @@ struct TpLink {
 };
 constexpr size_t kScratchHeadBytes = 256;  // the error word, padded to the scratch alignment
 constexpr int kCounterCount = 4096;
-constexpr int kBarrierO = 4000;          // grid-barrier generation counters (multiples of the grid)
+constexpr int kBarrierO = 4000;          // finished-tile counters of the residual tails (30 per call)
 constexpr int kBarrierDown = 4001;
 constexpr int kHeadCounterBase = 3968;  // 32 per-head tickets of the QKV op
 constexpr size_t kPartialFloats = size_t(1) << 21;  // 8 MiB of split-K partials

@@ -160,6 +160,51 @@ __device__ __forceinline__ void nvf4_digit_rows8(const uint4& raw, int pc, uint3
   }
 }
 
+// A finished piece of a tile (the units [.., kc] of it that this CTA ran), on the 128 epilogue
+// threads. A whole tile is final; the pieces of a tile whose K range is split across CTAs are
+// published to `partials` and the last CTA to arrive (ticket in `counters`) adds them up in CTA
+// order, so the result never depends on timing. Ops that finish their pieces themselves
+// (kOwnPieces) get them as they are.
+template <class Shape, class Op>
+__device__ void finish_piece(Op& op, GemvCtl& ctl, const Scratch& sc, uint32_t* counters, float* partials, int tile,
+                             int row, float val, int in_piece) {
+  constexpr int UPT = Shape::kUnitsPerTile;
+  const int64_t total = Shape::kTotalUnits, grid = gridDim.x;
+  if constexpr (Op::kOwnPieces) {
+    op.finish_piece(tile, row, val, in_piece, ctl);
+  } else if (in_piece == UPT) {
+    op.finalize_tile(tile, row, val, ctl);
+  } else {
+    const int first = cta_of_unit(int64_t(tile) * UPT, grid, total);
+    const int lastc = cta_of_unit(int64_t(tile) * UPT + UPT - 1, grid, total);
+    float* part = partials + size_t(tile) * kMaxCtasPerGroup * kTileRows;
+    if (lastc - first >= kMaxCtasPerGroup) {  // launchers keep every tile within the slots
+      if (row == 0) atomicOr(sc.err, kErrInternal);
+      return;
+    }
+    part[(blockIdx.x - first) * kTileRows + row] = val;
+    named_bar(kEpiBarrier, kEpiThreads);
+    if (row == 0) {
+      const uint32_t before = atomic_add_acq_rel_gpu(counters + tile, uint32_t(in_piece));
+      const bool done = before + uint32_t(in_piece) == uint32_t(UPT);
+      if (done) counters[tile] = 0;
+      ctl.bcast = done ? 1u : 0u;
+    }
+    __syncwarp();
+    named_bar(kEpiBarrier, kEpiThreads);
+    if (ctl.bcast) {
+      float pv[kMaxCtasPerGroup];  // every load in flight at once, then the sum in CTA order
+#pragma unroll
+      for (int k = 0; k < kMaxCtasPerGroup; ++k) pv[k] = k <= lastc - first ? ld_cg_f32(part + k * kTileRows + row) : 0.f;
+      float tot = 0.f;
+#pragma unroll
+      for (int k = 0; k < kMaxCtasPerGroup; ++k)
+        if (k <= lastc - first) tot += pv[k];
+      op.finalize_tile(tile, row, tot, ctl);
+    }
+  }
+}
+
 // Engine driver. `op` supplies:
 //   void load_unit(uint8_t* stage, int tile, int kc, uint64_t* bar, uint64_t policy) const  (TMA)
 //   void load_scales(uint8_t* dst, int tile, int kc, uint64_t* bar, uint64_t policy) const (nvfp4)
@@ -573,42 +618,7 @@ __device__ void gemv_run(Op& op, uint8_t* smem_raw, const Scratch& sc) {
 #ifdef G4_TRACE
       if (sc.trace && blockIdx.x == 0 && i < 64 && row == 0) sc.trace[3192 + i] = globaltimer_ns();
 #endif
-      const float val = acc;
-      if constexpr (Op::kOwnPieces) {
-        op.finish_piece(tile, row, val, in_piece, ctl);
-      } else if (in_piece == UPT) {
-        op.finalize_tile(tile, row, val, ctl);
-      } else {
-        // the tile's K range is split across CTAs: publish, the last to arrive adds them up
-        const int first = cta_of_unit(int64_t(tile) * UPT, grid, total);
-        const int lastc = cta_of_unit(int64_t(tile) * UPT + UPT - 1, grid, total);
-        float* part = sc.partials + size_t(tile) * kMaxCtasPerGroup * kTileRows;
-        if (lastc - first >= kMaxCtasPerGroup) {  // cannot happen for the shapes launched here
-          if (row == 0) atomicOr(sc.err, kErrInternal);
-        } else {
-          part[(blockIdx.x - first) * kTileRows + row] = val;
-          named_bar(kEpiBarrier, kEpiThreads);
-          if (row == 0) {
-            const uint32_t before = atomic_add_acq_rel_gpu(sc.counters + tile, uint32_t(in_piece));
-            const bool done = before + uint32_t(in_piece) == uint32_t(UPT);
-            if (done) sc.counters[tile] = 0;
-            ctl.bcast = done ? 1u : 0u;
-          }
-          __syncwarp();
-          named_bar(kEpiBarrier, kEpiThreads);
-          if (ctl.bcast) {
-            float pv[kMaxCtasPerGroup];  // every load in flight at once, then the sum in CTA order
-#pragma unroll
-            for (int k = 0; k < kMaxCtasPerGroup; ++k)
-              pv[k] = k <= lastc - first ? ld_cg_f32(part + k * kTileRows + row) : 0.f;
-            float tot = 0.f;
-#pragma unroll
-            for (int k = 0; k < kMaxCtasPerGroup; ++k)
-              if (k <= lastc - first) tot += pv[k];
-            op.finalize_tile(tile, row, tot, ctl);
-          }
-        }
-      }
+      finish_piece<Shape>(op, ctl, sc, sc.counters, sc.partials, tile, row, acc, in_piece);
       acc = 0.f;
       in_piece = 0;
     }

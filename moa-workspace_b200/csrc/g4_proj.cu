@@ -139,11 +139,12 @@ __device__ float tp_allreduce(const TpLink& tp, int op, int tile, int row, float
 // ---------------------------------------------------------------------------------------
 // Post-RMSNorm + residual (O and FFN down): residual <- bf16(residual + RMSNorm_gamma(y)) [then
 // bf16(. * layer_scalar)] over the H outputs. The statistic needs every output, so each CTA that
-// finishes a tile keeps its 128 values of y in shared memory and publishes their sum of squares;
-// after a grid-wide barrier every CTA reads the 30 sums (fixed order) and updates its own rows.
-// The barrier is safe because the grid has one CTA per SM and all of them become resident
-// (the next kernel cannot take an SM before this one's CTAs have all started); its wait is
-// bounded.
+// finishes a tile keeps its 128 values of y in shared memory and publishes their sum of squares.
+// Only those CTAs (at most one per tile) wait: each adds its tile count to a counter, waits until
+// all 30 tiles of this call are counted, reads the 30 sums (fixed order) and updates its own
+// rows. Every other CTA leaves at once, so the next kernel's CTAs can take its SM and start their
+// weight copies during the tail. The finishing CTAs are all resident (each is running when it
+// arrives); the wait is bounded.
 
 constexpr int kMaxFinTiles = 4;  // tiles one CTA can finish (it overlaps at most 3 here)
 
@@ -178,15 +179,17 @@ __device__ void tail_record(ResidualTail& t, const uint16_t* gamma, const uint16
   named_bar(kEpiBarrier, kEpiThreads);
 }
 
-// Whole CTA, after gemv_run: the grid barrier, then the update of the recorded rows.
+// Whole CTA, after gemv_run: a CTA that finished tiles waits for every tile of the call (the
+// counter grows by `tiles` per call), then updates its recorded rows; the others return.
 __device__ void tail_update(ResidualTail& t, uint16_t* residual, const Scratch& sc, uint32_t* barrier, int tiles,
                             const uint16_t* layer_scalar) {
   const float lam = layer_scalar ? bf16_to_f32(layer_scalar[0]) : 1.0f;
   cp_async_wait_all();
   __syncthreads();  // every record (and tile_ss store) of this CTA precedes the arrival
+  if (t.n == 0) return;  // CTA-uniform: nothing of this CTA's waits on the statistic
   if (threadIdx.x == 0) {
-    const uint32_t old = atomic_add_release_gpu(barrier, 1u);
-    const uint32_t target = old - old % gridDim.x + gridDim.x;
+    const uint32_t old = atomic_add_release_gpu(barrier, uint32_t(t.n));
+    const uint32_t target = old - old % uint32_t(tiles) + uint32_t(tiles);
     const uint64_t t0 = globaltimer_ns();
     while (int32_t(ld_acquire_gpu(barrier) - target) < 0) {
       if (globaltimer_ns() - t0 > kWaitLimitNs) {
