@@ -166,7 +166,7 @@ g4_status g4_ctx_create(int device, g4_ctx** out) {
   const size_t off_y = off_partials + g4::kPartialFloats * sizeof(float);
   const size_t off_act = off_y + g4::kYElems * sizeof(uint16_t);
   const size_t off_ss = off_act + size_t(64) * g4::kL * sizeof(uint16_t);
-  const size_t off_trace = off_ss + size_t(g4::kTileSsCount) * sizeof(double);
+  const size_t off_trace = off_ss + g4::kTileSsBytes;
 #ifdef G4_TRACE
   const size_t total = off_trace + size_t(65536 + 4096 * 32 * 8) * sizeof(uint64_t);
 #else
@@ -190,7 +190,7 @@ g4_status g4_ctx_create(int device, g4_ctx** out) {
   ctx->sc.y = reinterpret_cast<uint16_t*>(base + off_y);
   ctx->sc.act = reinterpret_cast<uint16_t*>(base + off_act);
   ctx->act_bytes = off_ss - off_act;
-  ctx->sc.tile_ss = reinterpret_cast<double*>(base + off_ss);
+  ctx->sc.tile_ss = reinterpret_cast<unsigned long long*>(base + off_ss);
 #ifdef G4_TRACE
   ctx->sc.trace = reinterpret_cast<uint64_t*>(base + off_trace);
 #else
@@ -227,8 +227,10 @@ g4_status g4_ctx_check(g4_ctx* ctx, void* stream, uint32_t* flags) {
   if (e == cudaSuccess) e = cudaMemcpy(&word, ctx->sc.err, sizeof word, cudaMemcpyDeviceToHost);
   if (e == cudaSuccess && word) e = cudaMemset(ctx->sc.err, 0, sizeof word);
   if (e == cudaSuccess && (word & (G4_DEVERR_WAIT_TIMEOUT | G4_DEVERR_PEER_TIMEOUT))) {
-    // an abandoned launch can leave tickets half counted: start the next call clean
+    // an abandoned launch can leave tickets half counted: start the next call clean (the
+    // epoch-tagged tile sums too, as the epochs restart)
     e = cudaMemset(ctx->sc.counters, 0, g4::kCounterCount * sizeof(uint32_t));
+    if (e == cudaSuccess) e = cudaMemset(ctx->sc.tile_ss, 0, g4::kTileSsBytes);
   }
   // the ranks' exchange counters are out of step after a missed peer: refuse ops until the
   // caller sets the group up again
@@ -524,7 +526,7 @@ g4_status g4_pack_tiles(g4_ctx* ctx, const uint8_t* src, const uint8_t* src2, ui
 
 namespace {
 
-// 288 KiB per device (the O op needs 262,912 bytes on a 148-SM B200). Zero when the module
+// 288 KiB per device (the O op needs 263,424 bytes on a 148-SM B200). Zero when the module
 // loads; the entry point zeroes the error word and the tickets again before every launch.
 constexpr size_t kStaticScratchBytes = size_t(288) << 10;
 constexpr int kStaticMaxDevices = 64;
@@ -581,8 +583,8 @@ g4_status g4_sliding_attention_output_noalloc(const uint16_t* x, const uint16_t*
   if ((st = static_setup(dev, &base, &sms)) != G4_OK) return st;
 
   const size_t off_counters = g4::kScratchHeadBytes;
-  const size_t off_partials = off_counters + size_t(g4::kCounterCount) * sizeof(uint32_t);
-  const size_t off_ss = need - size_t(g4::kTileSsCount) * sizeof(double);  // the last region
+  const size_t off_ss = off_counters + size_t(g4::kCounterCount) * sizeof(uint32_t);
+  const size_t off_partials = off_ss + g4::kTileSsBytes;
   g4::LaunchEnv env;
   env.device = dev;
   env.sm_count = sms;
@@ -593,11 +595,11 @@ g4_status g4_sliding_attention_output_noalloc(const uint16_t* x, const uint16_t*
   env.sc.partials = reinterpret_cast<float*>(base + off_partials);
   env.sc.y = nullptr;
   env.sc.act = nullptr;
-  env.sc.tile_ss = reinterpret_cast<double*>(base + off_ss);
+  env.sc.tile_ss = reinterpret_cast<unsigned long long*>(base + off_ss);
   env.sc.trace = nullptr;
   env.maps = nullptr;
-  // the error word and every ticket (the grid-barrier counter included) must be zero when the
-  // kernel starts
+  // the error word, every ticket and epoch counter, and the epoch-tagged tile sums must be zero
+  // when the kernel starts
   if (cudaMemsetAsync(base, 0, off_partials, env.stream) != cudaSuccess) return G4_ERR_CUDA;
   const g4::OArgs a{x, post_attn_rms_weight, o_weight, o_weight_scale, residual_hbm, false};
   return g4::launch_o_uncached(a, env) == cudaSuccess ? G4_OK : G4_ERR_CUDA;

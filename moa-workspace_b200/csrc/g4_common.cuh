@@ -60,10 +60,12 @@ struct Scratch {
   float* partials;     // split-K partial row sums
   uint16_t* y;         // bf16 projected rows awaiting a grid-level epilogue
   uint16_t* act;       // bf16 GeGLU activation [M][L]
-  double* tile_ss;     // per output tile: sum of squares of its bf16 rows (kTileSsCount)
+  unsigned long long* tile_ss;  // per output tile: sum of squares of its bf16 rows, as two words
+                                // (epoch << 32 | low / high half of the f64), kTileSsCount tiles
   uint64_t* trace;     // per-CTA phase timestamps (profiling builds only; null otherwise)
 };
 constexpr int kTileSsCount = 64;
+constexpr size_t kTileSsBytes = size_t(kTileSsCount) * 2 * sizeof(unsigned long long);
 
 // Tensor-parallel exchange (one-shot all-reduce of the O / down partials over NVLink peer
 // memory). Every rank owns one exchange buffer, mapped into every peer's address space:
@@ -83,8 +85,8 @@ struct TpLink {
 };
 constexpr size_t kScratchHeadBytes = 256;  // the error word, padded to the scratch alignment
 constexpr int kCounterCount = 4096;
-constexpr int kBarrierO = 4000;          // finished-tile counters of the residual tails (30 per call)
-constexpr int kBarrierDown = 4001;
+constexpr int kTailEpochO = 3840;        // residual tails: calls so far, per output tile (30 each)
+constexpr int kTailEpochDown = 3872;
 constexpr int kHeadCounterBase = 3968;  // 32 per-head tickets of the QKV op
 constexpr size_t kPartialFloats = size_t(1) << 21;  // 8 MiB of split-K partials
 constexpr size_t kYElems = 65536;
@@ -215,6 +217,15 @@ __device__ __forceinline__ void st_relaxed_sys_u64(unsigned long long* p, unsign
 __device__ __forceinline__ unsigned long long ld_relaxed_sys_u64(const unsigned long long* p) {
   unsigned long long v;
   asm volatile("ld.relaxed.sys.global.u64 %0, [%1];" : "=l"(v) : "l"(p) : "memory");
+  return v;
+}
+// The same at GPU scope (words other CTAs of this GPU write).
+__device__ __forceinline__ void st_relaxed_gpu_u64(unsigned long long* p, unsigned long long v) {
+  asm volatile("st.relaxed.gpu.global.u64 [%0], %1;" ::"l"(p), "l"(v) : "memory");
+}
+__device__ __forceinline__ unsigned long long ld_relaxed_gpu_u64(const unsigned long long* p) {
+  unsigned long long v;
+  asm volatile("ld.relaxed.gpu.global.u64 %0, [%1];" : "=l"(v) : "l"(p) : "memory");
   return v;
 }
 

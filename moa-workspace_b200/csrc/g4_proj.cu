@@ -139,12 +139,18 @@ __device__ float tp_allreduce(const TpLink& tp, int op, int tile, int row, float
 // ---------------------------------------------------------------------------------------
 // Post-RMSNorm + residual (O and FFN down): residual <- bf16(residual + RMSNorm_gamma(y)) [then
 // bf16(. * layer_scalar)] over the H outputs. The statistic needs every output, so each CTA that
-// finishes a tile keeps its 128 values of y in shared memory and publishes their sum of squares.
-// Only those CTAs (at most one per tile) wait: each adds its tile count to a counter, waits until
-// all 30 tiles of this call are counted, reads the 30 sums (fixed order) and updates its own
-// rows. Every other CTA leaves at once, so the next kernel's CTAs can take its SM and start their
-// weight copies during the tail. The finishing CTAs are all resident (each is running when it
-// arrives); the wait is bounded.
+// finishes a tile keeps its 128 values of y in shared memory and publishes their sum of squares
+// as two 64-bit words tagged with the call's epoch (epoch << 32 | half of the f64): a reader that
+// sees this call's epoch in both words has the sum, with no flag or fence. Only those CTAs (at
+// most one per tile) wait: they poll the 30 tiles' words, add the sums in a fixed order and update
+// their own rows. Every other CTA leaves at once, so the next kernel's CTAs can take its SM and
+// start their weight copies during the tail. The finishing CTAs are all resident (each is running
+// when it publishes); the wait is bounded.
+//
+// The epoch is the number of calls so far. Each tile keeps its own count (in `epochs`), written
+// only by the CTA that finishes the tile; every CTA reads the count of the first tile of its own
+// run after the dependency wait, before it publishes anything, so that tile cannot have been
+// finished yet in this call and every tile's count is the same.
 
 constexpr int kMaxFinTiles = 4;  // tiles one CTA can finish (it overlaps at most 3 here)
 
@@ -158,10 +164,21 @@ struct ResidualTail {
   double ss[kTileSsCount];
 };
 
+// The tile of this CTA's first unit (the engine's contiguous split of Shape's units).
+template <class Shape>
+__device__ __forceinline__ int first_tile() {
+  return int(int64_t(blockIdx.x) * Shape::kTotalUnits / gridDim.x) / Shape::kUnitsPerTile;
+}
+
+// The epoch of this call for a CTA whose run starts in `first_tile` (all threads may call it).
+__device__ __forceinline__ uint32_t tail_epoch(const uint32_t* epochs, int first_tile) {
+  return __ldcg(epochs + first_tile) + 1u;
+}
+
 // Called by the 128 epilogue threads when a tile is final: record it and publish its sum of
-// squares (f64, rows in order over the four warps).
+// squares (f64, rows in order over the four warps) with the call's epoch.
 __device__ void tail_record(ResidualTail& t, const uint16_t* gamma, const uint16_t* residual, const Scratch& sc,
-                            int tile, int row, float y) {
+                            uint32_t* epochs, uint32_t epoch, int tile, int row, float y) {
   const int f = t.n;
   t.y[f][row] = y;
   if (row < 16) {  // 16 x 16 bytes each, in flight while the kernel goes on
@@ -172,37 +189,42 @@ __device__ void tail_record(ResidualTail& t, const uint16_t* gamma, const uint16
   if ((threadIdx.x & 31) == 0) t.red[row / 32] = ss;
   named_bar(kEpiBarrier, kEpiThreads);
   if (row == 0) {
-    sc.tile_ss[tile] = ((t.red[0] + t.red[1]) + t.red[2]) + t.red[3];
+    const double sum = ((t.red[0] + t.red[1]) + t.red[2]) + t.red[3];
+    const unsigned long long bits = static_cast<unsigned long long>(__double_as_longlong(sum));
+    const unsigned long long tag = static_cast<unsigned long long>(epoch) << 32;
+    st_relaxed_gpu_u64(sc.tile_ss + 2 * tile, tag | (bits & 0xffffffffull));
+    st_relaxed_gpu_u64(sc.tile_ss + 2 * tile + 1, tag | (bits >> 32));
+    epochs[tile] = epoch;
     t.tile[f] = tile;
     t.n = f + 1;
   }
   named_bar(kEpiBarrier, kEpiThreads);
 }
 
-// Whole CTA, after gemv_run: a CTA that finished tiles waits for every tile of the call (the
-// counter grows by `tiles` per call), then updates its recorded rows; the others return.
-__device__ void tail_update(ResidualTail& t, uint16_t* residual, const Scratch& sc, uint32_t* barrier, int tiles,
+// Whole CTA, after gemv_run: a CTA that finished tiles waits for every tile's sum of this call,
+// then updates its recorded rows; the others return.
+__device__ void tail_update(ResidualTail& t, uint16_t* residual, const Scratch& sc, uint32_t epoch, int tiles,
                             const uint16_t* layer_scalar) {
   const float lam = layer_scalar ? bf16_to_f32(layer_scalar[0]) : 1.0f;
   cp_async_wait_all();
-  __syncthreads();  // every record (and tile_ss store) of this CTA precedes the arrival
+  __syncthreads();  // t.n is final
   if (t.n == 0) return;  // CTA-uniform: nothing of this CTA's waits on the statistic
-  if (threadIdx.x == 0) {
-    const uint32_t old = atomic_add_release_gpu(barrier, uint32_t(t.n));
-    const uint32_t target = old - old % uint32_t(tiles) + uint32_t(tiles);
+  if (threadIdx.x < tiles) {  // thread i polls tile i's two words
+    const unsigned long long* w = sc.tile_ss + 2 * threadIdx.x;
+    unsigned long long lo = ld_relaxed_gpu_u64(w), hi = ld_relaxed_gpu_u64(w + 1);
     const uint64_t t0 = globaltimer_ns();
-    while (int32_t(ld_acquire_gpu(barrier) - target) < 0) {
+    while (uint32_t(lo >> 32) != epoch || uint32_t(hi >> 32) != epoch) {
       if (globaltimer_ns() - t0 > kWaitLimitNs) {
         atomicOr(sc.err, kErrWaitTimeout);
         break;
       }
-      __nanosleep(32);
+      lo = ld_relaxed_gpu_u64(w);
+      hi = ld_relaxed_gpu_u64(w + 1);
     }
+    t.ss[threadIdx.x] = __longlong_as_double(static_cast<long long>((hi << 32) | (lo & 0xffffffffull)));
   }
   __syncthreads();
   G4_STAMP(sc, 12);
-  if (threadIdx.x < tiles) t.ss[threadIdx.x] = __ldcg(sc.tile_ss + threadIdx.x);
-  __syncthreads();
   double sum = 0.0;
   for (int i = 0; i < tiles; ++i) sum += t.ss[i];  // fixed order: identical in every CTA
   const float inv = rms_inverse(sum, kH);
@@ -440,7 +462,7 @@ struct OOp {
   __device__ void prefetch_l2(int u0, int u1) const {
     if (a.tiled) prefetch_units(a.o_weight, u0, u1, OShape::kABytes);
   }
-  __device__ void prologue(GemvCtl&) {}
+  __device__ void prologue(GemvCtl&) { epoch = tail_epoch(sc.counters + kTailEpochO, first_tile<OShape>()); }
   __device__ void load_static(int, uint4 (&)[4]) const {}
   __device__ void load_group(int g, uint4 (&raw)[4]) const { load_group_cg(a.x, g, raw); }
   __device__ void finish_group(const uint4 (&raw)[4], float, float (&v)[16]) const {
@@ -449,10 +471,12 @@ struct OOp {
   __device__ void finalize_tile(int tile, int row, float v, GemvCtl&) const {
     const int r = tile * kTileRows + row;
     const float sum = tp_allreduce(*tp, 0, tile, row, v, sc.err);  // the K slices of every rank
-    tail_record(*tail, a.post_rms, a.residual, sc, tile, row, bf16_round(sum * bf16_to_f32(a.o_scale[r])));
+    tail_record(*tail, a.post_rms, a.residual, sc, sc.counters + kTailEpochO, epoch, tile, row,
+                bf16_round(sum * bf16_to_f32(a.o_scale[r])));
   }
   ResidualTail* tail;
   const TpLink* tp;
+  uint32_t epoch = 0;  // this call's, for the residual tail
 };
 
 template <int NTP>
@@ -465,7 +489,7 @@ __global__ void __launch_bounds__(kGemvThreads, 1) o_kernel(const __grid_constan
   op.tail = &tail;
   op.tp = &tp;
   gemv_run<typename Shapes<NTP>::O>(op, smem, sc);
-  tail_update(tail, a.residual, sc, sc.counters + kBarrierO, kH / kTileRows, nullptr);
+  tail_update(tail, a.residual, sc, op.epoch, kH / kTileRows, nullptr);
   G4_STAMP(sc, 8);
 }
 
@@ -578,7 +602,10 @@ struct DownOp {
     prefetch_units(a.down_packed, u0, u1, DownShape::kABytes);
     prefetch_units(a.down_scale, u0, u1, DownShape::kScaleBytes);
   }
-  __device__ void prologue(GemvCtl&) { g_down = *a.down_global; }
+  __device__ void prologue(GemvCtl&) {
+    g_down = *a.down_global;
+    epoch = tail_epoch(sc.counters + kTailEpochDown, first_tile<DownShape>());
+  }
   __device__ void load_static(int, uint4 (&)[4]) const {}
   __device__ void load_group(int g, uint4 (&raw)[4]) const { load_group_cg(sc.act, g, raw); }
   __device__ void finish_group(const uint4 (&raw)[4], float, float (&v)[16]) const {
@@ -587,10 +614,12 @@ struct DownOp {
   __device__ void finalize_tile(int tile, int row, float v, GemvCtl&) const {
     const float sum = tp_allreduce(*tp, 1, tile, row, v, sc.err);  // the K slices of every rank
     // GloballyScaled(nn.Linear): bf16(bf16(x @ W.T) * g)  (generate_references.py:358-413)
-    tail_record(*tail, a.post_rms, a.residual, sc, tile, row, bf16_round(bf16_round(sum) * g_down));
+    tail_record(*tail, a.post_rms, a.residual, sc, sc.counters + kTailEpochDown, epoch, tile, row,
+                bf16_round(bf16_round(sum) * g_down));
   }
   ResidualTail* tail;
   const TpLink* tp;
+  uint32_t epoch = 0;  // this call's, for the residual tail
 };
 
 template <int NTP>
@@ -603,7 +632,7 @@ __global__ void __launch_bounds__(kGemvThreads, 1) ffn_down_kernel(const __grid_
   op.tail = &tail;
   op.tp = &tp;
   gemv_run<typename Shapes<NTP>::Down>(op, smem, sc);
-  tail_update(tail, a.residual, sc, sc.counters + kBarrierDown, kH / kTileRows, a.layer_scalar);
+  tail_update(tail, a.residual, sc, op.epoch, kH / kTileRows, a.layer_scalar);
   G4_STAMP(sc, 8);
 }
 
@@ -875,9 +904,8 @@ cudaError_t TmapCache::u8(const void* base, uint64_t cols, uint64_t rows, uint32
 // O projection on scratch the caller provides, with nothing cached or allocated
 
 size_t o_scratch_bytes() {
-  return kScratchHeadBytes + size_t(kCounterCount) * sizeof(uint32_t) +
-         size_t(Shapes<1>::O::kTiles) * kMaxCtasPerGroup * kTileRows * sizeof(float) +
-         size_t(kTileSsCount) * sizeof(double);
+  return kScratchHeadBytes + size_t(kCounterCount) * sizeof(uint32_t) + kTileSsBytes +
+         size_t(Shapes<1>::O::kTiles) * kMaxCtasPerGroup * kTileRows * sizeof(float);
 }
 
 cudaError_t launch_o_uncached(const OArgs& a, const LaunchEnv& env) {
