@@ -158,13 +158,11 @@ g4_status g4_decoder_feedforward_tiled(g4_ctx* ctx, uint16_t* residual_hbm, cons
  * process under a fixed device-memory budget, or a latency-critical thread where an allocation
  * (and the synchronisation cudaMalloc/cudaFree may imply) is not acceptable.
  * Arguments and result are those of g4_sliding_attention_output on reference-layout weights,
- * on the CURRENT device and `stream`. The op's scratch (error word, tickets and epoch counters,
- * per-tile sums of squares, split-K partial sums: 263,424 bytes on a B200) lives in one
- * file-scope 288 KiB block of static device memory in this library, one per device. Returns
- * G4_ERR_UNSUPPORTED if a GPU
- * would need more than that, or is not sm_100. The error word, tickets, epoch counters and tile
- * sums must be zero when the kernel starts: the call zeroes them with cudaMemsetAsync on
- * `stream` before each launch.
+ * on the CURRENT device and `stream`. The op's scratch (error word, epoch counters, per-tile sums
+ * of squares, split-K partial sums: 510,208 bytes on a B200) lives in one file-scope 512 KiB
+ * block of static device memory in this library, one per device. Returns G4_ERR_UNSUPPORTED if
+ * a GPU would need more than that, or is not sm_100. The block must be zero when the kernel
+ * starts: the call zeroes it with cudaMemsetAsync on `stream` before each launch.
  * The first call on a device looks up the block's address (cudaGetSymbolAddress, which may load
  * the module) and sets kernel attributes: make that first call before any stream capture that
  * should contain this op. The block is shared by every call on the device, so two calls whose

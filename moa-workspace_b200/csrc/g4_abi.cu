@@ -228,9 +228,10 @@ g4_status g4_ctx_check(g4_ctx* ctx, void* stream, uint32_t* flags) {
   if (e == cudaSuccess && word) e = cudaMemset(ctx->sc.err, 0, sizeof word);
   if (e == cudaSuccess && (word & (G4_DEVERR_WAIT_TIMEOUT | G4_DEVERR_PEER_TIMEOUT))) {
     // an abandoned launch can leave tickets half counted: start the next call clean (the
-    // epoch-tagged tile sums too, as the epochs restart)
+    // epoch-tagged tile sums and split-K words too, as the epochs restart)
     e = cudaMemset(ctx->sc.counters, 0, g4::kCounterCount * sizeof(uint32_t));
     if (e == cudaSuccess) e = cudaMemset(ctx->sc.tile_ss, 0, g4::kTileSsBytes);
+    if (e == cudaSuccess) e = cudaMemset(ctx->sc.partials, 0, g4::kPartialFloats * sizeof(float));
   }
   // the ranks' exchange counters are out of step after a missed peer: refuse ops until the
   // caller sets the group up again
@@ -526,9 +527,9 @@ g4_status g4_pack_tiles(g4_ctx* ctx, const uint8_t* src, const uint8_t* src2, ui
 
 namespace {
 
-// 288 KiB per device (the O op needs 263,424 bytes on a 148-SM B200). Zero when the module
-// loads; the entry point zeroes the error word and the tickets again before every launch.
-constexpr size_t kStaticScratchBytes = size_t(288) << 10;
+// 512 KiB per device (the O op needs 510,208 bytes on a 148-SM B200). The entry point zeroes
+// the whole block before every launch, so every call starts at epoch 1 with no stale word.
+constexpr size_t kStaticScratchBytes = size_t(512) << 10;
 constexpr int kStaticMaxDevices = 64;
 static __device__ __align__(256) uint8_t g_static_scratch[kStaticScratchBytes];
 
@@ -598,9 +599,9 @@ g4_status g4_sliding_attention_output_noalloc(const uint16_t* x, const uint16_t*
   env.sc.tile_ss = reinterpret_cast<unsigned long long*>(base + off_ss);
   env.sc.trace = nullptr;
   env.maps = nullptr;
-  // the error word, every ticket and epoch counter, and the epoch-tagged tile sums must be zero
-  // when the kernel starts
-  if (cudaMemsetAsync(base, 0, off_partials, env.stream) != cudaSuccess) return G4_ERR_CUDA;
+  // the error word, the epoch counters and every epoch-tagged word must be zero when the kernel
+  // starts
+  if (cudaMemsetAsync(base, 0, need, env.stream) != cudaSuccess) return G4_ERR_CUDA;
   const g4::OArgs a{x, post_attn_rms_weight, o_weight, o_weight_scale, residual_hbm, false};
   return g4::launch_o_uncached(a, env) == cudaSuccess ? G4_OK : G4_ERR_CUDA;
 }

@@ -85,10 +85,17 @@ struct TpLink {
 };
 constexpr size_t kScratchHeadBytes = 256;  // the error word, padded to the scratch alignment
 constexpr int kCounterCount = 4096;
-constexpr int kTailEpochO = 3840;        // residual tails: calls so far, per output tile (30 each)
+constexpr int kSplitEpochUpGate = 0;     // calls so far, per tile: up/gate (240 tiles), ...
+constexpr int kTailEpochO = 3840;        // ... O and down (30 each; split-K and residual tail)
 constexpr int kTailEpochDown = 3872;
-constexpr int kHeadCounterBase = 3968;  // 32 per-head tickets of the QKV op
+constexpr int kHeadEpochBase = 3968;    // ... and QKV heads (32)
 constexpr size_t kPartialFloats = size_t(1) << 21;  // 8 MiB of split-K partials
+// Split-K slots of each op: [tile][CTA of the tile][128 rows] epoch-tagged words (offsets in words
+// from `partials`); one region per op, so a word of one op never reads as another op's.
+constexpr size_t kSplitWordsO = 0;
+constexpr size_t kSplitWordsDown = size_t(1) << 16;
+constexpr size_t kSplitWordsQkv = size_t(1) << 17;
+constexpr size_t kSplitWordsUpGate = size_t(1) << 18;
 constexpr size_t kYElems = 65536;
 
 // ---------------------------------------------------------------------------------------

@@ -27,8 +27,9 @@
 //   tile. Block scales live in TMEM in the scale-factor layout of the MMA: the scales of MMA j
 //   (blocks 4j..4j+3 of a row, 4 bytes) of row m sit in column 4j + m / 32, lane m % 32 of every
 //   lane quarter; each MMA's 4 columns start on a multiple of 4.
-// Rows whose K range is split across CTAs are published to global memory and summed by the
-// last CTA to finish the tile, in CTA order: the result never depends on timing.
+// Rows whose K range is split across CTAs are published to global memory as epoch-tagged words
+// and summed by the CTA holding the tile's first unit, in CTA order: the result never depends on
+// timing.
 #pragma once
 
 #include "g4_tc.cuh"
@@ -90,8 +91,6 @@ struct GemvCtl {
   uint64_t full[12], sready[12], done[16], tempty[16], dfull[4], dempty[4], drain;
   uint32_t tmem_base;
   uint32_t abort;
-  uint32_t bcast;
-  uint32_t bcast2;
   uint32_t unit_max[16];  // per B slot: max |activation| bits (fp8 weights)
   int pmax;               // nvfp4: largest exponent of this CTA's activation
   uint32_t nonfinite;     // nvfp4: an activation of this CTA is Inf or NaN
@@ -160,48 +159,77 @@ __device__ __forceinline__ void nvf4_digit_rows8(const uint4& raw, int pc, uint3
   }
 }
 
-// A finished piece of a tile (the units [.., kc] of it that this CTA ran), on the 128 epilogue
-// threads. A whole tile is final; the pieces of a tile whose K range is split across CTAs are
-// published to `partials` and the last CTA to arrive (ticket in `counters`) adds them up in CTA
-// order, so the result never depends on timing. Ops that finish their pieces themselves
-// (kOwnPieces) get them as they are.
+// Poll the tagged words (epoch << 32 | f32 bits) at words[k * kTileRows], k < n, except k = own
+// (whose value is `own_val`), until each carries `epoch`; return their sum in k order. A word
+// that never arrives (bounded wait) raises kErrWaitTimeout and counts as NaN.
+__device__ __forceinline__ float sum_tagged(const unsigned long long* words, int n, int own, float own_val,
+                                            uint32_t epoch, uint32_t* err) {
+  float pv[kMaxCtasPerGroup];
+  uint32_t pending = 0u;
+#pragma unroll
+  for (int k = 0; k < kMaxCtasPerGroup; ++k) {
+    pv[k] = k == own ? own_val : 0.f;
+    if (k < n && k != own) pending |= 1u << k;
+  }
+  const uint64_t t0 = globaltimer_ns();
+  while (pending) {
+#pragma unroll
+    for (int k = 0; k < kMaxCtasPerGroup; ++k) {
+      if (pending & (1u << k)) {
+        const unsigned long long w = ld_relaxed_gpu_u64(words + k * kTileRows);
+        if (uint32_t(w >> 32) == epoch) {
+          pv[k] = __uint_as_float(uint32_t(w));
+          pending &= ~(1u << k);
+        }
+      }
+    }
+    if (pending && globaltimer_ns() - t0 > kWaitLimitNs) {
+      atomicOr(err, kErrWaitTimeout);
+#pragma unroll
+      for (int k = 0; k < kMaxCtasPerGroup; ++k)
+        if (pending & (1u << k)) pv[k] = __uint_as_float(0x7fc00000u);
+      break;
+    }
+  }
+  float sum = 0.f;
+#pragma unroll
+  for (int k = 0; k < kMaxCtasPerGroup; ++k)
+    if (k < n) sum += pv[k];
+  return sum;
+}
+
+// A finished piece of a tile (the units of it that this CTA ran), on the 128 epilogue threads.
+// A whole tile is final. A tile whose K range is split across CTAs is finished by a fixed CTA,
+// the one holding its first unit: that piece is the last of its run, so waiting there holds up
+// nothing else. Every other CTA of the tile stores its partial rows into the tile's slots
+// (op.split_words) as 64-bit words tagged with the call's epoch (op.epoch); the finishing CTA
+// polls them and adds the pieces in CTA order, so the result never depends on timing, then
+// records the call in the tile's epoch count (op.split_epochs). Ops that finish their pieces
+// themselves (kOwnPieces) get them as they are.
 template <class Shape, class Op>
-__device__ void finish_piece(Op& op, GemvCtl& ctl, const Scratch& sc, uint32_t* counters, float* partials, int tile,
-                             int row, float val, int in_piece) {
+__device__ void finish_piece(Op& op, GemvCtl& ctl, const Scratch& sc, int tile, int row, float val, int in_piece) {
   constexpr int UPT = Shape::kUnitsPerTile;
   const int64_t total = Shape::kTotalUnits, grid = gridDim.x;
   if constexpr (Op::kOwnPieces) {
     op.finish_piece(tile, row, val, in_piece, ctl);
-  } else if (in_piece == UPT) {
-    op.finalize_tile(tile, row, val, ctl);
   } else {
-    const int first = cta_of_unit(int64_t(tile) * UPT, grid, total);
-    const int lastc = cta_of_unit(int64_t(tile) * UPT + UPT - 1, grid, total);
-    float* part = partials + size_t(tile) * kMaxCtasPerGroup * kTileRows;
-    if (lastc - first >= kMaxCtasPerGroup) {  // launchers keep every tile within the slots
-      if (row == 0) atomicOr(sc.err, kErrInternal);
-      return;
+    if (in_piece != UPT) {
+      const int first = cta_of_unit(int64_t(tile) * UPT, grid, total);
+      const int span = cta_of_unit(int64_t(tile) * UPT + UPT - 1, grid, total) - first + 1;
+      if (span > kMaxCtasPerGroup) {  // launchers keep every tile within the slots
+        if (row == 0) atomicOr(sc.err, kErrInternal);
+        return;
+      }
+      unsigned long long* words = op.split_words + size_t(tile) * kMaxCtasPerGroup * kTileRows + row;
+      if (int(blockIdx.x) != first) {
+        st_relaxed_gpu_u64(words + (blockIdx.x - first) * kTileRows,
+                           (static_cast<unsigned long long>(op.epoch) << 32) | __float_as_uint(val));
+        return;
+      }
+      val = sum_tagged(words, span, 0, val, op.epoch, sc.err);
     }
-    part[(blockIdx.x - first) * kTileRows + row] = val;
-    named_bar(kEpiBarrier, kEpiThreads);
-    if (row == 0) {
-      const uint32_t before = atomic_add_acq_rel_gpu(counters + tile, uint32_t(in_piece));
-      const bool done = before + uint32_t(in_piece) == uint32_t(UPT);
-      if (done) counters[tile] = 0;
-      ctl.bcast = done ? 1u : 0u;
-    }
-    __syncwarp();
-    named_bar(kEpiBarrier, kEpiThreads);
-    if (ctl.bcast) {
-      float pv[kMaxCtasPerGroup];  // every load in flight at once, then the sum in CTA order
-#pragma unroll
-      for (int k = 0; k < kMaxCtasPerGroup; ++k) pv[k] = k <= lastc - first ? ld_cg_f32(part + k * kTileRows + row) : 0.f;
-      float tot = 0.f;
-#pragma unroll
-      for (int k = 0; k < kMaxCtasPerGroup; ++k)
-        if (k <= lastc - first) tot += pv[k];
-      op.finalize_tile(tile, row, tot, ctl);
-    }
+    if (row == 0) op.split_epochs[tile] = op.epoch;
+    op.finalize_tile(tile, row, val, ctl);
   }
 }
 
@@ -219,6 +247,8 @@ __device__ void finish_piece(Op& op, GemvCtl& ctl, const Scratch& sc, uint32_t* 
 //   void finish_group(const uint4 (&raw)[4], float inv, float (&v)[16]) const   the activation
 //                                      (bf16-exact values)
 //   void finalize_tile(int tile, int row, float v, GemvCtl&) const   all 128 epilogue threads
+//   unsigned long long* split_words, uint32_t* split_epochs, uint32_t epoch   split tiles' slots,
+//                                      per-tile call counts and this call's epoch (finish_piece)
 //   static bool kOwnPieces             the op finishes every tile piece itself:
 //   void finish_piece(int tile, int row, float v, int units, GemvCtl&) const
 //   uint32_t tx_bytes                  bytes one unit delivers (codes and, nvfp4, block scales)
@@ -618,7 +648,7 @@ __device__ void gemv_run(Op& op, uint8_t* smem_raw, const Scratch& sc) {
 #ifdef G4_TRACE
       if (sc.trace && blockIdx.x == 0 && i < 64 && row == 0) sc.trace[3192 + i] = globaltimer_ns();
 #endif
-      finish_piece<Shape>(op, ctl, sc, sc.counters, sc.partials, tile, row, acc, in_piece);
+      finish_piece<Shape>(op, ctl, sc, tile, row, acc, in_piece);
       acc = 0.f;
       in_piece = 0;
     }

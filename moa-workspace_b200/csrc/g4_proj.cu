@@ -306,11 +306,13 @@ struct QkvOp {
   }
   static constexpr bool kOwnPieces = true;
   QkvStatic* st;
+  uint32_t epoch = 0;  // this call's, for the heads' split-K words
 
   // the position offsets (device-resident, written before the call; byte offsets into the whole
   // layer's cache and table, the same on every tensor-parallel rank), then the RoPE row and the
   // per-head norm weights into shared memory, asynchronously (the epilogue threads wait for them)
   __device__ void prologue(GemvCtl&) {
+    epoch = tail_epoch(sc.counters + kHeadEpochBase, first_tile<QkvShape>() / 2);
     const int kv = *a.kv_offset, rope = *a.rope_offset;
     const bool kv_ok = kv >= 0 && (kv % (kPs * 2)) == 0 && kv / (kPs * 2) < a.ring_len;
     const bool rope_ok = rope >= 0 && (rope % (kDs * 2)) == 0 && rope / (kDs * 2) < a.rope_rows;
@@ -333,25 +335,31 @@ struct QkvOp {
     }
   }
 
-  __device__ void finish_piece(int tile, int row, float v, int in_piece, GemvCtl& ctl) const {
+  // A head's pieces: the CTA holding the head's first unit finishes the head at its last piece
+  // in the head (the last piece of its run); every other piece is published as epoch-tagged
+  // words in the slots of its tile.
+  __device__ void finish_piece(int tile, int row, float v, int, GemvCtl&) const {
     constexpr int UPT = QkvShape::kUnitsPerTile;
     const int64_t grid = gridDim.x, total = QkvShape::kTotalUnits;
-    const int first = cta_of_unit(int64_t(tile) * UPT, grid, total);
-    sc.partials[size_t(tile) * kMaxCtasPerGroup * kTileRows + (blockIdx.x - first) * kTileRows + row] = v;
-    named_bar(kEpiBarrier, kEpiThreads);
     const int head = tile / 2;
-    if (row == 0) {
-      const uint32_t before = atomic_add_acq_rel_gpu(sc.counters + kHeadCounterBase + head, uint32_t(in_piece));
-      const bool done = before + uint32_t(in_piece) == uint32_t(2 * UPT);
-      if (done) sc.counters[kHeadCounterBase + head] = 0;
-      ctl.bcast2 = done ? 1u : 0u;
+    const int run_last = int(int64_t(blockIdx.x + 1) * total / grid) - 1;  // this CTA's last unit
+    const int final_tile = run_last / UPT < 2 * head + 1 ? run_last / UPT : 2 * head + 1;
+    if (int(blockIdx.x) == cta_of_unit(int64_t(2 * head) * UPT, grid, total) && tile == final_tile) {
+      finish_head(head, row, tile, v);
+      return;
     }
-    __syncwarp();
-    named_bar(kEpiBarrier, kEpiThreads);
-    if (ctl.bcast2) finish_head(head, row);
+    const int first = cta_of_unit(int64_t(tile) * UPT, grid, total);
+    st_relaxed_gpu_u64(words(tile) + (blockIdx.x - first) * kTileRows + row,
+                       (static_cast<unsigned long long>(epoch) << 32) | __float_as_uint(v));
   }
 
-  __device__ void finish_head(int head, int e) const {
+  __device__ unsigned long long* words(int tile) const {
+    return reinterpret_cast<unsigned long long*>(sc.partials) + kSplitWordsQkv + size_t(tile) * kMaxCtasPerGroup * kTileRows;
+  }
+
+  // Thread e finishes elements e and e + 128 of the head: tile 2 head + t, row e. `own` is this
+  // CTA's piece of tile `own_tile` (not published).
+  __device__ void finish_head(int head, int e, int own_tile, float own) const {
     constexpr int UPT = QkvShape::kUnitsPerTile;
     const int64_t grid = gridDim.x, total = QkvShape::kTotalUnits;
     float y[2];
@@ -359,21 +367,19 @@ struct QkvOp {
     for (int t = 0; t < 2; ++t) {  // element e + 128 t of the head = row e of tile 2 head + t
       const int tile = 2 * head + t;
       const int first = cta_of_unit(int64_t(tile) * UPT, grid, total);
-      const int last = cta_of_unit(int64_t(tile) * UPT + UPT - 1, grid, total);
-      const float* part = sc.partials + size_t(tile) * kMaxCtasPerGroup * kTileRows + e;
+      const int span = cta_of_unit(int64_t(tile) * UPT + UPT - 1, grid, total) - first + 1;
       const int r = tile * kTileRows + e;
       const uint16_t sb =
           r < kQRows ? a.q_scale[r] : (r < kQRows + kKvRows ? a.k_scale[r - kQRows] : a.v_scale[r - kQRows - kKvRows]);
-      float pv[kMaxCtasPerGroup];  // every load in flight at once, then the sum in CTA order
-#pragma unroll
-      for (int k = 0; k < kMaxCtasPerGroup; ++k) pv[k] = k <= last - first ? ld_cg_f32(part + k * kTileRows) : 0.f;
-      float acc = 0.f;
-#pragma unroll
-      for (int k = 0; k < kMaxCtasPerGroup; ++k)
-        if (k <= last - first) acc += pv[k];
+      float acc = __uint_as_float(0x7fc00000u);
+      if (span <= kMaxCtasPerGroup)
+        acc = sum_tagged(words(tile) + e, span, tile == own_tile ? int(blockIdx.x) - first : -1, own, epoch, sc.err);
+      else if (e == 0)
+        atomicOr(sc.err, kErrInternal);
       // scaled_projection: bf16((x @ codes.T) * scale) (generate_references.py:265-274)
       y[t] = bf16_round(acc * bf16_to_f32(sb));
     }
+    if (e == 0) sc.counters[kHeadEpochBase + head] = epoch;
     // RMSNorm over the head's 256 values (gemma4.py:83-89), the sum in a fixed order
     double ss = warp_sum_d(double(y[0]) * double(y[0]) + double(y[1]) * double(y[1]));
     cp_async_wait_all();
@@ -476,7 +482,9 @@ struct OOp {
   }
   ResidualTail* tail;
   const TpLink* tp;
-  uint32_t epoch = 0;  // this call's, for the residual tail
+  uint32_t epoch = 0;  // this call's, for split tiles and the residual tail
+  unsigned long long* split_words = reinterpret_cast<unsigned long long*>(sc.partials) + kSplitWordsO;
+  uint32_t* split_epochs = sc.counters + kTailEpochO;
 };
 
 template <int NTP>
@@ -540,7 +548,11 @@ struct UpGateOp {
   __device__ void prologue(GemvCtl&) {
     g_up = *a.up_global;
     g_gate = *a.gate_global;
+    epoch = tail_epoch(split_epochs, first_tile<UpGateShape>());
   }
+  uint32_t epoch = 0;  // this call's, for split tiles
+  unsigned long long* split_words = reinterpret_cast<unsigned long long*>(sc.partials) + kSplitWordsUpGate;
+  uint32_t* split_epochs = sc.counters + kSplitEpochUpGate;
   __device__ void load_static(int g, uint4 (&raw)[4]) const { load_group_gamma(a.pre_rms, g, raw); }
   __device__ void load_group(int g, uint4 (&raw)[4]) const { load_group_cg(a.residual, g, raw); }
   __device__ void finish_group(const uint4 (&raw)[4], float inv, float (&v)[16]) const { rms_apply16(raw, inv, v); }
@@ -619,7 +631,9 @@ struct DownOp {
   }
   ResidualTail* tail;
   const TpLink* tp;
-  uint32_t epoch = 0;  // this call's, for the residual tail
+  uint32_t epoch = 0;  // this call's, for split tiles and the residual tail
+  unsigned long long* split_words = reinterpret_cast<unsigned long long*>(sc.partials) + kSplitWordsDown;
+  uint32_t* split_epochs = sc.counters + kTailEpochDown;
 };
 
 template <int NTP>
@@ -905,7 +919,7 @@ cudaError_t TmapCache::u8(const void* base, uint64_t cols, uint64_t rows, uint32
 
 size_t o_scratch_bytes() {
   return kScratchHeadBytes + size_t(kCounterCount) * sizeof(uint32_t) + kTileSsBytes +
-         size_t(Shapes<1>::O::kTiles) * kMaxCtasPerGroup * kTileRows * sizeof(float);
+         size_t(Shapes<1>::O::kTiles) * kMaxCtasPerGroup * kTileRows * sizeof(unsigned long long);
 }
 
 cudaError_t launch_o_uncached(const OArgs& a, const LaunchEnv& env) {
