@@ -173,14 +173,15 @@ __device__ __forceinline__ float sum_tagged(const unsigned long long* words, int
   }
   const uint64_t t0 = globaltimer_ns();
   while (pending) {
+    unsigned long long w[kMaxCtasPerGroup];  // every pending word in flight at once, then the checks
+#pragma unroll
+    for (int k = 0; k < kMaxCtasPerGroup; ++k)
+      if (pending & (1u << k)) w[k] = ld_relaxed_gpu_u64(words + k * kTileRows);
 #pragma unroll
     for (int k = 0; k < kMaxCtasPerGroup; ++k) {
-      if (pending & (1u << k)) {
-        const unsigned long long w = ld_relaxed_gpu_u64(words + k * kTileRows);
-        if (uint32_t(w >> 32) == epoch) {
-          pv[k] = __uint_as_float(uint32_t(w));
-          pending &= ~(1u << k);
-        }
+      if ((pending & (1u << k)) && uint32_t(w[k] >> 32) == epoch) {
+        pv[k] = __uint_as_float(uint32_t(w[k]));
+        pending &= ~(1u << k);
       }
     }
     if (pending && globaltimer_ns() - t0 > kWaitLimitNs) {

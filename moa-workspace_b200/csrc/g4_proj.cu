@@ -111,14 +111,15 @@ __device__ float tp_allreduce(const TpLink& tp, int op, int tile, int row, float
   }
   const uint64_t t0 = globaltimer_ns();
   while (pending) {
+    unsigned long long w[kMaxTp];  // every pending word in flight at once, then the checks
+#pragma unroll
+    for (int s = 0; s < kMaxTp; ++s)
+      if (pending & (1u << s)) w[s] = ld_relaxed_sys_u64(mine + s * kTileRows);
 #pragma unroll
     for (int s = 0; s < kMaxTp; ++s) {
-      if (pending & (1u << s)) {
-        const unsigned long long w = ld_relaxed_sys_u64(mine + s * kTileRows);
-        if (uint32_t(w >> 32) == e) {
-          pv[s] = __uint_as_float(uint32_t(w));
-          pending &= ~(1u << s);
-        }
+      if ((pending & (1u << s)) && uint32_t(w[s] >> 32) == e) {
+        pv[s] = __uint_as_float(uint32_t(w[s]));
+        pending &= ~(1u << s);
       }
     }
     if (pending && globaltimer_ns() - t0 > kWaitLimitNs) {  // a peer never arrived: flag it, poison the row
@@ -211,7 +212,7 @@ __device__ void tail_update(ResidualTail& t, uint16_t* residual, const Scratch& 
   if (t.n == 0) return;  // CTA-uniform: nothing of this CTA's waits on the statistic
   if (threadIdx.x < tiles) {  // thread i polls tile i's two words
     const unsigned long long* w = sc.tile_ss + 2 * threadIdx.x;
-    unsigned long long lo = ld_relaxed_gpu_u64(w), hi = ld_relaxed_gpu_u64(w + 1);
+    unsigned long long lo = ld_relaxed_gpu_u64(w), hi = ld_relaxed_gpu_u64(w + 1);  // both in flight
     const uint64_t t0 = globaltimer_ns();
     while (uint32_t(lo >> 32) != epoch || uint32_t(hi >> 32) != epoch) {
       if (globaltimer_ns() - t0 > kWaitLimitNs) {
