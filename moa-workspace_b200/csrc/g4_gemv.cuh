@@ -547,8 +547,16 @@ __device__ void gemv_run(Op& op, uint8_t* smem_raw, const Scratch& sc) {
                 (i >= T && !mbar_wait_or_abort(&ctl.tempty[i % T], uint32_t(((i / T) - 1) & 1), abort, sc.err));
         }
       }
+#ifdef G4_TRACE
+      if (sc.trace && blockIdx.x == 0 && i < 64 && c.lane == 0) sc.trace[3128 + i] = globaltimer_ns();  // unit ready
+#endif
       __syncwarp();
       if (named_bar_or(kIssueBarrier, kIssueThreads, bad)) break;
+      if (c.lane == 0 && i == 0) G4_STAMP_T(sc, 3);        // first unit released to the issuer
+      if (c.lane == 0 && i == c.n - 1) G4_STAMP_T(sc, 4);  // last unit released
+#ifdef G4_TRACE
+      if (sc.trace && blockIdx.x == 0 && i < 64 && c.lane == 0) sc.trace[3064 + i] = globaltimer_ns();  // released
+#endif
     }
   } else if (c.warp == 1) {
     // ---------------------------------------------------------------- MMA issuer
@@ -556,11 +564,7 @@ __device__ void gemv_run(Op& op, uint8_t* smem_raw, const Scratch& sc) {
     for (int i = 0; i < c.n; ++i) {
       if (named_bar_or(kIssueBarrier, kIssueThreads, false)) break;
       tc_fence_after();
-      if (i == 0) G4_STAMP_T(sc, 3);
-      if (c.lane == 0) {
-#ifdef G4_TRACE
-        if (sc.trace && blockIdx.x == 0 && i < 64) sc.trace[3064 + i] = globaltimer_ns();
-#endif
+      if (c.lane == 0) {  // (no trace stamps here: a global store of this thread waits for its MMAs)
         const int s = i % S, t = i % T, kc = (c.u0 + i) % UPT;
         const uint32_t a_base = smem_u32(c.stage(s));
         const uint32_t b_base = smem_u32(c.bsm) + uint32_t(c.bslot(kc)) * Shape::kBSlotBytes;
@@ -585,11 +589,7 @@ __device__ void gemv_run(Op& op, uint8_t* smem_raw, const Scratch& sc) {
           }
           umma_commit(&ctl.done[t]);
         }
-#ifdef G4_TRACE
-        if (sc.trace && blockIdx.x == 0 && i < 64) sc.trace[3128 + i] = globaltimer_ns();
-#endif
       }
-      if (i == c.n - 1) G4_STAMP_T(sc, 4);
       __syncwarp();
     }
     // nothing of ours may still be running when TMEM is released

@@ -258,11 +258,10 @@ __device__ __forceinline__ void split_terms16(const float (&v)[16], uint4 (&t)[N
     for (int j = 0; j < NT; ++j) {
       const uint32_t c = f32x2_to_e4m3x2(ra, rb);
       w[j][i / 2] |= c << sh;
-      if (j + 1 < NT) {
+      if (j + 1 < NT) {  // straight-line: once a remainder is zero its further terms are zero codes
         const float2 d = e4m3x2_to_f32x2(c);
         ra = (ra - d.x) * 16.0f;
         rb = (rb - d.y) * 16.0f;
-        if (ra == 0.f && rb == 0.f) break;  // every further term is zero
       }
     }
   }
