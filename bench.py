@@ -65,7 +65,7 @@ def op_bytes(world=1):
 BYTES = op_bytes(1)
 # DRAM bytes read + written per decoder_feedforward call (ffn_upgate + ffn_down): ncu --set full
 # capture of `python bench.py --only ffn --steps 3 --warmup 3` (dram__bytes_read.sum + write.sum)
-FFN_TRAFFIC = 66.43e6 + 0.63e6 + 33.28e6
+FFN_TRAFFIC = 66.43e6 + 0.66e6 + 33.37e6
 METRIC = "decode tokens/s through one Gemma-4 sliding decoder layer (QKV + attention + O + FFN ops, M=1)"
 WORKLOAD = ("gemma4-12b sliding decoder layer, M=1: fused QKV fp8 [8192x3840] + sliding attention "
             "(ring 1024 x 8 heads x 256, scale 1.0) + O fp8 [3840x4096] + NVFP4 GeGLU FFN [2x15360x3840 + 3840x15360]")
