@@ -21,7 +21,7 @@
  *   - Offsets that live in device memory (kv_offset, rope_offset) are checked on the
  *     device: an out-of-range value skips the writes that depend on it and raises a bit
  *     that g4_ctx_check() reports as G4_ERR_DEVICE.
- *   - A context owns scratch memory (split-K partials, tickets, the GeGLU activation).
+ *   - A context owns scratch memory (split-K partials, epoch counters, the GeGLU activation).
  *     Calls on one context must not overlap on the GPU (use one stream per context).
  *     A context is thread-compatible, not thread-safe, like the reference's single
  *     device-owning thread (src/api/worker.rs:45-72).

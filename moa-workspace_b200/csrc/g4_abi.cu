@@ -160,11 +160,10 @@ g4_status g4_ctx_create(int device, g4_ctx** out) {
     delete ctx;
     return G4_ERR_UNSUPPORTED;
   }
-  // scratch: error word + counters | partials | y | act
+  // scratch: error word + counters | split-K words | act | tile sums [| trace]
   const size_t off_counters = 256;
   const size_t off_partials = off_counters + g4::kCounterCount * sizeof(uint32_t);
-  const size_t off_y = off_partials + g4::kPartialFloats * sizeof(float);
-  const size_t off_act = off_y + g4::kYElems * sizeof(uint16_t);
+  const size_t off_act = off_partials + g4::kPartialFloats * sizeof(float);
   const size_t off_ss = off_act + size_t(64) * g4::kL * sizeof(uint16_t);
   const size_t off_trace = off_ss + g4::kTileSsBytes;
 #ifdef G4_TRACE
@@ -187,7 +186,6 @@ g4_status g4_ctx_create(int device, g4_ctx** out) {
   ctx->sc.err = reinterpret_cast<uint32_t*>(base);
   ctx->sc.counters = reinterpret_cast<uint32_t*>(base + off_counters);
   ctx->sc.partials = reinterpret_cast<float*>(base + off_partials);
-  ctx->sc.y = reinterpret_cast<uint16_t*>(base + off_y);
   ctx->sc.act = reinterpret_cast<uint16_t*>(base + off_act);
   ctx->act_bytes = off_ss - off_act;
   ctx->sc.tile_ss = reinterpret_cast<unsigned long long*>(base + off_ss);
@@ -227,8 +225,8 @@ g4_status g4_ctx_check(g4_ctx* ctx, void* stream, uint32_t* flags) {
   if (e == cudaSuccess) e = cudaMemcpy(&word, ctx->sc.err, sizeof word, cudaMemcpyDeviceToHost);
   if (e == cudaSuccess && word) e = cudaMemset(ctx->sc.err, 0, sizeof word);
   if (e == cudaSuccess && (word & (G4_DEVERR_WAIT_TIMEOUT | G4_DEVERR_PEER_TIMEOUT))) {
-    // an abandoned launch can leave tickets half counted: start the next call clean (the
-    // epoch-tagged tile sums and split-K words too, as the epochs restart)
+    // an abandoned launch can leave the epoch counters out of step: restart them, and clear the
+    // epoch-tagged tile sums and split-K words so no old word matches a restarted epoch
     e = cudaMemset(ctx->sc.counters, 0, g4::kCounterCount * sizeof(uint32_t));
     if (e == cudaSuccess) e = cudaMemset(ctx->sc.tile_ss, 0, g4::kTileSsBytes);
     if (e == cudaSuccess) e = cudaMemset(ctx->sc.partials, 0, g4::kPartialFloats * sizeof(float));
@@ -594,7 +592,6 @@ g4_status g4_sliding_attention_output_noalloc(const uint16_t* x, const uint16_t*
   env.sc.err = reinterpret_cast<uint32_t*>(base);
   env.sc.counters = reinterpret_cast<uint32_t*>(base + off_counters);
   env.sc.partials = reinterpret_cast<float*>(base + off_partials);
-  env.sc.y = nullptr;
   env.sc.act = nullptr;
   env.sc.tile_ss = reinterpret_cast<unsigned long long*>(base + off_ss);
   env.sc.trace = nullptr;
@@ -607,17 +604,6 @@ g4_status g4_sliding_attention_output_noalloc(const uint16_t* x, const uint16_t*
 }
 
 #ifdef G4_TRACE
-// Profiling builds only (not part of the public header): copy scratch vectors out
-// (which = 0: y [65536] bf16, 1: act [15360] bf16).
-g4_status g4_debug_read(g4_ctx* ctx, int which, void* host, int bytes) {
-  if (!ctx || !host || bytes < 0 || bytes > 131072) return G4_ERR_INVALID_ARGUMENT;
-  DeviceGuard guard(ctx->device);
-  cudaError_t e = cudaDeviceSynchronize();
-  const void* src = which == 0 ? static_cast<const void*>(ctx->sc.y) : static_cast<const void*>(ctx->sc.act);
-  if (e == cudaSuccess) e = cudaMemcpy(host, src, size_t(bytes), cudaMemcpyDeviceToHost);
-  return e == cudaSuccess ? G4_OK : G4_ERR_CUDA;
-}
-
 // Profiling builds only (not part of the public header): copy the phase timestamps out.
 g4_status g4_trace_read(g4_ctx* ctx, uint64_t* host, int n) {
   if (!ctx || !host || n < 0 || n > 65536 + 4096 * 32 * 8) return G4_ERR_INVALID_ARGUMENT;

@@ -52,13 +52,12 @@ enum : uint32_t {
   kErrPeerTimeout = 1u << 5,    // a tensor-parallel peer's partial did not arrive in time
 };
 
-// Global scratch owned by a context. Counters are zero between launches: every kernel that
-// bumps one resets it before it exits.
+// Global scratch owned by a context. The counters hold each op's call counts (per tile or
+// head), which tag its split-K words and tile sums with the call's epoch; they only grow.
 struct Scratch {
   uint32_t* err;       // error word
-  uint32_t* counters;  // ticket counters (kCounterCount)
-  float* partials;     // split-K partial row sums
-  uint16_t* y;         // bf16 projected rows awaiting a grid-level epilogue
+  uint32_t* counters;  // epoch counters (kCounterCount)
+  float* partials;     // split-K words of each op (kSplitWords*; the region is sized in floats)
   uint16_t* act;       // bf16 GeGLU activation [M][L]
   unsigned long long* tile_ss;  // per output tile: sum of squares of its bf16 rows, as two words
                                 // (epoch << 32 | low / high half of the f64), kTileSsCount tiles
@@ -96,7 +95,6 @@ constexpr size_t kSplitWordsO = 0;
 constexpr size_t kSplitWordsDown = size_t(1) << 16;
 constexpr size_t kSplitWordsQkv = size_t(1) << 17;
 constexpr size_t kSplitWordsUpGate = size_t(1) << 18;
-constexpr size_t kYElems = 65536;
 
 // ---------------------------------------------------------------------------------------
 // bf16 / f16 / fp8 / fp4 conversions
@@ -197,26 +195,6 @@ __device__ __forceinline__ void bulk_g2s(void* dst, const void* src, uint32_t by
 __device__ __forceinline__ void pdl_launch_dependents() { asm volatile("griddepcontrol.launch_dependents;" ::: "memory"); }
 __device__ __forceinline__ void pdl_wait_primary() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
 
-// Ticket atomics with release / acquire semantics (cheaper than a sequentially consistent
-// __threadfence). Writers of the published data are ordered before a release by a preceding
-// __syncwarp / __syncthreads; readers are ordered after an acquire by a following one.
-__device__ __forceinline__ uint32_t atomic_add_acq_rel_gpu(uint32_t* p, uint32_t v) {
-  uint32_t old;
-  asm volatile("atom.acq_rel.gpu.global.add.u32 %0, [%1], %2;" : "=r"(old) : "l"(p), "r"(v) : "memory");
-  return old;
-}
-__device__ __forceinline__ void fence_acq_rel_gpu() { asm volatile("fence.acq_rel.gpu;" ::: "memory"); }
-__device__ __forceinline__ uint32_t atomic_add_release_gpu(uint32_t* p, uint32_t v) {
-  uint32_t old;
-  asm volatile("atom.release.gpu.global.add.u32 %0, [%1], %2;" : "=r"(old) : "l"(p), "r"(v) : "memory");
-  return old;
-}
-__device__ __forceinline__ uint32_t ld_acquire_gpu(const uint32_t* p) {
-  uint32_t v;
-  asm volatile("ld.acquire.gpu.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
-  return v;
-}
-
 // System-scope 64-bit accesses for the tensor-parallel exchange words (peer memory over NVLink).
 __device__ __forceinline__ void st_relaxed_sys_u64(unsigned long long* p, unsigned long long v) {
   asm volatile("st.relaxed.sys.global.u64 [%0], %1;" ::"l"(p), "l"(v) : "memory");
@@ -236,8 +214,6 @@ __device__ __forceinline__ unsigned long long ld_relaxed_gpu_u64(const unsigned 
   return v;
 }
 
-// L2-coherent loads for data other CTAs of the same launch wrote.
-__device__ __forceinline__ float ld_cg_f32(const float* p) { return __ldcg(p); }
 // 16 bytes global (L2) -> shared memory without a register round trip; wait with cp_async_wait_all.
 __device__ __forceinline__ void cp_async_16(void* smem_dst, const void* src) {
   asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(smem_u32(smem_dst)), "l"(src) : "memory");
@@ -245,7 +221,6 @@ __device__ __forceinline__ void cp_async_16(void* smem_dst, const void* src) {
 __device__ __forceinline__ void cp_async_wait_all() {
   asm volatile("cp.async.commit_group;\n cp.async.wait_group 0;" ::: "memory");
 }
-__device__ __forceinline__ uint4 ld_cg_u4(const void* p) { return __ldcg(reinterpret_cast<const uint4*>(p)); }
 
 // Phase timestamps for profiling builds (-DG4_TRACE): thread 0 of each CTA records
 // %globaltimer at numbered points of a kernel into trace[blockIdx.x * 16 + point].
@@ -308,17 +283,6 @@ __device__ __forceinline__ double block_sum_d(double v, double* red) {
   for (int i = 0; i < nw; ++i) t += red[i];  // fixed order: identical in every CTA
   return t;
 }
-__device__ __forceinline__ float block_max(float v, float* red) {
-  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5, nw = blockDim.x >> 5;
-  v = warp_max(v);
-  __syncthreads();
-  if (lane == 0) red[warp] = v;
-  __syncwarp();
-  __syncthreads();
-  float t = 0.f;
-  for (int i = 0; i < nw; ++i) t = fmaxf(t, red[i]);
-  return t;
-}
 
 // RMSNorm statistics exactly as the reference computes them (gemma4.py:83-89): the mean of
 // squares of bf16 values, accumulated without loss in f64 and narrowed to f32, then
@@ -326,27 +290,6 @@ __device__ __forceinline__ float block_max(float v, float* red) {
 __device__ __forceinline__ float rms_inverse(double sumsq, int n) {
   const float ms = static_cast<float>(sumsq / static_cast<double>(n));
   return 1.0f / sqrtf(ms + kEps);
-}
-
-// Load a bf16 K-vector (16-byte aligned) as VPT 8-element vectors per thread, all loads in
-// flight at once. Elements past k read as zero. `coherent` loads go through L2 only (for data
-// another CTA or the preceding kernel wrote).
-template <int VPT>
-__device__ __forceinline__ void load_bf16_vec(const uint16_t* src, int k, float (&vals)[VPT][8], bool coherent) {
-  uint4 raw[VPT];
-#pragma unroll
-  for (int v = 0; v < VPT; ++v) {
-    const int base = (threadIdx.x + v * blockDim.x) * 8;
-    raw[v] = make_uint4(0, 0, 0, 0);
-    if (base < k)
-      raw[v] = coherent ? __ldcg(reinterpret_cast<const uint4*>(src + base)) : *reinterpret_cast<const uint4*>(src + base);
-  }
-#pragma unroll
-  for (int v = 0; v < VPT; ++v) {
-    const uint16_t* b = reinterpret_cast<const uint16_t*>(&raw[v]);
-#pragma unroll
-    for (int j = 0; j < 8; ++j) vals[v][j] = bf16_to_f32(b[j]);
-  }
 }
 
 // Global partial slots per split tile (a tile's K range spans at most this many CTAs).

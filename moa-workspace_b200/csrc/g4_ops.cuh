@@ -110,8 +110,8 @@ cudaError_t launch_attention(const AttnArgs& a, const LaunchEnv& env);
 cudaError_t launch_o(const OArgs& a, const LaunchEnv& env);
 cudaError_t launch_ffn_nvfp4(const FfnArgs& a, const LaunchEnv& env);
 
-// The O op without a context: scratch laid out as [error word | kScratchHeadBytes][tickets and
-// epoch counters][tile sums][split-K partials] at env.sc, o_scratch_bytes() in total; the tensor map is encoded on the
+// The O op without a context: scratch laid out as [error word | kScratchHeadBytes][epoch
+// counters][tile sums][split-K words] at env.sc, o_scratch_bytes() in total; the tensor map is encoded on the
 // stack (env.maps is not used). Row-major weights, one rank (env.tp.world == 1) only.
 size_t o_scratch_bytes();
 cudaError_t launch_o_uncached(const OArgs& a, const LaunchEnv& env);

@@ -250,11 +250,11 @@ __device__ void tail_update(ResidualTail& t, uint16_t* residual, const Scratch& 
 // QKV
 
 // Per-head RMSNorm (+ RoPE for q and k) and the store of one head (q_out, or the addressed ring
-// slot of the K / V cache). A head is 256 projected rows = two tiles; every CTA that computes a
-// piece of either tile publishes its partial row sums and adds its unit count to the head's
-// ticket, and the CTA that completes the 30 units sums the pieces (in CTA order) and finishes
-// the head with its 128 epilogue threads: thread e owns head elements e and e + 128, which are
-// exactly the two elements RoPE's half swap pairs.
+// slot of the K / V cache). A head is 256 projected rows = two tiles. The CTA holding the head's
+// first unit finishes it at its last piece in the head; every other CTA that computes a piece of
+// either tile publishes its partial row sums as epoch-tagged words, which the finishing CTA polls
+// and adds in CTA order. Its 128 epilogue threads finish the head: thread e owns head elements e
+// and e + 128, which are exactly the two elements RoPE's half swap pairs.
 
 struct QkvStatic {  // per CTA, loaded while the weights stream in
   __align__(16) uint16_t cos[kDs];
