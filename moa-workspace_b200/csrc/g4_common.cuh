@@ -64,7 +64,11 @@ struct Scratch {
   uint64_t* trace;     // per-CTA phase timestamps (profiling builds only; null otherwise)
 };
 constexpr int kTileSsCount = 64;
-constexpr size_t kTileSsBytes = size_t(kTileSsCount) * 2 * sizeof(unsigned long long);
+// One region of tile sums per op (O, down), in words from `tile_ss`: the ops count their calls
+// separately, so a word of one op must never be read by the other.
+constexpr size_t kTileSsO = 0;
+constexpr size_t kTileSsDown = size_t(kTileSsCount) * 2;
+constexpr size_t kTileSsBytes = 2 * size_t(kTileSsCount) * 2 * sizeof(unsigned long long);
 
 // Tensor-parallel exchange (one-shot all-reduce of the O / down partials over NVLink peer
 // memory). Every rank owns one exchange buffer, mapped into every peer's address space:

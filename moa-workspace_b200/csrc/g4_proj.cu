@@ -178,7 +178,7 @@ __device__ __forceinline__ uint32_t tail_epoch(const uint32_t* epochs, int first
 
 // Called by the 128 epilogue threads when a tile is final: record it and publish its sum of
 // squares (f64, rows in order over the four warps) with the call's epoch.
-__device__ void tail_record(ResidualTail& t, const uint16_t* gamma, const uint16_t* residual, const Scratch& sc,
+__device__ void tail_record(ResidualTail& t, const uint16_t* gamma, const uint16_t* residual, unsigned long long* sums,
                             uint32_t* epochs, uint32_t epoch, int tile, int row, float y) {
   const int f = t.n;
   t.y[f][row] = y;
@@ -193,8 +193,8 @@ __device__ void tail_record(ResidualTail& t, const uint16_t* gamma, const uint16
     const double sum = ((t.red[0] + t.red[1]) + t.red[2]) + t.red[3];
     const unsigned long long bits = static_cast<unsigned long long>(__double_as_longlong(sum));
     const unsigned long long tag = static_cast<unsigned long long>(epoch) << 32;
-    st_relaxed_gpu_u64(sc.tile_ss + 2 * tile, tag | (bits & 0xffffffffull));
-    st_relaxed_gpu_u64(sc.tile_ss + 2 * tile + 1, tag | (bits >> 32));
+    st_relaxed_gpu_u64(sums + 2 * tile, tag | (bits & 0xffffffffull));
+    st_relaxed_gpu_u64(sums + 2 * tile + 1, tag | (bits >> 32));
     epochs[tile] = epoch;
     t.tile[f] = tile;
     t.n = f + 1;
@@ -204,14 +204,14 @@ __device__ void tail_record(ResidualTail& t, const uint16_t* gamma, const uint16
 
 // Whole CTA, after gemv_run: a CTA that finished tiles waits for every tile's sum of this call,
 // then updates its recorded rows; the others return.
-__device__ void tail_update(ResidualTail& t, uint16_t* residual, const Scratch& sc, uint32_t epoch, int tiles,
-                            const uint16_t* layer_scalar) {
+__device__ void tail_update(ResidualTail& t, uint16_t* residual, const Scratch& sc, const unsigned long long* sums,
+                            uint32_t epoch, int tiles, const uint16_t* layer_scalar) {
   const float lam = layer_scalar ? bf16_to_f32(layer_scalar[0]) : 1.0f;
   cp_async_wait_all();
   __syncthreads();  // t.n is final
   if (t.n == 0) return;  // CTA-uniform: nothing of this CTA's waits on the statistic
   if (threadIdx.x < tiles) {  // thread i polls tile i's two words
-    const unsigned long long* w = sc.tile_ss + 2 * threadIdx.x;
+    const unsigned long long* w = sums + 2 * threadIdx.x;
     unsigned long long lo = ld_relaxed_gpu_u64(w), hi = ld_relaxed_gpu_u64(w + 1);  // both in flight
     const uint64_t t0 = globaltimer_ns();
     while (uint32_t(lo >> 32) != epoch || uint32_t(hi >> 32) != epoch) {
@@ -478,7 +478,7 @@ struct OOp {
   __device__ void finalize_tile(int tile, int row, float v, GemvCtl&) const {
     const int r = tile * kTileRows + row;
     const float sum = tp_allreduce(*tp, 0, tile, row, v, sc.err);  // the K slices of every rank
-    tail_record(*tail, a.post_rms, a.residual, sc, sc.counters + kTailEpochO, epoch, tile, row,
+    tail_record(*tail, a.post_rms, a.residual, sc.tile_ss + kTileSsO, sc.counters + kTailEpochO, epoch, tile, row,
                 bf16_round(sum * bf16_to_f32(a.o_scale[r])));
   }
   ResidualTail* tail;
@@ -498,7 +498,7 @@ __global__ void __launch_bounds__(kGemvThreads, 1) o_kernel(const __grid_constan
   op.tail = &tail;
   op.tp = &tp;
   gemv_run<typename Shapes<NTP>::O>(op, smem, sc);
-  tail_update(tail, a.residual, sc, op.epoch, kH / kTileRows, nullptr);
+  tail_update(tail, a.residual, sc, sc.tile_ss + kTileSsO, op.epoch, kH / kTileRows, nullptr);
   G4_STAMP(sc, 8);
 }
 
@@ -627,7 +627,7 @@ struct DownOp {
   __device__ void finalize_tile(int tile, int row, float v, GemvCtl&) const {
     const float sum = tp_allreduce(*tp, 1, tile, row, v, sc.err);  // the K slices of every rank
     // GloballyScaled(nn.Linear): bf16(bf16(x @ W.T) * g)  (generate_references.py:358-413)
-    tail_record(*tail, a.post_rms, a.residual, sc, sc.counters + kTailEpochDown, epoch, tile, row,
+    tail_record(*tail, a.post_rms, a.residual, sc.tile_ss + kTileSsDown, sc.counters + kTailEpochDown, epoch, tile, row,
                 bf16_round(bf16_round(sum) * g_down));
   }
   ResidualTail* tail;
@@ -647,7 +647,7 @@ __global__ void __launch_bounds__(kGemvThreads, 1) ffn_down_kernel(const __grid_
   op.tail = &tail;
   op.tp = &tp;
   gemv_run<typename Shapes<NTP>::Down>(op, smem, sc);
-  tail_update(tail, a.residual, sc, op.epoch, kH / kTileRows, a.layer_scalar);
+  tail_update(tail, a.residual, sc, sc.tile_ss + kTileSsDown, op.epoch, kH / kTileRows, a.layer_scalar);
   G4_STAMP(sc, 8);
 }
 

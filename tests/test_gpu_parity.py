@@ -113,6 +113,25 @@ def test_qkv_ring_2048_and_bad_offset(device):
     assert err.value.flags & 1
 
 
+def test_qkv_last_slot_and_last_rope_row(device):
+    """The largest valid offsets: the ring's last slot and the RoPE table's last row."""
+    d = synth.sliding_project_qkv(6)
+    ring, rows = 1024, 32768
+    d["pos"] = rows - 1
+    d["kv_offset"] = np.array([(ring - 1) * 8 * 256 * 2], np.int32)
+    d["rope_offset"] = np.array([(rows - 1) * 256 * 2], np.int32)
+    q, kc, vc = run_qkv(device, d, ring=ring, rows=rows)
+    ref_q, ref_k, ref_v = oracle.sliding_project_qkv(d["x"], d["q_weight"], d["k_weight"], d["v_weight"],
+                                                     d["q_weight_scale"], d["k_weight_scale"], d["v_weight_scale"],
+                                                     d["input_rms_weight"], d["q_rms_weight"], d["k_rms_weight"],
+                                                     d["cos_row"], d["sin_row"])
+    for want, got in ((ref_q, q), (ref_k, kc[ring - 1]), (ref_v, vc[ring - 1])):
+        ok, maxd, exact = within(want, got, ATOL["sliding_project_qkv"])
+        assert ok and exact > 0.99, (maxd, exact)
+    check_untouched(kc, ring - 1, SENTINEL_K)
+    check_untouched(vc, ring - 1, SENTINEL_V)
+
+
 # --------------------------------------------------------------------------------- O
 
 def run_o(device, x, gamma, w, s, residual):
@@ -165,6 +184,41 @@ def test_ffn_stress_exact(device, golden_stress):
     assert np.array_equal(got, golden_stress["expected"]), np.unique(got, return_counts=True)
 
 
+def test_interleaved_o_and_ffn_on_a_new_context(device):
+    """O and FFN calls alternating on a new context, as a decode loop issues them: every FFN
+    result is the stress case's exact expectation. The two ops' residual tails count their calls
+    separately (call n of each carries epoch n), so neither may take the other's tile sums."""
+    from g4b200 import ops
+
+    ctx = ops.Device(0)
+    try:
+        o = synth.sliding_attention_output(0)
+        stress = synth.ffn_stress()
+        for _ in range(3):
+            res = dev_tensor(o["residual"])
+            ops.sliding_attention_output(ctx, dev_tensor(o["x"]), dev_tensor(o["post_attn_rms_weight"]),
+                                         dev_tensor(o["o_weight"]), dev_tensor(o["o_weight_scale"]), res)
+            got = run_ffn(ctx, stress)
+            assert np.array_equal(got, stress["expected"]), np.unique(got, return_counts=True)
+    finally:
+        ctx.close()
+
+
+def test_ffn_zero_residual(device):
+    """An all-zero hidden state: every activation of the three projections is zero (the digit
+    exponent of an all-zero block), and the result is the oracle's zeros."""
+    d = synth.decoder_feedforward(2)
+    d["residual"] = np.zeros_like(d["residual"])
+    got = run_ffn(device, d)
+    want = oracle.decoder_feedforward(d["residual"], d["pre_ff_rms_weight"], d["up_weight_packed"],
+                                      d["gate_weight_packed"], d["down_weight_packed"], d["up_weight_scale"],
+                                      d["gate_weight_scale"], d["down_weight_scale"], d["up_global_scale"][0],
+                                      d["gate_global_scale"][0], d["down_global_scale"][0], d["post_ff_rms_weight"],
+                                      d["layer_scalar"])
+    assert not np.any(oracle.bf16_to_f32(want))
+    assert within(want, got, ATOL["decoder_feedforward"])[0]
+
+
 def test_ffn_deterministic(device):
     d = synth.decoder_feedforward(5)
     a = run_ffn(device, d)
@@ -198,9 +252,9 @@ def test_attention_matches_oracle_and_reference_sdpa(device, case, golden_attent
     assert within(golden_attention[f"case{case}.expected"], got, atol)[0]
 
 
-@pytest.mark.parametrize("ring,scale", [(1024, 1.0 / 16), (4096, 1.0 / 16), (2048, 1.0)])
+@pytest.mark.parametrize("ring,scale", [(1024, 1.0 / 16), (4096, 1.0 / 16), (2048, 1.0), (8192, 1.0 / 16)])
 def test_attention_rings_and_scales(device, ring, scale):
-    """BASELINE config c2 (L in {1024, 4096}, scale 1/16) and a masked ring."""
+    """BASELINE config c2 (L in {1024, 4096}, scale 1/16), a masked ring, and the largest ring."""
     from oracle import prng
 
     q = prng.bf16_signs(f"attn.{ring}.q", 16 * 256, 1.0).reshape(8, 2, 256)
