@@ -204,6 +204,53 @@ def test_interleaved_o_and_ffn_on_a_new_context(device):
         ctx.close()
 
 
+def test_layer_loop_matches_single_calls(device):
+    """The four ops called in a decode loop's order (QKV, attention, O, FFN) three times on one
+    context give bit for bit what each op gives alone on a new context: no op's call history
+    leaks into another's result."""
+    from g4b200 import ops
+
+    d = synth.sliding_project_qkv(3)
+    o = synth.sliding_attention_output(2)
+    f = synth.decoder_feedforward(4)
+    from oracle import prng
+
+    qa = prng.bf16_signs("loop.q", 16 * 256, 1.0).reshape(8, 2, 256)
+    ka = prng.bf16_uniform("loop.k", 1024 * 8 * 256, -1.0, 1.0).reshape(1024, 8, 256)
+    va = prng.bf16_uniform("loop.v", 1024 * 8 * 256, -1.0, 1.0).reshape(1024, 8, 256)
+    ma = (np.arange(1024) < 800).astype(np.float32)
+
+    def step(ctx):
+        out = list(run_qkv(ctx, d))
+        out.append(run_attention(ctx, qa, ka, va, ma, 1.0 / 16))
+        out.append(run_o(ctx, o["x"], o["post_attn_rms_weight"], o["o_weight"], o["o_weight_scale"], o["residual"]))
+        out.append(run_ffn(ctx, f))
+        return out
+
+    singles = []
+    for i in range(4):  # each op alone on its own new context
+        ctx = ops.Device(0)
+        try:
+            if i == 0:
+                singles += list(run_qkv(ctx, d))
+            elif i == 1:
+                singles.append(run_attention(ctx, qa, ka, va, ma, 1.0 / 16))
+            elif i == 2:
+                singles.append(run_o(ctx, o["x"], o["post_attn_rms_weight"], o["o_weight"], o["o_weight_scale"],
+                                     o["residual"]))
+            elif i == 3:
+                singles.append(run_ffn(ctx, f))
+        finally:
+            ctx.close()
+    ctx = ops.Device(0)
+    try:
+        for _ in range(3):
+            for got, want in zip(step(ctx), singles):
+                assert np.array_equal(got, want)
+    finally:
+        ctx.close()
+
+
 def test_ffn_zero_residual(device):
     """An all-zero hidden state: every activation of the three projections is zero (the digit
     exponent of an all-zero block), and the result is the oracle's zeros."""
