@@ -82,7 +82,8 @@ struct GemvShape {
   static constexpr size_t kOffH = kOffB + size_t(BSLOTS) * kBSlotBytes;
   static constexpr size_t kOffExp = kOffH + (FP4 ? size_t(BSLOTS) * 512 : 0);
   static constexpr size_t kOffCtl = kOffExp + (FP4 ? 0 : size_t(BSLOTS) * 16 * sizeof(float));
-  static constexpr size_t kSmemBytes = kOffCtl + 1024 + 1024;  // control block + alignment slack
+  static constexpr size_t kCtlBytes = 2048;
+  static constexpr size_t kSmemBytes = kOffCtl + kCtlBytes + 1024;  // control block + alignment slack
   static_assert(kStageBytes % 1024 == 0, "stages must keep 1024-byte alignment");
   static_assert(kSmemBytes <= 227 * 1024, "shared memory budget");
 };
@@ -97,8 +98,8 @@ struct GemvCtl {
   float xchg[64];
   __align__(16) uint16_t out16[kTileRows];  // a tile's bf16 results, stored to global 16 bytes at a time
   double red_d[8];
-  float red_f[8];
 };
+static_assert(sizeof(GemvCtl) <= 2048, "the control block's share of the engine's shared memory (kCtlBytes)");
 
 __device__ __forceinline__ uint8_t* align1024(uint8_t* p) {
   return reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(p) + 1023) & ~uintptr_t(1023));
