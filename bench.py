@@ -7,23 +7,28 @@ sliding_attention_output (FP8) -> decoder_feedforward (NVFP4), all through libg4
 
     python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
 
-- value: tokens/s through one layer, device-timed with CUDA events over K steps replayed from a
-  CUDA graph, with weights, caches and activations resident in HBM (max over ranks). N>1 splits
-  the layer tensor-parallel over the N GPUs (KV heads and FFN rows per rank; the O and down
-  partial sums are added across the GPUs inside those kernels over NVLink): one token per step
-  for the whole job, strong scaling.
-- e2e: the same metric through the public C ABI from pinned host buffers: every step copies the
-  token's hidden state and position offsets host->device, runs the four ops and reads the
-  resulting hidden state back.
+- parity: before anything is timed, one step on the bench's own layer is checked against the
+  CPU oracle (oracle/ops.py, numpy; the checker, outside every timed region): each op's output
+  within the reference grader's tolerance, and under tensor parallelism every rank's residual
+  bit for bit the same. The result is the line's "parity" object.
+- value: tokens/s through one layer, device-timed with CUDA events over exactly K steps (after
+  exactly W warm-up steps) replayed from CUDA graphs, with weights, caches and activations
+  resident in HBM (max over ranks). N>1 splits the layer tensor-parallel over the N GPUs (KV
+  heads and FFN rows per rank; the O and down partial sums are added across the GPUs inside
+  those kernels over NVLink): one token per step for the whole job, strong scaling.
+- e2e: the same metric through the public C ABI with host buffers: every step copies the
+  token's hidden state and position offsets from pinned host memory to the device, runs the four
+  ops and copies the resulting hidden state back to pinned host memory, all inside the timed
+  region (captured in the same graphs as the ops).
 - roofline: the dominant op (decoder_feedforward, 99.56 MB of algorithmic traffic per call)
   timed alone against the measured HBM copy bandwidth.
 - cpu_baseline / --impl reference: the CPU oracle port (numpy, test infrastructure) running the
-  same layer step on this host's cores.
+  same layer step on this host's cores, with every host thread.
 
 Synthetic data (no checkpoint exists on the box): weights ~N(0, 0.02) quantised the way
 BASELINE.json describes (FP8 e4m3 per output row; NVFP4 e2m1 codes with e4m3 per-16 block
 scales and an f32 per-tensor scale), activations and caches ~N(0, 1). Four distinct layers
-(588 MB of weights, > 4x the 126 MB L2) are rotated so no step reads weights from L2.
+(621 MB of weights, > 4x the 126 MB L2) are rotated so no step reads weights from L2.
 """
 
 from __future__ import annotations
@@ -139,7 +144,11 @@ def quant_fp8_rows(w):
 
 
 def quant_nvfp4(w):
-    """NVFP4: f32 global = amax/(6*448); e4m3 scale per 16 = block amax/6/global; e2m1 codes."""
+    """NVFP4: f32 global = amax/(6*448); e4m3 scale per 16 = block amax/6/global; e2m1 codes.
+
+    The op takes the global multiplier itself: the reciprocal of a checkpoint's
+    weight_global_scale (= 6*448/amax), as the reference's loader passes it
+    (FOG/src/host/load.rs:170-190)."""
     import torch
 
     rows, cols = w.shape
@@ -152,13 +161,16 @@ def quant_nvfp4(w):
     mag = torch.bucketize(x.abs(), bounds).to(torch.uint8)
     codes = mag | ((x < 0).to(torch.uint8) << 3)
     packed = (codes[:, 0::2] | (codes[:, 1::2] << 4)).contiguous()
-    return packed, bscale.view(torch.uint8).contiguous(), torch.tensor([1.0 / float(g)], device=w.device)
+    return packed, bscale.view(torch.uint8).contiguous(), g.reshape(1).to(torch.float32).contiguous()
 
 
 class Layer:
-    """One decoder layer's weights and ring caches (whole; `shard` keeps one rank's slices)."""
+    """One decoder layer's weights and ring caches (whole; `shard` keeps one rank's slices).
 
-    def __init__(self, gen, dev):
+    keep_host=True also keeps a host copy of the whole layer's tensors in the reference layout
+    (`self.host`, numpy: bf16 as uint16 bits, codes as uint8), for the parity check."""
+
+    def __init__(self, gen, dev, keep_host=False):
         import torch
 
         def normal(*shape, std=1.0):
@@ -184,6 +196,11 @@ class Layer:
         self.down_p, self.down_s, self.down_g = quant_nvfp4(normal(H, L, std=0.02))
         self.layer_scalar = bf(torch.full((8,), 0.375, device=dev))
         self.tiled = False
+        self.host = {k: host_array(getattr(self, k)) for k in self.HOST} if keep_host else None
+
+    HOST = ("input_rms", "q_w", "k_w", "v_w", "q_s", "k_s", "v_s", "q_rms", "k_rms", "post_attn_rms", "o_w", "o_s",
+            "pre_ff_rms", "post_ff_rms", "up_p", "up_s", "up_g", "gate_p", "gate_s", "gate_g", "down_p", "down_s",
+            "down_g", "layer_scalar")
 
     # attribute -> the reference op parameter it is passed as (g4b200.tp's slicing rules)
     SHARDED = {"q_w": "q_weight", "k_w": "k_weight", "v_w": "v_weight", "q_s": "q_weight_scale",
@@ -212,6 +229,19 @@ class Layer:
         return self
 
 
+def host_array(t):
+    """A torch tensor as numpy on the host: bf16 as uint16 bits, everything else as it is."""
+    import numpy as np
+    import torch
+
+    t = t.detach().contiguous().cpu()
+    if t.dtype == torch.bfloat16:
+        return t.view(torch.int16).numpy().view(np.uint16).copy()
+    if t.dtype == torch.float8_e4m3fn:
+        return t.view(torch.uint8).numpy().copy()
+    return t.numpy().copy()
+
+
 class Workspace:
     """Per-token buffers shared by the layers (the reference host's Workspace/Decode)."""
 
@@ -221,6 +251,7 @@ class Workspace:
 
         from oracle.ops import negate_low_half, rope_tables  # table construction only
 
+        self.pos = pos
         self.residual = (torch.randn(H, generator=gen, device=dev)).to(torch.bfloat16)
         cos = np.zeros((E, DS), np.float32)
         sin = np.zeros((E, DS), np.float32)
@@ -241,7 +272,7 @@ def layer_step(ops, device, w: Workspace, lay: Layer, which=("qkv", "attn", "o",
                                 lay.input_rms, lay.q_rms, lay.k_rms, w.kv_offset, w.rope_offset, w.cos, w.sin,
                                 lay.k_cache, lay.v_cache, w.q, tiled=lay.tiled)
     if "attn" in which:
-        ops.sliding_attention(device, w.q, lay.k_cache, lay.v_cache, w.mask, w.attn, scale=1.0)
+        ops.sliding_attention(device, w.q, lay.k_cache, lay.v_cache, w.mask, w.attn, scale=ATTN_SCALE)
     if "o" in which:
         ops.sliding_attention_output(device, w.attn, lay.post_attn_rms, lay.o_w, lay.o_s, w.residual,
                                      tiled=lay.tiled)
@@ -255,10 +286,116 @@ def layer_step(ops, device, w: Workspace, lay: Layer, which=("qkv", "attn", "o",
 
 
 KERNELS_PER_OP = {"qkv": 1, "attn": 1, "o": 1, "ffn": 2}
+ATTN_SCALE = 1.0  # the reference model's sliding attention (gemma4.py:179-181)
 
+
+# ------------------------------------------------------------------------------ parity gate
+
+# the reference grader's tolerances (FOG/src/bin/test_kernels.rs:447-465): |want - got| <=
+# atol + rtol |want|; attention (never graded by the reference) is held to 0.01
+RTOL = 1e-2
+ATOL = {"sliding_project_qkv": 0.04, "sliding_attention": 0.01, "sliding_attention_output": 0.05,
+        "decoder_feedforward": 0.01}
+
+
+def compare(name, want, got):
+    import numpy as np
+
+    from oracle.ops import bf16_to_f32
+
+    w, g = bf16_to_f32(np.asarray(want).reshape(-1)), bf16_to_f32(np.asarray(got).reshape(-1))
+    diff = np.abs(w - g)
+    ok = bool(np.isfinite(g).all() and (diff <= ATOL[name] + RTOL * np.abs(w)).all())
+    return {"ok": ok, "max_abs": float(diff.max()), "atol": ATOL[name], "rtol": RTOL,
+            "bit_exact": round(float(np.mean(np.asarray(want).reshape(-1) == np.asarray(got).reshape(-1))), 5)}
+
+
+def parity_step(ops, device, ws, lay, rank, world, dist):
+    """Run one layer step op by op and check every op's output against the CPU oracle, each op
+    on the inputs the GPU's previous op produced (so a failure names the op). Under tensor
+    parallelism the ranks' slices are gathered to rank 0, the O and FFN oracles add the ranks'
+    partial sums in rank order (oracle/ops.py *_tp), and every rank's residual must have the
+    same bits. Returns the line's "parity" object on rank 0 (None elsewhere)."""
+    import numpy as np
+    import torch
+
+    from g4b200 import tp
+
+    def gather(t):  # every rank's tensor, in rank order, on rank 0's host
+        t = t.contiguous()
+        if world == 1:
+            return [host_array(t)]
+        parts = [torch.empty_like(t) for _ in range(world)]
+        dist.all_gather(parts, t)
+        return [host_array(p) for p in parts]
+
+    slot = ws.pos % TS
+    res0 = host_array(ws.residual)
+    layer_step(ops, device, ws, lay, ("qkv",))
+    device.check()
+    q = np.concatenate(gather(ws.q), axis=0)
+    kc = np.concatenate(gather(lay.k_cache), axis=1)
+    vc = np.concatenate(gather(lay.v_cache), axis=1)
+    layer_step(ops, device, ws, lay, ("attn",))
+    device.check()
+    attn_parts = gather(ws.attn)
+    layer_step(ops, device, ws, lay, ("o",))
+    device.check()
+    res1_parts = gather(ws.residual)
+    layer_step(ops, device, ws, lay, ("ffn",))
+    device.check()
+    res2_parts = gather(ws.residual)
+    cos, sin = host_array(ws.cos[ws.pos]), host_array(ws.sin[ws.pos])
+    mask = host_array(ws.mask)
+    if rank != 0:
+        return None
+
+    from oracle import ops as oracle
+
+    h = lay.host
+    out = {}
+    wq, wk, wv = oracle.sliding_project_qkv(res0, h["q_w"], h["k_w"], h["v_w"], h["q_s"], h["k_s"], h["v_s"],
+                                            h["input_rms"], h["q_rms"], h["k_rms"], cos, sin)
+    got = np.concatenate([q.reshape(-1), kc[slot].reshape(-1), vc[slot].reshape(-1)])
+    out["sliding_project_qkv"] = compare("sliding_project_qkv", np.concatenate(
+        [wq.reshape(-1), wk.reshape(-1), wv.reshape(-1)]), got)
+    attn = np.concatenate(attn_parts, axis=0)
+    out["sliding_attention"] = compare("sliding_attention", oracle.sliding_attention(q, kc, vc, mask, ATTN_SCALE),
+                                       attn)
+
+    def cut(name, arr):
+        return tp.shard(name, torch.from_numpy(arr), r, world).numpy()
+
+    if world == 1:
+        want_o = oracle.sliding_attention_output(attn, h["post_attn_rms"], h["o_w"], h["o_s"], res0)
+        want_f = oracle.decoder_feedforward(res1_parts[0], h["pre_ff_rms"], h["up_p"], h["gate_p"], h["down_p"],
+                                            h["up_s"], h["gate_s"], h["down_s"], h["up_g"][0], h["gate_g"][0],
+                                            h["down_g"][0], h["post_ff_rms"], h["layer_scalar"])
+    else:
+        o_parts, up, gate, down = [], [], [], []
+        for r in range(world):
+            o_parts.append(cut("o_weight", h["o_w"]))
+            up.append((cut("up_weight_packed", h["up_p"]), cut("up_weight_scale", h["up_s"])))
+            gate.append((cut("gate_weight_packed", h["gate_p"]), cut("gate_weight_scale", h["gate_s"])))
+            down.append((cut("down_weight_packed", h["down_p"]), cut("down_weight_scale", h["down_s"])))
+        want_o = oracle.sliding_attention_output_tp([a.reshape(-1) for a in attn_parts], h["post_attn_rms"], o_parts,
+                                                    h["o_s"], res0)
+        want_f = oracle.decoder_feedforward_tp(res1_parts[0], h["pre_ff_rms"], up, gate, down, h["up_g"][0],
+                                               h["gate_g"][0], h["down_g"][0], h["post_ff_rms"], h["layer_scalar"])
+    out["sliding_attention_output"] = compare("sliding_attention_output", want_o, res1_parts[0])
+    out["decoder_feedforward"] = compare("decoder_feedforward", want_f, res2_parts[0])
+    same = all(np.array_equal(p, res1_parts[0]) for p in res1_parts) and \
+        all(np.array_equal(p, res2_parts[0]) for p in res2_parts)
+    return {"ok": all(v["ok"] for v in out.values()) and same, "ranks_bit_identical": same if world > 1 else None,
+            "ops": out, "checked": f"one step on layer copy 0 at position {ws.pos}, each op against oracle/ops.py "
+                                   "(numpy) on the previous op's GPU output" +
+                                   (", O/FFN as the rank-order sum of the ranks' partials" if world > 1 else "")}
+
+
+# ------------------------------------------------------------------------------ timing helpers
 
 def capture(torch, fn, reps):
-    """A CUDA graph of `reps` calls of fn(i)."""
+    """A CUDA graph of fn(0), ..., fn(reps - 1) (fn issues work on the current stream)."""
     s = torch.cuda.Stream()
     s.wait_stream(torch.cuda.current_stream())
     with torch.cuda.stream(s):
@@ -272,18 +409,66 @@ def capture(torch, fn, reps):
     return g
 
 
-def time_graph(torch, graph, replays):
+class Stepper:
+    """Replays exactly n steps of `step(layer)` rotating over `n_layers` layer copies: a graph of
+    `block` steps (a multiple of n_layers, starting at layer 0) where it fits, one-step graphs
+    (one per layer copy) elsewhere, so any n is honoured without breaking the rotation."""
+
+    def __init__(self, torch, step, n_layers, block):
+        assert block % n_layers == 0
+        self.n_layers, self.block = n_layers, block
+        self.big = capture(torch, lambda i: step(i % n_layers), block)
+        self.single = [capture(torch, lambda i, lay=lay: step(lay), 1) for lay in range(n_layers)]
+        self.at = 0  # index of the next step (its layer is at % n_layers)
+
+    def run(self, n):
+        left = n
+        while left:
+            if self.at % self.n_layers == 0 and left >= self.block:
+                self.big.replay()
+                self.at += self.block
+                left -= self.block
+            else:
+                self.single[self.at % self.n_layers].replay()
+                self.at += 1
+                left -= 1
+
+
+def timed(torch, fn):
+    """Device seconds of fn()'s work on the current stream (CUDA events, synchronised on both sides)."""
     start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     torch.cuda.synchronize()
     start.record()
-    for _ in range(replays):
-        graph.replay()
+    fn()
     end.record()
     torch.cuda.synchronize()
     return start.elapsed_time(end) / 1e3
 
 
+def max_over_ranks(torch, dist, dev, secs):
+    if dist is None:
+        return secs
+    t = torch.tensor([secs], device=dev)
+    dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    return float(t.item())
+
+
+def config_for(world):
+    return {"workload": WORKLOAD, "global_batch": 1, "seq_len": TS,
+            "parallelism": f"tp{world}" if world > 1 else "single GPU",
+            "l2": f"inputs larger than L2: {N_LAYERS} distinct layers ({N_LAYERS * sum(op_bytes(world).values()) / 1e6:.0f}"
+                  " MB per GPU) rotated step to step",
+            "launch": "CUDA graphs of C-ABI calls, programmatic dependent launch"}
+
+
 # ------------------------------------------------------------------------------ CPU legs
+
+def host_threads():
+    try:
+        return len(os.sched_getaffinity(0))
+    except AttributeError:
+        return os.cpu_count() or 1
+
 
 class CpuLayer:
     """The oracle port (numpy, all BLAS threads) running the same layer step on the host."""
@@ -338,20 +523,37 @@ class CpuLayer:
             self.step()
             n += 1
         elapsed = time.time() - t0
-        cores = os.cpu_count() or 1
-        return n / elapsed, cores, (f"{n} layer steps of the numpy oracle port over {elapsed:.1f} s on {cores} host "
-                                    f"threads (f32 BLAS GEMV on pre-dequantised weights; "
-                                    f"{self.setup_s:.1f} s of weight setup untimed)")
+        return n / elapsed, (f"{n} layer steps of the numpy oracle port over {elapsed:.1f} s on {host_threads()} host "
+                             f"threads (f32 BLAS GEMV on pre-dequantised weights; "
+                             f"{self.setup_s:.1f} s of weight setup untimed)")
+
+
+def use_all_host_threads():
+    """Every host thread for the CPU legs: torchrun sets OMP_NUM_THREADS=1 for its ranks, which
+    would leave the BLAS of the numpy port on one core. Set before numpy loads its BLAS, and
+    again through threadpoolctl in case it was already loaded."""
+    n = host_threads()
+    for var in ("OMP_NUM_THREADS", "OPENBLAS_NUM_THREADS", "MKL_NUM_THREADS"):
+        os.environ[var] = str(n)
+    try:
+        from threadpoolctl import threadpool_limits
+
+        threadpool_limits(limits=n)
+    except Exception:
+        pass
+    return n
 
 
 def run_reference(args):
     """The reference arm: the CPU oracle port on this host, same metric and workload.
 
-    Each step is one layer step of the port; at most ~90 s of steps run (the rest of K would
-    repeat identical work), and the line reports the median per-step rate."""
+    Under torchrun only rank 0 runs it (the others exit at once). Each step is one layer step of
+    the port; at most ~90 s of steps run (the rest of K would repeat identical work), and the
+    line reports the median per-step rate."""
     rank = int(os.environ.get("RANK", "0"))
     if rank != 0:
         return 0
+    cores = use_all_host_threads()
     cpu = CpuLayer()
     for _ in range(args.warmup):
         cpu.step()
@@ -364,14 +566,15 @@ def run_reference(args):
         if time.time() - t0 > 90.0:
             break
     value = statistics.median(rates)
-    cores = os.cpu_count() or 1
     sample = (f"{len(rates)} of {args.steps} requested layer steps of the numpy oracle port (median rate) on "
               f"{cores} host threads; f32 BLAS GEMV on pre-dequantised weights, {cpu.setup_s:.1f} s setup untimed")
     line = {
         "impl": "reference", "metric": METRIC, "value": value, "unit": "tokens/s", "n_gpus": args.gpus,
         "steps": len(rates), "warmup": args.warmup, "ms_per_step": 1e3 / value, "higher_is_better": True,
-        "scaling": "weak", "vs_baseline": None, "dtype": "f32 (numpy oracle port, bf16 rounding points emulated)",
-        "data": "synthetic", "config": {"workload": WORKLOAD, "parallelism": "host CPU, one process"},
+        "scaling": "strong" if args.gpus > 1 else "weak", "vs_baseline": None,
+        "dtype": "f32 (numpy oracle port, bf16 rounding points emulated)",
+        "data": "synthetic", "config": dict(config_for(args.gpus), parallelism=f"host CPU, {cores} threads, one process",
+                                           launch="numpy on the host"),
         "cpu_baseline": {"value": value, "unit": "tokens/s", "cores": cores, "kind": "port", "sample": sample},
         "e2e": {"value": value, "unit": "tokens/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
     }
@@ -394,7 +597,7 @@ def run_ours(args):
 
         import torch.distributed as dist
 
-        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120), device_id=torch.device("cuda", local))
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=300), device_id=torch.device("cuda", local))
 
     from g4b200 import ops, tp
 
@@ -405,91 +608,77 @@ def run_ours(args):
     dev = torch.device("cuda", local)
     gen = torch.Generator(device=dev)
     gen.manual_seed(1000)  # the same whole layers on every rank; each keeps its slices
-    layers = [Layer(gen, dev).shard(rank, world).tile(ops, device) for _ in range(N_LAYERS)]
+    layers = [Layer(gen, dev, keep_host=(i == 0 and rank == 0 and not args.no_parity)).shard(rank, world).tile(ops, device)
+              for i in range(N_LAYERS)]
     ws = Workspace(gen, dev, world=world)
     torch.cuda.synchronize()
     if dist:
         dist.barrier()  # the ranks' kernels wait on each other (bounded): start them together
 
-    # correctness gate before timing: one step, no device-side errors
-    layer_step(ops, device, ws, layers[0])
-    device.check()
+    # --- correctness gate before timing: one step against the CPU oracle
+    parity = None if args.no_parity else parity_step(ops, device, ws, layers[0], rank, world, dist)
+    if dist:
+        dist.barrier()
 
-    # --- device-resident throughput: a graph of N_LAYERS steps (one per layer copy)
+    # --- device-resident throughput: exactly W then K steps from graphs, layers rotated
     per_graph = N_LAYERS * 4
-    graph = capture(torch, lambda i: layer_step(ops, device, ws, layers[i % N_LAYERS]), per_graph)
-    warm_replays = max(1, -(-args.warmup // per_graph))
-    replays = max(1, -(-args.steps // per_graph))
-    steps = replays * per_graph
-    for _ in range(warm_replays):
-        graph.replay()
+    stepper = Stepper(torch, lambda lay: layer_step(ops, device, ws, layers[lay]), N_LAYERS, per_graph)
+    stepper.run(args.warmup)
     torch.cuda.synchronize()
     sampler = ClockSampler(local)
     if dist:
         dist.barrier()
-    torch.cuda.synchronize()
     with sampler:
-        elapsed = time_graph(torch, graph, replays)
-    if dist:
-        t = torch.tensor([elapsed], device=dev)
-        dist.all_reduce(t, op=dist.ReduceOp.MAX)
-        elapsed = float(t.item())
+        elapsed = max_over_ranks(torch, dist, dev, timed(torch, lambda: stepper.run(args.steps)))
+        device.check()
+        value = args.steps / elapsed  # one token through the layer per step, for the whole job
+
+        # --- per-op device time (each op alone, graph of many calls rotating the layers)
+        op_us = {}
+        reps = 64
+        if dist:
+            dist.barrier()
+        for key, name in (("qkv", "sliding_project_qkv"), ("attn", "sliding_attention"),
+                          ("o", "sliding_attention_output"), ("ffn", "decoder_feedforward")):
+            g = capture(torch, lambda i, k=key: layer_step(ops, device, ws, layers[i % N_LAYERS], (k,)), reps)
+            g.replay()
+            op_us[name] = max_over_ranks(torch, dist, dev, timed(torch, lambda: [g.replay() for _ in range(5)])) \
+                / (5 * reps) * 1e6
+            del g
+        device.check()
+
+        # --- end to end through the C ABI from pinned host buffers: every step copies its input
+        # hidden state and position offsets in and its resulting hidden state out
+        host_in = torch.empty(H, dtype=torch.bfloat16).pin_memory()
+        host_kv = torch.empty(1, dtype=torch.int32).pin_memory()
+        host_rope = torch.empty(1, dtype=torch.int32).pin_memory()
+        host_out = torch.empty(H, dtype=torch.bfloat16).pin_memory()
+        host_in.copy_(ws.residual.cpu())
+        host_kv.copy_(ws.kv_offset.cpu())
+        host_rope.copy_(ws.rope_offset.cpu())
+
+        def e2e_step(lay):
+            ws.residual.copy_(host_in, non_blocking=True)
+            ws.kv_offset.copy_(host_kv, non_blocking=True)
+            ws.rope_offset.copy_(host_rope, non_blocking=True)
+            layer_step(ops, device, ws, layers[lay])
+            host_out.copy_(ws.residual, non_blocking=True)
+
+        e2e = Stepper(torch, e2e_step, N_LAYERS, per_graph)
+        e2e.run(args.warmup)
+        torch.cuda.synchronize()
+        if dist:
+            dist.barrier()
+        e2e_elapsed = max_over_ranks(torch, dist, dev, timed(torch, lambda: e2e.run(args.steps)))
     device.check()
-    value = steps / elapsed  # one token through the layer per step, for the whole job
-
-    # --- per-op device time (each op alone, graph of many calls rotating the layers)
-    op_us = {}
-    reps = 64
-    if dist:
-        dist.barrier()
-    for key, name in (("qkv", "sliding_project_qkv"), ("attn", "sliding_attention"),
-                      ("o", "sliding_attention_output"), ("ffn", "decoder_feedforward")):
-        g = capture(torch, lambda i, k=key: layer_step(ops, device, ws, layers[i % N_LAYERS], (k,)), reps)
-        g.replay()
-        secs = time_graph(torch, g, 5) / (5 * reps)
-        op_us[name] = secs * 1e6
-        del g
-    device.check()
-
-    # --- end to end through the C ABI from pinned host buffers, no graph
-    host_in = torch.empty(H, dtype=torch.bfloat16).pin_memory()
-    host_off = torch.empty(2, dtype=torch.int32).pin_memory()
-    host_out = torch.empty(H, dtype=torch.bfloat16).pin_memory()
-    host_in.copy_(ws.residual.cpu())
-    host_off[0], host_off[1] = int(ws.kv_offset.item()), int(ws.rope_offset.item())
-    e2e_steps = max(per_graph, min(steps, 2000))
-
-    def e2e_step(i):
-        ws.residual.copy_(host_in, non_blocking=True)
-        ws.kv_offset.copy_(host_off[0:1], non_blocking=True)
-        ws.rope_offset.copy_(host_off[1:2], non_blocking=True)
-        layer_step(ops, device, ws, layers[i % N_LAYERS])
-        host_out.copy_(ws.residual, non_blocking=True)
-
-    for i in range(min(args.warmup, 8) + 1):
-        e2e_step(i)
-    torch.cuda.synchronize()
-    if dist:
-        dist.barrier()
-    start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    torch.cuda.synchronize()
-    start.record()
-    for i in range(e2e_steps):
-        e2e_step(i)
-    end.record()
-    torch.cuda.synchronize()
-    e2e_elapsed = start.elapsed_time(end) / 1e3
-    if dist:
-        t = torch.tensor([e2e_elapsed], device=dev)
-        dist.all_reduce(t, op=dist.ReduceOp.MAX)
-        e2e_elapsed = float(t.item())
-    device.check()
-    e2e_value = e2e_steps / e2e_elapsed
+    e2e_value = args.steps / e2e_elapsed
+    del stepper, e2e
 
     cpu = None
     if rank == 0 and world == 1 and not args.no_cpu:
-        rate, cores, sample = CpuLayer().sample(budget_s=12.0, min_steps=3)
-        cpu = {"value": rate, "unit": "tokens/s", "cores": cores, "kind": "port", "sample": sample}
+        use_all_host_threads()
+        rate, sample = CpuLayer().sample(budget_s=12.0, min_steps=3)
+        cpu = {"value": rate, "unit": "tokens/s", "cores": host_threads(), "kind": "port", "sample": sample}
 
     if dist:
         dist.barrier()
@@ -507,9 +696,9 @@ def run_ours(args):
         "value": value,
         "unit": "tokens/s",
         "n_gpus": world,
-        "steps": steps,
-        "warmup": warm_replays * per_graph,
-        "ms_per_step": elapsed / steps * 1e3,
+        "steps": args.steps,
+        "warmup": args.warmup,
+        "ms_per_step": elapsed / args.steps * 1e3,
         "higher_is_better": True,
         "scaling": "strong" if world > 1 else "weak",
         "vs_baseline": None,
@@ -518,23 +707,22 @@ def run_ours(args):
                       "e2m1 weights with e4m3 block scales (kind::mxf4nvf4) x the activation as exact e2m1 digits; "
                       "f32 accumulation in TMEM",
         "data": "synthetic",
-        "config": {"workload": WORKLOAD, "global_batch": 1, "seq_len": TS,
-                   "parallelism": f"tp{world}" if world > 1 else "single GPU",
-                   "l2": f"inputs larger than L2: {N_LAYERS} distinct layers ({N_LAYERS * layer_bytes / 1e6:.0f} MB "
-                         "per GPU) rotated step to step",
-                   "launch": "CUDA graph of C-ABI calls, programmatic dependent launch"},
+        "config": config_for(world),
+        "parity": parity,
         "ops_us": {k: round(v, 3) for k, v in op_us.items()},
         "ops_gbs": {k: round(rank_bytes[k] / (op_us[k] * 1e-6) / 1e9, 1) for k in op_us},
         "layer_bytes_per_gpu": layer_bytes,
-        "layer_gbs_per_gpu": round(layer_bytes * steps / elapsed / 1e9, 1),
+        "layer_gbs_per_gpu": round(layer_bytes * args.steps / elapsed / 1e9, 1),
         "roofline": {"bound": "hbm", "kernel": "decoder_feedforward (ffn_upgate + ffn_down kernels, one GPU's slice)",
                      "achieved": round(achieved, 1), "peak": pk["hbm_gbs"], "unit": "GB/s",
                      "frac": round(achieved / pk["hbm_gbs"], 4), "peak_source": pk_kind,
                      "algorithmic_bytes_per_launch": ffn_bytes,
                      "traffic": args.traffic if world == 1 else None},
         "e2e": {"value": e2e_value, "unit": "tokens/s", "h2d_bytes_per_step": (H * 2 + 8) * world,
-                "d2h_bytes_per_step": H * 2 * world, "steps": e2e_steps},
-        "gpu_launches": steps * sum(KERNELS_PER_OP.values()),
+                "d2h_bytes_per_step": H * 2 * world, "steps": args.steps,
+                "how": "CUDA graphs of [pinned host->device copy of the hidden state and offsets, the four C-ABI ops, "
+                       "device->pinned host copy of the new hidden state] per step"},
+        "gpu_launches": args.steps * sum(KERNELS_PER_OP.values()),
         "clocks": sampler.summary(),
         "cpu_baseline": cpu,
     }
@@ -578,15 +766,18 @@ def main():
     ap.add_argument("--only", choices=sorted(KERNELS_PER_OP), default=None,
                     help="profiling aid: eager calls of one op only (prints us/call, not the bench line)")
     ap.add_argument("--gpus", type=int, default=1)
-    ap.add_argument("--steps", type=int, default=4096)
+    ap.add_argument("--steps", type=int, default=2048)
     ap.add_argument("--warmup", type=int, default=64)
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--no-cpu", action="store_true", help="skip the CPU baseline sample")
+    ap.add_argument("--no-parity", action="store_true", help="skip the parity gate (profiling runs)")
     ap.add_argument("--traffic", type=float, default=FFN_TRAFFIC,
                     help="ncu dram bytes (read + write) per decoder_feedforward call")
     args = ap.parse_args()
     if args.warmup < 3:
         args.warmup = 3
+    if args.steps < 1:
+        ap.error("--steps must be at least 1")
     if args.only:
         return run_only(args)
     return run_reference(args) if args.impl == "reference" else run_ours(args)

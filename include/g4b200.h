@@ -50,6 +50,7 @@ typedef int32_t g4_status;
 #define G4_DEVERR_NEGATIVE_SCALE 16u /* an nvfp4 block scale is negative (the reference's loader
                                        * and harness only produce non-negative ones) */
 #define G4_DEVERR_PEER_TIMEOUT 32u   /* a tensor-parallel peer's partial sums did not arrive */
+#define G4_DEVERR_TOKEN_OFFSET 64u   /* an embedding offset outside the table or not row-aligned */
 
 typedef struct g4_ctx g4_ctx;
 
@@ -68,6 +69,22 @@ g4_status g4_ctx_set_overlap(g4_ctx* ctx, int enable);
 
 const char* g4_status_string(g4_status status);
 const char* g4_last_error(const g4_ctx* ctx);
+
+/* Replaces ops::embed_token (src/ops.rs:8-35): out[H] = bf16(f32(embedding_table[row]) * 61.967734),
+ * where offset is one device i32, the BYTE offset of the row (token * H * 2, as
+ * src/host/runtime.rs:348 computes it). embedding_table [vocab_rows, H] bf16: the reference's
+ * W = 262144 rows (any count up to 262144 is accepted). An out-of-table or misaligned offset
+ * writes nothing and raises G4_DEVERR_TOKEN_OFFSET. */
+g4_status g4_embed_token(g4_ctx* ctx, const uint16_t* embedding_table, const int32_t* offset, uint16_t* out,
+                         int32_t vocab_rows, void* stream);
+
+/* Replaces ops::final_norm_and_logits (src/ops.rs:241-298): h = RMSNorm_rms_weight(input) (bf16),
+ * out[v] = bf16(tanh(f32(bf16(h . lm_head_weight[v])) / 30) * 30) with an f32 contraction.
+ * input, rms_weight [H] bf16; lm_head_weight [vocab_rows, H] bf16 (the reference ties it to the
+ * embedding table, W = 262144 rows; a tensor-parallel rank passes its slice of rows and gets those
+ * rows' logits); out [vocab_rows] bf16. */
+g4_status g4_final_norm_and_logits(g4_ctx* ctx, const uint16_t* input, const uint16_t* rms_weight,
+                                   const uint16_t* lm_head_weight, uint16_t* out, int32_t vocab_rows, void* stream);
 
 /* Replaces ops::sliding_project_qkv (src/ops.rs:37-76).
  * x[H], q_weight[Qs,H], k_weight[Ps,H], v_weight[Ps,H] (f8e4m3), *_weight_scale bf16 per row,
@@ -111,6 +128,21 @@ g4_status g4_decoder_feedforward(g4_ctx* ctx, uint16_t* residual_hbm, const uint
                                  const float* down_global_scale, const uint16_t* post_ff_rms_weight,
                                  const uint16_t* layer_scalar, void* stream);
 
+/* The GeGLU feed-forward with FP8 weights (the reference's op,
+ * src/ops.rs:201-239, stores NVFP4): the same pre-RMSNorm, GeGLU, post-RMSNorm, residual and
+ * layer-scalar epilogue around three scaled projections bf16((x @ codes.T) * scale) with f32
+ * per-output-channel scales (the reference oracle's scaled_projection,
+ * scripts/generate_references.py:265-274). residual_hbm [H] bf16 in place; up_weight /
+ * gate_weight [L, H] and down_weight [H, L] f8e4m3; up/gate_weight_scale [L] and
+ * down_weight_scale [H] f32; layer_scalar bf16 (element 0 is used). Parameter order follows
+ * decoder_feedforward with the packed codes, block scales and global scales replaced by the
+ * codes and the channel scales. */
+g4_status g4_decoder_feedforward_fp8(g4_ctx* ctx, uint16_t* residual_hbm, const uint16_t* pre_ff_rms_weight,
+                                     const uint8_t* up_weight, const uint8_t* gate_weight, const uint8_t* down_weight,
+                                     const float* up_weight_scale, const float* gate_weight_scale,
+                                     const float* down_weight_scale, const uint16_t* post_ff_rms_weight,
+                                     const uint16_t* layer_scalar, void* stream);
+
 /* GPU-native weight layout (no reference counterpart: the reference's loader,
  * src/host/load.rs:142-325, writes row-major HBM tensors). The weights are static, so a caller
  * packs them once at load time; the *_tiled entry points below then fetch every pipeline unit
@@ -125,7 +157,9 @@ g4_status g4_decoder_feedforward(g4_ctx* ctx, uint16_t* residual_hbm, const uint
  *   up + gate packed codes (src = up, src2 = gate)              128, 64
  *   up + gate block scales (src = up, src2 = gate)              16, 64
  *   down packed codes                                           128, 128
- *   down block scales                                           16, 128 */
+ *   down block scales                                           16, 128
+ *   FP8 feed-forward: up + gate codes (src = up, src2 = gate)   128, 64
+ *   FP8 feed-forward: down codes                                128, 128 */
 g4_status g4_pack_tiles(g4_ctx* ctx, const uint8_t* src, const uint8_t* src2, uint8_t* dst, int32_t rows,
                         int32_t row_bytes, int32_t unit_bytes, int32_t tile_rows, void* stream);
 
@@ -149,6 +183,11 @@ g4_status g4_decoder_feedforward_tiled(g4_ctx* ctx, uint16_t* residual_hbm, cons
                                        const float* up_global_scale, const float* gate_global_scale,
                                        const float* down_global_scale, const uint16_t* post_ff_rms_weight,
                                        const uint16_t* layer_scalar, void* stream);
+g4_status g4_decoder_feedforward_fp8_tiled(g4_ctx* ctx, uint16_t* residual_hbm, const uint16_t* pre_ff_rms_weight,
+                                           const uint8_t* up_gate_weight_tiled, const uint8_t* down_weight_tiled,
+                                           const float* up_weight_scale, const float* gate_weight_scale,
+                                           const float* down_weight_scale, const uint16_t* post_ff_rms_weight,
+                                           const uint16_t* layer_scalar, void* stream);
 
 /* No counterpart in the reference: ops::sliding_attention_output (src/ops.rs:130-146) with no
  * context and no allocation, for callers that cannot create a g4_ctx. g4_ctx_create allocates
@@ -165,13 +204,117 @@ g4_status g4_decoder_feedforward_tiled(g4_ctx* ctx, uint16_t* residual_hbm, cons
  * starts: the call zeroes it with cudaMemsetAsync on `stream` before each launch.
  * The first call on a device looks up the block's address (cudaGetSymbolAddress, which may load
  * the module) and sets kernel attributes: make that first call before any stream capture that
- * should contain this op. The block is shared by every call on the device, so two calls whose
+ * should contain this op. The address belongs to the CUDA context it was looked up in: a call
+ * whose current context on the device is another one (after cudaDeviceReset, or under a
+ * driver-API context) looks it up again. The block is shared by every call on the device, so two calls whose
  * executions overlap on the GPU (two streams, two threads) race and corrupt each other's
  * results: order them on one stream. Device-side error bits of this entry point are not
  * reported (there is no context to read them from). */
 g4_status g4_sliding_attention_output_noalloc(const uint16_t* x, const uint16_t* post_attn_rms_weight,
                                               const uint8_t* o_weight, const uint16_t* o_weight_scale,
                                               uint16_t* residual_hbm, void* stream);
+
+/* ---- Decode: one token through a whole model per call (the reference host's
+ * Decode::run / run_layers, src/host/runtime.rs:340-451, and its per-token position offsets,
+ * runtime.rs:231-247). No reference counterpart as a single call: the reference host launches
+ * the ops one by one; here the ops of every layer are issued on one stream with programmatic
+ * dependent launch and can be captured into one CUDA graph.
+ *
+ * A model is a table of layers. Each layer is the reference's sliding layer
+ * (sliding_project_qkv -> sliding_attention -> sliding_attention_output -> decoder_feedforward)
+ * with its own KV ring of ring_len slots and one of two RoPE tables: G4_ROPE_LOCAL (theta 1e4,
+ * the sliding layers) or G4_ROPE_GLOBAL (theta 1e6: the BASELINE-shaped global layers, which keep
+ * the sliding geometry with a longer ring). The feed-forward is NVFP4 (decoder_feedforward) or
+ * FP8 (decoder_feedforward_fp8). Pointers are those of the op entry points (device memory of the
+ * context's device, 16-byte aligned; on a tensor-parallel context, this rank's slices). */
+#define G4_ROPE_LOCAL 0
+#define G4_ROPE_GLOBAL 1
+#define G4_FFN_NVFP4 0
+#define G4_FFN_FP8 1
+typedef struct g4_layer {
+  int32_t rope;       /* G4_ROPE_LOCAL or G4_ROPE_GLOBAL */
+  int32_t ring_len;   /* KV ring slots: a positive multiple of 256, at most 8192 */
+  int32_t ffn;        /* G4_FFN_NVFP4 or G4_FFN_FP8 */
+  int32_t tiled;      /* weights in the g4_pack_tiles layout (the *_tiled entry points) */
+  float attn_scale;   /* sliding_attention's scale (the reference model: 1.0) */
+  const uint16_t* input_rms_weight;
+  const uint8_t* q_weight;
+  const uint8_t* k_weight;
+  const uint8_t* v_weight;
+  const uint16_t* q_weight_scale;
+  const uint16_t* k_weight_scale;
+  const uint16_t* v_weight_scale;
+  const uint16_t* q_rms_weight;
+  const uint16_t* k_rms_weight;
+  uint16_t* k_cache; /* [ring_len, Ns, Ds] */
+  uint16_t* v_cache;
+  const uint16_t* post_attn_rms_weight;
+  const uint8_t* o_weight;
+  const uint16_t* o_weight_scale;
+  const uint16_t* pre_ff_rms_weight;
+  const uint16_t* post_ff_rms_weight;
+  const uint16_t* layer_scalar;
+  /* NVFP4: packed codes, e4m3 block scales, f32 global multipliers (tiled: up_* hold the
+   * interleaved up|gate buffers, gate_* are not read). FP8: e4m3 codes, f32 channel scales (as
+   * const float*), the global scales unused (may be NULL). */
+  const uint8_t* up_weight;
+  const uint8_t* gate_weight;
+  const uint8_t* down_weight;
+  const void* up_scale;
+  const void* gate_scale;
+  const void* down_scale;
+  const float* up_global_scale;
+  const float* gate_global_scale;
+  const float* down_global_scale;
+} g4_layer;
+
+typedef struct g4_model {
+  const g4_layer* layers;
+  int32_t n_layers;
+  /* embed_token's table [vocab_rows, H] bf16, or NULL: the caller writes the hidden state into
+   * the decoder's hidden buffer before each step */
+  const uint16_t* embedding_table;
+  int32_t vocab_rows;
+  /* final_norm_and_logits's weights (lm_head [lm_head_rows, H] bf16: this rank's rows), or NULL:
+   * no logits */
+  const uint16_t* final_norm_weight;
+  const uint16_t* lm_head_weight;
+  int32_t lm_head_rows;
+  /* RoPE tables [rope_rows, Ds] bf16, sin with its low half negated (the ops' operands) */
+  const uint16_t* cos_local;
+  const uint16_t* sin_local;
+  const uint16_t* cos_global; /* may be NULL if no layer uses G4_ROPE_GLOBAL */
+  const uint16_t* sin_global;
+  int32_t rope_rows;
+} g4_model;
+
+typedef struct g4_decoder g4_decoder;
+
+/* Validate the model (every layer's pointers and sizes) and allocate the per-token buffers:
+ * the device-resident input {token, position} (two i32), the hidden state [H], the per-ring
+ * position offsets and mask rows, q / attention outputs and the logits [lm_head_rows]. The layer
+ * table is copied; the tensors it points to must outlive the decoder. */
+g4_status g4_decoder_create(g4_ctx* ctx, const g4_model* model, g4_decoder** out);
+g4_status g4_decoder_destroy(g4_decoder* dec);
+
+/* Device addresses of the decoder's buffers (any may be NULL): `input` = {token, position} i32
+ * (write it before each step, e.g. cudaMemcpyAsync from pinned memory on the step's stream),
+ * `hidden` [H] bf16 (the residual stream: the embedding after the first kernel, the last layer's
+ * output at the end), `logits` [lm_head_rows] bf16. */
+g4_status g4_decoder_buffers(g4_decoder* dec, int32_t** input, uint16_t** hidden, uint16_t** logits);
+
+/* One token: from the device-resident {token, position}, derive every layer's ring slot, RoPE row
+ * and mask row (c <= min(position, ring_len - 1)) as the reference host does once per token, gather
+ * and scale the token's embedding (if the model has a table), run every layer's four ops in order,
+ * then the final norm and logits (if the model has an lm_head). Asynchronous on `stream`. After
+ * g4_decoder_capture, a step replays the captured graph. Device-side errors (an out-of-table
+ * token, a position past the RoPE table) are reported by g4_ctx_check. */
+g4_status g4_decoder_step(g4_decoder* dec, void* stream);
+
+/* Capture one step into a CUDA graph owned by the decoder (stream must not be the legacy default
+ * stream); later g4_decoder_step calls launch the graph. Every rank of a tensor-parallel group
+ * must capture too (their kernels wait on each other). */
+g4_status g4_decoder_capture(g4_decoder* dec, void* stream);
 
 /* ---- Tensor parallelism over the GPUs of one node (no reference counterpart: the reference
  * runs a layer on one chip). A Megatron split over `world` ranks (1, 2, 4 or 8), one process
@@ -192,6 +335,10 @@ g4_status g4_sliding_attention_output_noalloc(const uint16_t* x, const uint16_t*
  *                         [3840][D/2] packed matrix and [3840][D/16] scales, where D is 15360/w
  *                         rounded up to a multiple of 256 (2048 at w = 8: columns past 1920 are
  *                         zero codes with zero scales); global scales and norm weights whole.
+ *   decoder_feedforward_fp8  up / gate rows [15360 r/w, 15360 (r+1)/w) and their channel
+ *                         scales; down columns of the same range as a row-major [3840][D] matrix
+ *                         (D as above, zero codes past 15360/w); down_weight_scale and norm
+ *                         weights whole.
  * The O and down projections add the ranks' partial sums inside the kernel (a one-shot
  * all-reduce over NVLink peer memory, in rank order: every rank's residual_hbm gets the same
  * bits), then apply the same epilogue on every rank. Every rank must issue the same sequence of
@@ -202,7 +349,13 @@ g4_status g4_sliding_attention_output_noalloc(const uint16_t* x, const uint16_t*
  * them in rank order. The ranks must be on distinct GPUs of one node (checked: the in-kernel
  * exchange waits on the peers' kernels, which two ranks sharing a GPU cannot guarantee). A
  * peer that does not arrive within 2 s sets G4_DEVERR_PEER_TIMEOUT; the ranks' exchange
- * counters are then out of step: call g4_tp_init and g4_tp_connect again on every rank. */
+ * counters are then out of step: call g4_tp_init and g4_tp_connect again on every rank.
+ * g4_tp_init frees the rank's previous exchange buffer, which the peers of the previous setup
+ * store into: before any rank calls it again, every rank must have synchronised the streams of
+ * its ops (a host-side barrier over the ranks; g4b200.tp.connect does this). Each setup carries
+ * a generation that every rank agrees on at g4_tp_connect (the largest of the ranks' setup
+ * counts), and every exchanged word is tagged with it, so a word stored under an earlier setup
+ * never counts as one of the new setup's (the tag keeps 8 bits of it: 255 setups in a row). */
 #define G4_TP_BLOB_BYTES 128
 g4_status g4_tp_init(g4_ctx* ctx, int32_t rank, int32_t world, void* blob_out);
 g4_status g4_tp_connect(g4_ctx* ctx, const void* blobs);

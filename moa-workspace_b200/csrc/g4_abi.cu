@@ -1,92 +1,14 @@
 // C ABI of libg4b200.so (declared in include/g4b200.h): contexts, argument validation and
 // the op entry points. No computation happens here; every op launches the sm_100a kernels
 // of g4_proj.cu / g4_attention.cu and there is no host or CPU fallback.
-#include <atomic>
-#include <cstdio>
 #include <cstring>
-#include <utility>
+#include <mutex>
 
-#include "../../include/g4b200.h"
-#include "g4_ops.cuh"
+#include "g4_ctx.cuh"
 
-namespace g4 {
-int attention_slot_multiple();
-int attention_max_ring();
-}  // namespace g4
-
-struct g4_ctx {
-  int device = 0;
-  int sm_count = 0;
-  bool overlap = false;
-  void* scratch = nullptr;
-  size_t scratch_bytes = 0;
-  g4::Scratch sc{};
-  size_t act_bytes = 0;
-  g4::TmapCache maps;
-  // tensor parallelism (g4_tp_init / g4_tp_connect); world 1 until then
-  int tp_rank = 0, tp_world = 1;
-  bool tp_ready = true;                    // connected (a world of 1 needs no peers)
-  void* tp_buf = nullptr;                  // this rank's exchange buffer, then its epoch counters
-  void* tp_peer[g4::kMaxTp] = {};          // the peers' buffers, opened in this process
-  unsigned char tp_blob[G4_TP_BLOB_BYTES] = {0};
-  g4::TpLink tp{0, 1, {}, nullptr};
-  char last_error[256] = {0};
-};
+using namespace g4::host;
 
 namespace {
-
-// Restores the caller's current device when the call returns.
-struct DeviceGuard {
-  int prev = -1;
-  explicit DeviceGuard(int dev) {
-    if (cudaGetDevice(&prev) != cudaSuccess) prev = -1;
-    if (prev != dev) cudaSetDevice(dev);
-  }
-  ~DeviceGuard() {
-    int cur = -1;
-    if (prev >= 0 && cudaGetDevice(&cur) == cudaSuccess && cur != prev) cudaSetDevice(prev);
-  }
-};
-
-g4_status fail(g4_ctx* ctx, g4_status st, const char* fmt, const char* what) {
-  if (ctx) snprintf(ctx->last_error, sizeof ctx->last_error, fmt, what);
-  return st;
-}
-
-g4_status cuda_status(g4_ctx* ctx, cudaError_t e, const char* where) {
-  if (e == cudaSuccess) return G4_OK;
-  if (ctx) snprintf(ctx->last_error, sizeof ctx->last_error, "%s: %s", where, cudaGetErrorString(e));
-  return G4_ERR_CUDA;
-}
-
-bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
-
-// Every pointer non-null and 16-byte aligned.
-g4_status check_ptrs(g4_ctx* ctx, std::initializer_list<std::pair<const void*, const char*>> ptrs) {
-  for (const auto& p : ptrs) {
-    if (!p.first) return fail(ctx, G4_ERR_INVALID_ARGUMENT, "null pointer: %s", p.second);
-    if (!aligned16(p.first)) return fail(ctx, G4_ERR_MISALIGNED, "pointer not 16-byte aligned: %s", p.second);
-  }
-  return G4_OK;
-}
-
-g4::LaunchEnv env_of(g4_ctx* ctx, void* stream) {
-  g4::LaunchEnv env;
-  env.device = ctx->device;
-  env.sm_count = ctx->sm_count;
-  env.stream = static_cast<cudaStream_t>(stream);
-  env.pdl = ctx->overlap;
-  env.sc = ctx->sc;
-  env.maps = &ctx->maps;
-  env.tp = ctx->tp;
-  return env;
-}
-
-// Ops of a tensor-parallel context run only once it is connected to its peers.
-g4_status check_tp(g4_ctx* ctx) {
-  if (ctx->tp_ready) return G4_OK;
-  return fail(ctx, G4_ERR_INVALID_ARGUMENT, "%s", "tensor-parallel context is not connected (g4_tp_connect)");
-}
 
 // Close the peers' mappings and free this rank's exchange buffer; back to a world of 1.
 cudaError_t tp_release(g4_ctx* ctx) {
@@ -106,7 +28,7 @@ cudaError_t tp_release(g4_ctx* ctx) {
   ctx->tp_rank = 0;
   ctx->tp_world = 1;
   ctx->tp_ready = true;
-  ctx->tp = g4::TpLink{0, 1, {}, nullptr};
+  ctx->tp = g4::TpLink{0, 1, {}, nullptr, 0};
   return first;
 }
 
@@ -117,9 +39,11 @@ struct TpBlob {
   unsigned char uuid[16];      // the rank's GPU
   cudaIpcMemHandle_t handle;   // its exchange buffer
   uint64_t bytes;              // the buffer's size
+  uint32_t generation;         // the rank's count of setups (the group takes the largest)
 };
 static_assert(sizeof(TpBlob) <= G4_TP_BLOB_BYTES, "blob size");
 constexpr uint32_t kTpMagic = 0x50543447u;  // "G4TP"
+constexpr uint32_t kTpVersion = 2;
 constexpr size_t kTpBufferBytes = g4::kTpExchangeWords * sizeof(unsigned long long) + 256;  // + epochs
 
 }  // namespace
@@ -156,7 +80,8 @@ g4_status g4_ctx_create(int device, g4_ctx** out) {
     delete ctx;
     return G4_ERR_CUDA;
   }
-  if (major != 10 || minor != 0) {  // the kernels are built for sm_100a only
+  if (major != 10 || minor != 0 || !g4::proj_geometry_fits(ctx->sm_count)) {
+    // the kernels are built for sm_100a only, and their launch geometry for its SM count
     delete ctx;
     return G4_ERR_UNSUPPORTED;
   }
@@ -406,6 +331,78 @@ g4_status g4_decoder_feedforward_tiled(g4_ctx* ctx, uint16_t* residual_hbm, cons
                              stream);
 }
 
+g4_status g4_embed_token(g4_ctx* ctx, const uint16_t* embedding_table, const int32_t* offset, uint16_t* out,
+                         int32_t vocab_rows, void* stream) {
+  if (!ctx) return G4_ERR_INVALID_ARGUMENT;
+  g4_status st = check_ptrs(ctx, {{embedding_table, "embedding_table"}, {offset, "offset"}, {out, "out"}});
+  if (st != G4_OK) return st;
+  if (vocab_rows <= 0 || vocab_rows > g4::kVocab)
+    return fail(ctx, G4_ERR_INVALID_ARGUMENT, "%s must be in [1, 262144]", "vocab_rows");
+  DeviceGuard guard(ctx->device);
+  return cuda_status(ctx, g4::launch_embed(embedding_table, offset, out, vocab_rows, env_of(ctx, stream)),
+                     "embed_token launch");
+}
+
+g4_status g4_final_norm_and_logits(g4_ctx* ctx, const uint16_t* input, const uint16_t* rms_weight,
+                                   const uint16_t* lm_head_weight, uint16_t* out, int32_t vocab_rows, void* stream) {
+  if (!ctx) return G4_ERR_INVALID_ARGUMENT;
+  g4_status st = check_ptrs(ctx, {{input, "input"}, {rms_weight, "rms_weight"}, {lm_head_weight, "lm_head_weight"},
+                                  {out, "out"}});
+  if (st != G4_OK) return st;
+  if (vocab_rows <= 0 || vocab_rows > g4::kVocab)
+    return fail(ctx, G4_ERR_INVALID_ARGUMENT, "%s must be in [1, 262144]", "vocab_rows");
+  DeviceGuard guard(ctx->device);
+  return cuda_status(ctx, g4::launch_logits(input, rms_weight, lm_head_weight, out, vocab_rows, env_of(ctx, stream)),
+                     "final_norm_and_logits launch");
+}
+
+static g4_status decoder_feedforward_fp8(bool tiled, g4_ctx* ctx, uint16_t* residual_hbm,
+                                         const uint16_t* pre_ff_rms_weight, const uint8_t* up_weight,
+                                         const uint8_t* gate_weight, const uint8_t* down_weight,
+                                         const float* up_weight_scale, const float* gate_weight_scale,
+                                         const float* down_weight_scale, const uint16_t* post_ff_rms_weight,
+                                         const uint16_t* layer_scalar, void* stream) {
+  if (!ctx) return G4_ERR_INVALID_ARGUMENT;
+  g4_status st = check_ptrs(ctx, {{residual_hbm, "residual_hbm"},
+                                  {pre_ff_rms_weight, "pre_ff_rms_weight"},
+                                  {up_weight, "up_weight"},
+                                  {gate_weight, "gate_weight"},
+                                  {down_weight, "down_weight"},
+                                  {up_weight_scale, "up_weight_scale"},
+                                  {gate_weight_scale, "gate_weight_scale"},
+                                  {down_weight_scale, "down_weight_scale"},
+                                  {post_ff_rms_weight, "post_ff_rms_weight"},
+                                  {layer_scalar, "layer_scalar"}});
+  if (st != G4_OK) return st;
+  if ((st = check_tp(ctx)) != G4_OK) return st;
+  DeviceGuard guard(ctx->device);
+  g4::Ffn8Args a{residual_hbm,      pre_ff_rms_weight, up_weight,          gate_weight,  down_weight, up_weight_scale,
+                 gate_weight_scale, down_weight_scale, post_ff_rms_weight, layer_scalar, tiled};
+  return cuda_status(ctx, g4::launch_ffn_fp8(a, env_of(ctx, stream)), "decoder_feedforward_fp8 launch");
+}
+
+g4_status g4_decoder_feedforward_fp8(g4_ctx* ctx, uint16_t* residual_hbm, const uint16_t* pre_ff_rms_weight,
+                                     const uint8_t* up_weight, const uint8_t* gate_weight, const uint8_t* down_weight,
+                                     const float* up_weight_scale, const float* gate_weight_scale,
+                                     const float* down_weight_scale, const uint16_t* post_ff_rms_weight,
+                                     const uint16_t* layer_scalar, void* stream) {
+  return decoder_feedforward_fp8(false, ctx, residual_hbm, pre_ff_rms_weight, up_weight, gate_weight, down_weight,
+                                 up_weight_scale, gate_weight_scale, down_weight_scale, post_ff_rms_weight,
+                                 layer_scalar, stream);
+}
+
+g4_status g4_decoder_feedforward_fp8_tiled(g4_ctx* ctx, uint16_t* residual_hbm, const uint16_t* pre_ff_rms_weight,
+                                           const uint8_t* up_gate_weight_tiled, const uint8_t* down_weight_tiled,
+                                           const float* up_weight_scale, const float* gate_weight_scale,
+                                           const float* down_weight_scale, const uint16_t* post_ff_rms_weight,
+                                           const uint16_t* layer_scalar, void* stream) {
+  // the gate rows are interleaved into the up buffer: it is passed again for the gate pointer
+  // (validated, not read)
+  return decoder_feedforward_fp8(true, ctx, residual_hbm, pre_ff_rms_weight, up_gate_weight_tiled,
+                                 up_gate_weight_tiled, down_weight_tiled, up_weight_scale, gate_weight_scale,
+                                 down_weight_scale, post_ff_rms_weight, layer_scalar, stream);
+}
+
 g4_status g4_tp_init(g4_ctx* ctx, int32_t rank, int32_t world, void* blob_out) {
   if (!ctx) return G4_ERR_INVALID_ARGUMENT;
   if (!blob_out) return fail(ctx, G4_ERR_INVALID_ARGUMENT, "null pointer: %s", "blob_out");
@@ -428,17 +425,18 @@ g4_status g4_tp_init(g4_ctx* ctx, int32_t rank, int32_t world, void* blob_out) {
     return cuda_status(ctx, e, "g4_tp_init");
   }
   b.magic = kTpMagic;
-  b.version = 1;
+  b.version = kTpVersion;
   b.rank = rank;
   b.world = world;
   std::memcpy(b.uuid, prop.uuid.bytes, sizeof b.uuid);
   b.bytes = kTpBufferBytes;
+  b.generation = ++ctx->tp_generation;
   std::memset(ctx->tp_blob, 0, sizeof ctx->tp_blob);
   std::memcpy(ctx->tp_blob, &b, sizeof b);
   std::memcpy(blob_out, ctx->tp_blob, G4_TP_BLOB_BYTES);
   ctx->tp_rank = rank;
   ctx->tp_world = world;
-  ctx->tp = g4::TpLink{0, 1, {}, nullptr};
+  ctx->tp = g4::TpLink{0, 1, {}, nullptr, 0};
   ctx->tp_ready = world == 1;
   return G4_OK;
 }
@@ -452,7 +450,7 @@ g4_status g4_tp_connect(g4_ctx* ctx, const void* blobs) {
   TpBlob b[g4::kMaxTp];
   for (int s = 0; s < world; ++s) {
     std::memcpy(&b[s], raw + size_t(s) * G4_TP_BLOB_BYTES, sizeof(TpBlob));
-    if (b[s].magic != kTpMagic || b[s].version != 1 || b[s].rank != s || b[s].world != world ||
+    if (b[s].magic != kTpMagic || b[s].version != kTpVersion || b[s].rank != s || b[s].world != world ||
         b[s].bytes != kTpBufferBytes)
       return fail(ctx, G4_ERR_INVALID_ARGUMENT, "%s: blobs are not every rank's g4_tp_init output in rank order",
                   "g4_tp_connect");
@@ -470,7 +468,12 @@ g4_status g4_tp_connect(g4_ctx* ctx, const void* blobs) {
     if (p) cudaIpcCloseMemHandle(p);
     p = nullptr;
   }
-  g4::TpLink link{rank, world, {}, nullptr};
+  // every rank sees the same blobs, so every rank takes the same generation, larger than any
+  // earlier setup of any member: words stored under an earlier setup never match this one's tags
+  uint32_t gen = 0;
+  for (int s = 0; s < world; ++s) gen = b[s].generation > gen ? b[s].generation : gen;
+  ctx->tp_generation = gen;
+  g4::TpLink link{rank, world, {}, nullptr, gen % 255u + 1u};
   for (int s = 0; s < world; ++s) {
     if (s == rank) {
       link.slots[s] = static_cast<unsigned long long*>(ctx->tp_buf);
@@ -531,16 +534,46 @@ constexpr size_t kStaticScratchBytes = size_t(512) << 10;
 constexpr int kStaticMaxDevices = 64;
 static __device__ __align__(256) uint8_t g_static_scratch[kStaticScratchBytes];
 
-// Per device: the block's address (cudaGetSymbolAddress) and the SM count, filled by the first
-// call on that device. Concurrent first calls store identical values.
-std::atomic<uint8_t*> g_static_base[kStaticMaxDevices];
-std::atomic<int> g_static_sms[kStaticMaxDevices];
+// Per device: the block's address (cudaGetSymbolAddress) and the SM count, looked up by the first
+// call on that device. A __device__ symbol's address belongs to a CUDA context, so the entry
+// also records the context it was looked up in and is redone when the calling thread's current
+// context on that device is another one (a cudaDeviceReset, or a driver-API context).
+struct StaticEntry {
+  void* cu_ctx = nullptr;
+  uint8_t* base = nullptr;
+  int sms = 0;
+};
+StaticEntry g_static[kStaticMaxDevices];
+std::mutex g_static_mutex;
+
+typedef int (*CtxGetCurrentFn)(void**);  // cuCtxGetCurrent: CUresult (CUcontext*)
+CtxGetCurrentFn ctx_get_current() {
+  static CtxGetCurrentFn fn = [] {
+    void* p = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPoint("cuCtxGetCurrent", &p, cudaEnableDefault, &q) != cudaSuccess ||
+        q != cudaDriverEntryPointSuccess)
+      p = nullptr;
+    return reinterpret_cast<CtxGetCurrentFn>(p);
+  }();
+  return fn;
+}
 
 g4_status static_setup(int dev, uint8_t** base, int* sms) {
-  uint8_t* b = g_static_base[dev].load(std::memory_order_acquire);
-  if (b) {
-    *base = b;
-    *sms = g_static_sms[dev].load(std::memory_order_relaxed);
+  // the calling thread's current context; with none yet, the runtime's first call on the
+  // device (the symbol lookup) creates and binds the device's primary context
+  void* cur = nullptr;
+  CtxGetCurrentFn get = ctx_get_current();
+  if (!get || get(&cur) != 0) return G4_ERR_CUDA;
+  if (!cur) {
+    void* p = nullptr;
+    if (cudaGetSymbolAddress(&p, g_static_scratch) != cudaSuccess || get(&cur) != 0 || !cur) return G4_ERR_CUDA;
+  }
+  std::lock_guard<std::mutex> lock(g_static_mutex);
+  StaticEntry& e = g_static[dev];
+  if (e.base && e.cu_ctx == cur) {
+    *base = e.base;
+    *sms = e.sms;
     return G4_OK;
   }
   int major = 0, minor = 0, count = 0;
@@ -548,13 +581,14 @@ g4_status static_setup(int dev, uint8_t** base, int* sms) {
       cudaDeviceGetAttribute(&minor, cudaDevAttrComputeCapabilityMinor, dev) != cudaSuccess ||
       cudaDeviceGetAttribute(&count, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess)
     return G4_ERR_CUDA;
-  if (major != 10 || minor != 0) return G4_ERR_UNSUPPORTED;  // built for sm_100a only
+  if (major != 10 || minor != 0 || !g4::proj_geometry_fits(count)) return G4_ERR_UNSUPPORTED;  // built for sm_100a only
   if (g4::prepare_proj_kernels() != cudaSuccess) return G4_ERR_CUDA;
   void* p = nullptr;
   if (cudaGetSymbolAddress(&p, g_static_scratch) != cudaSuccess || !p) return G4_ERR_CUDA;
-  g_static_sms[dev].store(count, std::memory_order_relaxed);
-  g_static_base[dev].store(static_cast<uint8_t*>(p), std::memory_order_release);
-  *base = static_cast<uint8_t*>(p);
+  e.cu_ctx = cur;
+  e.base = static_cast<uint8_t*>(p);
+  e.sms = count;
+  *base = e.base;
   *sms = count;
   return G4_OK;
 }

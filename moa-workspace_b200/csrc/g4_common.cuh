@@ -21,6 +21,7 @@ constexpr int kQs = kNs * kGs * kDs;  // 4096
 constexpr int kPs = kNs * kDs;        // 2048
 constexpr int kTs = 1024;
 constexpr int kE = 32768;
+constexpr int kVocab = 262144;  // W: embedding / lm_head rows
 constexpr float kEps = 1e-6f;
 
 // Tensor-parallel geometry (Megatron split over NTP ranks of one node): rank r owns KV heads
@@ -50,6 +51,7 @@ enum : uint32_t {
   kErrInternal = 1u << 3,  // a launch-geometry invariant did not hold (work was skipped)
   kErrNegativeScale = 1u << 4,  // an nvfp4 block scale has its sign bit set
   kErrPeerTimeout = 1u << 5,    // a tensor-parallel peer's partial did not arrive in time
+  kErrTokenOffset = 1u << 6,    // an embedding-row offset outside the table or not row-aligned
 };
 
 // Global scratch owned by a context. The counters hold each op's call counts (per tile or
@@ -72,12 +74,14 @@ constexpr size_t kTileSsBytes = 2 * size_t(kTileSsCount) * 2 * sizeof(unsigned l
 
 // Tensor-parallel exchange (one-shot all-reduce of the O / down partials over NVLink peer
 // memory). Every rank owns one exchange buffer, mapped into every peer's address space:
-//   words [op][parity][tile][source rank][row], 8 bytes = (epoch << 32) | f32 bits,
-// written by the source with one 64-bit store, so a reader that sees the call's epoch sees the
-// value too. Each rank counts its calls per (op, tile) in `epoch` (local, never shared): the
-// n-th call writes epoch n into parity n & 1. A source can be at most one call ahead of a
-// reader per (op, tile): its next call's exchange needs the reader's contribution of this
-// call, which the reader posts only after its previous kernels completed.
+//   words [op][parity][tile][source rank][row], 8 bytes = (tag << 32) | f32 bits,
+// written by the source with one 64-bit store, so a reader that sees the call's tag sees the
+// value too. The tag is (generation << 24) | (epoch & 0xFFFFFF). Each rank counts its calls per
+// (op, tile) in `epoch` (local, never shared): the n-th call writes epoch n into parity n & 1. A
+// source can be at most one call ahead of a reader per (op, tile): its next call's exchange needs
+// the reader's contribution of this call, which the reader posts only after its previous kernels
+// completed. The generation changes with every setup of the group (all ranks agree on it), so a
+// word that a peer of an earlier setup stored late never matches a call of the new one.
 constexpr int kTpOps = 2;      // 0: O projection, 1: FFN down
 constexpr int kTpTiles = 30;   // H / 128 output tiles
 constexpr size_t kTpExchangeWords = size_t(kTpOps) * 2 * kTpTiles * kMaxTp * 128;
@@ -85,7 +89,11 @@ struct TpLink {
   int rank, world;                                 // world 1: no exchange
   unsigned long long* slots[kMaxTp];               // rank s's exchange buffer (this process's mapping)
   uint32_t* epoch;                                 // [op][tile] calls so far (this rank's memory)
+  uint32_t generation;                             // 1..255: this setup of the group
 };
+__host__ __device__ constexpr uint32_t tp_tag(uint32_t generation, uint32_t epoch) {
+  return (generation << 24) | (epoch & 0xFFFFFFu);
+}
 constexpr size_t kScratchHeadBytes = 256;  // the error word, padded to the scratch alignment
 constexpr int kCounterCount = 4096;
 constexpr int kSplitEpochUpGate = 0;     // calls so far, per tile: up/gate (240 tiles), ...
@@ -255,6 +263,26 @@ __device__ __forceinline__ void cp_async_wait_all() {
   do {                           \
   } while (0)
 #endif
+
+// ---------------------------------------------------------------------------------------
+// The token embedding: out = bf16(f32(row) * EMBED_SCALE) for one row of the table, the threads
+// of the calling block striding over its 16-byte chunks (the reference op: ops.rs:8-35; the scale
+// is the device op's f32 constant, src/lib.rs:23).
+constexpr float kEmbedScale = 61.967734f;
+__device__ __forceinline__ void embed_row(const uint16_t* __restrict__ row, uint16_t* out) {
+  for (int c = threadIdx.x; c < kH * 2 / 16; c += blockDim.x) {
+    const uint4 raw = __ldg(reinterpret_cast<const uint4*>(row) + c);
+    const uint32_t w[4] = {raw.x, raw.y, raw.z, raw.w};
+    uint32_t o[4];
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+      const float lo = __uint_as_float(w[i] << 16) * kEmbedScale;
+      const float hi = __uint_as_float(w[i] & 0xffff0000u) * kEmbedScale;
+      o[i] = uint32_t(f32_to_bf16(lo)) | (uint32_t(f32_to_bf16(hi)) << 16);
+    }
+    reinterpret_cast<uint4*>(out)[c] = make_uint4(o[0], o[1], o[2], o[3]);
+  }
+}
 
 // ---------------------------------------------------------------------------------------
 // Reductions

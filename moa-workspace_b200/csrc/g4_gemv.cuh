@@ -106,7 +106,7 @@ __device__ __forceinline__ uint8_t* align1024(uint8_t* p) {
 }
 
 // The CTA (of `grid`) whose run contains unit u (runs are [c*total/grid, (c+1)*total/grid)).
-__device__ __forceinline__ int cta_of_unit(int64_t u, int64_t grid, int64_t total) {
+__host__ __device__ __forceinline__ int cta_of_unit(int64_t u, int64_t grid, int64_t total) {
   return int(((u + 1) * grid + total - 1) / total - 1);
 }
 

@@ -5,6 +5,9 @@
 #include <cuda_runtime.h>
 #include <stdint.h>
 
+#include <unordered_map>
+#include <utility>
+
 #include "g4_common.cuh"
 
 namespace g4 {
@@ -69,8 +72,26 @@ struct FfnArgs {
   bool tiled;
 };
 
+// The GeGLU feed-forward on FP8 e4m3 weights with f32 per-output-channel scales (BASELINE
+// configs[0]; the reference's decoder_feedforward epilogue, FOG/src/ops.rs:201-239, around three
+// scaled projections, FOG/scripts/generate_references.py:265-274).
+struct Ffn8Args {
+  uint16_t* residual;
+  const uint16_t* pre_rms;
+  const uint8_t* up_w;      // [L, H] (tiled: up and gate interleaved, g4_pack_tiles (128, 64))
+  const uint8_t* gate_w;    // [L, H] (row-major only)
+  const uint8_t* down_w;    // [H, L]
+  const float* up_s;        // [L]
+  const float* gate_s;      // [L]
+  const float* down_s;      // [H]
+  const uint16_t* post_rms;
+  const uint16_t* layer_scalar;
+  bool tiled;
+};
+
 // TMA tensor maps of the weight matrices, encoded on the host once per (pointer, shape) and
-// kept by the context (encoding costs microseconds; a map is 128 bytes).
+// kept by the context (encoding costs microseconds; a map is 128 bytes). A whole model's maps
+// (ten or so per layer) stay cached: the table grows as needed.
 class TmapCache {
  public:
   // Row-major uint8 matrix [rows, cols] (fp8 codes, e4m3 scales), box {box_cols, box_rows}.
@@ -81,14 +102,12 @@ class TmapCache {
   cudaError_t kv(const void* base, uint64_t ring, uint32_t heads, uint32_t dim, uint32_t box_slots, CUtensorMap* out);
 
  private:
-  struct Entry {
-    const void* base = nullptr;
-    uint64_t key = 0;
-    CUtensorMap map;
+  struct KeyHash {
+    size_t operator()(const std::pair<const void*, uint64_t>& k) const {
+      return std::hash<const void*>()(k.first) ^ (std::hash<uint64_t>()(k.second) * 0x9E3779B97F4A7C15ull);
+    }
   };
-  static constexpr int kEntries = 256;
-  Entry entries_[kEntries];
-  int next_ = 0;
+  std::unordered_map<std::pair<const void*, uint64_t>, CUtensorMap, KeyHash> entries_;
   const CUtensorMap* find(const void* base, uint64_t key) const;
   void put(const void* base, uint64_t key, const CUtensorMap& map);
 };
@@ -100,15 +119,22 @@ struct LaunchEnv {
   bool pdl;  // launch with programmatic stream serialization
   Scratch sc;
   TmapCache* maps;
-  TpLink tp{0, 1, {}, nullptr};  // tensor-parallel rank (world 1: the whole layer on this GPU)
+  TpLink tp{0, 1, {}, nullptr, 0};  // tensor-parallel rank (world 1: the whole layer on this GPU)
 };
 
 cudaError_t prepare_proj_kernels();       // one-time attributes (dynamic shared memory)
+bool proj_geometry_fits(int sm_count);    // the launch geometry on this many SMs meets the kernels' limits
 cudaError_t prepare_attention_kernels();  // one-time attributes (clusters)
 cudaError_t launch_qkv(const QkvArgs& a, const LaunchEnv& env);
 cudaError_t launch_attention(const AttnArgs& a, const LaunchEnv& env);
 cudaError_t launch_o(const OArgs& a, const LaunchEnv& env);
 cudaError_t launch_ffn_nvfp4(const FfnArgs& a, const LaunchEnv& env);
+cudaError_t launch_ffn_fp8(const Ffn8Args& a, const LaunchEnv& env);
+// The vocabulary ends (g4_vocab.cu): the embedding-row gather and the final norm + lm_head.
+cudaError_t launch_embed(const uint16_t* table, const int32_t* offset, uint16_t* out, int vocab_rows,
+                         const LaunchEnv& env);
+cudaError_t launch_logits(const uint16_t* input, const uint16_t* gamma, const uint16_t* weight, uint16_t* out,
+                          int rows, const LaunchEnv& env);
 
 // The O op without a context: scratch laid out as [error word | kScratchHeadBytes][epoch
 // counters][tile sums][split-K words] at env.sc, o_scratch_bytes() in total; the tensor map is encoded on the

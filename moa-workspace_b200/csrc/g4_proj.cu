@@ -31,6 +31,9 @@ struct Shapes {
   using O = GemvShape<false, 6, kOUnits, kH / kTileRows, (kOUnits < 4 ? kOUnits : 4)>;
   using UpGate = GemvShape<true, 10, kH / kUnitK, Geo::kFfnRows / 64, 15>;  // tile = 64 up rows + 64 gate rows
   using Down = GemvShape<true, 10, kDownUnits, kH / kTileRows, (kDownUnits < 13 ? kDownUnits : 13)>;
+  // FP8 feed-forward: up/gate tiles of 64 up + 64 gate rows (K = H), down like O with K = L
+  using UpGate8 = GemvShape<false, 6, kH / kUnitK, Geo::kFfnRows / 64, 15>;
+  using Down8 = GemvShape<false, 5, kDownUnits, kH / kTileRows, (kDownUnits < 13 ? kDownUnits : 13)>;
 };
 
 __device__ __forceinline__ float gelu_tanh(float x) {
@@ -87,7 +90,7 @@ __device__ __forceinline__ void rms_apply16(const uint4 (&raw)[4], float inv, fl
 // ---------------------------------------------------------------------------------------
 // Tensor parallelism: the one-shot all-reduce of a finished tile's partial rows (O and down).
 // Called by the 128 epilogue threads of the CTA that finishes the tile; thread `row` stores its
-// word (epoch, value) into every peer's exchange buffer with one 64-bit system-scope store,
+// word (tag, value) into every peer's exchange buffer with one 64-bit system-scope store,
 // waits (bounded) until every peer's word of this call is in its own buffer and adds the
 // world's partials in rank order: every rank computes the same sum, bit for bit.
 __device__ float tp_allreduce(const TpLink& tp, int op, int tile, int row, float v, uint32_t* err) {
@@ -97,7 +100,8 @@ __device__ float tp_allreduce(const TpLink& tp, int op, int tile, int row, float
   named_bar(kEpiBarrier, kEpiThreads);  // every thread has read the count before it moves on
   if (row == 0) *ep = e;
   const size_t base = ((size_t(op) * 2 + (e & 1u)) * kTpTiles + tile) * kMaxTp;
-  const unsigned long long word = (static_cast<unsigned long long>(e) << 32) | __float_as_uint(v);
+  const uint32_t tag = tp_tag(tp.generation, e);
+  const unsigned long long word = (static_cast<unsigned long long>(tag) << 32) | __float_as_uint(v);
 #pragma unroll
   for (int s = 0; s < kMaxTp; ++s)
     if (s < tp.world && s != tp.rank) st_relaxed_sys_u64(tp.slots[s] + (base + tp.rank) * kTileRows + row, word);
@@ -117,7 +121,7 @@ __device__ float tp_allreduce(const TpLink& tp, int op, int tile, int row, float
       if (pending & (1u << s)) w[s] = ld_relaxed_sys_u64(mine + s * kTileRows);
 #pragma unroll
     for (int s = 0; s < kMaxTp; ++s) {
-      if ((pending & (1u << s)) && uint32_t(w[s] >> 32) == e) {
+      if ((pending & (1u << s)) && uint32_t(w[s] >> 32) == tag) {
         pv[s] = __uint_as_float(uint32_t(w[s]));
         pending &= ~(1u << s);
       }
@@ -153,7 +157,7 @@ __device__ float tp_allreduce(const TpLink& tp, int op, int tile, int row, float
 // run after the dependency wait, before it publishes anything, so that tile cannot have been
 // finished yet in this call and every tile's count is the same.
 
-constexpr int kMaxFinTiles = 4;  // tiles one CTA can finish (it overlaps at most 3 here)
+constexpr int kMaxFinTiles = 4;  // tiles one CTA can finish (checked at set-up: check_geometry)
 
 struct ResidualTail {
   float y[kMaxFinTiles][kTileRows];                     // the finished tiles' outputs (bf16 values)
@@ -652,6 +656,126 @@ __global__ void __launch_bounds__(kGemvThreads, 1) ffn_down_kernel(const __grid_
 }
 
 // ---------------------------------------------------------------------------------------
+// FP8 feed-forward (per-output-channel f32 scales): up/gate + GeGLU, then down + post-RMSNorm +
+// residual + layer scalar. Each projection is the reference's scaled_projection,
+// bf16((x @ codes.T) * scale) (generate_references.py:265-274); the epilogues are those of the
+// NVFP4 op (ops.rs:201-239). The two kernels share the NVFP4 op's scratch regions and epoch
+// counters (same tile counts), so a model may mix both formats on one context.
+
+struct UpGate8Maps {
+  CUtensorMap up, gate;
+};
+
+template <int NTP>
+struct UpGate8Op {
+  using Shape = typename Shapes<NTP>::UpGate8;
+  const UpGate8Maps* maps;
+  Ffn8Args a;
+  Scratch sc;
+  uint32_t tx_bytes = Shape::kABytes;
+  static constexpr bool kOwnPieces = false;
+  static constexpr bool kRms = true;
+  static constexpr int kRmsGroups = kH / 16;
+
+  // stage: [K half 0: 64 up rows | 64 gate rows][K half 1: same] x 128 codes
+  __device__ void load_unit(uint8_t* stage, int tile, int kc, uint64_t* bar, uint64_t policy) const {
+    if (a.tiled) {  // up and gate interleaved per 128-element half: one 256-row box per unit
+      tma_load_2d(stage, &maps->up, 0, (tile * Shape::kUnitsPerTile + kc) * kUnitBox, bar, policy);
+    } else {
+#pragma unroll
+      for (int h = 0; h < 2; ++h) {
+        tma_load_2d(stage + h * 16384, &maps->up, kc * kUnitK + h * 128, tile * 64, bar, policy);
+        tma_load_2d(stage + h * 16384 + 8192, &maps->gate, kc * kUnitK + h * 128, tile * 64, bar, policy);
+      }
+    }
+  }
+  __device__ void prefetch_l2(int u0, int u1) const {
+    if (a.tiled) prefetch_units(a.up_w, u0, u1, Shape::kABytes);
+  }
+  __device__ void prologue(GemvCtl&) { epoch = tail_epoch(split_epochs, first_tile<Shape>()); }
+  uint32_t epoch = 0;
+  unsigned long long* split_words = reinterpret_cast<unsigned long long*>(sc.partials) + kSplitWordsUpGate;
+  uint32_t* split_epochs = sc.counters + kSplitEpochUpGate;
+  __device__ void load_static(int g, uint4 (&raw)[4]) const { load_group_gamma(a.pre_rms, g, raw); }
+  __device__ void load_group(int g, uint4 (&raw)[4]) const { load_group_cg(a.residual, g, raw); }
+  __device__ void finish_group(const uint4 (&raw)[4], float inv, float (&v)[16]) const { rms_apply16(raw, inv, v); }
+  __device__ void finalize_tile(int tile, int row, float v, GemvCtl& ctl) const {
+    const float s = row < 64 ? __ldg(a.up_s + tile * 64 + row) : __ldg(a.gate_s + tile * 64 + row - 64);
+    const float val = bf16_round(v * s);
+    if (row >= 64) ctl.xchg[row - 64] = val;
+    named_bar(kEpiBarrier, kEpiThreads);
+    // down_proj input: bf16(bf16(gelu_tanh(gate)) * up)  (gemma4.py:197)
+    if (row < 64) ctl.out16[row] = f32_to_bf16(bf16_round(gelu_tanh(ctl.xchg[row])) * val);
+    named_bar(kEpiBarrier, kEpiThreads);
+    if (row < 8) reinterpret_cast<uint4*>(sc.act + tile * 64)[row] = reinterpret_cast<const uint4*>(ctl.out16)[row];
+  }
+};
+
+template <int NTP>
+__global__ void __launch_bounds__(kGemvThreads, 1) ffn8_upgate_kernel(const __grid_constant__ UpGate8Maps maps,
+                                                                      Ffn8Args a, Scratch sc) {
+  extern __shared__ __align__(1024) uint8_t smem[];
+  UpGate8Op<NTP> op{&maps, a, sc};
+  gemv_run<typename Shapes<NTP>::UpGate8>(op, smem, sc);
+}
+
+template <int NTP>
+struct Down8Op {
+  using Shape = typename Shapes<NTP>::Down8;
+  const CUtensorMap* map;
+  Ffn8Args a;
+  Scratch sc;
+  uint32_t tx_bytes = Shape::kABytes;
+  static constexpr bool kOwnPieces = false;
+  static constexpr bool kRms = false;
+  static constexpr int kRmsGroups = 0;
+
+  __device__ void load_unit(uint8_t* stage, int tile, int kc, uint64_t* bar, uint64_t policy) const {
+    if (a.tiled) {
+      tma_load_2d(stage, map, 0, (tile * Shape::kUnitsPerTile + kc) * kUnitBox, bar, policy);
+    } else {
+      tma_load_2d(stage, map, kc * kUnitK, tile * kTileRows, bar, policy);
+      tma_load_2d(stage + 16384, map, kc * kUnitK + 128, tile * kTileRows, bar, policy);
+    }
+  }
+  __device__ void prefetch_l2(int u0, int u1) const {
+    if (a.tiled) prefetch_units(a.down_w, u0, u1, Shape::kABytes);
+  }
+  __device__ void prologue(GemvCtl&) { epoch = tail_epoch(sc.counters + kTailEpochDown, first_tile<Shape>()); }
+  __device__ void load_static(int, uint4 (&)[4]) const {}
+  __device__ void load_group(int g, uint4 (&raw)[4]) const { load_group_cg(sc.act, g, raw); }
+  __device__ void finish_group(const uint4 (&raw)[4], float, float (&v)[16]) const {
+    bf16x16_to_f32(raw[0], raw[1], v);
+  }
+  __device__ void finalize_tile(int tile, int row, float v, GemvCtl&) const {
+    const int r = tile * kTileRows + row;
+    const float s = __ldg(a.down_s + r);
+    const float sum = tp_allreduce(*tp, 1, tile, row, v, sc.err);  // the K slices of every rank
+    tail_record(*tail, a.post_rms, a.residual, sc.tile_ss + kTileSsDown, sc.counters + kTailEpochDown, epoch, tile,
+                row, bf16_round(sum * s));
+  }
+  ResidualTail* tail;
+  const TpLink* tp;
+  uint32_t epoch = 0;
+  unsigned long long* split_words = reinterpret_cast<unsigned long long*>(sc.partials) + kSplitWordsDown;
+  uint32_t* split_epochs = sc.counters + kTailEpochDown;
+};
+
+template <int NTP>
+__global__ void __launch_bounds__(kGemvThreads, 1) ffn8_down_kernel(const __grid_constant__ CUtensorMap map,
+                                                                    Ffn8Args a, Scratch sc,
+                                                                    const __grid_constant__ TpLink tp) {
+  extern __shared__ __align__(1024) uint8_t smem[];
+  __shared__ ResidualTail tail;
+  if (threadIdx.x == 0) tail.n = 0;  // ordered by the engine's first barrier
+  Down8Op<NTP> op{&map, a, sc};
+  op.tail = &tail;
+  op.tp = &tp;
+  gemv_run<typename Shapes<NTP>::Down8>(op, smem, sc);
+  tail_update(tail, a.residual, sc, sc.tile_ss + kTileSsDown, op.epoch, kH / kTileRows, a.layer_scalar);
+}
+
+// ---------------------------------------------------------------------------------------
 // launch helpers
 
 template <class... KArgs, class... Args>
@@ -693,6 +817,32 @@ cudaError_t by_degree(int world, F&& f) {
   }
 }
 
+// The most tiles one CTA of a `grid`-CTA launch finishes: a tile is finished by the CTA holding
+// its first unit (whole or split), so this counts the tiles whose first unit lies in one run.
+template <class Shape>
+int max_tiles_finished(int grid) {
+  int best = 0, run = 0, prev = -1;
+  for (int t = 0; t < Shape::kTiles; ++t) {
+    const int c = cta_of_unit(int64_t(t) * Shape::kUnitsPerTile, grid, Shape::kTotalUnits);
+    run = c == prev ? run + 1 : 1;
+    prev = c;
+    best = run > best ? run : best;
+  }
+  return best;
+}
+
+template <int NTP>
+bool geometry_fits(int sm_count) {
+  using S = Shapes<NTP>;
+  LaunchEnv env{};
+  env.sm_count = sm_count;
+  // the residual tails keep at most kMaxFinTiles finished tiles of a CTA in shared memory, and a
+  // split tile's pieces must fit its kMaxCtasPerGroup slots
+  return max_tiles_finished<typename S::O>(grid_for<typename S::O>(env)) <= kMaxFinTiles &&
+         max_tiles_finished<typename S::Down>(grid_for<typename S::Down>(env)) <= kMaxFinTiles &&
+         max_tiles_finished<typename S::Down8>(grid_for<typename S::Down8>(env)) <= kMaxFinTiles;
+}
+
 template <int NTP>
 cudaError_t prepare_degree() {
   using S = Shapes<NTP>;
@@ -704,8 +854,14 @@ cudaError_t prepare_degree() {
   if ((e = cudaFuncSetAttribute(ffn_upgate_kernel<NTP>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                 int(S::UpGate::kSmemBytes))))
     return e;
-  return cudaFuncSetAttribute(ffn_down_kernel<NTP>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                              int(S::Down::kSmemBytes));
+  if ((e = cudaFuncSetAttribute(ffn_down_kernel<NTP>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                int(S::Down::kSmemBytes))))
+    return e;
+  if ((e = cudaFuncSetAttribute(ffn8_upgate_kernel<NTP>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                int(S::UpGate8::kSmemBytes))))
+    return e;
+  return cudaFuncSetAttribute(ffn8_down_kernel<NTP>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                              int(S::Down8::kSmemBytes));
 }
 
 template <int NTP>
@@ -784,7 +940,38 @@ cudaError_t launch_ffn_t(const FfnArgs& a, const LaunchEnv& env) {
   return launch(ffn_down_kernel<NTP>, grid_for<DN>(env), DN::kSmemBytes, chained, dn, a, chained.sc, env.tp);
 }
 
+template <int NTP>
+cudaError_t launch_ffn8_t(const Ffn8Args& a, const LaunchEnv& env) {
+  constexpr int kRows = TpGeo<NTP>::kFfnRows, kDownK = TpGeo<NTP>::kDownK;
+  using UG = typename Shapes<NTP>::UpGate8;
+  using DN = typename Shapes<NTP>::Down8;
+  UpGate8Maps ug;
+  CUtensorMap dn;
+  cudaError_t e;
+  if (a.tiled) {
+    // up|gate interleaved per 128-element half of each tile's 64 + 64 rows: [2 kRows * H / 128, 128]
+    // bytes, one 256-row box per unit; down unit-tiled like O
+    ug.gate = ug.up;
+    if ((e = env.maps->u8(a.up_w, 128, uint64_t(2 * kRows) * (kH / 128), 128, kUnitBox, true, &ug.up))) return e;
+    if ((e = env.maps->u8(a.down_w, 128, uint64_t(kH) * (kDownK / 128), 128, kUnitBox, true, &dn))) return e;
+  } else {
+    if ((e = env.maps->u8(a.up_w, kH, kRows, 128, 64, true, &ug.up))) return e;
+    if ((e = env.maps->u8(a.gate_w, kH, kRows, 128, 64, true, &ug.gate))) return e;
+    if ((e = env.maps->u8(a.down_w, kDownK, kH, 128, kTileRows, true, &dn))) return e;
+  }
+  e = launch(ffn8_upgate_kernel<NTP>, grid_for<UG>(env), UG::kSmemBytes, env, ug, a, env.sc);
+  if (e != cudaSuccess) return e;
+  LaunchEnv chained = env;
+  chained.pdl = true;  // the down pass prefetches its weights while the up/gate pass drains
+  return launch(ffn8_down_kernel<NTP>, grid_for<DN>(env), DN::kSmemBytes, chained, dn, a, chained.sc, env.tp);
+}
+
 }  // namespace
+
+bool proj_geometry_fits(int sm_count) {
+  return geometry_fits<1>(sm_count) && geometry_fits<2>(sm_count) && geometry_fits<4>(sm_count) &&
+         geometry_fits<8>(sm_count);
+}
 
 cudaError_t prepare_proj_kernels() {
   cudaError_t e;
@@ -804,6 +991,10 @@ cudaError_t launch_o(const OArgs& a, const LaunchEnv& env) {
 
 cudaError_t launch_ffn_nvfp4(const FfnArgs& a, const LaunchEnv& env) {
   return by_degree(env.tp.world, [&](auto d) { return launch_ffn_t<decltype(d)::value>(a, env); });
+}
+
+cudaError_t launch_ffn_fp8(const Ffn8Args& a, const LaunchEnv& env) {
+  return by_degree(env.tp.world, [&](auto d) { return launch_ffn8_t<decltype(d)::value>(a, env); });
 }
 
 // ---------------------------------------------------------------------------------------
@@ -858,17 +1049,11 @@ PFN_cuTensorMapEncodeTiled_v12000 encode_fn() {
 }  // namespace
 
 const CUtensorMap* TmapCache::find(const void* base, uint64_t key) const {
-  for (int i = 0; i < kEntries; ++i)
-    if (entries_[i].base == base && entries_[i].key == key) return &entries_[i].map;
-  return nullptr;
+  const auto it = entries_.find({base, key});
+  return it == entries_.end() ? nullptr : &it->second;
 }
 
-void TmapCache::put(const void* base, uint64_t key, const CUtensorMap& map) {
-  entries_[next_].base = base;
-  entries_[next_].key = key;
-  entries_[next_].map = map;
-  next_ = (next_ + 1) % kEntries;
-}
+void TmapCache::put(const void* base, uint64_t key, const CUtensorMap& map) { entries_[{base, key}] = map; }
 
 cudaError_t TmapCache::kv(const void* base, uint64_t ring, uint32_t heads, uint32_t dim, uint32_t box_slots,
                           CUtensorMap* out) {

@@ -23,6 +23,7 @@ DEVERR_ROPE_OFFSET = 2
 DEVERR_WAIT_TIMEOUT = 4
 DEVERR_NEGATIVE_SCALE = 16
 DEVERR_PEER_TIMEOUT = 32
+DEVERR_TOKEN_OFFSET = 64
 
 TP_BLOB_BYTES = 128
 
@@ -43,8 +44,17 @@ SIGNATURES = {
     "g4_sliding_project_qkv_tiled": [_p] * 18 + [_i32, _i32, _p],
     "g4_sliding_attention_output_tiled": [_p] * 6 + [_p],
     "g4_decoder_feedforward_tiled": [_p] * 12 + [_p],
+    "g4_embed_token": [_p] * 4 + [_i32, _p],
+    "g4_final_norm_and_logits": [_p] * 5 + [_i32, _p],
+    "g4_decoder_feedforward_fp8": [_p] * 11 + [_p],
+    "g4_decoder_feedforward_fp8_tiled": [_p] * 10 + [_p],
     "g4_pack_tiles": [_p, _p, _p, _p, _i32, _i32, _i32, _i32, _p],
     "g4_sliding_attention_output_noalloc": [_p] * 5 + [_p],
+    "g4_decoder_create": [_p, _p, _p],
+    "g4_decoder_destroy": [_p],
+    "g4_decoder_buffers": [_p, _p, _p, _p],
+    "g4_decoder_step": [_p, _p],
+    "g4_decoder_capture": [_p, _p],
     "g4_tp_init": [_p, _i32, _i32, _p],
     "g4_tp_connect": [_p, _p],
 }

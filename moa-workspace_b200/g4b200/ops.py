@@ -116,6 +116,31 @@ def _arg(t: torch.Tensor, name: str, dtypes, shape, device: Device) -> ctypes.c_
     return ctypes.c_void_p(t.data_ptr())
 
 
+W = 262144  # vocabulary rows of the embedding / lm_head table
+
+
+def embed_token(device: Device, embedding_table, offset, out, *, stream=None) -> None:
+    """ops::embed_token (src/ops.rs:8-35): out = bf16(embedding_table[row] * 61.967734), the row at
+    the device-resident BYTE offset `offset` (i32 [1], token * H * 2). embedding_table [rows, H]."""
+    bf = torch.bfloat16
+    rows = embedding_table.shape[0] if embedding_table.dim() == 2 else -1
+    args = [_arg(embedding_table, "embedding_table", bf, (rows, H), device),
+            _arg(offset, "offset", torch.int32, (1,), device), _arg(out, "out", bf, (H,), device)]
+    st = _abi.lib().g4_embed_token(device.handle, *args, rows, _stream_ptr(stream, device.index))
+    _check(device, st, "embed_token")
+
+
+def final_norm_and_logits(device: Device, input, rms_weight, lm_head_weight, out, *, stream=None) -> None:
+    """ops::final_norm_and_logits (src/ops.rs:241-298): out = softcap_30(bf16(RMSNorm(input) @
+    lm_head_weight.T)). lm_head_weight [rows, H] (a tensor-parallel rank's slice of the W rows), out [rows]."""
+    bf = torch.bfloat16
+    rows = lm_head_weight.shape[0] if lm_head_weight.dim() == 2 else -1
+    args = [_arg(input, "input", bf, (H,), device), _arg(rms_weight, "rms_weight", bf, (H,), device),
+            _arg(lm_head_weight, "lm_head_weight", bf, (rows, H), device), _arg(out, "out", bf, (rows,), device)]
+    st = _abi.lib().g4_final_norm_and_logits(device.handle, *args, rows, _stream_ptr(stream, device.index))
+    _check(device, st, "final_norm_and_logits")
+
+
 def sliding_project_qkv(device: Device, x, q_weight, k_weight, v_weight, q_weight_scale, k_weight_scale,
                         v_weight_scale, input_rms_weight, q_rms_weight, k_rms_weight, kv_offset, rope_offset,
                         cos, sin, k_cache, v_cache, q_out, *, tiled=False, stream=None) -> None:
@@ -246,6 +271,58 @@ def decoder_feedforward_tiled(device: Device, residual_hbm, pre_ff_rms_weight, u
     _check(device, st, "decoder_feedforward_tiled")
 
 
+def decoder_feedforward_fp8(device: Device, residual_hbm, pre_ff_rms_weight, up_weight, gate_weight, down_weight,
+                            up_weight_scale, gate_weight_scale, down_weight_scale, post_ff_rms_weight, layer_scalar, *,
+                            stream=None) -> None:
+    """The GeGLU feed-forward on FP8 weights with f32 per-output-channel scales (BASELINE
+    configs[0]): decoder_feedforward's epilogue (src/ops.rs:201-239) around three scaled
+    projections (scripts/generate_references.py:265-274). residual_hbm is updated in place.
+
+    up/gate_weight [L, H] and down_weight [H, L] e4m3; up/gate_weight_scale [L] and
+    down_weight_scale [H] f32. On a tensor-parallel device the up/gate rows (and their scales)
+    and the down columns are this rank's slices (g4b200.tp names: up_weight, gate_weight,
+    down_weight, up_channel_scale, gate_channel_scale, down_channel_scale)."""
+    bf = torch.bfloat16
+    g = geometry(device.world)
+    fr, dk = g["ffn_rows"], g["down_k"]
+    args = [
+        _arg(residual_hbm, "residual_hbm", bf, (H,), device),
+        _arg(pre_ff_rms_weight, "pre_ff_rms_weight", bf, (H,), device),
+        _arg(up_weight, "up_weight", _BYTE_DTYPES, (fr, H), device),
+        _arg(gate_weight, "gate_weight", _BYTE_DTYPES, (fr, H), device),
+        _arg(down_weight, "down_weight", _BYTE_DTYPES, (H, dk), device),
+        _arg(up_weight_scale, "up_weight_scale", torch.float32, (fr,), device),
+        _arg(gate_weight_scale, "gate_weight_scale", torch.float32, (fr,), device),
+        _arg(down_weight_scale, "down_weight_scale", torch.float32, (H,), device),
+        _arg(post_ff_rms_weight, "post_ff_rms_weight", bf, (H,), device),
+        _arg(layer_scalar, "layer_scalar", bf, (8,), device),
+    ]
+    st = _abi.lib().g4_decoder_feedforward_fp8(device.handle, *args, _stream_ptr(stream, device.index))
+    _check(device, st, "decoder_feedforward_fp8")
+
+
+def decoder_feedforward_fp8_tiled(device: Device, residual_hbm, pre_ff_rms_weight, up_gate_weight_tiled,
+                                  down_weight_tiled, up_weight_scale, gate_weight_scale, down_weight_scale,
+                                  post_ff_rms_weight, layer_scalar, *, stream=None) -> None:
+    """decoder_feedforward_fp8 on weights packed by `pack_upgate_fp8` / `tile_weight(.., "down_weight")`."""
+    bf = torch.bfloat16
+    g = geometry(device.world)
+    fr, dk = g["ffn_rows"], g["down_k"]
+    args = [
+        _arg(residual_hbm, "residual_hbm", bf, (H,), device),
+        _arg(pre_ff_rms_weight, "pre_ff_rms_weight", bf, (H,), device),
+        _arg(up_gate_weight_tiled, "up_gate_weight_tiled", _BYTE_DTYPES, (2 * fr, H), device),
+        _arg(down_weight_tiled, "down_weight_tiled", _BYTE_DTYPES, (H, dk), device),
+        _arg(up_weight_scale, "up_weight_scale", torch.float32, (fr,), device),
+        _arg(gate_weight_scale, "gate_weight_scale", torch.float32, (fr,), device),
+        _arg(down_weight_scale, "down_weight_scale", torch.float32, (H,), device),
+        _arg(post_ff_rms_weight, "post_ff_rms_weight", bf, (H,), device),
+        _arg(layer_scalar, "layer_scalar", bf, (8,), device),
+    ]
+    st = _abi.lib().g4_decoder_feedforward_fp8_tiled(device.handle, *args, _stream_ptr(stream, device.index))
+    _check(device, st, "decoder_feedforward_fp8_tiled")
+
+
 # GPU-native (unit-tiled) layout of each weight matrix: (unit_bytes, tile_rows). A unit is the
 # 256 K elements of a tile of rows (fp8: one tensor-memory-accelerator box of two 128-element
 # halves; nvfp4: 128 bytes of packed codes, or 16 block-scale bytes, per row); the units of a
@@ -255,6 +332,7 @@ TILING = {
     "q_weight": (128, 128), "k_weight": (128, 128), "v_weight": (128, 128), "o_weight": (128, 128),
     "up_gate_weight": (128, 64), "up_gate_scale": (16, 64),
     "down_weight_packed": (128, 128), "down_weight_scale": (16, 128),
+    "up_gate_weight_fp8": (128, 64), "down_weight": (128, 128),
 }
 
 
@@ -287,4 +365,10 @@ def pack_upgate(device: Device, up: torch.Tensor, gate: torch.Tensor, *, scales:
     """The up and gate packed codes (scales=False) or block scales (scales=True), interleaved in
     the GPU-native layout of decoder_feedforward_tiled."""
     unit_bytes, tile_rows = TILING["up_gate_scale" if scales else "up_gate_weight"]
+    return pack_tiles(device, up, gate, unit_bytes=unit_bytes, tile_rows=tile_rows, stream=stream)
+
+
+def pack_upgate_fp8(device: Device, up: torch.Tensor, gate: torch.Tensor, *, stream=None) -> torch.Tensor:
+    """The FP8 up and gate codes interleaved in the GPU-native layout of decoder_feedforward_fp8_tiled."""
+    unit_bytes, tile_rows = TILING["up_gate_weight_fp8"]
     return pack_tiles(device, up, gate, unit_bytes=unit_bytes, tile_rows=tile_rows, stream=stream)

@@ -22,12 +22,16 @@ _ROW_SLICED = {  # leading dimension, by output rows
     "q_weight": QS, "q_weight_scale": QS,
     "k_weight": PS, "k_weight_scale": PS, "v_weight": PS, "v_weight_scale": PS,
     "up_weight_packed": L, "gate_weight_packed": L, "up_weight_scale": L, "gate_weight_scale": L,
+    # FP8 feed-forward (decoder_feedforward_fp8): codes and f32 channel scales of up and gate
+    "up_weight": L, "gate_weight": L, "up_channel_scale": L, "gate_channel_scale": L,
 }
 _HEAD_SLICED = {"k_cache": 1, "v_cache": 1, "q_out": 0, "q": 0, "out_hbm": 0, "attn": 0}  # KV-head axis
-_COL_SLICED = {"o_weight": (QS, 1), "down_weight_packed": (L, 2), "down_weight_scale": (L, 16)}  # (K, elems/byte)
+_COL_SLICED = {"o_weight": (QS, 1), "down_weight_packed": (L, 2), "down_weight_scale": (L, 16),
+               "down_weight": (L, 1)}  # (K, elems/byte)
 REPLICATED = ("x", "input_rms_weight", "q_rms_weight", "k_rms_weight", "kv_offset", "rope_offset", "cos", "sin",
               "mask", "post_attn_rms_weight", "o_weight_scale", "residual_hbm", "pre_ff_rms_weight",
-              "up_global_scale", "gate_global_scale", "down_global_scale", "post_ff_rms_weight", "layer_scalar")
+              "up_global_scale", "gate_global_scale", "down_global_scale", "post_ff_rms_weight", "layer_scalar",
+              "down_channel_scale")
 
 
 def shard(name: str, full: torch.Tensor, rank: int, world: int) -> torch.Tensor:
@@ -89,6 +93,11 @@ def connect(device, group=None) -> None:
     import torch.distributed as dist
 
     rank, world = dist.get_rank(group), dist.get_world_size(group)
+    # g4_tp_init frees this rank's previous exchange buffer: no rank may still be running ops of
+    # a previous setup that store into it
+    if torch.cuda.is_available() and getattr(device, "index", None) is not None:
+        torch.cuda.synchronize(device.index)
+    dist.barrier(group)
     blob = device.tp_init(rank, world)
     device.tp_connect(exchange_blobs(blob, group))
     dist.barrier(group)

@@ -18,7 +18,11 @@ rounding is explicit. Citations use `FOG` = `furiosa-opt-gemma4-12B/` of the ref
 - sliding_attention           FOG/src/device/sliding/attention.rs:7-199 (op: FOG/src/ops.rs:118-128);
                               the reference's tests never pin this op, so its restatement follows
                               the device semantics and is validated against a float64 softmax.
-- *_tp                        tensor-parallel split of O and the FFN (no reference counterpart)
+- embed_token                 FOG/src/ops.rs:8-35 (device semantics: f32 scale, one bf16 cast)
+- final_norm_and_logits       FOG/src/ops.rs:241-298, FOG/src/device/shared/lm_head.rs:13-80
+- feedforward_fp8             FP8-per-channel FFN: scaled_projection
+                              (generate_references.py:265-274) in the decoder_feedforward epilogue
+- *_tp                        tensor-parallel split of O and the FFNs (no reference counterpart)
 
 Dot products accumulate in f32 (numpy sgemv); the reference's torch CPU kernels also
 accumulate in f32 but in their own order, so results agree to within the reference
@@ -286,6 +290,55 @@ def decoder_feedforward_tp(residual, pre_rms_weight, up_parts, gate_parts, down_
     down = f32_to_bf16(bf16_to_f32(f32_to_bf16(acc)) * np.float32(down_global))
     summed = add_bf16(residual, rms_norm(down, post_rms_weight))
     return mul_bf16(summed, np.full(summed.shape, np.asarray(layer_scalar).reshape(-1)[0], dtype=np.uint16))
+
+
+def feedforward_fp8_tp(residual, pre_rms_weight, up_parts, gate_parts, down_parts, down_s, post_rms_weight,
+                       layer_scalar, hidden=3840):
+    """feedforward_fp8 with the FFN rows split over ranks. up_parts[r] / gate_parts[r] are
+    (e4m3 codes [rows_r, H], f32 channel scales [rows_r]) and down_parts[r] the e4m3 codes
+    [H, k_r], k_r >= rows_r (columns past rows_r are zero padding); down_s is the whole [H]
+    channel scale. The ranks' f32 partial sums of the down contraction are added in rank order
+    before the channel scale."""
+    h = rms_norm(residual, pre_rms_weight)
+    acc = None
+    for (up_w, up_s), (gate_w, gate_s), down_w in zip(up_parts, gate_parts, down_parts):
+        rows = up_w.shape[0]
+        up = scaled_projection(h, e4m3_to_f32(up_w).reshape(rows, hidden), up_s)
+        gate = scaled_projection(h, e4m3_to_f32(gate_w).reshape(rows, hidden), gate_s)
+        act = bf16_to_f32(mul_bf16(gelu_tanh(gate), up))
+        k = down_w.shape[1]
+        act_pad = np.zeros(k, np.float32)
+        act_pad[:rows] = act
+        part = (e4m3_to_f32(down_w).reshape(hidden, k) @ act_pad).astype(np.float32)
+        acc = part if acc is None else (acc + part).astype(np.float32)
+    down = f32_to_bf16(acc * np.asarray(down_s, dtype=np.float32))
+    summed = add_bf16(residual, rms_norm(down, post_rms_weight))
+    return mul_bf16(summed, np.full(summed.shape, np.asarray(layer_scalar).reshape(-1)[0], dtype=np.uint16))
+
+
+EMBED_SCALE = np.float32(61.967734)   # FOG/src/lib.rs:23 (sqrt(3840) as the device op's f32 constant)
+LOGIT_SOFTCAP = np.float32(30.0)      # FOG/src/lib.rs:24
+
+
+def embed_token(table_bits, token):
+    """ops::embed_token (FOG/src/ops.rs:8-35): the row times EMBED_SCALE in f32, one bf16 cast.
+
+    (The model oracle, gemma4.py:92-100, multiplies by the scale cast to bf16 (62.0) instead; the
+    device op, which this library replaces, keeps the f32 constant.)"""
+    row = bf16_to_f32(np.asarray(table_bits)[token])
+    return f32_to_bf16((row * EMBED_SCALE).astype(np.float32))
+
+
+def final_norm_and_logits(x_bits, rms_weight_bits, lm_head_bits):
+    """ops::final_norm_and_logits (FOG/src/ops.rs:241-298): h = RMSNorm(x) in bf16, logits =
+    bf16(h @ W.T) with an f32 contraction (shared/lm_head.rs:13-80), then the device op's f32
+    softcap: bf16(tanh(logit / 30) * 30) with one rounding (the model oracle, gemma4.py:258-261,
+    rounds to bf16 after each of the three steps instead)."""
+    h = bf16_to_f32(rms_norm(x_bits, rms_weight_bits))
+    w = bf16_to_f32(lm_head_bits)
+    logits = bf16_round((w @ h).astype(np.float32))
+    capped = (np.tanh((logits / LOGIT_SOFTCAP).astype(np.float32)).astype(np.float32) * LOGIT_SOFTCAP)
+    return f32_to_bf16(capped.astype(np.float32))
 
 
 def sliding_attention(q, k_cache, v_cache, mask, scale=1.0):

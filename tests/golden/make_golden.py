@@ -43,7 +43,8 @@ def bits(t) -> np.ndarray:
 
 def main() -> None:
     ap = argparse.ArgumentParser()
-    ap.add_argument("--reference", type=Path, default=Path("/root/reference"))
+    ap.add_argument("--reference", type=Path, required=True,
+                    help="root of the reference workspace (the directory holding furiosa-opt-gemma4-12B/)")
     ap.add_argument("--runs", type=int, default=len(RUNS))
     args = ap.parse_args()
 

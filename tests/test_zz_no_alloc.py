@@ -2,8 +2,11 @@
 
 It must give what g4_sliding_attention_output gives on the same inputs, call after call: two
 calls in a row update the residual in place twice, and each result is compared with the
-context-based entry point's result at the same step (within the O tolerance of the reference
-grader). The file name sorts last so the check also runs after every other GPU test.
+context-based entry point's result at the same step. Both launch the same kernel with the same
+fixed summation order, so the results must be identical bit for bit (a stale word or a missed
+clear of the static block would show up as a difference); the oracle tolerance of the reference
+grader applies only to the comparison with the reference's expected output. The file name sorts
+last so the check also runs after every other GPU test.
 """
 
 import ctypes
@@ -21,7 +24,7 @@ def _ptr(t):
     return ctypes.c_void_p(t.data_ptr())
 
 
-def test_noalloc_matches_context_entry_point_twice(device):
+def test_noalloc_matches_context_entry_point_twice(device, golden_runs):
     import torch
 
     from g4b200 import _abi, ops
@@ -47,9 +50,12 @@ def test_noalloc_matches_context_entry_point_twice(device):
         assert st == _abi.G4_OK, lib.g4_status_string(st).decode()
         torch.cuda.synchronize()
         device.check()
-        ok, maxd, exact = within(bits(res_ctx), bits(res_static), ATOL["sliding_attention_output"])
-        assert ok, (step, maxd)
-        assert exact > 0.99, (step, exact)
+        got, want = bits(res_static), bits(res_ctx)
+        assert np.array_equal(got, want), (step, int(np.sum(got != want)))
+        if step == 0:  # one call on the reference's run-0 inputs: the grader's tolerance holds
+            ok, maxd, _ = within(golden_runs["run0.sliding_attention_output.expected"], got,
+                                 ATOL["sliding_attention_output"])
+            assert ok, maxd
 
 
 def test_noalloc_rejects_bad_pointers(device):
