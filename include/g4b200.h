@@ -360,6 +360,11 @@ g4_status g4_decoder_capture(g4_decoder* dec, void* stream);
 g4_status g4_tp_init(g4_ctx* ctx, int32_t rank, int32_t world, void* blob_out);
 g4_status g4_tp_connect(g4_ctx* ctx, const void* blobs);
 
+/* How long the O and down kernels wait for the peers' partial sums before they give up, poison
+ * the rows with NaN and raise G4_DEVERR_PEER_TIMEOUT (default 2 s; 1 ms to 60 s). Applies to the
+ * current setup and to later ones. No reference counterpart (the reference runs on one chip). */
+g4_status g4_tp_set_wait_limit(g4_ctx* ctx, uint64_t limit_ns);
+
 #ifdef __cplusplus
 }
 #endif

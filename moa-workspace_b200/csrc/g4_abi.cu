@@ -28,7 +28,7 @@ cudaError_t tp_release(g4_ctx* ctx) {
   ctx->tp_rank = 0;
   ctx->tp_world = 1;
   ctx->tp_ready = true;
-  ctx->tp = g4::TpLink{0, 1, {}, nullptr, 0};
+  ctx->tp = g4::TpLink{0, 1, {}, nullptr, 0, ctx->tp_wait_ns};
   return first;
 }
 
@@ -436,7 +436,7 @@ g4_status g4_tp_init(g4_ctx* ctx, int32_t rank, int32_t world, void* blob_out) {
   std::memcpy(blob_out, ctx->tp_blob, G4_TP_BLOB_BYTES);
   ctx->tp_rank = rank;
   ctx->tp_world = world;
-  ctx->tp = g4::TpLink{0, 1, {}, nullptr, 0};
+  ctx->tp = g4::TpLink{0, 1, {}, nullptr, 0, ctx->tp_wait_ns};
   ctx->tp_ready = world == 1;
   return G4_OK;
 }
@@ -473,7 +473,7 @@ g4_status g4_tp_connect(g4_ctx* ctx, const void* blobs) {
   uint32_t gen = 0;
   for (int s = 0; s < world; ++s) gen = b[s].generation > gen ? b[s].generation : gen;
   ctx->tp_generation = gen;
-  g4::TpLink link{rank, world, {}, nullptr, gen % 255u + 1u};
+  g4::TpLink link{rank, world, {}, nullptr, gen % 255u + 1u, ctx->tp_wait_ns};
   for (int s = 0; s < world; ++s) {
     if (s == rank) {
       link.slots[s] = static_cast<unsigned long long*>(ctx->tp_buf);
@@ -495,6 +495,15 @@ g4_status g4_tp_connect(g4_ctx* ctx, const void* blobs) {
                                            g4::kTpExchangeWords * sizeof(unsigned long long));
   ctx->tp = link;
   ctx->tp_ready = true;
+  return G4_OK;
+}
+
+g4_status g4_tp_set_wait_limit(g4_ctx* ctx, uint64_t limit_ns) {
+  if (!ctx) return G4_ERR_INVALID_ARGUMENT;
+  if (limit_ns < 1000000ull || limit_ns > 60000000000ull)
+    return fail(ctx, G4_ERR_INVALID_ARGUMENT, "%s must be in [1 ms, 60 s]", "limit_ns");
+  ctx->tp_wait_ns = limit_ns;
+  ctx->tp.wait_ns = limit_ns;
   return G4_OK;
 }
 

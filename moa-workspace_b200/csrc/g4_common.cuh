@@ -90,6 +90,7 @@ struct TpLink {
   unsigned long long* slots[kMaxTp];               // rank s's exchange buffer (this process's mapping)
   uint32_t* epoch;                                 // [op][tile] calls so far (this rank's memory)
   uint32_t generation;                             // 1..255: this setup of the group
+  uint64_t wait_ns;                                // limit of the wait for the peers' words
 };
 __host__ __device__ constexpr uint32_t tp_tag(uint32_t generation, uint32_t epoch) {
   return (generation << 24) | (epoch & 0xFFFFFFu);

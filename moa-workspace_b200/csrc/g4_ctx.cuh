@@ -30,7 +30,8 @@ struct g4_ctx {
   void* tp_peer[g4::kMaxTp] = {};          // the peers' buffers, opened in this process
   unsigned char tp_blob[G4_TP_BLOB_BYTES] = {0};
   uint32_t tp_generation = 0;              // setups of the group so far (agreed at connect)
-  g4::TpLink tp{0, 1, {}, nullptr, 0};
+  uint64_t tp_wait_ns = g4::kWaitLimitNs;  // limit of the exchange's wait for the peers
+  g4::TpLink tp{0, 1, {}, nullptr, 0, g4::kWaitLimitNs};
   char last_error[256] = {0};
 };
 

@@ -119,7 +119,7 @@ struct LaunchEnv {
   bool pdl;  // launch with programmatic stream serialization
   Scratch sc;
   TmapCache* maps;
-  TpLink tp{0, 1, {}, nullptr, 0};  // tensor-parallel rank (world 1: the whole layer on this GPU)
+  TpLink tp{0, 1, {}, nullptr, 0, kWaitLimitNs};  // tensor-parallel rank (world 1: the whole layer on this GPU)
 };
 
 cudaError_t prepare_proj_kernels();       // one-time attributes (dynamic shared memory)

@@ -126,7 +126,7 @@ __device__ float tp_allreduce(const TpLink& tp, int op, int tile, int row, float
         pending &= ~(1u << s);
       }
     }
-    if (pending && globaltimer_ns() - t0 > kWaitLimitNs) {  // a peer never arrived: flag it, poison the row
+    if (pending && globaltimer_ns() - t0 > tp.wait_ns) {  // a peer never arrived: flag it, poison the row
       atomicOr(err, kErrPeerTimeout);
 #pragma unroll
       for (int s = 0; s < kMaxTp; ++s)

@@ -57,6 +57,7 @@ SIGNATURES = {
     "g4_decoder_capture": [_p, _p],
     "g4_tp_init": [_p, _i32, _i32, _p],
     "g4_tp_connect": [_p, _p],
+    "g4_tp_set_wait_limit": [_p, ctypes.c_uint64],
 }
 STRING_FUNCS = {"g4_status_string": [ctypes.c_int32], "g4_last_error": [_p]}
 

@@ -81,6 +81,10 @@ class Device:
         self.rank, self.world = rank, world
         return blob.raw
 
+    def tp_set_wait_limit(self, seconds: float) -> None:
+        """g4_tp_set_wait_limit: how long O / down wait for the peers before raising a peer timeout."""
+        _check(self, _abi.lib().g4_tp_set_wait_limit(self.handle, int(seconds * 1e9)), "g4_tp_set_wait_limit")
+
     def tp_connect(self, blobs: bytes) -> None:
         """g4_tp_connect with every rank's blob, concatenated in rank order."""
         if len(blobs) != _abi.TP_BLOB_BYTES * self.world:

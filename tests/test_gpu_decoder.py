@@ -169,7 +169,7 @@ def equal(a, b):
 def test_decoder_step_equals_ops_one_by_one(device, model, pos):
     import torch
 
-    token = 1234 + pos
+    token = (1234 + pos) % VOCAB
     start = caches(model["layers"])
     want_x, want_logits = one_by_one(device, model, token, pos)
     want_caches = caches(model["layers"])
