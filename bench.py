@@ -952,13 +952,31 @@ def run_ours(args):
 def run_only(args):
     """Eager calls of one op (no graph, no CPU leg, no parity): the small case the ncu captures
     use. Builds the first `--layers` layers only, runs --warmup + --steps calls of the op
-    rotating over them, and prints the mean device time per call."""
+    rotating over them, and prints the mean device time per call. `--only decode` instead runs
+    --warmup + --steps whole decode steps from the decoder's graph (the launch-list capture)."""
     import torch
 
     from g4b200 import ops
 
     device = ops.Device(0)
     dev = torch.device("cuda", 0)
+    if args.only == "decode":  # the whole decode step, replayed from the decoder's graph
+        m = Model(ops, device, dev, 0, 1)
+        dec = m.decoder(device)
+        stream = torch.cuda.Stream(dev)
+        dec.set_input(1234, POSITION, stream=stream)
+        dec.capture(stream=stream)
+        with torch.cuda.stream(stream):
+            for _ in range(args.warmup):
+                dec.step(stream=stream)
+            device.check(stream)
+            secs = timed(torch, lambda: [dec.step(stream=stream) for _ in range(args.steps)])
+        device.check(stream)
+        print(json.dumps({"only": "decode", "steps": args.steps, "ms_per_step": round(secs / args.steps * 1e3, 4),
+                          "launches_per_step": 2 + KERNELS_PER_LAYER * N_MODEL}), flush=True)
+        dec.close()
+        device.close()
+        return 0
     gen = torch.Generator(device=dev)
     gen.manual_seed(1000)
     ffn = "nvfp4" if args.only == "ffn4" else "fp8"
@@ -990,7 +1008,7 @@ def run_only(args):
 
 def main():
     ap = argparse.ArgumentParser()
-    ap.add_argument("--only", choices=["qkv", "attn", "o", "ffn8", "ffn4"], default=None,
+    ap.add_argument("--only", choices=["qkv", "attn", "o", "ffn8", "ffn4", "decode"], default=None,
                     help="profiling aid: eager calls of one op only (prints us/call, not the bench line)")
     ap.add_argument("--layers", type=int, default=4, help="--only: layer copies to rotate over")
     ap.add_argument("--gpus", type=int, default=1)

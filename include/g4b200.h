@@ -101,6 +101,39 @@ g4_status g4_sliding_project_qkv(g4_ctx* ctx, const uint16_t* x, const uint8_t* 
                                  const uint16_t* cos, const uint16_t* sin, uint16_t* k_cache, uint16_t* v_cache,
                                  uint16_t* q_out, int32_t ring_len, int32_t rope_rows, void* stream);
 
+/* Replaces ops::full_project_qkv (src/ops.rs:78-116), the global (full-attention) layers' fused
+ * QKV: x[H], q_weight[Qf = 8192, H] and k_weight[Pf = 512, H] f8e4m3 with bf16 row scales,
+ * input_rms_weight[H], q_rms_weight / k_rms_weight[Df = 512]; kv_offset / rope_offset device i32
+ * BYTE offsets ((pos % Tf) * Df * 2 into this page, pos * Df * 2 into the tables); cos / sin
+ * [rope_rows, Df] bf16 (the global table: theta 1e6, partial rotation, sin's low half negated);
+ * k_cache / v_cache: the current page [Tf = 512, Df] (only the addressed slot is written; v is the
+ * raw k projection normalised without a gamma: K = V); q_out [Gf = 16, Df]. One GPU only. */
+g4_status g4_full_project_qkv(g4_ctx* ctx, const uint16_t* x, const uint8_t* q_weight, const uint8_t* k_weight,
+                              const uint16_t* q_weight_scale, const uint16_t* k_weight_scale,
+                              const uint16_t* input_rms_weight, const uint16_t* q_rms_weight,
+                              const uint16_t* k_rms_weight, const int32_t* kv_offset, const int32_t* rope_offset,
+                              const uint16_t* cos, const uint16_t* sin, uint16_t* k_cache, uint16_t* v_cache,
+                              uint16_t* q_out, int32_t rope_rows, void* stream);
+
+/* Replace ops::full_attention_first_page / ops::full_attention_page (src/ops.rs:148-182): one page
+ * of the global attention with online-softmax state. q [Gf, Df], k / v one page [Tf, Df] bf16,
+ * mask [Tf] f32 (0/1), running_max / running_sum [Gf] f32 (written; read too by _page), out_hbm
+ * [Gf, Df] bf16 (written; read too by _page). The result is divided by running_sum in
+ * g4_full_attention_output. One GPU only. */
+g4_status g4_full_attention_first_page(g4_ctx* ctx, const uint16_t* q, const uint16_t* k, const uint16_t* v,
+                                       const float* mask, float* running_max, float* running_sum, uint16_t* out_hbm,
+                                       void* stream);
+g4_status g4_full_attention_page(g4_ctx* ctx, const uint16_t* q, const uint16_t* k, const uint16_t* v,
+                                 const float* mask, float* running_max, float* running_sum, uint16_t* out_hbm,
+                                 void* stream);
+
+/* Replaces ops::full_attention_output (src/ops.rs:184-199): bf16(x / running_sum) per head, the O
+ * projection o_weight [H, Qf] f8e4m3 with bf16 row scales, the post-attention RMSNorm and the
+ * residual add; residual_hbm [H] in place. One GPU only. */
+g4_status g4_full_attention_output(g4_ctx* ctx, const uint16_t* x, const float* running_sum,
+                                   const uint16_t* post_attn_rms_weight, const uint8_t* o_weight,
+                                   const uint16_t* o_weight_scale, uint16_t* residual_hbm, void* stream);
+
 /* Replaces ops::sliding_attention (src/ops.rs:118-128).
  * q [Ns, Gs, Ds], k/v [ring_len, Ns, Ds] bf16, mask [ring_len] f32 (the reference passes a
  * 0/1 row), out_hbm [Ns, Gs, Ds]. `scale` multiplies q.k before the bf16 score rounding; the
@@ -220,20 +253,28 @@ g4_status g4_sliding_attention_output_noalloc(const uint16_t* x, const uint16_t*
  * the ops one by one; here the ops of every layer are issued on one stream with programmatic
  * dependent launch and can be captured into one CUDA graph.
  *
- * A model is a table of layers. Each layer is the reference's sliding layer
+ * A model is a table of layers. A G4_LAYER_SLIDING layer is the reference's sliding layer
  * (sliding_project_qkv -> sliding_attention -> sliding_attention_output -> decoder_feedforward)
  * with its own KV ring of ring_len slots and one of two RoPE tables: G4_ROPE_LOCAL (theta 1e4,
- * the sliding layers) or G4_ROPE_GLOBAL (theta 1e6: the BASELINE-shaped global layers, which keep
- * the sliding geometry with a longer ring). The feed-forward is NVFP4 (decoder_feedforward) or
- * FP8 (decoder_feedforward_fp8). Pointers are those of the op entry points (device memory of the
- * context's device, 16-byte aligned; on a tensor-parallel context, this rank's slices). */
+ * the sliding layers) or G4_ROPE_GLOBAL (theta 1e6: BASELINE-shaped global layers, which keep the
+ * sliding geometry with a longer ring). A G4_LAYER_FULL layer is the reference's global layer
+ * (full_project_qkv -> full_attention_first_page / full_attention_page over every page up to the
+ * position -> full_attention_output -> the feed-forward; src/host/runtime.rs:462-541): q_weight
+ * [Qf, H], k_weight [Df, H] (K = V, v_* unused), o_weight [H, Qf], q/k_rms_weight [Df], the K and V
+ * pages [ring_len / 512][512][Df] back to back, the global RoPE table; one GPU only. The
+ * feed-forward is NVFP4 (decoder_feedforward) or FP8 (decoder_feedforward_fp8). Pointers are those
+ * of the op entry points (device memory of the context's device, 16-byte aligned; on a
+ * tensor-parallel context, this rank's slices). */
+#define G4_LAYER_SLIDING 0
+#define G4_LAYER_FULL 1
 #define G4_ROPE_LOCAL 0
 #define G4_ROPE_GLOBAL 1
 #define G4_FFN_NVFP4 0
 #define G4_FFN_FP8 1
 typedef struct g4_layer {
-  int32_t rope;       /* G4_ROPE_LOCAL or G4_ROPE_GLOBAL */
-  int32_t ring_len;   /* KV ring slots: a positive multiple of 256, at most 8192 */
+  int32_t kind;       /* G4_LAYER_SLIDING or G4_LAYER_FULL */
+  int32_t rope;       /* G4_ROPE_LOCAL or G4_ROPE_GLOBAL (a full layer: G4_ROPE_GLOBAL) */
+  int32_t ring_len;   /* KV slots: sliding, a positive multiple of 256 up to 8192; full, of 512 up to 32768 */
   int32_t ffn;        /* G4_FFN_NVFP4 or G4_FFN_FP8 */
   int32_t tiled;      /* weights in the g4_pack_tiles layout (the *_tiled entry points) */
   float attn_scale;   /* sliding_attention's scale (the reference model: 1.0) */
@@ -283,9 +324,13 @@ typedef struct g4_model {
   /* RoPE tables [rope_rows, Ds] bf16, sin with its low half negated (the ops' operands) */
   const uint16_t* cos_local;
   const uint16_t* sin_local;
-  const uint16_t* cos_global; /* may be NULL if no layer uses G4_ROPE_GLOBAL */
+  const uint16_t* cos_global; /* may be NULL if no sliding layer uses G4_ROPE_GLOBAL */
   const uint16_t* sin_global;
   int32_t rope_rows;
+  /* the full layers' table [rope_rows, Df] bf16 (theta 1e6, a quarter of the dims rotating; sin's
+   * low half negated), or NULL if the model has no G4_LAYER_FULL layer */
+  const uint16_t* cos_full;
+  const uint16_t* sin_full;
 } g4_model;
 
 typedef struct g4_decoder g4_decoder;

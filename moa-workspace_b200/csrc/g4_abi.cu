@@ -356,6 +356,86 @@ g4_status g4_final_norm_and_logits(g4_ctx* ctx, const uint16_t* input, const uin
                      "final_norm_and_logits launch");
 }
 
+g4_status g4_full_project_qkv(g4_ctx* ctx, const uint16_t* x, const uint8_t* q_weight, const uint8_t* k_weight,
+                              const uint16_t* q_weight_scale, const uint16_t* k_weight_scale,
+                              const uint16_t* input_rms_weight, const uint16_t* q_rms_weight,
+                              const uint16_t* k_rms_weight, const int32_t* kv_offset, const int32_t* rope_offset,
+                              const uint16_t* cos, const uint16_t* sin, uint16_t* k_cache, uint16_t* v_cache,
+                              uint16_t* q_out, int32_t rope_rows, void* stream) {
+  if (!ctx) return G4_ERR_INVALID_ARGUMENT;
+  g4_status st = check_ptrs(ctx, {{x, "x"},
+                                  {q_weight, "q_weight"},
+                                  {k_weight, "k_weight"},
+                                  {q_weight_scale, "q_weight_scale"},
+                                  {k_weight_scale, "k_weight_scale"},
+                                  {input_rms_weight, "input_rms_weight"},
+                                  {q_rms_weight, "q_rms_weight"},
+                                  {k_rms_weight, "k_rms_weight"},
+                                  {kv_offset, "kv_offset"},
+                                  {rope_offset, "rope_offset"},
+                                  {cos, "cos"},
+                                  {sin, "sin"},
+                                  {k_cache, "k_cache"},
+                                  {v_cache, "v_cache"},
+                                  {q_out, "q_out"}});
+  if (st != G4_OK) return st;
+  if (rope_rows <= 0 || int64_t(rope_rows) * g4::kDf * 2 > INT32_MAX)
+    return fail(ctx, G4_ERR_INVALID_ARGUMENT, "%s must be positive (byte offsets within i32)", "rope_rows");
+  if (ctx->tp_world != 1) return fail(ctx, G4_ERR_UNSUPPORTED, "%s", "full_project_qkv runs on one GPU");
+  DeviceGuard guard(ctx->device);
+  const g4::FullQkvArgs a{x,           q_weight, k_weight, q_weight_scale, k_weight_scale, input_rms_weight,
+                          q_rms_weight, k_rms_weight, kv_offset, rope_offset, cos, sin, k_cache, v_cache, q_out,
+                          rope_rows,   false};
+  return cuda_status(ctx, g4::launch_full_qkv(a, env_of(ctx, stream)), "full_project_qkv launch");
+}
+
+static g4_status full_attention(bool first, g4_ctx* ctx, const uint16_t* q, const uint16_t* k, const uint16_t* v,
+                                const float* mask, float* running_max, float* running_sum, uint16_t* out_hbm,
+                                void* stream) {
+  if (!ctx) return G4_ERR_INVALID_ARGUMENT;
+  g4_status st = check_ptrs(ctx, {{q, "q"},
+                                  {k, "k"},
+                                  {v, "v"},
+                                  {mask, "mask"},
+                                  {running_max, "running_max"},
+                                  {running_sum, "running_sum"},
+                                  {out_hbm, "out_hbm"}});
+  if (st != G4_OK) return st;
+  if (ctx->tp_world != 1) return fail(ctx, G4_ERR_UNSUPPORTED, "%s", "full attention runs on one GPU");
+  DeviceGuard guard(ctx->device);
+  const g4::FullAttnArgs a{q, k, v, mask, running_max, running_sum, out_hbm, first};
+  return cuda_status(ctx, g4::launch_full_attention(a, env_of(ctx, stream)), "full attention page launch");
+}
+
+g4_status g4_full_attention_first_page(g4_ctx* ctx, const uint16_t* q, const uint16_t* k, const uint16_t* v,
+                                       const float* mask, float* running_max, float* running_sum, uint16_t* out_hbm,
+                                       void* stream) {
+  return full_attention(true, ctx, q, k, v, mask, running_max, running_sum, out_hbm, stream);
+}
+
+g4_status g4_full_attention_page(g4_ctx* ctx, const uint16_t* q, const uint16_t* k, const uint16_t* v,
+                                 const float* mask, float* running_max, float* running_sum, uint16_t* out_hbm,
+                                 void* stream) {
+  return full_attention(false, ctx, q, k, v, mask, running_max, running_sum, out_hbm, stream);
+}
+
+g4_status g4_full_attention_output(g4_ctx* ctx, const uint16_t* x, const float* running_sum,
+                                   const uint16_t* post_attn_rms_weight, const uint8_t* o_weight,
+                                   const uint16_t* o_weight_scale, uint16_t* residual_hbm, void* stream) {
+  if (!ctx) return G4_ERR_INVALID_ARGUMENT;
+  g4_status st = check_ptrs(ctx, {{x, "x"},
+                                  {running_sum, "running_sum"},
+                                  {post_attn_rms_weight, "post_attn_rms_weight"},
+                                  {o_weight, "o_weight"},
+                                  {o_weight_scale, "o_weight_scale"},
+                                  {residual_hbm, "residual_hbm"}});
+  if (st != G4_OK) return st;
+  if (ctx->tp_world != 1) return fail(ctx, G4_ERR_UNSUPPORTED, "%s", "full_attention_output runs on one GPU");
+  DeviceGuard guard(ctx->device);
+  const g4::FullOArgs a{x, running_sum, post_attn_rms_weight, o_weight, o_weight_scale, residual_hbm, false};
+  return cuda_status(ctx, g4::launch_full_o(a, env_of(ctx, stream)), "full_attention_output launch");
+}
+
 static g4_status decoder_feedforward_fp8(bool tiled, g4_ctx* ctx, uint16_t* residual_hbm,
                                          const uint16_t* pre_ff_rms_weight, const uint8_t* up_weight,
                                          const uint8_t* gate_weight, const uint8_t* down_weight,

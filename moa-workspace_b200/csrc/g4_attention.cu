@@ -7,16 +7,18 @@
 //   sum[g] = sum_t p[g,t] + 1e-6
 //   out    = bf16( bf16(sum_t bf16(p[g,t]) v[t]) / sum[g] )
 //
-// One thread-block cluster of kChunks CTAs per KV head (64 CTAs for the 8 heads; a
-// tensor-parallel rank holds 8 / n of them in its cache slice), each owning a contiguous run of
-// ring slots. A CTA copies its K and V rows into shared memory with TMA boxes of 32 rows, each
-// completing on its own barrier so that scoring starts as the first box lands, scores its slots
-// for the head's two query heads and computes its score maximum. The rounding
+// One thread-block cluster of C CTAs per KV head (C = 16 where the GPU can hold the clusters,
+// else the portable 8: 128 or 64 CTAs for the 8 heads; a tensor-parallel rank holds 8 / n of
+// them in its cache slice), each owning a contiguous run of ring slots. A CTA copies its K and V
+// rows into shared memory with TMA boxes of 32 rows, each completing on its own barrier so that
+// scoring starts as the first box lands (the V rows of the first pass are requested with the K
+// rows: they are not needed until the maximum is known), scores its slots for the head's two
+// query heads and computes its score maximum. The rounding
 // of p to bf16 depends on the maximum over the WHOLE ring, so the cluster exchanges maxima
 // through distributed shared memory (a cluster barrier, then each CTA reads the others') before
 // computing p. Each CTA then leaves its partial sum_t p and sum_t bf16(p) v in its shared memory;
-// after a second cluster barrier CTA c adds the partials of head dimensions [32c, 32c + 32) over
-// the cluster in chunk order, so the result does not depend on timing, and a third barrier keeps
+// after a second cluster barrier CTA c adds the partials of head dimensions [c Ds / C, (c + 1) Ds / C)
+// over the cluster in chunk order, so the result does not depend on timing, and a third barrier keeps
 // every CTA's shared memory alive until the others have read it.
 #include "g4_ops.cuh"
 #include "g4_tc.cuh"
@@ -24,7 +26,6 @@
 namespace g4 {
 namespace {
 
-constexpr int kChunks = 8;                 // CTAs per KV head = the cluster size (portable)
 constexpr int kThreads = 256;
 constexpr int kWarps = kThreads / 32;
 constexpr int kRowBytes = kDs * 2;         // one head's row in one slot
@@ -32,10 +33,12 @@ constexpr int kSub = 128;                  // slots resident in shared memory pe
 constexpr int kBox = 32;                   // slots per TMA box, each with its own barrier
 constexpr int kBoxes = kSub / kBox;
 constexpr int kMaxRing = 8192;
-constexpr int kMaxPer = kMaxRing / kChunks;
-constexpr int kDimsPerCta = kDs / kChunks; // head dimensions each CTA combines
+constexpr int kMinChunks = 8;              // the portable cluster size; 16 where it can be scheduled
 
+template <int C>  // CTAs per KV head = the cluster size
 struct AttnSmem {
+  static constexpr int kMaxPer = kMaxRing / C;
+  static constexpr int kDimsPerCta = kDs / C;  // head dimensions each CTA combines
   uint8_t k[kSub * kRowBytes];
   uint8_t v[kSub * kRowBytes];
   float score[kMaxPer][kGs];  // scores, then bf16-rounded probabilities
@@ -68,10 +71,13 @@ __device__ __forceinline__ float ld_cluster_f32(const void* own, uint32_t rank) 
   return v;
 }
 
+template <int C>
 __global__ void __launch_bounds__(kThreads, 1) attention_kernel(const __grid_constant__ KvMaps maps, AttnArgs a,
                                                                 Scratch sc) {
+  constexpr int kChunks = C;
+  constexpr int kDimsPerCta = AttnSmem<C>::kDimsPerCta;
   extern __shared__ __align__(1024) uint8_t smem_raw[];
-  AttnSmem& sm = *reinterpret_cast<AttnSmem*>(smem_raw);
+  AttnSmem<C>& sm = *reinterpret_cast<AttnSmem<C>*>(smem_raw);
   const int head = blockIdx.x / kChunks;
   const int chunk = int(cluster_ctarank());  // == blockIdx.x % kChunks
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
@@ -108,7 +114,7 @@ __global__ void __launch_bounds__(kThreads, 1) attention_kernel(const __grid_con
     }
   };
   fetch(&maps.k, sm.k, sm.kbar, 0, per < kSub ? per : kSub);
-  if (passes == 1) fetch(&maps.v, sm.v, sm.vbar, 0, per);
+  fetch(&maps.v, sm.v, sm.vbar, 0, per < kSub ? per : kSub);  // (its own buffer: in flight while scoring)
 
   // phase 1: scores, kSub slots at a time. The 8 lanes 8i .. 8i + 7 of a warp score one slot,
   // so a warp scores 4 slots per step (one box of 32 slots per step of the 8 warps). Lane
@@ -221,8 +227,8 @@ __global__ void __launch_bounds__(kThreads, 1) attention_kernel(const __grid_con
   float o0 = 0.f, o1 = 0.f;
   for (int p = 0; p < passes; ++p) {
     const int first = p * kSub, rows = per - first < kSub ? per - first : kSub;
-    if (passes > 1) {
-      __syncthreads();  // the previous pass is done with the V buffer
+    if (p > 0) {
+      __syncthreads();  // the previous pass is done with the V buffer (pass 0 was requested up front)
       fetch(&maps.v, sm.v, sm.vbar, first, rows);
     }
     for (int b = 0; b < rows / kBox; ++b) {
@@ -271,13 +277,317 @@ __global__ void __launch_bounds__(kThreads, 1) attention_kernel(const __grid_con
   G4_STAMP(sc, 6);
 }
 
+// ---------------------------------------------------------------------------------------
+// Global layers: one 512-slot page of the attention of 16 query heads over the single K = V head
+// of 512 dims (FOG/src/ops.rs:148-182; device semantics FOG/src/device/full/attention.rs:205-339):
+//   s = bf16(q . k) (f32 contraction); m = max over the page's slots (masked ones included), on a
+//   later page max(m, running max); e = min(exp(s - m), mask); page sum = sum e + 1e-6; per group
+//   of 32 rows g: P_g = bf16(sum_{t in g} bf16(e_t) v_t); values = bf16(sum_g P_g) (groups in order).
+//   First page: out = values, running max / sum = m / page sum. Later pages, r = exp(old max - m):
+//   running sum = old sum r + page sum, out = bf16(bf16(old out r) + values).
+// One cluster of C CTAs per page, CTA c owning rows [c Tf / C, (c + 1) Tf / C) (whole 32-row
+// groups). Its warps score (warp w: heads 2w, 2w + 1; lane l: dims [16 l, 16 l + 16), the 32
+// slots' partial dots reduced across the lanes by a shuffle reduce-scatter so lane t ends with
+// slot t's sums), the cluster exchanges the heads' maxima and then the group values through
+// distributed shared memory, and CTA c adds dims [c Df / C, (c + 1) Df / C) of every head over
+// the groups in order.
+
+constexpr int kFullThreads = 256;
+constexpr int kGroup = 32;
+
+template <int C>
+struct FullAttnSmem {
+  static constexpr int kRows = kTf / C;
+  static constexpr int kGroups = kRows / kGroup;
+  __align__(16) uint16_t q[kGf][kDf];
+  __align__(16) uint16_t k[kRows][kDf];
+  __align__(16) uint16_t v[kRows][kDf];
+  float s[kGf][kRows];               // scores, then bf16(e)
+  float part[kGroups][kGf][kDf];     // this CTA's group values P_g (read by the cluster)
+  float cmax[kGf], csum[kGf];        // this CTA's maxima and sums of e (read by the cluster)
+  float gmax[kGf], old_max[kGf], old_sum[kGf];
+};
+
+__device__ __forceinline__ void cp_async_commit() { asm volatile("cp.async.commit_group;" ::: "memory"); }
+template <int N>
+__device__ __forceinline__ void cp_async_wait_group() { asm volatile("cp.async.wait_group %0;" ::"n"(N) : "memory"); }
+
+// Lane L holds v[j] = its partial of slot j (j < 32); afterwards v[0] is slot L's sum over the
+// warp's 32 lanes (a fixed butterfly order: the same in every call).
+__device__ __forceinline__ float reduce_scatter32(float (&v)[32]) {
+  const int lane = threadIdx.x & 31;
+#pragma unroll
+  for (int h = 16; h >= 1; h >>= 1) {
+    const bool upper = (lane & h) != 0;
+#pragma unroll
+    for (int j = 0; j < h; ++j) {
+      const float send = upper ? v[j] : v[j + h];
+      const float keep = upper ? v[j + h] : v[j];
+      v[j] = keep + __shfl_xor_sync(0xffffffffu, send, h);
+    }
+  }
+  return v[0];
+}
+
+template <int C>
+__global__ void __launch_bounds__(kFullThreads, 1) full_attention_kernel(FullAttnArgs a, Scratch sc) {
+  using Sm = FullAttnSmem<C>;
+  constexpr int kRows = Sm::kRows, kGroups = Sm::kGroups, kDims = kDf / C;
+  extern __shared__ __align__(1024) uint8_t smem_raw[];
+  Sm& sm = *reinterpret_cast<Sm*>(smem_raw);
+  const int c = int(cluster_ctarank());
+  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+  const int r0 = c * kRows;
+  const uint8_t* krow = reinterpret_cast<const uint8_t*>(a.k + size_t(r0) * kDf);
+  const uint8_t* vrow = reinterpret_cast<const uint8_t*>(a.v + size_t(r0) * kDf);
+  constexpr int kLines = kRows * kDf * 2 / 128;  // 128-byte lines of this CTA's K (and V) rows
+  // while the preceding QKV op finishes: this CTA's rows into L2 (it writes one slot of the page;
+  // L2 is coherent, so the copies after the wait still read it)
+  for (int i = tid; i < 2 * kLines; i += kFullThreads)
+    asm volatile("prefetch.global.L2 [%0];" ::"l"((i < kLines ? krow : vrow) + size_t(i % kLines) * 128) : "memory");
+  pdl_wait_primary();
+  pdl_launch_dependents();
+  int pos = 0;
+  if (a.position) {  // the decode driver: a page past the position does not exist yet
+    pos = __ldcg(a.position);
+    if (a.page * kTf > pos) return;  // (every CTA of the cluster sees the same position)
+  }
+  // q and K rows, then V rows, into shared memory (16-byte copies; V is waited for later)
+  for (int i = tid; i < kGf * kDf / 8; i += kFullThreads) cp_async_16(&sm.q[0][0] + i * 8, a.q + i * 8);
+  for (int i = tid; i < kRows * kDf / 8; i += kFullThreads) cp_async_16(&sm.k[0][0] + i * 8, a.k + size_t(r0) * kDf + i * 8);
+  cp_async_commit();
+  for (int i = tid; i < kRows * kDf / 8; i += kFullThreads) cp_async_16(&sm.v[0][0] + i * 8, a.v + size_t(r0) * kDf + i * 8);
+  cp_async_commit();
+  if (!a.first && tid < kGf) {
+    sm.old_max[tid] = __ldcg(a.running_max + tid);
+    sm.old_sum[tid] = __ldcg(a.running_sum + tid);
+  }
+  cp_async_wait_group<1>();
+  __syncthreads();
+
+  // scores: warp w takes heads 2w and 2w + 1; lane l dims [16 l, 16 l + 16)
+  const int h0 = 2 * warp;
+  float qa[16], qb[16];
+  {
+    const uint4* pa = reinterpret_cast<const uint4*>(&sm.q[h0][16 * lane]);
+    const uint4* pb = reinterpret_cast<const uint4*>(&sm.q[h0 + 1][16 * lane]);
+    const uint4 a0 = pa[0], a1 = pa[1], b0 = pb[0], b1 = pb[1];
+    const uint32_t wa[8] = {a0.x, a0.y, a0.z, a0.w, a1.x, a1.y, a1.z, a1.w};
+    const uint32_t wb[8] = {b0.x, b0.y, b0.z, b0.w, b1.x, b1.y, b1.z, b1.w};
+#pragma unroll
+    for (int i = 0; i < 8; ++i) {
+      qa[2 * i] = __uint_as_float(wa[i] << 16);
+      qa[2 * i + 1] = __uint_as_float(wa[i] & 0xffff0000u);
+      qb[2 * i] = __uint_as_float(wb[i] << 16);
+      qb[2 * i + 1] = __uint_as_float(wb[i] & 0xffff0000u);
+    }
+  }
+  float mya = -INFINITY, myb = -INFINITY;
+#pragma unroll 1
+  for (int blk = 0; blk < kRows / 32; ++blk) {
+    float pa[32], pb[32];
+#pragma unroll
+    for (int t = 0; t < 32; ++t) {
+      const uint4* pk = reinterpret_cast<const uint4*>(&sm.k[blk * 32 + t][16 * lane]);
+      const uint4 k0 = pk[0], k1 = pk[1];
+      const uint32_t wk[8] = {k0.x, k0.y, k0.z, k0.w, k1.x, k1.y, k1.z, k1.w};
+      float sa = 0.f, sb = 0.f;
+#pragma unroll
+      for (int i = 0; i < 8; ++i) {
+        const float lo = __uint_as_float(wk[i] << 16), hi = __uint_as_float(wk[i] & 0xffff0000u);
+        sa = fmaf(qa[2 * i], lo, sa);
+        sa = fmaf(qa[2 * i + 1], hi, sa);
+        sb = fmaf(qb[2 * i], lo, sb);
+        sb = fmaf(qb[2 * i + 1], hi, sb);
+      }
+      pa[t] = sa;
+      pb[t] = sb;
+    }
+    const float sa = bf16_round(reduce_scatter32(pa)), sb = bf16_round(reduce_scatter32(pb));
+    sm.s[h0][blk * 32 + lane] = sa;
+    sm.s[h0 + 1][blk * 32 + lane] = sb;
+    mya = fmaxf(mya, sa);
+    myb = fmaxf(myb, sb);
+  }
+  mya = warp_max(mya);
+  myb = warp_max(myb);
+  if (lane == 0) {
+    sm.cmax[h0] = mya;
+    sm.cmax[h0 + 1] = myb;
+  }
+  cluster_sync();  // every CTA's maxima are in its shared memory
+  if (tid < kGf) {
+    float pm[C];
+#pragma unroll
+    for (int j = 0; j < C; ++j) pm[j] = ld_cluster_f32(&sm.cmax[tid], uint32_t(j));
+    float m = -INFINITY;
+#pragma unroll
+    for (int j = 0; j < C; ++j) m = fmaxf(m, pm[j]);
+    if (!a.first) m = fmaxf(m, sm.old_max[tid]);
+    sm.gmax[tid] = m;
+  }
+  __syncthreads();
+  // e = min(exp(s - m), mask), kept as bf16(e); the CTA's sum of e per head
+  {
+    float za = 0.f, zb = 0.f;
+    for (int t = lane; t < kRows; t += 32) {
+      const float mk = a.mask ? a.mask[r0 + t] : (a.page * kTf + r0 + t <= pos ? 1.0f : 0.0f);
+      const float ea = fminf(expf(sm.s[h0][t] - sm.gmax[h0]), mk);
+      const float eb = fminf(expf(sm.s[h0 + 1][t] - sm.gmax[h0 + 1]), mk);
+      za += ea;
+      zb += eb;
+      sm.s[h0][t] = bf16_round(ea);
+      sm.s[h0 + 1][t] = bf16_round(eb);
+    }
+    za = warp_sum(za);
+    zb = warp_sum(zb);
+    if (lane == 0) {
+      sm.csum[h0] = za;
+      sm.csum[h0 + 1] = zb;
+    }
+  }
+  cp_async_wait_group<0>();
+  __syncthreads();  // bf16(e) of every head and the V rows are in shared memory
+  // group values: thread tid owns dims 2 tid, 2 tid + 1 of every head
+#pragma unroll 1
+  for (int g = 0; g < kGroups; ++g) {
+    float acc[kGf][2];
+#pragma unroll
+    for (int h = 0; h < kGf; ++h) acc[h][0] = acc[h][1] = 0.f;
+#pragma unroll 4
+    for (int t = g * kGroup; t < (g + 1) * kGroup; ++t) {
+      const uint32_t w2 = reinterpret_cast<const uint32_t*>(sm.v[t])[tid];
+      const float v0 = __uint_as_float(w2 << 16), v1 = __uint_as_float(w2 & 0xffff0000u);
+#pragma unroll
+      for (int h = 0; h < kGf; ++h) {
+        acc[h][0] = fmaf(sm.s[h][t], v0, acc[h][0]);
+        acc[h][1] = fmaf(sm.s[h][t], v1, acc[h][1]);
+      }
+    }
+#pragma unroll
+    for (int h = 0; h < kGf; ++h) {
+      sm.part[g][h][2 * tid] = bf16_round(acc[h][0]);
+      sm.part[g][h][2 * tid + 1] = bf16_round(acc[h][1]);
+    }
+  }
+  cluster_sync();  // every CTA's group values and sums are in its shared memory
+  // CTA c combines dims [c kDims, (c + 1) kDims) of every head over the page's groups, in order
+  for (int o = tid; o < kGf * kDims; o += kFullThreads) {
+    const int h = o / kDims, d = c * kDims + o % kDims;
+    float total = 0.f, z = 0.f;
+#pragma unroll 1
+    for (int j = 0; j < C; ++j) {
+#pragma unroll
+      for (int g = 0; g < kGroups; ++g) total += ld_cluster_f32(&sm.part[g][h][d], uint32_t(j));
+      z += ld_cluster_f32(&sm.csum[h], uint32_t(j));
+    }
+    const float values = bf16_round(total), page_sum = z + kEps, m = sm.gmax[h];
+    float outv, sum;
+    if (a.first) {
+      outv = values;
+      sum = page_sum;
+    } else {
+      const float r = expf(sm.old_max[h] - m);
+      outv = bf16_round(bf16_round(bf16_to_f32(__ldcg(a.out + h * kDf + d)) * r) + values);
+      sum = sm.old_sum[h] * r + page_sum;
+    }
+    a.out[h * kDf + d] = f32_to_bf16(outv);
+    if (c == 0 && d == 0) {  // one thread per head: the running statistics
+      a.running_max[h] = m;
+      a.running_sum[h] = sum;
+    }
+  }
+  cluster_sync();  // the others are done reading this CTA's shared memory
+}
+
+template <int C>
+cudaLaunchConfig_t full_attention_config(cudaStream_t stream, bool pdl, cudaLaunchAttribute (&attr)[2]) {
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(C);
+  cfg.blockDim = dim3(kFullThreads);
+  cfg.dynamicSmemBytes = sizeof(FullAttnSmem<C>);
+  cfg.stream = stream;
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = pdl ? 1 : 0;
+  attr[1].id = cudaLaunchAttributeClusterDimension;
+  attr[1].val.clusterDim.x = C;
+  attr[1].val.clusterDim.y = 1;
+  attr[1].val.clusterDim.z = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 2;
+  return cfg;
+}
+
+template <int C>
+cudaLaunchConfig_t attention_config(int heads, cudaStream_t stream, bool pdl, cudaLaunchAttribute (&attr)[2]) {
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(heads * C);
+  cfg.blockDim = dim3(kThreads);
+  cfg.dynamicSmemBytes = sizeof(AttnSmem<C>);
+  cfg.stream = stream;
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = pdl ? 1 : 0;
+  attr[1].id = cudaLaunchAttributeClusterDimension;  // one cluster per KV head
+  attr[1].val.clusterDim.x = C;
+  attr[1].val.clusterDim.y = 1;
+  attr[1].val.clusterDim.z = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 2;
+  return cfg;
+}
+
+// Per device: whether 16-CTA clusters of the kernel fit the GPU a whole layer at a time (all 8
+// heads' clusters resident together); otherwise every call uses the portable 8.
+constexpr int kMaxDevices = 64;
+int g_clusters16[kMaxDevices];  // 0 unknown, 1 yes, -1 no
+
 }  // namespace
 
 cudaError_t prepare_attention_kernels() {
-  return cudaFuncSetAttribute(attention_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, int(sizeof(AttnSmem)));
+  cudaError_t e;
+  if ((e = cudaFuncSetAttribute(attention_kernel<8>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                int(sizeof(AttnSmem<8>)))))
+    return e;
+  if ((e = cudaFuncSetAttribute(attention_kernel<16>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                int(sizeof(AttnSmem<16>)))))
+    return e;
+  int dev = 0;
+  if ((e = cudaGetDevice(&dev))) return e;
+  if (dev < 0 || dev >= kMaxDevices) return cudaSuccess;  // such a device keeps the portable size
+  int fits = 0;
+  if (cudaFuncSetAttribute(attention_kernel<16>, cudaFuncAttributeNonPortableClusterSizeAllowed, 1) == cudaSuccess) {
+    cudaLaunchAttribute attr[2];
+    cudaLaunchConfig_t cfg = attention_config<16>(kNs, nullptr, false, attr);
+    if (cudaOccupancyMaxActiveClusters(&fits, attention_kernel<16>, &cfg) != cudaSuccess) fits = 0;
+  }
+  cudaGetLastError();  // a refused query is not an error of this call
+  g_clusters16[dev] = fits >= kNs ? 1 : -1;
+  if ((e = cudaFuncSetAttribute(full_attention_kernel<8>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                int(sizeof(FullAttnSmem<8>)))))
+    return e;
+  if ((e = cudaFuncSetAttribute(full_attention_kernel<16>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                int(sizeof(FullAttnSmem<16>)))))
+    return e;
+  if (g_clusters16[dev] == 1 &&
+      cudaFuncSetAttribute(full_attention_kernel<16>, cudaFuncAttributeNonPortableClusterSizeAllowed, 1) != cudaSuccess) {
+    cudaGetLastError();
+    g_clusters16[dev] = -1;
+  }
+  return cudaSuccess;
 }
 
-int attention_slot_multiple() { return kChunks * 32; }
+cudaError_t launch_full_attention(const FullAttnArgs& a, const LaunchEnv& env) {
+  if (env.tp.world != 1) return cudaErrorNotSupported;  // the global layers run on one GPU
+  cudaLaunchAttribute attr[2];
+  if (env.device >= 0 && env.device < kMaxDevices && g_clusters16[env.device] == 1) {
+    const cudaLaunchConfig_t cfg = full_attention_config<16>(env.stream, env.pdl, attr);
+    return cudaLaunchKernelEx(&cfg, full_attention_kernel<16>, a, env.sc);
+  }
+  const cudaLaunchConfig_t cfg = full_attention_config<8>(env.stream, env.pdl, attr);
+  return cudaLaunchKernelEx(&cfg, full_attention_kernel<8>, a, env.sc);
+}
+
+int attention_slot_multiple() { return kMinChunks * 32; }
 int attention_max_ring() { return kMaxRing; }
 
 cudaError_t launch_attention(const AttnArgs& a, const LaunchEnv& env) {
@@ -286,25 +596,19 @@ cudaError_t launch_attention(const AttnArgs& a, const LaunchEnv& env) {
   if (a.heads < 1 || a.heads > kNs) return cudaErrorInvalidValue;
   if ((e = env.maps->kv(a.k_cache, uint64_t(a.ring_len), uint32_t(a.heads), kDs, uint32_t(kBox), &maps.k))) return e;
   if ((e = env.maps->kv(a.v_cache, uint64_t(a.ring_len), uint32_t(a.heads), kDs, uint32_t(kBox), &maps.v))) return e;
-  cudaLaunchConfig_t cfg = {};
-  cfg.gridDim = dim3(a.heads * kChunks);
-  cfg.blockDim = dim3(kThreads);
-  cfg.dynamicSmemBytes = sizeof(AttnSmem);
-  cfg.stream = env.stream;
-  cudaLaunchAttribute attr[2];
-  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
-  attr[0].val.programmaticStreamSerializationAllowed = env.pdl ? 1 : 0;
-  attr[1].id = cudaLaunchAttributeClusterDimension;  // one cluster per KV head
-  attr[1].val.clusterDim.x = kChunks;
-  attr[1].val.clusterDim.y = 1;
-  attr[1].val.clusterDim.z = 1;
-  cfg.attrs = attr;
-  cfg.numAttrs = 2;
   Scratch sc = env.sc;
 #ifdef G4_TRACE
   if (sc.trace) sc.trace += 4096;  // profiling builds: separate stamp rows per kernel
 #endif
-  return cudaLaunchKernelEx(&cfg, attention_kernel, maps, a, sc);
+  cudaLaunchAttribute attr[2];
+  const bool c16 = env.device >= 0 && env.device < kMaxDevices && g_clusters16[env.device] == 1 &&
+                   a.ring_len % (16 * kBox) == 0;
+  if (c16) {
+    const cudaLaunchConfig_t cfg = attention_config<16>(a.heads, env.stream, env.pdl, attr);
+    return cudaLaunchKernelEx(&cfg, attention_kernel<16>, maps, a, sc);
+  }
+  const cudaLaunchConfig_t cfg = attention_config<8>(a.heads, env.stream, env.pdl, attr);
+  return cudaLaunchKernelEx(&cfg, attention_kernel<8>, maps, a, sc);
 }
 
 }  // namespace g4

@@ -101,6 +101,7 @@ constexpr int kSplitEpochUpGate = 0;     // calls so far, per tile: up/gate (240
 constexpr int kTailEpochO = 3840;        // ... O and down (30 each; split-K and residual tail)
 constexpr int kTailEpochDown = 3872;
 constexpr int kHeadEpochBase = 3968;    // ... and QKV heads (32)
+constexpr int kFullHeadEpochBase = 4000; // ... and the global layers' QKV heads (17)
 constexpr size_t kPartialFloats = size_t(1) << 21;  // 8 MiB of split-K partials
 // Split-K slots of each op: [tile][CTA of the tile][128 rows] epoch-tagged words (offsets in words
 // from `partials`); one region per op, so a word of one op never reads as another op's.
@@ -108,6 +109,13 @@ constexpr size_t kSplitWordsO = 0;
 constexpr size_t kSplitWordsDown = size_t(1) << 16;
 constexpr size_t kSplitWordsQkv = size_t(1) << 17;
 constexpr size_t kSplitWordsUpGate = size_t(1) << 18;
+constexpr size_t kSplitWordsFullQkv = size_t(3) << 18;  // 68 tiles x 16 x 128 words, below 1 << 20
+// Global (full-attention) layers: 16 query heads and one K = V head of 512 (the reference's Gf,
+// Df, Qf = Gf * Df, Pf = Df) over pages of Tf = 512 slots.
+constexpr int kGf = 16;
+constexpr int kDf = 512;
+constexpr int kQf = kGf * kDf;
+constexpr int kTf = 512;
 
 // ---------------------------------------------------------------------------------------
 // bf16 / f16 / fp8 / fp4 conversions

@@ -76,6 +76,9 @@ struct g4_decoder {
   int32_t* kv_off = nullptr;
   float* mask = nullptr;
   uint16_t *hidden = nullptr, *q = nullptr, *attn = nullptr, *logits = nullptr;
+  // full-attention layers: q [Gf, Df], the attention output [Gf, Df], running max / sum [Gf]
+  uint16_t *q_full = nullptr, *attn_full = nullptr;
+  float *run_max = nullptr, *run_sum = nullptr;
   cudaGraph_t graph = nullptr;
   cudaGraphExec_t exec = nullptr;
 };
@@ -83,13 +86,19 @@ struct g4_decoder {
 namespace {
 
 g4_status check_layer(g4_ctx* ctx, const g4_layer& l) {
+  if (l.kind != G4_LAYER_SLIDING && l.kind != G4_LAYER_FULL)
+    return fail(ctx, G4_ERR_INVALID_ARGUMENT, "%s", "layer.kind must be G4_LAYER_SLIDING or G4_LAYER_FULL");
+  const bool full = l.kind == G4_LAYER_FULL;
+  if (full && ctx->tp_world != 1) return fail(ctx, G4_ERR_UNSUPPORTED, "%s", "full-attention layers run on one GPU");
+  if (!full) {
+    g4_status st = check_ptrs(ctx, {{l.v_weight, "layer.v_weight"}, {l.v_weight_scale, "layer.v_weight_scale"}});
+    if (st != G4_OK) return st;
+  }
   g4_status st = check_ptrs(ctx, {{l.input_rms_weight, "layer.input_rms_weight"},
                                   {l.q_weight, "layer.q_weight"},
                                   {l.k_weight, "layer.k_weight"},
-                                  {l.v_weight, "layer.v_weight"},
                                   {l.q_weight_scale, "layer.q_weight_scale"},
                                   {l.k_weight_scale, "layer.k_weight_scale"},
-                                  {l.v_weight_scale, "layer.v_weight_scale"},
                                   {l.q_rms_weight, "layer.q_rms_weight"},
                                   {l.k_rms_weight, "layer.k_rms_weight"},
                                   {l.k_cache, "layer.k_cache"},
@@ -121,8 +130,14 @@ g4_status check_layer(g4_ctx* ctx, const g4_layer& l) {
   }
   if (l.rope != G4_ROPE_LOCAL && l.rope != G4_ROPE_GLOBAL)
     return fail(ctx, G4_ERR_INVALID_ARGUMENT, "%s", "layer.rope must be G4_ROPE_LOCAL or G4_ROPE_GLOBAL");
-  if (l.ring_len <= 0 || l.ring_len % g4::attention_slot_multiple() != 0 || l.ring_len > g4::attention_max_ring())
+  if (full) {
+    if (l.ring_len <= 0 || l.ring_len % g4::kTf != 0 || l.ring_len > 64 * g4::kTf)
+      return fail(ctx, G4_ERR_UNSUPPORTED, "%s must be a positive multiple of 512, at most 32768", "layer.ring_len");
+    if (l.rope != G4_ROPE_GLOBAL) return fail(ctx, G4_ERR_INVALID_ARGUMENT, "%s", "a full layer uses G4_ROPE_GLOBAL");
+  } else if (l.ring_len <= 0 || l.ring_len % g4::attention_slot_multiple() != 0 ||
+             l.ring_len > g4::attention_max_ring()) {
     return fail(ctx, G4_ERR_UNSUPPORTED, "%s must be a positive multiple of 256, at most 8192", "layer.ring_len");
+  }
   if (!(l.attn_scale == l.attn_scale)) return fail(ctx, G4_ERR_INVALID_ARGUMENT, "%s is NaN", "layer.attn_scale");
   return G4_OK;
 }
@@ -164,19 +179,42 @@ cudaError_t issue_step(g4_decoder* d, cudaStream_t stream) {
     const int r = d->ring_of[i];
     const bool global = l.rope == G4_ROPE_GLOBAL;
     const bool tiled = l.tiled != 0;
+    cudaError_t e;
+    if (l.kind == G4_LAYER_FULL) {
+      // the reference host's full-layer launches (runtime.rs:462-541): QKV into the position's page,
+      // every page up to it (later pages see the position and do nothing), then O
+      const int32_t* pos = d->input + 1;
+      g4::FullQkvArgs fq{d->hidden,        l.q_weight,       l.k_weight,     l.q_weight_scale, l.k_weight_scale,
+                         l.input_rms_weight, l.q_rms_weight, l.k_rms_weight, nullptr,          nullptr,
+                         m.cos_full,       m.sin_full,       l.k_cache,      l.v_cache,        d->q_full,
+                         m.rope_rows,      tiled};
+      fq.slots = l.ring_len;
+      fq.position = pos;
+      if ((e = g4::launch_full_qkv(fq, env)) != cudaSuccess) return e;
+      for (int p = 0; p < l.ring_len / g4::kTf; ++p) {
+        g4::FullAttnArgs fa{d->q_full, l.k_cache + size_t(p) * g4::kTf * g4::kDf, l.v_cache + size_t(p) * g4::kTf * g4::kDf,
+                            nullptr,   d->run_max, d->run_sum, d->attn_full, p == 0};
+        fa.page = p;
+        fa.position = pos;
+        if ((e = g4::launch_full_attention(fa, env)) != cudaSuccess) return e;
+      }
+      const g4::FullOArgs fo{d->attn_full, d->run_sum, l.post_attn_rms_weight, l.o_weight, l.o_weight_scale,
+                             d->hidden,    tiled};
+      if ((e = g4::launch_full_o(fo, env)) != cudaSuccess) return e;
+    } else {
     const g4::QkvArgs qa{d->hidden,        l.q_weight,       l.k_weight,         l.v_weight,
                          l.q_weight_scale, l.k_weight_scale, l.v_weight_scale,   l.input_rms_weight,
                          l.q_rms_weight,   l.k_rms_weight,   d->kv_off + 4 * r,  d->rope_off,
                          global ? m.cos_global : m.cos_local,  global ? m.sin_global : m.sin_local,
                          l.k_cache,        l.v_cache,        d->q,               l.ring_len,
                          m.rope_rows,      tiled};
-    cudaError_t e = g4::launch_qkv(qa, env);
-    if (e != cudaSuccess) return e;
+    if ((e = g4::launch_qkv(qa, env)) != cudaSuccess) return e;
     const g4::AttnArgs aa{d->q, l.k_cache, l.v_cache, d->mask + size_t(r) * d->mask_stride, d->attn, l.ring_len, heads,
                           l.attn_scale};
     if ((e = g4::launch_attention(aa, env)) != cudaSuccess) return e;
     const g4::OArgs oa{d->attn, l.post_attn_rms_weight, l.o_weight, l.o_weight_scale, d->hidden, tiled};
     if ((e = g4::launch_o(oa, env)) != cudaSuccess) return e;
+    }
     if (l.ffn == G4_FFN_FP8) {
       const g4::Ffn8Args fa{d->hidden,
                             l.pre_ff_rms_weight,
@@ -260,9 +298,17 @@ g4_status g4_decoder_create(g4_ctx* ctx, const g4_model* model, g4_decoder** out
       delete d;
       return st;
     }
-    if (l.rope == G4_ROPE_GLOBAL && (!m.cos_global || !m.sin_global)) {
+    if (l.kind == G4_LAYER_FULL && (!m.cos_full || !m.sin_full)) {
+      delete d;
+      return fail(ctx, G4_ERR_INVALID_ARGUMENT, "%s", "a G4_LAYER_FULL layer needs model.cos_full / sin_full");
+    }
+    if (l.kind == G4_LAYER_SLIDING && l.rope == G4_ROPE_GLOBAL && (!m.cos_global || !m.sin_global)) {
       delete d;
       return fail(ctx, G4_ERR_INVALID_ARGUMENT, "%s", "a G4_ROPE_GLOBAL layer needs model.cos_global / sin_global");
+    }
+    if (l.kind == G4_LAYER_FULL) {  // its kernels derive the slot and the mask from the position
+      d->ring_of.push_back(0);
+      continue;
     }
     int r = 0;
     while (r < d->n_rings && d->rings[r] != l.ring_len) ++r;
@@ -280,6 +326,10 @@ g4_status g4_decoder_create(g4_ctx* ctx, const g4_model* model, g4_decoder** out
     delete d;
     return st;
   }
+  if (m.cos_full && (st = check_ptrs(ctx, {{m.cos_full, "model.cos_full"}, {m.sin_full, "model.sin_full"}})) != G4_OK) {
+    delete d;
+    return st;
+  }
   d->model = m;
   d->model.layers = nullptr;  // the decoder's own copy is d->layers
   // device buffers: control words | hidden | q | attention | logits | masks
@@ -288,7 +338,8 @@ g4_status g4_decoder_create(g4_ctx* ctx, const g4_model* model, g4_decoder** out
   const size_t off_attn = off_q + align_up(size_t(g4::kQs) * 2);
   const size_t off_logits = off_attn + align_up(size_t(g4::kQs) * 2);
   const size_t off_mask = off_logits + align_up(size_t(m.lm_head_weight ? m.lm_head_rows : 0) * 2);
-  const size_t total = off_mask + align_up(size_t(d->n_rings) * d->mask_stride * sizeof(float));
+  const size_t off_full = off_mask + align_up(size_t(d->n_rings) * d->mask_stride * sizeof(float));
+  const size_t total = off_full + 2 * align_up(size_t(g4::kQf) * 2) + 2 * align_up(g4::kGf * sizeof(float));
   DeviceGuard guard(ctx->device);
   cudaError_t e = cudaMalloc(&d->buf, total);
   if (e == cudaSuccess) e = cudaMemset(d->buf, 0, total);
@@ -307,6 +358,10 @@ g4_status g4_decoder_create(g4_ctx* ctx, const g4_model* model, g4_decoder** out
   d->attn = reinterpret_cast<uint16_t*>(base + off_attn);
   d->logits = m.lm_head_weight ? reinterpret_cast<uint16_t*>(base + off_logits) : nullptr;
   d->mask = reinterpret_cast<float*>(base + off_mask);
+  d->q_full = reinterpret_cast<uint16_t*>(base + off_full);
+  d->attn_full = reinterpret_cast<uint16_t*>(base + off_full + align_up(size_t(g4::kQf) * 2));
+  d->run_max = reinterpret_cast<float*>(base + off_full + 2 * align_up(size_t(g4::kQf) * 2));
+  d->run_sum = d->run_max + 256 / sizeof(float);
   *out = d;
   return G4_OK;
 }

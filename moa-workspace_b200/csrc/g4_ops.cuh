@@ -72,6 +72,57 @@ struct FfnArgs {
   bool tiled;
 };
 
+// The global layer's fused QKV (FOG/src/ops.rs:78-116): one page [Tf, Df] of the K and V caches.
+struct FullQkvArgs {
+  const uint16_t* x;
+  const uint8_t* q_weight;  // [Qf, H]
+  const uint8_t* k_weight;  // [Df, H]
+  const uint16_t* q_scale;
+  const uint16_t* k_scale;
+  const uint16_t* input_rms;
+  const uint16_t* q_rms;    // [Df]
+  const uint16_t* k_rms;
+  const int32_t* kv_offset;  // byte offset of the slot in the page: (pos % Tf) * Df * 2
+  const int32_t* rope_offset;  // pos * Df * 2
+  const uint16_t* cos;       // [rope_rows, Df]
+  const uint16_t* sin;
+  uint16_t* k_cache;         // [Tf, Df]
+  uint16_t* v_cache;
+  uint16_t* q_out;           // [Gf, Df]
+  int rope_rows;
+  bool tiled;
+  int slots = kTf;           // cache slots behind k_cache / v_cache (the op: one page)
+  // the decode driver: the device-resident position, from which the kernel derives both offsets
+  // ((pos % slots) * Df * 2 and pos * Df * 2) instead of reading kv_offset / rope_offset
+  const int32_t* position = nullptr;
+};
+
+// One page of the global layer's attention (FOG/src/ops.rs:148-182) and its output projection
+// (ops.rs:184-199).
+struct FullAttnArgs {
+  const uint16_t* q;     // [Gf, Df]
+  const uint16_t* k;     // [Tf, Df]
+  const uint16_t* v;
+  const float* mask;     // [Tf]
+  float* running_max;    // [Gf]
+  float* running_sum;
+  uint16_t* out;         // [Gf, Df]
+  bool first;
+  // the decode driver: the page's index and the device-resident position; a page past the
+  // position does nothing, and the mask (null here) is slot <= position
+  int page = 0;
+  const int32_t* position = nullptr;
+};
+struct FullOArgs {
+  const uint16_t* x;            // [Gf, Df]
+  const float* running_sum;     // [Gf]
+  const uint16_t* post_rms;
+  const uint8_t* o_weight;      // [H, Qf]
+  const uint16_t* o_scale;
+  uint16_t* residual;
+  bool tiled;
+};
+
 // The GeGLU feed-forward on FP8 e4m3 weights with f32 per-output-channel scales (BASELINE
 // configs[0]; the reference's decoder_feedforward epilogue, FOG/src/ops.rs:201-239, around three
 // scaled projections, FOG/scripts/generate_references.py:265-274).
@@ -130,6 +181,9 @@ cudaError_t launch_attention(const AttnArgs& a, const LaunchEnv& env);
 cudaError_t launch_o(const OArgs& a, const LaunchEnv& env);
 cudaError_t launch_ffn_nvfp4(const FfnArgs& a, const LaunchEnv& env);
 cudaError_t launch_ffn_fp8(const Ffn8Args& a, const LaunchEnv& env);
+cudaError_t launch_full_qkv(const FullQkvArgs& a, const LaunchEnv& env);
+cudaError_t launch_full_attention(const FullAttnArgs& a, const LaunchEnv& env);
+cudaError_t launch_full_o(const FullOArgs& a, const LaunchEnv& env);
 // The vocabulary ends (g4_vocab.cu): the embedding-row gather and the final norm + lm_head.
 cudaError_t launch_embed(const uint16_t* table, const int32_t* offset, uint16_t* out, int vocab_rows,
                          const LaunchEnv& env);

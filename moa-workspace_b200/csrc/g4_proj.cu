@@ -36,6 +36,11 @@ struct Shapes {
   using Down8 = GemvShape<false, 5, kDownUnits, kH / kTileRows, (kDownUnits < 13 ? kDownUnits : 13)>;
 };
 
+// The global layers' projections (one GPU): q (16 heads x 512) and the single k head, then O with
+// K = Qf = 8192.
+using FullQkvShape = GemvShape<false, 6, kH / kUnitK, (kQf + kDf) / kTileRows, 8>;
+using FullOShape = GemvShape<false, 6, kQf / kUnitK, kH / kTileRows, 8>;
+
 __device__ __forceinline__ float gelu_tanh(float x) {
   // F.gelu(approximate="tanh"): 0.5 * x * (1 + tanh(sqrt(2/pi) * (x + 0.044715 * x^3)))
   const float cube = x * x * x;
@@ -656,6 +661,249 @@ __global__ void __launch_bounds__(kGemvThreads, 1) ffn_down_kernel(const __grid_
 }
 
 // ---------------------------------------------------------------------------------------
+// Global layer QKV (FOG/src/ops.rs:78-116): the q heads and the single K = V head are 512 rows =
+// four tiles each. As in the sliding QKV, the CTA holding a head's first unit finishes the head at
+// its last piece in it, adding the other CTAs' epoch-tagged partial rows in CTA order; thread e of
+// its 128 epilogue threads owns head elements e + 128 t (t < 4), so the RoPE pairs (i, i ^ 256)
+// are both its own (t and t ^ 2). The k head also yields v: the same raw projection normalised
+// without a gamma (K = V, FOG/src/device/full/rmsnorm.rs:182-200).
+
+struct FullQkvStatic {
+  __align__(16) uint16_t cos[kDf];
+  __align__(16) uint16_t sin[kDf];
+  __align__(16) uint16_t qg[kDf];
+  __align__(16) uint16_t kg[kDf];
+  __align__(16) uint16_t out[kDf];
+  __align__(16) uint16_t out_v[kDf];
+  double red[4];
+  int slot, row;
+  bool kv_ok, rope_ok;
+};
+
+struct FullQkvMaps {
+  CUtensorMap q, k;
+};
+
+struct FullQkvOp {
+  using Shape = FullQkvShape;
+  static constexpr int kQTiles = kQf / kTileRows;  // 64; tiles 64..67 are the k head
+  static constexpr int kTilesPerHead = kDf / kTileRows;
+  const FullQkvMaps* maps;
+  FullQkvArgs a;
+  Scratch sc;
+  uint32_t tx_bytes = Shape::kABytes;
+  static constexpr bool kRms = true;
+  static constexpr int kRmsGroups = kH / 16;
+  static constexpr bool kOwnPieces = true;
+  FullQkvStatic* st;
+  uint32_t epoch = 0;
+
+  __device__ void load_unit(uint8_t* stage, int tile, int kc, uint64_t* bar, uint64_t policy) const {
+    const CUtensorMap* m = tile < kQTiles ? &maps->q : &maps->k;
+    const int t = tile < kQTiles ? tile : tile - kQTiles;
+    if (a.tiled) {
+      tma_load_2d(stage, m, 0, (t * Shape::kUnitsPerTile + kc) * kUnitBox, bar, policy);
+    } else {
+      tma_load_2d(stage, m, kc * kUnitK, t * kTileRows, bar, policy);
+      tma_load_2d(stage + 16384, m, kc * kUnitK + 128, t * kTileRows, bar, policy);
+    }
+  }
+  __device__ void prefetch_l2(int u0, int u1) const {
+    if (!a.tiled) return;
+    constexpr int kQU = kQTiles * Shape::kUnitsPerTile;
+    prefetch_units(a.q_weight, u0, u1 < kQU ? u1 : kQU, Shape::kABytes);
+    prefetch_units(a.k_weight, (u0 > kQU ? u0 : kQU) - kQU, u1 - kQU, Shape::kABytes);
+  }
+  __device__ void prologue(GemvCtl&) {
+    epoch = tail_epoch(sc.counters + kFullHeadEpochBase, first_tile<Shape>() / kTilesPerHead);
+    int kv, rope;
+    if (a.position) {
+      const int pos = *a.position;
+      kv = pos >= 0 ? (pos % a.slots) * kDf * 2 : -1;
+      rope = pos >= 0 && pos < a.rope_rows ? pos * kDf * 2 : -1;
+    } else {
+      kv = *a.kv_offset;
+      rope = *a.rope_offset;
+    }
+    const bool kv_ok = kv >= 0 && (kv % (kDf * 2)) == 0 && kv / (kDf * 2) < a.slots;
+    const bool rope_ok = rope >= 0 && (rope % (kDf * 2)) == 0 && rope / (kDf * 2) < a.rope_rows;
+    const int e = threadIdx.x - 64;
+    if (e == 0) {
+      st->kv_ok = kv_ok;
+      st->rope_ok = rope_ok;
+      st->slot = kv / (kDf * 2);
+      st->row = rope / (kDf * 2);
+    }
+    if (e >= 0 && e < 64) {  // 64 x 16 bytes per 512-element row
+      if (rope_ok) {
+        const size_t row = size_t(rope / (kDf * 2)) * kDf;
+        cp_async_16(st->cos + e * 8, a.cos + row + e * 8);
+        cp_async_16(st->sin + e * 8, a.sin + row + e * 8);
+      }
+      cp_async_16(st->qg + e * 8, a.q_rms + e * 8);
+      cp_async_16(st->kg + e * 8, a.k_rms + e * 8);
+    }
+  }
+
+  __device__ unsigned long long* words(int tile) const {
+    return reinterpret_cast<unsigned long long*>(sc.partials) + kSplitWordsFullQkv +
+           size_t(tile) * kMaxCtasPerGroup * kTileRows;
+  }
+
+  __device__ void finish_piece(int tile, int row, float v, int, GemvCtl&) const {
+    constexpr int UPT = Shape::kUnitsPerTile;
+    const int64_t grid = gridDim.x, total = Shape::kTotalUnits;
+    const int head = tile / kTilesPerHead;
+    const int run_last = int(int64_t(blockIdx.x + 1) * total / grid) - 1;
+    const int head_last = kTilesPerHead * head + kTilesPerHead - 1;
+    const int final_tile = run_last / UPT < head_last ? run_last / UPT : head_last;
+    if (int(blockIdx.x) == cta_of_unit(int64_t(kTilesPerHead * head) * UPT, grid, total) && tile == final_tile) {
+      finish_head(head, row, tile, v);
+      return;
+    }
+    const int first = cta_of_unit(int64_t(tile) * UPT, grid, total);
+    st_relaxed_gpu_u64(words(tile) + (blockIdx.x - first) * kTileRows + row,
+                       (static_cast<unsigned long long>(epoch) << 32) | __float_as_uint(v));
+  }
+
+  __device__ void finish_head(int head, int e, int own_tile, float own) const {
+    constexpr int UPT = Shape::kUnitsPerTile;
+    const int64_t grid = gridDim.x, total = Shape::kTotalUnits;
+    float y[kTilesPerHead];
+#pragma unroll
+    for (int t = 0; t < kTilesPerHead; ++t) {  // element e + 128 t of the head = row e of its tile t
+      const int tile = kTilesPerHead * head + t;
+      const int first = cta_of_unit(int64_t(tile) * UPT, grid, total);
+      const int span = cta_of_unit(int64_t(tile) * UPT + UPT - 1, grid, total) - first + 1;
+      const int r = tile * kTileRows + e;
+      const uint16_t sb = r < kQf ? a.q_scale[r] : a.k_scale[r - kQf];
+      float acc = __uint_as_float(0x7fc00000u);
+      if (span <= kMaxCtasPerGroup)
+        acc = sum_tagged(words(tile) + e, span, tile == own_tile ? int(blockIdx.x) - first : -1, own, epoch, sc.err);
+      else if (e == 0)
+        atomicOr(sc.err, kErrInternal);
+      y[t] = bf16_round(acc * bf16_to_f32(sb));  // scaled_projection (generate_references.py:265-274)
+    }
+    if (e == 0) sc.counters[kFullHeadEpochBase + head] = epoch;
+    double ss = 0.0;
+#pragma unroll
+    for (int t = 0; t < kTilesPerHead; ++t) ss += double(y[t]) * double(y[t]);
+    ss = warp_sum_d(ss);
+    cp_async_wait_all();
+    if ((threadIdx.x & 31) == 0) st->red[e / 32] = ss;
+    named_bar(kEpiBarrier, kEpiThreads);
+    const float inv = rms_inverse(((st->red[0] + st->red[1]) + st->red[2]) + st->red[3], kDf);
+    if (!st->kv_ok || !st->rope_ok) {
+      if (e == 0) atomicOr(sc.err, (st->kv_ok ? 0u : kErrKvOffset) | (st->rope_ok ? 0u : kErrRopeOffset));
+      named_bar(kEpiBarrier, kEpiThreads);
+      return;
+    }
+    const bool is_k = head == kGf;
+    const uint16_t* gamma = is_k ? st->kg : st->qg;
+    float nrm[kTilesPerHead];
+#pragma unroll
+    for (int t = 0; t < kTilesPerHead; ++t) {
+      const float sv = y[t] * inv;
+      nrm[t] = bf16_round(sv * bf16_to_f32(gamma[e + 128 * t]));
+      if (is_k) st->out_v[e + 128 * t] = f32_to_bf16(sv);  // v: no gamma, no rotation
+    }
+    // RoPE over 512: out[i] = bf16(bf16(n[i] cos[i]) + bf16(n[i ^ 256] sin'[i])), sin' with its
+    // low half negated (the partial rotation lives in the table: cos 1, sin 0 where it does not turn)
+#pragma unroll
+    for (int t = 0; t < kTilesPerHead; ++t) {
+      const int i = e + 128 * t;
+      const float c = bf16_round(nrm[t] * bf16_to_f32(st->cos[i]));
+      const float sn = bf16_round(nrm[t ^ 2] * bf16_to_f32(st->sin[i]));
+      st->out[i] = f32_to_bf16(c + sn);
+    }
+    named_bar(kEpiBarrier, kEpiThreads);
+    if (e < 64) {  // 16-byte stores
+      if (is_k) {
+        reinterpret_cast<uint4*>(a.k_cache + size_t(st->slot) * kDf)[e] = reinterpret_cast<const uint4*>(st->out)[e];
+        reinterpret_cast<uint4*>(a.v_cache + size_t(st->slot) * kDf)[e] = reinterpret_cast<const uint4*>(st->out_v)[e];
+      } else {
+        reinterpret_cast<uint4*>(a.q_out + head * kDf)[e] = reinterpret_cast<const uint4*>(st->out)[e];
+      }
+    }
+    named_bar(kEpiBarrier, kEpiThreads);
+  }
+
+  __device__ void load_static(int g, uint4 (&raw)[4]) const { load_group_gamma(a.input_rms, g, raw); }
+  __device__ void load_group(int g, uint4 (&raw)[4]) const { load_group_cg(a.x, g, raw); }
+  __device__ void finish_group(const uint4 (&raw)[4], float inv, float (&v)[16]) const { rms_apply16(raw, inv, v); }
+};
+
+__global__ void __launch_bounds__(kGemvThreads, 1) full_qkv_kernel(const __grid_constant__ FullQkvMaps maps,
+                                                                   FullQkvArgs a, Scratch sc) {
+  extern __shared__ __align__(1024) uint8_t smem[];
+  __shared__ FullQkvStatic st;
+  FullQkvOp op{&maps, a, sc};
+  op.st = &st;
+  gemv_run<FullQkvShape>(op, smem, sc);
+  cp_async_wait_all();
+}
+
+// Global layer O (FOG/src/ops.rs:184-199): the attention output divided by the softmax sum of its
+// head, bf16 (FOG/src/device/full/attention.rs:341-364), then the O projection with K = Qf, the
+// post-attention RMSNorm and the residual add: the sliding O's engine and tail (it shares their
+// scratch regions and counters: one op at a time per context).
+struct FullOOp {
+  using Shape = FullOShape;
+  const CUtensorMap* map;
+  FullOArgs a;
+  Scratch sc;
+  uint32_t tx_bytes = Shape::kABytes;
+  static constexpr bool kOwnPieces = false;
+  static constexpr bool kRms = false;
+  static constexpr int kRmsGroups = 0;
+
+  __device__ void load_unit(uint8_t* stage, int tile, int kc, uint64_t* bar, uint64_t policy) const {
+    if (a.tiled) {
+      tma_load_2d(stage, map, 0, (tile * Shape::kUnitsPerTile + kc) * kUnitBox, bar, policy);
+    } else {
+      tma_load_2d(stage, map, kc * kUnitK, tile * kTileRows, bar, policy);
+      tma_load_2d(stage + 16384, map, kc * kUnitK + 128, tile * kTileRows, bar, policy);
+    }
+  }
+  __device__ void prefetch_l2(int u0, int u1) const {
+    if (a.tiled) prefetch_units(a.o_weight, u0, u1, Shape::kABytes);
+  }
+  __device__ void prologue(GemvCtl&) { epoch = tail_epoch(sc.counters + kTailEpochO, first_tile<Shape>()); }
+  __device__ void load_static(int, uint4 (&)[4]) const {}
+  // the 16 elements of group g and the softmax sum of their head (raw[2].x)
+  __device__ void load_group(int g, uint4 (&raw)[4]) const {
+    load_group_cg(a.x, g, raw);
+    raw[2].x = __float_as_uint(__ldcg(a.running_sum + g * 16 / kDf));
+  }
+  __device__ void finish_group(const uint4 (&raw)[4], float, float (&v)[16]) const {
+    bf16x16_to_f32(raw[0], raw[1], v);
+    const float sum = __uint_as_float(raw[2].x);
+#pragma unroll
+    for (int j = 0; j < 16; ++j) v[j] = bf16_round(v[j] / sum);
+  }
+  __device__ void finalize_tile(int tile, int row, float v, GemvCtl&) const {
+    const int r = tile * kTileRows + row;
+    tail_record(*tail, a.post_rms, a.residual, sc.tile_ss + kTileSsO, sc.counters + kTailEpochO, epoch, tile, row,
+                bf16_round(v * bf16_to_f32(a.o_scale[r])));
+  }
+  ResidualTail* tail;
+  uint32_t epoch = 0;
+  unsigned long long* split_words = reinterpret_cast<unsigned long long*>(sc.partials) + kSplitWordsO;
+  uint32_t* split_epochs = sc.counters + kTailEpochO;
+};
+
+__global__ void __launch_bounds__(kGemvThreads, 1) full_o_kernel(const __grid_constant__ CUtensorMap map, FullOArgs a,
+                                                                 Scratch sc) {
+  extern __shared__ __align__(1024) uint8_t smem[];
+  __shared__ ResidualTail tail;
+  if (threadIdx.x == 0) tail.n = 0;  // ordered by the engine's first barrier
+  FullOOp op{&map, a, sc};
+  op.tail = &tail;
+  gemv_run<FullOShape>(op, smem, sc);
+  tail_update(tail, a.residual, sc, sc.tile_ss + kTileSsO, op.epoch, kH / kTileRows, nullptr);
+}
+
+// ---------------------------------------------------------------------------------------
 // FP8 feed-forward (per-output-channel f32 scales): up/gate + GeGLU, then down + post-RMSNorm +
 // residual + layer scalar. Each projection is the reference's scaled_projection,
 // bf16((x @ codes.T) * scale) (generate_references.py:265-274); the epilogues are those of the
@@ -838,6 +1086,7 @@ bool geometry_fits(int sm_count) {
   env.sm_count = sm_count;
   // the residual tails keep at most kMaxFinTiles finished tiles of a CTA in shared memory, and a
   // split tile's pieces must fit its kMaxCtasPerGroup slots
+  if (NTP == 1 && max_tiles_finished<FullOShape>(grid_for<FullOShape>(env)) > kMaxFinTiles) return false;
   return max_tiles_finished<typename S::O>(grid_for<typename S::O>(env)) <= kMaxFinTiles &&
          max_tiles_finished<typename S::Down>(grid_for<typename S::Down>(env)) <= kMaxFinTiles &&
          max_tiles_finished<typename S::Down8>(grid_for<typename S::Down8>(env)) <= kMaxFinTiles;
@@ -959,11 +1208,18 @@ cudaError_t launch_ffn8_t(const Ffn8Args& a, const LaunchEnv& env) {
     if ((e = env.maps->u8(a.gate_w, kH, kRows, 128, 64, true, &ug.gate))) return e;
     if ((e = env.maps->u8(a.down_w, kDownK, kH, 128, kTileRows, true, &dn))) return e;
   }
-  e = launch(ffn8_upgate_kernel<NTP>, grid_for<UG>(env), UG::kSmemBytes, env, ug, a, env.sc);
+  Scratch sc = env.sc;
+#ifdef G4_TRACE
+  if (sc.trace) sc.trace += 7 * 4096;  // profiling builds: separate stamp rows per kernel
+#endif
+  e = launch(ffn8_upgate_kernel<NTP>, grid_for<UG>(env), UG::kSmemBytes, env, ug, a, sc);
   if (e != cudaSuccess) return e;
   LaunchEnv chained = env;
   chained.pdl = true;  // the down pass prefetches its weights while the up/gate pass drains
-  return launch(ffn8_down_kernel<NTP>, grid_for<DN>(env), DN::kSmemBytes, chained, dn, a, chained.sc, env.tp);
+#ifdef G4_TRACE
+  if (sc.trace) sc.trace += 4096;
+#endif
+  return launch(ffn8_down_kernel<NTP>, grid_for<DN>(env), DN::kSmemBytes, chained, dn, a, sc, env.tp);
 }
 
 }  // namespace
@@ -975,6 +1231,12 @@ bool proj_geometry_fits(int sm_count) {
 
 cudaError_t prepare_proj_kernels() {
   cudaError_t e;
+  if ((e = cudaFuncSetAttribute(full_qkv_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                int(FullQkvShape::kSmemBytes))))
+    return e;
+  if ((e = cudaFuncSetAttribute(full_o_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                int(FullOShape::kSmemBytes))))
+    return e;
   if ((e = prepare_degree<1>())) return e;
   if ((e = prepare_degree<2>())) return e;
   if ((e = prepare_degree<4>())) return e;
@@ -991,6 +1253,27 @@ cudaError_t launch_o(const OArgs& a, const LaunchEnv& env) {
 
 cudaError_t launch_ffn_nvfp4(const FfnArgs& a, const LaunchEnv& env) {
   return by_degree(env.tp.world, [&](auto d) { return launch_ffn_t<decltype(d)::value>(a, env); });
+}
+
+cudaError_t launch_full_qkv(const FullQkvArgs& a, const LaunchEnv& env) {
+  if (env.tp.world != 1) return cudaErrorNotSupported;  // the global layers run on one GPU
+  FullQkvMaps m;
+  cudaError_t e;
+  const uint64_t cols = a.tiled ? 128 : kH, fq = a.tiled ? kH / 128 : 1;
+  const uint32_t box = a.tiled ? kUnitBox : kTileRows;
+  if ((e = env.maps->u8(a.q_weight, cols, uint64_t(kQf) * fq, 128, box, true, &m.q))) return e;
+  if ((e = env.maps->u8(a.k_weight, cols, uint64_t(kDf) * fq, 128, box, true, &m.k))) return e;
+  return launch(full_qkv_kernel, grid_for<FullQkvShape>(env), FullQkvShape::kSmemBytes, env, m, a, env.sc);
+}
+
+cudaError_t launch_full_o(const FullOArgs& a, const LaunchEnv& env) {
+  if (env.tp.world != 1) return cudaErrorNotSupported;
+  CUtensorMap m;
+  cudaError_t e;
+  if ((e = env.maps->u8(a.o_weight, a.tiled ? 128 : kQf, a.tiled ? uint64_t(kH) * (kQf / 128) : kH, 128,
+                        a.tiled ? kUnitBox : kTileRows, true, &m)))
+    return e;
+  return launch(full_o_kernel, grid_for<FullOShape>(env), FullOShape::kSmemBytes, env, m, a, env.sc);
 }
 
 cudaError_t launch_ffn_fp8(const Ffn8Args& a, const LaunchEnv& env) {

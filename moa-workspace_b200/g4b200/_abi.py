@@ -44,6 +44,10 @@ SIGNATURES = {
     "g4_sliding_project_qkv_tiled": [_p] * 18 + [_i32, _i32, _p],
     "g4_sliding_attention_output_tiled": [_p] * 6 + [_p],
     "g4_decoder_feedforward_tiled": [_p] * 12 + [_p],
+    "g4_full_project_qkv": [_p] * 16 + [_i32, _p],
+    "g4_full_attention_first_page": [_p] * 8 + [_p],
+    "g4_full_attention_page": [_p] * 8 + [_p],
+    "g4_full_attention_output": [_p] * 7 + [_p],
     "g4_embed_token": [_p] * 4 + [_i32, _p],
     "g4_final_norm_and_logits": [_p] * 5 + [_i32, _p],
     "g4_decoder_feedforward_fp8": [_p] * 11 + [_p],

@@ -18,12 +18,14 @@ import torch
 from . import _abi
 from .ops import Device, _check, _stream_ptr
 
+LAYER_SLIDING, LAYER_FULL = 0, 1
 ROPE_LOCAL, ROPE_GLOBAL = 0, 1
 FFN_NVFP4, FFN_FP8 = 0, 1
 
 
 class _Layer(ctypes.Structure):
-    _fields_ = [("rope", ctypes.c_int32), ("ring_len", ctypes.c_int32), ("ffn", ctypes.c_int32),
+    _fields_ = [("kind", ctypes.c_int32), ("rope", ctypes.c_int32), ("ring_len", ctypes.c_int32),
+                ("ffn", ctypes.c_int32),
                 ("tiled", ctypes.c_int32), ("attn_scale", ctypes.c_float)] + [
         (name, ctypes.c_void_p) for name in (
             "input_rms_weight", "q_weight", "k_weight", "v_weight", "q_weight_scale", "k_weight_scale",
@@ -38,7 +40,8 @@ class _Model(ctypes.Structure):
                 ("embedding_table", ctypes.c_void_p), ("vocab_rows", ctypes.c_int32),
                 ("final_norm_weight", ctypes.c_void_p), ("lm_head_weight", ctypes.c_void_p),
                 ("lm_head_rows", ctypes.c_int32), ("cos_local", ctypes.c_void_p), ("sin_local", ctypes.c_void_p),
-                ("cos_global", ctypes.c_void_p), ("sin_global", ctypes.c_void_p), ("rope_rows", ctypes.c_int32)]
+                ("cos_global", ctypes.c_void_p), ("sin_global", ctypes.c_void_p), ("rope_rows", ctypes.c_int32),
+                ("cos_full", ctypes.c_void_p), ("sin_full", ctypes.c_void_p)]
 
 
 @dataclass
@@ -50,10 +53,10 @@ class Layer:
     input_rms_weight: torch.Tensor
     q_weight: torch.Tensor
     k_weight: torch.Tensor
-    v_weight: torch.Tensor
+    v_weight: torch.Tensor | None
     q_weight_scale: torch.Tensor
     k_weight_scale: torch.Tensor
-    v_weight_scale: torch.Tensor
+    v_weight_scale: torch.Tensor | None
     q_rms_weight: torch.Tensor
     k_rms_weight: torch.Tensor
     k_cache: torch.Tensor
@@ -75,11 +78,13 @@ class Layer:
     down_global_scale: torch.Tensor | None = None
     rope: int = ROPE_LOCAL
     ffn: int = FFN_NVFP4
+    kind: int = LAYER_SLIDING
     tiled: bool = False
     attn_scale: float = 1.0
 
     @property
     def ring_len(self) -> int:
+        """KV slots: a sliding ring [slots, Ns, Ds], or a full layer's pages [slots, Df]."""
         return self.k_cache.shape[0]
 
 
@@ -92,17 +97,18 @@ class Decoder:
     as the decoder does (it keeps references)."""
 
     def __init__(self, device: Device, layers: list[Layer], *, cos_local, sin_local, cos_global=None,
-                 sin_global=None, embedding_table=None, final_norm_weight=None, lm_head_weight=None):
+                 sin_global=None, embedding_table=None, final_norm_weight=None, lm_head_weight=None, cos_full=None,
+                 sin_full=None):
         self.device = device
         self._keep = (layers, cos_local, sin_local, cos_global, sin_global, embedding_table, final_norm_weight,
-                      lm_head_weight)
+                      lm_head_weight, cos_full, sin_full)
         arr = (_Layer * max(1, len(layers)))()
         for i, lay in enumerate(layers):
             s = arr[i]
-            s.rope, s.ring_len, s.ffn, s.tiled, s.attn_scale = lay.rope, lay.ring_len, lay.ffn, int(lay.tiled), \
-                lay.attn_scale
+            s.kind, s.rope, s.ring_len, s.ffn, s.tiled, s.attn_scale = lay.kind, lay.rope, lay.ring_len, lay.ffn, \
+                int(lay.tiled), lay.attn_scale
             for f in fields(Layer):
-                if f.name in ("rope", "ffn", "tiled", "attn_scale"):
+                if f.name in ("kind", "rope", "ffn", "tiled", "attn_scale"):
                     continue
                 setattr(s, f.name, _ptr(getattr(lay, f.name)).value)
         self._layers = arr
@@ -117,6 +123,7 @@ class Decoder:
         m.cos_local, m.sin_local = _ptr(cos_local).value, _ptr(sin_local).value
         m.cos_global, m.sin_global = _ptr(cos_global).value, _ptr(sin_global).value
         m.rope_rows = cos_local.shape[0]
+        m.cos_full, m.sin_full = _ptr(cos_full).value, _ptr(sin_full).value
         self._model = m
         self._dec = ctypes.c_void_p()
         _check(device, _abi.lib().g4_decoder_create(device.handle, ctypes.byref(m), ctypes.byref(self._dec)),

@@ -145,6 +145,65 @@ def final_norm_and_logits(device: Device, input, rms_weight, lm_head_weight, out
     _check(device, st, "final_norm_and_logits")
 
 
+GF, DF, QF, TF = 16, 512, 8192, 512  # global layers: query heads, head dim, q rows, page slots
+
+
+def full_project_qkv(device: Device, x, q_weight, k_weight, q_weight_scale, k_weight_scale, input_rms_weight,
+                     q_rms_weight, k_rms_weight, kv_offset, rope_offset, cos, sin, k_cache, v_cache, q_out, *,
+                     stream=None) -> None:
+    """ops::full_project_qkv (src/ops.rs:78-116). k_cache / v_cache: the current page [Tf, Df];
+    cos / sin: [rows, Df] (the global table). One GPU only."""
+    bf = torch.bfloat16
+    rows = cos.shape[0] if cos.dim() == 2 else -1
+    args = [
+        _arg(x, "x", bf, (H,), device),
+        _arg(q_weight, "q_weight", _BYTE_DTYPES, (QF, H), device),
+        _arg(k_weight, "k_weight", _BYTE_DTYPES, (DF, H), device),
+        _arg(q_weight_scale, "q_weight_scale", bf, (QF,), device),
+        _arg(k_weight_scale, "k_weight_scale", bf, (DF,), device),
+        _arg(input_rms_weight, "input_rms_weight", bf, (H,), device),
+        _arg(q_rms_weight, "q_rms_weight", bf, (DF,), device),
+        _arg(k_rms_weight, "k_rms_weight", bf, (DF,), device),
+        _arg(kv_offset, "kv_offset", torch.int32, (1,), device),
+        _arg(rope_offset, "rope_offset", torch.int32, (1,), device),
+        _arg(cos, "cos", bf, (rows, DF), device),
+        _arg(sin, "sin", bf, (rows, DF), device),
+        _arg(k_cache, "k_cache", bf, (TF, DF), device),
+        _arg(v_cache, "v_cache", bf, (TF, DF), device),
+        _arg(q_out, "q_out", bf, (GF, DF), device),
+    ]
+    st = _abi.lib().g4_full_project_qkv(device.handle, *args, rows, _stream_ptr(stream, device.index))
+    _check(device, st, "full_project_qkv")
+
+
+def full_attention_page(device: Device, q, k, v, mask, running_max, running_sum, out_hbm, *, first: bool,
+                        stream=None) -> None:
+    """ops::full_attention_first_page (first=True) / ops::full_attention_page (src/ops.rs:148-182):
+    one page [Tf, Df] of K and V; running_max / running_sum [Gf] f32 and out_hbm [Gf, Df] carry the
+    online softmax from page to page."""
+    bf = torch.bfloat16
+    args = [_arg(q, "q", bf, (GF, DF), device), _arg(k, "k", bf, (TF, DF), device),
+            _arg(v, "v", bf, (TF, DF), device), _arg(mask, "mask", torch.float32, (TF,), device),
+            _arg(running_max, "running_max", torch.float32, (GF,), device),
+            _arg(running_sum, "running_sum", torch.float32, (GF,), device),
+            _arg(out_hbm, "out_hbm", bf, (GF, DF), device)]
+    fn = _abi.lib().g4_full_attention_first_page if first else _abi.lib().g4_full_attention_page
+    _check(device, fn(device.handle, *args, _stream_ptr(stream, device.index)), "full_attention_page")
+
+
+def full_attention_output(device: Device, x, running_sum, post_attn_rms_weight, o_weight, o_weight_scale,
+                          residual_hbm, *, stream=None) -> None:
+    """ops::full_attention_output (src/ops.rs:184-199). residual_hbm is updated in place."""
+    bf = torch.bfloat16
+    args = [_arg(x, "x", bf, (GF, DF), device), _arg(running_sum, "running_sum", torch.float32, (GF,), device),
+            _arg(post_attn_rms_weight, "post_attn_rms_weight", bf, (H,), device),
+            _arg(o_weight, "o_weight", _BYTE_DTYPES, (H, QF), device),
+            _arg(o_weight_scale, "o_weight_scale", bf, (H,), device),
+            _arg(residual_hbm, "residual_hbm", bf, (H,), device)]
+    st = _abi.lib().g4_full_attention_output(device.handle, *args, _stream_ptr(stream, device.index))
+    _check(device, st, "full_attention_output")
+
+
 def sliding_project_qkv(device: Device, x, q_weight, k_weight, v_weight, q_weight_scale, k_weight_scale,
                         v_weight_scale, input_rms_weight, q_rms_weight, k_rms_weight, kv_offset, rope_offset,
                         cos, sin, k_cache, v_cache, q_out, *, tiled=False, stream=None) -> None:

@@ -20,6 +20,9 @@ rounding is explicit. Citations use `FOG` = `furiosa-opt-gemma4-12B/` of the ref
                               the device semantics and is validated against a float64 softmax.
 - embed_token                 FOG/src/ops.rs:8-35 (device semantics: f32 scale, one bf16 cast)
 - final_norm_and_logits       FOG/src/ops.rs:241-298, FOG/src/device/shared/lm_head.rs:13-80
+- full_project_qkv            FOG/src/ops.rs:78-116 (global layers: 16 x 512 q heads, one K = V head)
+- full_attention_page         FOG/src/ops.rs:148-182, FOG/src/device/full/attention.rs:205-339
+- full_attention_output       FOG/src/ops.rs:184-199
 - feedforward_fp8             FP8-per-channel FFN: scaled_projection
                               (generate_references.py:265-274) in the decoder_feedforward epilogue
 - *_tp                        tensor-parallel split of O and the FFNs (no reference counterpart)
@@ -339,6 +342,85 @@ def final_norm_and_logits(x_bits, rms_weight_bits, lm_head_bits):
     logits = bf16_round((w @ h).astype(np.float32))
     capped = (np.tanh((logits / LOGIT_SOFTCAP).astype(np.float32)).astype(np.float32) * LOGIT_SOFTCAP)
     return f32_to_bf16(capped.astype(np.float32))
+
+
+# --- global (full-attention) layers: 16 query heads x 512, one KV head of 512 with K = V ---------
+
+def full_project_qkv(x, q_weight, k_weight, q_scale, k_scale, input_rms_weight, q_rms_weight, k_rms_weight,
+                     cos_row, sin_row_kernel, n_q=16, head_dim=512):
+    """ops::full_project_qkv (FOG/src/ops.rs:78-116): pre-RMSNorm, the q [16 x 512] and the single
+    k [512] projections (scaled_projection), per-head RMSNorm of q (gamma q_rms) and of k (gamma
+    k_rms); v is the same raw k projection normalised without a gamma (K = V,
+    FOG/src/device/full/rmsnorm.rs:182-200); RoPE on q and k with the global table (partial
+    rotation: the table's non-rotated frequencies are cos 1 / sin 0). Rounding points as the
+    sliding op's (each product and the sum of the rotation rounded to bf16). `sin_row_kernel` has
+    its low half negated. Returns (q [16, 512], k [512], v [512]) bf16 bits."""
+    h = rms_norm(x, input_rms_weight)
+    sin_true = np.array(sin_row_kernel, dtype=np.uint16, copy=True)
+    sin_true[: head_dim // 2] ^= np.uint16(0x8000)
+    q = scaled_projection(h, e4m3_to_f32(q_weight), bf16_to_f32(q_scale)).reshape(n_q, head_dim)
+    q = rope(rms_norm(q, q_rms_weight), cos_row, sin_true)
+    k_raw = scaled_projection(h, e4m3_to_f32(k_weight), bf16_to_f32(k_scale)).reshape(head_dim)
+    k = rope(rms_norm(k_raw, k_rms_weight), cos_row, sin_true)
+    v = rms_norm(k_raw, None)
+    return q, k, v
+
+
+FULL_GROUP = 32  # page rows contracted per bf16 partial (FOG/src/device/full/attention.rs:145-203)
+
+
+def full_attention_page(q, k_page, v_page, mask, running_max=None, running_sum=None, out=None):
+    """ops::full_attention_first_page / full_attention_page (FOG/src/ops.rs:148-182,
+    FOG/src/device/full/attention.rs:205-339) on one 512-slot page: s = bf16(q . k) in f32;
+    m = max over the page's slots (masked ones included), on later pages max(m, running max);
+    e = min(exp(s - m), mask); the page's sum = sum(e) + 1e-6; the page's values: for each group of
+    32 rows, bf16(sum_t bf16(e_t) v_t), then the groups added in f32 and rounded to bf16. The first
+    page stores them; a later page rescales by r = exp(old max - new max): sum = old sum * r +
+    page sum, out = bf16(bf16(old out * r) + page values). Returns (running_max [16] f32,
+    running_sum [16] f32, out [16, 512] bf16 bits)."""
+    qf, kf, vf = bf16_to_f32(q), bf16_to_f32(k_page), bf16_to_f32(v_page)
+    mk = np.asarray(mask, dtype=np.float32)
+    s = bf16_round((qf @ kf.T).astype(np.float32))                       # [16, T]
+    m = s.max(axis=-1).astype(np.float32)
+    if running_max is not None:
+        m = np.maximum(m, np.asarray(running_max, np.float32))
+    e = np.minimum(np.exp((s - m[:, None]).astype(np.float32)).astype(np.float32), mk[None, :])
+    page_sum = (e.sum(axis=-1, dtype=np.float32) + EPS).astype(np.float32)
+    w = bf16_round(e)
+    groups = [bf16_round((w[:, g:g + FULL_GROUP] @ vf[g:g + FULL_GROUP]).astype(np.float32))
+              for g in range(0, kf.shape[0], FULL_GROUP)]
+    total = np.zeros_like(groups[0])
+    for part in groups:
+        total = (total + part).astype(np.float32)
+    values = bf16_round(total)
+    if running_max is None:
+        return m, page_sum, f32_to_bf16(values)
+    r = np.exp((np.asarray(running_max, np.float32) - m).astype(np.float32)).astype(np.float32)
+    new_sum = (np.asarray(running_sum, np.float32) * r + page_sum).astype(np.float32)
+    scaled = bf16_round(bf16_to_f32(out) * r[:, None])
+    return m, new_sum, f32_to_bf16((scaled + values).astype(np.float32))
+
+
+def full_attention_output(x, running_sum, post_rms_weight, o_weight, o_scale, residual):
+    """ops::full_attention_output (FOG/src/ops.rs:184-199): bf16(out / running sum) per head
+    (full/attention.rs:341-364), the O projection (scaled_projection, K = 8192), RMSNorm,
+    residual add."""
+    xf = bf16_to_f32(x).reshape(16, 512)
+    y = f32_to_bf16((xf / np.asarray(running_sum, np.float32)[:, None]).astype(np.float32)).reshape(-1)
+    projected = scaled_projection(y, e4m3_to_f32(o_weight), bf16_to_f32(o_scale))
+    return add_bf16(residual, rms_norm(projected, post_rms_weight))
+
+
+def full_attention_float64(q, k_pages, v_pages, masks):
+    """Masked softmax attention over the pages in float64 (the mathematical op: gemma4.py's SDPA
+    with scale 1.0), for validating the paged restatement."""
+    qf = bf16_to_f32(q).astype(np.float64)
+    kf = np.concatenate([bf16_to_f32(k) for k in k_pages]).astype(np.float64)
+    vf = np.concatenate([bf16_to_f32(v) for v in v_pages]).astype(np.float64)
+    mk = np.concatenate([np.asarray(m) for m in masks])
+    s = np.where(mk[None, :] > 0, qf @ kf.T, -np.inf)
+    p = np.exp(s - s.max(axis=-1, keepdims=True))
+    return (p / p.sum(axis=-1, keepdims=True)) @ vf
 
 
 def sliding_attention(q, k_cache, v_cache, mask, scale=1.0):

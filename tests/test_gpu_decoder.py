@@ -17,11 +17,13 @@ H, L, NS, GS, DS, QS, PS = 3840, 15360, 8, 2, 256, 4096, 2048
 ROPE_ROWS, VOCAB, LM_ROWS = 4096, 4096, 8192
 
 
-def rope_table(theta):
+def rope_table(theta, dim=DS, rotated=DS):
+    """cos / sin [ROPE_ROWS, dim] for every position; `rotated` of the dims turn (the rest: cos 1, sin 0)."""
     import torch
 
     pos = np.arange(ROPE_ROWS, dtype=np.float64)[:, None]
-    inv = 1.0 / (np.float64(theta) ** (np.arange(0, DS, 2, dtype=np.float64) / DS))
+    inv = 1.0 / (np.float64(theta) ** (np.arange(0, rotated, 2, dtype=np.float64) / dim))
+    inv = np.concatenate([inv, np.zeros(dim // 2 - rotated // 2)])
     emb = np.concatenate([pos * inv, pos * inv], axis=1)
     cos, sin = np.cos(emb).astype(np.float32), np.sin(emb).astype(np.float32)
     sin = np.stack([negate_low_half(r) for r in sin])
@@ -76,6 +78,38 @@ def make_layer(gen, ring, rope, ffn, tiled, device):
     return lay
 
 
+def make_full_layer(gen, ring, ffn, tiled, device):
+    """A global (full-attention) layer: q [8192, H], the K = V head [512, H], O [H, 8192], pages of K / V."""
+    import torch
+    from g4b200 import decoder, ops
+
+    base = make_layer(gen, 1024, decoder.ROPE_GLOBAL, ffn, False, device)
+
+    def normal(*shape, std=1.0):
+        return torch.randn(*shape, generator=gen, device="cuda") * std
+
+    q_w, q_s = bench.quant_fp8_rows(normal(8192, H, std=0.02))
+    k_w, k_s = bench.quant_fp8_rows(normal(512, H, std=0.02))
+    o_w, o_s = bench.quant_fp8_rows(normal(H, 8192, std=0.02))
+    base.q_weight, base.k_weight, base.o_weight = q_w, k_w, o_w
+    base.q_weight_scale, base.k_weight_scale, base.o_weight_scale = (t.to(torch.bfloat16) for t in (q_s, k_s, o_s))
+    base.v_weight = base.v_weight_scale = None
+    base.q_rms_weight = (1 + normal(512, std=0.1)).to(torch.bfloat16)
+    base.k_rms_weight = (1 + normal(512, std=0.1)).to(torch.bfloat16)
+    base.k_cache = normal(ring, 512).to(torch.bfloat16)
+    base.v_cache = normal(ring, 512).to(torch.bfloat16)
+    base.kind = decoder.LAYER_FULL
+    base.rowmajor_q, base.rowmajor_k, base.rowmajor_o = q_w, k_w, o_w  # the full ops take the reference layout
+    if tiled:
+        for name in ("q_weight", "k_weight", "o_weight"):
+            setattr(base, name, ops.tile_weight(device, name, getattr(base, name)))
+        if ffn == decoder.FFN_FP8:
+            base.up_weight = ops.pack_upgate_fp8(device, base.rowmajor["up_weight"], base.rowmajor["gate_weight"])
+            base.down_weight = ops.tile_weight(device, "down_weight", base.rowmajor["down_weight"])
+        base.tiled = True
+    return base
+
+
 @pytest.fixture(scope="module")
 def model(device):
     import torch
@@ -85,15 +119,18 @@ def model(device):
     gen.manual_seed(77)
     layers = [make_layer(gen, 1024, decoder.ROPE_LOCAL, decoder.FFN_NVFP4, False, device),
               make_layer(gen, 4096, decoder.ROPE_GLOBAL, decoder.FFN_FP8, True, device),
+              make_full_layer(gen, 2048, decoder.FFN_FP8, True, device),
               make_layer(gen, 1024, decoder.ROPE_LOCAL, decoder.FFN_FP8, False, device),
+              make_full_layer(gen, 1024, decoder.FFN_NVFP4, False, device),
               make_layer(gen, 1024, decoder.ROPE_LOCAL, decoder.FFN_NVFP4, True, device)]
     cos_l, sin_l = rope_table(1e4)
     cos_g, sin_g = rope_table(1e6)
+    cos_f, sin_f = rope_table(1e6, 512, 128)
     table = (torch.randn((VOCAB, H), generator=gen, device="cuda") * 0.03).to(torch.bfloat16)
     lm_head = (torch.randn((LM_ROWS, H), generator=gen, device="cuda") * 0.03).to(torch.bfloat16)
     final_norm = (1 + torch.randn(H, generator=gen, device="cuda") * 0.1).to(torch.bfloat16)
-    return dict(layers=layers, cos_l=cos_l, sin_l=sin_l, cos_g=cos_g, sin_g=sin_g, table=table, lm_head=lm_head,
-                final_norm=final_norm)
+    return dict(layers=layers, cos_l=cos_l, sin_l=sin_l, cos_g=cos_g, sin_g=sin_g, cos_f=cos_f, sin_f=sin_f,
+                table=table, lm_head=lm_head, final_norm=final_norm)
 
 
 def caches(layers):
@@ -118,6 +155,30 @@ def one_by_one(device, m, token, pos):
     rope_off = torch.tensor([pos * DS * 2], dtype=torch.int32, device="cuda")
     for lay in m["layers"]:
         ring = lay.ring_len
+        if lay.kind == decoder.LAYER_FULL:  # the reference host's full-layer launches (runtime.rs:462-541)
+            slot = pos % ring
+            page = slot // 512
+            qf = torch.zeros((16, 512), dtype=torch.bfloat16, device="cuda")
+            of = torch.zeros_like(qf)
+            rmax = torch.zeros(16, dtype=torch.float32, device="cuda")
+            rsum = torch.zeros_like(rmax)
+            ops.full_project_qkv(device, x, lay.q_weight if not lay.tiled else lay.rowmajor_q, lay.k_weight
+                                 if not lay.tiled else lay.rowmajor_k, lay.q_weight_scale, lay.k_weight_scale,
+                                 lay.input_rms_weight, lay.q_rms_weight, lay.k_rms_weight,
+                                 torch.tensor([(slot % 512) * 512 * 2], dtype=torch.int32, device="cuda"),
+                                 torch.tensor([pos * 512 * 2], dtype=torch.int32, device="cuda"), m["cos_f"],
+                                 m["sin_f"], lay.k_cache[page * 512:(page + 1) * 512],
+                                 lay.v_cache[page * 512:(page + 1) * 512], qf)
+            for p in range(ring // 512):
+                if p * 512 > pos:
+                    break
+                mask = (torch.arange(512, device="cuda") + p * 512 <= pos).to(torch.float32)
+                ops.full_attention_page(device, qf, lay.k_cache[p * 512:(p + 1) * 512],
+                                        lay.v_cache[p * 512:(p + 1) * 512], mask, rmax, rsum, of, first=p == 0)
+            ops.full_attention_output(device, of, rsum, lay.post_attn_rms_weight,
+                                      lay.o_weight if not lay.tiled else lay.rowmajor_o, lay.o_weight_scale, x)
+            ffn_one(device, x, lay)
+            continue
         kv_off = torch.tensor([(pos % ring) * NS * DS * 2], dtype=torch.int32, device="cuda")
         mask = (torch.arange(ring, device="cuda") <= min(pos, ring - 1)).to(torch.float32)
         cos, sin = (m["cos_g"], m["sin_g"]) if lay.rope == decoder.ROPE_GLOBAL else (m["cos_l"], m["sin_l"])
@@ -128,27 +189,34 @@ def one_by_one(device, m, token, pos):
         ops.sliding_attention(device, q, lay.k_cache, lay.v_cache, mask, attn, scale=lay.attn_scale)
         ops.sliding_attention_output(device, attn, lay.post_attn_rms_weight, lay.o_weight, lay.o_weight_scale, x,
                                      tiled=lay.tiled)
-        if lay.ffn == decoder.FFN_FP8 and lay.tiled:
-            ops.decoder_feedforward_fp8_tiled(device, x, lay.pre_ff_rms_weight, lay.up_weight, lay.down_weight,
-                                              lay.up_scale, lay.gate_scale, lay.down_scale, lay.post_ff_rms_weight,
-                                              lay.layer_scalar)
-        elif lay.ffn == decoder.FFN_FP8:
-            ops.decoder_feedforward_fp8(device, x, lay.pre_ff_rms_weight, lay.up_weight, lay.gate_weight,
-                                        lay.down_weight, lay.up_scale, lay.gate_scale, lay.down_scale,
-                                        lay.post_ff_rms_weight, lay.layer_scalar)
-        elif lay.tiled:
-            ops.decoder_feedforward_tiled(device, x, lay.pre_ff_rms_weight, lay.up_weight, lay.down_weight,
-                                          lay.up_scale, lay.down_scale, lay.up_global_scale, lay.gate_global_scale,
-                                          lay.down_global_scale, lay.post_ff_rms_weight, lay.layer_scalar)
-        else:
-            ops.decoder_feedforward(device, x, lay.pre_ff_rms_weight, lay.up_weight, lay.gate_weight,
-                                    lay.down_weight, lay.up_scale, lay.gate_scale, lay.down_scale,
-                                    lay.up_global_scale, lay.gate_global_scale, lay.down_global_scale,
-                                    lay.post_ff_rms_weight, lay.layer_scalar)
+        ffn_one(device, x, lay)
     logits = torch.zeros(LM_ROWS, dtype=torch.bfloat16, device="cuda")
     ops.final_norm_and_logits(device, x, m["final_norm"], m["lm_head"], logits)
     device.check()
     return x.clone(), logits.clone()
+
+
+def ffn_one(device, x, lay):
+    """The layer's feed-forward through its entry point (NVFP4 or FP8, row-major or tiled)."""
+    from g4b200 import decoder, ops
+
+    if lay.ffn == decoder.FFN_FP8 and lay.tiled:
+        ops.decoder_feedforward_fp8_tiled(device, x, lay.pre_ff_rms_weight, lay.up_weight, lay.down_weight,
+                                          lay.up_scale, lay.gate_scale, lay.down_scale, lay.post_ff_rms_weight,
+                                          lay.layer_scalar)
+    elif lay.ffn == decoder.FFN_FP8:
+        ops.decoder_feedforward_fp8(device, x, lay.pre_ff_rms_weight, lay.up_weight, lay.gate_weight,
+                                    lay.down_weight, lay.up_scale, lay.gate_scale, lay.down_scale,
+                                    lay.post_ff_rms_weight, lay.layer_scalar)
+    elif lay.tiled:
+        ops.decoder_feedforward_tiled(device, x, lay.pre_ff_rms_weight, lay.up_weight, lay.down_weight,
+                                      lay.up_scale, lay.down_scale, lay.up_global_scale, lay.gate_global_scale,
+                                      lay.down_global_scale, lay.post_ff_rms_weight, lay.layer_scalar)
+    else:
+        ops.decoder_feedforward(device, x, lay.pre_ff_rms_weight, lay.up_weight, lay.gate_weight,
+                                lay.down_weight, lay.up_scale, lay.gate_scale, lay.down_scale,
+                                lay.up_global_scale, lay.gate_global_scale, lay.down_global_scale,
+                                lay.post_ff_rms_weight, lay.layer_scalar)
 
 
 def make_decoder(device, m):
@@ -156,7 +224,7 @@ def make_decoder(device, m):
 
     return decoder.Decoder(device, m["layers"], cos_local=m["cos_l"], sin_local=m["sin_l"], cos_global=m["cos_g"],
                            sin_global=m["sin_g"], embedding_table=m["table"], final_norm_weight=m["final_norm"],
-                           lm_head_weight=m["lm_head"])
+                           lm_head_weight=m["lm_head"], cos_full=m["cos_f"], sin_full=m["sin_f"])
 
 
 def equal(a, b):
