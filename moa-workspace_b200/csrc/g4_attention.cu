@@ -29,9 +29,9 @@ namespace {
 constexpr int kThreads = 256;
 constexpr int kWarps = kThreads / 32;
 constexpr int kRowBytes = kDs * 2;         // one head's row in one slot
-constexpr int kSub = 128;                  // slots resident in shared memory per pass
+constexpr int kSubMax = 128;               // slots resident in shared memory per pass (C = 8)
 constexpr int kBox = 32;                   // slots per TMA box, each with its own barrier
-constexpr int kBoxes = kSub / kBox;
+constexpr int kBoxes = kSubMax / kBox;
 constexpr int kMaxRing = 8192;
 constexpr int kMinChunks = 8;              // the portable cluster size; 16 where it can be scheduled
 
@@ -39,6 +39,9 @@ template <int C>  // CTAs per KV head = the cluster size
 struct AttnSmem {
   static constexpr int kMaxPer = kMaxRing / C;
   static constexpr int kDimsPerCta = kDs / C;  // head dimensions each CTA combines
+  // slots per pass: C = 16 serves rings of up to 1024 slots in one pass of 64, small enough that
+  // several CTAs share an SM (so eight 16-CTA clusters fit the GPU together)
+  static constexpr int kSub = C == 16 ? 64 : kSubMax;
   uint8_t k[kSub * kRowBytes];
   uint8_t v[kSub * kRowBytes];
   float score[kMaxPer][kGs];  // scores, then bf16-rounded probabilities
@@ -72,7 +75,7 @@ __device__ __forceinline__ float ld_cluster_f32(const void* own, uint32_t rank) 
 }
 
 template <int C>
-__global__ void __launch_bounds__(kThreads, 1) attention_kernel(const __grid_constant__ KvMaps maps, AttnArgs a,
+__global__ void __launch_bounds__(kThreads, 2) attention_kernel(const __grid_constant__ KvMaps maps, AttnArgs a,
                                                                 Scratch sc) {
   constexpr int kChunks = C;
   constexpr int kDimsPerCta = AttnSmem<C>::kDimsPerCta;
@@ -81,6 +84,7 @@ __global__ void __launch_bounds__(kThreads, 1) attention_kernel(const __grid_con
   const int head = blockIdx.x / kChunks;
   const int chunk = int(cluster_ctarank());  // == blockIdx.x % kChunks
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+  constexpr int kSub = AttnSmem<C>::kSub;
   const int per = a.ring_len / kChunks;  // a multiple of 32, at most kMaxPer
   const int slot0 = chunk * per;
   const int passes = (per + kSub - 1) / kSub;
@@ -602,7 +606,7 @@ cudaError_t launch_attention(const AttnArgs& a, const LaunchEnv& env) {
 #endif
   cudaLaunchAttribute attr[2];
   const bool c16 = env.device >= 0 && env.device < kMaxDevices && g_clusters16[env.device] == 1 &&
-                   a.ring_len % (16 * kBox) == 0;
+                   a.ring_len % (16 * kBox) == 0 && a.ring_len <= 16 * AttnSmem<16>::kSub;
   if (c16) {
     const cudaLaunchConfig_t cfg = attention_config<16>(a.heads, env.stream, env.pdl, attr);
     return cudaLaunchKernelEx(&cfg, attention_kernel<16>, maps, a, sc);

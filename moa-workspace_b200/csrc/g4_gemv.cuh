@@ -392,10 +392,12 @@ __device__ void gemv_run(Op& op, uint8_t* smem_raw, const Scratch& sc) {
   pdl_launch_dependents();
   G4_STAMP(sc, 1);
   {
-    op.prologue(ctl);  // scalar loads only
+    // the activation's loads go out first: the op's scalar prologue (offsets, then the copies that
+    // depend on them) would otherwise hold them back by a round trip
 #pragma unroll
     for (int q = 0; q < MAXG; ++q)
       if (have[q]) op.load_group(grp[q], raw[q]);
+    op.prologue(ctl);  // scalar loads only
     // The rest of the ring (and the L2 prefetch beyond it) is requested once the issuing
     // thread's activation loads have landed: issued earlier, the weight data queued for this SM
     // delays the activation's return by microseconds.
