@@ -104,9 +104,10 @@ WORKLOAD = ("gemma4-12b-shaped decode, batch 1, context 4096: embed_token + 48 l
             "rings, theta 1e4; 8 global-shaped on 4096-slot rings, theta 1e6; each fused QKV fp8 [8192x3840], "
             "attention 16 q / 8 kv heads x 256, O fp8 [3840x4096], FP8 GeGLU FFN [2x15360x3840 + 3840x15360] "
             "with f32 channel scales) + final norm and lm_head bf16 [262144x3840] with softcap 30")
-# DRAM bytes read + written per decoder_feedforward_fp8 call (ffn8 up/gate + down kernels), from an
-# ncu capture (dram__bytes_read.sum + dram__bytes_write.sum); None until measured
-FFN8_TRAFFIC = None
+# DRAM bytes read + written per decoder_feedforward_fp8 call (ffn8 up/gate + down kernels): ncu --set
+# full capture of `python bench.py --only ffn8 --layers 4 --steps 3 --warmup 3` (dram__bytes_read.sum +
+# dram__bytes_write.sum, profiles/ffn8_upgate_down_full.md)
+FFN8_TRAFFIC = 118.17e6 + 3.26e6 + 59.18e6 + 0.07e6
 
 
 def peaks():
