@@ -90,9 +90,9 @@ struct GemvShape {
 
 struct GemvCtl {
   uint64_t full[12], sready[12], done[16], tempty[16], dfull[4], dempty[4], drain;
+  uint64_t bready[16];    // fp8: the B slot's terms and exponent are in shared memory
   uint32_t tmem_base;
   uint32_t abort;
-  uint32_t unit_max[16];  // per B slot: max |activation| bits (fp8 weights)
   int pmax;               // nvfp4: largest exponent of this CTA's activation
   uint32_t nonfinite;     // nvfp4: an activation of this CTA is Inf or NaN
   float xchg[64];
@@ -288,12 +288,12 @@ __device__ void gemv_run(Op& op, uint8_t* smem_raw, const Scratch& sc) {
       mbar_init(&ctl.dempty[i], 4);  // nvfp4: the epilogue has read it
     }
     mbar_init(&ctl.drain, 1);
+    for (int i = 0; i < 16; ++i) mbar_init(&ctl.bready[i], 1);  // fp8: one arrival per built B slot
     ctl.abort = 0;
     ctl.pmax = -1000;
     ctl.nonfinite = 0;
     fence_mbar_init();
   }
-  if (c.tid < 16) ctl.unit_max[c.tid] = 0u;
   __syncwarp();
   if (c.warp == 1) tmem_alloc(&ctl.tmem_base, Shape::kTmemCols);
   tc_fence_before();
@@ -421,10 +421,12 @@ __device__ void gemv_run(Op& op, uint8_t* smem_raw, const Scratch& sc) {
     }
     float v[MAXG][16];
     int slot[MAXG];
+    uint32_t umax[MAXG];  // fp8: this group's max |v| bits
 #pragma unroll
     for (int q = 0; q < MAXG; ++q) {
       slot[q] = c.bslot(grp[q] / 16);
       have[q] = have[q] && slot[q] < nslots;
+      umax[q] = 0u;
       if (have[q]) {
         op.finish_group(raw[q], inv, v[q]);
         float amax = 0.f;
@@ -446,12 +448,12 @@ __device__ void gemv_run(Op& op, uint8_t* smem_raw, const Scratch& sc) {
           dst[0] = make_uint4(bits[0], bits[1], bits[2], bits[3]);
           dst[1] = make_uint4(bits[4], bits[5], bits[6], bits[7]);
         } else {  // one exponent per 256-element unit; non-negative floats order as ints
-          atomicMax(&ctl.unit_max[slot[q]], __float_as_uint(amax));
+          umax[q] = __float_as_uint(amax);
         }
       }
     }
     if constexpr (!Op::kRms) request_rest();
-    __syncthreads();
+    if constexpr (Shape::kFp4) __syncthreads();  // the CTA's largest exponent (pmax) is complete
     G4_STAMP(sc, 10);
     if constexpr (Shape::kFp4) {
       // digit rows, one thread per 8 elements
@@ -474,28 +476,42 @@ __device__ void gemv_run(Op& op, uint8_t* smem_raw, const Scratch& sc) {
         }
         return e;
       };
+      // Slot by slot, with no CTA-wide barrier: the 16 groups of a K unit are held by 16
+      // consecutive threads (j = tid + 224 q and j / 16 name the unit), an aligned half-warp, so
+      // the unit's largest |v| is a half-warp reduction; the half-warp then writes the unit's
+      // terms and arrives on the slot's barrier, and the relay releases a unit as soon as its
+      // slot is ready (the first MMAs start while later slots are still being built).
 #pragma unroll
       for (int q = 0; q < MAXG; ++q) {
-        if (!have[q]) continue;
-        const int e16 = (grp[q] % 16) * 16;
-        const int e = exponent_of(__uint_as_float(ctl.unit_max[slot[q]]));
-        const float up = pow2f(e);
-        gexp[slot[q] * 16 + grp[q] % 16] = pow2f(-e);
+        uint32_t m = umax[q];
 #pragma unroll
-        for (int j = 0; j < 16; ++j) v[q][j] *= up;
-        uint4 tm[8];
-        split_terms16<8>(v[q], tm);
-        uint8_t* atom = c.bsm + size_t(slot[q]) * Shape::kBSlotBytes + (e16 / 128) * 1024;
-        const uint32_t kb = e16 % 128;
+        for (int o = 8; o; o >>= 1) m = max(m, __shfl_xor_sync(0xffffffffu, m, o));
+        if (have[q]) {
+          const int e16 = (grp[q] % 16) * 16;
+          const int e = exponent_of(__uint_as_float(m));
+          const float up = pow2f(e);
+          gexp[slot[q] * 16 + grp[q] % 16] = pow2f(-e);
 #pragma unroll
-        for (int r = 0; r < 8; ++r) *reinterpret_cast<uint4*>(atom + sw128_offset(r, kb)) = tm[r];
+          for (int j = 0; j < 16; ++j) v[q][j] *= up;
+          uint4 tm[8];
+          split_terms16<8>(v[q], tm);
+          uint8_t* atom = c.bsm + size_t(slot[q]) * Shape::kBSlotBytes + (e16 / 128) * 1024;
+          const uint32_t kb = e16 % 128;
+#pragma unroll
+          for (int r = 0; r < 8; ++r) *reinterpret_cast<uint4*>(atom + sw128_offset(r, kb)) = tm[r];
+          asm volatile("fence.proxy.async.shared::cta;" ::: "memory");  // the tensor cores read it
+        }
+        __syncwarp();
+        if (have[q] && (c.lane & 15) == 0) mbar_arrive(&ctl.bready[slot[q]]);
       }
     }
     G4_STAMP(sc, 11);
   }
-  asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
-  tc_fence_before();
-  __syncthreads();
+  if constexpr (Shape::kFp4) {
+    asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+    tc_fence_before();
+    __syncthreads();
+  }
   G4_STAMP(sc, 2);
 
   if (c.warp == 0) {
@@ -547,7 +563,8 @@ __device__ void gemv_run(Op& op, uint8_t* smem_raw, const Scratch& sc) {
                                       abort, sc.err);
         } else {
           bad = !mbar_wait_or_abort(&ctl.full[s], uint32_t((i / S) & 1), abort, sc.err) ||
-                (i >= T && !mbar_wait_or_abort(&ctl.tempty[i % T], uint32_t(((i / T) - 1) & 1), abort, sc.err));
+                (i >= T && !mbar_wait_or_abort(&ctl.tempty[i % T], uint32_t(((i / T) - 1) & 1), abort, sc.err)) ||
+                !mbar_wait_or_abort(&ctl.bready[c.bslot(kc)], 0u, abort, sc.err);
         }
       }
 #ifdef G4_TRACE
@@ -636,6 +653,9 @@ __device__ void gemv_run(Op& op, uint8_t* smem_raw, const Scratch& sc) {
         }
       } else {
         if (ok) ok = mbar_wait_or_abort(&ctl.done[t], uint32_t((i / T) & 1), abort, sc.err);
+        // (the slot's exponent below was written before its barrier, which the unit's release
+        // passed; this test makes that order explicit for these threads)
+        if (ok) ok = mbar_wait_or_abort(&ctl.bready[c.bslot(kc)], 0u, abort, sc.err);
         if (row == 0 && i == 0) G4_STAMP_T(sc, 5);
         tc_fence_after();
         if (ok) {
