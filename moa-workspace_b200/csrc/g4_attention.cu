@@ -39,7 +39,7 @@ template <int C>  // CTAs per KV head = the cluster size
 struct AttnSmem {
   static constexpr int kMaxPer = kMaxRing / C;
   static constexpr int kDimsPerCta = kDs / C;  // head dimensions each CTA combines
-  // slots per pass: C = 16 serves rings of up to 1024 slots in one pass of 64, small enough that
+  // slots per pass: C = 16 serves rings of up to 4096 slots in passes of 64, small enough that
   // several CTAs share an SM (so eight 16-CTA clusters fit the GPU together)
   static constexpr int kSub = C == 16 ? 64 : kSubMax;
   uint8_t k[kSub * kRowBytes];
@@ -606,7 +606,7 @@ cudaError_t launch_attention(const AttnArgs& a, const LaunchEnv& env) {
 #endif
   cudaLaunchAttribute attr[2];
   const bool c16 = env.device >= 0 && env.device < kMaxDevices && g_clusters16[env.device] == 1 &&
-                   a.ring_len % (16 * kBox) == 0 && a.ring_len <= 16 * AttnSmem<16>::kSub;
+                   a.ring_len % (16 * kBox) == 0 && a.ring_len <= 4 * 16 * AttnSmem<16>::kSub;  // <= 4 passes
   if (c16) {
     const cudaLaunchConfig_t cfg = attention_config<16>(a.heads, env.stream, env.pdl, attr);
     return cudaLaunchKernelEx(&cfg, attention_kernel<16>, maps, a, sc);
