@@ -772,8 +772,7 @@ def run_reference(args):
         "steps": len(rates), "warmup": min(args.warmup, 2), "ms_per_step": 1e3 / value, "higher_is_better": True,
         "scaling": "strong" if args.gpus > 1 else "weak", "vs_baseline": None,
         "dtype": "f32 (numpy oracle port, bf16 rounding points emulated)",
-        "data": "synthetic", "config": dict(config_for(args.gpus), parallelism=f"host CPU, {cores} threads, one process",
-                                           launch="numpy on the host"),
+        "data": "synthetic", "config": dict(config_for(args.gpus), parallelism=f"host CPU, {cores} threads, one process"),
         "cpu_baseline": {"value": value, "unit": "tokens/s", "cores": cores, "kind": "port", "sample": sample},
         "e2e": {"value": value, "unit": "tokens/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
     }

@@ -114,6 +114,19 @@ def _tp_rank(rank, world, port, out_dir):
             ops.decoder_feedforward(dev, res, *ffn_in)
             dev.check()
             out[f"ffn{i}"] = host(res)
+        # the FP8 feed-forward on BASELINE's Gaussian data, twice
+        import gaussian
+
+        g8 = gaussian.ffn_fp8()
+        ffn8_in = [cuda(g8["pre_ff_rms_weight"]), cuda(g8["up_weight"], "up_weight"),
+                   cuda(g8["gate_weight"], "gate_weight"), cuda(g8["down_weight"], "down_weight"),
+                   cuda(g8["up_weight_scale"], "up_channel_scale"), cuda(g8["gate_weight_scale"], "gate_channel_scale"),
+                   cuda(g8["down_weight_scale"]), cuda(g8["post_ff_rms_weight"]), cuda(g8["layer_scalar"])]
+        for i in range(2):
+            res = cuda(g8["residual"])
+            ops.decoder_feedforward_fp8(dev, res, *ffn8_in)
+            dev.check()
+            out[f"ffn8_{i}"] = host(res)
         np.savez(os.path.join(out_dir, f"rank{rank}.npz"), **out)
         dist.barrier()
     finally:
@@ -160,6 +173,29 @@ def test_tensor_parallel_layer(world, tmp_path, golden_runs):
                 assert np.array_equal(o[f"{key}{i}"], first), (key, i)
         ok, maxd, exact = within(golden_runs[f"run{run}.{name}.expected"], first, ATOL[name])
         assert ok and exact > floor, (key, maxd, exact)
+
+    # FP8 feed-forward: one result on every rank, each call; against the rank-order oracle
+    import gaussian
+    import torch
+    from g4b200 import tp
+
+    g8 = gaussian.ffn_fp8()
+    first = outs[0]["ffn8_0"]
+    for o in outs:
+        assert np.array_equal(o["ffn8_0"], first) and np.array_equal(o["ffn8_1"], first)
+
+    def cut(name, arr, r):
+        return tp.shard(name, torch.from_numpy(arr), r, world).numpy()
+
+    want = oracle.feedforward_fp8_tp(
+        g8["residual"], g8["pre_ff_rms_weight"],
+        [(cut("up_weight", g8["up_weight"], r), cut("up_channel_scale", g8["up_weight_scale"], r)) for r in range(world)],
+        [(cut("gate_weight", g8["gate_weight"], r), cut("gate_channel_scale", g8["gate_weight_scale"], r))
+         for r in range(world)],
+        [cut("down_weight", g8["down_weight"], r) for r in range(world)], g8["down_weight_scale"],
+        g8["post_ff_rms_weight"], g8["layer_scalar"])
+    ok, maxd, exact = within(want, first, ATOL["decoder_feedforward"])
+    assert ok and exact > 0.95, ("ffn8", maxd, exact)
 
 
 def test_setup_refusals():
