@@ -7,8 +7,9 @@
 //   sum[g] = sum_t p[g,t] + 1e-6
 //   out    = bf16( bf16(sum_t bf16(p[g,t]) v[t]) / sum[g] )
 //
-// One thread-block cluster of C CTAs per KV head (C = 16 where the GPU can hold the clusters,
-// else the portable 8: 128 or 64 CTAs for the 8 heads; a tensor-parallel rank holds 8 / n of
+// One thread-block cluster of C CTAs per KV head (C = 16 for rings of 2048 to 4096 slots where
+// the GPU can hold the clusters, else the portable 8: 128 or 64 CTAs for the 8 heads; a
+// tensor-parallel rank holds 8 / n of
 // them in its cache slice), each owning a contiguous run of ring slots. A CTA copies its K and V
 // rows into shared memory with TMA boxes of 32 rows, each completing on its own barrier so that
 // scoring starts as the first box lands (the V rows of the first pass are requested with the K
@@ -606,7 +607,8 @@ cudaError_t launch_attention(const AttnArgs& a, const LaunchEnv& env) {
 #endif
   cudaLaunchAttribute attr[2];
   const bool c16 = env.device >= 0 && env.device < kMaxDevices && g_clusters16[env.device] == 1 &&
-                   a.ring_len % (16 * kBox) == 0 && a.ring_len <= 4 * 16 * AttnSmem<16>::kSub;  // <= 4 passes
+                   a.ring_len % (16 * kBox) == 0 && a.ring_len >= 2048 &&
+                   a.ring_len <= 4 * 16 * AttnSmem<16>::kSub;  // 2 to 4 passes (shorter rings: measured faster at 8)
   if (c16) {
     const cudaLaunchConfig_t cfg = attention_config<16>(a.heads, env.stream, env.pdl, attr);
     return cudaLaunchKernelEx(&cfg, attention_kernel<16>, maps, a, sc);
