@@ -60,6 +60,7 @@ RING_LOCAL, RING_GLOBAL = 1024, 4096
 NVFP4_COPIES = 4      # NVFP4 layer copies for the configs[3] per-op timing (> 3x L2 together)
 POSITION = 4000       # the decoded token's position (context 4096)
 KERNELS_PER_LAYER = 5  # qkv, attention, o, ffn up/gate, ffn down
+BATCH_SWEEP = (8, 16, 64)  # configs[3]: the NVFP4 feed-forward's token batches beyond M = 1
 
 
 def is_global(i):
@@ -87,6 +88,9 @@ def op_bytes(world=1):
         "decoder_feedforward": 2 * (fr * H // 2 + fr * H // 16) + (H * dk // 2 + H * dk // 16) + H * 2 * 4 + 8 * 2
                                + 12,
         "final_norm_and_logits": rows * H * 2 + H * 2 * 2 + rows * 2,
+        # the NVFP4 feed-forward on M tokens: the same weights once, M residual rows in and out
+        **{f"decoder_feedforward_m{mb}": 2 * (L * H // 2 + L * H // 16) + (H * L // 2 + H * L // 16)
+           + mb * H * 2 * 2 + H * 2 * 2 + 8 * 2 + 12 for mb in BATCH_SWEEP},
     }
 
 
@@ -403,6 +407,12 @@ def layer_ops(ops, device, m: Model, b: Buffers, lay: Layer, which=("qkv", "attn
                                           lay.up_g, lay.gate_g, lay.down_g, lay.post_ff_rms, lay.layer_scalar)
 
 
+def ffn_batch(ops, device, lay: Layer, rows):
+    """The NVFP4 feed-forward of `lay` on the token batch `rows` [M, H] (updated in place)."""
+    ops.decoder_feedforward_batch_tiled(device, rows, lay.pre_ff_rms, lay.up_w, lay.down_w, lay.up_s, lay.down_s,
+                                        lay.up_g, lay.gate_g, lay.down_g, lay.post_ff_rms, lay.layer_scalar)
+
+
 def decode_one_by_one(ops, device, m: Model, b: Buffers, logits):
     ops.embed_token(device, m.table, b.token_off, b.x)
     for lay in m.layers:
@@ -557,10 +567,25 @@ def parity(torch, ops, device, dev, m: Model, rank, world, dist):
         if rank == 0:
             res.update(r[0])
             same = same and r[1]
+    batch_rows = None
+    if world == 1:  # the NVFP4 feed-forward on a batch of 8 tokens (configs[3]'s sweep)
+        rows = (torch.randn(8, H, device=dev, generator=torch.Generator(device=dev).manual_seed(8))
+                .to(torch.bfloat16))
+        batch_in = host_array(rows)
+        ffn_batch(ops, device, m.nvfp4[0], rows)
+        device.check()
+        batch_rows = host_array(rows)
     if rank != 0:
         return None
     from oracle import ops as oracle
 
+    if batch_rows is not None:
+        h = m.nvfp4[0].host
+        want_b = oracle.decoder_feedforward_batch(batch_in, h["pre_ff_rms"], h["up_w"], h["gate_w"], h["down_w"],
+                                                  h["up_s"], h["gate_s"], h["down_s"], h["up_g"][0], h["gate_g"][0],
+                                                  h["down_g"][0], h["post_ff_rms"], h["layer_scalar"])
+        res["nvfp4.decoder_feedforward_batch_m8"] = compare("decoder_feedforward", want_b.reshape(-1),
+                                                            batch_rows.reshape(-1))
     table_rows = host_array(m.table[b.token])
     emb = host_array(dec_embed(torch, ops, device, m, b))
     res["embed_token"] = {"ok": bool(np.array_equal(emb, oracle.embed_token(table_rows[None, :], 0))),
@@ -575,7 +600,8 @@ def parity(torch, ops, device, dev, m: Model, rank, world, dist):
             "ranks_bit_identical": same if world > 1 else None, "ops": res,
             "checked": f"token {b.token} at position {b.pos}: the decoder step against the ops one by one (bit for "
                        "bit), then each op of layers 0 (sliding) and 5 (global-shaped) and of an NVFP4 layer against "
-                       "oracle/ops.py (numpy) on the previous op's GPU output, the embedding and every 61st logit" +
+                       "oracle/ops.py (numpy) on the previous op's GPU output, the NVFP4 feed-forward on a batch of 8 "
+                       "tokens row by row (one GPU), the embedding and every 61st logit" +
                        (", O/FFN as the rank-order sum of the ranks' partials" if world > 1 else "")}
 
 
@@ -799,6 +825,12 @@ def op_timings(torch, ops, device, dev, m: Model, dist, reps=64):
         "decoder_feedforward": lambda i: layer_ops(ops, device, m, b, m.nvfp4[i % NVFP4_COPIES], ("ffn",)),
         "final_norm_and_logits": lambda i: ops.final_norm_and_logits(device, b.x, m.final_norm, m.lm_head, logits),
     }
+    if m.world == 1:  # configs[3]'s token batches (one GPU)
+        rows = (torch.randn(max(BATCH_SWEEP), H, device=dev, generator=torch.Generator(device=dev).manual_seed(3))
+                .to(torch.bfloat16))
+        for mb in BATCH_SWEEP:
+            cases[f"decoder_feedforward_m{mb}"] = (
+                lambda i, mb=mb: ffn_batch(ops, device, m.nvfp4[i % NVFP4_COPIES], rows[:mb]))
     us = {}
     for name, fn in cases.items():
         n = reps if name != "final_norm_and_logits" else 8  # 2 GB / 8 per call: the logits stream from HBM
@@ -979,7 +1011,7 @@ def run_only(args):
         return 0
     gen = torch.Generator(device=dev)
     gen.manual_seed(1000)
-    ffn = "nvfp4" if args.only == "ffn4" else "fp8"
+    ffn = "nvfp4" if args.only in ("ffn4", "ffn4b") else "fp8"
     layers = [Layer(gen, dev, ffn, RING_LOCAL).tile(ops, device) for _ in range(args.layers)]
 
     class Mini:  # the parts of Model that layer_ops needs
@@ -990,14 +1022,23 @@ def run_only(args):
             return Mini.cos_l, Mini.sin_l
 
     b = Buffers(dev, 1)
-    which = {"qkv": ("qkv",), "attn": ("attn",), "o": ("o",), "ffn8": ("ffn",), "ffn4": ("ffn",)}[args.only]
+    if args.only == "ffn4b":  # the NVFP4 feed-forward on a batch of --batch tokens
+        rows = torch.randn(args.batch, H, device=dev, generator=gen).to(torch.bfloat16)
+
+        def call(i):
+            ffn_batch(ops, device, layers[i % len(layers)], rows)
+    else:
+        which = {"qkv": ("qkv",), "attn": ("attn",), "o": ("o",), "ffn8": ("ffn",), "ffn4": ("ffn",)}[args.only]
+
+        def call(i):
+            layer_ops(ops, device, Mini, b, layers[i % len(layers)], which)
     for i in range(args.warmup):
-        layer_ops(ops, device, Mini, b, layers[i % len(layers)], which)
+        call(i)
     device.check()
     start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     start.record()
     for i in range(args.steps):
-        layer_ops(ops, device, Mini, b, layers[i % len(layers)], which)
+        call(i)
     end.record()
     device.check()
     us = start.elapsed_time(end) * 1e3 / max(args.steps, 1)
@@ -1008,7 +1049,8 @@ def run_only(args):
 
 def main():
     ap = argparse.ArgumentParser()
-    ap.add_argument("--only", choices=["qkv", "attn", "o", "ffn8", "ffn4", "decode"], default=None,
+    ap.add_argument("--batch", type=int, default=16, help="--only ffn4b: tokens per call")
+    ap.add_argument("--only", choices=["qkv", "attn", "o", "ffn8", "ffn4", "ffn4b", "decode"], default=None,
                     help="profiling aid: eager calls of one op only (prints us/call, not the bench line)")
     ap.add_argument("--layers", type=int, default=4, help="--only: layer copies to rotate over")
     ap.add_argument("--gpus", type=int, default=1)

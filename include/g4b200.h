@@ -222,6 +222,27 @@ g4_status g4_decoder_feedforward_fp8_tiled(g4_ctx* ctx, uint16_t* residual_hbm, 
                                            const float* down_weight_scale, const uint16_t* post_ff_rms_weight,
                                            const uint16_t* layer_scalar, void* stream);
 
+/* ops::decoder_feedforward (src/ops.rs:201-239) on a batch of m tokens (the token-batch sweep of
+ * the NVFP4 feed-forward): each row of residual_hbm [m, H] (row stride H) is updated exactly as
+ * g4_decoder_feedforward updates one residual, and the weights are read from HBM once for all m
+ * rows. m in [1, 64]; m = 1 runs g4_decoder_feedforward's kernels. For m > 1 the contraction runs
+ * on tcgen05 kind::f16 tiles (the weights dequantised to bf16 in shared memory, exactly) with the
+ * tokens as the MMA's N. A tensor-parallel context supports m = 1 only (G4_ERR_UNSUPPORTED). The
+ * _tiled form takes g4_pack_tiles buffers like g4_decoder_feedforward_tiled. */
+g4_status g4_decoder_feedforward_batch(g4_ctx* ctx, uint16_t* residual_hbm, const uint16_t* pre_ff_rms_weight,
+                                       const uint8_t* up_weight_packed, const uint8_t* gate_weight_packed,
+                                       const uint8_t* down_weight_packed, const uint8_t* up_weight_scale,
+                                       const uint8_t* gate_weight_scale, const uint8_t* down_weight_scale,
+                                       const float* up_global_scale, const float* gate_global_scale,
+                                       const float* down_global_scale, const uint16_t* post_ff_rms_weight,
+                                       const uint16_t* layer_scalar, int32_t m, void* stream);
+g4_status g4_decoder_feedforward_batch_tiled(g4_ctx* ctx, uint16_t* residual_hbm, const uint16_t* pre_ff_rms_weight,
+                                             const uint8_t* up_gate_weight_tiled, const uint8_t* down_weight_tiled,
+                                             const uint8_t* up_gate_scale_tiled, const uint8_t* down_scale_tiled,
+                                             const float* up_global_scale, const float* gate_global_scale,
+                                             const float* down_global_scale, const uint16_t* post_ff_rms_weight,
+                                             const uint16_t* layer_scalar, int32_t m, void* stream);
+
 /* No counterpart in the reference: ops::sliding_attention_output (src/ops.rs:130-146) with no
  * context and no allocation, for callers that cannot create a g4_ctx. g4_ctx_create allocates
  * device scratch (cudaMalloc) and host state; some callers may not allocate at all: a host

@@ -14,7 +14,7 @@ import sys
 from pathlib import Path
 
 HERE = Path(__file__).resolve().parent
-SOURCES = ["csrc/g4_proj.cu", "csrc/g4_attention.cu", "csrc/g4_vocab.cu", "csrc/g4_decoder.cu", "csrc/g4_abi.cu"]
+SOURCES = ["csrc/g4_proj.cu", "csrc/g4_batch.cu", "csrc/g4_attention.cu", "csrc/g4_vocab.cu", "csrc/g4_decoder.cu", "csrc/g4_abi.cu"]
 HEADERS = ["csrc/g4_common.cuh", "csrc/g4_tc.cuh", "csrc/g4_gemv.cuh", "csrc/g4_ops.cuh", "csrc/g4_ctx.cuh",
            "../include/g4b200.h"]
 OUTPUT = HERE / "g4b200" / "libg4b200.so"

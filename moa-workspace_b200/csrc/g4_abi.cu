@@ -90,7 +90,11 @@ g4_status g4_ctx_create(int device, g4_ctx** out) {
   const size_t off_partials = off_counters + g4::kCounterCount * sizeof(uint32_t);
   const size_t off_act = off_partials + g4::kPartialFloats * sizeof(float);
   const size_t off_ss = off_act + size_t(64) * g4::kL * sizeof(uint16_t);
-  const size_t off_trace = off_ss + g4::kTileSsBytes;
+  const size_t off_bh = off_ss + g4::kTileSsBytes;  // batched feed-forward: h | y | split-K words | sums
+  const size_t off_by = off_bh + size_t(g4::kBatchMax) * g4::kH * sizeof(uint16_t);
+  const size_t off_bw = off_by + size_t(g4::kBatchMax) * g4::kH * sizeof(uint16_t);
+  const size_t off_bs = off_bw + g4::batch_words_count(ctx->sm_count) * sizeof(unsigned long long);
+  const size_t off_trace = off_bs + g4::kBatchSsWords * sizeof(unsigned long long);
 #ifdef G4_TRACE
   const size_t total = off_trace + size_t(65536 + 4096 * 32 * 8) * sizeof(uint64_t);
 #else
@@ -100,6 +104,7 @@ g4_status g4_ctx_create(int device, g4_ctx** out) {
   if (e == cudaSuccess) e = cudaMemset(ctx->scratch, 0, total);
   if (e == cudaSuccess) e = g4::prepare_proj_kernels();
   if (e == cudaSuccess) e = g4::prepare_attention_kernels();
+  if (e == cudaSuccess) e = g4::prepare_batch_kernels();
   if (e == cudaSuccess) e = cudaDeviceSynchronize();
   if (e != cudaSuccess) {
     if (ctx->scratch) cudaFree(ctx->scratch);
@@ -114,6 +119,11 @@ g4_status g4_ctx_create(int device, g4_ctx** out) {
   ctx->sc.act = reinterpret_cast<uint16_t*>(base + off_act);
   ctx->act_bytes = off_ss - off_act;
   ctx->sc.tile_ss = reinterpret_cast<unsigned long long*>(base + off_ss);
+  ctx->sc.batch_h = reinterpret_cast<uint16_t*>(base + off_bh);
+  ctx->sc.batch_y = reinterpret_cast<uint16_t*>(base + off_by);
+  ctx->sc.batch_words = reinterpret_cast<unsigned long long*>(base + off_bw);
+  ctx->sc.batch_ss = reinterpret_cast<unsigned long long*>(base + off_bs);
+  ctx->batch_ok = g4::batch_geometry_fits(ctx->sm_count);
 #ifdef G4_TRACE
   ctx->sc.trace = reinterpret_cast<uint64_t*>(base + off_trace);
 #else
@@ -242,8 +252,11 @@ static g4_status decoder_feedforward(bool tiled, g4_ctx* ctx, uint16_t* residual
                                  const uint8_t* gate_weight_scale, const uint8_t* down_weight_scale,
                                  const float* up_global_scale, const float* gate_global_scale,
                                  const float* down_global_scale, const uint16_t* post_ff_rms_weight,
-                                 const uint16_t* layer_scalar, void* stream) {
+                                 const uint16_t* layer_scalar, void* stream, int32_t m = 1) {
   if (!ctx) return G4_ERR_INVALID_ARGUMENT;
+  if (m < 1 || m > g4::kBatchMax) return fail(ctx, G4_ERR_INVALID_ARGUMENT, "%s", "m must be in [1, 64]");
+  if (m > 1 && (ctx->tp_world != 1 || !ctx->batch_ok))
+    return fail(ctx, G4_ERR_UNSUPPORTED, "%s", "a batch of tokens runs on a one-GPU context only");
   g4_status st = check_ptrs(ctx, {{residual_hbm, "residual_hbm"},
                                   {pre_ff_rms_weight, "pre_ff_rms_weight"},
                                   {up_weight_packed, "up_weight_packed"},
@@ -263,6 +276,8 @@ static g4_status decoder_feedforward(bool tiled, g4_ctx* ctx, uint16_t* residual
   g4::FfnArgs a{residual_hbm,      pre_ff_rms_weight, up_weight_packed, gate_weight_packed, down_weight_packed,
                 up_weight_scale,   gate_weight_scale, down_weight_scale, up_global_scale,   gate_global_scale,
                 down_global_scale, post_ff_rms_weight, layer_scalar, tiled};
+  if (m > 1)
+    return cuda_status(ctx, g4::launch_ffn_nvfp4_batch(a, m, env_of(ctx, stream)), "decoder_feedforward_batch launch");
   return cuda_status(ctx, g4::launch_ffn_nvfp4(a, env_of(ctx, stream)), "decoder_feedforward launch");
 }
 
@@ -329,6 +344,31 @@ g4_status g4_decoder_feedforward_tiled(g4_ctx* ctx, uint16_t* residual_hbm, cons
                              down_weight_tiled, up_gate_scale_tiled, up_gate_scale_tiled, down_scale_tiled,
                              up_global_scale, gate_global_scale, down_global_scale, post_ff_rms_weight, layer_scalar,
                              stream);
+}
+
+g4_status g4_decoder_feedforward_batch(g4_ctx* ctx, uint16_t* residual_hbm, const uint16_t* pre_ff_rms_weight,
+                                       const uint8_t* up_weight_packed, const uint8_t* gate_weight_packed,
+                                       const uint8_t* down_weight_packed, const uint8_t* up_weight_scale,
+                                       const uint8_t* gate_weight_scale, const uint8_t* down_weight_scale,
+                                       const float* up_global_scale, const float* gate_global_scale,
+                                       const float* down_global_scale, const uint16_t* post_ff_rms_weight,
+                                       const uint16_t* layer_scalar, int32_t m, void* stream) {
+  return decoder_feedforward(false, ctx, residual_hbm, pre_ff_rms_weight, up_weight_packed, gate_weight_packed,
+                             down_weight_packed, up_weight_scale, gate_weight_scale, down_weight_scale,
+                             up_global_scale, gate_global_scale, down_global_scale, post_ff_rms_weight, layer_scalar,
+                             stream, m);
+}
+
+g4_status g4_decoder_feedforward_batch_tiled(g4_ctx* ctx, uint16_t* residual_hbm, const uint16_t* pre_ff_rms_weight,
+                                             const uint8_t* up_gate_weight_tiled, const uint8_t* down_weight_tiled,
+                                             const uint8_t* up_gate_scale_tiled, const uint8_t* down_scale_tiled,
+                                             const float* up_global_scale, const float* gate_global_scale,
+                                             const float* down_global_scale, const uint16_t* post_ff_rms_weight,
+                                             const uint16_t* layer_scalar, int32_t m, void* stream) {
+  return decoder_feedforward(true, ctx, residual_hbm, pre_ff_rms_weight, up_gate_weight_tiled, up_gate_weight_tiled,
+                             down_weight_tiled, up_gate_scale_tiled, up_gate_scale_tiled, down_scale_tiled,
+                             up_global_scale, gate_global_scale, down_global_scale, post_ff_rms_weight, layer_scalar,
+                             stream, m);
 }
 
 g4_status g4_embed_token(g4_ctx* ctx, const uint16_t* embedding_table, const int32_t* offset, uint16_t* out,

@@ -1,0 +1,770 @@
+// The NVFP4 GeGLU feed-forward for a batch of M = 2..64 tokens on sm_100a: the reference op
+// (furiosa-opt-gemma4-12B/src/ops.rs:201-239, oracle generate_references.py:358-413) applied to
+// each of M residual rows, with the weights streamed from HBM once for all M tokens.
+//
+//   ffn_batch_norm_kernel    h[m] = bf16(RMSNorm(residual[m]) * gamma_pre)           (M CTAs)
+//   ffn_batch_upgate_kernel  act[m] = bf16(bf16(gelu_tanh(gate[m])) * up[m])          (one CTA per SM)
+//   ffn_batch_down_kernel    residual[m] = bf16(bf16(residual[m] + RMSNorm_post(down[m])) * lambda)
+//
+// Contraction: tcgen05.mma kind::f16 with bf16 operands, M = 128 weight rows, N = MPAD (the
+// tokens, zero-padded to a multiple of 16), K = 16 per instruction. The weights arrive in the
+// M = 1 kernels' layouts (packed e2m1 codes and ue4m3 block scales, row-major or unit-tiled);
+// eight dequantisation warps expand each 256-element unit into bf16 rows in shared memory. A
+// code times its block scale has at most 6 significant bits and lies in [2^-10, 2688] (or is 0),
+// so it is exact in f16 (where the product is formed) and in bf16, every product with a bf16
+// activation is exact, and the tensor cores sum them in f32 as the reference's f32 contraction
+// of dequantised weights does. The activation rows (h, then act) reach shared memory by TMA per
+// unit (128-byte swizzle; rows past M read as zeros), from L2 where the preceding kernel left them.
+//
+// Work split and determinism as in the M = 1 engine (g4_gemv.cuh): contiguous runs of (tile,
+// K unit) per CTA; a tile whose units span several CTAs is finished by the CTA holding its first
+// unit, which adds the others' epoch-tagged partial rows in CTA order. A CTA publishes at most one
+// partial piece (the first of its run), so the split-K words are indexed by CTA.
+#include <type_traits>
+
+#include "g4_gemv.cuh"
+#include "g4_ops.cuh"
+
+namespace g4 {
+namespace {
+
+static_assert(kBatchEpoch < kCounterCount, "batch epoch counter inside the counter block");
+
+constexpr int kBThreads = 480;  // 15 warps
+constexpr int kWProducer = 0, kWIssuer = 1, kWRelay = 2, kWDq0 = 7, kDqWarps = 8;  // epilogue: warps 3-6
+constexpr int kBIssueBarrier = 2;  // issuer + relay (64 threads)
+constexpr int kBEpiBarrier = 1;    // the four epilogue warps
+constexpr int kBMaxStages = 6;
+constexpr int kBMaxFin = 2;        // tiles one down CTA may finish (checked at set-up)
+
+struct BatchCtl {
+  uint64_t full_a[kBMaxStages], full_b[kBMaxStages], empty[kBMaxStages];
+  uint64_t hfull[2], hempty[2], done[4], tempty[4], drain;
+  uint32_t tmem_base;
+  uint32_t abort;
+  int fin_tile[kBMaxFin];
+  int fin_n;
+  float inv[kBatchMax];
+  double wsum[4][kBatchMax];  // down: each epilogue warp's sums of squares per token
+};
+
+// Profiling builds: per-unit timestamps of CTA 0 at trace[3000 + 64 k + i] (k: 0 producer issued,
+// 1 dequantised, 2 released to the issuer, 3 epilogue done).
+#ifdef G4_TRACE
+#define G4_UNIT_STAMP(sc, k, i)                                                                           \
+  do {                                                                                                \
+    if ((sc).trace && blockIdx.x == 0 && (i) < 64) (sc).trace[3000 + 64 * (k) + (i)] = globaltimer_ns(); \
+  } while (0)
+#else
+#define G4_UNIT_STAMP(sc, k, i) \
+  do {                          \
+  } while (0)
+#endif
+
+template <int MPAD>
+struct BatchShape {
+  static constexpr int kMpad = MPAD;  // B rows: the tokens, zero-padded
+  static constexpr int kStages = MPAD <= 16 ? 6 : (MPAD <= 32 ? 4 : 3);
+  static constexpr int kABytes = kTileRows * 128;     // packed e2m1 codes: 128 rows x 256 K
+  static constexpr int kScaleBytes = kTileRows * 16;  // ue4m3 block scales
+  static constexpr int kBColBytes = MPAD * 128;       // B: one 64-element K column block of MPAD rows
+  static constexpr int kBBytes = 4 * kBColBytes;
+  static constexpr int kStageBytes = kABytes + kScaleBytes + kBBytes;
+  static constexpr int kHalfBytes = 2 * kTileRows * 128;  // dequantised A: 128 rows x 128 K bf16
+  static constexpr int kTSlots = 4;                       // TMEM accumulators of MPAD columns, one per unit
+  static constexpr uint32_t kTmemCols = 4 * MPAD <= 64 ? 64u : (4 * MPAD <= 128 ? 128u : 256u);
+  static constexpr uint32_t kIdesc = umma_idesc_bf16(kTileRows, MPAD);
+  static constexpr size_t kOffHalf = size_t(kStages) * kStageBytes;
+  static constexpr size_t kOffX = kOffHalf + 2 * size_t(kHalfBytes);
+  static constexpr size_t kXBytes = size_t(64) * MPAD * 2;  // up/gate: bf16(gelu(gate)) [token][64]
+  static constexpr size_t kOffCtl = kOffX + kXBytes;
+  static constexpr size_t kSmemBytes = kOffCtl + sizeof(BatchCtl) + 1024;
+  static_assert(MPAD % 16 == 0 && MPAD <= kBatchMax, "N of the MMA");
+  static_assert(kStages <= kBMaxStages, "barrier arrays");
+  static_assert(kStageBytes % 1024 == 0 && (kABytes + kScaleBytes) % 1024 == 0, "1024-byte swizzle atoms");
+  static_assert(kSmemBytes <= 227 * 1024, "shared memory budget");
+};
+
+__device__ __forceinline__ uint64_t l2_evict_last_policy() {
+  uint64_t p;
+  asm volatile("createpolicy.fractional.L2::evict_last.b64 %0, 1.0;" : "=l"(p));
+  return p;
+}
+
+// Eight packed e2m1 codes (element 2i in the low nibble of byte i) times their ue4m3 block scale,
+// as eight bf16 (element j in half j % 2 of word j / 2). Exact: see the file comment.
+__device__ __forceinline__ uint4 dequant8_bf16(uint32_t codes, uint32_t scale_byte) {
+  uint32_t s2, h[4];
+  asm("{\n .reg .b16 t;\n cvt.u16.u32 t, %1;\n cvt.rn.f16x2.e4m3x2 %0, t;\n}" : "=r"(s2) : "r"(scale_byte * 0x101u));
+  asm("{\n .reg .b8 b0, b1, b2, b3;\n mov.b32 {b0, b1, b2, b3}, %4;\n"
+      " cvt.rn.f16x2.e2m1x2 %0, b0;\n cvt.rn.f16x2.e2m1x2 %1, b1;\n"
+      " cvt.rn.f16x2.e2m1x2 %2, b2;\n cvt.rn.f16x2.e2m1x2 %3, b3;\n}"
+      : "=r"(h[0]), "=r"(h[1]), "=r"(h[2]), "=r"(h[3])
+      : "r"(codes));
+  const __half2 sc = *reinterpret_cast<const __half2*>(&s2);
+  uint32_t o[4];
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    const __half2 p = __hmul2(*reinterpret_cast<const __half2*>(&h[i]), sc);
+    const float2 f = __half22float2(p);
+    const __nv_bfloat162 b = __floats2bfloat162_rn(f.x, f.y);
+    o[i] = *reinterpret_cast<const uint32_t*>(&b);
+  }
+  return make_uint4(o[0], o[1], o[2], o[3]);
+}
+
+__device__ __forceinline__ void st_release_gpu_u64(unsigned long long* p, unsigned long long v) {
+  asm volatile("st.release.gpu.global.u64 [%0], %1;" ::"l"(p), "l"(v) : "memory");
+}
+__device__ __forceinline__ unsigned long long ld_acquire_gpu_u64(const unsigned long long* p) {
+  unsigned long long v;
+  asm volatile("ld.acquire.gpu.global.u64 %0, [%1];" : "=l"(v) : "l"(p) : "memory");
+  return v;
+}
+
+// The tile piece of the CTA holding the tile's first unit gets the other pieces (later CTAs of the
+// tile) added in CTA order; every other piece is published as epoch-tagged words, one per (token,
+// row), in its CTA's slot. The publishing thread of a row stores its last token's word with
+// release semantics after the others, so a reader that acquires that word with this call's tag
+// sees the whole row: the finisher polls one word per piece (all pieces in flight at once), then
+// reads the rest with independent loads. `ok` false: nothing is read (the values become NaN).
+// Epilogue threads.
+template <int MPAD>
+__device__ void split_finish(float (&acc)[MPAD], int M, int tile, int upt, int64_t total, int row, uint32_t tag,
+                             unsigned long long* words, bool& ok, uint32_t* err, bool& publish_only) {
+  const int64_t first_unit = int64_t(tile) * upt, grid = gridDim.x;
+  const int first = cta_of_unit(first_unit, grid, total);
+  const unsigned long long tag_bits = static_cast<unsigned long long>(tag) << 32;
+  publish_only = first != int(blockIdx.x);
+  if (publish_only) {
+    unsigned long long* w = words + size_t(blockIdx.x) * kBatchMax * kTileRows + row;
+#pragma unroll
+    for (int m = 0; m < MPAD; ++m)
+      if (m < M - 1) st_relaxed_gpu_u64(w + m * kTileRows, tag_bits | __float_as_uint(acc[m]));
+#pragma unroll
+    for (int m = 0; m < MPAD; ++m)
+      if (m == M - 1) st_release_gpu_u64(w + m * kTileRows, tag_bits | __float_as_uint(acc[m]));
+    return;
+  }
+  const int later = cta_of_unit(first_unit + upt - 1, grid, total) - first;  // pieces after this CTA's
+  if (later > kMaxCtasPerGroup) {  // launchers keep every tile within the slots
+    atomicOr(err, kErrInternal);
+    ok = false;
+  }
+  auto slot = [&](int k) { return words + size_t(first + 1 + k) * kBatchMax * kTileRows + row; };
+  constexpr int kPoll = 8;  // pieces whose last word is polled together
+  const uint64_t t0 = globaltimer_ns();
+  for (int g0 = 0; g0 < later && ok; g0 += kPoll) {
+    uint32_t pending = 0u;
+#pragma unroll
+    for (int k = 0; k < kPoll; ++k)
+      if (g0 + k < later) pending |= 1u << k;
+    while (pending) {
+      unsigned long long x[kPoll];  // every pending piece's last word in flight at once
+#pragma unroll
+      for (int k = 0; k < kPoll; ++k)
+        if (pending & (1u << k)) x[k] = ld_acquire_gpu_u64(slot(g0 + k) + size_t(M - 1) * kTileRows);
+#pragma unroll
+      for (int k = 0; k < kPoll; ++k)
+        if ((pending & (1u << k)) && uint32_t(x[k] >> 32) == tag) pending &= ~(1u << k);
+      if (pending && globaltimer_ns() - t0 > kWaitLimitNs) {
+        atomicOr(err, kErrWaitTimeout);
+        ok = false;
+        break;
+      }
+    }
+  }
+  for (int k = 0; k < later; ++k) {
+    const unsigned long long* w = slot(k);
+#pragma unroll
+    for (int c = 0; c < MPAD; c += 16) {  // 16 independent loads in flight, then their sums
+      float v[16];
+#pragma unroll
+      for (int j = 0; j < 16; ++j)
+        if (c + j < M) {
+          const unsigned long long x = ok ? __ldcg(w + (c + j) * kTileRows) : 0ull;
+          v[j] = uint32_t(x >> 32) == tag ? __uint_as_float(uint32_t(x)) : __uint_as_float(0x7fc00000u);
+        }
+#pragma unroll
+      for (int j = 0; j < 16; ++j)
+        if (c + j < M) acc[c + j] += v[j];
+    }
+  }
+}
+
+// Engine driver. `op` supplies:
+//   static int kUnitsPerTile, kTiles                 the unit grid
+//   void load_a(uint8_t* stage, int tile, int kc, uint64_t* bar, uint64_t policy) const
+//                                                    codes (kABytes) then scales (kScaleBytes)
+//   void load_b(uint8_t* dst, int kc, uint64_t* bar, uint64_t policy) const    4 column blocks
+//   void prefetch_l2(int u0, int u1) const
+//   void prologue()                                  after the dependency wait (all threads)
+//   void finish(BatchCtl&, uint8_t* xbuf, int tile, int row, float (&acc)[MPAD], int in_piece, bool ok)
+//                                                    the 128 epilogue threads, per tile piece
+template <class Shape, class Op>
+__device__ void batch_run(Op& op, uint8_t* smem_raw, const Scratch& sc) {
+  constexpr int S = Shape::kStages, MP = Shape::kMpad;
+  constexpr int UPT = Op::kUnitsPerTile;
+  uint8_t* smem = align1024(smem_raw);
+  BatchCtl& ctl = *reinterpret_cast<BatchCtl*>(smem + Shape::kOffCtl);
+  uint8_t* halves = smem + Shape::kOffHalf;
+  auto stage = [&](int s) { return smem + size_t(s) * Shape::kStageBytes; };
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  const int64_t total = int64_t(UPT) * Op::kTiles, grid = gridDim.x;
+  const int u0 = int(int64_t(blockIdx.x) * total / grid);
+  const int n = int(int64_t(blockIdx.x + 1) * total / grid) - u0;
+  volatile uint32_t* abort = &ctl.abort;
+  constexpr uint32_t kATx = Shape::kABytes + Shape::kScaleBytes;
+
+  G4_STAMP(sc, 0);
+  if (tid == 0) {
+    for (int i = 0; i < S; ++i) {
+      mbar_init(&ctl.full_a[i], 1);
+      mbar_init(&ctl.full_b[i], 1);
+      mbar_init(&ctl.empty[i], 1);
+    }
+    for (int i = 0; i < 2; ++i) {
+      mbar_init(&ctl.hfull[i], kDqWarps);  // every dequantisation warp wrote its rows
+      mbar_init(&ctl.hempty[i], 1);        // the half's MMAs completed
+    }
+    for (int i = 0; i < 4; ++i) {
+      mbar_init(&ctl.done[i], 1);    // the unit's MMAs completed
+      mbar_init(&ctl.tempty[i], 4);  // the epilogue warps read the unit's accumulator
+    }
+    mbar_init(&ctl.drain, 1);
+    ctl.abort = 0;
+    ctl.fin_n = 0;
+    fence_mbar_init();
+  }
+  __syncwarp();
+  if (warp == kWIssuer) tmem_alloc(&ctl.tmem_base, Shape::kTmemCols);
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tbase = ctl.tmem_base;
+  const uint64_t policy = l2_evict_first_policy();
+  const uint64_t policy_b = l2_evict_last_policy();  // every CTA reads the activation rows
+  const int prefetch = n < S ? n : S;
+
+  // the first units' weights before the wait on the preceding kernel (thread i: unit i), their
+  // activation rows after it
+  if (tid < prefetch) {
+    const int u = u0 + tid;
+    mbar_arrive_expect_tx(&ctl.full_a[tid], kATx);
+    op.load_a(stage(tid), u / UPT, u % UPT, &ctl.full_a[tid], policy);
+  }
+  __syncwarp();
+  pdl_wait_primary();
+  pdl_launch_dependents();
+  G4_STAMP(sc, 1);
+  op.prologue();
+  if (tid < prefetch) {
+    mbar_arrive_expect_tx(&ctl.full_b[tid], Shape::kBBytes);
+    op.load_b(stage(tid) + kATx, (u0 + tid) % UPT, &ctl.full_b[tid], policy_b);
+  }
+  if (tid == kBThreads - 1) op.prefetch_l2(u0 + prefetch, u0 + (prefetch + 6 < n ? prefetch + 6 : n));
+  __syncwarp();
+
+  if (warp == kWProducer) {
+    // ---------------------------------------------------------------- producer
+    if (lane == 0) {
+      int issued = prefetch;
+      for (int i = prefetch; i < n; ++i) {
+        const int s = i % S, r = i - S;
+        if (!mbar_wait_or_abort(&ctl.empty[s], uint32_t((r / S) & 1), abort, sc.err)) break;
+        const int u = u0 + i;
+        mbar_arrive_expect_tx(&ctl.full_a[s], kATx);
+        op.load_a(stage(s), u / UPT, u % UPT, &ctl.full_a[s], policy);
+        mbar_arrive_expect_tx(&ctl.full_b[s], Shape::kBBytes);
+        op.load_b(stage(s) + kATx, u % UPT, &ctl.full_b[s], policy_b);
+        G4_UNIT_STAMP(sc, 0, i);
+        if ((i - prefetch) % 2 == 0 && i + 6 < n) op.prefetch_l2(u + 6, u0 + (i + 8 < n ? i + 8 : n));
+        issued = i + 1;
+      }
+      // every requested copy has landed before the CTA may exit
+      for (int i = issued - S > 0 ? issued - S : 0; i < issued; ++i) {
+        const uint64_t t0 = globaltimer_ns();
+        while (!(mbar_try_wait(&ctl.full_a[i % S], uint32_t((i / S) & 1)) &&
+                 mbar_try_wait(&ctl.full_b[i % S], uint32_t((i / S) & 1))))
+          if (globaltimer_ns() - t0 > kWaitLimitNs) break;
+      }
+    }
+    __syncwarp();
+  } else if (warp >= kWDq0) {
+    // ---------------------------------------------------------------- dequantisation
+    // thread (sub, r): row r, K elements [64 sub, 64 sub + 64) of each half (one column block of
+    // the half's bf16 rows: two 16-byte chunks of codes, four block scales)
+    const int dq = tid - kWDq0 * 32, r = dq & 127, sub = dq >> 7;
+    bool ok = true;
+    for (int i = 0; i < n; ++i) {
+      const int s = i % S;
+      if (ok) ok = mbar_wait_or_abort(&ctl.full_a[s], uint32_t((i / S) & 1), abort, sc.err);
+      const uint8_t* a4 = stage(s);
+      for (int h = 0; h < 2; ++h) {
+        if (ok && i > 0) ok = mbar_wait_or_abort(&ctl.hempty[h], uint32_t((i - 1) & 1), abort, sc.err);
+        if (ok) {
+          const int c0 = 4 * h + 2 * sub;  // code chunks c0, c0 + 1 (32 elements each)
+          const uint4 q0 = *reinterpret_cast<const uint4*>(a4 + r * 128 + (((c0) ^ (r & 7)) << 4));
+          const uint4 q1 = *reinterpret_cast<const uint4*>(a4 + r * 128 + (((c0 + 1) ^ (r & 7)) << 4));
+          const uint32_t sw = *reinterpret_cast<const uint32_t*>(a4 + Shape::kABytes + r * 16 + 8 * h + 4 * sub);
+          if (sw & 0x80808080u) atomicOr(sc.err, kErrNegativeScale);
+          uint8_t* dst = halves + h * Shape::kHalfBytes + sub * (Shape::kHalfBytes / 2) + r * 128;
+          const uint32_t w[8] = {q0.x, q0.y, q0.z, q0.w, q1.x, q1.y, q1.z, q1.w};
+#pragma unroll
+          for (int j = 0; j < 8; ++j)  // elements 8j .. 8j + 7 of the column block: block j / 2
+            *reinterpret_cast<uint4*>(dst + ((j ^ (r & 7)) << 4)) = dequant8_bf16(w[j], (sw >> (8 * (j / 2))) & 0xffu);
+          asm volatile("fence.proxy.async.shared::cta;" ::: "memory");  // the tensor cores read them
+        }
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&ctl.hfull[h]);
+        if (h == 1 && warp == kWDq0 && lane == 0) G4_UNIT_STAMP(sc, 1, i);
+      }
+    }
+  } else if (warp == kWRelay) {
+    // ---------------------------------------------------------------- relay
+    // Each half of unit i may be issued once its bf16 rows are written (and, the first half,
+    // once the unit's activation rows landed and its TMEM accumulator is free).
+    bool stop = false;
+    for (int i = 0; i < n && !stop; ++i) {
+      const int s = i % S, t = i % Shape::kTSlots;
+      for (int h = 0; h < 2; ++h) {
+        bool bad = false;
+        if (lane == 0) {
+          bad = !mbar_wait_or_abort(&ctl.hfull[h], uint32_t(i & 1), abort, sc.err);
+          if (!bad && h == 0) bad = !mbar_wait_or_abort(&ctl.full_b[s], uint32_t((i / S) & 1), abort, sc.err);
+          if (!bad && h == 0 && i >= Shape::kTSlots)
+            bad = !mbar_wait_or_abort(&ctl.tempty[t], uint32_t(((i / Shape::kTSlots) - 1) & 1), abort, sc.err);
+        }
+        __syncwarp();
+        if (named_bar_or(kBIssueBarrier, 64, bad)) {
+          stop = true;
+          break;
+        }
+        if (h == 0 && lane == 0) G4_UNIT_STAMP(sc, 2, i);
+      }
+    }
+  } else if (warp == kWIssuer) {
+    // ---------------------------------------------------------------- MMA issuer
+    // Every unit has its own accumulator (16 MMAs, K = 256): the tensor cores' f32 sums stay
+    // short and the epilogue adds the units with round-to-nearest, in unit order.
+    bool stop = false;
+    for (int i = 0; i < n && !stop; ++i) {
+      const int s = i % S, t = i % Shape::kTSlots;
+      for (int h = 0; h < 2; ++h) {
+        if (named_bar_or(kBIssueBarrier, 64, false)) {
+          stop = true;
+          break;
+        }
+        tc_fence_after();
+        if (lane == 0) {
+          const uint32_t d = tbase + uint32_t(t) * MP;
+          const uint32_t a0 = smem_u32(halves + h * Shape::kHalfBytes);
+          const uint32_t b0 = smem_u32(stage(s) + kATx) + uint32_t(2 * h) * Shape::kBColBytes;
+#pragma unroll
+          for (int j = 0; j < 8; ++j) {  // K = 16 each: column block j / 4, 32 bytes per step inside it
+            const uint32_t cb = j / 4, kk = j % 4;
+            umma_bf16(d, umma_desc_sw128(a0 + cb * uint32_t(Shape::kHalfBytes / 2) + kk * 32u),
+                      umma_desc_sw128(b0 + cb * uint32_t(Shape::kBColBytes) + kk * 32u), Shape::kIdesc,
+                      uint32_t(!(h == 0 && j == 0)));
+          }
+          umma_commit(&ctl.hempty[h]);
+          if (h == 1) {
+            umma_commit(&ctl.empty[s]);
+            umma_commit(&ctl.done[t]);
+          }
+        }
+        __syncwarp();
+      }
+    }
+    if (lane == 0) {  // nothing of ours may still be running when TMEM is released
+      umma_commit(&ctl.drain);
+      const uint64_t t0 = globaltimer_ns();
+      while (!mbar_try_wait(&ctl.drain, 0))
+        if (globaltimer_ns() - t0 > kWaitLimitNs) break;
+    }
+    __syncwarp();
+  } else {
+    // ---------------------------------------------------------------- epilogue (warps 3-6)
+    const int quarter = warp & 3;
+    const int row = quarter * 32 + lane;
+    const uint32_t lane_addr = uint32_t(quarter * 32) << 16;
+    uint8_t* xbuf = smem + Shape::kOffX;
+    bool ok = true;
+    int in_piece = 0;
+    float acc[MP];
+#pragma unroll
+    for (int j = 0; j < MP; ++j) acc[j] = 0.f;
+    for (int i = 0; i < n; ++i) {
+      const int u = u0 + i, tile = u / UPT, kc = u % UPT, t = i % Shape::kTSlots;
+      ++in_piece;
+      if (ok) ok = mbar_wait_or_abort(&ctl.done[t], uint32_t((i / Shape::kTSlots) & 1), abort, sc.err);
+      tc_fence_after();
+#pragma unroll
+      for (int c = 0; c < MP / 16; ++c) {
+        float part[16];
+        if (ok) tmem_ld16(tbase + lane_addr + uint32_t(t * MP + 16 * c), part);
+        if (ok) tmem_ld_wait();
+#pragma unroll
+        for (int j = 0; j < 16; ++j) acc[16 * c + j] = ok ? acc[16 * c + j] + part[j] : __uint_as_float(0x7fc00000u);
+      }
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&ctl.tempty[t]);
+      if (row == 0) G4_UNIT_STAMP(sc, 3, i);
+      if (!(kc == UPT - 1 || i == n - 1)) continue;
+      op.finish(ctl, xbuf, tile, row, acc, in_piece, ok);
+      if (row == 0) G4_STAMP_T(sc, 5);
+      in_piece = 0;
+#pragma unroll
+      for (int j = 0; j < MP; ++j) acc[j] = 0.f;
+    }
+  }
+
+  // teardown: every MMA has completed (drain) and every TMEM load has been waited for
+  tc_fence_before();
+  __syncthreads();
+  G4_STAMP(sc, 6);
+  if (warp == kWIssuer) {
+    tc_fence_after();
+    tmem_dealloc(tbase, Shape::kTmemCols);
+  }
+}
+
+// ---------------------------------------------------------------------------------------
+// The ops
+
+// h[m] = bf16(RMSNorm(residual[m]) * gamma_pre): one CTA per token, 240 threads x 16 elements.
+// Thread 0 of CTA 0 also counts the call (the epoch of its split-K words and tile sums).
+__global__ void __launch_bounds__(256) ffn_batch_norm_kernel(FfnArgs a, Scratch sc) {
+  __shared__ double red[8];
+  const int m = blockIdx.x, g = threadIdx.x;
+  const bool have = g < kH / 16;
+  uint4 raw[4];
+  if (have) load_group_gamma(a.pre_rms, g, raw);
+  pdl_wait_primary();
+  pdl_launch_dependents();
+  if (m == 0 && g == 0) sc.counters[kBatchEpoch] = __ldcg(sc.counters + kBatchEpoch) + 1u;
+  if (have) load_group_cg(a.residual + size_t(m) * kH, g, raw);
+  const double ss = have ? sum_squares_bf16x16(raw[0], raw[1]) : 0.0;
+  const float inv = rms_inverse(block_sum_d(ss, red), kH);
+  if (have) {
+    float v[16];
+    rms_apply16(raw, inv, v);
+    uint32_t w[8];
+#pragma unroll
+    for (int j = 0; j < 8; ++j) w[j] = (__float_as_uint(v[2 * j]) >> 16) | (__float_as_uint(v[2 * j + 1]) & 0xffff0000u);
+    uint4* dst = reinterpret_cast<uint4*>(sc.batch_h + size_t(m) * kH + 16 * g);
+    dst[0] = make_uint4(w[0], w[1], w[2], w[3]);
+    dst[1] = make_uint4(w[4], w[5], w[6], w[7]);
+  }
+}
+
+struct BatchMaps {
+  CUtensorMap a, a2, s, s2;  // weights: up (or down) codes, gate codes, their block scales
+  CUtensorMap b;             // activation rows [M, K] bf16, box {64, MPAD}
+};
+
+template <int MPAD>
+struct BatchUpGateOp {
+  using Shape = BatchShape<MPAD>;
+  static constexpr int kUnitsPerTile = kH / kUnitK;  // 15
+  static constexpr int kTiles = kL / 64;             // 64 up + 64 gate rows per tile
+  const BatchMaps* maps;
+  FfnArgs a;
+  Scratch sc;
+  int M;
+  float g_up = 0.f, g_gate = 0.f;
+  uint32_t tag = 0;
+
+  __device__ void load_a(uint8_t* stage, int tile, int kc, uint64_t* bar, uint64_t policy) const {
+    uint8_t* scl = stage + Shape::kABytes;
+    if (a.tiled) {
+      tma_load_2d(stage, &maps->a, 0, (tile * kUnitsPerTile + kc) * kTileRows, bar, policy);
+      bulk_g2s(scl, a.up_scale + size_t(tile * kUnitsPerTile + kc) * Shape::kScaleBytes, Shape::kScaleBytes, bar,
+               policy);
+    } else {
+      tma_load_2d(stage, &maps->a, kc * 128, tile * 64, bar, policy);
+      tma_load_2d(stage + 8192, &maps->a2, kc * 128, tile * 64, bar, policy);
+      tma_load_2d(scl, &maps->s, kc * 16, tile * 64, bar, policy);
+      tma_load_2d(scl + 1024, &maps->s2, kc * 16, tile * 64, bar, policy);
+    }
+  }
+  __device__ void load_b(uint8_t* dst, int kc, uint64_t* bar, uint64_t policy) const {
+#pragma unroll
+    for (int q = 0; q < 4; ++q) tma_load_2d(dst + q * Shape::kBColBytes, &maps->b, kc * kUnitK + 64 * q, 0, bar, policy);
+  }
+  __device__ void prefetch_l2(int u0, int u1) const {
+    if (!a.tiled) return;
+    prefetch_units(a.up_packed, u0, u1, Shape::kABytes);
+    prefetch_units(a.up_scale, u0, u1, Shape::kScaleBytes);
+  }
+  __device__ void prologue() {
+    g_up = *a.up_global;
+    g_gate = *a.gate_global;
+    tag = (__ldcg(sc.counters + kBatchEpoch) << 1) | 0u;
+  }
+  // GloballyScaled(nn.Linear): bf16(bf16(h @ W.T) * g) (generate_references.py:358-372), then the
+  // down input bf16(bf16(gelu_tanh(gate)) * up) (gemma4.py:197), token by token.
+  __device__ void finish(BatchCtl&, uint8_t* xbuf, int tile, int row, float (&acc)[MPAD], int, bool ok) {
+    bool publish_only = false;
+    split_finish<MPAD>(acc, M, tile, kUnitsPerTile, int64_t(kUnitsPerTile) * kTiles, row, tag, sc.batch_words, ok,
+                       sc.err, publish_only);
+    if (publish_only) return;  // CTA-uniform for the tile: no barrier is skipped by part of the warps
+    uint16_t* gel = reinterpret_cast<uint16_t*>(xbuf);  // [token][64]
+    if (row >= 64) {
+#pragma unroll
+      for (int m = 0; m < MPAD; ++m)
+        if (m < M) gel[m * 64 + row - 64] = f32_to_bf16(gelu_tanh(bf16_round(bf16_round(acc[m]) * g_gate)));
+    }
+    named_bar(kBEpiBarrier, 128);
+    if (row < 64) {
+#pragma unroll
+      for (int m = 0; m < MPAD; ++m)
+        if (m < M) {
+          const float up = bf16_round(bf16_round(acc[m]) * g_up);
+          sc.act[size_t(m) * kL + tile * 64 + row] = f32_to_bf16(bf16_to_f32(gel[m * 64 + row]) * up);
+        }
+    }
+    named_bar(kBEpiBarrier, 128);  // the exchange buffer is free for the next tile
+  }
+};
+
+template <int MPAD>
+struct BatchDownOp {
+  using Shape = BatchShape<MPAD>;
+  static constexpr int kUnitsPerTile = kL / kUnitK;  // 60
+  static constexpr int kTiles = kH / kTileRows;      // 30
+  const BatchMaps* maps;
+  FfnArgs a;
+  Scratch sc;
+  int M;
+  float g_down = 0.f;
+  uint32_t epoch = 0, tag = 0;
+
+  __device__ void load_a(uint8_t* stage, int tile, int kc, uint64_t* bar, uint64_t policy) const {
+    uint8_t* scl = stage + Shape::kABytes;
+    if (a.tiled) {
+      tma_load_2d(stage, &maps->a, 0, (tile * kUnitsPerTile + kc) * kTileRows, bar, policy);
+      bulk_g2s(scl, a.down_scale + size_t(tile * kUnitsPerTile + kc) * Shape::kScaleBytes, Shape::kScaleBytes, bar,
+               policy);
+    } else {
+      tma_load_2d(stage, &maps->a, kc * 128, tile * kTileRows, bar, policy);
+      tma_load_2d(scl, &maps->s, kc * 16, tile * kTileRows, bar, policy);
+    }
+  }
+  __device__ void load_b(uint8_t* dst, int kc, uint64_t* bar, uint64_t policy) const {
+#pragma unroll
+    for (int q = 0; q < 4; ++q) tma_load_2d(dst + q * Shape::kBColBytes, &maps->b, kc * kUnitK + 64 * q, 0, bar, policy);
+  }
+  __device__ void prefetch_l2(int u0, int u1) const {
+    if (!a.tiled) return;
+    prefetch_units(a.down_packed, u0, u1, Shape::kABytes);
+    prefetch_units(a.down_scale, u0, u1, Shape::kScaleBytes);
+  }
+  __device__ void prologue() {
+    g_down = *a.down_global;
+    epoch = __ldcg(sc.counters + kBatchEpoch);
+    tag = (epoch << 1) | 1u;
+  }
+  // y[m] = bf16(bf16(h @ W.T) * g) for the tile's rows; kept (bf16) in batch_y for the residual
+  // tail, with each token's sum of squares over the tile published as two epoch-tagged words.
+  __device__ void finish(BatchCtl& ctl, uint8_t*, int tile, int row, float (&acc)[MPAD], int, bool ok) {
+    bool publish_only = false;
+    split_finish<MPAD>(acc, M, tile, kUnitsPerTile, int64_t(kUnitsPerTile) * kTiles, row, tag, sc.batch_words, ok,
+                       sc.err, publish_only);
+    if (publish_only) return;
+    const int lane = threadIdx.x & 31, quarter = (threadIdx.x >> 5) & 3;
+#pragma unroll
+    for (int m = 0; m < MPAD; ++m) {
+      if (m >= M) continue;
+      const float y = bf16_round(bf16_round(acc[m]) * g_down);
+      sc.batch_y[size_t(m) * kH + tile * kTileRows + row] = f32_to_bf16(y);
+      const double s = warp_sum_d(double(y) * double(y));
+      if (lane == 0) ctl.wsum[quarter][m] = s;
+    }
+    named_bar(kBEpiBarrier, 128);
+    if (row < M) {  // quarters in row order: warp 3 holds rows 96-127
+      const double sum = ((ctl.wsum[0][row] + ctl.wsum[1][row]) + ctl.wsum[2][row]) + ctl.wsum[3][row];
+      const unsigned long long bits = static_cast<unsigned long long>(__double_as_longlong(sum));
+      const unsigned long long t = static_cast<unsigned long long>(epoch) << 32;
+      unsigned long long* w = sc.batch_ss + (size_t(tile) * kBatchMax + row) * 2;
+      st_relaxed_gpu_u64(w, t | (bits & 0xffffffffull));
+      st_relaxed_gpu_u64(w + 1, t | (bits >> 32));
+    }
+    if (row == 0) {
+      if (ctl.fin_n < kBMaxFin) ctl.fin_tile[ctl.fin_n] = tile;
+      else atomicOr(sc.err, kErrInternal);
+      ctl.fin_n = ctl.fin_n + 1;
+    }
+    named_bar(kBEpiBarrier, 128);
+  }
+};
+
+template <int MPAD>
+__global__ void __launch_bounds__(kBThreads, 1) ffn_batch_upgate_kernel(const __grid_constant__ BatchMaps maps,
+                                                                        FfnArgs a, Scratch sc, int M) {
+  extern __shared__ __align__(1024) uint8_t smem[];
+  BatchUpGateOp<MPAD> op{&maps, a, sc, M};
+  batch_run<BatchShape<MPAD>>(op, smem, sc);
+}
+
+// After the contraction, the CTAs that finished tiles wait for every tile's per-token sums of
+// squares, then update their rows: residual[m] = bf16(bf16(residual[m] + bf16(y inv_m gamma)) lambda).
+template <int MPAD>
+__global__ void __launch_bounds__(kBThreads, 1) ffn_batch_down_kernel(const __grid_constant__ BatchMaps maps,
+                                                                      FfnArgs a, Scratch sc, int M) {
+  extern __shared__ __align__(1024) uint8_t smem[];
+  using Shape = BatchShape<MPAD>;
+  BatchDownOp<MPAD> op{&maps, a, sc, M};
+  batch_run<Shape>(op, smem, sc);
+  uint8_t* base = align1024(smem);
+  BatchCtl& ctl = *reinterpret_cast<BatchCtl*>(base + Shape::kOffCtl);
+  __syncthreads();
+  const int nfin = ctl.fin_n < kBMaxFin ? ctl.fin_n : kBMaxFin;
+  if (nfin == 0) return;  // CTA-uniform
+  constexpr int kT = BatchDownOp<MPAD>::kTiles;
+  double* ss = reinterpret_cast<double*>(base + Shape::kOffHalf);  // [tile][token] (the halves are free)
+  for (int w = threadIdx.x; w < kT * M; w += kBThreads) {
+    const int t = w / M, m = w % M;
+    const unsigned long long* p = sc.batch_ss + (size_t(t) * kBatchMax + m) * 2;
+    unsigned long long lo = ld_relaxed_gpu_u64(p), hi = ld_relaxed_gpu_u64(p + 1);
+    const uint64_t t0 = globaltimer_ns();
+    while (uint32_t(lo >> 32) != op.epoch || uint32_t(hi >> 32) != op.epoch) {
+      if (globaltimer_ns() - t0 > kWaitLimitNs) {
+        atomicOr(sc.err, kErrWaitTimeout);
+        break;
+      }
+      lo = ld_relaxed_gpu_u64(p);
+      hi = ld_relaxed_gpu_u64(p + 1);
+    }
+    ss[t * kBatchMax + m] = __longlong_as_double(static_cast<long long>((hi << 32) | (lo & 0xffffffffull)));
+  }
+  __syncthreads();
+  G4_STAMP(sc, 7);
+  if (threadIdx.x < M) {
+    double sum = 0.0;
+    for (int t = 0; t < kT; ++t) sum += ss[t * kBatchMax + threadIdx.x];  // fixed order
+    ctl.inv[threadIdx.x] = rms_inverse(sum, kH);
+  }
+  __syncthreads();
+  const float lam = a.layer_scalar ? bf16_to_f32(a.layer_scalar[0]) : 1.0f;
+  for (int f = 0; f < nfin; ++f) {
+    const int tile = ctl.fin_tile[f];
+    for (int idx = threadIdx.x; idx < M * kTileRows; idx += kBThreads) {
+      const int m = idx / kTileRows, e = tile * kTileRows + idx % kTileRows;
+      const float y = bf16_to_f32(sc.batch_y[size_t(m) * kH + e]);
+      const float nrm = bf16_round((y * ctl.inv[m]) * bf16_to_f32(a.post_rms[e]));
+      uint16_t* res = a.residual + size_t(m) * kH + e;
+      float r = bf16_round(bf16_to_f32(*res) + nrm);
+      if (a.layer_scalar) r = bf16_round(r * lam);
+      *res = f32_to_bf16(r);
+    }
+  }
+}
+
+template <class... KArgs, class... Args>
+cudaError_t launch_batch(void (*kernel)(KArgs...), int grid, int threads, size_t smem, bool pdl, cudaStream_t stream,
+                         Args&&... args) {
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(grid);
+  cfg.blockDim = dim3(threads);
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = stream;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = pdl ? 1 : 0;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  return cudaLaunchKernelEx(&cfg, kernel, std::forward<Args>(args)...);
+}
+
+// The most tiles one CTA of a `grid`-CTA launch finishes (those whose first unit is in its run).
+int batch_max_fin(int upt, int tiles, int grid) {
+  int best = 0, run = 0, prev = -1;
+  for (int t = 0; t < tiles; ++t) {
+    const int c = cta_of_unit(int64_t(t) * upt, grid, int64_t(upt) * tiles);
+    run = c == prev ? run + 1 : 1;
+    prev = c;
+    best = run > best ? run : best;
+  }
+  return best;
+}
+
+template <int MPAD>
+cudaError_t launch_batch_t(const FfnArgs& a, int M, const LaunchEnv& env) {
+  using Shape = BatchShape<MPAD>;
+  BatchMaps ug{}, dn{};
+  cudaError_t e;
+  if (a.tiled) {
+    if ((e = env.maps->u8(a.up_packed, 128, uint64_t(kL) / 64 * (kH / kUnitK) * kTileRows, 128, kTileRows, true,
+                          &ug.a)))
+      return e;
+    if ((e = env.maps->u8(a.down_packed, 128, uint64_t(kH) / kTileRows * (kL / kUnitK) * kTileRows, 128, kTileRows,
+                          true, &dn.a)))
+      return e;
+  } else {
+    if ((e = env.maps->u8(a.up_packed, kH / 2, kL, 128, 64, true, &ug.a))) return e;
+    if ((e = env.maps->u8(a.gate_packed, kH / 2, kL, 128, 64, true, &ug.a2))) return e;
+    if ((e = env.maps->u8(a.up_scale, kH / 16, kL, 16, 64, false, &ug.s))) return e;
+    if ((e = env.maps->u8(a.gate_scale, kH / 16, kL, 16, 64, false, &ug.s2))) return e;
+    if ((e = env.maps->u8(a.down_packed, kL / 2, kH, 128, kTileRows, true, &dn.a))) return e;
+    if ((e = env.maps->u8(a.down_scale, kL / 16, kH, 16, kTileRows, false, &dn.s))) return e;
+  }
+  if ((e = env.maps->bf16(env.sc.batch_h, kH, uint64_t(M), 64, MPAD, &ug.b))) return e;
+  if ((e = env.maps->bf16(env.sc.act, kL, uint64_t(M), 64, MPAD, &dn.b))) return e;
+  const int gu = env.sm_count < BatchUpGateOp<MPAD>::kUnitsPerTile * BatchUpGateOp<MPAD>::kTiles
+                     ? env.sm_count
+                     : BatchUpGateOp<MPAD>::kUnitsPerTile * BatchUpGateOp<MPAD>::kTiles;
+  const int gd = env.sm_count;
+  Scratch su = env.sc, sd = env.sc;
+#ifdef G4_TRACE
+  if (su.trace) su.trace += 11 * 4096;  // profiling builds: stamp rows of their own
+  if (sd.trace) sd.trace += 12 * 4096;
+#endif
+  if ((e = launch_batch(ffn_batch_norm_kernel, M, 256, 0, env.pdl, env.stream, a, env.sc))) return e;
+  if ((e = launch_batch(ffn_batch_upgate_kernel<MPAD>, gu, kBThreads, Shape::kSmemBytes, true, env.stream, ug, a, su,
+                        M)))
+    return e;
+  return launch_batch(ffn_batch_down_kernel<MPAD>, gd, kBThreads, Shape::kSmemBytes, true, env.stream, dn, a, sd, M);
+}
+
+template <int MPAD>
+cudaError_t prepare_batch_t() {
+  cudaError_t e;
+  if ((e = cudaFuncSetAttribute(ffn_batch_upgate_kernel<MPAD>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                int(BatchShape<MPAD>::kSmemBytes))))
+    return e;
+  return cudaFuncSetAttribute(ffn_batch_down_kernel<MPAD>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                              int(BatchShape<MPAD>::kSmemBytes));
+}
+
+}  // namespace
+
+cudaError_t prepare_batch_kernels() {
+  cudaError_t e;
+  if ((e = prepare_batch_t<16>())) return e;
+  if ((e = prepare_batch_t<32>())) return e;
+  if ((e = prepare_batch_t<48>())) return e;
+  return prepare_batch_t<64>();
+}
+
+bool batch_geometry_fits(int sm_count) {
+  // a down CTA keeps at most kBMaxFin finished tiles for its residual tail
+  const int grid = sm_count;
+  return batch_max_fin(kL / kUnitK, kH / kTileRows, grid) <= kBMaxFin;
+}
+
+size_t batch_words_count(int sm_count) { return size_t(sm_count) * kBatchMax * kTileRows; }
+
+cudaError_t launch_ffn_nvfp4_batch(const FfnArgs& a, int M, const LaunchEnv& env) {
+  if (env.tp.world != 1) return cudaErrorNotSupported;  // the batched feed-forward runs on one GPU
+  if (M < 2 || M > kBatchMax) return cudaErrorInvalidValue;
+  switch ((M + 15) / 16) {
+    case 1: return launch_batch_t<16>(a, M, env);
+    case 2: return launch_batch_t<32>(a, M, env);
+    case 3: return launch_batch_t<48>(a, M, env);
+    default: return launch_batch_t<64>(a, M, env);
+  }
+}
+
+}  // namespace g4

@@ -64,7 +64,18 @@ struct Scratch {
   unsigned long long* tile_ss;  // per output tile: sum of squares of its bf16 rows, as two words
                                 // (epoch << 32 | low / high half of the f64), kTileSsCount tiles
   uint64_t* trace;     // per-CTA phase timestamps (profiling builds only; null otherwise)
+  // the token-batched feed-forward (M > 1): its normalised input h [kBatchMax][H], the down
+  // projection's bf16 rows [kBatchMax][H], split-K words [CTA][kBatchMax tokens][128 rows] and the
+  // per (tile, token) sums of squares of the residual tail (two words each, kBatchSsWords)
+  uint16_t* batch_h;
+  uint16_t* batch_y;
+  unsigned long long* batch_words;
+  unsigned long long* batch_ss;
 };
+constexpr int kBatchMax = 64;  // tokens per batched feed-forward call
+constexpr size_t kBatchSsWords = size_t(32) * kBatchMax * 2;
+// the batched feed-forward's call count (tags its split-K words and tile sums)
+constexpr int kBatchEpoch = 4080;
 constexpr int kTileSsCount = 64;
 // One region of tile sums per op (O, down), in words from `tile_ss`: the ops count their calls
 // separately, so a word of one op must never be read by the other.
@@ -291,6 +302,13 @@ __device__ __forceinline__ void embed_row(const uint16_t* __restrict__ row, uint
     }
     reinterpret_cast<uint4*>(out)[c] = make_uint4(o[0], o[1], o[2], o[3]);
   }
+}
+
+__device__ __forceinline__ float gelu_tanh(float x) {
+  // F.gelu(approximate="tanh"): 0.5 * x * (1 + tanh(sqrt(2/pi) * (x + 0.044715 * x^3)))
+  const float cube = x * x * x;
+  const float inner = 0.7978845608028654f * (x + 0.044715f * cube);
+  return 0.5f * x * (1.0f + tanhf(inner));
 }
 
 // ---------------------------------------------------------------------------------------

@@ -22,6 +22,7 @@ struct g4_ctx {
   size_t scratch_bytes = 0;
   g4::Scratch sc{};
   size_t act_bytes = 0;
+  bool batch_ok = false;  // the batched feed-forward's launch geometry fits this GPU
   g4::TmapCache maps;
   // tensor parallelism (g4_tp_init / g4_tp_connect); world 1 until then
   int tp_rank = 0, tp_world = 1;

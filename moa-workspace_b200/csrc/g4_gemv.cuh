@@ -136,6 +136,44 @@ __device__ __forceinline__ double sum_squares_bf16x16(const uint4& a, const uint
   return ss;
 }
 
+// Bring units [u0, u1) of a unit-tiled matrix (unit_bytes each) into L2 with one bulk prefetch.
+__device__ __forceinline__ void prefetch_units(const uint8_t* base, int u0, int u1, uint32_t unit_bytes) {
+  if (u1 > u0)
+    asm volatile("cp.async.bulk.prefetch.L2.global [%0], %1;" ::"l"(base + size_t(u0) * unit_bytes),
+                 "r"(uint32_t(u1 - u0) * unit_bytes)
+                 : "memory");
+}
+
+// Loads of one 16-element group: bf16 input written by the preceding kernel (L2-coherent) and,
+// for the normalised ops, its gamma.
+__device__ __forceinline__ void load_group_cg(const uint16_t* x, int g, uint4 (&raw)[4]) {
+  raw[0] = __ldcg(reinterpret_cast<const uint4*>(x + 16 * g));
+  raw[1] = __ldcg(reinterpret_cast<const uint4*>(x + 16 * g + 8));
+}
+__device__ __forceinline__ void load_group_gamma(const uint16_t* gamma, int g, uint4 (&raw)[4]) {
+  raw[2] = *reinterpret_cast<const uint4*>(gamma + 16 * g);
+  raw[3] = *reinterpret_cast<const uint4*>(gamma + 16 * g + 8);
+}
+
+// The 16 bf16 values of two uint4 (element j in half j % 2 of word j / 2).
+__device__ __forceinline__ void bf16x16_to_f32(const uint4& a, const uint4& b, float (&v)[16]) {
+  const uint32_t w[8] = {a.x, a.y, a.z, a.w, b.x, b.y, b.z, b.w};
+#pragma unroll
+  for (int i = 0; i < 8; ++i) {
+    v[2 * i] = __uint_as_float(w[i] << 16);
+    v[2 * i + 1] = __uint_as_float(w[i] & 0xffff0000u);
+  }
+}
+
+// h = bf16((x * inv) * gamma) for one group (the RMSNorm of gemma4.py:83-89).
+__device__ __forceinline__ void rms_apply16(const uint4 (&raw)[4], float inv, float (&v)[16]) {
+  float g[16];
+  bf16x16_to_f32(raw[0], raw[1], v);
+  bf16x16_to_f32(raw[2], raw[3], g);
+#pragma unroll
+  for (int j = 0; j < 16; ++j) v[j] = bf16_round((v[j] * inv) * g[j]);
+}
+
 // nvfp4 B operand: the digits of 8 consecutive activation elements (bf16 bits in `raw`) as
 // 4-byte pieces of the 16 B rows. An element of exponent e >= pc - 14 is class 0 (rows 0-7,
 // X = RN(v 2^(21 - pc)), exact); a smaller one is class 1 (rows 8-15, X = RN(v 2^(36 - pc)),

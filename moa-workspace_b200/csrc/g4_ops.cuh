@@ -148,6 +148,10 @@ class TmapCache {
   // Row-major uint8 matrix [rows, cols] (fp8 codes, e4m3 scales), box {box_cols, box_rows}.
   cudaError_t u8(const void* base, uint64_t cols, uint64_t rows, uint32_t box_cols, uint32_t box_rows, bool swizzle128,
                  CUtensorMap* out);
+  // Row-major bf16 matrix [rows, cols], box {box_cols, box_rows}, 128-byte swizzle (box_cols = 64):
+  // rows past the end read as zeros.
+  cudaError_t bf16(const void* base, uint64_t cols, uint64_t rows, uint32_t box_cols, uint32_t box_rows,
+                   CUtensorMap* out);
   // KV ring cache [ring, heads, dim] bf16 as a 3-D tensor (dim, head, slot), box {dim, 1, box_slots}:
   // one load brings box_slots rows of one head.
   cudaError_t kv(const void* base, uint64_t ring, uint32_t heads, uint32_t dim, uint32_t box_slots, CUtensorMap* out);
@@ -181,6 +185,11 @@ cudaError_t launch_attention(const AttnArgs& a, const LaunchEnv& env);
 cudaError_t launch_o(const OArgs& a, const LaunchEnv& env);
 cudaError_t launch_ffn_nvfp4(const FfnArgs& a, const LaunchEnv& env);
 cudaError_t launch_ffn_fp8(const Ffn8Args& a, const LaunchEnv& env);
+// The NVFP4 feed-forward on m = 2..64 tokens (g4_batch.cu): residual [m][H]; one GPU.
+cudaError_t prepare_batch_kernels();
+bool batch_geometry_fits(int sm_count);
+size_t batch_words_count(int sm_count);  // split-K words of the batched kernels
+cudaError_t launch_ffn_nvfp4_batch(const FfnArgs& a, int m, const LaunchEnv& env);
 cudaError_t launch_full_qkv(const FullQkvArgs& a, const LaunchEnv& env);
 cudaError_t launch_full_attention(const FullAttnArgs& a, const LaunchEnv& env);
 cudaError_t launch_full_o(const FullOArgs& a, const LaunchEnv& env);

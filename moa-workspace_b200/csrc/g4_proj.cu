@@ -41,56 +41,12 @@ struct Shapes {
 using FullQkvShape = GemvShape<false, 6, kH / kUnitK, (kQf + kDf) / kTileRows, 8>;
 using FullOShape = GemvShape<false, 6, kQf / kUnitK, kH / kTileRows, 8>;
 
-__device__ __forceinline__ float gelu_tanh(float x) {
-  // F.gelu(approximate="tanh"): 0.5 * x * (1 + tanh(sqrt(2/pi) * (x + 0.044715 * x^3)))
-  const float cube = x * x * x;
-  const float inner = 0.7978845608028654f * (x + 0.044715f * cube);
-  return 0.5f * x * (1.0f + tanhf(inner));
-}
-
 // Unit-tiled weights (g4_pack_tiles): pipeline unit u of a matrix is one contiguous block,
 // fetched by one TMA box: fp8, kUnitBox rows of 128 codes (both 128-element halves of its 128
 // rows); nvfp4, 128 rows of 128 bytes (64 up + 64 gate rows, or 128 down rows, each the unit's
 // 256 packed codes), its block scales one 2 KB block of the same 128 rows x 16 bytes.
 constexpr int kUnitBox = 2 * kTileRows;
 
-// Bring units [u0, u1) of a unit-tiled matrix (unit_bytes each) into L2 with one bulk prefetch.
-__device__ __forceinline__ void prefetch_units(const uint8_t* base, int u0, int u1, uint32_t unit_bytes) {
-  if (u1 > u0)
-    asm volatile("cp.async.bulk.prefetch.L2.global [%0], %1;" ::"l"(base + size_t(u0) * unit_bytes),
-                 "r"(uint32_t(u1 - u0) * unit_bytes)
-                 : "memory");
-}
-
-// Loads of one 16-element group: bf16 input written by the preceding kernel (L2-coherent) and,
-// for the normalised ops, its gamma.
-__device__ __forceinline__ void load_group_cg(const uint16_t* x, int g, uint4 (&raw)[4]) {
-  raw[0] = __ldcg(reinterpret_cast<const uint4*>(x + 16 * g));
-  raw[1] = __ldcg(reinterpret_cast<const uint4*>(x + 16 * g + 8));
-}
-__device__ __forceinline__ void load_group_gamma(const uint16_t* gamma, int g, uint4 (&raw)[4]) {
-  raw[2] = *reinterpret_cast<const uint4*>(gamma + 16 * g);
-  raw[3] = *reinterpret_cast<const uint4*>(gamma + 16 * g + 8);
-}
-
-// The 16 bf16 values of two uint4 (element j in half j % 2 of word j / 2).
-__device__ __forceinline__ void bf16x16_to_f32(const uint4& a, const uint4& b, float (&v)[16]) {
-  const uint32_t w[8] = {a.x, a.y, a.z, a.w, b.x, b.y, b.z, b.w};
-#pragma unroll
-  for (int i = 0; i < 8; ++i) {
-    v[2 * i] = __uint_as_float(w[i] << 16);
-    v[2 * i + 1] = __uint_as_float(w[i] & 0xffff0000u);
-  }
-}
-
-// h = bf16((x * inv) * gamma) for one group (the RMSNorm of gemma4.py:83-89).
-__device__ __forceinline__ void rms_apply16(const uint4 (&raw)[4], float inv, float (&v)[16]) {
-  float g[16];
-  bf16x16_to_f32(raw[0], raw[1], v);
-  bf16x16_to_f32(raw[2], raw[3], g);
-#pragma unroll
-  for (int j = 0; j < 16; ++j) v[j] = bf16_round((v[j] * inv) * g[j]);
-}
 
 // ---------------------------------------------------------------------------------------
 // Tensor parallelism: the one-shot all-reduce of a finished tile's partial rows (O and down).
@@ -1382,6 +1338,27 @@ cudaError_t TmapCache::u8(const void* base, uint64_t cols, uint64_t rows, uint32
   return cudaSuccess;
 }
 
+cudaError_t TmapCache::bf16(const void* base, uint64_t cols, uint64_t rows, uint32_t box_cols, uint32_t box_rows,
+                            CUtensorMap* out) {
+  const uint64_t key = (cols << 34) ^ (rows << 12) ^ (uint64_t(box_cols) << 4) ^ (uint64_t(box_rows) << 1) ^
+                       (uint64_t(1) << 62);
+  if (const CUtensorMap* m = find(base, key)) {
+    *out = *m;
+    return cudaSuccess;
+  }
+  auto enc = encode_fn();
+  if (!enc) return cudaErrorNotSupported;
+  const cuuint64_t gdim[2] = {cols, rows};
+  const cuuint64_t gstride[1] = {cols * 2};
+  const cuuint32_t box[2] = {box_cols, box_rows};
+  const cuuint32_t estride[2] = {1, 1};
+  const CUresult r = enc(out, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, const_cast<void*>(base), gdim, gstride, box,
+                         estride, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+                         CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  if (r != CUDA_SUCCESS) return cudaErrorInvalidValue;
+  put(base, key, *out);
+  return cudaSuccess;
+}
 
 // ---------------------------------------------------------------------------------------
 // O projection on scratch the caller provides, with nothing cached or allocated

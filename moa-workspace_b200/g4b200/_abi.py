@@ -50,6 +50,8 @@ SIGNATURES = {
     "g4_full_attention_output": [_p] * 7 + [_p],
     "g4_embed_token": [_p] * 4 + [_i32, _p],
     "g4_final_norm_and_logits": [_p] * 5 + [_i32, _p],
+    "g4_decoder_feedforward_batch": [_p] * 14 + [_i32, _p],
+    "g4_decoder_feedforward_batch_tiled": [_p] * 12 + [_i32, _p],
     "g4_decoder_feedforward_fp8": [_p] * 11 + [_p],
     "g4_decoder_feedforward_fp8_tiled": [_p] * 10 + [_p],
     "g4_pack_tiles": [_p, _p, _p, _p, _i32, _i32, _i32, _i32, _p],

@@ -334,6 +334,67 @@ def decoder_feedforward_tiled(device: Device, residual_hbm, pre_ff_rms_weight, u
     _check(device, st, "decoder_feedforward_tiled")
 
 
+BATCH_MAX = 64  # tokens per decoder_feedforward_batch call
+
+
+def _batch_rows(residual_hbm) -> int:
+    m = residual_hbm.shape[0] if residual_hbm.dim() == 2 else 0
+    if not 1 <= m <= BATCH_MAX:
+        raise ValueError(f"residual_hbm: shape {tuple(residual_hbm.shape)}, expected [m, {H}] with m in [1, {BATCH_MAX}]")
+    return m
+
+
+def decoder_feedforward_batch(device: Device, residual_hbm, pre_ff_rms_weight, up_weight_packed, gate_weight_packed,
+                              down_weight_packed, up_weight_scale, gate_weight_scale, down_weight_scale,
+                              up_global_scale, gate_global_scale, down_global_scale, post_ff_rms_weight, layer_scalar,
+                              *, stream=None) -> None:
+    """decoder_feedforward (src/ops.rs:201-239) on each row of residual_hbm [m, H], m in [1, 64]:
+    the weights are read once for all m tokens (the NVFP4 token-batch sweep). One GPU."""
+    bf = torch.bfloat16
+    m = _batch_rows(residual_hbm)
+    args = [
+        _arg(residual_hbm, "residual_hbm", bf, (m, H), device),
+        _arg(pre_ff_rms_weight, "pre_ff_rms_weight", bf, (H,), device),
+        _arg(up_weight_packed, "up_weight_packed", torch.uint8, (L, H // 2), device),
+        _arg(gate_weight_packed, "gate_weight_packed", torch.uint8, (L, H // 2), device),
+        _arg(down_weight_packed, "down_weight_packed", torch.uint8, (H, L // 2), device),
+        _arg(up_weight_scale, "up_weight_scale", _BYTE_DTYPES, (L, H // 16), device),
+        _arg(gate_weight_scale, "gate_weight_scale", _BYTE_DTYPES, (L, H // 16), device),
+        _arg(down_weight_scale, "down_weight_scale", _BYTE_DTYPES, (H, L // 16), device),
+        _arg(up_global_scale, "up_global_scale", torch.float32, (1,), device),
+        _arg(gate_global_scale, "gate_global_scale", torch.float32, (1,), device),
+        _arg(down_global_scale, "down_global_scale", torch.float32, (1,), device),
+        _arg(post_ff_rms_weight, "post_ff_rms_weight", bf, (H,), device),
+        _arg(layer_scalar, "layer_scalar", bf, (8,), device),
+    ]
+    st = _abi.lib().g4_decoder_feedforward_batch(device.handle, *args, m, _stream_ptr(stream, device.index))
+    _check(device, st, "decoder_feedforward_batch")
+
+
+def decoder_feedforward_batch_tiled(device: Device, residual_hbm, pre_ff_rms_weight, up_gate_weight_tiled,
+                                    down_weight_tiled, up_gate_scale_tiled, down_scale_tiled, up_global_scale,
+                                    gate_global_scale, down_global_scale, post_ff_rms_weight, layer_scalar, *,
+                                    stream=None) -> None:
+    """decoder_feedforward_batch on weights packed by `pack_upgate` / `tile_weight`."""
+    bf = torch.bfloat16
+    m = _batch_rows(residual_hbm)
+    args = [
+        _arg(residual_hbm, "residual_hbm", bf, (m, H), device),
+        _arg(pre_ff_rms_weight, "pre_ff_rms_weight", bf, (H,), device),
+        _arg(up_gate_weight_tiled, "up_gate_weight_tiled", torch.uint8, (2 * L, H // 2), device),
+        _arg(down_weight_tiled, "down_weight_tiled", torch.uint8, (H, L // 2), device),
+        _arg(up_gate_scale_tiled, "up_gate_scale_tiled", _BYTE_DTYPES, (2 * L, H // 16), device),
+        _arg(down_scale_tiled, "down_scale_tiled", _BYTE_DTYPES, (H, L // 16), device),
+        _arg(up_global_scale, "up_global_scale", torch.float32, (1,), device),
+        _arg(gate_global_scale, "gate_global_scale", torch.float32, (1,), device),
+        _arg(down_global_scale, "down_global_scale", torch.float32, (1,), device),
+        _arg(post_ff_rms_weight, "post_ff_rms_weight", bf, (H,), device),
+        _arg(layer_scalar, "layer_scalar", bf, (8,), device),
+    ]
+    st = _abi.lib().g4_decoder_feedforward_batch_tiled(device.handle, *args, m, _stream_ptr(stream, device.index))
+    _check(device, st, "decoder_feedforward_batch_tiled")
+
+
 def decoder_feedforward_fp8(device: Device, residual_hbm, pre_ff_rms_weight, up_weight, gate_weight, down_weight,
                             up_weight_scale, gate_weight_scale, down_weight_scale, post_ff_rms_weight, layer_scalar, *,
                             stream=None) -> None:

@@ -235,6 +235,21 @@ def decoder_feedforward(residual, pre_rms_weight, up_packed, gate_packed, down_p
                              layer_scalar)
 
 
+def decoder_feedforward_batch(residual, pre_rms_weight, up_packed, gate_packed, down_packed,
+                              up_scale, gate_scale, down_scale, up_global, gate_global, down_global,
+                              post_rms_weight, layer_scalar, hidden=3840, inter=15360):
+    """decoder_feedforward (FOG/src/ops.rs:201-239) on each row of residual [M, H], row by row
+    (the reference op is per token; the weights are dequantised once)."""
+    w_up = nvfp4_dequant(up_packed, up_scale, inter, hidden)
+    w_gate = nvfp4_dequant(gate_packed, gate_scale, inter, hidden)
+    w_down = nvfp4_dequant(down_packed, down_scale, hidden, inter)
+    rows = [feedforward_dense(r, pre_rms_weight, post_rms_weight, w_up, w_gate, w_down,
+                              np.float32(up_global), np.float32(gate_global), np.float32(down_global),
+                              layer_scalar)
+            for r in np.asarray(residual).reshape(-1, hidden)]
+    return np.stack(rows)
+
+
 def feedforward_fp8(residual, pre_rms_weight, up_w, gate_w, down_w, up_s, gate_s, down_s,
                     post_rms_weight, layer_scalar, hidden=3840, inter=15360):
     """FP8-per-channel FFN variant (no counterpart op in the reference).
