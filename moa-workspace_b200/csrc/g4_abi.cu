@@ -94,7 +94,8 @@ g4_status g4_ctx_create(int device, g4_ctx** out) {
   const size_t off_by = off_bh + size_t(g4::kBatchMax) * g4::kH * sizeof(uint16_t);
   const size_t off_bw = off_by + size_t(g4::kBatchMax) * g4::kH * sizeof(uint16_t);
   const size_t off_bs = off_bw + g4::batch_words_count(ctx->sm_count) * sizeof(unsigned long long);
-  const size_t off_trace = off_bs + g4::kBatchSsWords * sizeof(unsigned long long);
+  const size_t off_bu = off_bs + g4::kBatchSsWords * sizeof(unsigned long long);
+  const size_t off_trace = off_bu + size_t(g4::kBatchMax) * sizeof(float);
 #ifdef G4_TRACE
   const size_t total = off_trace + size_t(65536 + 4096 * 32 * 8) * sizeof(uint64_t);
 #else
@@ -123,6 +124,7 @@ g4_status g4_ctx_create(int device, g4_ctx** out) {
   ctx->sc.batch_y = reinterpret_cast<uint16_t*>(base + off_by);
   ctx->sc.batch_words = reinterpret_cast<unsigned long long*>(base + off_bw);
   ctx->sc.batch_ss = reinterpret_cast<unsigned long long*>(base + off_bs);
+  ctx->sc.batch_unscale = reinterpret_cast<float*>(base + off_bu);
   ctx->batch_ok = g4::batch_geometry_fits(ctx->sm_count);
 #ifdef G4_TRACE
   ctx->sc.trace = reinterpret_cast<uint64_t*>(base + off_trace);

@@ -34,12 +34,12 @@ constexpr int kBThreads = 480;  // 15 warps
 constexpr int kWProducer = 0, kWIssuer = 1, kWRelay = 2, kWDq0 = 7, kDqWarps = 8;  // epilogue: warps 3-6
 constexpr int kBIssueBarrier = 2;  // issuer + relay (64 threads)
 constexpr int kBEpiBarrier = 1;    // the four epilogue warps
-constexpr int kBMaxStages = 6;
+constexpr int kBMaxStages = 8;
 constexpr int kBMaxFin = 2;        // tiles one down CTA may finish (checked at set-up)
 
 struct BatchCtl {
   uint64_t full_a[kBMaxStages], full_b[kBMaxStages], empty[kBMaxStages];
-  uint64_t hfull[2], hempty[2], done[4], tempty[4], drain;
+  uint64_t hfull[3], hempty[3], done[8], tempty[8], drain;
   uint32_t tmem_base;
   uint32_t abort;
   int fin_tile[kBMaxFin];
@@ -49,7 +49,8 @@ struct BatchCtl {
 };
 
 // Profiling builds: per-unit timestamps of CTA 0 at trace[3000 + 64 k + i] (k: 0 producer issued,
-// 1 dequantised, 2 released to the issuer, 3 epilogue done).
+// 1 second half dequantised, 2 released to the issuer, 3 epilogue done, 4 / 6 first / second half's
+// A slot free, 5 first half dequantised).
 #ifdef G4_TRACE
 #define G4_UNIT_STAMP(sc, k, i)                                                                           \
   do {                                                                                                \
@@ -64,21 +65,27 @@ struct BatchCtl {
 template <int MPAD>
 struct BatchShape {
   static constexpr int kMpad = MPAD;  // B rows: the tokens, zero-padded
-  static constexpr int kStages = MPAD <= 16 ? 6 : (MPAD <= 32 ? 4 : 3);
   static constexpr int kABytes = kTileRows * 128;     // packed e2m1 codes: 128 rows x 256 K
   static constexpr int kScaleBytes = kTileRows * 16;  // ue4m3 block scales
   static constexpr int kBColBytes = MPAD * 128;       // B: one 64-element K column block of MPAD rows
   static constexpr int kBBytes = 4 * kBColBytes;
   static constexpr int kStageBytes = kABytes + kScaleBytes + kBBytes;
-  static constexpr int kHalfBytes = 2 * kTileRows * 128;  // dequantised A: 128 rows x 128 K bf16
-  static constexpr int kTSlots = 4;                       // TMEM accumulators of MPAD columns, one per unit
-  static constexpr uint32_t kTmemCols = 4 * MPAD <= 64 ? 64u : (4 * MPAD <= 128 ? 128u : 256u);
-  static constexpr uint32_t kIdesc = umma_idesc_bf16(kTileRows, MPAD);
-  static constexpr size_t kOffHalf = size_t(kStages) * kStageBytes;
-  static constexpr size_t kOffX = kOffHalf + 2 * size_t(kHalfBytes);
-  static constexpr size_t kXBytes = size_t(64) * MPAD * 2;  // up/gate: bf16(gelu(gate)) [token][64]
+  static constexpr size_t kXBytes = size_t(16) * 64 * 2;  // up/gate: bf16 gate, then gelu [16 tokens][64]
+  static constexpr int kStagesFit = int((227 * 1024 - kXBytes - sizeof(BatchCtl) - 1024) / kStageBytes);
+  static constexpr int kStages = kStagesFit < kBMaxStages ? kStagesFit : kBMaxStages;
+  // TMEM (512 columns): kTSlots accumulators of MPAD columns (one per unit in flight), each row's
+  // running sum of its tile piece (MPAD columns), then the dequantised A operand: a ring of
+  // kAHalves half units, 64 columns each (128 rows x 128 K 16-bit values, two per column).
+  static constexpr int kTSlots = MPAD <= 32 ? 8 : 4;
+  static constexpr uint32_t kColSum = uint32_t(kTSlots) * MPAD;
+  static constexpr uint32_t kColA = (kColSum + MPAD + 31) / 32 * 32;
+  static constexpr int kAHalves = 3;
+  static constexpr uint32_t kTmemCols = 512;
+  static constexpr size_t kOffX = size_t(kStages) * kStageBytes;
   static constexpr size_t kOffCtl = kOffX + kXBytes;
   static constexpr size_t kSmemBytes = kOffCtl + sizeof(BatchCtl) + 1024;
+  static_assert(kColA + kAHalves * 64 <= kTmemCols, "TMEM budget");
+  static_assert(kStages >= 3, "pipeline depth");
   static_assert(MPAD % 16 == 0 && MPAD <= kBatchMax, "N of the MMA");
   static_assert(kStages <= kBMaxStages, "barrier arrays");
   static_assert(kStageBytes % 1024 == 0 && (kABytes + kScaleBytes) % 1024 == 0, "1024-byte swizzle atoms");
@@ -113,6 +120,25 @@ __device__ __forceinline__ uint4 dequant8_bf16(uint32_t codes, uint32_t scale_by
   return make_uint4(o[0], o[1], o[2], o[3]);
 }
 
+// The same as eight f16 (exact too): the conversion and one multiply per pair.
+__device__ __forceinline__ uint4 dequant8_f16(uint32_t codes, uint32_t scale_byte) {
+  uint32_t s2, h[4];
+  asm("{\n .reg .b16 t;\n cvt.u16.u32 t, %1;\n cvt.rn.f16x2.e4m3x2 %0, t;\n}" : "=r"(s2) : "r"(scale_byte * 0x101u));
+  asm("{\n .reg .b8 b0, b1, b2, b3;\n mov.b32 {b0, b1, b2, b3}, %4;\n"
+      " cvt.rn.f16x2.e2m1x2 %0, b0;\n cvt.rn.f16x2.e2m1x2 %1, b1;\n"
+      " cvt.rn.f16x2.e2m1x2 %2, b2;\n cvt.rn.f16x2.e2m1x2 %3, b3;\n}"
+      : "=r"(h[0]), "=r"(h[1]), "=r"(h[2]), "=r"(h[3])
+      : "r"(codes));
+  const __half2 sc = *reinterpret_cast<const __half2*>(&s2);
+  uint32_t o[4];
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    const __half2 p = __hmul2(*reinterpret_cast<const __half2*>(&h[i]), sc);
+    o[i] = *reinterpret_cast<const uint32_t*>(&p);
+  }
+  return make_uint4(o[0], o[1], o[2], o[3]);
+}
+
 __device__ __forceinline__ void st_release_gpu_u64(unsigned long long* p, unsigned long long v) {
   asm volatile("st.release.gpu.global.u64 [%0], %1;" ::"l"(p), "l"(v) : "memory");
 }
@@ -122,48 +148,62 @@ __device__ __forceinline__ unsigned long long ld_acquire_gpu_u64(const unsigned 
   return v;
 }
 
-// The tile piece of the CTA holding the tile's first unit gets the other pieces (later CTAs of the
-// tile) added in CTA order; every other piece is published as epoch-tagged words, one per (token,
-// row), in its CTA's slot. The publishing thread of a row stores its last token's word with
-// release semantics after the others, so a reader that acquires that word with this call's tag
-// sees the whole row: the finisher polls one word per piece (all pieces in flight at once), then
-// reads the rest with independent loads. `ok` false: nothing is read (the values become NaN).
-// Epilogue threads.
+// Split tiles. The tile piece of the CTA holding the tile's first unit gets the other pieces (later
+// CTAs of the tile) added in CTA order; every other piece is published as epoch-tagged words, one
+// per (token, row), in its CTA's slot. The publishing thread of a row stores its last token's word
+// with release semantics after the others, so a reader that acquires that word with this call's
+// tag sees the whole row: the finisher polls one word per piece (all pieces in flight at once),
+// then reads the rest with independent loads. Tokens go 16 at a time from the row's running sum
+// in TMEM (`tsum`, this thread's lane). Epilogue threads; `ok` false: nothing is read (NaN).
+struct SplitPiece {
+  unsigned long long* words;
+  uint32_t tag;
+  int first, later;  // the tile's first CTA; pieces after it
+  bool publish;      // this CTA holds a later piece
+};
+
 template <int MPAD>
-__device__ void split_finish(float (&acc)[MPAD], int M, int tile, int upt, int64_t total, int row, uint32_t tag,
-                             unsigned long long* words, bool& ok, uint32_t* err, bool& publish_only) {
+__device__ SplitPiece split_begin(int tile, int upt, int64_t total, int row, int M, uint32_t tsum, uint32_t tag,
+                                  unsigned long long* words, bool& ok, uint32_t* err) {
+  SplitPiece sp;
   const int64_t first_unit = int64_t(tile) * upt, grid = gridDim.x;
-  const int first = cta_of_unit(first_unit, grid, total);
+  sp.words = words;
+  sp.tag = tag;
+  sp.first = cta_of_unit(first_unit, grid, total);
+  sp.later = cta_of_unit(first_unit + upt - 1, grid, total) - sp.first;
+  sp.publish = sp.first != int(blockIdx.x);
   const unsigned long long tag_bits = static_cast<unsigned long long>(tag) << 32;
-  publish_only = first != int(blockIdx.x);
-  if (publish_only) {
+  if (sp.publish) {
     unsigned long long* w = words + size_t(blockIdx.x) * kBatchMax * kTileRows + row;
 #pragma unroll
-    for (int m = 0; m < MPAD; ++m)
-      if (m < M - 1) st_relaxed_gpu_u64(w + m * kTileRows, tag_bits | __float_as_uint(acc[m]));
+    for (int c = 0; c < MPAD; c += 16) {
+      float a[16];
+      if (ok) {
+        tmem_ld16(tsum + uint32_t(c), a);
+        tmem_ld_wait();
+      }
 #pragma unroll
-    for (int m = 0; m < MPAD; ++m)
-      if (m == M - 1) st_release_gpu_u64(w + m * kTileRows, tag_bits | __float_as_uint(acc[m]));
-    return;
+      for (int j = 0; j < 16; ++j) {
+        const unsigned long long x = tag_bits | (ok ? __float_as_uint(a[j]) : 0x7fc00000u);
+        if (c + j < M - 1) st_relaxed_gpu_u64(w + (c + j) * kTileRows, x);
+        if (c + j == M - 1) st_release_gpu_u64(w + (c + j) * kTileRows, x);
+      }
+    }
+    return sp;
   }
-  const int later = cta_of_unit(first_unit + upt - 1, grid, total) - first;  // pieces after this CTA's
-  if (later > kMaxCtasPerGroup) {  // launchers keep every tile within the slots
-    atomicOr(err, kErrInternal);
-    ok = false;
-  }
-  auto slot = [&](int k) { return words + size_t(first + 1 + k) * kBatchMax * kTileRows + row; };
   constexpr int kPoll = 8;  // pieces whose last word is polled together
   const uint64_t t0 = globaltimer_ns();
-  for (int g0 = 0; g0 < later && ok; g0 += kPoll) {
+  for (int g0 = 0; g0 < sp.later && ok; g0 += kPoll) {
     uint32_t pending = 0u;
 #pragma unroll
     for (int k = 0; k < kPoll; ++k)
-      if (g0 + k < later) pending |= 1u << k;
+      if (g0 + k < sp.later) pending |= 1u << k;
     while (pending) {
       unsigned long long x[kPoll];  // every pending piece's last word in flight at once
 #pragma unroll
       for (int k = 0; k < kPoll; ++k)
-        if (pending & (1u << k)) x[k] = ld_acquire_gpu_u64(slot(g0 + k) + size_t(M - 1) * kTileRows);
+        if (pending & (1u << k))
+          x[k] = ld_acquire_gpu_u64(words + (size_t(sp.first + 1 + g0 + k) * kBatchMax + (M - 1)) * kTileRows + row);
 #pragma unroll
       for (int k = 0; k < kPoll; ++k)
         if ((pending & (1u << k)) && uint32_t(x[k] >> 32) == tag) pending &= ~(1u << k);
@@ -174,21 +214,29 @@ __device__ void split_finish(float (&acc)[MPAD], int M, int tile, int upt, int64
       }
     }
   }
-  for (int k = 0; k < later; ++k) {
-    const unsigned long long* w = slot(k);
+  return sp;
+}
+
+// The finisher's sums of tokens [c, c + 16): its own piece from TMEM plus the later pieces in CTA order.
+__device__ __forceinline__ void split_chunk(const SplitPiece& sp, int c, int M, int row, uint32_t tsum, bool ok,
+                                            float (&a)[16]) {
+  if (ok) {
+    tmem_ld16(tsum + uint32_t(c), a);
+    tmem_ld_wait();
+  }
 #pragma unroll
-    for (int c = 0; c < MPAD; c += 16) {  // 16 independent loads in flight, then their sums
-      float v[16];
+  for (int j = 0; j < 16; ++j)
+    if (!ok) a[j] = __uint_as_float(0x7fc00000u);
+  for (int k = 0; k < sp.later; ++k) {
+    const unsigned long long* w = sp.words + (size_t(sp.first + 1 + k) * kBatchMax + c) * kTileRows + row;
+    float v[16];
 #pragma unroll
-      for (int j = 0; j < 16; ++j)
-        if (c + j < M) {
-          const unsigned long long x = ok ? __ldcg(w + (c + j) * kTileRows) : 0ull;
-          v[j] = uint32_t(x >> 32) == tag ? __uint_as_float(uint32_t(x)) : __uint_as_float(0x7fc00000u);
-        }
-#pragma unroll
-      for (int j = 0; j < 16; ++j)
-        if (c + j < M) acc[c + j] += v[j];
+    for (int j = 0; j < 16; ++j) {  // independent loads, all in flight before the sums
+      const unsigned long long x = (ok && c + j < M) ? __ldcg(w + j * kTileRows) : 0ull;
+      v[j] = uint32_t(x >> 32) == sp.tag ? __uint_as_float(uint32_t(x)) : __uint_as_float(0x7fc00000u);
     }
+#pragma unroll
+    for (int j = 0; j < 16; ++j) a[j] += v[j];
   }
 }
 
@@ -199,15 +247,15 @@ __device__ void split_finish(float (&acc)[MPAD], int M, int tile, int upt, int64
 //   void load_b(uint8_t* dst, int kc, uint64_t* bar, uint64_t policy) const    4 column blocks
 //   void prefetch_l2(int u0, int u1) const
 //   void prologue()                                  after the dependency wait (all threads)
-//   void finish(BatchCtl&, uint8_t* xbuf, int tile, int row, float (&acc)[MPAD], int in_piece, bool ok)
-//                                                    the 128 epilogue threads, per tile piece
+//   void finish(BatchCtl&, uint8_t* xbuf, int tile, int row, uint32_t tsum, bool ok)
+//                                                    the 128 epilogue threads, per tile piece (its sums:
+//                                                    MPAD TMEM columns of this thread's lane at tsum)
 template <class Shape, class Op>
 __device__ void batch_run(Op& op, uint8_t* smem_raw, const Scratch& sc) {
   constexpr int S = Shape::kStages, MP = Shape::kMpad;
   constexpr int UPT = Op::kUnitsPerTile;
   uint8_t* smem = align1024(smem_raw);
   BatchCtl& ctl = *reinterpret_cast<BatchCtl*>(smem + Shape::kOffCtl);
-  uint8_t* halves = smem + Shape::kOffHalf;
   auto stage = [&](int s) { return smem + size_t(s) * Shape::kStageBytes; };
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
   const int64_t total = int64_t(UPT) * Op::kTiles, grid = gridDim.x;
@@ -215,6 +263,7 @@ __device__ void batch_run(Op& op, uint8_t* smem_raw, const Scratch& sc) {
   const int n = int(int64_t(blockIdx.x + 1) * total / grid) - u0;
   volatile uint32_t* abort = &ctl.abort;
   constexpr uint32_t kATx = Shape::kABytes + Shape::kScaleBytes;
+  constexpr uint32_t kIdesc = Op::kF16 ? umma_idesc_f16(kTileRows, MP) : umma_idesc_bf16(kTileRows, MP);
 
   G4_STAMP(sc, 0);
   if (tid == 0) {
@@ -223,11 +272,11 @@ __device__ void batch_run(Op& op, uint8_t* smem_raw, const Scratch& sc) {
       mbar_init(&ctl.full_b[i], 1);
       mbar_init(&ctl.empty[i], 1);
     }
-    for (int i = 0; i < 2; ++i) {
+    for (int i = 0; i < Shape::kAHalves; ++i) {
       mbar_init(&ctl.hfull[i], kDqWarps);  // every dequantisation warp wrote its rows
       mbar_init(&ctl.hempty[i], 1);        // the half's MMAs completed
     }
-    for (int i = 0; i < 4; ++i) {
+    for (int i = 0; i < Shape::kTSlots; ++i) {
       mbar_init(&ctl.done[i], 1);    // the unit's MMAs completed
       mbar_init(&ctl.tempty[i], 4);  // the epilogue warps read the unit's accumulator
     }
@@ -292,32 +341,45 @@ __device__ void batch_run(Op& op, uint8_t* smem_raw, const Scratch& sc) {
     __syncwarp();
   } else if (warp >= kWDq0) {
     // ---------------------------------------------------------------- dequantisation
-    // thread (sub, r): row r, K elements [64 sub, 64 sub + 64) of each half (one column block of
-    // the half's bf16 rows: two 16-byte chunks of codes, four block scales)
-    const int dq = tid - kWDq0 * 32, r = dq & 127, sub = dq >> 7;
+    // Warp w writes TMEM lane quarter w % 4: thread (row, sub), row = 32 (w % 4) + lane, expands K
+    // elements [64 sub, 64 sub + 64) of each half unit (two 16-byte chunks of codes, four block
+    // scales) into 32 TMEM columns of the half's slot in the A ring.
+    const int quarter = warp & 3, r = quarter * 32 + lane, sub = (warp - kWDq0) >> 2;
+    const uint32_t a_lane = tbase + (uint32_t(quarter * 32) << 16) + Shape::kColA + uint32_t(sub * 32);
     bool ok = true;
     for (int i = 0; i < n; ++i) {
       const int s = i % S;
       if (ok) ok = mbar_wait_or_abort(&ctl.full_a[s], uint32_t((i / S) & 1), abort, sc.err);
       const uint8_t* a4 = stage(s);
       for (int h = 0; h < 2; ++h) {
-        if (ok && i > 0) ok = mbar_wait_or_abort(&ctl.hempty[h], uint32_t((i - 1) & 1), abort, sc.err);
+        const int q = 2 * i + h, slot = q % Shape::kAHalves, use = q / Shape::kAHalves;
+        if (ok && use > 0) ok = mbar_wait_or_abort(&ctl.hempty[slot], uint32_t((use - 1) & 1), abort, sc.err);
+        tc_fence_after();  // the slot's previous MMAs (complete) before this thread's TMEM stores
+        if (warp == kWDq0 && lane == 0) G4_UNIT_STAMP(sc, h == 0 ? 4 : 6, i);
         if (ok) {
           const int c0 = 4 * h + 2 * sub;  // code chunks c0, c0 + 1 (32 elements each)
           const uint4 q0 = *reinterpret_cast<const uint4*>(a4 + r * 128 + (((c0) ^ (r & 7)) << 4));
           const uint4 q1 = *reinterpret_cast<const uint4*>(a4 + r * 128 + (((c0 + 1) ^ (r & 7)) << 4));
           const uint32_t sw = *reinterpret_cast<const uint32_t*>(a4 + Shape::kABytes + r * 16 + 8 * h + 4 * sub);
           if (sw & 0x80808080u) atomicOr(sc.err, kErrNegativeScale);
-          uint8_t* dst = halves + h * Shape::kHalfBytes + sub * (Shape::kHalfBytes / 2) + r * 128;
           const uint32_t w[8] = {q0.x, q0.y, q0.z, q0.w, q1.x, q1.y, q1.z, q1.w};
+          uint32_t o[32];
 #pragma unroll
-          for (int j = 0; j < 8; ++j)  // elements 8j .. 8j + 7 of the column block: block j / 2
-            *reinterpret_cast<uint4*>(dst + ((j ^ (r & 7)) << 4)) = dequant8_bf16(w[j], (sw >> (8 * (j / 2))) & 0xffu);
-          asm volatile("fence.proxy.async.shared::cta;" ::: "memory");  // the tensor cores read them
+          for (int j = 0; j < 8; ++j) {  // elements 8j .. 8j + 7: block j / 2, columns 4j .. 4j + 3
+            const uint4 v = Op::kF16 ? dequant8_f16(w[j], (sw >> (8 * (j / 2))) & 0xffu)
+                                     : dequant8_bf16(w[j], (sw >> (8 * (j / 2))) & 0xffu);
+            o[4 * j] = v.x;
+            o[4 * j + 1] = v.y;
+            o[4 * j + 2] = v.z;
+            o[4 * j + 3] = v.w;
+          }
+          tmem_st32(a_lane + uint32_t(slot * 64), o);
+          tmem_st_wait();
         }
+        tc_fence_before();
         __syncwarp();
-        if (lane == 0) mbar_arrive(&ctl.hfull[h]);
-        if (h == 1 && warp == kWDq0 && lane == 0) G4_UNIT_STAMP(sc, 1, i);
+        if (lane == 0) mbar_arrive(&ctl.hfull[slot]);
+        if (warp == kWDq0 && lane == 0) G4_UNIT_STAMP(sc, h == 1 ? 1 : 5, i);
       }
     }
   } else if (warp == kWRelay) {
@@ -328,9 +390,10 @@ __device__ void batch_run(Op& op, uint8_t* smem_raw, const Scratch& sc) {
     for (int i = 0; i < n && !stop; ++i) {
       const int s = i % S, t = i % Shape::kTSlots;
       for (int h = 0; h < 2; ++h) {
+        const int q = 2 * i + h, slot = q % Shape::kAHalves;
         bool bad = false;
         if (lane == 0) {
-          bad = !mbar_wait_or_abort(&ctl.hfull[h], uint32_t(i & 1), abort, sc.err);
+          bad = !mbar_wait_or_abort(&ctl.hfull[slot], uint32_t((q / Shape::kAHalves) & 1), abort, sc.err);
           if (!bad && h == 0) bad = !mbar_wait_or_abort(&ctl.full_b[s], uint32_t((i / S) & 1), abort, sc.err);
           if (!bad && h == 0 && i >= Shape::kTSlots)
             bad = !mbar_wait_or_abort(&ctl.tempty[t], uint32_t(((i / Shape::kTSlots) - 1) & 1), abort, sc.err);
@@ -357,17 +420,17 @@ __device__ void batch_run(Op& op, uint8_t* smem_raw, const Scratch& sc) {
         }
         tc_fence_after();
         if (lane == 0) {
+          const int slot = (2 * i + h) % Shape::kAHalves;
           const uint32_t d = tbase + uint32_t(t) * MP;
-          const uint32_t a0 = smem_u32(halves + h * Shape::kHalfBytes);
+          const uint32_t a0 = tbase + Shape::kColA + uint32_t(slot * 64);
           const uint32_t b0 = smem_u32(stage(s) + kATx) + uint32_t(2 * h) * Shape::kBColBytes;
 #pragma unroll
-          for (int j = 0; j < 8; ++j) {  // K = 16 each: column block j / 4, 32 bytes per step inside it
+          for (int j = 0; j < 8; ++j) {  // K = 16 each: A 8 TMEM columns; B column block j / 4, 32 bytes a step
             const uint32_t cb = j / 4, kk = j % 4;
-            umma_bf16(d, umma_desc_sw128(a0 + cb * uint32_t(Shape::kHalfBytes / 2) + kk * 32u),
-                      umma_desc_sw128(b0 + cb * uint32_t(Shape::kBColBytes) + kk * 32u), Shape::kIdesc,
-                      uint32_t(!(h == 0 && j == 0)));
+            umma_16bit_ta(d, a0 + uint32_t(8 * j), umma_desc_sw128(b0 + cb * uint32_t(Shape::kBColBytes) + kk * 32u),
+                          kIdesc, uint32_t(!(h == 0 && j == 0)));
           }
-          umma_commit(&ctl.hempty[h]);
+          umma_commit(&ctl.hempty[slot]);
           if (h == 1) {
             umma_commit(&ctl.empty[s]);
             umma_commit(&ctl.done[t]);
@@ -389,34 +452,39 @@ __device__ void batch_run(Op& op, uint8_t* smem_raw, const Scratch& sc) {
     const int row = quarter * 32 + lane;
     const uint32_t lane_addr = uint32_t(quarter * 32) << 16;
     uint8_t* xbuf = smem + Shape::kOffX;
+    const uint32_t tsum = tbase + lane_addr + Shape::kColSum;
     bool ok = true;
     int in_piece = 0;
-    float acc[MP];
-#pragma unroll
-    for (int j = 0; j < MP; ++j) acc[j] = 0.f;
     for (int i = 0; i < n; ++i) {
       const int u = u0 + i, tile = u / UPT, kc = u % UPT, t = i % Shape::kTSlots;
       ++in_piece;
       if (ok) ok = mbar_wait_or_abort(&ctl.done[t], uint32_t((i / Shape::kTSlots) & 1), abort, sc.err);
       tc_fence_after();
+      // running sum of the piece += this unit, 16 tokens at a time (f32, round to nearest)
 #pragma unroll
-      for (int c = 0; c < MP / 16; ++c) {
-        float part[16];
-        if (ok) tmem_ld16(tbase + lane_addr + uint32_t(t * MP + 16 * c), part);
-        if (ok) tmem_ld_wait();
+      for (int c = 0; c < MP; c += 16) {
+        float part[16], sum[16];
+        if (ok) {
+          tmem_ld16(tbase + lane_addr + uint32_t(t * MP + c), part);
+          if (in_piece > 1) tmem_ld16(tsum + uint32_t(c), sum);
+          tmem_ld_wait();
 #pragma unroll
-        for (int j = 0; j < 16; ++j) acc[16 * c + j] = ok ? acc[16 * c + j] + part[j] : __uint_as_float(0x7fc00000u);
+          for (int j = 0; j < 16; ++j) sum[j] = in_piece > 1 ? sum[j] + part[j] : part[j];
+          uint32_t bits[16];
+#pragma unroll
+          for (int j = 0; j < 16; ++j) bits[j] = __float_as_uint(sum[j]);
+          tmem_st16(tsum + uint32_t(c), bits);
+        }
       }
+      if (ok) tmem_st_wait();
       tc_fence_before();
       __syncwarp();
       if (lane == 0) mbar_arrive(&ctl.tempty[t]);
       if (row == 0) G4_UNIT_STAMP(sc, 3, i);
       if (!(kc == UPT - 1 || i == n - 1)) continue;
-      op.finish(ctl, xbuf, tile, row, acc, in_piece, ok);
+      op.finish(ctl, xbuf, tile, row, tsum, ok);
       if (row == 0) G4_STAMP_T(sc, 5);
       in_piece = 0;
-#pragma unroll
-      for (int j = 0; j < MP; ++j) acc[j] = 0.f;
     }
   }
 
@@ -433,10 +501,14 @@ __device__ void batch_run(Op& op, uint8_t* smem_raw, const Scratch& sc) {
 // ---------------------------------------------------------------------------------------
 // The ops
 
-// h[m] = bf16(RMSNorm(residual[m]) * gamma_pre): one CTA per token, 240 threads x 16 elements.
-// Thread 0 of CTA 0 also counts the call (the epoch of its split-K words and tile sums).
+// h[m] = bf16(RMSNorm(residual[m]) * gamma_pre): one CTA per token, 240 threads x 16 elements,
+// stored as f16 times 2^k, k per token so that max |h| 2^k lies in [2^14, 2^15): every element of
+// at least max |h| 2^-31 is exact in f16, and the up/gate sums are multiplied back by 2^-k
+// (batch_unscale) before their bf16 rounding. Thread 0 of CTA 0 also counts the call (the epoch
+// of the split-K words and tile sums).
 __global__ void __launch_bounds__(256) ffn_batch_norm_kernel(FfnArgs a, Scratch sc) {
   __shared__ double red[8];
+  __shared__ float wmax[8];
   const int m = blockIdx.x, g = threadIdx.x;
   const bool have = g < kH / 16;
   uint4 raw[4];
@@ -447,12 +519,33 @@ __global__ void __launch_bounds__(256) ffn_batch_norm_kernel(FfnArgs a, Scratch 
   if (have) load_group_cg(a.residual + size_t(m) * kH, g, raw);
   const double ss = have ? sum_squares_bf16x16(raw[0], raw[1]) : 0.0;
   const float inv = rms_inverse(block_sum_d(ss, red), kH);
+  float v[16];
+  float amax = 0.f;
   if (have) {
-    float v[16];
     rms_apply16(raw, inv, v);
+#pragma unroll
+    for (int j = 0; j < 16; ++j) amax = fmaxf(amax, fabsf(v[j]));  // NaN-free here: a NaN max is caught below
+#pragma unroll
+    for (int j = 0; j < 16; ++j)
+      if (v[j] != v[j]) amax = __uint_as_float(0x7f800000u);
+  }
+  amax = warp_max(amax);
+  if ((g & 31) == 0) wmax[g >> 5] = amax;
+  __syncthreads();
+  amax = wmax[0];
+#pragma unroll
+  for (int w = 1; w < 8; ++w) amax = fmaxf(amax, wmax[w]);
+  int k = amax > 0.f ? 14 - block_exponent(amax) : 0;
+  k = k > 120 ? 120 : (k < -120 ? -120 : k);
+  if (g == 0) sc.batch_unscale[m] = pow2f(-k);
+  if (have) {
+    const float up = pow2f(k);
     uint32_t w[8];
 #pragma unroll
-    for (int j = 0; j < 8; ++j) w[j] = (__float_as_uint(v[2 * j]) >> 16) | (__float_as_uint(v[2 * j + 1]) & 0xffff0000u);
+    for (int j = 0; j < 8; ++j) {
+      const __half2 h = __floats2half2_rn(v[2 * j] * up, v[2 * j + 1] * up);
+      w[j] = *reinterpret_cast<const uint32_t*>(&h);
+    }
     uint4* dst = reinterpret_cast<uint4*>(sc.batch_h + size_t(m) * kH + 16 * g);
     dst[0] = make_uint4(w[0], w[1], w[2], w[3]);
     dst[1] = make_uint4(w[4], w[5], w[6], w[7]);
@@ -461,7 +554,7 @@ __global__ void __launch_bounds__(256) ffn_batch_norm_kernel(FfnArgs a, Scratch 
 
 struct BatchMaps {
   CUtensorMap a, a2, s, s2;  // weights: up (or down) codes, gate codes, their block scales
-  CUtensorMap b;             // activation rows [M, K] bf16, box {64, MPAD}
+  CUtensorMap b;             // activation rows [M, K] (up/gate: f16, down: bf16), box {64, MPAD}
 };
 
 template <int MPAD>
@@ -469,6 +562,7 @@ struct BatchUpGateOp {
   using Shape = BatchShape<MPAD>;
   static constexpr int kUnitsPerTile = kH / kUnitK;  // 15
   static constexpr int kTiles = kL / 64;             // 64 up + 64 gate rows per tile
+  static constexpr bool kF16 = true;                 // f16 weights x the scaled f16 h
   const BatchMaps* maps;
   FfnArgs a;
   Scratch sc;
@@ -504,28 +598,41 @@ struct BatchUpGateOp {
     tag = (__ldcg(sc.counters + kBatchEpoch) << 1) | 0u;
   }
   // GloballyScaled(nn.Linear): bf16(bf16(h @ W.T) * g) (generate_references.py:358-372), then the
-  // down input bf16(bf16(gelu_tanh(gate)) * up) (gemma4.py:197), token by token.
-  __device__ void finish(BatchCtl&, uint8_t* xbuf, int tile, int row, float (&acc)[MPAD], int, bool ok) {
-    bool publish_only = false;
-    split_finish<MPAD>(acc, M, tile, kUnitsPerTile, int64_t(kUnitsPerTile) * kTiles, row, tag, sc.batch_words, ok,
-                       sc.err, publish_only);
-    if (publish_only) return;  // CTA-uniform for the tile: no barrier is skipped by part of the warps
-    uint16_t* gel = reinterpret_cast<uint16_t*>(xbuf);  // [token][64]
-    if (row >= 64) {
+  // down input bf16(bf16(gelu_tanh(gate)) * up) (gemma4.py:197), 16 tokens at a time: the gate rows
+  // leave their bf16 values in shared memory, all 128 threads apply GeGLU's gelu to them, and the up
+  // rows form the products.
+  __device__ void finish(BatchCtl&, uint8_t* xbuf, int tile, int row, uint32_t tsum, bool ok) {
+    const SplitPiece sp = split_begin<MPAD>(tile, kUnitsPerTile, int64_t(kUnitsPerTile) * kTiles, row, M, tsum, tag,
+                                            sc.batch_words, ok, sc.err);
+    if (sp.publish) return;  // CTA-uniform for the tile: no barrier is skipped by part of the warps
+    uint16_t* gel = reinterpret_cast<uint16_t*>(xbuf);  // [16 tokens][64]
+#pragma unroll 1
+    for (int c = 0; c < MPAD && c < M; c += 16) {
+      float a[16];
+      split_chunk(sp, c, M, row, tsum, ok, a);
 #pragma unroll
-      for (int m = 0; m < MPAD; ++m)
-        if (m < M) gel[m * 64 + row - 64] = f32_to_bf16(gelu_tanh(bf16_round(bf16_round(acc[m]) * g_gate)));
-    }
-    named_bar(kBEpiBarrier, 128);
-    if (row < 64) {
+      for (int j = 0; j < 16; ++j) a[j] *= c + j < M ? __ldcg(sc.batch_unscale + c + j) : 1.f;  // exact: 2^-k
+      if (row >= 64) {
 #pragma unroll
-      for (int m = 0; m < MPAD; ++m)
-        if (m < M) {
-          const float up = bf16_round(bf16_round(acc[m]) * g_up);
-          sc.act[size_t(m) * kL + tile * 64 + row] = f32_to_bf16(bf16_to_f32(gel[m * 64 + row]) * up);
-        }
+        for (int j = 0; j < 16; ++j) gel[j * 64 + row - 64] = f32_to_bf16(bf16_round(a[j]) * g_gate);
+      }
+      named_bar(kBEpiBarrier, 128);
+#pragma unroll
+      for (int q = 0; q < 8; ++q) {  // 1024 gate values over 128 threads
+        const int e = q * 128 + row;
+        gel[e] = f32_to_bf16(gelu_tanh(bf16_to_f32(gel[e])));
+      }
+      named_bar(kBEpiBarrier, 128);
+      if (row < 64) {
+#pragma unroll
+        for (int j = 0; j < 16; ++j)
+          if (c + j < M) {
+            const float up = bf16_round(bf16_round(a[j]) * g_up);
+            sc.act[size_t(c + j) * kL + tile * 64 + row] = f32_to_bf16(bf16_to_f32(gel[j * 64 + row]) * up);
+          }
+      }
+      named_bar(kBEpiBarrier, 128);  // the exchange buffer is free for the next chunk
     }
-    named_bar(kBEpiBarrier, 128);  // the exchange buffer is free for the next tile
   }
 };
 
@@ -534,6 +641,7 @@ struct BatchDownOp {
   using Shape = BatchShape<MPAD>;
   static constexpr int kUnitsPerTile = kL / kUnitK;  // 60
   static constexpr int kTiles = kH / kTileRows;      // 30
+  static constexpr bool kF16 = false;                // bf16 weights x the bf16 GeGLU activation
   const BatchMaps* maps;
   FfnArgs a;
   Scratch sc;
@@ -568,19 +676,23 @@ struct BatchDownOp {
   }
   // y[m] = bf16(bf16(h @ W.T) * g) for the tile's rows; kept (bf16) in batch_y for the residual
   // tail, with each token's sum of squares over the tile published as two epoch-tagged words.
-  __device__ void finish(BatchCtl& ctl, uint8_t*, int tile, int row, float (&acc)[MPAD], int, bool ok) {
-    bool publish_only = false;
-    split_finish<MPAD>(acc, M, tile, kUnitsPerTile, int64_t(kUnitsPerTile) * kTiles, row, tag, sc.batch_words, ok,
-                       sc.err, publish_only);
-    if (publish_only) return;
+  __device__ void finish(BatchCtl& ctl, uint8_t*, int tile, int row, uint32_t tsum, bool ok) {
+    const SplitPiece sp = split_begin<MPAD>(tile, kUnitsPerTile, int64_t(kUnitsPerTile) * kTiles, row, M, tsum, tag,
+                                            sc.batch_words, ok, sc.err);
+    if (sp.publish) return;
     const int lane = threadIdx.x & 31, quarter = (threadIdx.x >> 5) & 3;
+#pragma unroll 1
+    for (int c = 0; c < MPAD && c < M; c += 16) {
+      float a[16];
+      split_chunk(sp, c, M, row, tsum, ok, a);
 #pragma unroll
-    for (int m = 0; m < MPAD; ++m) {
-      if (m >= M) continue;
-      const float y = bf16_round(bf16_round(acc[m]) * g_down);
-      sc.batch_y[size_t(m) * kH + tile * kTileRows + row] = f32_to_bf16(y);
-      const double s = warp_sum_d(double(y) * double(y));
-      if (lane == 0) ctl.wsum[quarter][m] = s;
+      for (int j = 0; j < 16; ++j) {
+        if (c + j >= M) continue;  // warp-uniform
+        const float y = bf16_round(bf16_round(a[j]) * g_down);
+        sc.batch_y[size_t(c + j) * kH + tile * kTileRows + row] = f32_to_bf16(y);
+        const double s = warp_sum_d(double(y) * double(y));
+        if (lane == 0) ctl.wsum[quarter][c + j] = s;
+      }
     }
     named_bar(kBEpiBarrier, 128);
     if (row < M) {  // quarters in row order: warp 3 holds rows 96-127
@@ -623,7 +735,7 @@ __global__ void __launch_bounds__(kBThreads, 1) ffn_batch_down_kernel(const __gr
   const int nfin = ctl.fin_n < kBMaxFin ? ctl.fin_n : kBMaxFin;
   if (nfin == 0) return;  // CTA-uniform
   constexpr int kT = BatchDownOp<MPAD>::kTiles;
-  double* ss = reinterpret_cast<double*>(base + Shape::kOffHalf);  // [tile][token] (the halves are free)
+  double* ss = reinterpret_cast<double*>(base);  // [tile][token] (the stages are free)
   for (int w = threadIdx.x; w < kT * M; w += kBThreads) {
     const int t = w / M, m = w % M;
     const unsigned long long* p = sc.batch_ss + (size_t(t) * kBatchMax + m) * 2;
@@ -710,7 +822,7 @@ cudaError_t launch_batch_t(const FfnArgs& a, int M, const LaunchEnv& env) {
     if ((e = env.maps->u8(a.down_packed, kL / 2, kH, 128, kTileRows, true, &dn.a))) return e;
     if ((e = env.maps->u8(a.down_scale, kL / 16, kH, 16, kTileRows, false, &dn.s))) return e;
   }
-  if ((e = env.maps->bf16(env.sc.batch_h, kH, uint64_t(M), 64, MPAD, &ug.b))) return e;
+  if ((e = env.maps->bf16(env.sc.batch_h, kH, uint64_t(M), 64, MPAD, &ug.b, /*half=*/true))) return e;
   if ((e = env.maps->bf16(env.sc.act, kL, uint64_t(M), 64, MPAD, &dn.b))) return e;
   const int gu = env.sm_count < BatchUpGateOp<MPAD>::kUnitsPerTile * BatchUpGateOp<MPAD>::kTiles
                      ? env.sm_count

@@ -64,11 +64,13 @@ struct Scratch {
   unsigned long long* tile_ss;  // per output tile: sum of squares of its bf16 rows, as two words
                                 // (epoch << 32 | low / high half of the f64), kTileSsCount tiles
   uint64_t* trace;     // per-CTA phase timestamps (profiling builds only; null otherwise)
-  // the token-batched feed-forward (M > 1): its normalised input h [kBatchMax][H], the down
+  // the token-batched feed-forward (M > 1): its normalised input h [kBatchMax][H] (f16, scaled by a
+  // power of two per token), the down
   // projection's bf16 rows [kBatchMax][H], split-K words [CTA][kBatchMax tokens][128 rows] and the
   // per (tile, token) sums of squares of the residual tail (two words each, kBatchSsWords)
   uint16_t* batch_h;
   uint16_t* batch_y;
+  float* batch_unscale;  // [kBatchMax]: 2^-k of each token's f16 scaling of h
   unsigned long long* batch_words;
   unsigned long long* batch_ss;
 };

@@ -148,10 +148,10 @@ class TmapCache {
   // Row-major uint8 matrix [rows, cols] (fp8 codes, e4m3 scales), box {box_cols, box_rows}.
   cudaError_t u8(const void* base, uint64_t cols, uint64_t rows, uint32_t box_cols, uint32_t box_rows, bool swizzle128,
                  CUtensorMap* out);
-  // Row-major bf16 matrix [rows, cols], box {box_cols, box_rows}, 128-byte swizzle (box_cols = 64):
-  // rows past the end read as zeros.
+  // Row-major bf16 (or, half = true, f16) matrix [rows, cols], box {box_cols, box_rows}, 128-byte
+  // swizzle (box_cols = 64): rows past the end read as zeros.
   cudaError_t bf16(const void* base, uint64_t cols, uint64_t rows, uint32_t box_cols, uint32_t box_rows,
-                   CUtensorMap* out);
+                   CUtensorMap* out, bool half = false);
   // KV ring cache [ring, heads, dim] bf16 as a 3-D tensor (dim, head, slot), box {dim, 1, box_slots}:
   // one load brings box_slots rows of one head.
   cudaError_t kv(const void* base, uint64_t ring, uint32_t heads, uint32_t dim, uint32_t box_slots, CUtensorMap* out);

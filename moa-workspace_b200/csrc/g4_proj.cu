@@ -1339,9 +1339,9 @@ cudaError_t TmapCache::u8(const void* base, uint64_t cols, uint64_t rows, uint32
 }
 
 cudaError_t TmapCache::bf16(const void* base, uint64_t cols, uint64_t rows, uint32_t box_cols, uint32_t box_rows,
-                            CUtensorMap* out) {
+                            CUtensorMap* out, bool half) {
   const uint64_t key = (cols << 34) ^ (rows << 12) ^ (uint64_t(box_cols) << 4) ^ (uint64_t(box_rows) << 1) ^
-                       (uint64_t(1) << 62);
+                       (uint64_t(1) << 62) ^ (uint64_t(half) << 61);
   if (const CUtensorMap* m = find(base, key)) {
     *out = *m;
     return cudaSuccess;
@@ -1352,8 +1352,9 @@ cudaError_t TmapCache::bf16(const void* base, uint64_t cols, uint64_t rows, uint
   const cuuint64_t gstride[1] = {cols * 2};
   const cuuint32_t box[2] = {box_cols, box_rows};
   const cuuint32_t estride[2] = {1, 1};
-  const CUresult r = enc(out, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, const_cast<void*>(base), gdim, gstride, box,
-                         estride, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+  const CUresult r = enc(out, half ? CU_TENSOR_MAP_DATA_TYPE_FLOAT16 : CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2,
+                         const_cast<void*>(base), gdim, gstride, box, estride, CU_TENSOR_MAP_INTERLEAVE_NONE,
+                         CU_TENSOR_MAP_SWIZZLE_128B,
                          CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
   if (r != CUDA_SUCCESS) return cudaErrorInvalidValue;
   put(base, key, *out);
