@@ -90,11 +90,9 @@ g4_status g4_ctx_create(int device, g4_ctx** out) {
   const size_t off_partials = off_counters + g4::kCounterCount * sizeof(uint32_t);
   const size_t off_act = off_partials + g4::kPartialFloats * sizeof(float);
   const size_t off_ss = off_act + size_t(64) * g4::kL * sizeof(uint16_t);
-  const size_t off_bh = off_ss + g4::kTileSsBytes;  // batched feed-forward: h | y | split-K words | sums
-  const size_t off_by = off_bh + size_t(g4::kBatchMax) * g4::kH * sizeof(uint16_t);
-  const size_t off_bw = off_by + size_t(g4::kBatchMax) * g4::kH * sizeof(uint16_t);
-  const size_t off_bs = off_bw + g4::batch_words_count(ctx->sm_count) * sizeof(unsigned long long);
-  const size_t off_bu = off_bs + g4::kBatchSsWords * sizeof(unsigned long long);
+  const size_t off_bh = off_ss + g4::kTileSsBytes;  // batched feed-forward: h | split-K words | unscale
+  const size_t off_bw = off_bh + size_t(g4::kBatchMax) * g4::kH * sizeof(uint16_t);
+  const size_t off_bu = off_bw + g4::batch_words_count(ctx->sm_count) * sizeof(unsigned long long);
   const size_t off_trace = off_bu + size_t(g4::kBatchMax) * sizeof(float);
 #ifdef G4_TRACE
   const size_t total = off_trace + size_t(65536 + 4096 * 32 * 8) * sizeof(uint64_t);
@@ -121,9 +119,7 @@ g4_status g4_ctx_create(int device, g4_ctx** out) {
   ctx->act_bytes = off_ss - off_act;
   ctx->sc.tile_ss = reinterpret_cast<unsigned long long*>(base + off_ss);
   ctx->sc.batch_h = reinterpret_cast<uint16_t*>(base + off_bh);
-  ctx->sc.batch_y = reinterpret_cast<uint16_t*>(base + off_by);
   ctx->sc.batch_words = reinterpret_cast<unsigned long long*>(base + off_bw);
-  ctx->sc.batch_ss = reinterpret_cast<unsigned long long*>(base + off_bs);
   ctx->sc.batch_unscale = reinterpret_cast<float*>(base + off_bu);
   ctx->batch_ok = g4::batch_geometry_fits(ctx->sm_count);
 #ifdef G4_TRACE

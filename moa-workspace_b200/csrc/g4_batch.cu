@@ -35,17 +35,12 @@ constexpr int kWProducer = 0, kWIssuer = 1, kWRelay = 2, kWDq0 = 7, kDqWarps = 8
 constexpr int kBIssueBarrier = 2;  // issuer + relay (64 threads)
 constexpr int kBEpiBarrier = 1;    // the four epilogue warps
 constexpr int kBMaxStages = 8;
-constexpr int kBMaxFin = 2;        // tiles one down CTA may finish (checked at set-up)
 
 struct BatchCtl {
   uint64_t full_a[kBMaxStages], full_b[kBMaxStages], empty[kBMaxStages];
   uint64_t hfull[3], hempty[3], done[8], tempty[8], drain;
   uint32_t tmem_base;
   uint32_t abort;
-  int fin_tile[kBMaxFin];
-  int fin_n;
-  float inv[kBatchMax];
-  double wsum[4][kBatchMax];  // down: each epilogue warp's sums of squares per token
 };
 
 // Profiling builds: per-unit timestamps of CTA 0 at trace[3000 + 64 k + i] (k: 0 producer issued,
@@ -73,18 +68,25 @@ struct BatchShape {
   static constexpr size_t kXBytes = size_t(16) * 64 * 2;  // up/gate: bf16 gate, then gelu [16 tokens][64]
   static constexpr int kStagesFit = int((227 * 1024 - kXBytes - sizeof(BatchCtl) - 1024) / kStageBytes);
   static constexpr int kStages = kStagesFit < kBMaxStages ? kStagesFit : kBMaxStages;
-  // TMEM (512 columns): kTSlots accumulators of MPAD columns (one per unit in flight), each row's
-  // running sum of its tile piece (MPAD columns), then the dequantised A operand: a ring of
-  // kAHalves half units, 64 columns each (128 rows x 128 K 16-bit values, two per column).
-  static constexpr int kTSlots = MPAD <= 32 ? 8 : 4;
-  static constexpr uint32_t kColSum = uint32_t(kTSlots) * MPAD;
+  // TMEM (512 columns): kTSlots unit accumulators (one per unit in flight) of kChains x MPAD
+  // columns, each row's running sum of its tile piece (MPAD columns), then the dequantised A
+  // operand: a ring of kAHalves half units, 64 columns each (128 rows x 128 K 16-bit values, two
+  // per column). A unit's 16 K steps go round-robin to kChains independent accumulators: MMAs
+  // that accumulate into one D run back to back at the tensor cores' latency, independent ones
+  // overlap (one chain of 16 held a unit to about 1 us). The same count for every MPAD keeps a
+  // token's result independent of the batch it came in.
+  static constexpr int kChains = 2;
+  static constexpr int kTSlotsFit = (512 - 3 * 64 - MPAD) / (kChains * MPAD);
+  static constexpr int kTSlots = kTSlotsFit < 8 ? kTSlotsFit : 8;
+  static constexpr uint32_t kSlotCols = uint32_t(kChains) * MPAD;
+  static constexpr uint32_t kColSum = uint32_t(kTSlots) * kSlotCols;
   static constexpr uint32_t kColA = (kColSum + MPAD + 31) / 32 * 32;
   static constexpr int kAHalves = 3;
   static constexpr uint32_t kTmemCols = 512;
   static constexpr size_t kOffX = size_t(kStages) * kStageBytes;
   static constexpr size_t kOffCtl = kOffX + kXBytes;
   static constexpr size_t kSmemBytes = kOffCtl + sizeof(BatchCtl) + 1024;
-  static_assert(kColA + kAHalves * 64 <= kTmemCols, "TMEM budget");
+  static_assert(kColA + kAHalves * 64 <= kTmemCols && kTSlots >= 2, "TMEM budget");
   static_assert(kStages >= 3, "pipeline depth");
   static_assert(MPAD % 16 == 0 && MPAD <= kBatchMax, "N of the MMA");
   static_assert(kStages <= kBMaxStages, "barrier arrays");
@@ -282,7 +284,6 @@ __device__ void batch_run(Op& op, uint8_t* smem_raw, const Scratch& sc) {
     }
     mbar_init(&ctl.drain, 1);
     ctl.abort = 0;
-    ctl.fin_n = 0;
     fence_mbar_init();
   }
   __syncwarp();
@@ -421,14 +422,16 @@ __device__ void batch_run(Op& op, uint8_t* smem_raw, const Scratch& sc) {
         tc_fence_after();
         if (lane == 0) {
           const int slot = (2 * i + h) % Shape::kAHalves;
-          const uint32_t d = tbase + uint32_t(t) * MP;
+          const uint32_t d = tbase + uint32_t(t) * Shape::kSlotCols;
           const uint32_t a0 = tbase + Shape::kColA + uint32_t(slot * 64);
           const uint32_t b0 = smem_u32(stage(s) + kATx) + uint32_t(2 * h) * Shape::kBColBytes;
 #pragma unroll
           for (int j = 0; j < 8; ++j) {  // K = 16 each: A 8 TMEM columns; B column block j / 4, 32 bytes a step
             const uint32_t cb = j / 4, kk = j % 4;
-            umma_16bit_ta(d, a0 + uint32_t(8 * j), umma_desc_sw128(b0 + cb * uint32_t(Shape::kBColBytes) + kk * 32u),
-                          kIdesc, uint32_t(!(h == 0 && j == 0)));
+            const int step = 8 * h + j, chain = step % Shape::kChains;
+            umma_16bit_ta(d + uint32_t(chain * MP), a0 + uint32_t(8 * j),
+                          umma_desc_sw128(b0 + cb * uint32_t(Shape::kBColBytes) + kk * 32u), kIdesc,
+                          uint32_t(step >= Shape::kChains));
           }
           umma_commit(&ctl.hempty[slot]);
           if (h == 1) {
@@ -460,14 +463,24 @@ __device__ void batch_run(Op& op, uint8_t* smem_raw, const Scratch& sc) {
       ++in_piece;
       if (ok) ok = mbar_wait_or_abort(&ctl.done[t], uint32_t((i / Shape::kTSlots) & 1), abort, sc.err);
       tc_fence_after();
-      // running sum of the piece += this unit, 16 tokens at a time (f32, round to nearest)
+      // running sum of the piece += this unit (its chains added in order), 16 tokens at a time (f32,
+      // round to nearest)
 #pragma unroll
       for (int c = 0; c < MP; c += 16) {
         float part[16], sum[16];
         if (ok) {
-          tmem_ld16(tbase + lane_addr + uint32_t(t * MP + c), part);
+          const uint32_t slot = tbase + lane_addr + uint32_t(t) * Shape::kSlotCols + uint32_t(c);
+          tmem_ld16(slot, part);
           if (in_piece > 1) tmem_ld16(tsum + uint32_t(c), sum);
           tmem_ld_wait();
+#pragma unroll
+          for (int ch = 1; ch < Shape::kChains; ++ch) {
+            float more[16];
+            tmem_ld16(slot + uint32_t(ch * MP), more);
+            tmem_ld_wait();
+#pragma unroll
+            for (int j = 0; j < 16; ++j) part[j] += more[j];
+          }
 #pragma unroll
           for (int j = 0; j < 16; ++j) sum[j] = in_piece > 1 ? sum[j] + part[j] : part[j];
           uint32_t bits[16];
@@ -674,42 +687,27 @@ struct BatchDownOp {
     epoch = __ldcg(sc.counters + kBatchEpoch);
     tag = (epoch << 1) | 1u;
   }
-  // y[m] = bf16(bf16(h @ W.T) * g) for the tile's rows; kept (bf16) in batch_y for the residual
-  // tail, with each token's sum of squares over the tile published as two epoch-tagged words.
-  __device__ void finish(BatchCtl& ctl, uint8_t*, int tile, int row, uint32_t tsum, bool ok) {
-    const SplitPiece sp = split_begin<MPAD>(tile, kUnitsPerTile, int64_t(kUnitsPerTile) * kTiles, row, M, tsum, tag,
-                                            sc.batch_words, ok, sc.err);
-    if (sp.publish) return;
-    const int lane = threadIdx.x & 31, quarter = (threadIdx.x >> 5) & 3;
-#pragma unroll 1
-    for (int c = 0; c < MPAD && c < M; c += 16) {
-      float a[16];
-      split_chunk(sp, c, M, row, tsum, ok, a);
+  // Every piece (at most two per CTA: the end of one tile and the start of the next) goes out as
+  // epoch-tagged words in the CTA's slot (its piece ordinal); ffn_batch_finalize_kernel adds them.
+  __device__ void finish(BatchCtl&, uint8_t*, int, int row, uint32_t tsum, bool ok) {
+    unsigned long long* w = sc.batch_words + (size_t(blockIdx.x) * 2 + (piece_no < 2 ? piece_no : 1)) * kBatchMax * kTileRows + row;
+    if (piece_no >= 2 && row == 0) atomicOr(sc.err, kErrInternal);  // the launcher keeps runs within two tiles
+    ++piece_no;
+    const unsigned long long tag_bits = static_cast<unsigned long long>(tag) << 32;
 #pragma unroll
-      for (int j = 0; j < 16; ++j) {
-        if (c + j >= M) continue;  // warp-uniform
-        const float y = bf16_round(bf16_round(a[j]) * g_down);
-        sc.batch_y[size_t(c + j) * kH + tile * kTileRows + row] = f32_to_bf16(y);
-        const double s = warp_sum_d(double(y) * double(y));
-        if (lane == 0) ctl.wsum[quarter][c + j] = s;
+    for (int c = 0; c < MPAD; c += 16) {
+      if (c >= M) break;
+      float a[16];
+      if (ok) {
+        tmem_ld16(tsum + uint32_t(c), a);
+        tmem_ld_wait();
       }
+#pragma unroll
+      for (int j = 0; j < 16; ++j)
+        if (c + j < M) w[size_t(c + j) * kTileRows] = tag_bits | (ok ? __float_as_uint(a[j]) : 0x7fc00000u);
     }
-    named_bar(kBEpiBarrier, 128);
-    if (row < M) {  // quarters in row order: warp 3 holds rows 96-127
-      const double sum = ((ctl.wsum[0][row] + ctl.wsum[1][row]) + ctl.wsum[2][row]) + ctl.wsum[3][row];
-      const unsigned long long bits = static_cast<unsigned long long>(__double_as_longlong(sum));
-      const unsigned long long t = static_cast<unsigned long long>(epoch) << 32;
-      unsigned long long* w = sc.batch_ss + (size_t(tile) * kBatchMax + row) * 2;
-      st_relaxed_gpu_u64(w, t | (bits & 0xffffffffull));
-      st_relaxed_gpu_u64(w + 1, t | (bits >> 32));
-    }
-    if (row == 0) {
-      if (ctl.fin_n < kBMaxFin) ctl.fin_tile[ctl.fin_n] = tile;
-      else atomicOr(sc.err, kErrInternal);
-      ctl.fin_n = ctl.fin_n + 1;
-    }
-    named_bar(kBEpiBarrier, 128);
   }
+  int piece_no = 0;
 };
 
 template <int MPAD>
@@ -720,57 +718,92 @@ __global__ void __launch_bounds__(kBThreads, 1) ffn_batch_upgate_kernel(const __
   batch_run<BatchShape<MPAD>>(op, smem, sc);
 }
 
-// After the contraction, the CTAs that finished tiles wait for every tile's per-token sums of
-// squares, then update their rows: residual[m] = bf16(bf16(residual[m] + bf16(y inv_m gamma)) lambda).
 template <int MPAD>
 __global__ void __launch_bounds__(kBThreads, 1) ffn_batch_down_kernel(const __grid_constant__ BatchMaps maps,
                                                                       FfnArgs a, Scratch sc, int M) {
   extern __shared__ __align__(1024) uint8_t smem[];
-  using Shape = BatchShape<MPAD>;
   BatchDownOp<MPAD> op{&maps, a, sc, M};
-  batch_run<Shape>(op, smem, sc);
-  uint8_t* base = align1024(smem);
-  BatchCtl& ctl = *reinterpret_cast<BatchCtl*>(base + Shape::kOffCtl);
+  batch_run<BatchShape<MPAD>>(op, smem, sc);
+}
+
+// The down projection's pieces added per token, then the epilogue of the reference op
+// (FOG/src/ops.rs:201-239): y = bf16(bf16(sum) * g), residual = bf16(bf16(residual +
+// bf16(y inv gamma)) lambda) with inv the RMS statistic of the token's y. One CTA per token; every
+// tile's pieces are added in CTA order, so the result does not depend on timing.
+constexpr int kMaxDownPieces = 6;  // CTAs one down tile may span (checked at set-up)
+constexpr int kFinThreads = 768;  // 5 rows of H per thread: every load of a row in flight at once
+__global__ void __launch_bounds__(kFinThreads) ffn_batch_finalize_kernel(FfnArgs a, Scratch sc, int down_grid) {
+  constexpr int kUpt = kL / kUnitK, kTiles = kH / kTileRows;
+  constexpr int kTotal = kUpt * kTiles;
+  constexpr int kMaxGrid = 1024;
+  constexpr int kRows = kH / kFinThreads;
+  static_assert(kH % kFinThreads == 0, "rows per thread");
+  __shared__ double red[kFinThreads / 32];
+  __shared__ int first_cta[kTiles], last_cta[kTiles];
+  __shared__ uint8_t run_tile[kMaxGrid];  // the tile of each down CTA's first unit
+  const int m = blockIdx.x;
+  for (int t = threadIdx.x; t < kTiles; t += blockDim.x) {
+    first_cta[t] = cta_of_unit(int64_t(t) * kUpt, down_grid, kTotal);
+    last_cta[t] = cta_of_unit(int64_t(t) * kUpt + kUpt - 1, down_grid, kTotal);
+  }
+  for (int c = threadIdx.x; c < down_grid && c < kMaxGrid; c += blockDim.x)
+    run_tile[c] = uint8_t(int(int64_t(c) * kTotal / down_grid) / kUpt);
+  // the epilogue's static operands, then the residual rows (written by earlier kernels), before
+  // the wait on the down kernel
+  float gamma[kRows];
+#pragma unroll
+  for (int q = 0; q < kRows; ++q) gamma[q] = bf16_to_f32(a.post_rms[threadIdx.x + q * kFinThreads]);
   __syncthreads();
-  const int nfin = ctl.fin_n < kBMaxFin ? ctl.fin_n : kBMaxFin;
-  if (nfin == 0) return;  // CTA-uniform
-  constexpr int kT = BatchDownOp<MPAD>::kTiles;
-  double* ss = reinterpret_cast<double*>(base);  // [tile][token] (the stages are free)
-  for (int w = threadIdx.x; w < kT * M; w += kBThreads) {
-    const int t = w / M, m = w % M;
-    const unsigned long long* p = sc.batch_ss + (size_t(t) * kBatchMax + m) * 2;
-    unsigned long long lo = ld_relaxed_gpu_u64(p), hi = ld_relaxed_gpu_u64(p + 1);
-    const uint64_t t0 = globaltimer_ns();
-    while (uint32_t(lo >> 32) != op.epoch || uint32_t(hi >> 32) != op.epoch) {
-      if (globaltimer_ns() - t0 > kWaitLimitNs) {
-        atomicOr(sc.err, kErrWaitTimeout);
-        break;
+  pdl_wait_primary();
+  pdl_launch_dependents();
+  uint16_t* res = a.residual + size_t(m) * kH;
+  uint16_t rbits[kRows];
+#pragma unroll
+  for (int q = 0; q < kRows; ++q) rbits[q] = __ldcg(res + threadIdx.x + q * kFinThreads);
+  const uint32_t tag = (__ldcg(sc.counters + kBatchEpoch) << 1) | 1u;
+  const float g = *a.down_global;
+  unsigned long long w[kRows][kMaxDownPieces];
+#pragma unroll
+  for (int q = 0; q < kRows; ++q) {  // every piece of every row in flight at once
+    const int e = threadIdx.x + q * kFinThreads, t = e / kTileRows, r = e % kTileRows;
+    const int first = first_cta[t], last = last_cta[t];
+#pragma unroll
+    for (int k = 0; k < kMaxDownPieces; ++k) {
+      w[q][k] = 0ull;
+      const int c = first + k;
+      if (c <= last) {
+        const int piece = run_tile[c] < t ? 1 : 0;  // tile t is CTA c's second piece when its run began earlier
+        w[q][k] = __ldcg(sc.batch_words + ((size_t(c) * 2 + piece) * kBatchMax + m) * kTileRows + r);
       }
-      lo = ld_relaxed_gpu_u64(p);
-      hi = ld_relaxed_gpu_u64(p + 1);
     }
-    ss[t * kBatchMax + m] = __longlong_as_double(static_cast<long long>((hi << 32) | (lo & 0xffffffffull)));
   }
-  __syncthreads();
-  G4_STAMP(sc, 7);
-  if (threadIdx.x < M) {
-    double sum = 0.0;
-    for (int t = 0; t < kT; ++t) sum += ss[t * kBatchMax + threadIdx.x];  // fixed order
-    ctl.inv[threadIdx.x] = rms_inverse(sum, kH);
+  float y[kRows];
+  double ss = 0.0;
+#pragma unroll
+  for (int q = 0; q < kRows; ++q) {
+    const int e = threadIdx.x + q * kFinThreads, t = e / kTileRows;
+    const int n = last_cta[t] - first_cta[t] + 1;
+    float sum = 0.f;  // the pieces in CTA order
+#pragma unroll
+    for (int k = 0; k < kMaxDownPieces; ++k) {
+      if (k >= n) break;
+      if (uint32_t(w[q][k] >> 32) != tag) {
+        atomicOr(sc.err, kErrInternal);
+        sum = __uint_as_float(0x7fc00000u);
+      }
+      sum += __uint_as_float(uint32_t(w[q][k]));
+    }
+    y[q] = bf16_round(bf16_round(sum) * g);
+    ss += double(y[q]) * double(y[q]);
   }
-  __syncthreads();
+  const float inv = rms_inverse(block_sum_d(ss, red), kH);
   const float lam = a.layer_scalar ? bf16_to_f32(a.layer_scalar[0]) : 1.0f;
-  for (int f = 0; f < nfin; ++f) {
-    const int tile = ctl.fin_tile[f];
-    for (int idx = threadIdx.x; idx < M * kTileRows; idx += kBThreads) {
-      const int m = idx / kTileRows, e = tile * kTileRows + idx % kTileRows;
-      const float y = bf16_to_f32(sc.batch_y[size_t(m) * kH + e]);
-      const float nrm = bf16_round((y * ctl.inv[m]) * bf16_to_f32(a.post_rms[e]));
-      uint16_t* res = a.residual + size_t(m) * kH + e;
-      float r = bf16_round(bf16_to_f32(*res) + nrm);
-      if (a.layer_scalar) r = bf16_round(r * lam);
-      *res = f32_to_bf16(r);
-    }
+#pragma unroll
+  for (int q = 0; q < kRows; ++q) {
+    const float nrm = bf16_round((y[q] * inv) * gamma[q]);
+    float r = bf16_round(bf16_to_f32(rbits[q]) + nrm);
+    if (a.layer_scalar) r = bf16_round(r * lam);
+    res[threadIdx.x + q * kFinThreads] = f32_to_bf16(r);
   }
 }
 
@@ -788,18 +821,6 @@ cudaError_t launch_batch(void (*kernel)(KArgs...), int grid, int threads, size_t
   cfg.attrs = attr;
   cfg.numAttrs = 1;
   return cudaLaunchKernelEx(&cfg, kernel, std::forward<Args>(args)...);
-}
-
-// The most tiles one CTA of a `grid`-CTA launch finishes (those whose first unit is in its run).
-int batch_max_fin(int upt, int tiles, int grid) {
-  int best = 0, run = 0, prev = -1;
-  for (int t = 0; t < tiles; ++t) {
-    const int c = cta_of_unit(int64_t(t) * upt, grid, int64_t(upt) * tiles);
-    run = c == prev ? run + 1 : 1;
-    prev = c;
-    best = run > best ? run : best;
-  }
-  return best;
 }
 
 template <int MPAD>
@@ -837,7 +858,10 @@ cudaError_t launch_batch_t(const FfnArgs& a, int M, const LaunchEnv& env) {
   if ((e = launch_batch(ffn_batch_upgate_kernel<MPAD>, gu, kBThreads, Shape::kSmemBytes, true, env.stream, ug, a, su,
                         M)))
     return e;
-  return launch_batch(ffn_batch_down_kernel<MPAD>, gd, kBThreads, Shape::kSmemBytes, true, env.stream, dn, a, sd, M);
+  if ((e = launch_batch(ffn_batch_down_kernel<MPAD>, gd, kBThreads, Shape::kSmemBytes, true, env.stream, dn, a, sd,
+                        M)))
+    return e;
+  return launch_batch(ffn_batch_finalize_kernel, M, kFinThreads, 0, true, env.stream, a, env.sc, gd);
 }
 
 template <int MPAD>
@@ -861,12 +885,26 @@ cudaError_t prepare_batch_kernels() {
 }
 
 bool batch_geometry_fits(int sm_count) {
-  // a down CTA keeps at most kBMaxFin finished tiles for its residual tail
+  // a down CTA's run lies within two tiles (its two piece slots) and a down tile spans at most
+  // kMaxDownPieces CTAs (the finalize kernel's loads); an up/gate tile at most kMaxCtasPerGroup
+  constexpr int kDownUpt = kL / kUnitK, kDownTiles = kH / kTileRows, kUgUpt = kH / kUnitK, kUgTiles = kL / 64;
   const int grid = sm_count;
-  return batch_max_fin(kL / kUnitK, kH / kTileRows, grid) <= kBMaxFin;
+  if (grid > 1024) return false;  // the finalize kernel's table of down CTAs
+  if (int64_t(kDownUpt) * kDownTiles / grid + 1 > kDownUpt) return false;
+  for (int t = 0; t < kDownTiles; ++t)
+    if (cta_of_unit(int64_t(t) * kDownUpt + kDownUpt - 1, grid, int64_t(kDownUpt) * kDownTiles) -
+            cta_of_unit(int64_t(t) * kDownUpt, grid, int64_t(kDownUpt) * kDownTiles) + 1 > kMaxDownPieces)
+      return false;
+  const int gu = grid < kUgUpt * kUgTiles ? grid : kUgUpt * kUgTiles;
+  for (int t = 0; t < kUgTiles; ++t)
+    if (cta_of_unit(int64_t(t) * kUgUpt + kUgUpt - 1, gu, int64_t(kUgUpt) * kUgTiles) -
+            cta_of_unit(int64_t(t) * kUgUpt, gu, int64_t(kUgUpt) * kUgTiles) > kMaxCtasPerGroup)
+      return false;
+  return true;
 }
 
-size_t batch_words_count(int sm_count) { return size_t(sm_count) * kBatchMax * kTileRows; }
+// split-K words of the batched kernels: two piece slots per CTA
+size_t batch_words_count(int sm_count) { return size_t(sm_count) * 2 * kBatchMax * kTileRows; }
 
 cudaError_t launch_ffn_nvfp4_batch(const FfnArgs& a, int M, const LaunchEnv& env) {
   if (env.tp.world != 1) return cudaErrorNotSupported;  // the batched feed-forward runs on one GPU

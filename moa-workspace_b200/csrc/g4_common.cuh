@@ -65,17 +65,13 @@ struct Scratch {
                                 // (epoch << 32 | low / high half of the f64), kTileSsCount tiles
   uint64_t* trace;     // per-CTA phase timestamps (profiling builds only; null otherwise)
   // the token-batched feed-forward (M > 1): its normalised input h [kBatchMax][H] (f16, scaled by a
-  // power of two per token), the down
-  // projection's bf16 rows [kBatchMax][H], split-K words [CTA][kBatchMax tokens][128 rows] and the
-  // per (tile, token) sums of squares of the residual tail (two words each, kBatchSsWords)
+  // power of two per token), those factors' inverses, and the split-K words [CTA][2 pieces]
+  // [kBatchMax tokens][128 rows]
   uint16_t* batch_h;
-  uint16_t* batch_y;
   float* batch_unscale;  // [kBatchMax]: 2^-k of each token's f16 scaling of h
   unsigned long long* batch_words;
-  unsigned long long* batch_ss;
 };
 constexpr int kBatchMax = 64;  // tokens per batched feed-forward call
-constexpr size_t kBatchSsWords = size_t(32) * kBatchMax * 2;
 // the batched feed-forward's call count (tags its split-K words and tile sums)
 constexpr int kBatchEpoch = 4080;
 constexpr int kTileSsCount = 64;
