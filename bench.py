@@ -395,7 +395,8 @@ def layer_ops(ops, device, m: Model, b: Buffers, lay: Layer, which=("qkv", "attn
                                 lay.q_rms, lay.k_rms, b.kv_off[lay.ring], b.rope_off, cos, sin, lay.k_cache,
                                 lay.v_cache, b.q, tiled=lay.tiled)
     if "attn" in which:
-        ops.sliding_attention(device, b.q, lay.k_cache, lay.v_cache, b.mask[lay.ring], b.attn, scale=ATTN_SCALE)
+        ops.sliding_attention(device, b.q, lay.k_cache, lay.v_cache, b.mask[lay.ring], b.attn, scale=ATTN_SCALE,
+                              kv_offset=b.kv_off[lay.ring])
     if "o" in which:
         ops.sliding_attention_output(device, b.attn, lay.post_attn_rms, lay.o_w, lay.o_s, b.x, tiled=lay.tiled)
     if "ffn" in which:

@@ -141,6 +141,14 @@ g4_status g4_full_attention_output(g4_ctx* ctx, const uint16_t* x, const float* 
 g4_status g4_sliding_attention(g4_ctx* ctx, const uint16_t* q, const uint16_t* k, const uint16_t* v,
                                const float* mask, uint16_t* out_hbm, int32_t ring_len, float scale, void* stream);
 
+/* No counterpart in the reference: g4_sliding_attention for a caller that has just issued the
+ * layer's g4_sliding_project_qkv on the same stream and passes the kv_offset it gave that op.
+ * Every other row of k and v is then final, so the kernel copies them while the QKV op finishes
+ * and reads only the addressed slot's rows after it. Results are those of g4_sliding_attention. */
+g4_status g4_sliding_attention_after_qkv(g4_ctx* ctx, const uint16_t* q, const uint16_t* k, const uint16_t* v,
+                                         const float* mask, uint16_t* out_hbm, int32_t ring_len, float scale,
+                                         const int32_t* kv_offset, void* stream);
+
 /* Replaces ops::sliding_attention_output (src/ops.rs:130-146).
  * x [Ns, Gs, Ds] (= [Qs]) bf16, post_attn_rms_weight [H], o_weight [H, Qs] f8e4m3,
  * o_weight_scale [H] bf16, residual_hbm [H] bf16 read and overwritten in place. */

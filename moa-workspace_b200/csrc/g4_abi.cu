@@ -214,8 +214,9 @@ static g4_status project_qkv(bool tiled, g4_ctx* ctx, const uint16_t* x, const u
   return cuda_status(ctx, g4::launch_qkv(a, env_of(ctx, stream)), "sliding_project_qkv launch");
 }
 
-g4_status g4_sliding_attention(g4_ctx* ctx, const uint16_t* q, const uint16_t* k, const uint16_t* v,
-                               const float* mask, uint16_t* out_hbm, int32_t ring_len, float scale, void* stream) {
+static g4_status sliding_attention(g4_ctx* ctx, const uint16_t* q, const uint16_t* k, const uint16_t* v,
+                                   const float* mask, uint16_t* out_hbm, int32_t ring_len, float scale,
+                                   const int32_t* kv_offset, void* stream) {
   if (!ctx) return G4_ERR_INVALID_ARGUMENT;
   g4_status st = check_ptrs(ctx, {{q, "q"}, {k, "k"}, {v, "v"}, {mask, "mask"}, {out_hbm, "out_hbm"}});
   if (st != G4_OK) return st;
@@ -224,8 +225,20 @@ g4_status g4_sliding_attention(g4_ctx* ctx, const uint16_t* q, const uint16_t* k
   if (!(scale == scale)) return fail(ctx, G4_ERR_INVALID_ARGUMENT, "%s is NaN", "scale");
   if ((st = check_tp(ctx)) != G4_OK) return st;
   DeviceGuard guard(ctx->device);
-  g4::AttnArgs a{q, k, v, mask, out_hbm, ring_len, g4::kNs / ctx->tp_world, scale};
+  g4::AttnArgs a{q, k, v, mask, out_hbm, ring_len, g4::kNs / ctx->tp_world, scale, kv_offset};
   return cuda_status(ctx, g4::launch_attention(a, env_of(ctx, stream)), "sliding_attention launch");
+}
+
+g4_status g4_sliding_attention(g4_ctx* ctx, const uint16_t* q, const uint16_t* k, const uint16_t* v,
+                               const float* mask, uint16_t* out_hbm, int32_t ring_len, float scale, void* stream) {
+  return sliding_attention(ctx, q, k, v, mask, out_hbm, ring_len, scale, nullptr, stream);
+}
+
+g4_status g4_sliding_attention_after_qkv(g4_ctx* ctx, const uint16_t* q, const uint16_t* k, const uint16_t* v,
+                                         const float* mask, uint16_t* out_hbm, int32_t ring_len, float scale,
+                                         const int32_t* kv_offset, void* stream) {
+  if (!kv_offset) return g4::host::fail(ctx, G4_ERR_INVALID_ARGUMENT, "null pointer: %s", "kv_offset");
+  return sliding_attention(ctx, q, k, v, mask, out_hbm, ring_len, scale, kv_offset, stream);
 }
 
 static g4_status attention_output(bool tiled, g4_ctx* ctx, const uint16_t* x, const uint16_t* post_attn_rms_weight,

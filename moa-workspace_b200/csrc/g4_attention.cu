@@ -96,18 +96,6 @@ __global__ void __launch_bounds__(kThreads, 2) attention_kernel(const __grid_con
     mbar_init(&sm.vbar[tid], 1);
     fence_mbar_init();
   }
-  // While the preceding QKV op finishes, bring this CTA's K and V rows into L2: it writes one
-  // slot of them, but L2 is coherent, so the copies below (after the wait) still read its rows.
-  for (int b = tid; b < 2 * (per / kBox); b += kThreads) {
-    const int nb = per / kBox;
-    tma_prefetch_l2_3d(b < nb ? &maps.k : &maps.v, 0, head, slot0 + (b < nb ? b : b - nb) * kBox);
-  }
-  __syncthreads();
-
-  pdl_wait_primary();  // q and the cache rows come from the preceding QKV op
-  pdl_launch_dependents();
-  G4_STAMP(sc, 1);
-
   // rows [first, first + count) of a cache into a shared-memory buffer: box b (kBox rows) by
   // thread b, completing on its own barrier, so the rows can be used as their box lands
   const uint64_t policy = l2_evict_first_policy();  // each row is read once per step
@@ -118,8 +106,52 @@ __global__ void __launch_bounds__(kThreads, 2) attention_kernel(const __grid_con
       tma_load_3d(dst + b * kBox * kRowBytes, map, 0, head, slot0 + first + b * kBox, &bars[b], policy);
     }
   };
-  fetch(&maps.k, sm.k, sm.kbar, 0, per < kSub ? per : kSub);
-  fetch(&maps.v, sm.v, sm.vbar, 0, per < kSub ? per : kSub);  // (its own buffer: in flight while scoring)
+  const int first_rows = per < kSub ? per : kSub;
+  // The slot the preceding QKV op writes, when the caller says which (-1: any row may change).
+  int cur = -1;
+  if (a.kv_offset) {
+    const int kv = __ldg(a.kv_offset);  // written before the QKV op ran, not by it
+    if (kv >= 0 && kv % (kPs * 2) == 0 && kv / (kPs * 2) < a.ring_len) cur = kv / (kPs * 2);
+  }
+  if (a.kv_offset) {
+    // every row but the slot's is final: the first pass's K and V rows go straight into shared
+    // memory while the QKV op finishes (the slot's rows are read again after the wait)
+    __syncthreads();  // the barriers are initialised
+    fetch(&maps.k, sm.k, sm.kbar, 0, first_rows);
+    fetch(&maps.v, sm.v, sm.vbar, 0, first_rows);
+  }
+  // While the preceding QKV op finishes, bring this CTA's other K and V rows into L2 (L2 is
+  // coherent, so copies made after the wait still see the slot that op writes).
+  {
+    const int nb = per / kBox, skip = a.kv_offset ? first_rows / kBox : 0;
+    for (int b = skip + tid; b < nb; b += kThreads) {
+      tma_prefetch_l2_3d(&maps.k, 0, head, slot0 + b * kBox);
+      tma_prefetch_l2_3d(&maps.v, 0, head, slot0 + b * kBox);
+    }
+  }
+  __syncthreads();
+
+  pdl_wait_primary();  // q and the cache rows come from the preceding QKV op
+  pdl_launch_dependents();
+  G4_STAMP(sc, 1);
+
+  if (!a.kv_offset) {
+    fetch(&maps.k, sm.k, sm.kbar, 0, first_rows);
+    fetch(&maps.v, sm.v, sm.vbar, 0, first_rows);  // (its own buffer: in flight while scoring)
+  } else if (cur >= slot0 && cur < slot0 + first_rows) {
+    // the slot's fresh K and V rows over the early copies, once the boxes holding them landed
+    const int t = cur - slot0, box = t / kBox;
+    bool okb = mbar_wait_or_abort(&sm.kbar[box], 0u, &abort_flag, sc.err);
+    okb = mbar_wait_or_abort(&sm.vbar[box], 0u, &abort_flag, sc.err) && okb;
+    if (okb && tid < 2 * (kRowBytes / 16)) {  // 32 x 16 bytes per row, K then V
+      const bool is_v = tid >= kRowBytes / 16;
+      const int q16 = tid % (kRowBytes / 16);
+      const uint16_t* src = (is_v ? a.v_cache : a.k_cache) + (size_t(cur) * a.heads + head) * kDs;
+      const uint4 x = __ldcg(reinterpret_cast<const uint4*>(src) + q16);
+      reinterpret_cast<uint4*>((is_v ? sm.v : sm.k) + t * kRowBytes)[q16] = x;
+    }
+    __syncthreads();  // the rows are in place before anyone scores (or reads V)
+  }
 
   // phase 1: scores, kSub slots at a time. The 8 lanes 8i .. 8i + 7 of a warp score one slot,
   // so a warp scores 4 slots per step (one box of 32 slots per step of the 8 warps). Lane

@@ -209,8 +209,9 @@ cudaError_t issue_step(g4_decoder* d, cudaStream_t stream) {
                          l.k_cache,        l.v_cache,        d->q,               l.ring_len,
                          m.rope_rows,      tiled};
     if ((e = g4::launch_qkv(qa, env)) != cudaSuccess) return e;
-    const g4::AttnArgs aa{d->q, l.k_cache, l.v_cache, d->mask + size_t(r) * d->mask_stride, d->attn, l.ring_len, heads,
-                          l.attn_scale};
+    const g4::AttnArgs aa{d->q,      l.k_cache, l.v_cache,    d->mask + size_t(r) * d->mask_stride,
+                          d->attn,   l.ring_len, heads,        l.attn_scale,
+                          d->kv_off + 4 * r};  // the slot the QKV op above writes
     if ((e = g4::launch_attention(aa, env)) != cudaSuccess) return e;
     const g4::OArgs oa{d->attn, l.post_attn_rms_weight, l.o_weight, l.o_weight_scale, d->hidden, tiled};
     if ((e = g4::launch_o(oa, env)) != cudaSuccess) return e;

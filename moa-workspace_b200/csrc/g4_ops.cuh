@@ -44,6 +44,10 @@ struct AttnArgs {
   int ring_len;
   int heads;  // KV heads in the cache (8 / tensor-parallel degree)
   float scale;
+  // the preceding QKV op's kv_offset (slot * Ns * Ds * 2), when the caller has it: every other
+  // row of the cache is final, so the first pass's K and V rows are loaded before the wait on
+  // that op and only the slot's rows after it (null: every row after the wait)
+  const int32_t* kv_offset = nullptr;
 };
 
 struct OArgs {

@@ -39,6 +39,7 @@ SIGNATURES = {
     "g4_ctx_set_overlap": [_p, ctypes.c_int],
     "g4_sliding_project_qkv": [_p] * 18 + [_i32, _i32, _p],
     "g4_sliding_attention": [_p, _p, _p, _p, _p, _p, _i32, _f32, _p],
+    "g4_sliding_attention_after_qkv": [_p, _p, _p, _p, _p, _p, _i32, _f32, _p, _p],
     "g4_sliding_attention_output": [_p] * 6 + [_p],
     "g4_decoder_feedforward": [_p] * 14 + [_p],
     "g4_sliding_project_qkv_tiled": [_p] * 18 + [_i32, _i32, _p],

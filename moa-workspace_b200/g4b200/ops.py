@@ -240,10 +240,13 @@ def sliding_project_qkv(device: Device, x, q_weight, k_weight, v_weight, q_weigh
     _check(device, st, "sliding_project_qkv")
 
 
-def sliding_attention(device: Device, q, k, v, mask, out_hbm, *, scale: float = 1.0, stream=None) -> None:
+def sliding_attention(device: Device, q, k, v, mask, out_hbm, *, scale: float = 1.0, kv_offset=None,
+                      stream=None) -> None:
     """ops::sliding_attention (src/ops.rs:118-128). k/v: [ring, Ns, Ds]; mask: [ring] f32.
 
-    On a tensor-parallel device q, k, v and out_hbm are this rank's heads (`geometry`)."""
+    On a tensor-parallel device q, k, v and out_hbm are this rank's heads (`geometry`).
+    kv_offset: the i32 [1] the layer's sliding_project_qkv just got on the same stream; the
+    kernel then copies every other cache row while that op finishes (g4_sliding_attention_after_qkv)."""
     bf = torch.bfloat16
     nh = geometry(device.world)["kv_heads"]
     ring = k.shape[0] if k.dim() == 3 else -1
@@ -254,7 +257,12 @@ def sliding_attention(device: Device, q, k, v, mask, out_hbm, *, scale: float = 
         _arg(mask, "mask", torch.float32, (ring,), device),
         _arg(out_hbm, "out_hbm", bf, (nh, GS, DS), device),
     ]
-    st = _abi.lib().g4_sliding_attention(device.handle, *args, ring, float(scale), _stream_ptr(stream, device.index))
+    if kv_offset is None:
+        st = _abi.lib().g4_sliding_attention(device.handle, *args, ring, float(scale), _stream_ptr(stream, device.index))
+    else:
+        st = _abi.lib().g4_sliding_attention_after_qkv(device.handle, *args, ring, float(scale),
+                                                       _arg(kv_offset, "kv_offset", torch.int32, (1,), device),
+                                                       _stream_ptr(stream, device.index))
     _check(device, st, "sliding_attention")
 
 

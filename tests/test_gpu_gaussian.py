@@ -147,3 +147,41 @@ def test_attention_output_gaussian(device):
     ok, maxd, exact = within(want, got, ATOL["sliding_attention_output"])
     assert ok, maxd
     assert exact > 0.99, exact
+
+
+@pytest.mark.parametrize("ring,theta", [(1024, 1e4), (2048, 1e6), (4096, 1e6)])
+def test_attention_after_qkv_sees_the_new_slot(device, ring, theta):
+    """g4_sliding_attention_after_qkv issued right after the QKV op (the decoder's order, with
+    programmatic dependent launch): the early copies of the cache rows may not miss the slot the
+    QKV op writes. Bit-identical to g4_sliding_attention on the updated cache, and within the
+    attention tolerance of the oracle."""
+    import torch
+    from g4b200 import ops
+
+    d = gaussian.qkv(theta, ring=ring)
+    pos = d["pos"]
+    cos = np.zeros((32768, 256), np.uint16)
+    sin = np.zeros((32768, 256), np.uint16)
+    cos[pos], sin[pos] = d["cos_row"], d["sin_row"]
+    kc, vc = dev_tensor(d["k_cache"]), dev_tensor(d["v_cache"])
+    qo = dev_tensor(np.zeros((8, 2, 256), np.uint16))
+    mask = (np.arange(ring) <= min(pos, ring - 1)).astype(np.float32)
+    kv_off = dev_tensor(d["kv_offset"])
+    out_fast = torch.zeros((8, 2, 256), dtype=torch.bfloat16, device="cuda")
+    out_plain = torch.zeros_like(out_fast)
+    device.set_overlap(True)
+    try:
+        ops.sliding_project_qkv(device, *(dev_tensor(d[k]) for k in (
+            "x", "q_weight", "k_weight", "v_weight", "q_weight_scale", "k_weight_scale", "v_weight_scale",
+            "input_rms_weight", "q_rms_weight", "k_rms_weight")), kv_off, dev_tensor(d["rope_offset"]),
+            dev_tensor(cos), dev_tensor(sin), kc, vc, qo)
+        ops.sliding_attention(device, qo, kc, vc, dev_tensor(mask), out_fast, scale=1.0 / 16, kv_offset=kv_off)
+        ops.sliding_attention(device, qo, kc, vc, dev_tensor(mask), out_plain, scale=1.0 / 16)
+        device.check()
+    finally:
+        device.set_overlap(False)
+    got = host_bits(out_fast)
+    assert np.array_equal(got, host_bits(out_plain))
+    want = oracle.sliding_attention(host_bits(qo), host_bits(kc), host_bits(vc), mask, 1.0 / 16)
+    ok, maxd, exact = within(want, got, 0.01)
+    assert ok and exact > 0.9, (maxd, exact)
