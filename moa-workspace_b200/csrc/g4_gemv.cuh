@@ -90,7 +90,7 @@ struct GemvShape {
 
 struct GemvCtl {
   uint64_t full[12], sready[12], done[16], tempty[16], dfull[4], dempty[4], drain;
-  uint64_t bready[16];    // fp8: the B slot's terms and exponent are in shared memory
+  uint64_t bready[16];    // the B slot is built in shared memory (fp8: its terms and exponent)
   uint32_t tmem_base;
   uint32_t abort;
   int pmax;               // nvfp4: largest exponent of this CTA's activation
@@ -326,7 +326,7 @@ __device__ void gemv_run(Op& op, uint8_t* smem_raw, const Scratch& sc) {
       mbar_init(&ctl.dempty[i], 4);  // nvfp4: the epilogue has read it
     }
     mbar_init(&ctl.drain, 1);
-    for (int i = 0; i < 16; ++i) mbar_init(&ctl.bready[i], 1);  // fp8: one arrival per built B slot
+    for (int i = 0; i < 16; ++i) mbar_init(&ctl.bready[i], 1);  // one arrival per built B slot
     ctl.abort = 0;
     ctl.pmax = -1000;
     ctl.nonfinite = 0;
@@ -494,15 +494,19 @@ __device__ void gemv_run(Op& op, uint8_t* smem_raw, const Scratch& sc) {
     if constexpr (Shape::kFp4) __syncthreads();  // the CTA's largest exponent (pmax) is complete
     G4_STAMP(sc, 10);
     if constexpr (Shape::kFp4) {
-      // digit rows, one thread per 8 elements
+      // digit rows, one thread per 8 elements: a warp builds a whole slot (warp w slots w, w + 7,
+      // ...) and arrives on its barrier, so the relay releases a unit as soon as its slot is built
       const int pc = ctl.pmax;
-      for (int hb = c.tid; hb < nslots * 32; hb += kGemvThreads) {
+      for (int hb = c.tid; hb < nslots * 32; hb += kGemvThreads) {  // warp-uniform
         const int sl = hb / 32, e8 = hb % 32;  // elements 8 e8 .. 8 e8 + 7 of slot sl
         uint32_t rows[16];
         nvf4_digit_rows8(*reinterpret_cast<const uint4*>(hsm + sl * 256 + e8 * 8), pc, rows);
         uint8_t* bs = c.bsm + size_t(sl) * Shape::kBSlotBytes;
 #pragma unroll
         for (int r = 0; r < 16; ++r) *reinterpret_cast<uint32_t*>(bs + sw128_offset(r, e8 * 4)) = rows[r];
+        asm volatile("fence.proxy.async.shared::cta;" ::: "memory");  // the tensor cores read it
+        __syncwarp();
+        if (c.lane == 0) mbar_arrive(&ctl.bready[sl]);
       }
     } else {
       // exponent E of a max |v| so that max |v| 2^E lies in [128, 256)
@@ -544,11 +548,6 @@ __device__ void gemv_run(Op& op, uint8_t* smem_raw, const Scratch& sc) {
       }
     }
     G4_STAMP(sc, 11);
-  }
-  if constexpr (Shape::kFp4) {
-    asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
-    tc_fence_before();
-    __syncthreads();
   }
   G4_STAMP(sc, 2);
 
@@ -595,7 +594,8 @@ __device__ void gemv_run(Op& op, uint8_t* smem_raw, const Scratch& sc) {
         if constexpr (Shape::kFp4) {
           const bool first = i == 0 || kc == 0;
           if (first) ++piece;
-          bad = !mbar_wait_or_abort(&ctl.sready[s], uint32_t((i / S) & 1), abort, sc.err);
+          bad = !mbar_wait_or_abort(&ctl.sready[s], uint32_t((i / S) & 1), abort, sc.err) ||
+                !mbar_wait_or_abort(&ctl.bready[c.bslot(kc)], 0u, abort, sc.err);
           if (!bad && first && piece >= Shape::kDSlots)
             bad = !mbar_wait_or_abort(&ctl.dempty[piece % Shape::kDSlots], uint32_t(((piece / Shape::kDSlots) - 1) & 1),
                                       abort, sc.err);
