@@ -91,6 +91,8 @@ def op_bytes(world=1):
         # the NVFP4 feed-forward on M tokens: the same weights once, M residual rows in and out
         **{f"decoder_feedforward_m{mb}": 2 * (L * H // 2 + L * H // 16) + (H * L // 2 + H * L // 16)
            + mb * H * 2 * 2 + H * 2 * 2 + 8 * 2 + 12 for mb in BATCH_SWEEP},
+        **{f"decoder_feedforward_fp8_m{mb}": 2 * L * H + H * L + (2 * L + H) * 4 + mb * H * 2 * 2 + H * 2 * 2 + 8 * 2
+           for mb in BATCH_SWEEP},
     }
 
 
@@ -409,9 +411,13 @@ def layer_ops(ops, device, m: Model, b: Buffers, lay: Layer, which=("qkv", "attn
 
 
 def ffn_batch(ops, device, lay: Layer, rows):
-    """The NVFP4 feed-forward of `lay` on the token batch `rows` [M, H] (updated in place)."""
-    ops.decoder_feedforward_batch_tiled(device, rows, lay.pre_ff_rms, lay.up_w, lay.down_w, lay.up_s, lay.down_s,
-                                        lay.up_g, lay.gate_g, lay.down_g, lay.post_ff_rms, lay.layer_scalar)
+    """The feed-forward of `lay` (NVFP4 or FP8) on the token batch `rows` [M, H] (updated in place)."""
+    if lay.ffn == "fp8":
+        ops.decoder_feedforward_fp8_batch_tiled(device, rows, lay.pre_ff_rms, lay.up_w, lay.down_w, lay.up_s,
+                                                lay.gate_s, lay.down_s, lay.post_ff_rms, lay.layer_scalar)
+    else:
+        ops.decoder_feedforward_batch_tiled(device, rows, lay.pre_ff_rms, lay.up_w, lay.down_w, lay.up_s, lay.down_s,
+                                            lay.up_g, lay.gate_g, lay.down_g, lay.post_ff_rms, lay.layer_scalar)
 
 
 def decode_one_by_one(ops, device, m: Model, b: Buffers, logits):
@@ -573,9 +579,11 @@ def parity(torch, ops, device, dev, m: Model, rank, world, dist):
         rows = (torch.randn(8, H, device=dev, generator=torch.Generator(device=dev).manual_seed(8))
                 .to(torch.bfloat16))
         batch_in = host_array(rows)
+        rows8 = rows.clone()
         ffn_batch(ops, device, m.nvfp4[0], rows)
+        ffn_batch(ops, device, m.layers[0], rows8)  # FP8
         device.check()
-        batch_rows = host_array(rows)
+        batch_rows, batch_rows8 = host_array(rows), host_array(rows8)
     if rank != 0:
         return None
     from oracle import ops as oracle
@@ -587,6 +595,12 @@ def parity(torch, ops, device, dev, m: Model, rank, world, dist):
                                                   h["down_g"][0], h["post_ff_rms"], h["layer_scalar"])
         res["nvfp4.decoder_feedforward_batch_m8"] = compare("decoder_feedforward", want_b.reshape(-1),
                                                             batch_rows.reshape(-1))
+        h = m.layers[0].host
+        want_b8 = oracle.feedforward_fp8_batch(batch_in, h["pre_ff_rms"], h["up_w"], h["gate_w"], h["down_w"],
+                                               h["up_s"], h["gate_s"], h["down_s"], h["post_ff_rms"],
+                                               h["layer_scalar"])
+        res["layer0.decoder_feedforward_fp8_batch_m8"] = compare("decoder_feedforward_fp8", want_b8.reshape(-1),
+                                                                 batch_rows8.reshape(-1))
     table_rows = host_array(m.table[b.token])
     emb = host_array(dec_embed(torch, ops, device, m, b))
     res["embed_token"] = {"ok": bool(np.array_equal(emb, oracle.embed_token(table_rows[None, :], 0))),
@@ -601,8 +615,8 @@ def parity(torch, ops, device, dev, m: Model, rank, world, dist):
             "ranks_bit_identical": same if world > 1 else None, "ops": res,
             "checked": f"token {b.token} at position {b.pos}: the decoder step against the ops one by one (bit for "
                        "bit), then each op of layers 0 (sliding) and 5 (global-shaped) and of an NVFP4 layer against "
-                       "oracle/ops.py (numpy) on the previous op's GPU output, the NVFP4 feed-forward on a batch of 8 "
-                       "tokens row by row (one GPU), the embedding and every 61st logit" +
+                       "oracle/ops.py (numpy) on the previous op's GPU output, the NVFP4 and FP8 feed-forwards on a batch "
+                       "of 8 tokens row by row (one GPU), the embedding and every 61st logit" +
                        (", O/FFN as the rank-order sum of the ranks' partials" if world > 1 else "")}
 
 
@@ -832,6 +846,9 @@ def op_timings(torch, ops, device, dev, m: Model, dist, reps=64):
         for mb in BATCH_SWEEP:
             cases[f"decoder_feedforward_m{mb}"] = (
                 lambda i, mb=mb: ffn_batch(ops, device, m.nvfp4[i % NVFP4_COPIES], rows[:mb]))
+        for mb in BATCH_SWEEP:  # the decoder's FP8 FFN layers on a batch of tokens
+            cases[f"decoder_feedforward_fp8_m{mb}"] = (
+                lambda i, mb=mb: ffn_batch(ops, device, m.layers[i % N_MODEL], rows[:mb]))
     us = {}
     for name, fn in cases.items():
         n = reps if name != "final_norm_and_logits" else 8  # 2 GB / 8 per call: the logits stream from HBM

@@ -251,6 +251,23 @@ g4_status g4_decoder_feedforward_batch_tiled(g4_ctx* ctx, uint16_t* residual_hbm
                                              const float* down_global_scale, const uint16_t* post_ff_rms_weight,
                                              const uint16_t* layer_scalar, int32_t m, void* stream);
 
+/* The FP8-per-channel feed-forward (g4_decoder_feedforward_fp8) on a batch of m tokens, the same
+ * way g4_decoder_feedforward_batch treats the NVFP4 one: residual_hbm [m, H], m in [1, 64], the
+ * weights read once for all rows; m = 1 runs the single-token kernels; one GPU only. The codes are
+ * expanded exactly to f16 / bf16 in tensor memory and the f32 row scales applied after the sums. */
+g4_status g4_decoder_feedforward_fp8_batch(g4_ctx* ctx, uint16_t* residual_hbm, const uint16_t* pre_ff_rms_weight,
+                                           const uint8_t* up_weight, const uint8_t* gate_weight,
+                                           const uint8_t* down_weight, const float* up_weight_scale,
+                                           const float* gate_weight_scale, const float* down_weight_scale,
+                                           const uint16_t* post_ff_rms_weight, const uint16_t* layer_scalar, int32_t m,
+                                           void* stream);
+g4_status g4_decoder_feedforward_fp8_batch_tiled(g4_ctx* ctx, uint16_t* residual_hbm,
+                                                 const uint16_t* pre_ff_rms_weight,
+                                                 const uint8_t* up_gate_weight_tiled, const uint8_t* down_weight_tiled,
+                                                 const float* up_weight_scale, const float* gate_weight_scale,
+                                                 const float* down_weight_scale, const uint16_t* post_ff_rms_weight,
+                                                 const uint16_t* layer_scalar, int32_t m, void* stream);
+
 /* No counterpart in the reference: ops::sliding_attention_output (src/ops.rs:130-146) with no
  * context and no allocation, for callers that cannot create a g4_ctx. g4_ctx_create allocates
  * device scratch (cudaMalloc) and host state; some callers may not allocate at all: a host

@@ -492,8 +492,11 @@ static g4_status decoder_feedforward_fp8(bool tiled, g4_ctx* ctx, uint16_t* resi
                                          const uint8_t* gate_weight, const uint8_t* down_weight,
                                          const float* up_weight_scale, const float* gate_weight_scale,
                                          const float* down_weight_scale, const uint16_t* post_ff_rms_weight,
-                                         const uint16_t* layer_scalar, void* stream) {
+                                         const uint16_t* layer_scalar, void* stream, int32_t m = 1) {
   if (!ctx) return G4_ERR_INVALID_ARGUMENT;
+  if (m < 1 || m > g4::kBatchMax) return fail(ctx, G4_ERR_INVALID_ARGUMENT, "%s", "m must be in [1, 64]");
+  if (m > 1 && (ctx->tp_world != 1 || !ctx->batch_ok))
+    return fail(ctx, G4_ERR_UNSUPPORTED, "%s", "a batch of tokens runs on a one-GPU context only");
   g4_status st = check_ptrs(ctx, {{residual_hbm, "residual_hbm"},
                                   {pre_ff_rms_weight, "pre_ff_rms_weight"},
                                   {up_weight, "up_weight"},
@@ -509,6 +512,8 @@ static g4_status decoder_feedforward_fp8(bool tiled, g4_ctx* ctx, uint16_t* resi
   DeviceGuard guard(ctx->device);
   g4::Ffn8Args a{residual_hbm,      pre_ff_rms_weight, up_weight,          gate_weight,  down_weight, up_weight_scale,
                  gate_weight_scale, down_weight_scale, post_ff_rms_weight, layer_scalar, tiled};
+  if (m > 1)
+    return cuda_status(ctx, g4::launch_ffn_fp8_batch(a, m, env_of(ctx, stream)), "decoder_feedforward_fp8_batch launch");
   return cuda_status(ctx, g4::launch_ffn_fp8(a, env_of(ctx, stream)), "decoder_feedforward_fp8 launch");
 }
 
@@ -532,6 +537,28 @@ g4_status g4_decoder_feedforward_fp8_tiled(g4_ctx* ctx, uint16_t* residual_hbm, 
   return decoder_feedforward_fp8(true, ctx, residual_hbm, pre_ff_rms_weight, up_gate_weight_tiled,
                                  up_gate_weight_tiled, down_weight_tiled, up_weight_scale, gate_weight_scale,
                                  down_weight_scale, post_ff_rms_weight, layer_scalar, stream);
+}
+
+g4_status g4_decoder_feedforward_fp8_batch(g4_ctx* ctx, uint16_t* residual_hbm, const uint16_t* pre_ff_rms_weight,
+                                           const uint8_t* up_weight, const uint8_t* gate_weight,
+                                           const uint8_t* down_weight, const float* up_weight_scale,
+                                           const float* gate_weight_scale, const float* down_weight_scale,
+                                           const uint16_t* post_ff_rms_weight, const uint16_t* layer_scalar, int32_t m,
+                                           void* stream) {
+  return decoder_feedforward_fp8(false, ctx, residual_hbm, pre_ff_rms_weight, up_weight, gate_weight, down_weight,
+                                 up_weight_scale, gate_weight_scale, down_weight_scale, post_ff_rms_weight,
+                                 layer_scalar, stream, m);
+}
+
+g4_status g4_decoder_feedforward_fp8_batch_tiled(g4_ctx* ctx, uint16_t* residual_hbm,
+                                                 const uint16_t* pre_ff_rms_weight,
+                                                 const uint8_t* up_gate_weight_tiled, const uint8_t* down_weight_tiled,
+                                                 const float* up_weight_scale, const float* gate_weight_scale,
+                                                 const float* down_weight_scale, const uint16_t* post_ff_rms_weight,
+                                                 const uint16_t* layer_scalar, int32_t m, void* stream) {
+  return decoder_feedforward_fp8(true, ctx, residual_hbm, pre_ff_rms_weight, up_gate_weight_tiled,
+                                 up_gate_weight_tiled, down_weight_tiled, up_weight_scale, gate_weight_scale,
+                                 down_weight_scale, post_ff_rms_weight, layer_scalar, stream, m);
 }
 
 g4_status g4_tp_init(g4_ctx* ctx, int32_t rank, int32_t world, void* blob_out) {

@@ -57,11 +57,13 @@ struct BatchCtl {
   } while (0)
 #endif
 
-template <int MPAD>
+template <int MPAD, bool FP8 = false>
 struct BatchShape {
   static constexpr int kMpad = MPAD;  // B rows: the tokens, zero-padded
-  static constexpr int kABytes = kTileRows * 128;     // packed e2m1 codes: 128 rows x 256 K
-  static constexpr int kScaleBytes = kTileRows * 16;  // ue4m3 block scales
+  // a unit's weights: packed e2m1 codes (128 rows x 256 K) and their ue4m3 block scales, or fp8
+  // codes as two K halves of 128 rows x 128 codes (per-row scales come with the epilogue)
+  static constexpr int kABytes = FP8 ? 2 * kTileRows * 128 : kTileRows * 128;
+  static constexpr int kScaleBytes = FP8 ? 0 : kTileRows * 16;
   static constexpr int kBColBytes = MPAD * 128;       // B: one 64-element K column block of MPAD rows
   static constexpr int kBBytes = 4 * kBColBytes;
   static constexpr int kStageBytes = kABytes + kScaleBytes + kBBytes;
@@ -93,6 +95,26 @@ struct BatchShape {
   static_assert(kStageBytes % 1024 == 0 && (kABytes + kScaleBytes) % 1024 == 0, "1024-byte swizzle atoms");
   static_assert(kSmemBytes <= 227 * 1024, "shared memory budget");
 };
+
+// Eight e4m3 codes (element i in byte i) as eight f16 or, bf16 = true, bf16 (exact: every e4m3
+// value is an f16 and a bf16 value).
+__device__ __forceinline__ uint4 expand8_e4m3(uint32_t lo, uint32_t hi, bool bf16) {
+  uint32_t h[4];
+  asm("{\n .reg .b16 a, b, c, d;\n mov.b32 {a, b}, %4;\n mov.b32 {c, d}, %5;\n"
+      " cvt.rn.f16x2.e4m3x2 %0, a;\n cvt.rn.f16x2.e4m3x2 %1, b;\n"
+      " cvt.rn.f16x2.e4m3x2 %2, c;\n cvt.rn.f16x2.e4m3x2 %3, d;\n}"
+      : "=r"(h[0]), "=r"(h[1]), "=r"(h[2]), "=r"(h[3])
+      : "r"(lo), "r"(hi));
+  if (bf16) {
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+      const float2 f = __half22float2(*reinterpret_cast<const __half2*>(&h[i]));
+      const __nv_bfloat162 b = __floats2bfloat162_rn(f.x, f.y);
+      h[i] = *reinterpret_cast<const uint32_t*>(&b);
+    }
+  }
+  return make_uint4(h[0], h[1], h[2], h[3]);
+}
 
 __device__ __forceinline__ uint64_t l2_evict_last_policy() {
   uint64_t p;
@@ -358,21 +380,33 @@ __device__ void batch_run(Op& op, uint8_t* smem_raw, const Scratch& sc) {
         tc_fence_after();  // the slot's previous MMAs (complete) before this thread's TMEM stores
         if (warp == kWDq0 && lane == 0) G4_UNIT_STAMP(sc, h == 0 ? 4 : 6, i);
         if (ok) {
-          const int c0 = 4 * h + 2 * sub;  // code chunks c0, c0 + 1 (32 elements each)
-          const uint4 q0 = *reinterpret_cast<const uint4*>(a4 + r * 128 + (((c0) ^ (r & 7)) << 4));
-          const uint4 q1 = *reinterpret_cast<const uint4*>(a4 + r * 128 + (((c0 + 1) ^ (r & 7)) << 4));
-          const uint32_t sw = *reinterpret_cast<const uint32_t*>(a4 + Shape::kABytes + r * 16 + 8 * h + 4 * sub);
-          if (sw & 0x80808080u) atomicOr(sc.err, kErrNegativeScale);
-          const uint32_t w[8] = {q0.x, q0.y, q0.z, q0.w, q1.x, q1.y, q1.z, q1.w};
           uint32_t o[32];
+          if constexpr (Shape::kScaleBytes == 0) {
+            // fp8: this half's row r holds 128 codes in eight 16-byte chunks; chunks 4 sub .. 4 sub + 3
+            const uint8_t* row = a4 + h * (kTileRows * 128) + r * 128;
 #pragma unroll
-          for (int j = 0; j < 8; ++j) {  // elements 8j .. 8j + 7: block j / 2, columns 4j .. 4j + 3
-            const uint4 v = Op::kF16 ? dequant8_f16(w[j], (sw >> (8 * (j / 2))) & 0xffu)
-                                     : dequant8_bf16(w[j], (sw >> (8 * (j / 2))) & 0xffu);
-            o[4 * j] = v.x;
-            o[4 * j + 1] = v.y;
-            o[4 * j + 2] = v.z;
-            o[4 * j + 3] = v.w;
+            for (int q = 0; q < 4; ++q) {
+              const uint4 cq = *reinterpret_cast<const uint4*>(row + (((4 * sub + q) ^ (r & 7)) << 4));
+              const uint4 lo = expand8_e4m3(cq.x, cq.y, !Op::kF16), hi = expand8_e4m3(cq.z, cq.w, !Op::kF16);
+              o[8 * q] = lo.x, o[8 * q + 1] = lo.y, o[8 * q + 2] = lo.z, o[8 * q + 3] = lo.w;
+              o[8 * q + 4] = hi.x, o[8 * q + 5] = hi.y, o[8 * q + 6] = hi.z, o[8 * q + 7] = hi.w;
+            }
+          } else {
+            const int c0 = 4 * h + 2 * sub;  // code chunks c0, c0 + 1 (32 elements each)
+            const uint4 q0 = *reinterpret_cast<const uint4*>(a4 + r * 128 + (((c0) ^ (r & 7)) << 4));
+            const uint4 q1 = *reinterpret_cast<const uint4*>(a4 + r * 128 + (((c0 + 1) ^ (r & 7)) << 4));
+            const uint32_t sw = *reinterpret_cast<const uint32_t*>(a4 + Shape::kABytes + r * 16 + 8 * h + 4 * sub);
+            if (sw & 0x80808080u) atomicOr(sc.err, kErrNegativeScale);
+            const uint32_t w[8] = {q0.x, q0.y, q0.z, q0.w, q1.x, q1.y, q1.z, q1.w};
+#pragma unroll
+            for (int j = 0; j < 8; ++j) {  // elements 8j .. 8j + 7: block j / 2, columns 4j .. 4j + 3
+              const uint4 v = Op::kF16 ? dequant8_f16(w[j], (sw >> (8 * (j / 2))) & 0xffu)
+                                       : dequant8_bf16(w[j], (sw >> (8 * (j / 2))) & 0xffu);
+              o[4 * j] = v.x;
+              o[4 * j + 1] = v.y;
+              o[4 * j + 2] = v.z;
+              o[4 * j + 3] = v.w;
+            }
           }
           tmem_st32(a_lane + uint32_t(slot * 64), o);
           tmem_st_wait();
@@ -519,17 +553,18 @@ __device__ void batch_run(Op& op, uint8_t* smem_raw, const Scratch& sc) {
 // at least max |h| 2^-31 is exact in f16, and the up/gate sums are multiplied back by 2^-k
 // (batch_unscale) before their bf16 rounding. Thread 0 of CTA 0 also counts the call (the epoch
 // of the split-K words and tile sums).
-__global__ void __launch_bounds__(256) ffn_batch_norm_kernel(FfnArgs a, Scratch sc) {
+__global__ void __launch_bounds__(256) ffn_batch_norm_kernel(const uint16_t* residual, const uint16_t* pre_rms,
+                                                             Scratch sc) {
   __shared__ double red[8];
   __shared__ float wmax[8];
   const int m = blockIdx.x, g = threadIdx.x;
   const bool have = g < kH / 16;
   uint4 raw[4];
-  if (have) load_group_gamma(a.pre_rms, g, raw);
+  if (have) load_group_gamma(pre_rms, g, raw);
   pdl_wait_primary();
   pdl_launch_dependents();
   if (m == 0 && g == 0) sc.counters[kBatchEpoch] = __ldcg(sc.counters + kBatchEpoch) + 1u;
-  if (have) load_group_cg(a.residual + size_t(m) * kH, g, raw);
+  if (have) load_group_cg(residual + size_t(m) * kH, g, raw);
   const double ss = have ? sum_squares_bf16x16(raw[0], raw[1]) : 0.0;
   const float inv = rms_inverse(block_sum_d(ss, red), kH);
   float v[16];
@@ -570,30 +605,47 @@ struct BatchMaps {
   CUtensorMap b;             // activation rows [M, K] (up/gate: f16, down: bf16), box {64, MPAD}
 };
 
-template <int MPAD>
+// The weights' format: NVFP4 (FfnArgs: packed codes, block scales, reciprocal global scales) or
+// FP8 (Ffn8Args: e4m3 codes, f32 per-row scales).
+template <bool FP8>
+using BatchArgs = std::conditional_t<FP8, Ffn8Args, FfnArgs>;
+
+template <int MPAD, bool FP8>
 struct BatchUpGateOp {
-  using Shape = BatchShape<MPAD>;
+  using Shape = BatchShape<MPAD, FP8>;
   static constexpr int kUnitsPerTile = kH / kUnitK;  // 15
   static constexpr int kTiles = kL / 64;             // 64 up + 64 gate rows per tile
   static constexpr bool kF16 = true;                 // f16 weights x the scaled f16 h
   const BatchMaps* maps;
-  FfnArgs a;
+  BatchArgs<FP8> a;
   Scratch sc;
   int M;
   float g_up = 0.f, g_gate = 0.f;
   uint32_t tag = 0;
 
   __device__ void load_a(uint8_t* stage, int tile, int kc, uint64_t* bar, uint64_t policy) const {
-    uint8_t* scl = stage + Shape::kABytes;
-    if (a.tiled) {
-      tma_load_2d(stage, &maps->a, 0, (tile * kUnitsPerTile + kc) * kTileRows, bar, policy);
-      bulk_g2s(scl, a.up_scale + size_t(tile * kUnitsPerTile + kc) * Shape::kScaleBytes, Shape::kScaleBytes, bar,
-               policy);
+    if constexpr (FP8) {  // [K half][64 up rows | 64 gate rows] x 128 codes
+      if (a.tiled) {
+        tma_load_2d(stage, &maps->a, 0, (tile * kUnitsPerTile + kc) * 2 * kTileRows, bar, policy);
+      } else {
+#pragma unroll
+        for (int h = 0; h < 2; ++h) {
+          tma_load_2d(stage + h * 16384, &maps->a, kc * kUnitK + h * 128, tile * 64, bar, policy);
+          tma_load_2d(stage + h * 16384 + 8192, &maps->a2, kc * kUnitK + h * 128, tile * 64, bar, policy);
+        }
+      }
     } else {
-      tma_load_2d(stage, &maps->a, kc * 128, tile * 64, bar, policy);
-      tma_load_2d(stage + 8192, &maps->a2, kc * 128, tile * 64, bar, policy);
-      tma_load_2d(scl, &maps->s, kc * 16, tile * 64, bar, policy);
-      tma_load_2d(scl + 1024, &maps->s2, kc * 16, tile * 64, bar, policy);
+      uint8_t* scl = stage + Shape::kABytes;
+      if (a.tiled) {
+        tma_load_2d(stage, &maps->a, 0, (tile * kUnitsPerTile + kc) * kTileRows, bar, policy);
+        bulk_g2s(scl, a.up_scale + size_t(tile * kUnitsPerTile + kc) * Shape::kScaleBytes, Shape::kScaleBytes, bar,
+                 policy);
+      } else {
+        tma_load_2d(stage, &maps->a, kc * 128, tile * 64, bar, policy);
+        tma_load_2d(stage + 8192, &maps->a2, kc * 128, tile * 64, bar, policy);
+        tma_load_2d(scl, &maps->s, kc * 16, tile * 64, bar, policy);
+        tma_load_2d(scl + 1024, &maps->s2, kc * 16, tile * 64, bar, policy);
+      }
     }
   }
   __device__ void load_b(uint8_t* dst, int kc, uint64_t* bar, uint64_t policy) const {
@@ -602,18 +654,33 @@ struct BatchUpGateOp {
   }
   __device__ void prefetch_l2(int u0, int u1) const {
     if (!a.tiled) return;
-    prefetch_units(a.up_packed, u0, u1, Shape::kABytes);
-    prefetch_units(a.up_scale, u0, u1, Shape::kScaleBytes);
+    if constexpr (FP8) {
+      prefetch_units(a.up_w, u0, u1, Shape::kABytes);
+    } else {
+      prefetch_units(a.up_packed, u0, u1, Shape::kABytes);
+      prefetch_units(a.up_scale, u0, u1, Shape::kScaleBytes);
+    }
   }
   __device__ void prologue() {
-    g_up = *a.up_global;
-    g_gate = *a.gate_global;
+    if constexpr (!FP8) {
+      g_up = *a.up_global;
+      g_gate = *a.gate_global;
+    }
     tag = (__ldcg(sc.counters + kBatchEpoch) << 1) | 0u;
   }
-  // GloballyScaled(nn.Linear): bf16(bf16(h @ W.T) * g) (generate_references.py:358-372), then the
-  // down input bf16(bf16(gelu_tanh(gate)) * up) (gemma4.py:197), 16 tokens at a time: the gate rows
-  // leave their bf16 values in shared memory, all 128 threads apply GeGLU's gelu to them, and the up
-  // rows form the products.
+  // The projection's bf16 value: NVFP4 GloballyScaled(nn.Linear), bf16(bf16(h @ W.T) * g)
+  // (generate_references.py:358-372); FP8 scaled_projection, bf16((h @ codes.T) * s_row) (:265-274).
+  __device__ float project(float dot, int tile, int row) const {
+    if constexpr (FP8) {
+      const float s = row < 64 ? __ldg(a.up_s + tile * 64 + row) : __ldg(a.gate_s + tile * 64 + row - 64);
+      return bf16_round(dot * s);
+    } else {
+      return bf16_round(bf16_round(dot) * (row < 64 ? g_up : g_gate));
+    }
+  }
+  // Then the down input bf16(bf16(gelu_tanh(gate)) * up) (gemma4.py:197), 16 tokens at a time: the
+  // gate rows leave their bf16 values in shared memory, all 128 threads apply GeGLU's gelu to them,
+  // and the up rows form the products.
   __device__ void finish(BatchCtl&, uint8_t* xbuf, int tile, int row, uint32_t tsum, bool ok) {
     const SplitPiece sp = split_begin<MPAD>(tile, kUnitsPerTile, int64_t(kUnitsPerTile) * kTiles, row, M, tsum, tag,
                                             sc.batch_words, ok, sc.err);
@@ -627,7 +694,7 @@ struct BatchUpGateOp {
       for (int j = 0; j < 16; ++j) a[j] *= c + j < M ? __ldcg(sc.batch_unscale + c + j) : 1.f;  // exact: 2^-k
       if (row >= 64) {
 #pragma unroll
-        for (int j = 0; j < 16; ++j) gel[j * 64 + row - 64] = f32_to_bf16(bf16_round(a[j]) * g_gate);
+        for (int j = 0; j < 16; ++j) gel[j * 64 + row - 64] = f32_to_bf16(project(a[j], tile, row));
       }
       named_bar(kBEpiBarrier, 128);
 #pragma unroll
@@ -640,7 +707,7 @@ struct BatchUpGateOp {
 #pragma unroll
         for (int j = 0; j < 16; ++j)
           if (c + j < M) {
-            const float up = bf16_round(bf16_round(a[j]) * g_up);
+            const float up = project(a[j], tile, row);
             sc.act[size_t(c + j) * kL + tile * 64 + row] = f32_to_bf16(bf16_to_f32(gel[j * 64 + row]) * up);
           }
       }
@@ -649,28 +716,36 @@ struct BatchUpGateOp {
   }
 };
 
-template <int MPAD>
+template <int MPAD, bool FP8>
 struct BatchDownOp {
-  using Shape = BatchShape<MPAD>;
+  using Shape = BatchShape<MPAD, FP8>;
   static constexpr int kUnitsPerTile = kL / kUnitK;  // 60
   static constexpr int kTiles = kH / kTileRows;      // 30
   static constexpr bool kF16 = false;                // bf16 weights x the bf16 GeGLU activation
   const BatchMaps* maps;
-  FfnArgs a;
+  BatchArgs<FP8> a;
   Scratch sc;
   int M;
-  float g_down = 0.f;
-  uint32_t epoch = 0, tag = 0;
+  uint32_t tag = 0;
 
   __device__ void load_a(uint8_t* stage, int tile, int kc, uint64_t* bar, uint64_t policy) const {
-    uint8_t* scl = stage + Shape::kABytes;
-    if (a.tiled) {
-      tma_load_2d(stage, &maps->a, 0, (tile * kUnitsPerTile + kc) * kTileRows, bar, policy);
-      bulk_g2s(scl, a.down_scale + size_t(tile * kUnitsPerTile + kc) * Shape::kScaleBytes, Shape::kScaleBytes, bar,
-               policy);
+    if constexpr (FP8) {  // two K halves of 128 rows x 128 codes
+      if (a.tiled) {
+        tma_load_2d(stage, &maps->a, 0, (tile * kUnitsPerTile + kc) * 2 * kTileRows, bar, policy);
+      } else {
+        tma_load_2d(stage, &maps->a, kc * kUnitK, tile * kTileRows, bar, policy);
+        tma_load_2d(stage + 16384, &maps->a, kc * kUnitK + 128, tile * kTileRows, bar, policy);
+      }
     } else {
-      tma_load_2d(stage, &maps->a, kc * 128, tile * kTileRows, bar, policy);
-      tma_load_2d(scl, &maps->s, kc * 16, tile * kTileRows, bar, policy);
+      uint8_t* scl = stage + Shape::kABytes;
+      if (a.tiled) {
+        tma_load_2d(stage, &maps->a, 0, (tile * kUnitsPerTile + kc) * kTileRows, bar, policy);
+        bulk_g2s(scl, a.down_scale + size_t(tile * kUnitsPerTile + kc) * Shape::kScaleBytes, Shape::kScaleBytes, bar,
+                 policy);
+      } else {
+        tma_load_2d(stage, &maps->a, kc * 128, tile * kTileRows, bar, policy);
+        tma_load_2d(scl, &maps->s, kc * 16, tile * kTileRows, bar, policy);
+      }
     }
   }
   __device__ void load_b(uint8_t* dst, int kc, uint64_t* bar, uint64_t policy) const {
@@ -679,14 +754,14 @@ struct BatchDownOp {
   }
   __device__ void prefetch_l2(int u0, int u1) const {
     if (!a.tiled) return;
-    prefetch_units(a.down_packed, u0, u1, Shape::kABytes);
-    prefetch_units(a.down_scale, u0, u1, Shape::kScaleBytes);
+    if constexpr (FP8) {
+      prefetch_units(a.down_w, u0, u1, Shape::kABytes);
+    } else {
+      prefetch_units(a.down_packed, u0, u1, Shape::kABytes);
+      prefetch_units(a.down_scale, u0, u1, Shape::kScaleBytes);
+    }
   }
-  __device__ void prologue() {
-    g_down = *a.down_global;
-    epoch = __ldcg(sc.counters + kBatchEpoch);
-    tag = (epoch << 1) | 1u;
-  }
+  __device__ void prologue() { tag = (__ldcg(sc.counters + kBatchEpoch) << 1) | 1u; }
   // Every piece (at most two per CTA: the end of one tile and the start of the next) goes out as
   // epoch-tagged words in the CTA's slot (its piece ordinal); ffn_batch_finalize_kernel adds them.
   __device__ void finish(BatchCtl&, uint8_t*, int, int row, uint32_t tsum, bool ok) {
@@ -710,20 +785,20 @@ struct BatchDownOp {
   int piece_no = 0;
 };
 
-template <int MPAD>
+template <int MPAD, bool FP8>
 __global__ void __launch_bounds__(kBThreads, 1) ffn_batch_upgate_kernel(const __grid_constant__ BatchMaps maps,
-                                                                        FfnArgs a, Scratch sc, int M) {
+                                                                        BatchArgs<FP8> a, Scratch sc, int M) {
   extern __shared__ __align__(1024) uint8_t smem[];
-  BatchUpGateOp<MPAD> op{&maps, a, sc, M};
-  batch_run<BatchShape<MPAD>>(op, smem, sc);
+  BatchUpGateOp<MPAD, FP8> op{&maps, a, sc, M};
+  batch_run<BatchShape<MPAD, FP8>>(op, smem, sc);
 }
 
-template <int MPAD>
+template <int MPAD, bool FP8>
 __global__ void __launch_bounds__(kBThreads, 1) ffn_batch_down_kernel(const __grid_constant__ BatchMaps maps,
-                                                                      FfnArgs a, Scratch sc, int M) {
+                                                                      BatchArgs<FP8> a, Scratch sc, int M) {
   extern __shared__ __align__(1024) uint8_t smem[];
-  BatchDownOp<MPAD> op{&maps, a, sc, M};
-  batch_run<BatchShape<MPAD>>(op, smem, sc);
+  BatchDownOp<MPAD, FP8> op{&maps, a, sc, M};
+  batch_run<BatchShape<MPAD, FP8>>(op, smem, sc);
 }
 
 // The down projection's pieces added per token, then the epilogue of the reference op
@@ -732,7 +807,16 @@ __global__ void __launch_bounds__(kBThreads, 1) ffn_batch_down_kernel(const __gr
 // tile's pieces are added in CTA order, so the result does not depend on timing.
 constexpr int kMaxDownPieces = 6;  // CTAs one down tile may span (checked at set-up)
 constexpr int kFinThreads = 768;  // 5 rows of H per thread: every load of a row in flight at once
-__global__ void __launch_bounds__(kFinThreads) ffn_batch_finalize_kernel(FfnArgs a, Scratch sc, int down_grid) {
+// The epilogue's operands (NVFP4: the reciprocal global scale, y = bf16(bf16(sum) g); FP8: the f32
+// per-row scales, y = bf16(sum s_row)).
+struct FinalizeArgs {
+  uint16_t* residual;
+  const uint16_t* post_rms;
+  const uint16_t* layer_scalar;
+  const float* down_global;  // NVFP4, else null
+  const float* down_scale;   // FP8 [H], else null
+};
+__global__ void __launch_bounds__(kFinThreads) ffn_batch_finalize_kernel(FinalizeArgs a, Scratch sc, int down_grid) {
   constexpr int kUpt = kL / kUnitK, kTiles = kH / kTileRows;
   constexpr int kTotal = kUpt * kTiles;
   constexpr int kMaxGrid = 1024;
@@ -761,7 +845,7 @@ __global__ void __launch_bounds__(kFinThreads) ffn_batch_finalize_kernel(FfnArgs
 #pragma unroll
   for (int q = 0; q < kRows; ++q) rbits[q] = __ldcg(res + threadIdx.x + q * kFinThreads);
   const uint32_t tag = (__ldcg(sc.counters + kBatchEpoch) << 1) | 1u;
-  const float g = *a.down_global;
+  const float g = a.down_global ? *a.down_global : 1.0f;
   unsigned long long w[kRows][kMaxDownPieces];
 #pragma unroll
   for (int q = 0; q < kRows; ++q) {  // every piece of every row in flight at once
@@ -793,7 +877,8 @@ __global__ void __launch_bounds__(kFinThreads) ffn_batch_finalize_kernel(FfnArgs
       }
       sum += __uint_as_float(uint32_t(w[q][k]));
     }
-    y[q] = bf16_round(bf16_round(sum) * g);
+    y[q] = a.down_scale ? bf16_round(sum * __ldg(a.down_scale + threadIdx.x + q * kFinThreads))
+                        : bf16_round(bf16_round(sum) * g);
     ss += double(y[q]) * double(y[q]);
   }
   const float inv = rms_inverse(block_sum_d(ss, red), kH);
@@ -823,65 +908,100 @@ cudaError_t launch_batch(void (*kernel)(KArgs...), int grid, int threads, size_t
   return cudaLaunchKernelEx(&cfg, kernel, std::forward<Args>(args)...);
 }
 
-template <int MPAD>
-cudaError_t launch_batch_t(const FfnArgs& a, int M, const LaunchEnv& env) {
-  using Shape = BatchShape<MPAD>;
-  BatchMaps ug{}, dn{};
+// The weight maps of each format (row-major: the reference layout; tiled: g4_pack_tiles).
+cudaError_t batch_maps(const FfnArgs& a, const LaunchEnv& env, BatchMaps& ug, BatchMaps& dn) {
   cudaError_t e;
   if (a.tiled) {
     if ((e = env.maps->u8(a.up_packed, 128, uint64_t(kL) / 64 * (kH / kUnitK) * kTileRows, 128, kTileRows, true,
                           &ug.a)))
       return e;
-    if ((e = env.maps->u8(a.down_packed, 128, uint64_t(kH) / kTileRows * (kL / kUnitK) * kTileRows, 128, kTileRows,
-                          true, &dn.a)))
-      return e;
-  } else {
-    if ((e = env.maps->u8(a.up_packed, kH / 2, kL, 128, 64, true, &ug.a))) return e;
-    if ((e = env.maps->u8(a.gate_packed, kH / 2, kL, 128, 64, true, &ug.a2))) return e;
-    if ((e = env.maps->u8(a.up_scale, kH / 16, kL, 16, 64, false, &ug.s))) return e;
-    if ((e = env.maps->u8(a.gate_scale, kH / 16, kL, 16, 64, false, &ug.s2))) return e;
-    if ((e = env.maps->u8(a.down_packed, kL / 2, kH, 128, kTileRows, true, &dn.a))) return e;
-    if ((e = env.maps->u8(a.down_scale, kL / 16, kH, 16, kTileRows, false, &dn.s))) return e;
+    return env.maps->u8(a.down_packed, 128, uint64_t(kH) / kTileRows * (kL / kUnitK) * kTileRows, 128, kTileRows,
+                        true, &dn.a);
   }
+  if ((e = env.maps->u8(a.up_packed, kH / 2, kL, 128, 64, true, &ug.a))) return e;
+  if ((e = env.maps->u8(a.gate_packed, kH / 2, kL, 128, 64, true, &ug.a2))) return e;
+  if ((e = env.maps->u8(a.up_scale, kH / 16, kL, 16, 64, false, &ug.s))) return e;
+  if ((e = env.maps->u8(a.gate_scale, kH / 16, kL, 16, 64, false, &ug.s2))) return e;
+  if ((e = env.maps->u8(a.down_packed, kL / 2, kH, 128, kTileRows, true, &dn.a))) return e;
+  return env.maps->u8(a.down_scale, kL / 16, kH, 16, kTileRows, false, &dn.s);
+}
+cudaError_t batch_maps(const Ffn8Args& a, const LaunchEnv& env, BatchMaps& ug, BatchMaps& dn) {
+  cudaError_t e;
+  if (a.tiled) {  // one 256-row box per unit (both K halves), as the M = 1 kernels read them
+    if ((e = env.maps->u8(a.up_w, 128, uint64_t(2 * kL) * (kH / 128), 128, 2 * kTileRows, true, &ug.a))) return e;
+    return env.maps->u8(a.down_w, 128, uint64_t(kH) * (kL / 128), 128, 2 * kTileRows, true, &dn.a);
+  }
+  if ((e = env.maps->u8(a.up_w, kH, kL, 128, 64, true, &ug.a))) return e;
+  if ((e = env.maps->u8(a.gate_w, kH, kL, 128, 64, true, &ug.a2))) return e;
+  return env.maps->u8(a.down_w, kL, kH, 128, kTileRows, true, &dn.a);
+}
+
+template <int MPAD, bool FP8>
+cudaError_t launch_batch_t(const BatchArgs<FP8>& a, int M, const LaunchEnv& env) {
+  using Shape = BatchShape<MPAD, FP8>;
+  using UG = BatchUpGateOp<MPAD, FP8>;
+  BatchMaps ug{}, dn{};
+  cudaError_t e;
+  if ((e = batch_maps(a, env, ug, dn))) return e;
   if ((e = env.maps->bf16(env.sc.batch_h, kH, uint64_t(M), 64, MPAD, &ug.b, /*half=*/true))) return e;
   if ((e = env.maps->bf16(env.sc.act, kL, uint64_t(M), 64, MPAD, &dn.b))) return e;
-  const int gu = env.sm_count < BatchUpGateOp<MPAD>::kUnitsPerTile * BatchUpGateOp<MPAD>::kTiles
-                     ? env.sm_count
-                     : BatchUpGateOp<MPAD>::kUnitsPerTile * BatchUpGateOp<MPAD>::kTiles;
+  const int gu = env.sm_count < UG::kUnitsPerTile * UG::kTiles ? env.sm_count : UG::kUnitsPerTile * UG::kTiles;
   const int gd = env.sm_count;
   Scratch su = env.sc, sd = env.sc;
 #ifdef G4_TRACE
   if (su.trace) su.trace += 11 * 4096;  // profiling builds: stamp rows of their own
   if (sd.trace) sd.trace += 12 * 4096;
 #endif
-  if ((e = launch_batch(ffn_batch_norm_kernel, M, 256, 0, env.pdl, env.stream, a, env.sc))) return e;
-  if ((e = launch_batch(ffn_batch_upgate_kernel<MPAD>, gu, kBThreads, Shape::kSmemBytes, true, env.stream, ug, a, su,
-                        M)))
+  if ((e = launch_batch(ffn_batch_norm_kernel, M, 256, 0, env.pdl, env.stream,
+                        static_cast<const uint16_t*>(a.residual), a.pre_rms, env.sc)))
     return e;
-  if ((e = launch_batch(ffn_batch_down_kernel<MPAD>, gd, kBThreads, Shape::kSmemBytes, true, env.stream, dn, a, sd,
-                        M)))
+  if ((e = launch_batch(ffn_batch_upgate_kernel<MPAD, FP8>, gu, kBThreads, Shape::kSmemBytes, true, env.stream, ug, a,
+                        su, M)))
     return e;
-  return launch_batch(ffn_batch_finalize_kernel, M, kFinThreads, 0, true, env.stream, a, env.sc, gd);
+  if ((e = launch_batch(ffn_batch_down_kernel<MPAD, FP8>, gd, kBThreads, Shape::kSmemBytes, true, env.stream, dn, a,
+                        sd, M)))
+    return e;
+  FinalizeArgs fa{a.residual, a.post_rms, a.layer_scalar, nullptr, nullptr};
+  if constexpr (FP8) {
+    fa.down_scale = a.down_s;
+  } else {
+    fa.down_global = a.down_global;
+  }
+  return launch_batch(ffn_batch_finalize_kernel, M, kFinThreads, 0, true, env.stream, fa, env.sc, gd);
 }
 
-template <int MPAD>
+template <int MPAD, bool FP8>
 cudaError_t prepare_batch_t() {
   cudaError_t e;
-  if ((e = cudaFuncSetAttribute(ffn_batch_upgate_kernel<MPAD>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                int(BatchShape<MPAD>::kSmemBytes))))
+  if ((e = cudaFuncSetAttribute(ffn_batch_upgate_kernel<MPAD, FP8>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                int(BatchShape<MPAD, FP8>::kSmemBytes))))
     return e;
-  return cudaFuncSetAttribute(ffn_batch_down_kernel<MPAD>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                              int(BatchShape<MPAD>::kSmemBytes));
+  return cudaFuncSetAttribute(ffn_batch_down_kernel<MPAD, FP8>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                              int(BatchShape<MPAD, FP8>::kSmemBytes));
+}
+
+template <bool FP8>
+cudaError_t launch_batch_any(const BatchArgs<FP8>& a, int M, const LaunchEnv& env) {
+  if (env.tp.world != 1) return cudaErrorNotSupported;  // the batched feed-forward runs on one GPU
+  if (M < 2 || M > kBatchMax) return cudaErrorInvalidValue;
+  switch ((M + 15) / 16) {
+    case 1: return launch_batch_t<16, FP8>(a, M, env);
+    case 2: return launch_batch_t<32, FP8>(a, M, env);
+    case 3: return launch_batch_t<48, FP8>(a, M, env);
+    default: return launch_batch_t<64, FP8>(a, M, env);
+  }
 }
 
 }  // namespace
 
 cudaError_t prepare_batch_kernels() {
   cudaError_t e;
-  if ((e = prepare_batch_t<16>())) return e;
-  if ((e = prepare_batch_t<32>())) return e;
-  if ((e = prepare_batch_t<48>())) return e;
-  return prepare_batch_t<64>();
+  if ((e = prepare_batch_t<16, false>()) || (e = prepare_batch_t<32, false>()) || (e = prepare_batch_t<48, false>()) ||
+      (e = prepare_batch_t<64, false>()))
+    return e;
+  if ((e = prepare_batch_t<16, true>()) || (e = prepare_batch_t<32, true>()) || (e = prepare_batch_t<48, true>()))
+    return e;
+  return prepare_batch_t<64, true>();
 }
 
 bool batch_geometry_fits(int sm_count) {
@@ -907,14 +1027,11 @@ bool batch_geometry_fits(int sm_count) {
 size_t batch_words_count(int sm_count) { return size_t(sm_count) * 2 * kBatchMax * kTileRows; }
 
 cudaError_t launch_ffn_nvfp4_batch(const FfnArgs& a, int M, const LaunchEnv& env) {
-  if (env.tp.world != 1) return cudaErrorNotSupported;  // the batched feed-forward runs on one GPU
-  if (M < 2 || M > kBatchMax) return cudaErrorInvalidValue;
-  switch ((M + 15) / 16) {
-    case 1: return launch_batch_t<16>(a, M, env);
-    case 2: return launch_batch_t<32>(a, M, env);
-    case 3: return launch_batch_t<48>(a, M, env);
-    default: return launch_batch_t<64>(a, M, env);
-  }
+  return launch_batch_any<false>(a, M, env);
+}
+
+cudaError_t launch_ffn_fp8_batch(const Ffn8Args& a, int M, const LaunchEnv& env) {
+  return launch_batch_any<true>(a, M, env);
 }
 
 }  // namespace g4

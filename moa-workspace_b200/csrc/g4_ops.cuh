@@ -194,6 +194,7 @@ cudaError_t prepare_batch_kernels();
 bool batch_geometry_fits(int sm_count);
 size_t batch_words_count(int sm_count);  // split-K words of the batched kernels
 cudaError_t launch_ffn_nvfp4_batch(const FfnArgs& a, int m, const LaunchEnv& env);
+cudaError_t launch_ffn_fp8_batch(const Ffn8Args& a, int m, const LaunchEnv& env);
 cudaError_t launch_full_qkv(const FullQkvArgs& a, const LaunchEnv& env);
 cudaError_t launch_full_attention(const FullAttnArgs& a, const LaunchEnv& env);
 cudaError_t launch_full_o(const FullOArgs& a, const LaunchEnv& env);

@@ -55,6 +55,8 @@ SIGNATURES = {
     "g4_decoder_feedforward_batch_tiled": [_p] * 12 + [_i32, _p],
     "g4_decoder_feedforward_fp8": [_p] * 11 + [_p],
     "g4_decoder_feedforward_fp8_tiled": [_p] * 10 + [_p],
+    "g4_decoder_feedforward_fp8_batch": [_p] * 11 + [_i32, _p],
+    "g4_decoder_feedforward_fp8_batch_tiled": [_p] * 10 + [_i32, _p],
     "g4_pack_tiles": [_p, _p, _p, _p, _i32, _i32, _i32, _i32, _p],
     "g4_sliding_attention_output_noalloc": [_p] * 5 + [_p],
     "g4_decoder_create": [_p, _p, _p],

@@ -455,6 +455,50 @@ def decoder_feedforward_fp8_tiled(device: Device, residual_hbm, pre_ff_rms_weigh
     _check(device, st, "decoder_feedforward_fp8_tiled")
 
 
+def decoder_feedforward_fp8_batch(device: Device, residual_hbm, pre_ff_rms_weight, up_weight, gate_weight, down_weight,
+                                  up_weight_scale, gate_weight_scale, down_weight_scale, post_ff_rms_weight,
+                                  layer_scalar, *, stream=None) -> None:
+    """decoder_feedforward_fp8 on each row of residual_hbm [m, H], m in [1, 64]: the weights are
+    read once for all m tokens. One GPU."""
+    bf = torch.bfloat16
+    m = _batch_rows(residual_hbm)
+    args = [
+        _arg(residual_hbm, "residual_hbm", bf, (m, H), device),
+        _arg(pre_ff_rms_weight, "pre_ff_rms_weight", bf, (H,), device),
+        _arg(up_weight, "up_weight", _BYTE_DTYPES, (L, H), device),
+        _arg(gate_weight, "gate_weight", _BYTE_DTYPES, (L, H), device),
+        _arg(down_weight, "down_weight", _BYTE_DTYPES, (H, L), device),
+        _arg(up_weight_scale, "up_weight_scale", torch.float32, (L,), device),
+        _arg(gate_weight_scale, "gate_weight_scale", torch.float32, (L,), device),
+        _arg(down_weight_scale, "down_weight_scale", torch.float32, (H,), device),
+        _arg(post_ff_rms_weight, "post_ff_rms_weight", bf, (H,), device),
+        _arg(layer_scalar, "layer_scalar", bf, (8,), device),
+    ]
+    st = _abi.lib().g4_decoder_feedforward_fp8_batch(device.handle, *args, m, _stream_ptr(stream, device.index))
+    _check(device, st, "decoder_feedforward_fp8_batch")
+
+
+def decoder_feedforward_fp8_batch_tiled(device: Device, residual_hbm, pre_ff_rms_weight, up_gate_weight_tiled,
+                                        down_weight_tiled, up_weight_scale, gate_weight_scale, down_weight_scale,
+                                        post_ff_rms_weight, layer_scalar, *, stream=None) -> None:
+    """decoder_feedforward_fp8_batch on weights packed by `pack_upgate_fp8` / `tile_weight(.., "down_weight")`."""
+    bf = torch.bfloat16
+    m = _batch_rows(residual_hbm)
+    args = [
+        _arg(residual_hbm, "residual_hbm", bf, (m, H), device),
+        _arg(pre_ff_rms_weight, "pre_ff_rms_weight", bf, (H,), device),
+        _arg(up_gate_weight_tiled, "up_gate_weight_tiled", _BYTE_DTYPES, (2 * L, H), device),
+        _arg(down_weight_tiled, "down_weight_tiled", _BYTE_DTYPES, (H, L), device),
+        _arg(up_weight_scale, "up_weight_scale", torch.float32, (L,), device),
+        _arg(gate_weight_scale, "gate_weight_scale", torch.float32, (L,), device),
+        _arg(down_weight_scale, "down_weight_scale", torch.float32, (H,), device),
+        _arg(post_ff_rms_weight, "post_ff_rms_weight", bf, (H,), device),
+        _arg(layer_scalar, "layer_scalar", bf, (8,), device),
+    ]
+    st = _abi.lib().g4_decoder_feedforward_fp8_batch_tiled(device.handle, *args, m, _stream_ptr(stream, device.index))
+    _check(device, st, "decoder_feedforward_fp8_batch_tiled")
+
+
 # GPU-native (unit-tiled) layout of each weight matrix: (unit_bytes, tile_rows). A unit is the
 # 256 K elements of a tile of rows (fp8: one tensor-memory-accelerator box of two 128-element
 # halves; nvfp4: 128 bytes of packed codes, or 16 block-scale bytes, per row); the units of a

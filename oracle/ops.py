@@ -269,6 +269,24 @@ def feedforward_fp8(residual, pre_rms_weight, up_w, gate_w, down_w, up_s, gate_s
     return mul_bf16(summed, np.full(summed.shape, np.asarray(layer_scalar).reshape(-1)[0], dtype=np.uint16))
 
 
+def feedforward_fp8_batch(residual, pre_rms_weight, up_w, gate_w, down_w, up_s, gate_s, down_s,
+                          post_rms_weight, layer_scalar, hidden=3840, inter=15360):
+    """feedforward_fp8 on each row of residual [M, H], row by row (the weights decoded once)."""
+    w_up = e4m3_to_f32(up_w).reshape(inter, hidden)
+    w_gate = e4m3_to_f32(gate_w).reshape(inter, hidden)
+    w_down = e4m3_to_f32(down_w).reshape(hidden, inter)
+    out = []
+    for r in np.asarray(residual).reshape(-1, hidden):
+        h = rms_norm(r, pre_rms_weight)
+        up = scaled_projection(h, w_up, up_s)
+        gate = scaled_projection(h, w_gate, gate_s)
+        act = mul_bf16(gelu_tanh(gate), up)
+        down = scaled_projection(act, w_down, down_s)
+        summed = add_bf16(r, rms_norm(down, post_rms_weight))
+        out.append(mul_bf16(summed, np.full(summed.shape, np.asarray(layer_scalar).reshape(-1)[0], dtype=np.uint16)))
+    return np.stack(out)
+
+
 # --- tensor parallelism (no reference counterpart: the reference runs a layer on one chip) ---
 # The O and down contractions are split over `world` K slices; each rank's f32 partial sums
 # are added in rank order and the one-chip epilogue follows. The other ops are per head or per

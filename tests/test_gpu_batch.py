@@ -125,3 +125,60 @@ def test_batch_rejects_bad_sizes(device, gauss):
         run_batch(device, d, np.zeros((65, 3840), np.uint16))
     with pytest.raises(ValueError):
         ops.decoder_feedforward_batch(device, dev_tensor(rows[0]), *([None] * 12))
+
+
+# --- FP8 weights with f32 per-row scales (BASELINE configs[0]'s format, batched)
+
+FP8_WEIGHTS = ("up_weight", "gate_weight", "down_weight", "up_weight_scale", "gate_weight_scale", "down_weight_scale")
+
+
+def run_batch8(device, d, residual, tiled=False):
+    from g4b200 import ops
+
+    res = dev_tensor(np.ascontiguousarray(residual))
+    w = {k: dev_tensor(d[k]) for k in FP8_WEIGHTS}
+    tail = [w["up_weight_scale"], w["gate_weight_scale"], w["down_weight_scale"], dev_tensor(d["post_ff_rms_weight"]),
+            dev_tensor(d["layer_scalar"])]
+    if tiled:
+        ug = ops.pack_upgate_fp8(device, w["up_weight"], w["gate_weight"])
+        dn = ops.tile_weight(device, "down_weight", w["down_weight"])
+        ops.decoder_feedforward_fp8_batch_tiled(device, res, dev_tensor(d["pre_ff_rms_weight"]), ug, dn, *tail)
+    else:
+        ops.decoder_feedforward_fp8_batch(device, res, dev_tensor(d["pre_ff_rms_weight"]), w["up_weight"],
+                                          w["gate_weight"], w["down_weight"], *tail)
+    device.check()
+    return host_bits(res)
+
+
+@pytest.fixture(scope="module")
+def gauss8():
+    d = gaussian.ffn_fp8()
+    rows = gaussian.bf16(np.random.default_rng(3065).standard_normal((64, 3840)))
+    want = oracle.feedforward_fp8_batch(rows, d["pre_ff_rms_weight"], *(d[k] for k in FP8_WEIGHTS),
+                                        d["post_ff_rms_weight"], d["layer_scalar"])
+    return d, rows, want
+
+
+@pytest.mark.parametrize("m", [2, 16, 33, 64])
+def test_fp8_batch_matches_oracle_row_by_row(device, gauss8, m):
+    """configs[0]'s FP8 FFN on M tokens of N(0,1) activations."""
+    d, rows, want = gauss8
+    got = run_batch8(device, d, rows[:m])
+    for i in range(m):
+        ok, maxd, exact = within(want[i], got[i], ATOL["decoder_feedforward"])
+        assert ok, (m, i, maxd)
+        assert exact > 0.95, (m, i, exact)
+
+
+def test_fp8_batch_tiled_identical_and_rows_independent(device, gauss8):
+    d, rows, _ = gauss8
+    got = run_batch8(device, d, rows[:40])
+    assert np.array_equal(run_batch8(device, d, rows[:40], tiled=True), got)
+    assert np.array_equal(run_batch8(device, d, rows[3:9]), got[3:9])
+
+
+def test_fp8_batch_of_one_is_the_single_token_op(device, gauss8):
+    from test_gpu_gaussian import run_ffn_fp8
+
+    d, rows, _ = gauss8
+    assert np.array_equal(run_batch8(device, d, rows[:1]), run_ffn_fp8(device, dict(d, residual=rows[0])).reshape(1, -1))
