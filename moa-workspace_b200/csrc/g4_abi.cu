@@ -104,6 +104,8 @@ g4_status g4_ctx_create(int device, g4_ctx** out) {
   if (e == cudaSuccess) e = g4::prepare_proj_kernels();
   if (e == cudaSuccess) e = g4::prepare_attention_kernels();
   if (e == cudaSuccess) e = g4::prepare_batch_kernels();
+  if (e == cudaSuccess) e = g4::prepare_batch_attn_kernels();
+  if (e == cudaSuccess) e = g4::prepare_logits_batch_kernels();
   if (e == cudaSuccess) e = cudaDeviceSynchronize();
   if (e != cudaSuccess) {
     if (ctx->scratch) cudaFree(ctx->scratch);
@@ -121,7 +123,7 @@ g4_status g4_ctx_create(int device, g4_ctx** out) {
   ctx->sc.batch_h = reinterpret_cast<uint16_t*>(base + off_bh);
   ctx->sc.batch_words = reinterpret_cast<unsigned long long*>(base + off_bw);
   ctx->sc.batch_unscale = reinterpret_cast<float*>(base + off_bu);
-  ctx->batch_ok = g4::batch_geometry_fits(ctx->sm_count);
+  ctx->batch_ok = g4::batch_geometry_fits(ctx->sm_count) && g4::batch_attn_geometry_fits(ctx->sm_count);
 #ifdef G4_TRACE
   ctx->sc.trace = reinterpret_cast<uint64_t*>(base + off_trace);
 #else
@@ -176,15 +178,25 @@ g4_status g4_ctx_check(g4_ctx* ctx, void* stream, uint32_t* flags) {
   return G4_OK;
 }
 
+// m tokens (sequences) in one call: 1..64, and more than one only on a one-GPU context
+static g4_status check_batch(g4_ctx* ctx, int32_t m) {
+  if (m < 1 || m > g4::kBatchMax) return fail(ctx, G4_ERR_INVALID_ARGUMENT, "%s", "m must be in [1, 64]");
+  if (m > 1 && (ctx->tp_world != 1 || !ctx->batch_ok))
+    return fail(ctx, G4_ERR_UNSUPPORTED, "%s", "a batch of tokens runs on a one-GPU context only");
+  return G4_OK;
+}
+
 static g4_status project_qkv(bool tiled, g4_ctx* ctx, const uint16_t* x, const uint8_t* q_weight, const uint8_t* k_weight,
                                  const uint8_t* v_weight, const uint16_t* q_weight_scale,
                                  const uint16_t* k_weight_scale, const uint16_t* v_weight_scale,
                                  const uint16_t* input_rms_weight, const uint16_t* q_rms_weight,
                                  const uint16_t* k_rms_weight, const int32_t* kv_offset, const int32_t* rope_offset,
                                  const uint16_t* cos, const uint16_t* sin, uint16_t* k_cache, uint16_t* v_cache,
-                                 uint16_t* q_out, int32_t ring_len, int32_t rope_rows, void* stream) {
+                                 uint16_t* q_out, int32_t ring_len, int32_t rope_rows, void* stream, int32_t m = 1) {
   if (!ctx) return G4_ERR_INVALID_ARGUMENT;
-  g4_status st = check_ptrs(ctx, {{x, "x"},
+  g4_status st = check_batch(ctx, m);
+  if (st != G4_OK) return st;
+  st = check_ptrs(ctx, {{x, "x"},
                                   {q_weight, "q_weight"},
                                   {k_weight, "k_weight"},
                                   {v_weight, "v_weight"},
@@ -211,14 +223,17 @@ static g4_status project_qkv(bool tiled, g4_ctx* ctx, const uint16_t* x, const u
   g4::QkvArgs a{x,        q_weight,      k_weight,  v_weight, q_weight_scale, k_weight_scale, v_weight_scale,
                 input_rms_weight, q_rms_weight, k_rms_weight, kv_offset, rope_offset, cos, sin,
                 k_cache,  v_cache,       q_out,     ring_len, rope_rows, tiled};
+  if (m > 1) return cuda_status(ctx, g4::launch_qkv_batch(a, m, env_of(ctx, stream)), "sliding_project_qkv_batch launch");
   return cuda_status(ctx, g4::launch_qkv(a, env_of(ctx, stream)), "sliding_project_qkv launch");
 }
 
 static g4_status sliding_attention(g4_ctx* ctx, const uint16_t* q, const uint16_t* k, const uint16_t* v,
                                    const float* mask, uint16_t* out_hbm, int32_t ring_len, float scale,
-                                   const int32_t* kv_offset, void* stream) {
+                                   const int32_t* kv_offset, void* stream, int32_t m = 1) {
   if (!ctx) return G4_ERR_INVALID_ARGUMENT;
-  g4_status st = check_ptrs(ctx, {{q, "q"}, {k, "k"}, {v, "v"}, {mask, "mask"}, {out_hbm, "out_hbm"}});
+  g4_status st = check_batch(ctx, m);
+  if (st != G4_OK) return st;
+  st = check_ptrs(ctx, {{q, "q"}, {k, "k"}, {v, "v"}, {mask, "mask"}, {out_hbm, "out_hbm"}});
   if (st != G4_OK) return st;
   if (ring_len <= 0 || ring_len % g4::attention_slot_multiple() != 0 || ring_len > g4::attention_max_ring())
     return fail(ctx, G4_ERR_UNSUPPORTED, "%s must be a positive multiple of 256, at most 8192", "ring_len");
@@ -226,6 +241,8 @@ static g4_status sliding_attention(g4_ctx* ctx, const uint16_t* q, const uint16_
   if ((st = check_tp(ctx)) != G4_OK) return st;
   DeviceGuard guard(ctx->device);
   g4::AttnArgs a{q, k, v, mask, out_hbm, ring_len, g4::kNs / ctx->tp_world, scale, kv_offset};
+  a.batch = m;
+  a.mask_stride = ring_len;
   return cuda_status(ctx, g4::launch_attention(a, env_of(ctx, stream)), "sliding_attention launch");
 }
 
@@ -243,9 +260,11 @@ g4_status g4_sliding_attention_after_qkv(g4_ctx* ctx, const uint16_t* q, const u
 
 static g4_status attention_output(bool tiled, g4_ctx* ctx, const uint16_t* x, const uint16_t* post_attn_rms_weight,
                                       const uint8_t* o_weight, const uint16_t* o_weight_scale,
-                                      uint16_t* residual_hbm, void* stream) {
+                                      uint16_t* residual_hbm, void* stream, int32_t m = 1) {
   if (!ctx) return G4_ERR_INVALID_ARGUMENT;
-  g4_status st = check_ptrs(ctx, {{x, "x"},
+  g4_status st = check_batch(ctx, m);
+  if (st != G4_OK) return st;
+  st = check_ptrs(ctx, {{x, "x"},
                                   {post_attn_rms_weight, "post_attn_rms_weight"},
                                   {o_weight, "o_weight"},
                                   {o_weight_scale, "o_weight_scale"},
@@ -254,6 +273,7 @@ static g4_status attention_output(bool tiled, g4_ctx* ctx, const uint16_t* x, co
   if ((st = check_tp(ctx)) != G4_OK) return st;
   DeviceGuard guard(ctx->device);
   g4::OArgs a{x, post_attn_rms_weight, o_weight, o_weight_scale, residual_hbm, tiled};
+  if (m > 1) return cuda_status(ctx, g4::launch_o_batch(a, m, env_of(ctx, stream)), "sliding_attention_output_batch launch");
   return cuda_status(ctx, g4::launch_o(a, env_of(ctx, stream)), "sliding_attention_output launch");
 }
 
@@ -328,6 +348,52 @@ g4_status g4_sliding_attention_output_tiled(g4_ctx* ctx, const uint16_t* x, cons
                                             const uint8_t* o_weight, const uint16_t* o_weight_scale,
                                             uint16_t* residual_hbm, void* stream) {
   return attention_output(true, ctx, x, post_attn_rms_weight, o_weight, o_weight_scale, residual_hbm, stream);
+}
+
+g4_status g4_sliding_project_qkv_batch(g4_ctx* ctx, const uint16_t* x, const uint8_t* q_weight,
+                                       const uint8_t* k_weight, const uint8_t* v_weight,
+                                       const uint16_t* q_weight_scale, const uint16_t* k_weight_scale,
+                                       const uint16_t* v_weight_scale, const uint16_t* input_rms_weight,
+                                       const uint16_t* q_rms_weight, const uint16_t* k_rms_weight,
+                                       const int32_t* kv_offset, const int32_t* rope_offset, const uint16_t* cos,
+                                       const uint16_t* sin, uint16_t* k_cache, uint16_t* v_cache, uint16_t* q_out,
+                                       int32_t ring_len, int32_t rope_rows, int32_t m, void* stream) {
+  return project_qkv(false, ctx, x, q_weight, k_weight, v_weight, q_weight_scale, k_weight_scale, v_weight_scale,
+                     input_rms_weight, q_rms_weight, k_rms_weight, kv_offset, rope_offset, cos, sin, k_cache, v_cache,
+                     q_out, ring_len, rope_rows, stream, m);
+}
+
+g4_status g4_sliding_project_qkv_batch_tiled(g4_ctx* ctx, const uint16_t* x, const uint8_t* q_weight,
+                                             const uint8_t* k_weight, const uint8_t* v_weight,
+                                             const uint16_t* q_weight_scale, const uint16_t* k_weight_scale,
+                                             const uint16_t* v_weight_scale, const uint16_t* input_rms_weight,
+                                             const uint16_t* q_rms_weight, const uint16_t* k_rms_weight,
+                                             const int32_t* kv_offset, const int32_t* rope_offset,
+                                             const uint16_t* cos, const uint16_t* sin, uint16_t* k_cache,
+                                             uint16_t* v_cache, uint16_t* q_out, int32_t ring_len, int32_t rope_rows,
+                                             int32_t m, void* stream) {
+  return project_qkv(true, ctx, x, q_weight, k_weight, v_weight, q_weight_scale, k_weight_scale, v_weight_scale,
+                     input_rms_weight, q_rms_weight, k_rms_weight, kv_offset, rope_offset, cos, sin, k_cache, v_cache,
+                     q_out, ring_len, rope_rows, stream, m);
+}
+
+g4_status g4_sliding_attention_batch(g4_ctx* ctx, const uint16_t* q, const uint16_t* k, const uint16_t* v,
+                                     const float* mask, uint16_t* out_hbm, int32_t ring_len, float scale,
+                                     const int32_t* kv_offset, int32_t m, void* stream) {
+  return sliding_attention(ctx, q, k, v, mask, out_hbm, ring_len, scale, kv_offset, stream, m);
+}
+
+g4_status g4_sliding_attention_output_batch(g4_ctx* ctx, const uint16_t* x, const uint16_t* post_attn_rms_weight,
+                                            const uint8_t* o_weight, const uint16_t* o_weight_scale,
+                                            uint16_t* residual_hbm, int32_t m, void* stream) {
+  return attention_output(false, ctx, x, post_attn_rms_weight, o_weight, o_weight_scale, residual_hbm, stream, m);
+}
+
+g4_status g4_sliding_attention_output_batch_tiled(g4_ctx* ctx, const uint16_t* x,
+                                                  const uint16_t* post_attn_rms_weight, const uint8_t* o_weight,
+                                                  const uint16_t* o_weight_scale, uint16_t* residual_hbm, int32_t m,
+                                                  void* stream) {
+  return attention_output(true, ctx, x, post_attn_rms_weight, o_weight, o_weight_scale, residual_hbm, stream, m);
 }
 
 g4_status g4_decoder_feedforward(g4_ctx* ctx, uint16_t* residual_hbm, const uint16_t* pre_ff_rms_weight,
@@ -405,6 +471,23 @@ g4_status g4_final_norm_and_logits(g4_ctx* ctx, const uint16_t* input, const uin
   DeviceGuard guard(ctx->device);
   return cuda_status(ctx, g4::launch_logits(input, rms_weight, lm_head_weight, out, vocab_rows, env_of(ctx, stream)),
                      "final_norm_and_logits launch");
+}
+
+g4_status g4_final_norm_and_logits_batch(g4_ctx* ctx, const uint16_t* input, const uint16_t* rms_weight,
+                                         const uint16_t* lm_head_weight, uint16_t* out, int32_t vocab_rows, int32_t m,
+                                         void* stream) {
+  if (!ctx) return G4_ERR_INVALID_ARGUMENT;
+  if (m < 1 || m > g4::kBatchMax) return fail(ctx, G4_ERR_INVALID_ARGUMENT, "%s", "m must be in [1, 64]");
+  g4_status st = check_ptrs(ctx, {{input, "input"}, {rms_weight, "rms_weight"}, {lm_head_weight, "lm_head_weight"},
+                                  {out, "out"}});
+  if (st != G4_OK) return st;
+  if (vocab_rows <= 0 || vocab_rows > g4::kVocab)
+    return fail(ctx, G4_ERR_INVALID_ARGUMENT, "%s must be in [1, 262144]", "vocab_rows");
+  DeviceGuard guard(ctx->device);
+  const g4::LaunchEnv env = env_of(ctx, stream);
+  const cudaError_t e = m > 1 ? g4::launch_logits_batch(input, rms_weight, lm_head_weight, out, vocab_rows, m, env)
+                              : g4::launch_logits(input, rms_weight, lm_head_weight, out, vocab_rows, env);
+  return cuda_status(ctx, e, "final_norm_and_logits_batch launch");
 }
 
 g4_status g4_full_project_qkv(g4_ctx* ctx, const uint16_t* x, const uint8_t* q_weight, const uint8_t* k_weight,

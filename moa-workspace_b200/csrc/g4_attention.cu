@@ -84,10 +84,14 @@ __global__ void __launch_bounds__(kThreads, 2) attention_kernel(const __grid_con
   AttnSmem<C>& sm = *reinterpret_cast<AttnSmem<C>*>(smem_raw);
   const int head = blockIdx.x / kChunks;
   const int chunk = int(cluster_ctarank());  // == blockIdx.x % kChunks
+  const int seq = blockIdx.y;                // the sequence of a batch (its own ring)
+  const size_t qrow0 = size_t(seq) * a.heads * kGs * kDs;
+  const float* mask = a.mask + size_t(seq) * a.mask_stride;
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
   constexpr int kSub = AttnSmem<C>::kSub;
   const int per = a.ring_len / kChunks;  // a multiple of 32, at most kMaxPer
-  const int slot0 = chunk * per;
+  const int slot0 = chunk * per;                  // in this sequence's ring
+  const int gslot0 = seq * a.ring_len + slot0;  // in the batched caches
   const int passes = (per + kSub - 1) / kSub;
   volatile uint32_t abort_flag = 0;  // this CTA's own waits only
   G4_STAMP(sc, 0);
@@ -103,14 +107,14 @@ __global__ void __launch_bounds__(kThreads, 2) attention_kernel(const __grid_con
     const int b = tid;
     if (b < count / kBox) {
       mbar_arrive_expect_tx(&bars[b], uint32_t(kBox) * kRowBytes);
-      tma_load_3d(dst + b * kBox * kRowBytes, map, 0, head, slot0 + first + b * kBox, &bars[b], policy);
+      tma_load_3d(dst + b * kBox * kRowBytes, map, 0, head, gslot0 + first + b * kBox, &bars[b], policy);
     }
   };
   const int first_rows = per < kSub ? per : kSub;
   // The slot the preceding QKV op writes, when the caller says which (-1: any row may change).
   int cur = -1;
   if (a.kv_offset) {
-    const int kv = __ldg(a.kv_offset);  // written before the QKV op ran, not by it
+    const int kv = __ldg(a.kv_offset + seq);  // written before the QKV op ran, not by it
     if (kv >= 0 && kv % (kPs * 2) == 0 && kv / (kPs * 2) < a.ring_len) cur = kv / (kPs * 2);
   }
   if (a.kv_offset) {
@@ -125,8 +129,8 @@ __global__ void __launch_bounds__(kThreads, 2) attention_kernel(const __grid_con
   {
     const int nb = per / kBox, skip = a.kv_offset ? first_rows / kBox : 0;
     for (int b = skip + tid; b < nb; b += kThreads) {
-      tma_prefetch_l2_3d(&maps.k, 0, head, slot0 + b * kBox);
-      tma_prefetch_l2_3d(&maps.v, 0, head, slot0 + b * kBox);
+      tma_prefetch_l2_3d(&maps.k, 0, head, gslot0 + b * kBox);
+      tma_prefetch_l2_3d(&maps.v, 0, head, gslot0 + b * kBox);
     }
   }
   __syncthreads();
@@ -146,7 +150,8 @@ __global__ void __launch_bounds__(kThreads, 2) attention_kernel(const __grid_con
     if (okb && tid < 2 * (kRowBytes / 16)) {  // 32 x 16 bytes per row, K then V
       const bool is_v = tid >= kRowBytes / 16;
       const int q16 = tid % (kRowBytes / 16);
-      const uint16_t* src = (is_v ? a.v_cache : a.k_cache) + (size_t(cur) * a.heads + head) * kDs;
+      const uint16_t* src =
+          (is_v ? a.v_cache : a.k_cache) + (size_t(seq * a.ring_len + cur) * a.heads + head) * kDs;
       const uint4 x = __ldcg(reinterpret_cast<const uint4*>(src) + q16);
       reinterpret_cast<uint4*>((is_v ? sm.v : sm.k) + t * kRowBytes)[q16] = x;
     }
@@ -165,7 +170,8 @@ __global__ void __launch_bounds__(kThreads, 2) attention_kernel(const __grid_con
   for (int g = 0; g < kGs; ++g) {
 #pragma unroll
     for (int c = 0; c < 4; ++c) {
-      const uint4 raw = __ldcg(reinterpret_cast<const uint4*>(a.q + (head * kGs + g) * kDs + c * 64 + part * 8));
+      const uint4 raw =
+          __ldcg(reinterpret_cast<const uint4*>(a.q + qrow0 + (head * kGs + g) * kDs + c * 64 + part * 8));
       const uint16_t* b = reinterpret_cast<const uint16_t*>(&raw);
 #pragma unroll
       for (int j = 0; j < 8; ++j) qv[g][c * 8 + j] = bf16_to_f32(b[j]);
@@ -242,7 +248,7 @@ __global__ void __launch_bounds__(kThreads, 2) attention_kernel(const __grid_con
   // probabilities and this CTA's denominator (fixed summation order)
   float s0 = 0.f, s1 = 0.f;
   for (int t = tid; t < per; t += kThreads) {
-    const float mk = a.mask[slot0 + t];
+    const float mk = mask[slot0 + t];
     const float p0 = fminf(expf(sm.score[t][0] - gm[0]), mk);
     const float p1 = fminf(expf(sm.score[t][1] - gm[1]), mk);
     s0 += p0;
@@ -308,7 +314,7 @@ __global__ void __launch_bounds__(kThreads, 2) attention_kernel(const __grid_con
   cluster_sync();  // the others are done reading this CTA's partials (and sm.out is complete)
   if (tid < kGs * kDimsPerCta * 2 / 16) {  // 16-byte stores: 4 per query head
     const int g = tid / (kDimsPerCta * 2 / 16), q = tid % (kDimsPerCta * 2 / 16);
-    reinterpret_cast<uint4*>(a.out + (head * kGs + g) * kDs + chunk * kDimsPerCta)[q] =
+    reinterpret_cast<uint4*>(a.out + qrow0 + (head * kGs + g) * kDs + chunk * kDimsPerCta)[q] =
         reinterpret_cast<const uint4*>(sm.out + g * kDimsPerCta)[q];
   }
   G4_STAMP(sc, 6);
@@ -556,9 +562,10 @@ cudaLaunchConfig_t full_attention_config(cudaStream_t stream, bool pdl, cudaLaun
 }
 
 template <int C>
-cudaLaunchConfig_t attention_config(int heads, cudaStream_t stream, bool pdl, cudaLaunchAttribute (&attr)[2]) {
+cudaLaunchConfig_t attention_config(int heads, cudaStream_t stream, bool pdl, cudaLaunchAttribute (&attr)[2],
+                                    int batch = 1) {
   cudaLaunchConfig_t cfg = {};
-  cfg.gridDim = dim3(heads * C);
+  cfg.gridDim = dim3(heads * C, batch);
   cfg.blockDim = dim3(kThreads);
   cfg.dynamicSmemBytes = sizeof(AttnSmem<C>);
   cfg.stream = stream;
@@ -630,9 +637,11 @@ int attention_max_ring() { return kMaxRing; }
 cudaError_t launch_attention(const AttnArgs& a, const LaunchEnv& env) {
   KvMaps maps;
   cudaError_t e;
-  if (a.heads < 1 || a.heads > kNs) return cudaErrorInvalidValue;
-  if ((e = env.maps->kv(a.k_cache, uint64_t(a.ring_len), uint32_t(a.heads), kDs, uint32_t(kBox), &maps.k))) return e;
-  if ((e = env.maps->kv(a.v_cache, uint64_t(a.ring_len), uint32_t(a.heads), kDs, uint32_t(kBox), &maps.v))) return e;
+  if (a.heads < 1 || a.heads > kNs || a.batch < 1 || a.batch > 65535) return cudaErrorInvalidValue;
+  if (a.batch > 1 && a.mask_stride < a.ring_len) return cudaErrorInvalidValue;
+  const uint64_t slots = uint64_t(a.ring_len) * uint64_t(a.batch);  // every sequence's ring, back to back
+  if ((e = env.maps->kv(a.k_cache, slots, uint32_t(a.heads), kDs, uint32_t(kBox), &maps.k))) return e;
+  if ((e = env.maps->kv(a.v_cache, slots, uint32_t(a.heads), kDs, uint32_t(kBox), &maps.v))) return e;
   Scratch sc = env.sc;
 #ifdef G4_TRACE
   if (sc.trace) sc.trace += 4096;  // profiling builds: separate stamp rows per kernel
@@ -642,10 +651,10 @@ cudaError_t launch_attention(const AttnArgs& a, const LaunchEnv& env) {
                    a.ring_len % (16 * kBox) == 0 && a.ring_len >= 2048 &&
                    a.ring_len <= 4 * 16 * AttnSmem<16>::kSub;  // 2 to 4 passes (shorter rings: measured faster at 8)
   if (c16) {
-    const cudaLaunchConfig_t cfg = attention_config<16>(a.heads, env.stream, env.pdl, attr);
+    const cudaLaunchConfig_t cfg = attention_config<16>(a.heads, env.stream, env.pdl, attr, a.batch);
     return cudaLaunchKernelEx(&cfg, attention_kernel<16>, maps, a, sc);
   }
-  const cudaLaunchConfig_t cfg = attention_config<8>(a.heads, env.stream, env.pdl, attr);
+  const cudaLaunchConfig_t cfg = attention_config<8>(a.heads, env.stream, env.pdl, attr, a.batch);
   return cudaLaunchKernelEx(&cfg, attention_kernel<8>, maps, a, sc);
 }
 

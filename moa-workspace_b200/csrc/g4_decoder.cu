@@ -3,7 +3,8 @@
 // offsets it uploads once per token, runtime.rs:231-247).
 //
 // The host keeps the model as a table of layers. A step is:
-//   decode_begin   from the device-resident {token, position}: every distinct ring's slot offset,
+//   decode_begin   from the device-resident {token, position} (one pair per sequence of a batch):
+//                  every distinct ring's slot offset,
 //                  the RoPE row offset, every ring's mask row (c <= min(position, ring - 1), the
 //                  reference's mask_s rows, runtime.rs:159-160) and the token's scaled embedding
 //   per layer      sliding_project_qkv, sliding_attention, sliding_attention_output and the NVFP4 or
@@ -13,6 +14,11 @@
 // before touching what that one writes), so the next kernel's weight copies start while the
 // previous one drains; g4_decoder_capture records the whole step as one CUDA graph, so a token
 // costs one graph launch and one 8-byte input update on the host.
+//
+// A decoder made for a batch of m sequences (g4_decoder_create_batch, m in 2..64, one GPU) runs
+// the batched ops instead (g4_batch_attn.cu, g4_batch.cu): each layer's weights are read once for
+// all m tokens, every sequence keeping its own ring in the layer's caches ([m][ring][Ns][Ds]) and
+// its own position.
 #include <vector>
 
 #include "g4_ctx.cuh"
@@ -27,33 +33,36 @@ constexpr int kBeginThreads = 256;
 constexpr int kBeginBlocks = 16;
 
 struct BeginArgs {
-  const int32_t* input;  // {token, position}
-  int32_t* rope_off;     // position * Ds * 2 (-1 when the position is outside the RoPE table)
-  int32_t* kv_off;       // [kMaxRings] (position % ring) * Ns * Ds * 2 (16-byte spaced)
-  float* mask;           // [kMaxRings][mask_stride]
+  const int32_t* input;  // [batch] {token, position}
+  int32_t* rope_off;     // [batch] position * Ds * 2 (-1 when the position is outside the RoPE table)
+  int32_t* kv_off;       // [kMaxRings][kv_stride] (position % ring) * Ns * Ds * 2, per sequence
+  float* mask;           // [kMaxRings][batch][mask_stride]
+  int batch, kv_stride;
   int rings[kMaxRings];
   int n_rings, mask_stride, rope_rows;
   const uint16_t* table;  // embedding table or null
   int vocab_rows;
-  uint16_t* hidden;
+  uint16_t* hidden;  // [batch][H]
 };
 
 __global__ void __launch_bounds__(kBeginThreads) decode_begin_kernel(BeginArgs a, Scratch sc) {
   pdl_wait_primary();  // the previous step's last kernels still read these buffers
-  const int token = __ldcg(a.input), pos = __ldcg(a.input + 1);
-  if (blockIdx.x == 0) {
-    if (threadIdx.x == 0) *a.rope_off = pos >= 0 && pos < a.rope_rows ? pos * kDs * 2 : -1;
-    if (threadIdx.x < a.n_rings) a.kv_off[4 * threadIdx.x] = pos >= 0 ? (pos % a.rings[threadIdx.x]) * kPs * 2 : -1;
+  for (int b = blockIdx.x; b < a.batch; b += gridDim.x) {  // sequence b's offsets and embedding
+    const int token = __ldcg(a.input + 2 * b), pos = __ldcg(a.input + 2 * b + 1);
+    if (threadIdx.x == 0) a.rope_off[b] = pos >= 0 && pos < a.rope_rows ? pos * kDs * 2 : -1;
+    if (threadIdx.x < a.n_rings)
+      a.kv_off[threadIdx.x * a.kv_stride + b] = pos >= 0 ? (pos % a.rings[threadIdx.x]) * kPs * 2 : -1;
     if (a.table) {
       if (token >= 0 && token < a.vocab_rows)
-        embed_row(a.table + size_t(token) * kH, a.hidden);
+        embed_row(a.table + size_t(token) * kH, a.hidden + size_t(b) * kH);
       else if (threadIdx.x == 0)
         atomicOr(sc.err, kErrTokenOffset);
     }
   }
-  const int total = a.n_rings * a.mask_stride;
+  const int per_ring = a.batch * a.mask_stride, total = a.n_rings * per_ring;
   for (int i = blockIdx.x * blockDim.x + threadIdx.x; i < total; i += gridDim.x * blockDim.x) {
-    const int k = i / a.mask_stride, c = i % a.mask_stride;
+    const int k = i / per_ring, b = (i / a.mask_stride) % a.batch, c = i % a.mask_stride;
+    const int pos = __ldcg(a.input + 2 * b + 1);
     const int row = pos < a.rings[k] - 1 ? pos : a.rings[k] - 1;
     a.mask[i] = c <= row ? 1.0f : 0.0f;
   }
@@ -70,6 +79,8 @@ struct g4_decoder {
   g4_model model{};
   int rings[g4::kMaxRings] = {};
   int n_rings = 0, mask_stride = 0;
+  int batch = 1;   // sequences per step
+  int kvs = 4;     // i32 spacing of the rings' kv offsets (16 bytes at batch 1)
   void* buf = nullptr;
   int32_t* input = nullptr;
   int32_t* rope_off = nullptr;
@@ -156,6 +167,8 @@ cudaError_t issue_step(g4_decoder* d, cudaStream_t stream) {
   for (int k = 0; k < g4::kMaxRings; ++k) b.rings[k] = k < d->n_rings ? d->rings[k] : 1;
   b.n_rings = d->n_rings;
   b.mask_stride = d->mask_stride;
+  b.batch = d->batch;
+  b.kv_stride = d->kvs;
   b.rope_rows = m.rope_rows;
   b.table = m.embedding_table;
   b.vocab_rows = m.vocab_rows;
@@ -174,6 +187,7 @@ cudaError_t issue_step(g4_decoder* d, cudaStream_t stream) {
     if (e != cudaSuccess) return e;
   }
   const int heads = g4::kNs / ctx->tp_world;
+  const int nb = d->batch;
   for (size_t i = 0; i < d->layers.size(); ++i) {
     const g4_layer& l = d->layers[i];
     const int r = d->ring_of[i];
@@ -204,17 +218,19 @@ cudaError_t issue_step(g4_decoder* d, cudaStream_t stream) {
     } else {
     const g4::QkvArgs qa{d->hidden,        l.q_weight,       l.k_weight,         l.v_weight,
                          l.q_weight_scale, l.k_weight_scale, l.v_weight_scale,   l.input_rms_weight,
-                         l.q_rms_weight,   l.k_rms_weight,   d->kv_off + 4 * r,  d->rope_off,
+                         l.q_rms_weight,   l.k_rms_weight,   d->kv_off + d->kvs * r,  d->rope_off,
                          global ? m.cos_global : m.cos_local,  global ? m.sin_global : m.sin_local,
                          l.k_cache,        l.v_cache,        d->q,               l.ring_len,
                          m.rope_rows,      tiled};
-    if ((e = g4::launch_qkv(qa, env)) != cudaSuccess) return e;
-    const g4::AttnArgs aa{d->q,      l.k_cache, l.v_cache,    d->mask + size_t(r) * d->mask_stride,
-                          d->attn,   l.ring_len, heads,        l.attn_scale,
-                          d->kv_off + 4 * r};  // the slot the QKV op above writes
+    if ((e = nb > 1 ? g4::launch_qkv_batch(qa, nb, env) : g4::launch_qkv(qa, env)) != cudaSuccess) return e;
+    g4::AttnArgs aa{d->q,      l.k_cache, l.v_cache,    d->mask + size_t(r) * nb * d->mask_stride,
+                    d->attn,   l.ring_len, heads,        l.attn_scale,
+                    d->kv_off + d->kvs * r};  // the slots the QKV op above writes
+    aa.batch = nb;
+    aa.mask_stride = d->mask_stride;
     if ((e = g4::launch_attention(aa, env)) != cudaSuccess) return e;
     const g4::OArgs oa{d->attn, l.post_attn_rms_weight, l.o_weight, l.o_weight_scale, d->hidden, tiled};
-    if ((e = g4::launch_o(oa, env)) != cudaSuccess) return e;
+    if ((e = nb > 1 ? g4::launch_o_batch(oa, nb, env) : g4::launch_o(oa, env)) != cudaSuccess) return e;
     }
     if (l.ffn == G4_FFN_FP8) {
       const g4::Ffn8Args fa{d->hidden,
@@ -228,7 +244,7 @@ cudaError_t issue_step(g4_decoder* d, cudaStream_t stream) {
                             l.post_ff_rms_weight,
                             l.layer_scalar,
                             tiled};
-      e = g4::launch_ffn_fp8(fa, env);
+      e = nb > 1 ? g4::launch_ffn_fp8_batch(fa, nb, env) : g4::launch_ffn_fp8(fa, env);
     } else {
       const g4::FfnArgs fa{d->hidden,
                            l.pre_ff_rms_weight,
@@ -244,12 +260,16 @@ cudaError_t issue_step(g4_decoder* d, cudaStream_t stream) {
                            l.post_ff_rms_weight,
                            l.layer_scalar,
                            tiled};
-      e = g4::launch_ffn_nvfp4(fa, env);
+      e = nb > 1 ? g4::launch_ffn_nvfp4_batch(fa, nb, env) : g4::launch_ffn_nvfp4(fa, env);
     }
     if (e != cudaSuccess) return e;
   }
-  if (m.lm_head_weight)
+  if (m.lm_head_weight) {
+    if (nb > 1)
+      return g4::launch_logits_batch(d->hidden, m.final_norm_weight, m.lm_head_weight, d->logits, m.lm_head_rows, nb,
+                                     env);
     return g4::launch_logits(d->hidden, m.final_norm_weight, m.lm_head_weight, d->logits, m.lm_head_rows, env);
+  }
   return cudaSuccess;
 }
 
@@ -269,9 +289,16 @@ size_t align_up(size_t n) { return (n + 255) & ~size_t(255); }
 extern "C" {
 
 g4_status g4_decoder_create(g4_ctx* ctx, const g4_model* model, g4_decoder** out) {
+  return g4_decoder_create_batch(ctx, model, 1, out);
+}
+
+g4_status g4_decoder_create_batch(g4_ctx* ctx, const g4_model* model, int32_t batch, g4_decoder** out) {
   if (!ctx) return G4_ERR_INVALID_ARGUMENT;
   if (!out || !model) return fail(ctx, G4_ERR_INVALID_ARGUMENT, "null pointer: %s", out ? "model" : "out");
   *out = nullptr;
+  if (batch < 1 || batch > g4::kBatchMax) return fail(ctx, G4_ERR_INVALID_ARGUMENT, "%s", "batch must be in [1, 64]");
+  if (batch > 1 && (ctx->tp_world != 1 || !ctx->batch_ok))
+    return fail(ctx, G4_ERR_UNSUPPORTED, "%s", "a batch of sequences runs on a one-GPU context only");
   const g4_model& m = *model;
   if (m.n_layers < 0 || (m.n_layers > 0 && !m.layers))
     return fail(ctx, G4_ERR_INVALID_ARGUMENT, "%s", "model.layers / n_layers");
@@ -294,10 +321,16 @@ g4_status g4_decoder_create(g4_ctx* ctx, const g4_model* model, g4_decoder** out
   g4_decoder* d = new g4_decoder();
   d->ctx = ctx;
   d->layers.assign(m.layers, m.layers + m.n_layers);
+  d->batch = batch;
+  d->kvs = batch > 1 ? (batch + 3) / 4 * 4 : 4;
   for (const g4_layer& l : d->layers) {
     if ((st = check_layer(ctx, l)) != G4_OK) {
       delete d;
       return st;
+    }
+    if (batch > 1 && l.kind == G4_LAYER_FULL) {
+      delete d;
+      return fail(ctx, G4_ERR_UNSUPPORTED, "%s", "a batched decoder runs sliding-geometry layers only");
     }
     if (l.kind == G4_LAYER_FULL && (!m.cos_full || !m.sin_full)) {
       delete d;
@@ -333,13 +366,17 @@ g4_status g4_decoder_create(g4_ctx* ctx, const g4_model* model, g4_decoder** out
   }
   d->model = m;
   d->model.layers = nullptr;  // the decoder's own copy is d->layers
-  // device buffers: control words | hidden | q | attention | logits | masks
-  const size_t off_hidden = 256;
-  const size_t off_q = off_hidden + align_up(size_t(g4::kH) * 2);
-  const size_t off_attn = off_q + align_up(size_t(g4::kQs) * 2);
-  const size_t off_logits = off_attn + align_up(size_t(g4::kQs) * 2);
-  const size_t off_mask = off_logits + align_up(size_t(m.lm_head_weight ? m.lm_head_rows : 0) * 2);
-  const size_t off_full = off_mask + align_up(size_t(d->n_rings) * d->mask_stride * sizeof(float));
+  // device buffers: control words (inputs | rope offsets | kv offsets) | hidden | q | attention |
+  // logits | masks, the per-sequence ones `batch` times
+  const size_t nb = size_t(batch);
+  const size_t off_rope = align_up(nb * 2 * sizeof(int32_t));
+  const size_t off_kv = off_rope + align_up(nb * sizeof(int32_t));
+  const size_t off_hidden = off_kv + align_up(size_t(g4::kMaxRings) * d->kvs * sizeof(int32_t));
+  const size_t off_q = off_hidden + align_up(nb * g4::kH * 2);
+  const size_t off_attn = off_q + align_up(nb * g4::kQs * 2);
+  const size_t off_logits = off_attn + align_up(nb * g4::kQs * 2);
+  const size_t off_mask = off_logits + align_up(nb * size_t(m.lm_head_weight ? m.lm_head_rows : 0) * 2);
+  const size_t off_full = off_mask + align_up(size_t(d->n_rings) * nb * d->mask_stride * sizeof(float));
   const size_t total = off_full + 2 * align_up(size_t(g4::kQf) * 2) + 2 * align_up(g4::kGf * sizeof(float));
   DeviceGuard guard(ctx->device);
   cudaError_t e = cudaMalloc(&d->buf, total);
@@ -352,8 +389,8 @@ g4_status g4_decoder_create(g4_ctx* ctx, const g4_model* model, g4_decoder** out
   }
   uint8_t* base = static_cast<uint8_t*>(d->buf);
   d->input = reinterpret_cast<int32_t*>(base);
-  d->rope_off = reinterpret_cast<int32_t*>(base + 16);
-  d->kv_off = reinterpret_cast<int32_t*>(base + 32);  // 16 bytes per ring
+  d->rope_off = reinterpret_cast<int32_t*>(base + off_rope);
+  d->kv_off = reinterpret_cast<int32_t*>(base + off_kv);  // kvs i32 per ring
   d->hidden = reinterpret_cast<uint16_t*>(base + off_hidden);
   d->q = reinterpret_cast<uint16_t*>(base + off_q);
   d->attn = reinterpret_cast<uint16_t*>(base + off_attn);

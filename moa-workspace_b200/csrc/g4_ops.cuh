@@ -48,6 +48,11 @@ struct AttnArgs {
   // row of the cache is final, so the first pass's K and V rows are loaded before the wait on
   // that op and only the slot's rows after it (null: every row after the wait)
   const int32_t* kv_offset = nullptr;
+  // a batch of sequences (g4_sliding_attention_batch): sequence b's query / output rows at
+  // b heads Gs Ds, its ring at slots [b ring_len, (b + 1) ring_len) of the caches, its mask row at
+  // b mask_stride and its kv_offset at kv_offset[b]
+  int batch = 1;
+  int mask_stride = 0;
 };
 
 struct OArgs {
@@ -195,6 +200,17 @@ bool batch_geometry_fits(int sm_count);
 size_t batch_words_count(int sm_count);  // split-K words of the batched kernels
 cudaError_t launch_ffn_nvfp4_batch(const FfnArgs& a, int m, const LaunchEnv& env);
 cudaError_t launch_ffn_fp8_batch(const Ffn8Args& a, int m, const LaunchEnv& env);
+// The attention block's projections on m = 2..64 tokens (g4_batch_attn.cu), one GPU. QKV: x, q_out
+// [m][...], kv_offset / rope_offset [m], token i's ring at slots [i ring_len, (i + 1) ring_len) of
+// the caches. O: x (the attention rows) and residual [m][...].
+cudaError_t prepare_batch_attn_kernels();
+bool batch_attn_geometry_fits(int sm_count);
+cudaError_t launch_qkv_batch(const QkvArgs& a, int m, const LaunchEnv& env);
+cudaError_t launch_o_batch(const OArgs& a, int m, const LaunchEnv& env);
+// final_norm_and_logits on m = 2..64 tokens (g4_logits_batch.cu): input [m][H], out [m][rows].
+cudaError_t prepare_logits_batch_kernels();
+cudaError_t launch_logits_batch(const uint16_t* input, const uint16_t* gamma, const uint16_t* weight, uint16_t* out,
+                                int rows, int m, const LaunchEnv& env);
 cudaError_t launch_full_qkv(const FullQkvArgs& a, const LaunchEnv& env);
 cudaError_t launch_full_attention(const FullAttnArgs& a, const LaunchEnv& env);
 cudaError_t launch_full_o(const FullOArgs& a, const LaunchEnv& env);

@@ -57,6 +57,13 @@ SIGNATURES = {
     "g4_decoder_feedforward_fp8_tiled": [_p] * 10 + [_p],
     "g4_decoder_feedforward_fp8_batch": [_p] * 11 + [_i32, _p],
     "g4_decoder_feedforward_fp8_batch_tiled": [_p] * 10 + [_i32, _p],
+    "g4_final_norm_and_logits_batch": [_p] * 5 + [_i32, _i32, _p],
+    "g4_decoder_create_batch": [_p, _p, _i32, _p],
+    "g4_sliding_project_qkv_batch": [_p] * 18 + [_i32, _i32, _i32, _p],
+    "g4_sliding_project_qkv_batch_tiled": [_p] * 18 + [_i32, _i32, _i32, _p],
+    "g4_sliding_attention_batch": [_p, _p, _p, _p, _p, _p, _i32, _f32, _p, _i32, _p],
+    "g4_sliding_attention_output_batch": [_p] * 6 + [_i32, _p],
+    "g4_sliding_attention_output_batch_tiled": [_p] * 6 + [_i32, _p],
     "g4_pack_tiles": [_p, _p, _p, _p, _i32, _i32, _i32, _i32, _p],
     "g4_sliding_attention_output_noalloc": [_p] * 5 + [_p],
     "g4_decoder_create": [_p, _p, _p],

@@ -84,8 +84,9 @@ class Layer:
 
     @property
     def ring_len(self) -> int:
-        """KV slots: a sliding ring [slots, Ns, Ds], or a full layer's pages [slots, Df]."""
-        return self.k_cache.shape[0]
+        """KV slots: a sliding ring [slots, Ns, Ds] (a batched decoder's [batch, slots, Ns, Ds]), or a
+        full layer's pages [slots, Df]."""
+        return self.k_cache.shape[1] if self.k_cache.dim() == 4 else self.k_cache.shape[0]
 
 
 def _ptr(t):
@@ -94,12 +95,17 @@ def _ptr(t):
 
 class Decoder:
     """g4_decoder over `layers` on `device` (an ops.Device). The tensors must stay alive as long
-    as the decoder does (it keeps references)."""
+    as the decoder does (it keeps references).
+
+    batch > 1 (g4_decoder_create_batch, one GPU, sliding-geometry layers): `batch` sequences per
+    step; every layer's k_cache / v_cache is [batch, ring, Ns, Ds] (a ring per sequence), and
+    input / hidden / logits hold one row per sequence."""
 
     def __init__(self, device: Device, layers: list[Layer], *, cos_local, sin_local, cos_global=None,
                  sin_global=None, embedding_table=None, final_norm_weight=None, lm_head_weight=None, cos_full=None,
-                 sin_full=None):
+                 sin_full=None, batch: int = 1):
         self.device = device
+        self.batch = int(batch)
         self._keep = (layers, cos_local, sin_local, cos_global, sin_global, embedding_table, final_norm_weight,
                       lm_head_weight, cos_full, sin_full)
         arr = (_Layer * max(1, len(layers)))()
@@ -126,14 +132,14 @@ class Decoder:
         m.cos_full, m.sin_full = _ptr(cos_full).value, _ptr(sin_full).value
         self._model = m
         self._dec = ctypes.c_void_p()
-        _check(device, _abi.lib().g4_decoder_create(device.handle, ctypes.byref(m), ctypes.byref(self._dec)),
-               "g4_decoder_create")
+        _check(device, _abi.lib().g4_decoder_create_batch(device.handle, ctypes.byref(m), self.batch,
+                                                          ctypes.byref(self._dec)), "g4_decoder_create_batch")
         inp, hid, log = ctypes.c_void_p(), ctypes.c_void_p(), ctypes.c_void_p()
         _check(device, _abi.lib().g4_decoder_buffers(self._dec, ctypes.byref(inp), ctypes.byref(hid),
                                                       ctypes.byref(log)), "g4_decoder_buffers")
         self.input_ptr, self.hidden_ptr, self.logits_ptr = inp.value, hid.value, log.value
         self.lm_head_rows = m.lm_head_rows
-        self._host_input = torch.zeros(2, dtype=torch.int32).pin_memory()
+        self._host_input = torch.zeros(2 * self.batch, dtype=torch.int32).pin_memory()
 
     def close(self) -> None:
         if self._dec:
@@ -147,27 +153,35 @@ class Decoder:
             pass
 
     def input_view(self) -> torch.Tensor:
-        """The device-resident {token, position} (i32 [2]) as a tensor view."""
-        return _device_view(self.input_ptr, 2, torch.int32, self.device.index)
+        """The device-resident {token, position} (i32 [2], or [batch * 2]) as a tensor view."""
+        return _device_view(self.input_ptr, 2 * self.batch, torch.int32, self.device.index)
 
     def hidden(self) -> torch.Tensor:
-        """The hidden state [H] bf16 (a view of the decoder's buffer)."""
-        return _device_view(self.hidden_ptr, 3840, torch.bfloat16, self.device.index)
+        """The hidden state [H] bf16 ([batch, H] for a batch; a view of the decoder's buffer)."""
+        t = _device_view(self.hidden_ptr, 3840 * self.batch, torch.bfloat16, self.device.index)
+        return t.view(self.batch, 3840) if self.batch > 1 else t
 
     def logits(self) -> torch.Tensor:
         if not self.logits_ptr:
             raise ValueError("the model has no lm_head")
-        return _device_view(self.logits_ptr, self.lm_head_rows, torch.bfloat16, self.device.index)
+        t = _device_view(self.logits_ptr, self.lm_head_rows * self.batch, torch.bfloat16, self.device.index)
+        return t.view(self.batch, self.lm_head_rows) if self.batch > 1 else t
 
-    def set_input(self, token: int, position: int, stream=None) -> None:
-        """Write {token, position} on the stream (from pinned host memory)."""
+    def set_input(self, token, position, stream=None) -> None:
+        """Write {token, position} on the stream (from pinned host memory); for a batch, one token
+        and one position per sequence (sequences of length batch)."""
         s = stream if stream is not None else torch.cuda.current_stream(self.device.index)
         s.synchronize()  # the pinned staging buffer may still feed the previous copy
-        self._host_input[0], self._host_input[1] = token, position
+        tokens = [token] if self.batch == 1 and not hasattr(token, "__len__") else list(token)
+        positions = [position] if self.batch == 1 and not hasattr(position, "__len__") else list(position)
+        if len(tokens) != self.batch or len(positions) != self.batch:
+            raise ValueError(f"expected {self.batch} tokens and positions")
+        for i, (t, p) in enumerate(zip(tokens, positions)):
+            self._host_input[2 * i], self._host_input[2 * i + 1] = int(t), int(p)
         with torch.cuda.stream(s):
             self.input_view().copy_(self._host_input, non_blocking=True)
 
-    def step(self, token: int | None = None, position: int | None = None, stream=None) -> None:
+    def step(self, token=None, position=None, stream=None) -> None:
         if token is not None:
             self.set_input(token, position, stream)
         _check(self.device, _abi.lib().g4_decoder_step(self._dec, _stream_ptr(stream, self.device.index)),

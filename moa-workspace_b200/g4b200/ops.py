@@ -145,6 +145,18 @@ def final_norm_and_logits(device: Device, input, rms_weight, lm_head_weight, out
     _check(device, st, "final_norm_and_logits")
 
 
+def final_norm_and_logits_batch(device: Device, input, rms_weight, lm_head_weight, out, *, stream=None) -> None:
+    """final_norm_and_logits on each row of input [m, H] (m in [1, 64]), out [m, rows]: the table is
+    read once for all m (tcgen05 tiles when rows is a multiple of 128)."""
+    bf = torch.bfloat16
+    m = _batch_of(input, "input", 2)
+    rows = lm_head_weight.shape[0] if lm_head_weight.dim() == 2 else -1
+    args = [_arg(input, "input", bf, (m, H), device), _arg(rms_weight, "rms_weight", bf, (H,), device),
+            _arg(lm_head_weight, "lm_head_weight", bf, (rows, H), device), _arg(out, "out", bf, (m, rows), device)]
+    st = _abi.lib().g4_final_norm_and_logits_batch(device.handle, *args, rows, m, _stream_ptr(stream, device.index))
+    _check(device, st, "final_norm_and_logits_batch")
+
+
 GF, DF, QF, TF = 16, 512, 8192, 512  # global layers: query heads, head dim, q rows, page slots
 
 
@@ -453,6 +465,87 @@ def decoder_feedforward_fp8_tiled(device: Device, residual_hbm, pre_ff_rms_weigh
     ]
     st = _abi.lib().g4_decoder_feedforward_fp8_tiled(device.handle, *args, _stream_ptr(stream, device.index))
     _check(device, st, "decoder_feedforward_fp8_tiled")
+
+
+def _batch_of(t, name, dims) -> int:
+    m = t.shape[0] if t.dim() == dims else 0
+    if not 1 <= m <= BATCH_MAX:
+        raise ValueError(f"{name}: shape {tuple(t.shape)}, expected {dims} dimensions with the first, m, in [1, {BATCH_MAX}]")
+    return m
+
+
+def sliding_project_qkv_batch(device: Device, x, q_weight, k_weight, v_weight, q_weight_scale, k_weight_scale,
+                              v_weight_scale, input_rms_weight, q_rms_weight, k_rms_weight, kv_offset, rope_offset,
+                              cos, sin, k_cache, v_cache, q_out, *, tiled=False, stream=None) -> None:
+    """sliding_project_qkv (src/ops.rs:37-76) on each of m sequences, the weights read once for all m:
+    x [m, H]; kv_offset / rope_offset [m] i32 byte offsets; k_cache / v_cache [m, ring, Ns, Ds]
+    (sequence i's ring at [i]); q_out [m, Ns, Gs, Ds]. m in [1, 64]; one GPU."""
+    bf = torch.bfloat16
+    m = _batch_of(x, "x", 2)
+    ring = k_cache.shape[1] if k_cache.dim() == 4 else -1
+    rows = cos.shape[0] if cos.dim() == 2 else -1
+    args = [
+        _arg(x, "x", bf, (m, H), device),
+        _arg(q_weight, "q_weight", _BYTE_DTYPES, (QS, H), device),
+        _arg(k_weight, "k_weight", _BYTE_DTYPES, (PS, H), device),
+        _arg(v_weight, "v_weight", _BYTE_DTYPES, (PS, H), device),
+        _arg(q_weight_scale, "q_weight_scale", bf, (QS,), device),
+        _arg(k_weight_scale, "k_weight_scale", bf, (PS,), device),
+        _arg(v_weight_scale, "v_weight_scale", bf, (PS,), device),
+        _arg(input_rms_weight, "input_rms_weight", bf, (H,), device),
+        _arg(q_rms_weight, "q_rms_weight", bf, (DS,), device),
+        _arg(k_rms_weight, "k_rms_weight", bf, (DS,), device),
+        _arg(kv_offset, "kv_offset", torch.int32, (m,), device),
+        _arg(rope_offset, "rope_offset", torch.int32, (m,), device),
+        _arg(cos, "cos", bf, (rows, DS), device),
+        _arg(sin, "sin", bf, (rows, DS), device),
+        _arg(k_cache, "k_cache", bf, (m, ring, NS, DS), device),
+        _arg(v_cache, "v_cache", bf, (m, ring, NS, DS), device),
+        _arg(q_out, "q_out", bf, (m, NS, GS, DS), device),
+    ]
+    fn = _abi.lib().g4_sliding_project_qkv_batch_tiled if tiled else _abi.lib().g4_sliding_project_qkv_batch
+    st = fn(device.handle, *args, ring, rows, m, _stream_ptr(stream, device.index))
+    _check(device, st, "sliding_project_qkv_batch")
+
+
+def sliding_attention_batch(device: Device, q, k, v, mask, out_hbm, *, scale: float = 1.0, kv_offset=None,
+                            stream=None) -> None:
+    """sliding_attention (src/ops.rs:118-128) on each of m sequences: q / out_hbm [m, Ns, Gs, Ds],
+    k / v [m, ring, Ns, Ds], mask [m, ring] f32, kv_offset None or the [m] i32 the batched QKV op
+    just got. m in [1, 64]; one GPU."""
+    bf = torch.bfloat16
+    m = _batch_of(q, "q", 4)
+    ring = k.shape[1] if k.dim() == 4 else -1
+    args = [
+        _arg(q, "q", bf, (m, NS, GS, DS), device),
+        _arg(k, "k", bf, (m, ring, NS, DS), device),
+        _arg(v, "v", bf, (m, ring, NS, DS), device),
+        _arg(mask, "mask", torch.float32, (m, ring), device),
+        _arg(out_hbm, "out_hbm", bf, (m, NS, GS, DS), device),
+    ]
+    off = None if kv_offset is None else _arg(kv_offset, "kv_offset", torch.int32, (m,), device)
+    st = _abi.lib().g4_sliding_attention_batch(device.handle, *args, ring, float(scale), off, m,
+                                               _stream_ptr(stream, device.index))
+    _check(device, st, "sliding_attention_batch")
+
+
+def sliding_attention_output_batch(device: Device, x, post_attn_rms_weight, o_weight, o_weight_scale, residual_hbm, *,
+                                   tiled=False, stream=None) -> None:
+    """sliding_attention_output (src/ops.rs:130-146) on each of m sequences: x [m, Ns, Gs, Ds],
+    residual_hbm [m, H] updated in place; the O weights read once for all m. m in [1, 64]; one GPU."""
+    bf = torch.bfloat16
+    m = _batch_of(residual_hbm, "residual_hbm", 2)
+    args = [
+        _arg(x, "x", bf, (m, NS, GS, DS), device),
+        _arg(post_attn_rms_weight, "post_attn_rms_weight", bf, (H,), device),
+        _arg(o_weight, "o_weight", _BYTE_DTYPES, (H, QS), device),
+        _arg(o_weight_scale, "o_weight_scale", bf, (H,), device),
+        _arg(residual_hbm, "residual_hbm", bf, (m, H), device),
+    ]
+    fn = (_abi.lib().g4_sliding_attention_output_batch_tiled if tiled
+          else _abi.lib().g4_sliding_attention_output_batch)
+    st = fn(device.handle, *args, m, _stream_ptr(stream, device.index))
+    _check(device, st, "sliding_attention_output_batch")
 
 
 def decoder_feedforward_fp8_batch(device: Device, residual_hbm, pre_ff_rms_weight, up_weight, gate_weight, down_weight,
