@@ -31,6 +31,9 @@ scales (the feed-forward's f32), 48 distinct layers (10.8 GB), so no step reads 
 - roofline: the dominant kernel pair, decoder_feedforward_fp8 (177.1 MB per call, configs[0]).
 - cpu_baseline / --impl reference: the CPU oracle port (numpy, test infrastructure) running the
   same decode step on this host's cores, with every host thread.
+- decode_batch (one GPU): configs[4]'s batches 8 and 32 - that many sequences decoded together by
+  a batched decoder (g4_decoder_create_batch: the same 48 layers, each cache holding one ring per
+  sequence), tokens/s = sequences x K / the device time of exactly K steps after W.
 
 Synthetic data (no checkpoint exists on the box): weights ~N(0, 0.02) quantised the way
 BASELINE.json describes, the embedding / lm_head table ~N(0, 0.03) bf16, caches ~N(0, 1).
@@ -60,7 +63,8 @@ RING_LOCAL, RING_GLOBAL = 1024, 4096
 NVFP4_COPIES = 4      # NVFP4 layer copies for the configs[3] per-op timing (> 3x L2 together)
 POSITION = 4000       # the decoded token's position (context 4096)
 KERNELS_PER_LAYER = 5  # qkv, attention, o, ffn up/gate, ffn down
-BATCH_SWEEP = (8, 16, 64)  # configs[3]: the NVFP4 feed-forward's token batches beyond M = 1
+BATCH_SWEEP = (8, 16, 64)
+DECODE_BATCHES = (8, 32)  # configs[4]'s batches beyond 1: sequences decoded together (one GPU)  # configs[3]: the NVFP4 feed-forward's token batches beyond M = 1
 
 
 def is_global(i):
@@ -369,6 +373,47 @@ class Model:
 
     def tables_of(self, lay):
         return (self.cos_g, self.sin_g) if lay.ring == RING_GLOBAL else (self.cos_l, self.sin_l)
+
+
+def batched_decoder(m: "Model", ops_device, nb, dev):
+    """The benchmark model's decoder over `nb` sequences (g4_decoder_create_batch): the same layers,
+    every layer's caches holding nb seeded rings ([nb, ring, Ns, Ds])."""
+    import dataclasses
+
+    import torch
+    from g4b200 import decoder
+
+    gen = torch.Generator(device=dev)
+    gen.manual_seed(2000 + nb)
+    layers = []
+    for lay in m.layers:
+        shape = (nb, lay.ring, NS // m.world, DS)
+        k = torch.randn(shape, generator=gen, device=dev).to(torch.bfloat16)
+        v = torch.randn(shape, generator=gen, device=dev).to(torch.bfloat16)
+        layers.append(dataclasses.replace(lay.for_decoder(ATTN_SCALE), k_cache=k, v_cache=v))
+    return decoder.Decoder(ops_device, layers, cos_local=m.cos_l, sin_local=m.sin_l, cos_global=m.cos_g,
+                           sin_global=m.sin_g, embedding_table=m.table, final_norm_weight=m.final_norm,
+                           lm_head_weight=m.lm_head, batch=nb)
+
+
+def time_decode_batch(torch, m: "Model", device, dev, nb, steps, warmup):
+    """Decode tokens/s of `nb` sequences decoded together: exactly `warmup` then `steps` replays of
+    the batched decoder's graph (each step: nb tokens through the 48 layers and the lm_head)."""
+    dec = batched_decoder(m, device, nb, dev)
+    stream = torch.cuda.Stream(dev)
+    dec.set_input([1234 + 7 * i for i in range(nb)], [POSITION - i for i in range(nb)], stream=stream)
+    dec.capture(stream=stream)
+    with torch.cuda.stream(stream):
+        for _ in range(warmup):
+            dec.step(stream=stream)
+        torch.cuda.synchronize()
+        secs = timed(torch, lambda: [dec.step(stream=stream) for _ in range(steps)])
+    device.check()
+    dec.close()
+    del dec
+    torch.cuda.empty_cache()
+    return {"tokens_per_s": round(nb * steps / secs, 1), "ms_per_step": round(secs / steps * 1e3, 4),
+            "steps": steps, "warmup": warmup}
 
 
 class Buffers:
@@ -941,6 +986,13 @@ def run_ours(args):
     dec.close()
     e2e_dec.close()
 
+    # --- configs[4]'s larger batches: sequences decoded together, each layer's weights read once
+    # per step for all of them (one GPU)
+    decode_batch = None
+    if world == 1 and not args.no_batch:
+        decode_batch = {str(nb): time_decode_batch(torch, m, device, dev, nb, args.steps, args.warmup)
+                        for nb in DECODE_BATCHES}
+
     cpu = None
     if rank == 0 and world == 1 and not args.no_cpu:
         use_all_host_threads()
@@ -994,6 +1046,7 @@ def run_ours(args):
         "gpu_launches": args.steps * (2 + KERNELS_PER_LAYER * N_MODEL) * world,
         "clocks": sampler.summary(),
         "cpu_baseline": cpu,
+        "decode_batch": decode_batch,
     }
     print(json.dumps(line), flush=True)
     return 0
@@ -1012,9 +1065,13 @@ def run_only(args):
     dev = torch.device("cuda", 0)
     if args.only == "decode":  # the whole decode step, replayed from the decoder's graph
         m = Model(ops, device, dev, 0, 1)
-        dec = m.decoder(device)
+        nb = args.decode_batch
+        dec = m.decoder(device) if nb == 1 else batched_decoder(m, device, nb, dev)
         stream = torch.cuda.Stream(dev)
-        dec.set_input(1234, POSITION, stream=stream)
+        if nb == 1:
+            dec.set_input(1234, POSITION, stream=stream)
+        else:
+            dec.set_input([1234 + 7 * i for i in range(nb)], [POSITION - i for i in range(nb)], stream=stream)
         dec.capture(stream=stream)
         with torch.cuda.stream(stream):
             for _ in range(args.warmup):
@@ -1022,7 +1079,8 @@ def run_only(args):
             device.check(stream)
             secs = timed(torch, lambda: [dec.step(stream=stream) for _ in range(args.steps)])
         device.check(stream)
-        print(json.dumps({"only": "decode", "steps": args.steps, "ms_per_step": round(secs / args.steps * 1e3, 4),
+        print(json.dumps({"only": "decode", "batch": nb, "steps": args.steps,
+                          "ms_per_step": round(secs / args.steps * 1e3, 4),
                           "launches_per_step": 2 + KERNELS_PER_LAYER * N_MODEL}), flush=True)
         dec.close()
         device.close()
@@ -1076,6 +1134,8 @@ def main():
     ap.add_argument("--warmup", type=int, default=10)
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--no-cpu", action="store_true", help="skip the CPU baseline sample")
+    ap.add_argument("--no-batch", action="store_true", help="skip the batched decode legs (configs[4] batch 8, 32)")
+    ap.add_argument("--decode-batch", type=int, default=1, help="--only decode: sequences per step")
     ap.add_argument("--no-parity", action="store_true", help="skip the parity gate (profiling runs)")
     ap.add_argument("--traffic", type=float, default=FFN8_TRAFFIC,
                     help="ncu dram bytes (read + write) per decoder_feedforward_fp8 call")
