@@ -64,7 +64,7 @@ def run_qkv_batch(device, d, m=None, tiled=False, keep=None):
     return host_bits(qo), host_bits(kc), host_bits(vc)
 
 
-@pytest.mark.parametrize("m", [2, 8, 33])
+@pytest.mark.parametrize("m", [2, 8, 17, 32, 33])
 def test_qkv_batch_matches_oracle_per_sequence(device, m):
     """Each sequence's q, its K / V slot, and every other slot of every ring untouched."""
     ring = 1024
@@ -128,14 +128,13 @@ def attention_batch_inputs(m, ring, seed):
     return q, k, v, mask
 
 
-@pytest.mark.parametrize("ring", [1024, 4096])
-def test_attention_batch_is_the_single_op_per_sequence(device, ring):
+@pytest.mark.parametrize("ring,m", [(1024, 3), (4096, 3), (1024, 17), (4096, 17)])
+def test_attention_batch_is_the_single_op_per_sequence(device, ring, m):
     """Bit-identical to g4_sliding_attention on each sequence, and within 0.01 of the oracle."""
     import torch
     from g4b200 import ops
 
-    m = 3
-    q, k, v, mask = attention_batch_inputs(m, ring, ring)
+    q, k, v, mask = attention_batch_inputs(m, ring, ring + m)
     out = torch.zeros((m, NS, GS, DS), dtype=torch.bfloat16, device="cuda")
     ops.sliding_attention_batch(device, dev_tensor(q), dev_tensor(k), dev_tensor(v), dev_tensor(mask), out,
                                 scale=1.0 / 16)
@@ -201,7 +200,7 @@ def run_o_batch(device, d, m=None, tiled=False):
     return host_bits(res)
 
 
-@pytest.mark.parametrize("m", [2, 16, 64])
+@pytest.mark.parametrize("m", [2, 16, 17, 32, 64])
 def test_o_batch_matches_oracle_per_sequence(device, m):
     d = o_batch_inputs(m, seed=m)
     got = run_o_batch(device, d)
