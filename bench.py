@@ -97,6 +97,14 @@ def op_bytes(world=1):
            + mb * H * 2 * 2 + H * 2 * 2 + 8 * 2 + 12 for mb in BATCH_SWEEP},
         **{f"decoder_feedforward_fp8_m{mb}": 2 * L * H + H * L + (2 * L + H) * 4 + mb * H * 2 * 2 + H * 2 * 2 + 8 * 2
            for mb in BATCH_SWEEP},
+        # the batched decoder's ops on nb sequences (one GPU): the weights once, the per-sequence rows
+        # and caches nb times
+        **{f"sliding_project_qkv_m{nb}": (QS + 2 * PS) * H + (QS + 2 * PS) * 2 + H * 2 + 2 * DS * 2
+           + nb * (H * 2 + 2 * DS * 2 * 2 + 2 * PS * 2 + QS * 2 + 8) for nb in DECODE_BATCHES},
+        **{f"sliding_attention_m{nb}": nb * attention(RING_LOCAL) for nb in DECODE_BATCHES},
+        **{f"sliding_attention_4096_m{nb}": nb * attention(RING_GLOBAL) for nb in DECODE_BATCHES},
+        **{f"sliding_attention_output_m{nb}": H * QS + H * 2 * 2 + nb * (QS * 2 + H * 2 * 2) for nb in DECODE_BATCHES},
+        **{f"final_norm_and_logits_m{nb}": W * H * 2 + H * 2 + nb * (H * 2 + W * 2) for nb in DECODE_BATCHES},
     }
 
 
@@ -868,6 +876,52 @@ def run_reference(args):
 
 # ------------------------------------------------------------------------------ GPU leg
 
+def batched_op_cases(torch, ops, device, dev, m: Model):
+    """The batched decoder's ops alone on nb sequences (configs[4]'s batches), rotating over the
+    model's layers and over enough copies of nb rings that the caches of one call are not in L2."""
+    gen = torch.Generator(device=dev)
+    gen.manual_seed(4)
+    cases = {}
+    for nb in DECODE_BATCHES:
+        x = torch.randn((nb, H), generator=gen, device=dev).to(torch.bfloat16)
+        q = torch.randn((nb, NS, GS, DS), generator=gen, device=dev).to(torch.bfloat16)
+        attn = torch.zeros_like(q)
+        pos = [POSITION - i for i in range(nb)]
+        rope = torch.tensor([p * DS * 2 for p in pos], dtype=torch.int32, device=dev)
+        kv = {r: torch.tensor([(p % r) * NS * DS * 2 for p in pos], dtype=torch.int32, device=dev)
+              for r in (RING_LOCAL, RING_GLOBAL)}
+        mask = {r: torch.stack([(torch.arange(r, device=dev) <= min(p, r - 1)).to(torch.float32) for p in pos])
+                for r in (RING_LOCAL, RING_GLOBAL)}
+        copies = 4 if nb < 16 else 2
+        rings = {r: [tuple(torch.randn((nb, r, NS, DS), generator=gen, device=dev).to(torch.bfloat16)
+                           for _ in range(2)) for _ in range(copies)] for r in (RING_LOCAL, RING_GLOBAL)}
+        logits = torch.zeros((nb, W), dtype=torch.bfloat16, device=dev)
+
+        def qkv(i, nb=nb, x=x, q=q, rope=rope, kv=kv, rings=rings, copies=copies):
+            lay = m.layers[i % N_MODEL]
+            cos, sin = m.tables_of(lay)
+            k, v = rings[lay.ring][i % copies]
+            ops.sliding_project_qkv_batch(device, x, lay.q_w, lay.k_w, lay.v_w, lay.q_s, lay.k_s, lay.v_s,
+                                          lay.input_rms, lay.q_rms, lay.k_rms, kv[lay.ring], rope, cos, sin, k, v, q,
+                                          tiled=True)
+
+        def att(i, ring, q=q, attn=attn, kv=kv, mask=mask, rings=rings, copies=copies):
+            k, v = rings[ring][i % copies]
+            ops.sliding_attention_batch(device, q, k, v, mask[ring], attn, scale=ATTN_SCALE, kv_offset=kv[ring])
+
+        def o(i, x=x, attn=attn):
+            lay = m.layers[i % N_MODEL]
+            ops.sliding_attention_output_batch(device, attn, lay.post_attn_rms, lay.o_w, lay.o_s, x, tiled=True)
+
+        cases[f"sliding_project_qkv_m{nb}"] = qkv
+        cases[f"sliding_attention_m{nb}"] = lambda i, att=att: att(i, RING_LOCAL)
+        cases[f"sliding_attention_4096_m{nb}"] = lambda i, att=att: att(i, RING_GLOBAL)
+        cases[f"sliding_attention_output_m{nb}"] = o
+        cases[f"final_norm_and_logits_m{nb}"] = (
+            lambda i, x=x, logits=logits: ops.final_norm_and_logits_batch(device, x, m.final_norm, m.lm_head, logits))
+    return cases
+
+
 def op_timings(torch, ops, device, dev, m: Model, dist, reps=64):
     """Device microseconds per call of each op alone: a graph of `reps` calls rotating over the
     layers the op runs on, replayed 5 times (max over ranks)."""
@@ -894,9 +948,10 @@ def op_timings(torch, ops, device, dev, m: Model, dist, reps=64):
         for mb in BATCH_SWEEP:  # the decoder's FP8 FFN layers on a batch of tokens
             cases[f"decoder_feedforward_fp8_m{mb}"] = (
                 lambda i, mb=mb: ffn_batch(ops, device, m.layers[i % N_MODEL], rows[:mb]))
+        cases.update(batched_op_cases(torch, ops, device, dev, m))
     us = {}
     for name, fn in cases.items():
-        n = reps if name != "final_norm_and_logits" else 8  # 2 GB / 8 per call: the logits stream from HBM
+        n = 8 if name.startswith("final_norm_and_logits") else reps  # 2 GB per call: the logits stream from HBM
         if dist:
             dist.barrier()
         g = capture(torch, fn, n)

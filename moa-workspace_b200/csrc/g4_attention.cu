@@ -30,19 +30,29 @@ namespace {
 constexpr int kThreads = 256;
 constexpr int kWarps = kThreads / 32;
 constexpr int kRowBytes = kDs * 2;         // one head's row in one slot
-constexpr int kSubMax = 128;               // slots resident in shared memory per pass (C = 8)
 constexpr int kBox = 32;                   // slots per TMA box, each with its own barrier
-constexpr int kBoxes = kSubMax / kBox;
 constexpr int kMaxRing = 8192;
 constexpr int kMinChunks = 8;              // the portable cluster size; 16 where it can be scheduled
 
-template <int C>  // CTAs per KV head = the cluster size
+// Batches of sequences: the cluster size and the slots per pass (several CTAs per SM, so one CTA's
+// loads overlap another's scoring; a whole batch fills the GPU without long single-head rings).
+#ifndef G4_ATTN_BATCH_C
+#define G4_ATTN_BATCH_C 4
+#endif
+#ifndef G4_ATTN_BATCH_SUB
+#define G4_ATTN_BATCH_SUB 64
+#endif
+
+// C CTAs per KV head (the cluster size); SUB slots resident in shared memory per pass. One
+// sequence: C = 8 with passes of 128, or C = 16 with passes of 64 for rings of 2048 to 4096 slots
+// (small enough that several CTAs share an SM, so eight 16-CTA clusters fit the GPU together).
+template <int C, int SUB>
 struct AttnSmem {
   static constexpr int kMaxPer = kMaxRing / C;
   static constexpr int kDimsPerCta = kDs / C;  // head dimensions each CTA combines
-  // slots per pass: C = 16 serves rings of up to 4096 slots in passes of 64, small enough that
-  // several CTAs share an SM (so eight 16-CTA clusters fit the GPU together)
-  static constexpr int kSub = C == 16 ? 64 : kSubMax;
+  static constexpr int kSub = SUB;
+  static constexpr int kBoxes = SUB / kBox;
+  static_assert(SUB % kBox == 0 && kBoxes <= kThreads, "boxes per pass");
   uint8_t k[kSub * kRowBytes];
   uint8_t v[kSub * kRowBytes];
   float score[kMaxPer][kGs];  // scores, then bf16-rounded probabilities
@@ -53,6 +63,9 @@ struct AttnSmem {
   __align__(16) uint16_t out[kGs * kDimsPerCta];
   uint64_t kbar[kBoxes], vbar[kBoxes];
 };
+using Attn8 = AttnSmem<8, 128>;
+using Attn16 = AttnSmem<16, 64>;
+using AttnBatch = AttnSmem<G4_ATTN_BATCH_C, G4_ATTN_BATCH_SUB>;
 
 struct KvMaps {
   CUtensorMap k, v;  // [ring][heads][dim] as (dim, head, slot), box {dim, 1, kBox}
@@ -75,20 +88,22 @@ __device__ __forceinline__ float ld_cluster_f32(const void* own, uint32_t rank) 
   return v;
 }
 
-template <int C>
+template <int C, int SUB>
 __global__ void __launch_bounds__(kThreads, 2) attention_kernel(const __grid_constant__ KvMaps maps, AttnArgs a,
                                                                 Scratch sc) {
+  using Sm = AttnSmem<C, SUB>;
   constexpr int kChunks = C;
-  constexpr int kDimsPerCta = AttnSmem<C>::kDimsPerCta;
+  constexpr int kDimsPerCta = Sm::kDimsPerCta;
+  constexpr int kBoxes = Sm::kBoxes;
   extern __shared__ __align__(1024) uint8_t smem_raw[];
-  AttnSmem<C>& sm = *reinterpret_cast<AttnSmem<C>*>(smem_raw);
+  Sm& sm = *reinterpret_cast<Sm*>(smem_raw);
   const int head = blockIdx.x / kChunks;
   const int chunk = int(cluster_ctarank());  // == blockIdx.x % kChunks
   const int seq = blockIdx.y;                // the sequence of a batch (its own ring)
   const size_t qrow0 = size_t(seq) * a.heads * kGs * kDs;
   const float* mask = a.mask + size_t(seq) * a.mask_stride;
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
-  constexpr int kSub = AttnSmem<C>::kSub;
+  constexpr int kSub = Sm::kSub;
   const int per = a.ring_len / kChunks;  // a multiple of 32, at most kMaxPer
   const int slot0 = chunk * per;                  // in this sequence's ring
   const int gslot0 = seq * a.ring_len + slot0;  // in the batched caches
@@ -561,13 +576,13 @@ cudaLaunchConfig_t full_attention_config(cudaStream_t stream, bool pdl, cudaLaun
   return cfg;
 }
 
-template <int C>
+template <class Sm, int C>
 cudaLaunchConfig_t attention_config(int heads, cudaStream_t stream, bool pdl, cudaLaunchAttribute (&attr)[2],
                                     int batch = 1) {
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = dim3(heads * C, batch);
   cfg.blockDim = dim3(kThreads);
-  cfg.dynamicSmemBytes = sizeof(AttnSmem<C>);
+  cfg.dynamicSmemBytes = sizeof(Sm);
   cfg.stream = stream;
   attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
   attr[0].val.programmaticStreamSerializationAllowed = pdl ? 1 : 0;
@@ -589,20 +604,28 @@ int g_clusters16[kMaxDevices];  // 0 unknown, 1 yes, -1 no
 
 cudaError_t prepare_attention_kernels() {
   cudaError_t e;
-  if ((e = cudaFuncSetAttribute(attention_kernel<8>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                int(sizeof(AttnSmem<8>)))))
+  if ((e = cudaFuncSetAttribute(attention_kernel<8, 128>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                int(sizeof(Attn8)))))
     return e;
-  if ((e = cudaFuncSetAttribute(attention_kernel<16>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                int(sizeof(AttnSmem<16>)))))
+  if ((e = cudaFuncSetAttribute(attention_kernel<16, 64>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                int(sizeof(Attn16)))))
+    return e;
+  if ((e = cudaFuncSetAttribute(attention_kernel<G4_ATTN_BATCH_C, G4_ATTN_BATCH_SUB>,
+                                cudaFuncAttributeMaxDynamicSharedMemorySize, int(sizeof(AttnBatch)))))
+    return e;
+  if (G4_ATTN_BATCH_C > 8 &&
+      (e = cudaFuncSetAttribute(attention_kernel<G4_ATTN_BATCH_C, G4_ATTN_BATCH_SUB>,
+                                cudaFuncAttributeNonPortableClusterSizeAllowed, 1)))
     return e;
   int dev = 0;
   if ((e = cudaGetDevice(&dev))) return e;
   if (dev < 0 || dev >= kMaxDevices) return cudaSuccess;  // such a device keeps the portable size
   int fits = 0;
-  if (cudaFuncSetAttribute(attention_kernel<16>, cudaFuncAttributeNonPortableClusterSizeAllowed, 1) == cudaSuccess) {
+  if (cudaFuncSetAttribute(attention_kernel<16, 64>, cudaFuncAttributeNonPortableClusterSizeAllowed, 1) ==
+      cudaSuccess) {
     cudaLaunchAttribute attr[2];
-    cudaLaunchConfig_t cfg = attention_config<16>(kNs, nullptr, false, attr);
-    if (cudaOccupancyMaxActiveClusters(&fits, attention_kernel<16>, &cfg) != cudaSuccess) fits = 0;
+    cudaLaunchConfig_t cfg = attention_config<Attn16, 16>(kNs, nullptr, false, attr);
+    if (cudaOccupancyMaxActiveClusters(&fits, attention_kernel<16, 64>, &cfg) != cudaSuccess) fits = 0;
   }
   cudaGetLastError();  // a refused query is not an error of this call
   g_clusters16[dev] = fits >= kNs ? 1 : -1;
@@ -647,15 +670,20 @@ cudaError_t launch_attention(const AttnArgs& a, const LaunchEnv& env) {
   if (sc.trace) sc.trace += 4096;  // profiling builds: separate stamp rows per kernel
 #endif
   cudaLaunchAttribute attr[2];
+  if (a.batch > 1 && a.ring_len % (G4_ATTN_BATCH_C * kBox) == 0) {
+    const cudaLaunchConfig_t cfg =
+        attention_config<AttnBatch, G4_ATTN_BATCH_C>(a.heads, env.stream, env.pdl, attr, a.batch);
+    return cudaLaunchKernelEx(&cfg, attention_kernel<G4_ATTN_BATCH_C, G4_ATTN_BATCH_SUB>, maps, a, sc);
+  }
   const bool c16 = env.device >= 0 && env.device < kMaxDevices && g_clusters16[env.device] == 1 &&
                    a.ring_len % (16 * kBox) == 0 && a.ring_len >= 2048 &&
-                   a.ring_len <= 4 * 16 * AttnSmem<16>::kSub;  // 2 to 4 passes (shorter rings: measured faster at 8)
+                   a.ring_len <= 4 * 16 * Attn16::kSub;  // 2 to 4 passes (shorter rings: measured faster at 8)
   if (c16) {
-    const cudaLaunchConfig_t cfg = attention_config<16>(a.heads, env.stream, env.pdl, attr, a.batch);
-    return cudaLaunchKernelEx(&cfg, attention_kernel<16>, maps, a, sc);
+    const cudaLaunchConfig_t cfg = attention_config<Attn16, 16>(a.heads, env.stream, env.pdl, attr, a.batch);
+    return cudaLaunchKernelEx(&cfg, attention_kernel<16, 64>, maps, a, sc);
   }
-  const cudaLaunchConfig_t cfg = attention_config<8>(a.heads, env.stream, env.pdl, attr, a.batch);
-  return cudaLaunchKernelEx(&cfg, attention_kernel<8>, maps, a, sc);
+  const cudaLaunchConfig_t cfg = attention_config<Attn8, 8>(a.heads, env.stream, env.pdl, attr, a.batch);
+  return cudaLaunchKernelEx(&cfg, attention_kernel<8, 128>, maps, a, sc);
 }
 
 }  // namespace g4

@@ -130,7 +130,8 @@ def attention_batch_inputs(m, ring, seed):
 
 @pytest.mark.parametrize("ring,m", [(1024, 3), (4096, 3), (1024, 17), (4096, 17)])
 def test_attention_batch_is_the_single_op_per_sequence(device, ring, m):
-    """Bit-identical to g4_sliding_attention on each sequence, and within 0.01 of the oracle."""
+    """Each sequence within 0.01 of the oracle and of g4_sliding_attention on it alone (a batch splits
+    each head's ring over 4 CTAs instead of 8: the partial sums are added in another order)."""
     import torch
     from g4b200 import ops
 
@@ -145,7 +146,8 @@ def test_attention_batch_is_the_single_op_per_sequence(device, ring, m):
         ops.sliding_attention(device, dev_tensor(q[i]), dev_tensor(k[i]), dev_tensor(v[i]), dev_tensor(mask[i]), one,
                               scale=1.0 / 16)
         device.check()
-        assert np.array_equal(got[i], host_bits(one)), i
+        ok, maxd, exact = within(host_bits(one), got[i], 0.01)
+        assert ok and exact > 0.95, (i, maxd, exact)
         ok, maxd, exact = within(oracle.sliding_attention(q[i], k[i], v[i], mask[i], 1.0 / 16), got[i], 0.01)
         assert ok and exact > 0.9, (i, maxd, exact)
 
