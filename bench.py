@@ -1153,7 +1153,20 @@ def run_only(args):
             return Mini.cos_l, Mini.sin_l
 
     b = Buffers(dev, 1)
-    if args.only == "ffn4b":  # the NVFP4 feed-forward on a batch of --batch tokens
+    if args.only == "attnb":  # the batched attention over --batch sequences' rings of --ring slots
+        nb, ring = args.batch, args.ring
+        q = torch.randn((nb, NS, GS, DS), device=dev, generator=gen).to(torch.bfloat16)
+        out = torch.zeros_like(q)
+        caches = [tuple(torch.randn((nb, ring, NS, DS), device=dev, generator=gen).to(torch.bfloat16)
+                        for _ in range(2)) for _ in range(args.layers)]
+        pos = [POSITION - i for i in range(nb)]
+        kv = torch.tensor([(p % ring) * NS * DS * 2 for p in pos], dtype=torch.int32, device=dev)
+        mask = torch.stack([(torch.arange(ring, device=dev) <= min(p, ring - 1)).to(torch.float32) for p in pos])
+
+        def call(i):
+            k, v = caches[i % len(caches)]
+            ops.sliding_attention_batch(device, q, k, v, mask, out, scale=ATTN_SCALE, kv_offset=kv)
+    elif args.only == "ffn4b":  # the NVFP4 feed-forward on a batch of --batch tokens
         rows = torch.randn(args.batch, H, device=dev, generator=gen).to(torch.bfloat16)
 
         def call(i):
@@ -1180,8 +1193,9 @@ def run_only(args):
 
 def main():
     ap = argparse.ArgumentParser()
-    ap.add_argument("--batch", type=int, default=16, help="--only ffn4b: tokens per call")
-    ap.add_argument("--only", choices=["qkv", "attn", "o", "ffn8", "ffn4", "ffn4b", "decode"], default=None,
+    ap.add_argument("--batch", type=int, default=16, help="--only ffn4b / attnb: tokens (sequences) per call")
+    ap.add_argument("--ring", type=int, default=RING_LOCAL, help="--only attnb: slots per sequence's ring")
+    ap.add_argument("--only", choices=["qkv", "attn", "o", "ffn8", "ffn4", "ffn4b", "attnb", "decode"], default=None,
                     help="profiling aid: eager calls of one op only (prints us/call, not the bench line)")
     ap.add_argument("--layers", type=int, default=4, help="--only: layer copies to rotate over")
     ap.add_argument("--gpus", type=int, default=1)
