@@ -46,16 +46,18 @@ constexpr int kMinChunks = 8;              // the portable cluster size; 16 wher
 // C CTAs per KV head (the cluster size); SUB slots resident in shared memory per pass. One
 // sequence: C = 8 with passes of 128, or C = 16 with passes of 64 for rings of 2048 to 4096 slots
 // (small enough that several CTAs share an SM, so eight 16-CTA clusters fit the GPU together).
-template <int C, int SUB>
+template <int C, int SUB, int MAXRING = kMaxRing>
 struct AttnSmem {
-  static constexpr int kMaxPer = kMaxRing / C;
+  static constexpr int kMaxPer = MAXRING / C;
   static constexpr int kDimsPerCta = kDs / C;  // head dimensions each CTA combines
   static constexpr int kSub = SUB;
   static constexpr int kBoxes = SUB / kBox;
   static_assert(SUB % kBox == 0 && kBoxes <= kThreads, "boxes per pass");
   uint8_t k[kSub * kRowBytes];
   uint8_t v[kSub * kRowBytes];
-  float score[kMaxPer][kGs];  // scores, then bf16-rounded probabilities
+  // per slot, the two query heads' bf16 scores, then their bf16-rounded probabilities (head 1 in
+  // the high half): the values the reference rounds to bf16 anyway
+  uint32_t score[kMaxPer];
   float red[kWarps][kGs];
   float cmax[kGs];            // this CTA's score maxima (read by the cluster)
   float po[kGs][kDs];         // this CTA's partial sum_t bf16(p) v (read by the cluster)
@@ -65,7 +67,19 @@ struct AttnSmem {
 };
 using Attn8 = AttnSmem<8, 128>;
 using Attn16 = AttnSmem<16, 64>;
-using AttnBatch = AttnSmem<G4_ATTN_BATCH_C, G4_ATTN_BATCH_SUB>;
+constexpr int kBatchMaxRing = 4096;  // a batch's rings (longer ones take the single-sequence shape)
+// Below kBatchWide sequences a batch's grid is too small to fill the GPU three CTAs per SM (the
+// clusters pack onto fewer SMs): those launches ask for kBatchNarrowSmem of shared memory, so two
+// CTAs share an SM (measured: batch 8 on 1024-slot rings 22.6 us three per SM, 19.9 two per SM).
+constexpr int kBatchWide = 16;
+constexpr size_t kBatchNarrowSmem = 100 * 1024;
+using AttnBatch = AttnSmem<G4_ATTN_BATCH_C, G4_ATTN_BATCH_SUB, kBatchMaxRing>;
+
+__device__ __forceinline__ float lo_bf16(uint32_t w) { return __uint_as_float(w << 16); }
+__device__ __forceinline__ float hi_bf16(uint32_t w) { return __uint_as_float(w & 0xffff0000u); }
+__device__ __forceinline__ uint32_t pack_bf16(float lo, float hi) {
+  return uint32_t(f32_to_bf16(lo)) | (uint32_t(f32_to_bf16(hi)) << 16);
+}
 
 struct KvMaps {
   CUtensorMap k, v;  // [ring][heads][dim] as (dim, head, slot), box {dim, 1, kBox}
@@ -88,10 +102,11 @@ __device__ __forceinline__ float ld_cluster_f32(const void* own, uint32_t rank) 
   return v;
 }
 
-template <int C, int SUB>
-__global__ void __launch_bounds__(kThreads, 2) attention_kernel(const __grid_constant__ KvMaps maps, AttnArgs a,
-                                                                Scratch sc) {
-  using Sm = AttnSmem<C, SUB>;
+// MINB: CTAs per SM the registers must allow (a batch runs three per SM).
+template <int C, int SUB, int MINB = 2, int MAXRING = kMaxRing>
+__global__ void __launch_bounds__(kThreads, MINB) attention_kernel(const __grid_constant__ KvMaps maps, AttnArgs a,
+                                                                   Scratch sc) {
+  using Sm = AttnSmem<C, SUB, MAXRING>;
   constexpr int kChunks = C;
   constexpr int kDimsPerCta = Sm::kDimsPerCta;
   constexpr int kBoxes = Sm::kBoxes;
@@ -180,16 +195,14 @@ __global__ void __launch_bounds__(kThreads, 2) attention_kernel(const __grid_con
   constexpr int kLanesPerSlot = 8, kSlotsPerStep = 32 / kLanesPerSlot;
   static_assert(kWarps * kSlotsPerStep == kBox, "one box per step of the CTA");
   const int sub = lane / kLanesPerSlot, part = lane % kLanesPerSlot;
-  float qv[kGs][32];
+  uint32_t qv[kGs][16];  // this lane's 32 q elements of each head as bf16 pairs (element 2i low)
 #pragma unroll
   for (int g = 0; g < kGs; ++g) {
 #pragma unroll
     for (int c = 0; c < 4; ++c) {
       const uint4 raw =
           __ldcg(reinterpret_cast<const uint4*>(a.q + qrow0 + (head * kGs + g) * kDs + c * 64 + part * 8));
-      const uint16_t* b = reinterpret_cast<const uint16_t*>(&raw);
-#pragma unroll
-      for (int j = 0; j < 8; ++j) qv[g][c * 8 + j] = bf16_to_f32(b[j]);
+      qv[g][4 * c] = raw.x, qv[g][4 * c + 1] = raw.y, qv[g][4 * c + 2] = raw.z, qv[g][4 * c + 3] = raw.w;
     }
   }
   bool ok = true;
@@ -207,12 +220,13 @@ __global__ void __launch_bounds__(kThreads, 2) attention_kernel(const __grid_con
 #pragma unroll
       for (int c = 0; c < 4; ++c) {
         const uint4 kr = *reinterpret_cast<const uint4*>(row + c * 128);
-        const uint16_t* kb = reinterpret_cast<const uint16_t*>(&kr);
+        const uint32_t kw[4] = {kr.x, kr.y, kr.z, kr.w};
 #pragma unroll
-        for (int j = 0; j < 8; ++j) {
-          const float kf = bf16_to_f32(kb[j]);
-          d0 = fmaf(qv[0][c * 8 + j], kf, d0);
-          d1 = fmaf(qv[1][c * 8 + j], kf, d1);
+        for (int i = 0; i < 4; ++i) {  // elements 2i and 2i + 1 of the chunk, in element order
+          d0 = fmaf(lo_bf16(qv[0][4 * c + i]), lo_bf16(kw[i]), d0);
+          d1 = fmaf(lo_bf16(qv[1][4 * c + i]), lo_bf16(kw[i]), d1);
+          d0 = fmaf(hi_bf16(qv[0][4 * c + i]), hi_bf16(kw[i]), d0);
+          d1 = fmaf(hi_bf16(qv[1][4 * c + i]), hi_bf16(kw[i]), d1);
         }
       }
 #pragma unroll
@@ -220,10 +234,7 @@ __global__ void __launch_bounds__(kThreads, 2) attention_kernel(const __grid_con
         d0 += __shfl_xor_sync(0xffffffffu, d0, o);
         d1 += __shfl_xor_sync(0xffffffffu, d1, o);
       }
-      if (part == 0) {
-        sm.score[first + t][0] = bf16_round(a.scale * d0);
-        sm.score[first + t][1] = bf16_round(a.scale * d1);
-      }
+      if (part == 0) sm.score[first + t] = pack_bf16(a.scale * d0, a.scale * d1);
     }
   }
   __syncthreads();
@@ -232,8 +243,9 @@ __global__ void __launch_bounds__(kThreads, 2) attention_kernel(const __grid_con
   // this CTA's maximum; then the head's maximum over the cluster (distributed shared memory)
   float m0 = -INFINITY, m1 = -INFINITY;
   for (int t = tid; t < per; t += kThreads) {
-    m0 = fmaxf(m0, sm.score[t][0]);
-    m1 = fmaxf(m1, sm.score[t][1]);
+    const uint32_t w = sm.score[t];
+    m0 = fmaxf(m0, lo_bf16(w));
+    m1 = fmaxf(m1, hi_bf16(w));
   }
   m0 = warp_max(m0);
   m1 = warp_max(m1);
@@ -264,12 +276,12 @@ __global__ void __launch_bounds__(kThreads, 2) attention_kernel(const __grid_con
   float s0 = 0.f, s1 = 0.f;
   for (int t = tid; t < per; t += kThreads) {
     const float mk = mask[slot0 + t];
-    const float p0 = fminf(expf(sm.score[t][0] - gm[0]), mk);
-    const float p1 = fminf(expf(sm.score[t][1] - gm[1]), mk);
+    const uint32_t w = sm.score[t];
+    const float p0 = fminf(expf(lo_bf16(w) - gm[0]), mk);
+    const float p1 = fminf(expf(hi_bf16(w) - gm[1]), mk);
     s0 += p0;
     s1 += p1;
-    sm.score[t][0] = bf16_round(p0);
-    sm.score[t][1] = bf16_round(p1);
+    sm.score[t] = pack_bf16(p0, p1);
   }
   s0 = warp_sum(s0);
   s1 = warp_sum(s1);
@@ -294,8 +306,9 @@ __global__ void __launch_bounds__(kThreads, 2) attention_kernel(const __grid_con
 #pragma unroll 8
       for (int t = b * kBox; t < (b + 1) * kBox; ++t) {
         const float vf = bf16_to_f32(reinterpret_cast<const uint16_t*>(sm.v + t * kRowBytes)[tid]);
-        o0 = fmaf(sm.score[first + t][0], vf, o0);
-        o1 = fmaf(sm.score[first + t][1], vf, o1);
+        const uint32_t w = sm.score[first + t];
+        o0 = fmaf(lo_bf16(w), vf, o0);
+        o1 = fmaf(hi_bf16(w), vf, o1);
       }
     }
   }
@@ -578,11 +591,11 @@ cudaLaunchConfig_t full_attention_config(cudaStream_t stream, bool pdl, cudaLaun
 
 template <class Sm, int C>
 cudaLaunchConfig_t attention_config(int heads, cudaStream_t stream, bool pdl, cudaLaunchAttribute (&attr)[2],
-                                    int batch = 1) {
+                                    int batch = 1, size_t smem = sizeof(Sm)) {
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = dim3(heads * C, batch);
   cfg.blockDim = dim3(kThreads);
-  cfg.dynamicSmemBytes = sizeof(Sm);
+  cfg.dynamicSmemBytes = smem;
   cfg.stream = stream;
   attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
   attr[0].val.programmaticStreamSerializationAllowed = pdl ? 1 : 0;
@@ -610,11 +623,12 @@ cudaError_t prepare_attention_kernels() {
   if ((e = cudaFuncSetAttribute(attention_kernel<16, 64>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                 int(sizeof(Attn16)))))
     return e;
-  if ((e = cudaFuncSetAttribute(attention_kernel<G4_ATTN_BATCH_C, G4_ATTN_BATCH_SUB>,
-                                cudaFuncAttributeMaxDynamicSharedMemorySize, int(sizeof(AttnBatch)))))
+  if ((e = cudaFuncSetAttribute(attention_kernel<G4_ATTN_BATCH_C, G4_ATTN_BATCH_SUB, 3, kBatchMaxRing>,
+                                cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                int(sizeof(AttnBatch) > kBatchNarrowSmem ? sizeof(AttnBatch) : kBatchNarrowSmem))))
     return e;
   if (G4_ATTN_BATCH_C > 8 &&
-      (e = cudaFuncSetAttribute(attention_kernel<G4_ATTN_BATCH_C, G4_ATTN_BATCH_SUB>,
+      (e = cudaFuncSetAttribute(attention_kernel<G4_ATTN_BATCH_C, G4_ATTN_BATCH_SUB, 3, kBatchMaxRing>,
                                 cudaFuncAttributeNonPortableClusterSizeAllowed, 1)))
     return e;
   int dev = 0;
@@ -670,10 +684,13 @@ cudaError_t launch_attention(const AttnArgs& a, const LaunchEnv& env) {
   if (sc.trace) sc.trace += 4096;  // profiling builds: separate stamp rows per kernel
 #endif
   cudaLaunchAttribute attr[2];
-  if (a.batch > 1 && a.ring_len % (G4_ATTN_BATCH_C * kBox) == 0) {
+  if (a.batch > 1 && a.ring_len % (G4_ATTN_BATCH_C * kBox) == 0 && a.ring_len <= kBatchMaxRing) {
+    const size_t smem = a.batch >= kBatchWide || sizeof(AttnBatch) > kBatchNarrowSmem ? sizeof(AttnBatch)
+                                                                                       : kBatchNarrowSmem;
     const cudaLaunchConfig_t cfg =
-        attention_config<AttnBatch, G4_ATTN_BATCH_C>(a.heads, env.stream, env.pdl, attr, a.batch);
-    return cudaLaunchKernelEx(&cfg, attention_kernel<G4_ATTN_BATCH_C, G4_ATTN_BATCH_SUB>, maps, a, sc);
+        attention_config<AttnBatch, G4_ATTN_BATCH_C>(a.heads, env.stream, env.pdl, attr, a.batch, smem);
+    return cudaLaunchKernelEx(&cfg, attention_kernel<G4_ATTN_BATCH_C, G4_ATTN_BATCH_SUB, 3, kBatchMaxRing>, maps, a,
+                              sc);
   }
   const bool c16 = env.device >= 0 && env.device < kMaxDevices && g_clusters16[env.device] == 1 &&
                    a.ring_len % (16 * kBox) == 0 && a.ring_len >= 2048 &&
