@@ -93,7 +93,10 @@ g4_status g4_ctx_create(int device, g4_ctx** out) {
   const size_t off_bh = off_ss + g4::kTileSsBytes;  // batched feed-forward: h | split-K words | unscale
   const size_t off_bw = off_bh + size_t(g4::kBatchMax) * g4::kH * sizeof(uint16_t);
   const size_t off_bu = off_bw + g4::batch_words_count(ctx->sm_count) * sizeof(unsigned long long);
-  const size_t off_trace = off_bu + size_t(g4::kBatchMax) * sizeof(float);
+  // term operands (1024-byte aligned: a TMA source) | their 2^-E
+  const size_t off_bt = (off_bu + size_t(g4::kBatchMax) * sizeof(float) + 1023) / 1024 * 1024;
+  const size_t off_be = off_bt + size_t(g4::kTermUnitsMax) * g4::kTermTokens * g4::kTerms * 256;
+  const size_t off_trace = off_be + size_t(g4::kTermUnitsMax) * g4::kTermTokens * sizeof(float);
 #ifdef G4_TRACE
   const size_t total = off_trace + size_t(65536 + 4096 * 32 * 8) * sizeof(uint64_t);
 #else
@@ -123,6 +126,8 @@ g4_status g4_ctx_create(int device, g4_ctx** out) {
   ctx->sc.batch_h = reinterpret_cast<uint16_t*>(base + off_bh);
   ctx->sc.batch_words = reinterpret_cast<unsigned long long*>(base + off_bw);
   ctx->sc.batch_unscale = reinterpret_cast<float*>(base + off_bu);
+  ctx->sc.batch_terms = base + off_bt;
+  ctx->sc.batch_texp = reinterpret_cast<float*>(base + off_be);
   ctx->batch_ok = g4::batch_geometry_fits(ctx->sm_count) && g4::batch_attn_geometry_fits(ctx->sm_count);
 #ifdef G4_TRACE
   ctx->sc.trace = reinterpret_cast<uint64_t*>(base + off_trace);

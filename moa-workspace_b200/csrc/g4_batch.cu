@@ -198,6 +198,24 @@ __global__ void __launch_bounds__(kBThreads, 1) ffn_batch_down_kernel(const __gr
   batch_run<BatchShape<MPAD, FP8>>(op, smem, sc);
 }
 
+// The same ops on the term-operand engine (FP8 weights, up to kTermTokens tokens): `maps.b` maps
+// the call's term rows instead of the activation rows.
+template <int MT>
+__global__ void __launch_bounds__(kTThreads, 1) ffn_term_upgate_kernel(const __grid_constant__ BatchMaps maps,
+                                                                       Ffn8Args a, Scratch sc, int M) {
+  extern __shared__ __align__(1024) uint8_t smem[];
+  BatchUpGateOp<kTermTokens, true> op{&maps, a, sc, M};
+  batch_term_run<TermShape<MT>>(op, &maps.b, smem, sc);
+}
+
+template <int MT>
+__global__ void __launch_bounds__(kTThreads, 1) ffn_term_down_kernel(const __grid_constant__ BatchMaps maps,
+                                                                     Ffn8Args a, Scratch sc, int M) {
+  extern __shared__ __align__(1024) uint8_t smem[];
+  BatchDownOp<kTermTokens, true> op{&maps, a, sc, M};
+  batch_term_run<TermShape<MT>>(op, &maps.b, smem, sc);
+}
+
 // The weight maps of each format (row-major: the reference layout; tiled: g4_pack_tiles).
 cudaError_t batch_maps(const FfnArgs& a, const LaunchEnv& env, BatchMaps& ug, BatchMaps& dn) {
   cudaError_t e;
@@ -260,6 +278,50 @@ cudaError_t launch_batch_t(const BatchArgs<FP8>& a, int M, const LaunchEnv& env)
   return launch_batch(batch_finalize_kernel<kL / kUnitK, kTagDown>, M, kFinThreads, 0, true, env.stream, fa, env.sc, gd);
 }
 
+// The FP8 feed-forward on the term-operand engine: the input's term rows (RMSNorm, counting the
+// call), up/gate, the GeGLU activation's term rows, down, the per-token finalize.
+template <int MT>
+cudaError_t launch_term_t(const Ffn8Args& a, int M, const LaunchEnv& env) {
+  using Shape = TermShape<MT>;
+  BatchMaps ug{}, dn{};
+  cudaError_t e;
+  if ((e = batch_maps(a, env, ug, dn))) return e;
+  constexpr int kUgUnits = kH / kUnitK, kDnUnits = kL / kUnitK;
+  if ((e = env.maps->u8(env.sc.batch_terms, 256, uint64_t(kUgUnits) * MT * kTerms, 128, MT * kTerms, true, &ug.b)))
+    return e;
+  if ((e = env.maps->u8(env.sc.batch_terms, 256, uint64_t(kDnUnits) * MT * kTerms, 128, MT * kTerms, true, &dn.b)))
+    return e;
+  using UG = BatchUpGateOp<kTermTokens, true>;
+  const int gu = env.sm_count < UG::kUnitsPerTile * UG::kTiles ? env.sm_count : UG::kUnitsPerTile * UG::kTiles;
+  const int gd = env.sm_count;
+  if ((e = launch_batch(batch_terms_kernel<true>, MT, 256, 0, env.pdl, env.stream,
+                        static_cast<const uint16_t*>(a.residual), kH, a.pre_rms, env.sc, M, true)))
+    return e;
+  if ((e = launch_batch(ffn_term_upgate_kernel<MT>, gu, kTThreads, Shape::kSmemBytes, true, env.stream, ug, a,
+                        env.sc, M)))
+    return e;
+  if ((e = launch_batch(batch_terms_kernel<false>, MT, 256, 0, true, env.stream,
+                        static_cast<const uint16_t*>(env.sc.act), kL, static_cast<const uint16_t*>(nullptr), env.sc,
+                        M, false)))
+    return e;
+  if ((e = launch_batch(ffn_term_down_kernel<MT>, gd, kTThreads, Shape::kSmemBytes, true, env.stream, dn, a, env.sc,
+                        M)))
+    return e;
+  const FinalizeArgs fa{a.residual, a.post_rms, a.layer_scalar, nullptr, a.down_s, nullptr};
+  return launch_batch(batch_finalize_kernel<kL / kUnitK, kTagDown>, M, kFinThreads, 0, true, env.stream, fa, env.sc,
+                      gd);
+}
+
+template <int MT>
+cudaError_t prepare_term_t() {
+  cudaError_t e;
+  if ((e = cudaFuncSetAttribute(ffn_term_upgate_kernel<MT>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                int(TermShape<MT>::kSmemBytes))))
+    return e;
+  return cudaFuncSetAttribute(ffn_term_down_kernel<MT>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                              int(TermShape<MT>::kSmemBytes));
+}
+
 template <int MPAD, bool FP8>
 cudaError_t prepare_batch_t() {
   cudaError_t e;
@@ -274,6 +336,11 @@ template <bool FP8>
 cudaError_t launch_batch_any(const BatchArgs<FP8>& a, int M, const LaunchEnv& env) {
   if (env.tp.world != 1) return cudaErrorNotSupported;  // the batched feed-forward runs on one GPU
   if (M < 2 || M > kBatchMax) return cudaErrorInvalidValue;
+  if constexpr (FP8) {  // up to kTermTokens tokens: the term-operand engine
+    if (M <= 4) return launch_term_t<4>(a, M, env);
+    if (M <= 8) return launch_term_t<8>(a, M, env);
+    if (M <= kTermTokens) return launch_term_t<16>(a, M, env);
+  }
   switch ((M + 15) / 16) {
     case 1: return launch_batch_t<16, FP8>(a, M, env);
     case 2: return launch_batch_t<32, FP8>(a, M, env);
@@ -290,6 +357,8 @@ cudaError_t prepare_batch_kernels() {
       (e = prepare_batch_t<64, false>()))
     return e;
   if ((e = prepare_batch_t<16, true>()) || (e = prepare_batch_t<32, true>()) || (e = prepare_batch_t<48, true>()))
+    return e;
+  if ((e = prepare_term_t<4>()) || (e = prepare_term_t<8>()) || (e = prepare_term_t<16>()))
     return e;
   return prepare_batch_t<64, true>();
 }

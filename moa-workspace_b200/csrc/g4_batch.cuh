@@ -571,6 +571,281 @@ __device__ void batch_run(Op& op, uint8_t* smem_raw, const Scratch& sc) {
   }
 }
 
+// ---------------------------------------------------------------------------------------
+// The term-operand engine: FP8 weights at up to kTermTokens tokens.
+//
+// The weights go to the tensor cores as they are: tcgen05.mma kind::f8f6f4, A = 128 weight rows x
+// 32 e4m3 codes from shared memory (K = 32 per instruction, 8 instructions per 256-element unit,
+// no dequantisation), B = each token's activation as kTerms = 4 e4m3 terms: for every (unit,
+// token) a power of two 2^E brings the unit's largest |h| into [128, 256), and h 2^E = sum_j
+// t_j 16^-j with e4m3 terms t_j, each the round-to-nearest e4m3 of the remainder so far (the
+// single-token FP8 kernels' split, split_terms16). A term carries 4 significant bits of its
+// remainder and the remainder's last bit moves up 4 places per term, so a bf16 element x = h 2^E
+// (8 significant bits) is represented exactly when |x| >= 2^-14, i.e. every element within about
+// 2^-22 of the unit's largest (below that, the error is under 2^-21 of the scaled unit). The B
+// rows are (token, term) pairs, N = 4 MT (MT: the tokens padded to 4, 8 or 16). The products are
+// exact and the tensor cores sum them in f32; the epilogue adds each token's terms (smallest
+// first) times 2^-E per unit, keeps the piece's running sums in registers and hands them to the
+// op's epilogue in TMEM, as batch_run does, so the ops (their tile pieces, split-K words and
+// finishing) are the same.
+//
+// The operand rows are built once per call by batch_terms_kernel into sc.batch_terms
+// ([unit][token][term][256 bytes]) and reach shared memory by TMA per unit, from L2.
+
+constexpr int kTThreads = 192;  // warp 0 producer, warp 1 MMA issuer, warps 2-5 epilogue
+
+template <int MT>
+struct TermShape {
+  static constexpr int kMt = MT;
+  static constexpr int kN = MT * kTerms;                // B rows: (token, term)
+  static constexpr int kABytes = 2 * kTileRows * 128;   // two K halves of 128 rows x 128 codes
+  static constexpr int kBHalfBytes = kN * 128;          // one K half of the B rows
+  static constexpr int kStageBytes = kABytes + 2 * kBHalfBytes;
+  static constexpr size_t kXBytes = size_t(16) * 64 * 2;  // the up/gate epilogue's exchange buffer
+  static constexpr size_t kTexpBytes = size_t(kTermUnitsMax) * MT * sizeof(float);  // the call's 2^-E
+  static constexpr int kStagesFit =
+      int((227 * 1024 - kXBytes - kTexpBytes - sizeof(BatchCtl) - 1024) / kStageBytes);
+  static constexpr int kStages = kStagesFit < kBMaxStages ? kStagesFit : kBMaxStages;
+  static constexpr int kTSlotsFit = (512 - 16) / kN;    // unit accumulators (N columns each)
+  static constexpr int kTSlots = kTSlotsFit < 4 ? kTSlotsFit : 4;
+  static constexpr uint32_t kColSum = uint32_t(kTSlots) * kN;  // the piece's sums: 16 columns
+  static constexpr uint32_t kTmemCols = 512;
+  static constexpr uint32_t kIdesc = umma_idesc_f8f6f4(kFmtE4M3, kFmtE4M3, kTileRows, kN);
+  static constexpr size_t kOffX = size_t(kStages) * kStageBytes;
+  static constexpr size_t kOffTexp = kOffX + kXBytes;
+  static constexpr size_t kOffCtl = kOffTexp + kTexpBytes;
+  static constexpr size_t kSmemBytes = kOffCtl + sizeof(BatchCtl) + 1024;
+  static_assert(MT >= 4 && MT <= kTermTokens && kN % 16 == 0, "N of the MMA");
+  static_assert(kStages >= 3 && kTSlots >= 2 && kColSum + 16 <= kTmemCols, "pipeline and TMEM");
+  static_assert(kStageBytes % 1024 == 0 && kBHalfBytes % 1024 == 0, "1024-byte swizzle atoms");
+  static_assert(kSmemBytes <= 227 * 1024, "shared memory budget");
+};
+
+// The term operand of a token batch, one CTA per padded token (gridDim.x = MT; tokens >= M get
+// zero terms). RMS = true: the rows are bf16(RMSNorm(src[m]) * gamma) over K = H (the QKV and
+// feed-forward inputs), bump = true also counts the call (the split-K words' epoch) and sets the
+// tokens' batch_unscale to 1 (the term sums are at true scale); RMS = false: src[m] itself (the
+// GeGLU activation, the attention rows). 256 threads; thread t holds 16-element groups t + 256 q,
+// so a unit's 16 groups sit in one half-warp and its largest |h| is a half-warp reduction.
+template <bool RMS>
+__global__ void __launch_bounds__(256) batch_terms_kernel(const uint16_t* src, int K, const uint16_t* gamma,
+                                                          Scratch sc, int M, bool bump) {
+  __shared__ double red[8];
+  const int m = blockIdx.x, mt = gridDim.x, tid = threadIdx.x, groups = K / 16;
+  const bool live = m < M;
+  uint4 raw[4] = {};
+  if (RMS && tid < groups) load_group_gamma(gamma, tid, raw);
+  pdl_wait_primary();
+  pdl_launch_dependents();
+  if (bump && m == 0 && tid == 0) sc.counters[kBatchEpoch] = __ldcg(sc.counters + kBatchEpoch) + 1u;
+  if (RMS && tid == 0 && m < kBatchMax) sc.batch_unscale[m] = 1.0f;
+  float inv = 0.f;
+  if constexpr (RMS) {  // K = H: one group per thread
+    if (live && tid < groups) load_group_cg(src + size_t(m) * K, tid, raw);
+    const double ss = live && tid < groups ? sum_squares_bf16x16(raw[0], raw[1]) : 0.0;
+    inv = rms_inverse(block_sum_d(ss, red), K);
+  }
+  for (int q = 0; q * 256 < groups; ++q) {  // the same count in every thread (whole half-warps)
+    const int g = tid + 256 * q;
+    const bool have = g < groups;
+    float v[16];
+#pragma unroll
+    for (int j = 0; j < 16; ++j) v[j] = 0.f;
+    if (have && live) {
+      if constexpr (RMS) {
+        rms_apply16(raw, inv, v);
+      } else {
+        uint4 r[4];
+        load_group_cg(src + size_t(m) * K, g, r);
+        bf16x16_to_f32(r[0], r[1], v);
+      }
+    }
+    uint32_t mx = 0u;  // |v| as bits (a NaN compares above every finite value)
+#pragma unroll
+    for (int j = 0; j < 16; ++j) mx = max(mx, __float_as_uint(v[j]) & 0x7fffffffu);
+#pragma unroll
+    for (int o = 8; o; o >>= 1) mx = max(mx, __shfl_xor_sync(0xffffffffu, mx, o));
+    if (have) {
+      int e = 0;  // 2^e brings the unit's largest |v| into [128, 256)
+      if (mx) {
+        e = 7 - (int((mx >> 23) & 0xff) - 127);
+        e = e > 120 ? 120 : (e < -120 ? -120 : e);
+      }
+      const float up = pow2f(e);
+#pragma unroll
+      for (int j = 0; j < 16; ++j) v[j] *= up;
+      uint4 tm[kTerms];
+      split_terms16<kTerms>(v, tm);
+      const int u = g / 16;
+      uint8_t* rows = sc.batch_terms + (size_t(u) * mt + m) * kTerms * 256 + (g % 16) * 16;
+#pragma unroll
+      for (int j = 0; j < kTerms; ++j) *reinterpret_cast<uint4*>(rows + j * 256) = tm[j];
+      if (g % 16 == 0) sc.batch_texp[u * mt + m] = live ? pow2f(-e) : 0.f;
+    }
+  }
+}
+
+// Engine driver (the op interface of batch_run; the op's load_b is not used: `terms` maps the
+// call's term rows, [units x MT x kTerms rows, 256 bytes], box {128 bytes, N rows}).
+template <class TShape, class Op>
+__device__ void batch_term_run(Op& op, const CUtensorMap* terms, uint8_t* smem_raw, const Scratch& sc) {
+  constexpr int S = TShape::kStages, T = TShape::kTSlots, N = TShape::kN, MT = TShape::kMt;
+  constexpr int UPT = Op::kUnitsPerTile;
+  uint8_t* smem = align1024(smem_raw);
+  BatchCtl& ctl = *reinterpret_cast<BatchCtl*>(smem + TShape::kOffCtl);
+  auto stage = [&](int s) { return smem + size_t(s) * TShape::kStageBytes; };
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  const int64_t total = int64_t(UPT) * Op::kTiles, grid = gridDim.x;
+  const int u0 = int(int64_t(blockIdx.x) * total / grid);
+  const int n = int(int64_t(blockIdx.x + 1) * total / grid) - u0;
+  volatile uint32_t* abort = &ctl.abort;
+
+  if (tid == 0) {
+    for (int i = 0; i < S; ++i) {
+      mbar_init(&ctl.full_a[i], 1);
+      mbar_init(&ctl.empty[i], 1);
+    }
+    for (int i = 0; i < T; ++i) {
+      mbar_init(&ctl.done[i], 1);    // the unit's MMAs completed
+      mbar_init(&ctl.tempty[i], 4);  // the epilogue warps read the unit's accumulator
+    }
+    mbar_init(&ctl.drain, 1);
+    ctl.abort = 0;
+    fence_mbar_init();
+  }
+  __syncwarp();
+  if (warp == 1) tmem_alloc(&ctl.tmem_base, TShape::kTmemCols);
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tbase = ctl.tmem_base;
+  const uint64_t policy = l2_evict_first_policy();
+  const uint64_t policy_b = l2_evict_last_policy();  // every CTA reads the term rows
+  const int prefetch = n < S ? n : S;
+  auto load_terms = [&](uint8_t* st, int kc, uint64_t* bar) {
+#pragma unroll
+    for (int h = 0; h < 2; ++h)
+      tma_load_2d(st + TShape::kABytes + h * TShape::kBHalfBytes, terms, h * 128, kc * N, bar, policy_b);
+  };
+  // the first units' weights before the wait on the preceding kernel, their term rows after it
+  if (tid < prefetch) {
+    const int u = u0 + tid;
+    mbar_arrive_expect_tx(&ctl.full_a[tid], uint32_t(TShape::kStageBytes));
+    op.load_a(stage(tid), u / UPT, u % UPT, &ctl.full_a[tid], policy);
+  }
+  __syncwarp();
+  pdl_wait_primary();
+  pdl_launch_dependents();
+  op.prologue();
+  if (tid < prefetch) load_terms(stage(tid), (u0 + tid) % UPT, &ctl.full_a[tid]);
+  if (tid == kTThreads - 1) op.prefetch_l2(u0 + prefetch, u0 + (prefetch + 6 < n ? prefetch + 6 : n));
+  __syncwarp();
+
+  if (warp == 0) {
+    // ---------------------------------------------------------------- producer
+    if (lane == 0) {
+      int issued = prefetch;
+      for (int i = prefetch; i < n; ++i) {
+        const int s = i % S, r = i - S;
+        if (!mbar_wait_or_abort(&ctl.empty[s], uint32_t((r / S) & 1), abort, sc.err)) break;
+        const int u = u0 + i;
+        mbar_arrive_expect_tx(&ctl.full_a[s], uint32_t(TShape::kStageBytes));
+        op.load_a(stage(s), u / UPT, u % UPT, &ctl.full_a[s], policy);
+        load_terms(stage(s), u % UPT, &ctl.full_a[s]);
+        if ((i - prefetch) % 2 == 0 && i + 6 < n) op.prefetch_l2(u + 6, u0 + (i + 8 < n ? i + 8 : n));
+        issued = i + 1;
+      }
+      // every requested copy has landed before the CTA may exit
+      for (int i = issued - S > 0 ? issued - S : 0; i < issued; ++i) {
+        const uint64_t t0 = globaltimer_ns();
+        while (!mbar_try_wait(&ctl.full_a[i % S], uint32_t((i / S) & 1)))
+          if (globaltimer_ns() - t0 > kWaitLimitNs) break;
+      }
+    }
+    __syncwarp();
+  } else if (warp == 1) {
+    // ---------------------------------------------------------------- MMA issuer
+    if (lane == 0) {
+      for (int i = 0; i < n; ++i) {
+        const int s = i % S, t = i % T;
+        bool ok = i < T || mbar_wait_or_abort(&ctl.tempty[t], uint32_t(((i / T) - 1) & 1), abort, sc.err);
+        ok = ok && mbar_wait_or_abort(&ctl.full_a[s], uint32_t((i / S) & 1), abort, sc.err);
+        if (!ok) break;
+        tc_fence_after();
+        const uint32_t a0 = smem_u32(stage(s)), b0 = a0 + uint32_t(TShape::kABytes);
+#pragma unroll
+        for (int j = 0; j < 8; ++j) {  // K = 32 each: K half j / 4, 32 bytes a step
+          const uint32_t h = j / 4, kk = j % 4;
+          umma_f8f6f4(tbase + uint32_t(t * N), umma_desc_sw128(a0 + h * uint32_t(kTileRows * 128) + kk * 32u),
+                      umma_desc_sw128(b0 + h * uint32_t(TShape::kBHalfBytes) + kk * 32u), TShape::kIdesc,
+                      uint32_t(j > 0));
+        }
+        umma_commit(&ctl.empty[s]);
+        umma_commit(&ctl.done[t]);
+      }
+      umma_commit(&ctl.drain);  // nothing of ours may still be running when TMEM is released
+      const uint64_t t0 = globaltimer_ns();
+      while (!mbar_try_wait(&ctl.drain, 0))
+        if (globaltimer_ns() - t0 > kWaitLimitNs) break;
+    }
+    __syncwarp();
+  } else {
+    // ---------------------------------------------------------------- epilogue (warps 2-5)
+    const int quarter = warp & 3, row = quarter * 32 + lane;
+    const uint32_t lane_addr = uint32_t(quarter * 32) << 16;
+    const uint32_t tsum = tbase + lane_addr + TShape::kColSum;
+    uint8_t* xbuf = smem + TShape::kOffX;
+    // the call's 2^-E of every (unit, token) into shared memory once (written before this kernel's wait)
+    float* texp = reinterpret_cast<float*>(smem + TShape::kOffTexp);
+    for (int k = tid - 64; k < UPT * MT; k += 128) texp[k] = __ldcg(sc.batch_texp + k);
+    named_bar(kBEpiBarrier, 128);
+    bool ok = true;
+    float acc[MT];
+#pragma unroll
+    for (int m = 0; m < MT; ++m) acc[m] = 0.f;
+    for (int i = 0; i < n; ++i) {
+      const int u = u0 + i, tile = u / UPT, kc = u % UPT, t = i % T;
+      if (ok) ok = mbar_wait_or_abort(&ctl.done[t], uint32_t((i / T) & 1), abort, sc.err);
+      tc_fence_after();
+      float d[N];  // the unit's N columns of this row: every load in flight, one wait
+      if (ok) {
+#pragma unroll
+        for (int c = 0; c < N; c += 16)
+          tmem_ld16(tbase + lane_addr + uint32_t(t * N + c), *reinterpret_cast<float(*)[16]>(d + c));
+        tmem_ld_wait();
+      }
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&ctl.tempty[t]);  // the accumulator is free for the next unit
+      if (ok) {
+#pragma unroll
+        for (int m = 0; m < MT; ++m)  // each token's terms, smallest first, times its 2^-E
+          acc[m] = fmaf(combine_terms<kTerms>(d + kTerms * m), texp[kc * MT + m], acc[m]);
+      }
+      if (!(kc == UPT - 1 || i == n - 1)) continue;
+      // the piece's sums (16 TMEM columns of this row) for the op's epilogue
+      uint32_t bits[16];
+#pragma unroll
+      for (int m = 0; m < 16; ++m) bits[m] = __float_as_uint(m < MT ? acc[m] : 0.f);
+      if (ok) {
+        tmem_st16(tsum, bits);
+        tmem_st_wait();
+      }
+      op.finish(ctl, xbuf, tile, row, tsum, ok);
+#pragma unroll
+      for (int m = 0; m < MT; ++m) acc[m] = 0.f;
+    }
+  }
+
+  // teardown: every MMA has completed (drain) and every TMEM access has been waited for
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 1) {
+    tc_fence_after();
+    tmem_dealloc(tbase, TShape::kTmemCols);
+  }
+}
+
 // The epoch-tagged words of one batched kernel: the call count kept by batch_norm_kernel (bumped
 // once per QKV and once per feed-forward call) and the kernel kind, so that words left by another
 // kernel or an earlier call never match.

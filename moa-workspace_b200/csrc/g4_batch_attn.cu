@@ -125,6 +125,24 @@ __global__ void __launch_bounds__(kBThreads, 1) o_batch_kernel(const __grid_cons
   batch_run<BatchShape<MPAD, true>>(op, smem, sc);
 }
 
+// The same projections on the term-operand engine (up to kTermTokens tokens; `maps.b` maps the
+// call's term rows).
+template <int MT>
+__global__ void __launch_bounds__(kTThreads, 1) qkv_term_kernel(const __grid_constant__ BatchMaps maps, QkvArgs a,
+                                                                Scratch sc, int M) {
+  extern __shared__ __align__(1024) uint8_t smem[];
+  BatchQkvOp<kTermTokens> op{&maps, a, sc, M};
+  batch_term_run<TermShape<MT>>(op, &maps.b, smem, sc);
+}
+
+template <int MT>
+__global__ void __launch_bounds__(kTThreads, 1) o_term_kernel(const __grid_constant__ BatchMaps maps, OArgs a,
+                                                              Scratch sc, int M) {
+  extern __shared__ __align__(1024) uint8_t smem[];
+  BatchOOp<kTermTokens> op{&maps, a, sc, M};
+  batch_term_run<TermShape<MT>>(op, &maps.b, smem, sc);
+}
+
 // Per (head, token), 256 threads (thread e: element e of the head, row e % 128 of tile
 // 2 head + e / 128): the tile's pieces added in CTA order, times the token's 2^-k (exact), the
 // row scale (scaled_projection: bf16((x @ codes.T) * scale), generate_references.py:265-274), the
@@ -242,6 +260,53 @@ cudaError_t launch_o_batch_t(const OArgs& a, int M, const LaunchEnv& env) {
   return launch_batch(batch_finalize_kernel<kOUpt, kTagO>, M, kFinThreads, 0, true, env.stream, fa, env.sc, grid);
 }
 
+template <int MT>
+cudaError_t launch_qkv_term_t(const QkvArgs& a, int M, const LaunchEnv& env) {
+  BatchMaps mp{};
+  cudaError_t e;
+  if ((e = fp8_map(env, a.q_weight, a.tiled, kQs, kH, &mp.a))) return e;
+  if ((e = fp8_map(env, a.k_weight, a.tiled, kPs, kH, &mp.a2))) return e;
+  if ((e = fp8_map(env, a.v_weight, a.tiled, kPs, kH, &mp.s))) return e;
+  if ((e = env.maps->u8(env.sc.batch_terms, 256, uint64_t(kQkvUpt) * MT * kTerms, 128, MT * kTerms, true, &mp.b)))
+    return e;
+  const int grid = env.sm_count;
+  if ((e = launch_batch(batch_terms_kernel<true>, MT, 256, 0, env.pdl, env.stream, a.x, kH, a.input_rms, env.sc, M,
+                        true)))
+    return e;
+  if ((e = launch_batch(qkv_term_kernel<MT>, grid, kTThreads, TermShape<MT>::kSmemBytes, true, env.stream, mp, a,
+                        env.sc, M)))
+    return e;
+  return launch_batch(qkv_batch_finalize_kernel, dim3(kQkvHeads, M), kDs, 0, true, env.stream, a, env.sc, grid);
+}
+
+template <int MT>
+cudaError_t launch_o_term_t(const OArgs& a, int M, const LaunchEnv& env) {
+  BatchMaps mp{};
+  cudaError_t e;
+  if ((e = fp8_map(env, a.o_weight, a.tiled, kH, kQs, &mp.a))) return e;
+  if ((e = env.maps->u8(env.sc.batch_terms, 256, uint64_t(kOUpt) * MT * kTerms, 128, MT * kTerms, true, &mp.b)))
+    return e;
+  const int grid = env.sm_count;
+  if ((e = launch_batch(batch_terms_kernel<false>, MT, 256, 0, env.pdl, env.stream, a.x, kQs,
+                        static_cast<const uint16_t*>(nullptr), env.sc, M, false)))
+    return e;
+  if ((e = launch_batch(o_term_kernel<MT>, grid, kTThreads, TermShape<MT>::kSmemBytes, true, env.stream, mp, a, env.sc,
+                        M)))
+    return e;
+  const FinalizeArgs fa{a.residual, a.post_rms, nullptr, nullptr, nullptr, a.o_scale};
+  return launch_batch(batch_finalize_kernel<kOUpt, kTagO>, M, kFinThreads, 0, true, env.stream, fa, env.sc, grid);
+}
+
+template <int MT>
+cudaError_t prepare_term_t() {
+  cudaError_t e;
+  if ((e = cudaFuncSetAttribute(qkv_term_kernel<MT>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                int(TermShape<MT>::kSmemBytes))))
+    return e;
+  return cudaFuncSetAttribute(o_term_kernel<MT>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                              int(TermShape<MT>::kSmemBytes));
+}
+
 template <int MPAD>
 cudaError_t prepare_t() {
   cudaError_t e;
@@ -269,8 +334,9 @@ bool split_fits(int grid, int upt, int tiles) {
 
 cudaError_t prepare_batch_attn_kernels() {
   cudaError_t e;
-  if ((e = prepare_t<16>()) || (e = prepare_t<32>()) || (e = prepare_t<48>())) return e;
-  return prepare_t<64>();
+  if ((e = prepare_t<16>()) || (e = prepare_t<32>()) || (e = prepare_t<48>()) || (e = prepare_t<64>())) return e;
+  if ((e = prepare_term_t<4>()) || (e = prepare_term_t<8>())) return e;
+  return prepare_term_t<16>();
 }
 
 bool batch_attn_geometry_fits(int sm_count) {
@@ -280,6 +346,9 @@ bool batch_attn_geometry_fits(int sm_count) {
 cudaError_t launch_qkv_batch(const QkvArgs& a, int M, const LaunchEnv& env) {
   if (env.tp.world != 1) return cudaErrorNotSupported;  // the batched ops run on one GPU
   if (M < 2 || M > kBatchMax) return cudaErrorInvalidValue;
+  if (M <= 4) return launch_qkv_term_t<4>(a, M, env);  // up to kTermTokens: the term-operand engine
+  if (M <= 8) return launch_qkv_term_t<8>(a, M, env);
+  if (M <= kTermTokens) return launch_qkv_term_t<16>(a, M, env);
   switch ((M + 15) / 16) {
     case 1: return launch_qkv_batch_t<16>(a, M, env);
     case 2: return launch_qkv_batch_t<32>(a, M, env);
@@ -291,6 +360,9 @@ cudaError_t launch_qkv_batch(const QkvArgs& a, int M, const LaunchEnv& env) {
 cudaError_t launch_o_batch(const OArgs& a, int M, const LaunchEnv& env) {
   if (env.tp.world != 1) return cudaErrorNotSupported;
   if (M < 2 || M > kBatchMax) return cudaErrorInvalidValue;
+  if (M <= 4) return launch_o_term_t<4>(a, M, env);  // up to kTermTokens: the term-operand engine
+  if (M <= 8) return launch_o_term_t<8>(a, M, env);
+  if (M <= kTermTokens) return launch_o_term_t<16>(a, M, env);
   switch ((M + 15) / 16) {
     case 1: return launch_o_batch_t<16>(a, M, env);
     case 2: return launch_o_batch_t<32>(a, M, env);

@@ -70,8 +70,16 @@ struct Scratch {
   uint16_t* batch_h;
   float* batch_unscale;  // [kBatchMax]: 2^-k of each token's f16 scaling of h
   unsigned long long* batch_words;
+  // the term-operand path of FP8 weights at up to kTermTokens tokens: each token's activation as
+  // exact e4m3 terms, [units][kTermTokens padded tokens][kTerms terms][256 bytes], and each
+  // (unit, token)'s 2^-E
+  uint8_t* batch_terms;
+  float* batch_texp;
 };
 constexpr int kBatchMax = 64;  // tokens per batched feed-forward call
+constexpr int kTermTokens = 16;   // the term-operand path's largest batch
+constexpr int kTerms = 4;         // e4m3 terms per activation element (the term-operand path)
+constexpr int kTermUnitsMax = 60;  // 256-element units of the longest activation (the FFN's 15360)
 // the batched feed-forward's call count (tags its split-K words and tile sums)
 constexpr int kBatchEpoch = 4080;
 constexpr int kTileSsCount = 64;

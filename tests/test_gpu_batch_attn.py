@@ -87,14 +87,17 @@ def test_qkv_batch_matches_oracle_per_sequence(device, m):
 
 
 def test_qkv_batch_tiled_identical_and_batch_independent(device):
-    """The unit-tiled weights give the same bits; a sequence's result does not depend on the
-    batch it came in (rows 0-1 of a batch of 33 equal a batch of 2)."""
+    """For both engines (kind::f16 tiles above 16 sequences, e4m3 term operands up to 16): the
+    unit-tiled weights give the same bits, and a sequence's result does not depend on the batch it
+    came in (33 vs 17 sequences, 16 vs 2)."""
     d = qkv_batch_inputs(33, 1024, 1e6, seed=7)
-    q, kc, vc = run_qkv_batch(device, d)
-    qt, kct, vct = run_qkv_batch(device, d, tiled=True)
-    assert np.array_equal(q, qt) and np.array_equal(kc, kct) and np.array_equal(vc, vct)
-    q2, kc2, vc2 = run_qkv_batch(device, d, m=2)
-    assert np.array_equal(q2, q[:2]) and np.array_equal(kc2, kc[:2]) and np.array_equal(vc2, vc[:2])
+    for big, small in ((33, 17), (16, 2)):
+        q, kc, vc = run_qkv_batch(device, d, m=big)
+        qt, kct, vct = run_qkv_batch(device, d, m=big, tiled=True)
+        assert np.array_equal(q, qt) and np.array_equal(kc, kct) and np.array_equal(vc, vct)
+        q2, kc2, vc2 = run_qkv_batch(device, d, m=small)
+        assert np.array_equal(q2, q[:small]) and np.array_equal(kc2, kc[:small])
+        assert np.array_equal(vc2, vc[:small])
 
 
 def test_qkv_batch_bad_offset_skips_only_that_sequence(device):
@@ -215,6 +218,7 @@ def test_o_batch_matches_oracle_per_sequence(device, m):
 
 def test_o_batch_tiled_identical_and_batch_independent(device):
     d = o_batch_inputs(40, seed=5)
-    got = run_o_batch(device, d)
-    assert np.array_equal(run_o_batch(device, d, tiled=True), got)
-    assert np.array_equal(run_o_batch(device, d, m=3), got[:3])
+    for big, small in ((40, 20), (16, 3)):  # each engine
+        got = run_o_batch(device, d, m=big)
+        assert np.array_equal(run_o_batch(device, d, m=big, tiled=True), got)
+        assert np.array_equal(run_o_batch(device, d, m=small), got[:small])
