@@ -1135,8 +1135,7 @@ def run_only(args):
             secs = timed(torch, lambda: [dec.step(stream=stream) for _ in range(args.steps)])
         device.check(stream)
         print(json.dumps({"only": "decode", "batch": nb, "steps": args.steps,
-                          "ms_per_step": round(secs / args.steps * 1e3, 4),
-                          "launches_per_step": 2 + KERNELS_PER_LAYER * N_MODEL}), flush=True)
+                          "ms_per_step": round(secs / args.steps * 1e3, 4)}), flush=True)
         dec.close()
         device.close()
         return 0
@@ -1166,7 +1165,7 @@ def run_only(args):
         def call(i):
             k, v = caches[i % len(caches)]
             ops.sliding_attention_batch(device, q, k, v, mask, out, scale=ATTN_SCALE, kv_offset=kv)
-    elif args.only == "ffn4b":  # the NVFP4 feed-forward on a batch of --batch tokens
+    elif args.only in ("ffn4b", "ffn8b"):  # the NVFP4 / FP8 feed-forward on a batch of --batch tokens
         rows = torch.randn(args.batch, H, device=dev, generator=gen).to(torch.bfloat16)
 
         def call(i):
@@ -1193,9 +1192,10 @@ def run_only(args):
 
 def main():
     ap = argparse.ArgumentParser()
-    ap.add_argument("--batch", type=int, default=16, help="--only ffn4b / attnb: tokens (sequences) per call")
+    ap.add_argument("--batch", type=int, default=16, help="--only ffn4b / ffn8b / attnb: tokens (sequences) per call")
     ap.add_argument("--ring", type=int, default=RING_LOCAL, help="--only attnb: slots per sequence's ring")
-    ap.add_argument("--only", choices=["qkv", "attn", "o", "ffn8", "ffn4", "ffn4b", "attnb", "decode"], default=None,
+    ap.add_argument("--only", choices=["qkv", "attn", "o", "ffn8", "ffn4", "ffn4b", "ffn8b", "attnb", "decode"],
+                    default=None,
                     help="profiling aid: eager calls of one op only (prints us/call, not the bench line)")
     ap.add_argument("--layers", type=int, default=4, help="--only: layer copies to rotate over")
     ap.add_argument("--gpus", type=int, default=1)
