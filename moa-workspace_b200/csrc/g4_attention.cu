@@ -53,8 +53,9 @@ struct AttnSmem {
   static constexpr int kSub = SUB;
   static constexpr int kBoxes = SUB / kBox;
   static_assert(SUB % kBox == 0 && kBoxes <= kThreads, "boxes per pass");
-  uint8_t k[kSub * kRowBytes];
-  uint8_t v[kSub * kRowBytes];
+  // two pass buffers: the K passes, then the V passes, alternate between them, so a pass's rows
+  // land while the previous pass is used
+  uint8_t buf[2][kSub * kRowBytes];
   // per slot, the two query heads' bf16 scores, then their bf16-rounded probabilities (head 1 in
   // the high half): the values the reference rounds to bf16 anyway
   uint32_t score[kMaxPer];
@@ -63,7 +64,7 @@ struct AttnSmem {
   float po[kGs][kDs];         // this CTA's partial sum_t bf16(p) v (read by the cluster)
   float pz[kGs];              // and sum_t p
   __align__(16) uint16_t out[kGs * kDimsPerCta];
-  uint64_t kbar[kBoxes], vbar[kBoxes];
+  uint64_t bar[2][kBoxes];
 };
 using Attn8 = AttnSmem<8, 128>;
 using Attn16 = AttnSmem<16, 64>;
@@ -126,8 +127,8 @@ __global__ void __launch_bounds__(kThreads, MINB) attention_kernel(const __grid_
   volatile uint32_t abort_flag = 0;  // this CTA's own waits only
   G4_STAMP(sc, 0);
   if (tid < kBoxes) {
-    mbar_init(&sm.kbar[tid], 1);
-    mbar_init(&sm.vbar[tid], 1);
+    mbar_init(&sm.bar[0][tid], 1);
+    mbar_init(&sm.bar[1][tid], 1);
     fence_mbar_init();
   }
   // rows [first, first + count) of a cache into a shared-memory buffer: box b (kBox rows) by
@@ -140,7 +141,20 @@ __global__ void __launch_bounds__(kThreads, MINB) attention_kernel(const __grid_
       tma_load_3d(dst + b * kBox * kRowBytes, map, 0, head, gslot0 + first + b * kBox, &bars[b], policy);
     }
   };
-  const int first_rows = per < kSub ? per : kSub;
+  // The loads as a sequence of jobs: job j < P is K pass j, job P + p is V pass p (P passes of
+  // kSub slots, the last possibly shorter), job j into buffer j % 2. Jobs 0 and 1 are requested up
+  // front, job j + 2 once job j is used. A box's barrier completes once per job that arms it: the
+  // K passes' last job (P - 1) arms only `last_rows` of them.
+  const int last_rows = per - (passes - 1) * kSub;
+  auto job_rows = [&](int j) { return (j % passes) == passes - 1 ? last_rows : kSub; };
+  auto issue = [&](int j) {
+    if (j < 2 * passes) fetch(j < passes ? &maps.k : &maps.v, sm.buf[j % 2], sm.bar[j % 2], (j % passes) * kSub,
+                              job_rows(j));
+  };
+  auto parity = [&](int j, int b) {
+    const int skipped = j > passes - 1 && (passes - 1) % 2 == j % 2 && last_rows <= b * kBox ? 1 : 0;
+    return uint32_t((j / 2 - skipped) & 1);
+  };
   // The slot the preceding QKV op writes, when the caller says which (-1: any row may change).
   int cur = -1;
   if (a.kv_offset) {
@@ -148,15 +162,16 @@ __global__ void __launch_bounds__(kThreads, MINB) attention_kernel(const __grid_
     if (kv >= 0 && kv % (kPs * 2) == 0 && kv / (kPs * 2) < a.ring_len) cur = kv / (kPs * 2);
   }
   if (a.kv_offset) {
-    // every row but the slot's is final: the first pass's K and V rows go straight into shared
-    // memory while the QKV op finishes (the slot's rows are read again after the wait)
+    // every row but the slot's is final: jobs 0 and 1 go straight into shared memory while the
+    // QKV op finishes (the slot's rows are read again after the wait)
     __syncthreads();  // the barriers are initialised
-    fetch(&maps.k, sm.k, sm.kbar, 0, first_rows);
-    fetch(&maps.v, sm.v, sm.vbar, 0, first_rows);
+    issue(0);
+    issue(1);
   }
   // While the preceding QKV op finishes, bring this CTA's other K and V rows into L2 (L2 is
   // coherent, so copies made after the wait still see the slot that op writes).
   {
+    const int first_rows = per < kSub ? per : kSub;
     const int nb = per / kBox, skip = a.kv_offset ? first_rows / kBox : 0;
     for (int b = skip + tid; b < nb; b += kThreads) {
       tma_prefetch_l2_3d(&maps.k, 0, head, gslot0 + b * kBox);
@@ -170,22 +185,30 @@ __global__ void __launch_bounds__(kThreads, MINB) attention_kernel(const __grid_
   G4_STAMP(sc, 1);
 
   if (!a.kv_offset) {
-    fetch(&maps.k, sm.k, sm.kbar, 0, first_rows);
-    fetch(&maps.v, sm.v, sm.vbar, 0, first_rows);  // (its own buffer: in flight while scoring)
-  } else if (cur >= slot0 && cur < slot0 + first_rows) {
-    // the slot's fresh K and V rows over the early copies, once the boxes holding them landed
-    const int t = cur - slot0, box = t / kBox;
-    bool okb = mbar_wait_or_abort(&sm.kbar[box], 0u, &abort_flag, sc.err);
-    okb = mbar_wait_or_abort(&sm.vbar[box], 0u, &abort_flag, sc.err) && okb;
-    if (okb && tid < 2 * (kRowBytes / 16)) {  // 32 x 16 bytes per row, K then V
-      const bool is_v = tid >= kRowBytes / 16;
-      const int q16 = tid % (kRowBytes / 16);
-      const uint16_t* src =
-          (is_v ? a.v_cache : a.k_cache) + (size_t(seq * a.ring_len + cur) * a.heads + head) * kDs;
-      const uint4 x = __ldcg(reinterpret_cast<const uint4*>(src) + q16);
-      reinterpret_cast<uint4*>((is_v ? sm.v : sm.k) + t * kRowBytes)[q16] = x;
+    issue(0);
+    issue(1);
+  } else if (cur >= slot0) {
+    // the slot's fresh rows over the early copies of jobs 0 and 1, once the boxes holding them
+    // landed (both waits first, then both rows: threads 32 j .. 32 j + 31 copy job j's 32 x 16 bytes)
+    int tj[2];
+    bool okb = true, fixed = false;
+    for (int j = 0; j < 2; ++j) {
+      tj[j] = cur - slot0 - (j % passes) * kSub;
+      if (j >= 2 * passes || tj[j] < 0 || tj[j] >= job_rows(j)) {
+        tj[j] = -1;
+        continue;
+      }
+      okb = mbar_wait_or_abort(&sm.bar[j % 2][tj[j] / kBox], 0u, &abort_flag, sc.err) && okb;
+      fixed = true;
     }
-    __syncthreads();  // the rows are in place before anyone scores (or reads V)
+    const int j = tid / (kRowBytes / 16), q16 = tid % (kRowBytes / 16);
+    const int t = j == 0 ? tj[0] : tj[1];
+    if (okb && j < 2 && t >= 0) {
+      const uint16_t* src =
+          (j < passes ? a.k_cache : a.v_cache) + (size_t(seq * a.ring_len + cur) * a.heads + head) * kDs;
+      reinterpret_cast<uint4*>(sm.buf[j % 2] + t * kRowBytes)[q16] = __ldcg(reinterpret_cast<const uint4*>(src) + q16);
+    }
+    if (fixed) __syncthreads();  // the rows are in place before anyone reads them (CTA-uniform)
   }
 
   // phase 1: scores, kSub slots at a time. The 8 lanes 8i .. 8i + 7 of a warp score one slot,
@@ -206,16 +229,12 @@ __global__ void __launch_bounds__(kThreads, MINB) attention_kernel(const __grid_
     }
   }
   bool ok = true;
-  for (int p = 0; p < passes; ++p) {
-    const int first = p * kSub, rows = per - first < kSub ? per - first : kSub;
-    if (p > 0) {
-      __syncthreads();  // the previous pass is done with the K buffer
-      fetch(&maps.k, sm.k, sm.kbar, first, rows);
-    }
+  for (int p = 0; p < passes; ++p) {  // job p
+    const int first = p * kSub, rows = job_rows(p);
     for (int b = 0; b < rows / kBox; ++b) {
-      if (ok) ok = mbar_wait_or_abort(&sm.kbar[b], uint32_t(p & 1), &abort_flag, sc.err);
+      if (ok) ok = mbar_wait_or_abort(&sm.bar[p % 2][b], parity(p, b), &abort_flag, sc.err);
       const int t = b * kBox + warp * kSlotsPerStep + sub;
-      const uint8_t* row = sm.k + t * kRowBytes + part * 16;
+      const uint8_t* row = sm.buf[p % 2] + t * kRowBytes + part * 16;
       float d0 = 0.f, d1 = 0.f;
 #pragma unroll
       for (int c = 0; c < 4; ++c) {
@@ -236,8 +255,9 @@ __global__ void __launch_bounds__(kThreads, MINB) attention_kernel(const __grid_
       }
       if (part == 0) sm.score[first + t] = pack_bf16(a.scale * d0, a.scale * d1);
     }
+    __syncthreads();  // every thread is done with buffer p % 2 (and, the last pass, every score is in)
+    issue(p + 2);     // the job after next into it
   }
-  __syncthreads();
   G4_STAMP(sc, 2);
 
   // this CTA's maximum; then the head's maximum over the cluster (distributed shared memory)
@@ -295,21 +315,22 @@ __global__ void __launch_bounds__(kThreads, MINB) attention_kernel(const __grid_
 
   // phase 2: o[g][d] = sum_t bf16(p[g][t]) v[t][d]; thread d owns dimension d of both heads
   float o0 = 0.f, o1 = 0.f;
-  for (int p = 0; p < passes; ++p) {
-    const int first = p * kSub, rows = per - first < kSub ? per - first : kSub;
-    if (p > 0) {
-      __syncthreads();  // the previous pass is done with the V buffer (pass 0 was requested up front)
-      fetch(&maps.v, sm.v, sm.vbar, first, rows);
-    }
+  for (int p = 0; p < passes; ++p) {  // job passes + p
+    const int j = passes + p, first = p * kSub, rows = job_rows(j);
+    const uint8_t* vb = sm.buf[j % 2];
     for (int b = 0; b < rows / kBox; ++b) {
-      if (ok) ok = mbar_wait_or_abort(&sm.vbar[b], uint32_t(p & 1), &abort_flag, sc.err);
+      if (ok) ok = mbar_wait_or_abort(&sm.bar[j % 2][b], parity(j, b), &abort_flag, sc.err);
 #pragma unroll 8
       for (int t = b * kBox; t < (b + 1) * kBox; ++t) {
-        const float vf = bf16_to_f32(reinterpret_cast<const uint16_t*>(sm.v + t * kRowBytes)[tid]);
+        const float vf = bf16_to_f32(reinterpret_cast<const uint16_t*>(vb + t * kRowBytes)[tid]);
         const uint32_t w = sm.score[first + t];
         o0 = fmaf(lo_bf16(w), vf, o0);
         o1 = fmaf(hi_bf16(w), vf, o1);
       }
+    }
+    if (j + 2 < 2 * passes) {  // CTA-uniform
+      __syncthreads();  // every thread is done with buffer j % 2
+      issue(j + 2);
     }
   }
   sm.po[0][tid] = o0;
