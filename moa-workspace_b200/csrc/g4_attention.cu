@@ -178,6 +178,9 @@ __global__ void __launch_bounds__(kThreads, MINB) attention_kernel(const __grid_
       tma_prefetch_l2_3d(&maps.v, 0, head, gslot0 + b * kBox);
     }
   }
+  // and the weights the following O and feed-forward kernels stream first (the decode driver's
+  // hints): this op moves few bytes, so HBM has time for them while it runs
+  issue_l2_hints(a.next, 2, blockIdx.y * gridDim.x + blockIdx.x, gridDim.x * gridDim.y);
   __syncthreads();
 
   pdl_wait_primary();  // q and the cache rows come from the preceding QKV op
@@ -218,7 +221,11 @@ __global__ void __launch_bounds__(kThreads, MINB) attention_kernel(const __grid_
   constexpr int kLanesPerSlot = 8, kSlotsPerStep = 32 / kLanesPerSlot;
   static_assert(kWarps * kSlotsPerStep == kBox, "one box per step of the CTA");
   const int sub = lane / kLanesPerSlot, part = lane % kLanesPerSlot;
-  uint32_t qv[kGs][16];  // this lane's 32 q elements of each head as bf16 pairs (element 2i low)
+  // This lane's 32 q elements of each head: as f32 where the registers allow (one or two CTAs per
+  // SM), else as bf16 pairs (element 2i low) converted at each use (the batch shape's three).
+  constexpr bool kQf32 = MINB <= 2;
+  uint32_t qv[kGs][16];
+  float qf[kGs][kQf32 ? 32 : 1];
 #pragma unroll
   for (int g = 0; g < kGs; ++g) {
 #pragma unroll
@@ -228,6 +235,19 @@ __global__ void __launch_bounds__(kThreads, MINB) attention_kernel(const __grid_
       qv[g][4 * c] = raw.x, qv[g][4 * c + 1] = raw.y, qv[g][4 * c + 2] = raw.z, qv[g][4 * c + 3] = raw.w;
     }
   }
+  if constexpr (kQf32) {
+#pragma unroll
+    for (int g = 0; g < kGs; ++g)
+#pragma unroll
+      for (int i = 0; i < 16; ++i) {
+        qf[g][2 * i] = lo_bf16(qv[g][i]);
+        qf[g][2 * i + 1] = hi_bf16(qv[g][i]);
+      }
+  }
+  auto q_at = [&](int g, int e) {  // element e (< 32) of this lane's share of query head g
+    if constexpr (kQf32) return qf[g][e];
+    else return e % 2 ? hi_bf16(qv[g][e / 2]) : lo_bf16(qv[g][e / 2]);
+  };
   bool ok = true;
   for (int p = 0; p < passes; ++p) {  // job p
     const int first = p * kSub, rows = job_rows(p);
@@ -235,19 +255,24 @@ __global__ void __launch_bounds__(kThreads, MINB) attention_kernel(const __grid_
       if (ok) ok = mbar_wait_or_abort(&sm.bar[p % 2][b], parity(p, b), &abort_flag, sc.err);
       const int t = b * kBox + warp * kSlotsPerStep + sub;
       const uint8_t* row = sm.buf[p % 2] + t * kRowBytes + part * 16;
-      float d0 = 0.f, d1 = 0.f;
+      // one accumulator per head and 64-dimension chunk (chains of 8), added pairwise after
+      float dc[kGs][4];
 #pragma unroll
       for (int c = 0; c < 4; ++c) {
         const uint4 kr = *reinterpret_cast<const uint4*>(row + c * 128);
         const uint32_t kw[4] = {kr.x, kr.y, kr.z, kr.w};
+        dc[0][c] = dc[1][c] = 0.f;
 #pragma unroll
         for (int i = 0; i < 4; ++i) {  // elements 2i and 2i + 1 of the chunk, in element order
-          d0 = fmaf(lo_bf16(qv[0][4 * c + i]), lo_bf16(kw[i]), d0);
-          d1 = fmaf(lo_bf16(qv[1][4 * c + i]), lo_bf16(kw[i]), d1);
-          d0 = fmaf(hi_bf16(qv[0][4 * c + i]), hi_bf16(kw[i]), d0);
-          d1 = fmaf(hi_bf16(qv[1][4 * c + i]), hi_bf16(kw[i]), d1);
+          const float k0 = lo_bf16(kw[i]), k1 = hi_bf16(kw[i]);
+          dc[0][c] = fmaf(q_at(0, 8 * c + 2 * i), k0, dc[0][c]);
+          dc[1][c] = fmaf(q_at(1, 8 * c + 2 * i), k0, dc[1][c]);
+          dc[0][c] = fmaf(q_at(0, 8 * c + 2 * i + 1), k1, dc[0][c]);
+          dc[1][c] = fmaf(q_at(1, 8 * c + 2 * i + 1), k1, dc[1][c]);
         }
       }
+      float d0 = (dc[0][0] + dc[0][1]) + (dc[0][2] + dc[0][3]);
+      float d1 = (dc[1][0] + dc[1][1]) + (dc[1][2] + dc[1][3]);
 #pragma unroll
       for (int o = kLanesPerSlot / 2; o; o >>= 1) {
         d0 += __shfl_xor_sync(0xffffffffu, d0, o);
@@ -313,19 +338,33 @@ __global__ void __launch_bounds__(kThreads, MINB) attention_kernel(const __grid_
   __syncthreads();
   G4_STAMP(sc, 4);
 
-  // phase 2: o[g][d] = sum_t bf16(p[g][t]) v[t][d]; thread d owns dimension d of both heads
-  float o0 = 0.f, o1 = 0.f;
+  // phase 2: o[g][d] = sum_t bf16(p[g][t]) v[t][d]. Thread tid owns the dimension pair
+  // (2 dp, 2 dp + 1), dp = tid % 128, of both heads over one half of every box's slots (slots
+  // [16 h, 16 h + 16) of the box, h = tid / 128), in two accumulator sets (even and odd slots);
+  // the sets, then the halves, are added in a fixed order.
+  constexpr int kHalf = kBox / 2;
+  static_assert(kThreads == kDs, "thread pairs cover the head's 128 dimension pairs twice");
+  const int dp = tid % (kThreads / 2), half = tid / (kThreads / 2);
+  float acc[2][kGs][2];
+#pragma unroll
+  for (int e = 0; e < 2; ++e)
+#pragma unroll
+    for (int g = 0; g < kGs; ++g) acc[e][g][0] = acc[e][g][1] = 0.f;
   for (int p = 0; p < passes; ++p) {  // job passes + p
     const int j = passes + p, first = p * kSub, rows = job_rows(j);
     const uint8_t* vb = sm.buf[j % 2];
     for (int b = 0; b < rows / kBox; ++b) {
       if (ok) ok = mbar_wait_or_abort(&sm.bar[j % 2][b], parity(j, b), &abort_flag, sc.err);
-#pragma unroll 8
-      for (int t = b * kBox; t < (b + 1) * kBox; ++t) {
-        const float vf = bf16_to_f32(reinterpret_cast<const uint16_t*>(vb + t * kRowBytes)[tid]);
-        const uint32_t w = sm.score[first + t];
-        o0 = fmaf(lo_bf16(w), vf, o0);
-        o1 = fmaf(hi_bf16(w), vf, o1);
+      const int t0 = b * kBox + half * kHalf;
+#pragma unroll
+      for (int k = 0; k < kHalf; ++k) {
+        const uint32_t vw = reinterpret_cast<const uint32_t*>(vb + (t0 + k) * kRowBytes)[dp];
+        const uint32_t w = sm.score[first + t0 + k];
+        const float v0 = lo_bf16(vw), v1 = hi_bf16(vw), p0 = lo_bf16(w), p1 = hi_bf16(w);
+        acc[k % 2][0][0] = fmaf(p0, v0, acc[k % 2][0][0]);
+        acc[k % 2][0][1] = fmaf(p0, v1, acc[k % 2][0][1]);
+        acc[k % 2][1][0] = fmaf(p1, v0, acc[k % 2][1][0]);
+        acc[k % 2][1][1] = fmaf(p1, v1, acc[k % 2][1][1]);
       }
     }
     if (j + 2 < 2 * passes) {  // CTA-uniform
@@ -333,8 +372,21 @@ __global__ void __launch_bounds__(kThreads, MINB) attention_kernel(const __grid_
       issue(j + 2);
     }
   }
-  sm.po[0][tid] = o0;
-  sm.po[1][tid] = o1;
+  if (half == 1) {
+#pragma unroll
+    for (int g = 0; g < kGs; ++g) {
+      sm.po[g][2 * dp] = acc[0][g][0] + acc[1][g][0];
+      sm.po[g][2 * dp + 1] = acc[0][g][1] + acc[1][g][1];
+    }
+  }
+  __syncthreads();  // the second half's sums are in place
+  if (half == 0) {
+#pragma unroll
+    for (int g = 0; g < kGs; ++g) {
+      sm.po[g][2 * dp] = (acc[0][g][0] + acc[1][g][0]) + sm.po[g][2 * dp];
+      sm.po[g][2 * dp + 1] = (acc[0][g][1] + acc[1][g][1]) + sm.po[g][2 * dp + 1];
+    }
+  }
   if (tid < kGs) {
     float z = 0.f;
     for (int w = 0; w < kWarps; ++w) z += sm.red[w][tid];

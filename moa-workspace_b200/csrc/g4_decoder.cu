@@ -19,6 +19,8 @@
 // the batched ops instead (g4_batch_attn.cu, g4_batch.cu): each layer's weights are read once for
 // all m tokens, every sequence keeping its own ring in the layer's caches ([m][ring][Ns][Ds]) and
 // its own position.
+#include <algorithm>
+#include <cstdlib>
 #include <vector>
 
 #include "g4_ctx.cuh"
@@ -31,6 +33,8 @@ namespace {
 constexpr int kMaxRings = 4;           // distinct ring lengths one model may use
 constexpr int kBeginThreads = 256;
 constexpr int kBeginBlocks = 16;
+// units of each FP8 up/gate CTA's run brought into L2 by a sliding layer's attention (hints)
+constexpr int kDefaultL2Units = 8;
 
 struct BeginArgs {
   const int32_t* input;  // [batch] {token, position}
@@ -92,6 +96,9 @@ struct g4_decoder {
   float *run_max = nullptr, *run_sum = nullptr;
   cudaGraph_t graph = nullptr;
   cudaGraphExec_t exec = nullptr;
+  // units of every FP8 up/gate CTA's run that a sliding layer's attention brings into L2 (0: no
+  // hints); G4_DECODER_L2_UNITS overrides the default at creation
+  int l2_units = g4::kDefaultL2Units;
 };
 
 namespace {
@@ -151,6 +158,21 @@ g4_status check_layer(g4_ctx* ctx, const g4_layer& l) {
   }
   if (!(l.attn_scale == l.attn_scale)) return fail(ctx, G4_ERR_INVALID_ARGUMENT, "%s is NaN", "layer.attn_scale");
   return G4_OK;
+}
+
+g4::Ffn8Args ffn8_args(const g4_decoder* d, const g4_layer& l) {
+  const bool tiled = l.tiled != 0;
+  return g4::Ffn8Args{d->hidden,
+                      l.pre_ff_rms_weight,
+                      l.up_weight,
+                      tiled ? l.up_weight : l.gate_weight,
+                      l.down_weight,
+                      static_cast<const float*>(l.up_scale),
+                      static_cast<const float*>(l.gate_scale),
+                      static_cast<const float*>(l.down_scale),
+                      l.post_ff_rms_weight,
+                      l.layer_scalar,
+                      tiled};
 }
 
 // Every kernel of one token on `stream`.
@@ -228,22 +250,18 @@ cudaError_t issue_step(g4_decoder* d, cudaStream_t stream) {
                     d->kv_off + d->kvs * r};  // the slots the QKV op above writes
     aa.batch = nb;
     aa.mask_stride = d->mask_stride;
-    if ((e = g4::launch_attention(aa, env)) != cudaSuccess) return e;
     const g4::OArgs oa{d->attn, l.post_attn_rms_weight, l.o_weight, l.o_weight_scale, d->hidden, tiled};
+    if (nb == 1 && d->l2_units > 0) {
+      // attention moves few bytes: it brings O's weights and the first units of every FP8
+      // up/gate CTA's run into L2 for the kernels that follow it
+      aa.next[0] = g4::l2_hint_o(oa, g4::kL2HintAllUnits, env);
+      if (l.ffn == G4_FFN_FP8) aa.next[1] = g4::l2_hint_ffn8_upgate(ffn8_args(d, l), d->l2_units, env);
+    }
+    if ((e = g4::launch_attention(aa, env)) != cudaSuccess) return e;
     if ((e = nb > 1 ? g4::launch_o_batch(oa, nb, env) : g4::launch_o(oa, env)) != cudaSuccess) return e;
     }
     if (l.ffn == G4_FFN_FP8) {
-      const g4::Ffn8Args fa{d->hidden,
-                            l.pre_ff_rms_weight,
-                            l.up_weight,
-                            tiled ? l.up_weight : l.gate_weight,
-                            l.down_weight,
-                            static_cast<const float*>(l.up_scale),
-                            static_cast<const float*>(l.gate_scale),
-                            static_cast<const float*>(l.down_scale),
-                            l.post_ff_rms_weight,
-                            l.layer_scalar,
-                            tiled};
+      const g4::Ffn8Args fa = ffn8_args(d, l);
       e = nb > 1 ? g4::launch_ffn_fp8_batch(fa, nb, env) : g4::launch_ffn_fp8(fa, env);
     } else {
       const g4::FfnArgs fa{d->hidden,
@@ -323,6 +341,7 @@ g4_status g4_decoder_create_batch(g4_ctx* ctx, const g4_model* model, int32_t ba
   d->layers.assign(m.layers, m.layers + m.n_layers);
   d->batch = batch;
   d->kvs = batch > 1 ? (batch + 3) / 4 * 4 : 4;
+  if (const char* v = std::getenv("G4_DECODER_L2_UNITS")) d->l2_units = std::max(0, std::atoi(v));
   for (const g4_layer& l : d->layers) {
     if ((st = check_layer(ctx, l)) != G4_OK) {
       delete d;

@@ -493,6 +493,7 @@ __device__ void gemv_run(Op& op, uint8_t* smem_raw, const Scratch& sc) {
     if constexpr (!Op::kRms) request_rest();
     if constexpr (Shape::kFp4) __syncthreads();  // the CTA's largest exponent (pmax) is complete
     G4_STAMP(sc, 10);
+    G4_STAMP_WARP(sc, 4);
     if constexpr (Shape::kFp4) {
       // digit rows, one thread per 8 elements: a warp builds a whole slot (warp w slots w, w + 7,
       // ...) and arrives on its barrier, so the relay releases a unit as soon as its slot is built
@@ -541,13 +542,16 @@ __device__ void gemv_run(Op& op, uint8_t* smem_raw, const Scratch& sc) {
           const uint32_t kb = e16 % 128;
 #pragma unroll
           for (int r = 0; r < 8; ++r) *reinterpret_cast<uint4*>(atom + sw128_offset(r, kb)) = tm[r];
+          if (q == 0) G4_STAMP_WARP(sc, 5);
           asm volatile("fence.proxy.async.shared::cta;" ::: "memory");  // the tensor cores read it
+          if (q == 0) G4_STAMP_WARP(sc, 6);
         }
         __syncwarp();
         if (have[q] && (c.lane & 15) == 0) mbar_arrive(&ctl.bready[slot[q]]);
       }
     }
     G4_STAMP(sc, 11);
+    G4_STAMP_WARP(sc, 7);
   }
   G4_STAMP(sc, 2);
 

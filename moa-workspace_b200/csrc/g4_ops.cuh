@@ -35,6 +35,45 @@ struct QkvArgs {
   bool tiled;  // weights in the unit-tiled layout of g4_pack_tiles (else the reference row-major)
 };
 
+// Weights a later engine kernel streams first, requested into L2 by an earlier kernel of the
+// decode step whose own HBM traffic is small (attention): the bytes then cross HBM while that
+// kernel and the next one's prologue run, and the consumer's TMA loads hit L2. A hint only:
+// nothing depends on it for correctness. The weights are unit-tiled (unit u at base + u
+// unit_bytes); the consumer's CTA c runs units [c total / grid, (c + 1) total / grid), and the
+// first `first_units` of every run are requested (runs' first units before their later ones).
+struct L2Hint {
+  const uint8_t* base = nullptr;
+  uint32_t unit_bytes = 0;
+  int total_units = 0;
+  int consumer_grid = 0;
+  int first_units = 0;
+};
+constexpr int kL2HintUnitsPerPrefetch = 2;  // units per bulk prefetch (64 KB of fp8 weights)
+constexpr int kL2HintAllUnits = 1 << 20;    // first_units: every unit of every run
+
+// This CTA's share (it is `cta` of `ctas` issuing CTAs) of the hints' bulk prefetches, one per
+// thread; every thread of the CTA calls it.
+__device__ __forceinline__ void issue_l2_hints(const L2Hint* hints, int nh, int cta, int ctas) {
+  for (int h = 0; h < nh; ++h) {
+    const L2Hint& hint = hints[h];
+    if (!hint.base || hint.first_units <= 0 || hint.consumer_grid <= 0) continue;
+    const int pieces = (hint.first_units + kL2HintUnitsPerPrefetch - 1) / kL2HintUnitsPerPrefetch;
+    const int items = pieces * hint.consumer_grid;
+    for (int k = cta + ctas * int(threadIdx.x); k < items; k += ctas * int(blockDim.x)) {
+      const int piece = k / hint.consumer_grid, c = k % hint.consumer_grid;
+      const int64_t t = hint.total_units, g = hint.consumer_grid;
+      const int r0 = int(c * t / g), r1 = int((c + 1) * t / g);
+      const int lim = r0 + hint.first_units < r1 ? r0 + hint.first_units : r1;
+      const int u0 = r0 + piece * kL2HintUnitsPerPrefetch;
+      const int u1 = u0 + kL2HintUnitsPerPrefetch < lim ? u0 + kL2HintUnitsPerPrefetch : lim;
+      if (u1 > u0)
+        asm volatile("cp.async.bulk.prefetch.L2.global [%0], %1;" ::"l"(hint.base + size_t(u0) * hint.unit_bytes),
+                     "r"(uint32_t(u1 - u0) * hint.unit_bytes)
+                     : "memory");
+    }
+  }
+}
+
 struct AttnArgs {
   const uint16_t* q;
   const uint16_t* k_cache;
@@ -53,6 +92,9 @@ struct AttnArgs {
   // b mask_stride and its kv_offset at kv_offset[b]
   int batch = 1;
   int mask_stride = 0;
+  // the decode driver's hints for the O and feed-forward kernels that follow (issued before the
+  // wait on the QKV op)
+  L2Hint next[2];
 };
 
 struct OArgs {
@@ -194,6 +236,10 @@ cudaError_t launch_attention(const AttnArgs& a, const LaunchEnv& env);
 cudaError_t launch_o(const OArgs& a, const LaunchEnv& env);
 cudaError_t launch_ffn_nvfp4(const FfnArgs& a, const LaunchEnv& env);
 cudaError_t launch_ffn_fp8(const Ffn8Args& a, const LaunchEnv& env);
+// L2 hints for the first `first_units` units of every CTA of a following O / FP8 up-gate kernel
+// on this env (unit-tiled weights only: an empty hint otherwise).
+L2Hint l2_hint_o(const OArgs& a, int first_units, const LaunchEnv& env);
+L2Hint l2_hint_ffn8_upgate(const Ffn8Args& a, int first_units, const LaunchEnv& env);
 // The NVFP4 feed-forward on m = 2..64 tokens (g4_batch.cu): residual [m][H]; one GPU.
 cudaError_t prepare_batch_kernels();
 bool batch_geometry_fits(int sm_count);

@@ -1236,6 +1236,46 @@ cudaError_t launch_ffn_fp8(const Ffn8Args& a, const LaunchEnv& env) {
   return by_degree(env.tp.world, [&](auto d) { return launch_ffn8_t<decltype(d)::value>(a, env); });
 }
 
+namespace {
+template <class Shape>
+L2Hint engine_hint(const uint8_t* w, int first_units, const LaunchEnv& env) {
+  L2Hint h;
+  h.base = w;
+  h.unit_bytes = uint32_t(Shape::kABytes);
+  h.total_units = Shape::kTotalUnits;
+  h.consumer_grid = grid_for<Shape>(env);
+  const int longest = (h.total_units + h.consumer_grid - 1) / h.consumer_grid;  // the longest run
+  h.first_units = first_units < longest ? first_units : longest;
+  return h;
+}
+template <template <int> class Pick>
+L2Hint hint_by_degree(const uint8_t* w, int first_units, const LaunchEnv& env) {
+  switch (env.tp.world) {
+    case 1: return engine_hint<typename Pick<1>::type>(w, first_units, env);
+    case 2: return engine_hint<typename Pick<2>::type>(w, first_units, env);
+    case 4: return engine_hint<typename Pick<4>::type>(w, first_units, env);
+    case 8: return engine_hint<typename Pick<8>::type>(w, first_units, env);
+    default: return L2Hint{};
+  }
+}
+template <int NTP>
+struct PickO {
+  using type = typename Shapes<NTP>::O;
+};
+template <int NTP>
+struct PickUpGate8 {
+  using type = typename Shapes<NTP>::UpGate8;
+};
+}  // namespace
+
+L2Hint l2_hint_o(const OArgs& a, int first_units, const LaunchEnv& env) {
+  return a.tiled ? hint_by_degree<PickO>(a.o_weight, first_units, env) : L2Hint{};
+}
+
+L2Hint l2_hint_ffn8_upgate(const Ffn8Args& a, int first_units, const LaunchEnv& env) {
+  return a.tiled ? hint_by_degree<PickUpGate8>(a.up_w, first_units, env) : L2Hint{};
+}
+
 // ---------------------------------------------------------------------------------------
 // unit-tiled weight layout
 
