@@ -16,11 +16,13 @@
 // rows: they are not needed until the maximum is known), scores its slots for the head's two
 // query heads and computes its score maximum. The rounding
 // of p to bf16 depends on the maximum over the WHOLE ring, so the cluster exchanges maxima
-// through distributed shared memory (a cluster barrier, then each CTA reads the others') before
-// computing p. Each CTA then leaves its partial sum_t p and sum_t bf16(p) v in its shared memory;
-// after a second cluster barrier CTA c adds the partials of head dimensions [c Ds / C, (c + 1) Ds / C)
-// over the cluster in chunk order, so the result does not depend on timing, and a third barrier keeps
-// every CTA's shared memory alive until the others have read it.
+// through distributed shared memory before computing p: each CTA stores its maxima into every
+// CTA's shared memory, and after a cluster barrier reads them from its own. Each CTA then stores
+// its partial sum_t p, and its partial sum_t bf16(p) v of head dimensions [c Ds / C, (c + 1) Ds / C),
+// into CTA c; after a second cluster barrier CTA c adds the partials in chunk order, so the result
+// does not depend on timing. No CTA reads another's shared memory, so none waits for the others
+// before it exits (the first barrier's arrival, at the start, only makes sure every CTA runs
+// before any stores into it).
 #include "g4_ops.cuh"
 #include "g4_tc.cuh"
 
@@ -60,9 +62,12 @@ struct AttnSmem {
   // the high half): the values the reference rounds to bf16 anyway
   uint32_t score[kMaxPer];
   float red[kWarps][kGs];
-  float cmax[kGs];            // this CTA's score maxima (read by the cluster)
-  float po[kGs][kDs];         // this CTA's partial sum_t bf16(p) v (read by the cluster)
-  float pz[kGs];              // and sum_t p
+  float po[kGs][kDs];         // this CTA's partial sum_t bf16(p) v (the value pass's two halves)
+  // written by the cluster's CTAs (CTA c at index c) before a cluster barrier: their score maxima,
+  // their partials of the head dimensions this CTA combines, and their sum_t p
+  float in_max[C][kGs];
+  float in_po[C][kGs][kDimsPerCta];
+  float in_z[C][kGs];
   __align__(16) uint16_t out[kGs * kDimsPerCta];
   uint64_t bar[2][kBoxes];
 };
@@ -93,6 +98,17 @@ __device__ __forceinline__ uint32_t cluster_ctarank() {
   uint32_t r;
   asm volatile("mov.u32 %0, %%cluster_ctarank;" : "=r"(r));
   return r;
+}
+// The cluster barrier in two halves: a relaxed arrival, and the wait for every CTA's.
+__device__ __forceinline__ void cluster_arrive_relaxed() {
+  asm volatile("barrier.cluster.arrive.relaxed.aligned;" ::: "memory");
+}
+__device__ __forceinline__ void cluster_wait() { asm volatile("barrier.cluster.wait.aligned;" ::: "memory"); }
+// Store a float into CTA `rank`'s shared memory at the address this CTA's copy of the object has.
+__device__ __forceinline__ void st_cluster_f32(void* own, uint32_t rank, float v) {
+  uint32_t a;
+  asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(a) : "r"(smem_u32(own)), "r"(rank));
+  asm volatile("st.shared::cluster.f32 [%0], %1;" ::"r"(a), "f"(v) : "memory");
 }
 // A float of CTA `rank`'s shared memory at the address this CTA's copy of the object has.
 __device__ __forceinline__ float ld_cluster_f32(const void* own, uint32_t rank) {
@@ -131,6 +147,9 @@ __global__ void __launch_bounds__(kThreads, MINB) attention_kernel(const __grid_
     mbar_init(&sm.bar[1][tid], 1);
     fence_mbar_init();
   }
+  // this CTA is running: the others may write into its shared memory once they have waited for
+  // this arrival (before the first exchange)
+  cluster_arrive_relaxed();
   // rows [first, first + count) of a cache into a shared-memory buffer: box b (kBox rows) by
   // thread b, completing on its own barrier, so the rows can be used as their box lands
   const uint64_t policy = l2_evict_first_policy();  // each row is read once per step
@@ -299,21 +318,20 @@ __global__ void __launch_bounds__(kThreads, MINB) attention_kernel(const __grid_
     sm.red[warp][1] = m1;
   }
   __syncthreads();
-  if (tid < kGs) {
+  cluster_wait();  // every CTA of the cluster is running
+  if (tid < kGs * kChunks) {  // thread (g, c): this CTA's maximum of head g into CTA c
+    const int g = tid / kChunks, c = tid % kChunks;
     float m = -INFINITY;
-    for (int w = 0; w < kWarps; ++w) m = fmaxf(m, sm.red[w][tid]);
-    sm.cmax[tid] = m;
+    for (int w = 0; w < kWarps; ++w) m = fmaxf(m, sm.red[w][g]);
+    st_cluster_f32(&sm.in_max[chunk][g], uint32_t(c), m);
   }
-  cluster_sync();  // every CTA's maxima are in its shared memory
+  cluster_sync();  // every CTA's maxima are in every CTA's shared memory
   float gm[kGs];
 #pragma unroll
   for (int g = 0; g < kGs; ++g) {
-    float pm[kChunks];
-#pragma unroll
-    for (int c = 0; c < kChunks; ++c) pm[c] = ld_cluster_f32(&sm.cmax[g], uint32_t(c));
     gm[g] = -INFINITY;
 #pragma unroll
-    for (int c = 0; c < kChunks; ++c) gm[g] = fmaxf(gm[g], pm[c]);
+    for (int c = 0; c < kChunks; ++c) gm[g] = fmaxf(gm[g], sm.in_max[c][g]);
   }
   G4_STAMP(sc, 3);
 
@@ -380,39 +398,38 @@ __global__ void __launch_bounds__(kThreads, MINB) attention_kernel(const __grid_
     }
   }
   __syncthreads();  // the second half's sums are in place
-  if (half == 0) {
+  if (half == 0) {  // this CTA's partial of dimensions 2 dp, 2 dp + 1 into the CTA that combines them
 #pragma unroll
     for (int g = 0; g < kGs; ++g) {
-      sm.po[g][2 * dp] = (acc[0][g][0] + acc[1][g][0]) + sm.po[g][2 * dp];
-      sm.po[g][2 * dp + 1] = (acc[0][g][1] + acc[1][g][1]) + sm.po[g][2 * dp + 1];
+#pragma unroll
+      for (int e = 0; e < 2; ++e) {
+        const int d = 2 * dp + e;
+        const float v = (acc[0][g][e] + acc[1][g][e]) + sm.po[g][d];
+        st_cluster_f32(&sm.in_po[chunk][g][d % kDimsPerCta], uint32_t(d / kDimsPerCta), v);
+      }
     }
   }
-  if (tid < kGs) {
+  if (tid >= kThreads - kGs * kChunks) {  // thread (g, c): this CTA's sum_t p of head g into CTA c
+    const int i = tid - (kThreads - kGs * kChunks), g = i / kChunks, c = i % kChunks;
     float z = 0.f;
-    for (int w = 0; w < kWarps; ++w) z += sm.red[w][tid];
-    sm.pz[tid] = z;
+    for (int w = 0; w < kWarps; ++w) z += sm.red[w][g];
+    st_cluster_f32(&sm.in_z[chunk][g], uint32_t(c), z);
   }
-  cluster_sync();  // every CTA's partials are in its shared memory
+  cluster_sync();  // every partial is in the shared memory of the CTA that combines it
   G4_STAMP(sc, 5);
 
   // CTA `chunk` combines dimensions [32 chunk, 32 chunk + 32) of both query heads, chunks in order
   if (tid < kGs * kDimsPerCta) {
-    const int g = tid / kDimsPerCta, d = chunk * kDimsPerCta + tid % kDimsPerCta;
-    float po[kChunks], pz[kChunks];
-#pragma unroll
-    for (int c = 0; c < kChunks; ++c) {  // every load in flight at once
-      po[c] = ld_cluster_f32(&sm.po[g][d], uint32_t(c));
-      pz[c] = ld_cluster_f32(&sm.pz[g], uint32_t(c));
-    }
+    const int g = tid / kDimsPerCta, dd = tid % kDimsPerCta;
     float o = 0.f, z = 0.f;
 #pragma unroll
     for (int c = 0; c < kChunks; ++c) {
-      o += po[c];
-      z += pz[c];
+      o += sm.in_po[c][g][dd];
+      z += sm.in_z[c][g];
     }
     sm.out[tid] = f32_to_bf16(bf16_round(o) / (z + kEps));
   }
-  cluster_sync();  // the others are done reading this CTA's partials (and sm.out is complete)
+  __syncthreads();  // sm.out is complete (no CTA reads another's shared memory after the barrier)
   if (tid < kGs * kDimsPerCta * 2 / 16) {  // 16-byte stores: 4 per query head
     const int g = tid / (kDimsPerCta * 2 / 16), q = tid % (kDimsPerCta * 2 / 16);
     reinterpret_cast<uint4*>(a.out + qrow0 + (head * kGs + g) * kDs + chunk * kDimsPerCta)[q] =
