@@ -206,6 +206,29 @@ __global__ void __launch_bounds__(kThreads, MINB) attention_kernel(const __grid_
   pdl_launch_dependents();
   G4_STAMP(sc, 1);
 
+  // phase 1: scores, kSub slots at a time. The 8 lanes 8i .. 8i + 7 of a warp score one slot,
+  // so a warp scores 4 slots per step (one box of 32 slots per step of the 8 warps). Lane
+  // `part` of a slot holds head dimensions c 64 + 8 part + j (c < 4, j < 8): for each c the 8
+  // lanes read 128 contiguous bytes of the row.
+  constexpr int kLanesPerSlot = 8, kSlotsPerStep = 32 / kLanesPerSlot;
+  static_assert(kWarps * kSlotsPerStep == kBox, "one box per step of the CTA");
+  const int sub = lane / kLanesPerSlot, part = lane % kLanesPerSlot;
+  // This lane's 32 q elements of each head (loaded first: the slot's fresh rows below wait on
+  // their boxes and on loads of their own), as f32 where the registers allow (one or two CTAs per
+  // SM), else as bf16 pairs (element 2i low) converted at each use (the batch shape's three).
+  constexpr bool kQf32 = MINB <= 2;
+  uint32_t qv[kGs][16];
+  float qf[kGs][kQf32 ? 32 : 1];
+#pragma unroll
+  for (int g = 0; g < kGs; ++g) {
+#pragma unroll
+    for (int c = 0; c < 4; ++c) {
+      const uint4 raw =
+          __ldcg(reinterpret_cast<const uint4*>(a.q + qrow0 + (head * kGs + g) * kDs + c * 64 + part * 8));
+      qv[g][4 * c] = raw.x, qv[g][4 * c + 1] = raw.y, qv[g][4 * c + 2] = raw.z, qv[g][4 * c + 3] = raw.w;
+    }
+  }
+
   if (!a.kv_offset) {
     issue(0);
     issue(1);
@@ -233,27 +256,6 @@ __global__ void __launch_bounds__(kThreads, MINB) attention_kernel(const __grid_
     if (fixed) __syncthreads();  // the rows are in place before anyone reads them (CTA-uniform)
   }
 
-  // phase 1: scores, kSub slots at a time. The 8 lanes 8i .. 8i + 7 of a warp score one slot,
-  // so a warp scores 4 slots per step (one box of 32 slots per step of the 8 warps). Lane
-  // `part` of a slot holds head dimensions c 64 + 8 part + j (c < 4, j < 8): for each c the 8
-  // lanes read 128 contiguous bytes of the row.
-  constexpr int kLanesPerSlot = 8, kSlotsPerStep = 32 / kLanesPerSlot;
-  static_assert(kWarps * kSlotsPerStep == kBox, "one box per step of the CTA");
-  const int sub = lane / kLanesPerSlot, part = lane % kLanesPerSlot;
-  // This lane's 32 q elements of each head: as f32 where the registers allow (one or two CTAs per
-  // SM), else as bf16 pairs (element 2i low) converted at each use (the batch shape's three).
-  constexpr bool kQf32 = MINB <= 2;
-  uint32_t qv[kGs][16];
-  float qf[kGs][kQf32 ? 32 : 1];
-#pragma unroll
-  for (int g = 0; g < kGs; ++g) {
-#pragma unroll
-    for (int c = 0; c < 4; ++c) {
-      const uint4 raw =
-          __ldcg(reinterpret_cast<const uint4*>(a.q + qrow0 + (head * kGs + g) * kDs + c * 64 + part * 8));
-      qv[g][4 * c] = raw.x, qv[g][4 * c + 1] = raw.y, qv[g][4 * c + 2] = raw.z, qv[g][4 * c + 3] = raw.w;
-    }
-  }
   if constexpr (kQf32) {
 #pragma unroll
     for (int g = 0; g < kGs; ++g)
