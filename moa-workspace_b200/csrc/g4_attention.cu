@@ -784,9 +784,13 @@ cudaError_t launch_attention(const AttnArgs& a, const LaunchEnv& env) {
     return cudaLaunchKernelEx(&cfg, attention_kernel<G4_ATTN_BATCH_C, G4_ATTN_BATCH_SUB, 3, kBatchMaxRing>, maps, a,
                               sc);
   }
+  // 16-CTA clusters for rings of 2 to 4 passes; for 1024-slot rings too when at most half the
+  // heads are on this GPU (tensor parallelism), as the eight heads' 128 CTAs would leave the next
+  // kernel too few SMs to start its weight copies on (measured slower at 8 heads)
+  const bool few_heads = a.heads * a.batch <= kNs / 2;
   const bool c16 = env.device >= 0 && env.device < kMaxDevices && g_clusters16[env.device] == 1 &&
-                   a.ring_len % (16 * kBox) == 0 && a.ring_len >= 2048 &&
-                   a.ring_len <= 4 * 16 * Attn16::kSub;  // 2 to 4 passes (shorter rings: measured faster at 8)
+                   a.ring_len % (16 * kBox) == 0 && a.ring_len >= (few_heads ? 1024 : 2048) &&
+                   a.ring_len <= 4 * 16 * Attn16::kSub;
   if (c16) {
     const cudaLaunchConfig_t cfg = attention_config<Attn16, 16>(a.heads, env.stream, env.pdl, attr, a.batch);
     return cudaLaunchKernelEx(&cfg, attention_kernel<16, 64>, maps, a, sc);
