@@ -34,7 +34,7 @@ constexpr int kMaxRings = 4;           // distinct ring lengths one model may us
 constexpr int kBeginThreads = 256;
 constexpr int kBeginBlocks = 16;
 // units of each FP8 up/gate CTA's run brought into L2 by a sliding layer's attention (hints)
-constexpr int kDefaultL2Units = 8;
+constexpr int kDefaultL2Units = 12;
 
 struct BeginArgs {
   const int32_t* input;  // [batch] {token, position}
