@@ -8,9 +8,9 @@
 //   out    = bf16( bf16(sum_t bf16(p[g,t]) v[t]) / sum[g] )
 //
 // One thread-block cluster of C CTAs per KV head (C = 16 for rings of 2048 to 4096 slots where
-// the GPU can hold the clusters, else the portable 8: 128 or 64 CTAs for the 8 heads; a
-// tensor-parallel rank holds 8 / n of
-// them in its cache slice), each owning a contiguous run of ring slots. A CTA copies its K and V
+// the GPU can hold the clusters, and for 1024-slot rings too when at most half the heads are on
+// the GPU; else the portable 8: 128 or 64 CTAs for the 8 heads; a tensor-parallel rank holds 8 / n
+// of them in its cache slice), each owning a contiguous run of ring slots. A CTA copies its K and V
 // rows into shared memory with TMA boxes of 32 rows, each completing on its own barrier so that
 // scoring starts as the first box lands (the V rows of the first pass are requested with the K
 // rows: they are not needed until the maximum is known), scores its slots for the head's two
